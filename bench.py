@@ -1,0 +1,339 @@
+#!/usr/bin/env python
+"""Benchmark of the zeroth-order hot path (one JSON line on rank 0).
+
+Workload (N=1 default): the kernel microbench on the full parameter set of a
+Llama-3.2-1B-shaped model (146 bf16 tensors, 1,235,814,400 params, N(0,0.02)),
+64 seeds per step drawn from a seeded uint64 stream, eps = 1e-3. One step = for each
+seed: +eps (fused with the previous seed's restore), -2eps; then the last restore,
+the 64-stream gradient estimate and the update in one pass: 129 fused passes, no
+forward (synthetic pair values). ``value`` = ZO steps/s over all ranks (seeds sharded
+round-robin over ranks, one all-gather of the pair values, replicated final pass).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+METRIC = "ZO steps/s + perturb-pass HBM GB/s (Llama-1B); EGGROLL member-evals/s (8B)"
+UNIT = "ZO steps/s"
+N_SEEDS = 64
+EPS = 1e-3
+LR = 1e-6
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seeds", type=int, default=N_SEEDS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def env_rank():
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+
+
+# ── clocks ─────────────────────────────────────────────────────────────────────────
+
+class ClockSampler:
+    """nvidia-smi sampled every 200 ms during the timed region (reading only)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", self.gpu_id], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ── CPU baseline: the oracle port on host cores ───────────────────────────────────────
+
+def cpu_sample_step_rate(total_numel: int, n_seeds: int, sample_elems: int = 1 << 24, pairs: int = 2):
+    """Time the reference's per-pair algorithm (materialise z, three perturb ops, one
+    grad_est accumulation, zotitan/train_zo.py:534-556) on `sample_elems` bf16 elements
+    for `pairs` pairs plus the update, with one thread per core (ctypes releases the GIL),
+    and extrapolate to steps/s of the full workload."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import philox as ph
+    cores = os.cpu_count() or 1
+    chunk = (sample_elems + cores - 1) // cores
+    rng = np.random.default_rng(0)
+    th = ph.rounded(ph.BF16, (rng.standard_normal(sample_elems) * 0.02).astype(np.float32))
+    ge = np.zeros_like(th)
+    lib = ph.lib()
+    a_p, a_m = float(np.float32(EPS)), float(np.float32(-2 * EPS))
+
+    def pair_chunk(args):
+        key, lo, hi, c = args
+        n = hi - lo
+        z = np.empty(n, np.float32)
+        lib.zo_randn(key, lo, n, ph._p(z))
+        t, g = th[lo:hi], ge[lo:hi]
+        for a in (a_p, a_m, a_p):
+            lib.zo_add_scaled(ph.BF16, ph._p(t), ph._p(z), a, n)
+        lib.zo_add_scaled(ph.BF16, ph._p(g), ph._p(z), c, n)
+
+    def update_chunk(args):
+        lo, hi = args
+        lib.zo_add_scaled(ph.BF16, ph._p(th[lo:hi]), ph._p(ge[lo:hi]), -float(np.float32(LR)), hi - lo)
+
+    spans = [(i * chunk, min(sample_elems, (i + 1) * chunk)) for i in range(cores) if i * chunk < sample_elems]
+    with ThreadPoolExecutor(cores) as ex:
+        t0 = time.perf_counter()
+        for j in range(pairs):
+            list(ex.map(pair_chunk, [(ph.param_key(j, 146, 0), lo, hi, 0.01) for lo, hi in spans]))
+        t1 = time.perf_counter()
+        list(ex.map(update_chunk, spans))
+        t2 = time.perf_counter()
+    per_pair_elem = (t1 - t0) / (pairs * sample_elems)
+    per_update_elem = (t2 - t1) / sample_elems
+    step_s = total_numel * (n_seeds * per_pair_elem + per_update_elem)
+    return {"value": 1.0 / step_s, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{pairs} pairs + update over {sample_elems} bf16 elements (C oracle, {cores} threads), "
+                      f"extrapolated to {n_seeds} seeds x {total_numel} elements; measured {t2 - t0:.2f} s"}
+
+
+# ── reference arm ───────────────────────────────────────────────────────────────────
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    from zotitan_b200.synthetic import LLAMA_1B, llama_param_shapes, numel
+    total = numel(llama_param_shapes(LLAMA_1B))
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_sample_step_rate(total, args.seeds, sample_elems=1 << 24, pairs=2)
+        if i >= args.warmup:
+            vals.append(r["value"])
+    v = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "Llama-3.2-1B-shaped parameter set, 64 seeds/step (kernel microbench)",
+                       "params": total, "seeds_per_step": args.seeds, "eps": EPS},
+            "cpu_baseline": {**r, "value": v},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ── our arm ─────────────────────────────────────────────────────────────────────────
+
+def run_ours(args, rank, local_rank, world):
+    import torch
+    import torch.distributed as dist
+
+    from zotitan_b200 import kernels as K
+    from zotitan_b200.objective import Score
+    from zotitan_b200.synthetic import LLAMA_1B, llama_param_shapes, make_params
+    from zotitan_b200.train_zo import ZOConfig, ZOOptimizer
+
+    cpu_line = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_line = cpu_sample_step_rate(1_235_814_400, args.seeds)   # before any CUDA work
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from zotitan_b200.distributed import init_process_group_from_env
+        init_process_group_from_env("nccl", timeout_s=300)
+
+    shapes = llama_param_shapes(LLAMA_1B)
+    named = make_params(shapes, torch.bfloat16, dev, seed=0)
+    numel = sum(p.numel() for _, p in named)
+    cfg = ZOConfig()
+    cfg.eps, cfg.z_batch, cfg.base.lr = EPS, args.seeds, LR
+
+    # synthetic pair values: fixed device scalars (no forward in this microbench)
+    g = torch.Generator().manual_seed(1)
+    vals_host = (2.0 + 0.01 * torch.randn(2 * args.seeds, generator=g)).float()
+    vals_dev = vals_host.to(dev)
+    vals_pinned = vals_host.pin_memory()
+
+    class Score_:
+        def __init__(self, from_host):
+            self.k = 0
+            self.from_host = from_host
+
+        def __call__(self, model, batch):
+            i = self.k % (2 * args.seeds)
+            self.k += 1
+            if self.from_host:   # e2e: the value arrives from pinned host memory
+                v = vals_pinned[i:i + 1].to(dev, non_blocking=True)[0]
+            else:
+                v = vals_dev[i]
+            return Score(v, {})
+
+    score = Score_(False)
+    opt = ZOOptimizer(named, cfg, score)
+    rng = np.random.default_rng(12345)   # seeded uint64 seed stream, identical on every rank
+    opt.planner._draw_seeds = lambda n: [int(x) for x in rng.integers(0, 2**64 - 1, n, dtype=np.uint64)]
+
+    # per-launch events on the -2eps passes (one noise stream, read+write of every element)
+    events, counter = [], {"launches": 0, "on": False}
+    orig_run = opt.table.run
+
+    def run(cfg_, streams):
+        if counter["on"]:
+            counter["launches"] += 1
+        rec = counter["on"] and len(streams) == 1 and streams[0].chain and streams[0].chain[0] < 0
+        if rec:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+        orig_run(cfg_, streams)
+        if rec:
+            b.record()
+            events.append((a, b))
+    opt.table.run = run
+
+    batches = [None] * args.seeds
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        opt.step(None, batches)
+    gpu_uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    clocks = ClockSampler(gpu_uuid)
+    barrier()
+    clocks.start()
+    counter["on"] = True
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        opt.step(None, batches)
+    t1.record()
+    barrier()
+    counter["on"] = False
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    kern_ms = [a.elapsed_time(b) for a, b in events]
+    launches = counter["launches"]
+
+    # e2e: same steps through the public API with every pair value copied from pinned host memory
+    score.from_host = True
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    w0 = time.perf_counter()
+    for _ in range(args.steps):
+        m = opt.step(None, batches)
+    e1.record()
+    barrier()
+    wall_e2e = time.perf_counter() - w0
+    e2e_ms = e0.elapsed_time(e1)
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms, float(np.mean(kern_ms)) if kern_ms else 0.0], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms, kmean = t.tolist()
+    else:
+        kmean = float(np.mean(kern_ms)) if kern_ms else 0.0
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(HERE, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    bytes_per_launch = 2 * 2 * numel          # bf16 read + write of every element
+    achieved = bytes_per_launch / (kmean * 1e-3) / 1e9 if kmean else None
+    traffic = None
+    prof = os.path.join(HERE, "profiles", "pass_kernel_traffic.json")
+    if os.path.exists(prof):
+        try:
+            traffic = json.load(open(prof)).get("dram_bytes_per_launch")
+        except ValueError:
+            traffic = None
+    value = args.steps / (ms * 1e-3)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "Llama-3.2-1B-shaped parameter set, 64 seeds/step (kernel microbench)",
+                   "params": numel, "tensors": len(named), "seeds_per_step": args.seeds, "eps": EPS,
+                   "passes_per_step": 2 * args.seeds + 1, "parallelism": f"seed-sharded x{world}",
+                   "l2": "inputs (2.47 GB of bf16 parameters) larger than L2"},
+        "perturb_pass_gbs": achieved, "perturb_pass_ms": kmean,
+        "philox_gelem_per_s": numel / (kmean * 1e-3) / 1e9 if kmean else None,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": (achieved / hbm_peak) if achieved else None, "traffic": traffic,
+                     "kernel": "pass_kernel, -2eps pass (1 noise stream)",
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback 6650 GB/s"},
+        "clocks": clk,
+        "gpu_launches": launches,
+        "e2e": {"value": args.steps / (e2e_ms * 1e-3), "unit": UNIT, "wall_value": args.steps / wall_e2e,
+                "h2d_bytes_per_step": 4 * 2 * args.seeds, "d2h_bytes_per_step": 4 * 2 * args.seeds},
+        "metrics_last_step": {k: m[k] for k in ("loss", "proj_grad")},
+    }
+    if cpu_line is not None:
+        line["cpu_baseline"] = cpu_line
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    rank, local_rank, world = env_rank()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    run_ours(args, rank, local_rank, world)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,197 @@
+/* zotitan_b200 — C ABI of the B200-native zeroth-order hot path.
+ *
+ * Replaces the reference's Triton noise kernel and the torch foreach passes
+ * built on it (zotitan/train_zo.py). All functions:
+ *   - return 0 on success and a nonzero ZT_ERR_* code on failure; the message is
+ *     available from zt_last_error() on the same host thread;
+ *   - never allocate device memory; callers own every buffer;
+ *   - enqueue work on the CUDA stream passed as `stream` (a cudaStream_t; NULL =
+ *     legacy default stream) and never synchronise the host;
+ *   - take device pointers for tensor data and host pointers for descriptors.
+ *
+ * Noise contract (bit-exact with the reference): element `o` of the parameter at
+ * position `index` of an `n_params`-long trainable list, for pair seed `seed`, is
+ *   Philox4x32-10(counter (o,0,0,0), key (k,0)), k = (seed*n_params+index) & 0x7FFFFFFF,
+ *   words 0,1 -> uniforms -> Box-Muller cosine branch,
+ * exactly as Triton 3.6.0's tl.random.randn(k, o) evaluates it on a GPU
+ * (zotitan/train_zo.py:18-28 and :302).
+ */
+#ifndef ZOTITAN_B200_H
+#define ZOTITAN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ZT_API __attribute__((visibility("default")))
+#else
+#define ZT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ZT_ABI_VERSION 1
+
+/* dtypes of parameter tensors */
+#define ZT_F32 0
+#define ZT_BF16 1
+#define ZT_F16 2
+
+/* status codes */
+#define ZT_OK 0
+#define ZT_ERR_INVALID 1   /* bad argument (null pointer, size out of range, ...) */
+#define ZT_ERR_CUDA 2      /* a CUDA runtime call or kernel launch failed */
+#define ZT_ERR_LIMIT 3     /* a documented maximum was exceeded */
+
+#define ZT_MAX_STREAMS 256      /* noise streams per zt_pass call */
+#define ZT_MAX_CHAIN 3          /* perturbation coefficients per stream */
+#define ZT_MAX_NUMEL 2147483647 /* per-tensor element limit (int32 offsets, as the reference) */
+
+/* Last error message of the calling host thread ("" if none). */
+ZT_API const char* zt_last_error(void);
+ZT_API int zt_abi_version(void);
+
+/* Per-tensor key (zotitan/train_zo.py:302); pure host function. */
+ZT_API uint32_t zt_param_key(uint64_t seed, uint32_t n_params, uint32_t index);
+
+/* ---- test entry points: raw noise ------------------------------------------------ */
+
+/* out4[4*i + w] = Philox word w at counter offsets[i] for key `key`.
+ * Replaces nothing in the reference (its words are internal to tl.random.randn,
+ * triton/language/random.py:88-110); exported to pin bit-exactness. */
+ZT_API int zt_philox_words(uint32_t key, const uint32_t* offsets, int64_t n, uint32_t* out4, void* stream);
+
+/* out[i] = N(0,1) sample at offset off0 + i for key `key`.
+ * Replaces _philox_randn(seed, n, device) (zotitan/train_zo.py:25-28) with off0 = 0. */
+ZT_API int zt_randn(uint32_t key, int64_t off0, int64_t n, float* out, void* stream);
+
+/* out[i] = N(0,1) sample at offsets[i]. */
+ZT_API int zt_randn_at(uint32_t key, const uint32_t* offsets, int64_t n, float* out, void* stream);
+
+/* ---- parameter tables -------------------------------------------------------------- */
+
+/* One trainable tensor. `data` is the parameter; the other buffers are optional
+ * (NULL when unused) and must have the same dtype and numel:
+ *   live   a second copy the model reads while `data` holds the unperturbed master
+ *          (seed-sharded multi-GPU mode);
+ *   m      stored-EMA first moment   (ZOOptimizer.m,  zotitan/train_zo.py:257-258)
+ *   v      second moment             (ZOOptimizer.v,  zotitan/train_zo.py:265-266)
+ *   anchor theta_0 for anchored weight decay (zotitan/train_zo.py:273-274). */
+typedef struct zt_tensor {
+  void* data;
+  void* live;
+  void* m;
+  void* v;
+  const void* anchor;
+  int64_t numel;
+  int32_t dtype;   /* ZT_F32 / ZT_BF16 / ZT_F16 */
+  int32_t index;   /* position in the reference's named-parameter list */
+} zt_tensor;
+
+/* A table of tensors resident in a caller-provided device workspace. */
+typedef struct zt_plan {
+  const zt_tensor* tensors;    /* device copy of the descriptors */
+  const int64_t* unit_prefix;  /* device: first work unit of each tensor, n_tensors+1 entries */
+  int64_t n_units;             /* work units of ZT_UNIT_ELEMS elements (per tensor, rounded up) */
+  int64_t numel_total;
+  int32_t n_tensors;
+  uint32_t n_params;           /* length of the reference's named-parameter list */
+  int32_t device;
+  int32_t reserved;
+} zt_plan;
+
+#define ZT_UNIT_ELEMS 2048
+
+/* Bytes of device workspace zt_plan_init needs for n_tensors tensors. */
+ZT_API size_t zt_plan_workspace_bytes(int32_t n_tensors);
+
+/* Validate `host_tensors`, copy them and their work-unit prefix into `workspace`
+ * (device memory of at least zt_plan_workspace_bytes(n_tensors), 16-byte aligned)
+ * and fill `plan`. The workspace must outlive every pass that uses the plan. */
+ZT_API int zt_plan_init(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_params,
+                 void* workspace, size_t workspace_bytes, zt_plan* plan, void* stream);
+
+/* ---- the fused pass ----------------------------------------------------------------- */
+
+/* Roles of a noise stream inside one pass (flags). */
+#define ZT_STREAM_GE 1   /* contributes ge_coef * z to the gradient estimate */
+#define ZT_STREAM_MOM 2  /* contributes mom_coef * z to the reconstructed momentum */
+
+/* One noise stream: z = the Gaussian field of pair seed `seed`. Streams are applied in
+ * array order. For each stream, the n_chain perturbations theta <- theta + chain[c] * z
+ * (rounded to the parameter dtype after each) come first, then its GE / MOM roles. */
+typedef struct zt_stream {
+  uint64_t seed;
+  float chain[ZT_MAX_CHAIN];
+  int32_t n_chain;
+  float ge_coef;
+  float mom_coef;
+  int32_t flags;
+  int32_t reserved;
+} zt_stream;
+
+/* gradient-estimate accumulation modes */
+#define ZT_GE_NONE 0
+#define ZT_GE_PRODUCT 1  /* ge = z * coef in fp32 (one stream; zotitan/train_zo.py:552) */
+#define ZT_GE_ACCUM 2    /* ge = 0; ge += coef * z rounded to the param dtype (:555-556, :575-577) */
+
+/* first-moment backends (MomentumConfig.momentum_method) */
+#define ZT_MOM_NONE 0
+#define ZT_MOM_STORED_EMA 1
+#define ZT_MOM_SEED_WINDOW 2
+
+/* weight decay (WeightDecayConfig) */
+#define ZT_WD_NONE 0
+#define ZT_WD_STANDARD 1
+#define ZT_WD_ANCHORED_L2 2
+#define ZT_WD_ANCHORED_L1 3
+
+/* source / destination buffers of theta */
+#define ZT_BUF_DATA 1
+#define ZT_BUF_LIVE 2
+
+/* Scalars are fp32 values the caller has already rounded the way torch's
+ * CUDA kernels round a Python scalar (fp32 opmath). */
+typedef struct zt_pass_cfg {
+  int32_t src;          /* ZT_BUF_DATA or ZT_BUF_LIVE: where theta is read */
+  int32_t dst;          /* bitmask of ZT_BUF_DATA | ZT_BUF_LIVE: where theta is written */
+  int32_t ge_mode;      /* ZT_GE_* */
+  int32_t ge_scale_on;  /* multiply ge by ge_scale after accumulation (norm clipping, :457) */
+  float ge_scale;
+  int32_t momentum;     /* ZT_MOM_*; requires update */
+  float beta1;          /* stored EMA: m <- m*beta1; m <- m + one_minus_beta1*ge (:418-419) */
+  float one_minus_beta1;
+  float m_scale;        /* stored EMA: m_t = m * m_scale, m_scale = fp32(1/fp32(1-beta1^t+denom_eps)):
+                         torch's CUDA tensor/scalar division multiplies by the reciprocal (:331) */
+  int32_t second_moment;
+  float beta2;          /* v <- v*beta2; v <- v + one_minus_beta2*ge*ge (:424-425) */
+  float one_minus_beta2;
+  float bc2;            /* fp32(1 - beta2^t) (:393) */
+  float denom_eps;      /* (:396) */
+  int32_t update;       /* apply the parameter update (:376-407) */
+  float lr;             /* fp32(lr) */
+  int32_t wd;           /* ZT_WD_* */
+  float wd_lam;         /* fp32(fp32(lambda) * lr) (:390) */
+  float wd_factor;      /* fp32(1 - wd_lam) (:402) */
+} zt_pass_cfg;
+
+/* One fused pass over every element of every tensor of `plan`:
+ *   1. theta = src buffer;
+ *   2. for each stream in order: regenerate z in registers, apply its chain to theta,
+ *      accumulate its ge / momentum contributions (noise is never written to memory);
+ *   3. optional ge scaling, optimizer state (m, v) update and parameter update with
+ *      weight decay, in the reference's op order (zotitan/train_zo.py:409-425, 376-407);
+ *   4. theta to every buffer in `dst`.
+ * Replaces, per call, any run of _apply_z (:350-351), the grad_est accumulation
+ * (:550-556, :575-577), _update_optimizer_state (:409-425), _get_gradient_ema (:324-346)
+ * and _apply_update (:376-407) that the caller fuses. */
+ZT_API int zt_pass(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* streams, int32_t n_streams,
+            void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ZOTITAN_B200_H */

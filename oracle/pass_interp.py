@@ -1,0 +1,71 @@
+"""Oracle interpreter of one fused pass (test infrastructure only).
+
+Executes the semantics that include/zotitan_b200.h documents for ``zt_pass``, one
+reference op at a time through the C oracle routines, over numpy carriers with z
+materialised. Used to check (a) on CPU, that the host planner's pass schedule
+reproduces the op-by-op optimizer step (oracle/zo_step.py), and (b) on GPU, that the
+CUDA pass computes bit-identical results given the same noise.
+
+tensors: list of dicts with keys data, live, m, v, anchor (numpy fp32 carriers or
+None), dtype (oracle.philox code) and index. cfg / streams: any objects with the
+attribute names of zotitan_b200.kernels.PassCfg / Stream.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import philox as ph
+
+GE_NONE, GE_PRODUCT, GE_ACCUM = 0, 1, 2
+MOM_NONE, MOM_STORED_EMA, MOM_SEED_WINDOW = 0, 1, 2
+WD_NONE, WD_STANDARD, WD_ANCHORED_L2, WD_ANCHORED_L1 = 0, 1, 2, 3
+BUF_DATA, BUF_LIVE = 1, 2
+
+
+def run_pass(tensors, n_params, cfg, streams, noise=ph.randn):
+    for t in tensors:
+        dt, n = t["dtype"], t["data"].size
+        src = t["live"] if cfg.src == BUF_LIVE else t["data"]
+        th = np.ascontiguousarray(src, dtype=np.float32).reshape(-1).copy()
+        ge = np.zeros(n, np.float32)
+        mom = np.zeros(n, np.float32)
+        for s in streams:
+            z = noise(ph.param_key(s.seed, n_params, t["index"]), n)
+            for a in s.chain:
+                ph.add_scaled_(dt, th, z, a)
+            if s.ge is not None:
+                if cfg.ge_mode == GE_PRODUCT:
+                    ge = ph.mul_scalar(ph.F32, z, s.ge)
+                else:
+                    ph.add_scaled_(dt, ge, z, s.ge)
+            if s.mom is not None:
+                ph.add_scaled_(dt, mom, z, s.mom)
+        if cfg.ge_scale is not None:
+            ge = ph.mul_scalar(ph.F32 if cfg.ge_mode == GE_PRODUCT else dt, ge, cfg.ge_scale)
+        if cfg.update:
+            if cfg.momentum == MOM_STORED_EMA:
+                m = ph.mul_scalar(dt, t["m"].reshape(-1).astype(np.float32), cfg.beta1)
+                ph.add_scaled_(dt, m, ge, cfg.one_minus_beta1)
+                t["m"][...] = m.reshape(t["m"].shape)
+                g = ph.mul_scalar(dt, m, cfg.m_scale)
+            elif cfg.momentum == MOM_SEED_WINDOW:
+                g = mom
+            else:
+                g = ge
+            if cfg.second_moment:
+                v = ph.mul_scalar(dt, t["v"].reshape(-1).astype(np.float32), cfg.beta2)
+                ph.addcmul_(dt, v, ge, ge, cfg.one_minus_beta2)
+                t["v"][...] = v.reshape(t["v"].shape)
+                vh = ph.div_scalar(dt, v, cfg.bc2)
+                ph.sqrt_add_(dt, vh, cfg.denom_eps)
+                ph.addcdiv_(dt, th, g, vh, -cfg.lr)
+            else:
+                ph.add_scaled_(dt, th, np.ascontiguousarray(g, dtype=np.float32), -cfg.lr)
+            if cfg.wd == WD_STANDARD:
+                th = ph.mul_scalar(dt, th, cfg.wd_factor)
+            elif cfg.wd in (WD_ANCHORED_L1, WD_ANCHORED_L2):
+                ph.anchored_(dt, th, t["anchor"].reshape(-1).astype(np.float32), cfg.wd_lam, cfg.wd == WD_ANCHORED_L1)
+        if cfg.dst & BUF_DATA:
+            t["data"][...] = th.reshape(t["data"].shape)
+        if cfg.dst & BUF_LIVE:
+            t["live"][...] = th.reshape(t["live"].shape)

@@ -1,0 +1,90 @@
+"""The C-ABI library loads and exports what include/zotitan_b200.h declares (CPU only:
+no call here launches GPU work; only argument validation paths run)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from zotitan_b200 import _lib as L
+from zotitan_b200.build import build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()
+    return L.load()
+
+
+def declared_functions():
+    src = open(os.path.join(ROOT, "include", "zotitan_b200.h")).read()
+    return sorted(set(re.findall(r"^ZT_API [^(]*?\b(zt_\w+)\(", src, flags=re.M)))
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared_functions()
+    assert names, "no declarations found"
+    assert sorted(L.EXPORTS) == names
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_abi_version_and_key(lib):
+    assert lib.zt_abi_version() == 1
+    from oracle import philox as ph
+    for seed, n, i in [(0, 1, 0), (1234, 39, 7), (2**40 + 3, 146, 145), (2**64 - 1, 448, 3)]:
+        assert lib.zt_param_key(seed, n, i) == ph.param_key(seed, n, i) == (seed * n + i) & 0x7FFFFFFF
+
+
+def test_struct_layouts_match_header(lib):
+    assert ctypes.sizeof(L.ZtTensor) == 56
+    assert ctypes.sizeof(L.ZtStream) == 40
+    assert ctypes.sizeof(L.ZtPlan) == 48
+    assert ctypes.sizeof(L.ZtPassCfg) == 19 * 4
+    assert lib.zt_plan_workspace_bytes(0) == 8
+    assert lib.zt_plan_workspace_bytes(3) == 256 + 8 * 4
+
+
+def test_invalid_arguments_are_reported(lib):
+    assert lib.zt_randn(1, 0, -1, None, None) == L.ZT_ERR_INVALID
+    assert b"negative" in lib.zt_last_error()
+    assert lib.zt_randn(1, 2**31 - 10, 100, None, None) == L.ZT_ERR_LIMIT
+    assert lib.zt_randn(1, 0, 0, None, None) == L.ZT_OK          # empty is a no-op
+    assert lib.zt_last_error() == b""
+    assert lib.zt_pass(None, None, None, 0, None) == L.ZT_ERR_INVALID
+    plan = L.ZtPlan()
+    cfg = L.ZtPassCfg()
+    cfg.src, cfg.dst = L.ZT_BUF_DATA, L.ZT_BUF_DATA
+    assert lib.zt_pass(ctypes.byref(plan), ctypes.byref(cfg), None, 300, None) == L.ZT_ERR_INVALID
+    arr = (L.ZtStream * 1)()
+    assert lib.zt_pass(ctypes.byref(plan), ctypes.byref(cfg), arr, 300, None) == L.ZT_ERR_LIMIT
+    cfg.src = 7
+    assert lib.zt_pass(ctypes.byref(plan), ctypes.byref(cfg), arr, 1, None) == L.ZT_ERR_INVALID
+    cfg.src, cfg.momentum, cfg.update = L.ZT_BUF_DATA, L.ZT_MOM_STORED_EMA, 0
+    assert lib.zt_pass(ctypes.byref(plan), ctypes.byref(cfg), arr, 1, None) == L.ZT_ERR_INVALID
+    assert b"require update" in lib.zt_last_error()
+    t = (L.ZtTensor * 1)()
+    t[0].numel, t[0].dtype, t[0].index, t[0].data = 2**31, L.ZT_BF16, 0, 16
+    out = L.ZtPlan()
+    assert lib.zt_plan_init(t, 1, 1, ctypes.c_void_p(256), 4096, ctypes.byref(out), None) == L.ZT_ERR_LIMIT
+    t[0].numel, t[0].index = 10, 5
+    assert lib.zt_plan_init(t, 1, 1, ctypes.c_void_p(256), 4096, ctypes.byref(out), None) == L.ZT_ERR_INVALID
+    assert lib.zt_plan_init(t, 1, 1, ctypes.c_void_p(256), 8, ctypes.byref(out), None) == L.ZT_ERR_INVALID
+
+
+def test_missing_library_raises(tmp_path, monkeypatch):
+    """No CPU fallback: a missing library is an error, not a silent torch path."""
+    monkeypatch.setattr(L, "_lib", None)
+    monkeypatch.setattr(L, "LIB_PATH", str(tmp_path / "nope.so"))
+    with pytest.raises(L.ZtError, match="no CPU fallback"):
+        L.load()
+
+
+def test_optimizer_refuses_cpu_tensors():
+    import torch
+    from zotitan_b200.train_zo import ZOConfig, ZOOptimizer
+    p = torch.nn.Parameter(torch.zeros(4))
+    with pytest.raises(ValueError, match="CUDA"):
+        ZOOptimizer([("w", p)], ZOConfig(), score_fn=None)

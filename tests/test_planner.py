@@ -1,0 +1,156 @@
+"""Host planner (zotitan_b200.train_zo.StepPlanner) vs the op-by-op oracle step, on CPU.
+
+The planner decides every fused pass of a step (which seeds, which perturbation
+chains, which gradient / momentum coefficients, which scalars). Executed through the
+oracle's pass interpreter, that schedule must reproduce the oracle's restatement of
+the reference step bit for bit, for every optimizer branch, in the single-GPU
+schedule and in the seed-sharded schedule (the sharded master must end each step
+bit-identical to the single-GPU result).
+"""
+import numpy as np
+import pytest
+
+from helpers import StepCase, flat, step_cases
+from oracle import philox as ph
+from oracle.pass_interp import run_pass
+from oracle.zo_step import OracleZO
+from zotitan_b200.train_zo import StepPlanner
+
+_G, _NAMES = step_cases()
+GAUSSIAN = [n for n in _NAMES if "lowrank" not in n]
+
+
+def make_tensors(params, dtypes, planner, sharded):
+    ts = []
+    for i, (p, dt) in enumerate(zip(params, dtypes)):
+        ts.append({"data": p, "live": p.copy() if sharded else None,
+                   "m": np.zeros_like(p) if planner.needs_m else None,
+                   "v": np.zeros_like(p) if planner.needs_v else None,
+                   "anchor": p.copy() if planner.needs_anchor else None,
+                   "dtype": dt, "index": i})
+    return ts
+
+
+def run_planner(case, world, rank=0):
+    params = case.params()
+    pl = StepPlanner(case.cfg, total_steps=case.spec["total_steps"], rank=rank, world=world)
+    ts = make_tensors(params, case.dtypes, pl, world > 1)
+    n = len(params)
+    vals_all = iter(case.values)
+    afters, metrics, snaps = [], [], []
+    for _ in range(case.spec["steps"]):
+        local = pl.start()
+        Z = case.cfg.z_batch
+        vals = [next(vals_all) for _ in range(2 * Z)]
+        prev = None
+        for j in local:
+            run_pass(ts, n, *_spec(pl.plus_pass(j, prev)))
+            snaps.append(flat([t["live"] if world > 1 else t["data"] for t in ts]))
+            run_pass(ts, n, *_spec(pl.minus_pass(j)))
+            snaps.append(flat([t["live"] if world > 1 else t["data"] for t in ts]))
+            prev = j
+        spec, m = pl.finish(vals)
+        run_pass(ts, n, spec.cfg, spec.streams)
+        afters.append(flat(params))
+        if world > 1:
+            assert np.array_equal(flat([t["live"] for t in ts]), afters[-1])
+        metrics.append(m)
+    return afters, metrics, snaps
+
+
+def _spec(s):
+    return s.cfg, s.streams
+
+
+def run_oracle(case):
+    params = case.params()
+    opt = OracleZO(params, case.dtypes, case.cfg, total_steps=case.spec["total_steps"], noise="c", semantics="cuda")
+    opt.record_trace = True
+    it = iter(case.values)
+    afters, metrics = [], []
+    for _ in range(case.spec["steps"]):
+        metrics.append(opt.step(lambda ps, b: (next(it), {}), [None] * case.cfg.z_batch))
+        afters.append(flat(params))
+    return afters, metrics, [flat(t) for t in opt.trace]
+
+
+@pytest.mark.parametrize("name", GAUSSIAN)
+def test_single_gpu_schedule_bit_exact(name):
+    case = StepCase(_G, name)
+    a_pl, m_pl, s_pl = run_planner(case, world=1)
+    a_or, m_or, s_or = run_oracle(case)
+    for a, b in zip(a_pl, a_or):
+        assert np.array_equal(a, b)
+    # every forward sees exactly the reference's perturbed parameters
+    assert len(s_pl) == len(s_or)
+    for a, b in zip(s_pl, s_or):
+        assert np.array_equal(a, b)
+    for x, y in zip(m_pl, m_or):
+        for k in ("loss", "proj_grad", "proj_grad_clipped", "clip_frac", "lr", "clip_tau"):
+            assert x[k] == y[k], k
+
+
+@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("name", ["mezo_bf16_z3", "seedwin_adam_bf16_z2", "clip_norm_bf16", "es_rank_f32",
+                                  "wd_anchored_l1_bf16", "ema_adam_f32_z2"])
+def test_sharded_schedule_master_matches_single_gpu(name, world):
+    """Seed-sharded: each rank perturbs a live copy; the final pass replays every pair's
+    rounding chain on the master, so every rank ends bit-identical to one GPU."""
+    case = StepCase(_G, name)
+    a1, m1, _ = run_planner(case, world=1)
+    for rank in range(world):
+        aw, mw, snaps = run_planner(case, world=world, rank=rank)
+        for a, b in zip(aw, a1):
+            assert np.array_equal(a, b), rank
+        for x, y in zip(mw, m1):
+            assert x["proj_grad"] == y["proj_grad"]
+
+
+def test_sharded_first_local_pair_sees_reference_perturbation():
+    """The first pair a rank evaluates is perturbed from the step's starting parameters,
+    exactly like the reference's first pair."""
+    case = StepCase(_G, "mezo_bf16_z3")
+    _, _, s_or = run_oracle(case)
+    _, _, s_w = run_planner(case, world=2, rank=0)
+    assert np.array_equal(s_w[0], s_or[0]) and np.array_equal(s_w[1], s_or[1])
+
+
+def test_planner_rejects_unsupported():
+    from helpers import ns
+    cfg = StepCase(_G, "mezo_f32_z1").cfg_dict
+    cfg["perturbation"]["distribution"] = "low_rank"
+    with pytest.raises(NotImplementedError):
+        StepPlanner(ns(cfg))
+    cfg["perturbation"]["distribution"] = "gaussian"
+    cfg["fitness"]["strategy"] = "centered_rank"
+    cfg["shared_batch"] = False
+    with pytest.raises(AssertionError):
+        StepPlanner(ns(cfg))
+
+
+def test_planner_stream_limit():
+    from helpers import ns
+    cfg = StepCase(_G, "mezo_f32_z1").cfg_dict
+    cfg["z_batch"] = 300
+    pl = StepPlanner(ns(cfg))
+    pl.start()
+    with pytest.raises(ValueError, match="noise streams"):
+        pl.finish([1.0, 0.5] * 300)
+
+
+def test_planner_state_dict_roundtrip():
+    """Exact resume: a planner restored from state_dict continues the same seed / window."""
+    case = StepCase(_G, "seedwin_adam_bf16_z2")
+    pl = StepPlanner(case.cfg)
+    vals = iter(case.values)
+    for _ in range(2):
+        pl.start()
+        pl.finish([next(vals) for _ in range(4)])
+    sd = pl.state_dict()
+    pl2 = StepPlanner(case.cfg)
+    pl2.load_state_dict(sd)
+    v = [next(vals) for _ in range(4)]
+    pl.start(); pl2.start()
+    s1, _ = pl.finish(v)
+    s2, _ = pl2.finish(v)
+    assert [(s.seed, s.chain, s.ge, s.mom) for s in s1.streams] == [(s.seed, s.chain, s.ge, s.mom) for s in s2.streams]

@@ -1,0 +1,101 @@
+"""ctypes binding of ``libzotitan_b200.so`` (the C ABI in include/zotitan_b200.h).
+
+There is no fallback: if the library is missing or fails to load, every entry
+point raises. Structures mirror the header field for field.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libzotitan_b200.so")
+
+ZT_F32, ZT_BF16, ZT_F16 = 0, 1, 2
+ZT_OK, ZT_ERR_INVALID, ZT_ERR_CUDA, ZT_ERR_LIMIT = 0, 1, 2, 3
+ZT_MAX_STREAMS = 256
+ZT_MAX_CHAIN = 3
+ZT_MAX_NUMEL = 2**31 - 1
+ZT_UNIT_ELEMS = 2048
+ZT_STREAM_GE, ZT_STREAM_MOM = 1, 2
+ZT_GE_NONE, ZT_GE_PRODUCT, ZT_GE_ACCUM = 0, 1, 2
+ZT_MOM_NONE, ZT_MOM_STORED_EMA, ZT_MOM_SEED_WINDOW = 0, 1, 2
+ZT_WD_NONE, ZT_WD_STANDARD, ZT_WD_ANCHORED_L2, ZT_WD_ANCHORED_L1 = 0, 1, 2, 3
+ZT_BUF_DATA, ZT_BUF_LIVE = 1, 2
+
+# every function include/zotitan_b200.h declares
+EXPORTS = ("zt_last_error", "zt_abi_version", "zt_param_key", "zt_philox_words", "zt_randn",
+           "zt_randn_at", "zt_plan_workspace_bytes", "zt_plan_init", "zt_pass")
+
+
+class ZtTensor(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("live", ctypes.c_void_p), ("m", ctypes.c_void_p),
+                ("v", ctypes.c_void_p), ("anchor", ctypes.c_void_p), ("numel", ctypes.c_int64),
+                ("dtype", ctypes.c_int32), ("index", ctypes.c_int32)]
+
+
+class ZtPlan(ctypes.Structure):
+    _fields_ = [("tensors", ctypes.c_void_p), ("unit_prefix", ctypes.c_void_p), ("n_units", ctypes.c_int64),
+                ("numel_total", ctypes.c_int64), ("n_tensors", ctypes.c_int32), ("n_params", ctypes.c_uint32),
+                ("device", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
+class ZtStream(ctypes.Structure):
+    _fields_ = [("seed", ctypes.c_uint64), ("chain", ctypes.c_float * ZT_MAX_CHAIN), ("n_chain", ctypes.c_int32),
+                ("ge_coef", ctypes.c_float), ("mom_coef", ctypes.c_float), ("flags", ctypes.c_int32),
+                ("reserved", ctypes.c_int32)]
+
+
+class ZtPassCfg(ctypes.Structure):
+    _fields_ = [("src", ctypes.c_int32), ("dst", ctypes.c_int32), ("ge_mode", ctypes.c_int32),
+                ("ge_scale_on", ctypes.c_int32), ("ge_scale", ctypes.c_float), ("momentum", ctypes.c_int32),
+                ("beta1", ctypes.c_float), ("one_minus_beta1", ctypes.c_float), ("m_scale", ctypes.c_float),
+                ("second_moment", ctypes.c_int32), ("beta2", ctypes.c_float), ("one_minus_beta2", ctypes.c_float),
+                ("bc2", ctypes.c_float), ("denom_eps", ctypes.c_float), ("update", ctypes.c_int32),
+                ("lr", ctypes.c_float), ("wd", ctypes.c_int32), ("wd_lam", ctypes.c_float),
+                ("wd_factor", ctypes.c_float)]
+
+
+class ZtError(RuntimeError):
+    """A C-ABI call returned a nonzero status."""
+
+
+_lib = None
+
+
+def load():
+    """Load the library once; raise if it is absent (no CPU fallback exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ZtError(f"{LIB_PATH} is missing: build it with `python -m zotitan_b200.build` "
+                      "(the zeroth-order kernels have no CPU fallback)")
+    lib = ctypes.CDLL(LIB_PATH)
+    P, I32, I64, U32, U64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32, ctypes.c_uint64
+    lib.zt_last_error.restype = ctypes.c_char_p
+    lib.zt_last_error.argtypes = []
+    lib.zt_abi_version.restype = ctypes.c_int
+    lib.zt_param_key.restype = U32
+    lib.zt_param_key.argtypes = [U64, U32, U32]
+    for name, args in [("zt_philox_words", [U32, P, I64, P, P]), ("zt_randn", [U32, I64, I64, P, P]),
+                       ("zt_randn_at", [U32, P, I64, P, P]),
+                       ("zt_plan_init", [ctypes.POINTER(ZtTensor), I32, U32, P, ctypes.c_size_t,
+                                         ctypes.POINTER(ZtPlan), P]),
+                       ("zt_pass", [ctypes.POINTER(ZtPlan), ctypes.POINTER(ZtPassCfg), ctypes.POINTER(ZtStream),
+                                    I32, P])]:
+        fn = getattr(lib, name)
+        fn.restype = ctypes.c_int
+        fn.argtypes = args
+    lib.zt_plan_workspace_bytes.restype = ctypes.c_size_t
+    lib.zt_plan_workspace_bytes.argtypes = [I32]
+    if lib.zt_abi_version() != 1:
+        raise ZtError(f"{LIB_PATH}: ABI version {lib.zt_abi_version()} != 1")
+    _lib = lib
+    return lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != ZT_OK:
+        msg = load().zt_last_error().decode(errors="replace")
+        raise ZtError(f"{what} failed with status {rc}: {msg}")

@@ -1,0 +1,50 @@
+// Error reporting, version and small host utilities of the C ABI.
+#include <mutex>
+
+#include "zt_common.cuh"
+#include "zt_philox.cuh"
+
+namespace zt {
+
+static thread_local std::string g_last_error;
+
+int set_error(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+void clear_error() { g_last_error.clear(); }
+
+int check_cuda(cudaError_t st, const char* what) {
+  if (st == cudaSuccess) return ZT_OK;
+  return set_error(ZT_ERR_CUDA, std::string(what) + ": " + cudaGetErrorName(st) + " (" +
+                                    cudaGetErrorString(st) + ")");
+}
+
+int sm_count() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+}  // namespace zt
+
+extern "C" {
+
+const char* zt_last_error(void) { return zt::g_last_error.c_str(); }
+
+int zt_abi_version(void) { return ZT_ABI_VERSION; }
+
+uint32_t zt_param_key(uint64_t seed, uint32_t n_params, uint32_t index) {
+  return zt::param_key(seed, n_params, index);
+}
+
+}  // extern "C"

@@ -1,0 +1,175 @@
+"""Thin torch-facing wrappers over the C ABI (include/zotitan_b200.h).
+
+Every call is enqueued on torch's current CUDA stream; none synchronises.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib as L
+
+_DT = {torch.float32: L.ZT_F32, torch.bfloat16: L.ZT_BF16, torch.float16: L.ZT_F16}
+
+
+def _stream_ptr(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def param_key(seed: int, n_params: int, index: int) -> int:
+    """(seed * n_params + index) & 0x7FFFFFFF with uint64 wrap-around (train_zo.py:302)."""
+    return int(L.load().zt_param_key(seed & 0xFFFFFFFFFFFFFFFF, n_params, index))
+
+
+def _check_cuda(t: torch.Tensor, name: str):
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+
+
+def philox_words(key: int, offsets: torch.Tensor) -> torch.Tensor:
+    """[n, 4] int32 tensor holding the uint32 Philox words at `offsets` (int32/uint32 bits)."""
+    _check_cuda(offsets, "offsets")
+    offs = offsets.to(torch.int32).contiguous()
+    out = torch.empty((offs.numel(), 4), dtype=torch.int32, device=offs.device)
+    L.check(L.load().zt_philox_words(key, offs.data_ptr(), offs.numel(), out.data_ptr(), _stream_ptr(offs.device)),
+            "zt_philox_words")
+    return out
+
+
+def randn(key: int, n: int, device, off0: int = 0) -> torch.Tensor:
+    """The reference's ``_philox_randn(key, n)`` (zotitan/train_zo.py:25-28), offsets off0..off0+n-1."""
+    device = torch.device(device)
+    out = torch.empty(n, dtype=torch.float32, device=device)
+    L.check(L.load().zt_randn(key, off0, n, out.data_ptr() if n else None, _stream_ptr(device)), "zt_randn")
+    return out
+
+
+def randn_at(key: int, offsets: torch.Tensor) -> torch.Tensor:
+    _check_cuda(offsets, "offsets")
+    offs = offsets.to(torch.int32).contiguous()
+    out = torch.empty(offs.numel(), dtype=torch.float32, device=offs.device)
+    L.check(L.load().zt_randn_at(key, offs.data_ptr(), offs.numel(), out.data_ptr(), _stream_ptr(offs.device)),
+            "zt_randn_at")
+    return out
+
+
+@dataclass
+class Stream:
+    """One noise stream of a pass (see zt_stream)."""
+    seed: int
+    chain: tuple = ()
+    ge: float | None = None
+    mom: float | None = None
+
+    def to_c(self) -> L.ZtStream:
+        if len(self.chain) > L.ZT_MAX_CHAIN:
+            raise ValueError("at most 3 chained perturbations per stream")
+        s = L.ZtStream()
+        s.seed = self.seed & 0xFFFFFFFFFFFFFFFF
+        for k, a in enumerate(self.chain):
+            s.chain[k] = a
+        s.n_chain = len(self.chain)
+        s.flags = (L.ZT_STREAM_GE if self.ge is not None else 0) | (L.ZT_STREAM_MOM if self.mom is not None else 0)
+        s.ge_coef = self.ge if self.ge is not None else 0.0
+        s.mom_coef = self.mom if self.mom is not None else 0.0
+        return s
+
+
+@dataclass
+class PassCfg:
+    """Python view of zt_pass_cfg; scalars must already be fp32-representable."""
+    src: int = L.ZT_BUF_DATA
+    dst: int = L.ZT_BUF_DATA
+    ge_mode: int = L.ZT_GE_NONE
+    ge_scale: float | None = None
+    momentum: int = L.ZT_MOM_NONE
+    beta1: float = 0.0
+    one_minus_beta1: float = 0.0
+    m_scale: float = 1.0
+    second_moment: bool = False
+    beta2: float = 0.0
+    one_minus_beta2: float = 0.0
+    bc2: float = 1.0
+    denom_eps: float = 0.0
+    update: bool = False
+    lr: float = 0.0
+    wd: int = L.ZT_WD_NONE
+    wd_lam: float = 0.0
+    wd_factor: float = 1.0
+
+    def to_c(self) -> L.ZtPassCfg:
+        c = L.ZtPassCfg()
+        c.src, c.dst, c.ge_mode = self.src, self.dst, self.ge_mode
+        c.ge_scale_on = int(self.ge_scale is not None)
+        c.ge_scale = self.ge_scale if self.ge_scale is not None else 1.0
+        c.momentum, c.beta1, c.one_minus_beta1, c.m_scale = self.momentum, self.beta1, self.one_minus_beta1, self.m_scale
+        c.second_moment, c.beta2, c.one_minus_beta2 = int(self.second_moment), self.beta2, self.one_minus_beta2
+        c.bc2, c.denom_eps, c.update, c.lr = self.bc2, self.denom_eps, int(self.update), self.lr
+        c.wd, c.wd_lam, c.wd_factor = self.wd, self.wd_lam, self.wd_factor
+        return c
+
+
+class ParamTable:
+    """A zt_plan over trainable tensors, resident on their device.
+
+    params[i] is the tensor at position indices[i] of an n_params-long trainable list
+    (the reference's ``named_params``; the index feeds the per-tensor noise key).
+    Optional parallel lists: live (second copy read by the model), m, v, anchor.
+    The table keeps references to every tensor, so the pointers stay valid.
+    """
+
+    def __init__(self, params, n_params=None, indices=None, live=None, m=None, v=None, anchor=None):
+        params = list(params)
+        if not params:
+            raise ValueError("empty parameter list")
+        self.device = params[0].device
+        if self.device.type != "cuda":
+            raise ValueError("ParamTable needs CUDA tensors (no CPU fallback)")
+        self.n_params = len(params) if n_params is None else n_params
+        self.indices = list(range(len(params))) if indices is None else list(indices)
+        self.params, self.live, self.m, self.v, self.anchor = params, live, m, v, anchor
+        arr = (L.ZtTensor * len(params))()
+        for i, p in enumerate(params):
+            self._check(p, p, f"param {i}")
+            arr[i].data = p.data_ptr()
+            for name in ("live", "m", "v", "anchor"):
+                lst = getattr(self, name)
+                if lst is not None and lst[i] is not None:
+                    self._check(lst[i], p, f"{name}[{i}]")
+                    setattr(arr[i], name, lst[i].data_ptr())
+            arr[i].numel = p.numel()
+            arr[i].dtype = _DT[p.dtype]
+            arr[i].index = self.indices[i]
+        self._host = arr
+        lib = L.load()
+        nbytes = lib.zt_plan_workspace_bytes(len(params))
+        self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        self.plan = L.ZtPlan()
+        with torch.cuda.device(self.device):
+            L.check(lib.zt_plan_init(arr, len(params), self.n_params, self.workspace.data_ptr(), nbytes,
+                                     ctypes.byref(self.plan), _stream_ptr(self.device)), "zt_plan_init")
+        self.numel = int(self.plan.numel_total)
+
+    def _check(self, t: torch.Tensor, like: torch.Tensor, name: str):
+        if t.device != self.device:
+            raise ValueError(f"{name} is on {t.device}, expected {self.device}")
+        if t.dtype not in _DT:
+            raise ValueError(f"{name} has unsupported dtype {t.dtype}")
+        if t.dtype != like.dtype or t.numel() != like.numel():
+            raise ValueError(f"{name} must match its parameter's dtype and numel")
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+
+    def run(self, cfg: PassCfg, streams: list[Stream]) -> None:
+        """One fused pass (zt_pass) on torch's current stream."""
+        if len(streams) > L.ZT_MAX_STREAMS:
+            raise ValueError(f"{len(streams)} noise streams > {L.ZT_MAX_STREAMS}")
+        arr = (L.ZtStream * max(1, len(streams)))()
+        for i, s in enumerate(streams):
+            arr[i] = s.to_c()
+        c = cfg.to_c()
+        with torch.cuda.device(self.device):
+            L.check(L.load().zt_pass(ctypes.byref(self.plan), ctypes.byref(c), arr, len(streams),
+                                     _stream_ptr(self.device)), "zt_pass")

@@ -1,0 +1,566 @@
+"""Zeroth-order optimizer with the reference's API on B200-native fused passes.
+
+Drop-in for zotitan/train_zo.py: the config tree (``ZOConfig`` and its sub-configs,
+field for field, :30-197), ``ZOOptimizer(named_params, cfg, score_fn, total_steps)``
+with ``.step(model, batches) -> dict`` (:242-606) and ``train_zo(...)`` (:609-675).
+
+What changes underneath: the reference materialises fp32 noise for every tensor
+with a Triton kernel and applies it with torch foreach ops (3 passes per pair plus a
+grad_est buffer, momentum replay and the update). Here every pass is one
+``zt_pass`` launch over all trainable tensors that regenerates the noise in
+registers (include/zotitan_b200.h):
+
+  pair j:    [restore of pair j-1 (+eps z_{j-1}) fused with] +eps z_j ; score ;
+             -2eps z_j ; score
+  step end:  restore of the last pair + gradient estimate from all pair seeds +
+             momentum replay + (m, v) update + parameter update + weight decay,
+             one pass, no noise or grad_est in memory.
+
+Arithmetic follows the reference's eager op order with the fp32 opmath scalars of
+torch's CUDA kernels (tensor / Python scalar multiplies by the fp32 reciprocal),
+one rounding to the parameter dtype per reference op.
+
+Seed sharding (torch.distributed initialised with world size W > 1): rank r
+evaluates pairs j = r, r+W, ...; the model reads a second ("live") copy of the
+trainable tensors while the master copy stays unperturbed; one all-gather shares
+the pair values; every rank then runs the same final pass over the master, which
+also replays every pair's +eps/-2eps/+eps rounding chain so the result equals the
+single-GPU sequence, and writes master and live.
+"""
+from __future__ import annotations
+
+import collections
+import math
+import os
+import time
+from dataclasses import dataclass, field
+from typing import Literal
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from .data import PrefetchLoader, get_batches
+from .distributed import gather_pair_values, local_pairs, world_info
+from .kernels import ParamTable, PassCfg, Stream
+from .schedule import BaseTrainConfig, wsd_is_constant, wsd_value
+
+
+# ── configuration (zotitan/train_zo.py:30-197, field for field) ───────────────
+
+@dataclass
+class MomentumConfig:
+    momentum_method: Literal["none", "stored_ema", "seed_window"] = "none"
+    """none | stored_ema (full EMA buffer m) | seed_window (m rebuilt from recent seeds)."""
+    beta1: float = 0.9
+    beta2: float = 0.999
+    second_moment: bool = False
+    """Materialised EMA v of grad_est^2; the update divides by the bias-corrected sqrt(v)."""
+    denom_eps: float = 1e-8
+
+
+@dataclass
+class SeedWindowConfig:
+    size: int = 0
+    """Number of past steps' seeds kept for seed_window momentum (0: unbounded)."""
+
+
+@dataclass
+class ClipConfig:
+    strategy: Literal["none", "per_pair", "norm"] = "none"
+    clip_pct: float = 0.0
+    window: int = 1000
+
+
+@dataclass
+class PerturbationConfig:
+    distribution: Literal["gaussian", "low_rank", "polar"] = "gaussian"
+    rank: int = 64
+
+
+@dataclass
+class WeightDecayConfig:
+    strategy: Literal["none", "standard", "anchored"] = "none"
+    lambda_: float = 0.0
+    penalty: Literal["l2", "l1"] = "l2"
+
+
+@dataclass
+class FitnessShapingConfig:
+    strategy: Literal["none", "centered_rank", "grpo"] = "none"
+    normalize_std: bool = True
+
+
+@dataclass
+class ZOConfig:
+    base: BaseTrainConfig = field(default_factory=lambda: BaseTrainConfig(lr=1e-5, ckpt_every=5_000))
+    eps: float = 1e-3
+    batch_size: int = 40
+    z_batch: int = 1
+    shared_batch: bool = False
+    mom: MomentumConfig = field(default_factory=MomentumConfig)
+    seed_window: SeedWindowConfig = field(default_factory=SeedWindowConfig)
+    perturbation: PerturbationConfig = field(default_factory=PerturbationConfig)
+    clip: ClipConfig = field(default_factory=ClipConfig)
+    fitness: FitnessShapingConfig = field(default_factory=FitnessShapingConfig)
+    weight_decay: WeightDecayConfig = field(default_factory=WeightDecayConfig)
+
+
+# ── host-side planning (no device work; unit-testable on CPU) ───────────────────
+
+def f32(x) -> float:
+    """Round a Python float to fp32, as torch's CUDA kernels take a Scalar (opmath)."""
+    return float(np.float32(x))
+
+
+def f32_recip(x) -> float:
+    """fp32(1 / fp32(x)): the multiplier torch's CUDA division by a Python scalar uses."""
+    return float(np.float32(1.0) / np.float32(x))
+
+
+@dataclass
+class PassSpec:
+    cfg: PassCfg
+    streams: list
+
+
+class StepPlanner:
+    """Host half of ``ZOOptimizer.step``: seed counter, clip history, seed window,
+    fitness shaping, the pass schedule and every scalar the passes take.
+
+    ``world > 1`` selects the seed-sharded schedule (master/live copies)."""
+
+    def __init__(self, cfg: ZOConfig, total_steps: int = 0, rank: int = 0, world: int = 1):
+        if cfg.perturbation.distribution != "gaussian":
+            # The fused passes regenerate Gaussian fields; low-rank / polar directions
+            # (train_zo.py:304-320) are not part of this path.
+            raise NotImplementedError(
+                f"perturbation.distribution={cfg.perturbation.distribution!r} is not supported by the fused "
+                "zeroth-order passes (gaussian only)")
+        self.cfg = cfg
+        self._t = 0
+        self._total_steps = total_steps
+        self._seed_ctr = 0
+        self.rank, self.world = rank, world
+        self.sharded = world > 1
+        self.has_momentum = cfg.mom.momentum_method != "none"
+        self._pg_hist = (collections.deque(maxlen=cfg.clip.window)
+                         if cfg.clip.strategy != "none" and cfg.clip.clip_pct > 0 else None)
+        if cfg.mom.momentum_method == "seed_window":
+            cap = cfg.seed_window.size if cfg.seed_window.size > 0 else None
+            self.seed_buf = collections.deque(maxlen=cap)
+            self.proj_buf = collections.deque(maxlen=cap)
+        self.shaping = cfg.fitness.strategy != "none"
+        if self.shaping:
+            assert cfg.shared_batch, (
+                f"{cfg.fitness.strategy} fitness shaping requires shared_batch=True, because the population "
+                "transform is only comparable when all z are scored on the same batch.")
+            assert not (cfg.clip.strategy != "none" and cfg.clip.clip_pct > 0), \
+                f"{cfg.fitness.strategy} fitness shaping is mutually exclusive with proj_grad clipping."
+        wd = cfg.weight_decay
+        self.wd_enabled = wd.strategy != "none" and wd.lambda_ > 0
+        self.needs_m = cfg.mom.momentum_method == "stored_ema"
+        self.needs_v = cfg.mom.second_moment
+        self.needs_anchor = wd.strategy == "anchored" and self.wd_enabled
+
+    # -- reference helpers (zotitan/train_zo.py:287-293, 427-508) ----------------
+    def _draw_seeds(self, n):
+        seeds = list(range(self._seed_ctr, self._seed_ctr + n))
+        self._seed_ctr += n
+        return seeds
+
+    def _clip_threshold(self):
+        cc = self.cfg.clip
+        if self._pg_hist is None or not self._pg_hist:
+            return float("inf")
+        xs = sorted(self._pg_hist)
+        return xs[min(len(xs) - 1, int((1.0 - cc.clip_pct) * len(xs)))]
+
+    @staticmethod
+    def _centered_ranks(fitness):
+        n = len(fitness)
+        if n < 2:
+            return [0.0] * n
+        order = sorted(range(n), key=lambda i: fitness[i])
+        ranks = [0.0] * n
+        for r, i in enumerate(order):
+            ranks[i] = r / (n - 1) - 0.5
+        return ranks
+
+    def _shape_fitness(self, vals):
+        u = self._centered_ranks([-v for v in vals])
+        return [u[2 * j + 1] - u[2 * j] for j in range(len(vals) // 2)]
+
+    def _grpo_advantages(self, vals):
+        n = len(vals)
+        mean = sum(vals) / n
+        adv = [mean - v for v in vals]
+        if self.cfg.fitness.normalize_std:
+            std = math.sqrt(sum(a * a for a in adv) / n)
+            adv = [a / (std + 1e-8) for a in adv]
+        return [adv[2 * j + 1] - adv[2 * j] for j in range(n // 2)]
+
+    # -- schedule -------------------------------------------------------------------
+    def start(self) -> list[int]:
+        """Begin a step; returns the pairs this rank evaluates, in order."""
+        self._t += 1
+        cfg = self.cfg
+        self.tau = self._clip_threshold()
+        self.clip_in_loop = cfg.clip.strategy == "per_pair" and math.isfinite(self.tau)
+        self.lr = wsd_value(self._t, self._total_steps, lo=0.0, hi=cfg.base.lr, cfg=cfg.base.lr_wsd)
+        self.seeds = self._draw_seeds(cfg.z_batch)
+        self.local = local_pairs(cfg.z_batch, self.rank, self.world)
+        return self.local
+
+    def plus_pass(self, j: int, prev: int | None) -> PassSpec:
+        """+eps z_j; single-GPU mode also restores the previous pair (+eps z_prev) first."""
+        a = f32(self.cfg.eps)
+        if self.sharded:
+            return PassSpec(PassCfg(src=L.ZT_BUF_DATA, dst=L.ZT_BUF_LIVE), [Stream(self.seeds[j], (a,))])
+        streams = ([Stream(self.seeds[prev], (a,))] if prev is not None else []) + [Stream(self.seeds[j], (a,))]
+        return PassSpec(PassCfg(src=L.ZT_BUF_DATA, dst=L.ZT_BUF_DATA), streams)
+
+    def minus_pass(self, j: int) -> PassSpec:
+        """-2eps z_j (train_zo.py:369)."""
+        a = f32(-2 * self.cfg.eps)
+        buf = L.ZT_BUF_LIVE if self.sharded else L.ZT_BUF_DATA
+        return PassSpec(PassCfg(src=buf, dst=buf), [Stream(self.seeds[j], (a,))])
+
+    def finish(self, vals: list[float]) -> tuple[PassSpec, dict]:
+        """vals = [v+_0, v-_0, v+_1, v-_1, ...] for all pairs (fp32 values). Returns the
+        final pass and the scalar metrics (loss, proj_grad, ..., lr)."""
+        cfg = self.cfg
+        Z = cfg.z_batch
+        mc = cfg.mom
+        eps_inv = f32_recip(2 * cfg.eps)
+        pg, pgc = [], []
+        for j in range(Z):
+            d = np.float32(np.float32(vals[2 * j]) - np.float32(vals[2 * j + 1]))
+            g = np.float32(d * np.float32(eps_inv))  # (L+ - L-) / (2 eps) on CUDA (:544)
+            pg.append(float(g))
+            pgc.append(float(np.float32(min(max(float(g), -self.tau), self.tau))) if self.clip_in_loop else float(g))
+        mean_loss = sum(vals) / len(vals)
+
+        ge_mode = L.ZT_GE_NONE
+        ge_coefs = [None] * Z
+        ge_scale = None
+        if self.shaping:  # (:568-578)
+            pgc = (self._grpo_advantages(vals) if cfg.fitness.strategy == "grpo" else self._shape_fitness(vals))
+            ge_mode = L.ZT_GE_ACCUM
+            ge_coefs = [f32(pgc[j] / Z) for j in range(Z)]
+            clip_frac = 0.0
+        else:
+            if Z == 1:
+                ge_mode = L.ZT_GE_PRODUCT  # grad_est = z * pgc in fp32 (:552)
+                ge_coefs = [f32(pgc[0])]
+            else:
+                ge_mode = L.ZT_GE_ACCUM    # zeros_like(p) += z * (pgc / Z) (:555-556)
+                inv_z = f32_recip(Z)
+                ge_coefs = [float(np.float32(np.float32(pgc[j]) * np.float32(inv_z))) for j in range(Z)]
+            # norm clipping (:453-458) and the lagged history (:461-472)
+            clip = cfg.clip
+            clip_scale = 1.0
+            if clip.strategy == "norm" and math.isfinite(self.tau):
+                pg_norm = math.sqrt(sum(g * g for g in pg))
+                clip_scale = min(1.0, self.tau * math.sqrt(Z) / (pg_norm + 1e-12))
+                if clip_scale < 1.0:
+                    ge_scale = f32(clip_scale)
+                    pgc = [g * clip_scale for g in pgc]
+            if self._pg_hist is not None:
+                self._pg_hist.extend(abs(g) for g in pg)
+            if clip.strategy == "per_pair" and math.isfinite(self.tau):
+                clip_frac = sum(abs(g) > self.tau for g in pg) / Z
+            elif clip.strategy == "norm":
+                clip_frac = float(clip_scale < 1.0)
+            else:
+                clip_frac = 0.0
+
+        # grad_est is consumed by: the update itself (no momentum), the stored EMA, or v.
+        need_ge = (not self.has_momentum) or mc.momentum_method == "stored_ema" or mc.second_moment
+        if not need_ge:
+            ge_mode = L.ZT_GE_NONE
+            ge_scale = None
+
+        # seed-window state (:420-422) and replay weights (:337-345)
+        mom_coefs = {}
+        if mc.momentum_method == "seed_window":
+            self.seed_buf.appendleft(list(self.seeds))
+            self.proj_buf.appendleft(list(pgc))
+            weights = [mc.beta1 ** i for i in range(len(self.seed_buf))]
+            total = sum(weights) + 1e-12
+            for i, (ss, pp, sw) in enumerate(zip(self.seed_buf, self.proj_buf, weights)):
+                w = sw / (len(ss) * total)
+                mom_coefs[i] = [f32(w * p) for p in pp]
+
+        a_pos, a_neg = f32(cfg.eps), f32(-2 * cfg.eps)
+        streams = []
+        for j in range(Z):
+            if self.sharded:
+                chain = (a_pos, a_neg, a_pos)   # replay pair j's rounding chain on the master
+            else:
+                chain = (a_pos,) if j == Z - 1 else ()   # restore of the last pair (:371)
+            streams.append(Stream(self.seeds[j], chain,
+                                  ge_coefs[j] if ge_mode != L.ZT_GE_NONE else None,
+                                  mom_coefs[0][j] if mom_coefs else None))
+        for i in range(1, len(mom_coefs)):
+            for s, c in zip(self.seed_buf[i], mom_coefs[i]):
+                streams.append(Stream(s, (), None, c))
+        if len(streams) > L.ZT_MAX_STREAMS:
+            raise ValueError(f"step needs {len(streams)} noise streams > {L.ZT_MAX_STREAMS} "
+                             "(reduce z_batch or seed_window.size)")
+
+        t = self._t
+        wd = cfg.weight_decay
+        lr32 = f32(self.lr)
+        wd_lam = f32(np.float32(wd.lambda_) * np.float32(lr32))
+        wd_code = L.ZT_WD_NONE
+        if wd.strategy == "standard":
+            wd_code = L.ZT_WD_STANDARD
+        elif wd.strategy == "anchored" and self.wd_enabled:
+            wd_code = L.ZT_WD_ANCHORED_L1 if wd.penalty == "l1" else L.ZT_WD_ANCHORED_L2
+        pcfg = PassCfg(
+            src=L.ZT_BUF_DATA,
+            dst=(L.ZT_BUF_DATA | L.ZT_BUF_LIVE) if self.sharded else L.ZT_BUF_DATA,
+            ge_mode=ge_mode, ge_scale=ge_scale,
+            momentum={"none": L.ZT_MOM_NONE, "stored_ema": L.ZT_MOM_STORED_EMA,
+                      "seed_window": L.ZT_MOM_SEED_WINDOW}[mc.momentum_method],
+            beta1=f32(mc.beta1), one_minus_beta1=f32(1 - mc.beta1),
+            m_scale=f32_recip(f32((1.0 - mc.beta1 ** t) + mc.denom_eps)) if mc.momentum_method == "stored_ema" else 1.0,
+            second_moment=mc.second_moment, beta2=f32(mc.beta2), one_minus_beta2=f32(1 - mc.beta2),
+            bc2=f32(1.0 - mc.beta2 ** t), denom_eps=f32(mc.denom_eps),
+            update=True, lr=lr32, wd=wd_code, wd_lam=wd_lam, wd_factor=f32(1.0 - wd_lam))
+        metrics = {
+            "loss": mean_loss,
+            "proj_grad": sum(pg) / Z,
+            "proj_grad_clipped": sum(pgc) / Z,
+            "clip_frac": clip_frac,
+            "clip_tau": self.tau if math.isfinite(self.tau) else None,
+            "lr": self.lr,
+            **({"fit_rms": (sum(s * s for s in pgc) / Z) ** 0.5} if self.shaping else {}),
+        }
+        return PassSpec(pcfg, streams), metrics
+
+    # -- exact resume: the whole optimizer trajectory is seeds + scalars ---------------
+    def state_dict(self) -> dict:
+        sd = {"t": self._t, "seed_ctr": self._seed_ctr}
+        if self._pg_hist is not None:
+            sd["pg_hist"] = list(self._pg_hist)
+        if self.cfg.mom.momentum_method == "seed_window":
+            sd["seed_buf"] = [list(x) for x in self.seed_buf]
+            sd["proj_buf"] = [list(x) for x in self.proj_buf]
+        return sd
+
+    def load_state_dict(self, sd: dict) -> None:
+        self._t, self._seed_ctr = int(sd["t"]), int(sd["seed_ctr"])
+        if self._pg_hist is not None:
+            self._pg_hist.clear()
+            self._pg_hist.extend(sd.get("pg_hist", []))
+        if self.cfg.mom.momentum_method == "seed_window":
+            self.seed_buf.clear(); self.proj_buf.clear()
+            self.seed_buf.extend(list(x) for x in sd.get("seed_buf", []))
+            self.proj_buf.extend(list(x) for x in sd.get("proj_buf", []))
+
+
+def _aggregate_metrics(dicts: list[dict]) -> dict[str, float]:
+    """Average each metric key over the collected score dicts (train_zo.py:228-239)."""
+    total: dict[str, float] = {}
+    count: dict[str, int] = {}
+    for d in dicts:
+        for k, v in d.items():
+            if v is None:
+                continue
+            total[k] = total.get(k, 0.0) + (v.item() if isinstance(v, torch.Tensor) else float(v))
+            count[k] = count.get(k, 0) + 1
+    return {k: total[k] / count[k] for k in total}
+
+
+# ── the optimizer ─────────────────────────────────────────────────────────────────
+
+class ZOOptimizer:
+    """``ZOOptimizer`` (zotitan/train_zo.py:242-606) on fused CUDA passes.
+
+    ``process_group``: torch.distributed group to shard pairs over; default: the
+    default group when it is initialised with more than one rank."""
+
+    def __init__(self, named_params: list, cfg: ZOConfig, score_fn, total_steps: int = 0, process_group=None):
+        self.named_params = named_params
+        self.params = [p.data for _, p in named_params]
+        self.cfg = cfg
+        self.score_fn = score_fn
+        for n, p in zip([n for n, _ in named_params], self.params):
+            if not p.is_cuda:
+                raise ValueError(f"{n}: the zeroth-order passes run on CUDA tensors only (no CPU fallback)")
+            if not p.is_contiguous():
+                raise ValueError(f"{n}: trainable tensors must be contiguous")
+        self.group = process_group
+        rank, world = world_info(process_group)
+        self.planner = StepPlanner(cfg, total_steps, rank, world)
+        self.rank, self.world = rank, world
+        pl = self.planner
+        self.m = [torch.zeros_like(p) for p in self.params] if pl.needs_m else None
+        self.v = [torch.zeros_like(p) for p in self.params] if pl.needs_v else None
+        # theta_0 for anchored decay stays in HBM (the reference pins it in host
+        # memory and copies it every step, train_zo.py:274, :406)
+        self.theta_0 = [p.clone() for p in self.params] if pl.needs_anchor else None
+        if pl.sharded:
+            # model reads `live` (the parameters' own storage); `master` stays unperturbed
+            self.master = [p.clone() for p in self.params]
+            self.table = ParamTable(self.master, live=self.params, m=self.m, v=self.v, anchor=self.theta_0)
+        else:
+            self.master = None
+            self.table = ParamTable(self.params, m=self.m, v=self.v, anchor=self.theta_0)
+        self._metric_keys = None
+
+    # properties mirroring the reference's attributes
+    @property
+    def _t(self):
+        return self.planner._t
+
+    @property
+    def _seed_ctr(self):
+        return self.planner._seed_ctr
+
+    @_seed_ctr.setter
+    def _seed_ctr(self, v):
+        self.planner._seed_ctr = int(v)
+
+    def _run(self, spec: PassSpec) -> None:
+        self.table.run(spec.cfg, spec.streams)
+
+    def _acquire(self, model, batch):
+        s = self.score_fn(model, batch)
+        value = s.value if isinstance(s.value, torch.Tensor) else torch.tensor(float(s.value))
+        return value, s.metrics
+
+    def step(self, model, batches: list) -> dict:
+        pl = self.planner
+        Z = self.cfg.z_batch
+        if len(batches) != Z:
+            raise ValueError(f"step expects z_batch={Z} batches (entries of other ranks' pairs may be None)")
+        local = pl.start()
+        dev = self.params[0].device
+        vals_t, metric_dicts = [], []
+        prev = None
+        with torch.inference_mode():
+            for j in local:
+                self._run(pl.plus_pass(j, prev))
+                vp, mp = self._acquire(model, batches[j])
+                self._run(pl.minus_pass(j))
+                vn, mn = self._acquire(model, batches[j])
+                prev = j
+                vals_t += [vp.detach().float().reshape(()).to(dev), vn.detach().float().reshape(()).to(dev)]
+                metric_dicts += [mp, mn]
+        if pl.sharded:
+            vals, metrics_avg = self._gather(vals_t, metric_dicts, local)
+        else:
+            vals = torch.stack(vals_t).tolist()          # the step's one host sync (:564-565)
+            metrics_avg = _aggregate_metrics(metric_dicts)
+        spec, metrics = pl.finish(vals)
+        with torch.inference_mode():
+            self._run(spec)
+        metrics.update(metrics_avg)
+        return metrics
+
+    def _gather(self, vals_t, metric_dicts, local):
+        """All-gather pair values and metric scalars; returns (vals in pair order, averaged metrics)."""
+        import torch.distributed as dist
+        if self._metric_keys is None:
+            mine = sorted({k for d in metric_dicts for k, v in d.items() if v is not None})
+            allk = [None] * self.world
+            dist.all_gather_object(allk, mine, group=self.group)
+            self._metric_keys = sorted({k for ks in allk for k in ks})
+        keys = self._metric_keys
+        dev = self.params[0].device
+        C = 2 + 2 * len(keys)
+        rows = torch.full((len(local), C), float("nan"), dtype=torch.float32, device=dev)
+        for r in range(len(local)):
+            rows[r, 0] = vals_t[2 * r]
+            rows[r, 1] = vals_t[2 * r + 1]
+            for s in range(2):
+                d = metric_dicts[2 * r + s]
+                for k_i, k in enumerate(keys):
+                    v = d.get(k)
+                    if v is not None:
+                        rows[r, 2 + 2 * k_i + s] = v.detach().float() if isinstance(v, torch.Tensor) else float(v)
+        allrows = gather_pair_values(rows, self.cfg.z_batch, self.rank, self.world, self.group).cpu().tolist()
+        vals = [x for row in allrows for x in row[:2]]
+        metrics = {}
+        for k_i, k in enumerate(keys):
+            xs = [x for row in allrows for x in row[2 + 2 * k_i: 4 + 2 * k_i] if not math.isnan(x)]
+            if xs:
+                metrics[k] = sum(xs) / len(xs)
+        return vals, metrics
+
+    # exact resume (the reference saves no optimizer state, train_zo.py:671-673)
+    def state_dict(self) -> dict:
+        sd = {"planner": self.planner.state_dict()}
+        for name in ("m", "v", "theta_0"):
+            lst = getattr(self, name)
+            if lst is not None:
+                sd[name] = [t.detach().cpu() for t in lst]
+        return sd
+
+    def load_state_dict(self, sd: dict) -> None:
+        self.planner.load_state_dict(sd["planner"])
+        for name in ("m", "v", "theta_0"):
+            lst = getattr(self, name)
+            if lst is not None and name in sd:
+                for dst, src in zip(lst, sd[name]):
+                    dst.copy_(src)
+        if self.master is not None:
+            for m, p in zip(self.master, self.params):
+                m.copy_(p)
+
+
+def train_zo(model, tokenizer, total_steps, seed, merge_fn, logger, cfg: ZOConfig | None = None, objective=None,
+             profiling_cfg=None):
+    """Zeroth-order training loop (zotitan/train_zo.py:609-675). Perturbs only
+    params with requires_grad=True; calls merge_fn(model) after each step.
+    ``profiling_cfg`` is accepted for signature parity and ignored (torch.profiler
+    traces are not part of this path; kernels are profiled with ncu)."""
+    if cfg is None:
+        cfg = ZOConfig()
+    if objective is None:
+        raise ValueError("train_zo needs an objective (dataset objectives are not bundled)")
+    named_params = [(n, p) for n, p in model.named_parameters() if p.requires_grad]
+    n_params = sum(p.numel() for _, p in named_params)
+    device = next(model.parameters()).device
+    move_fn = None if getattr(objective, "flat_batches", True) else objective.to_device
+    loader = PrefetchLoader(objective.train_batches(tokenizer, seed, cfg.batch_size), device, move_fn=move_fn)
+    run_dir = os.environ.get("MLSWEEP_RUN_DIR", ".")
+    opt = ZOOptimizer(named_params, cfg, objective.score, total_steps=total_steps)
+    print(f"  ZO train: {total_steps:,} steps | {n_params:,} params")
+    model.eval()
+    show_lr = not wsd_is_constant(cfg.base.lr_wsd)
+    overfit = cfg.base.overfit_first_batch
+    fixed_batches = None
+    for step in range(total_steps):
+        if fixed_batches is not None:
+            batches = fixed_batches
+        elif cfg.shared_batch or overfit:
+            one = get_batches(loader, 1)
+            batches = one * cfg.z_batch if one is not None else None
+        else:
+            batches = get_batches(loader, cfg.z_batch)
+        if batches is None:
+            print("Dataloader exhausted, ending training.")
+            break
+        if overfit:
+            fixed_batches = batches
+        t0 = time.perf_counter()
+        metrics = opt.step(model, batches)
+        if merge_fn is not None:
+            merge_fn(model)
+        metrics["step_time"] = time.perf_counter() - t0
+        if logger is not None:
+            logger.log(metrics)
+        lr_s = f" lr {metrics['lr']:.2e}" if show_lr else ""
+        print(f"  step {step + 1}/{total_steps} loss {metrics['loss']:.4f} pg {metrics['proj_grad']:+.4f}{lr_s}")
+        if (step + 1) % cfg.base.ckpt_every == 0:
+            ckpt = os.path.join(run_dir, "checkpoint")
+            if hasattr(model, "save_pretrained"):
+                model.save_pretrained(ckpt)
+            torch.save(opt.state_dict(), os.path.join(run_dir, "zo_optimizer.pt"))
+            if logger is not None and hasattr(logger, "sync"):
+                logger.sync()
+    return model
