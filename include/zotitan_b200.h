@@ -99,8 +99,13 @@ typedef struct zt_plan {
   int32_t n_tensors;
   uint32_t n_params;           /* length of the reference's named-parameter list */
   int32_t device;
-  int32_t reserved;
+  int32_t buffers;             /* ZT_HAS_* bits: optional buffers present on every tensor */
 } zt_plan;
+
+#define ZT_HAS_LIVE 1
+#define ZT_HAS_M 2
+#define ZT_HAS_V 4
+#define ZT_HAS_ANCHOR 8
 
 #define ZT_UNIT_ELEMS 2048
 
@@ -177,7 +182,11 @@ typedef struct zt_pass_cfg {
   float wd_factor;      /* fp32(1 - wd_lam) (:402) */
 } zt_pass_cfg;
 
-/* One fused pass over every element of every tensor of `plan`:
+/* A pass is rejected (ZT_ERR_INVALID) when cfg reads or writes a buffer (live, m, v,
+ * anchor) that some tensor of the plan lacks. Optional buffers must have their
+ * tensor's numel and dtype; the library cannot check sizes.
+ *
+ * One fused pass over every element of every tensor of `plan`:
  *   1. theta = src buffer;
  *   2. for each stream in order: regenerate z in registers, apply its chain to theta,
  *      accumulate its ge / momentum contributions (noise is never written to memory);

@@ -65,6 +65,11 @@ def test_invalid_arguments_are_reported(lib):
     cfg.src, cfg.momentum, cfg.update = L.ZT_BUF_DATA, L.ZT_MOM_STORED_EMA, 0
     assert lib.zt_pass(ctypes.byref(plan), ctypes.byref(cfg), arr, 1, None) == L.ZT_ERR_INVALID
     assert b"require update" in lib.zt_last_error()
+    cfg.momentum, cfg.update, cfg.src = L.ZT_MOM_NONE, 1, L.ZT_BUF_LIVE   # plan without live buffers
+    assert lib.zt_pass(ctypes.byref(plan), ctypes.byref(cfg), arr, 1, None) == L.ZT_ERR_INVALID
+    assert b"live" in lib.zt_last_error()
+    cfg.src, cfg.second_moment = L.ZT_BUF_DATA, 1
+    assert lib.zt_pass(ctypes.byref(plan), ctypes.byref(cfg), arr, 1, None) == L.ZT_ERR_INVALID
     t = (L.ZtTensor * 1)()
     t[0].numel, t[0].dtype, t[0].index, t[0].data = 2**31, L.ZT_BF16, 0, 16
     out = L.ZtPlan()

@@ -37,7 +37,7 @@ class ZtTensor(ctypes.Structure):
 class ZtPlan(ctypes.Structure):
     _fields_ = [("tensors", ctypes.c_void_p), ("unit_prefix", ctypes.c_void_p), ("n_units", ctypes.c_int64),
                 ("numel_total", ctypes.c_int64), ("n_tensors", ctypes.c_int32), ("n_params", ctypes.c_uint32),
-                ("device", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+                ("device", ctypes.c_int32), ("buffers", ctypes.c_int32)]
 
 
 class ZtStream(ctypes.Structure):

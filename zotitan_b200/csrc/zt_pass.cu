@@ -318,6 +318,7 @@ int zt_plan_init(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_pa
   if (((uintptr_t)workspace & 15) != 0) return zt::set_error(ZT_ERR_INVALID, "zt_plan_init: workspace not 16-byte aligned");
   std::vector<int64_t> prefix((size_t)n_tensors + 1, 0);
   int64_t total = 0;
+  int32_t buffers = ZT_HAS_LIVE | ZT_HAS_M | ZT_HAS_V | ZT_HAS_ANCHOR;
   for (int32_t i = 0; i < n_tensors; ++i) {
     const zt_tensor& t = host_tensors[i];
     if (t.numel < 0 || t.numel > (int64_t)ZT_MAX_NUMEL)
@@ -328,6 +329,12 @@ int zt_plan_init(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_pa
       return zt::set_error(ZT_ERR_INVALID, "zt_plan_init: tensor " + std::to_string(i) + " has an unsupported dtype");
     if (t.index < 0 || (uint32_t)t.index >= n_params)
       return zt::set_error(ZT_ERR_INVALID, "zt_plan_init: tensor " + std::to_string(i) + " index outside [0, n_params)");
+    if (t.numel > 0) {
+      if (!t.live) buffers &= ~ZT_HAS_LIVE;
+      if (!t.m) buffers &= ~ZT_HAS_M;
+      if (!t.v) buffers &= ~ZT_HAS_V;
+      if (!t.anchor) buffers &= ~ZT_HAS_ANCHOR;
+    }
     prefix[i + 1] = prefix[i] + (t.numel + ZT_UNIT_ELEMS - 1) / ZT_UNIT_ELEMS;
     total += t.numel;
   }
@@ -352,7 +359,7 @@ int zt_plan_init(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_pa
   plan->n_tensors = n_tensors;
   plan->n_params = n_params;
   plan->device = dev;
-  plan->reserved = 0;
+  plan->buffers = buffers;
   return ZT_OK;
 }
 
@@ -369,6 +376,17 @@ int zt_pass(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* stream
   if (cfg->wd < ZT_WD_NONE || cfg->wd > ZT_WD_ANCHORED_L1) return zt::set_error(ZT_ERR_INVALID, "zt_pass: bad wd");
   if (!cfg->update && (cfg->momentum != ZT_MOM_NONE || cfg->second_moment || cfg->wd != ZT_WD_NONE))
     return zt::set_error(ZT_ERR_INVALID, "zt_pass: optimizer state and weight decay require update");
+  {
+    const bool live = cfg->src == ZT_BUF_LIVE || (cfg->dst & ZT_BUF_LIVE);
+    const bool anchored = cfg->wd == ZT_WD_ANCHORED_L1 || cfg->wd == ZT_WD_ANCHORED_L2;
+    if (live && !(plan->buffers & ZT_HAS_LIVE)) return zt::set_error(ZT_ERR_INVALID, "zt_pass: cfg uses live buffers the plan lacks");
+    if (cfg->update && cfg->momentum == ZT_MOM_STORED_EMA && !(plan->buffers & ZT_HAS_M))
+      return zt::set_error(ZT_ERR_INVALID, "zt_pass: stored-EMA momentum needs m buffers");
+    if (cfg->update && cfg->second_moment && !(plan->buffers & ZT_HAS_V))
+      return zt::set_error(ZT_ERR_INVALID, "zt_pass: second moment needs v buffers");
+    if (cfg->update && anchored && !(plan->buffers & ZT_HAS_ANCHOR))
+      return zt::set_error(ZT_ERR_INVALID, "zt_pass: anchored weight decay needs anchor buffers");
+  }
   int dev = 0;
   if (int rc = zt::check_cuda(cudaGetDevice(&dev), "zt_pass: cudaGetDevice")) return rc;
   if (dev != plan->device) return zt::set_error(ZT_ERR_INVALID, "zt_pass: plan belongs to another device");
