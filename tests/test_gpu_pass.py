@@ -156,8 +156,10 @@ def test_final_pass_variants(K, variant):
 
 
 def test_pass_with_independent_oracle_noise(K):
-    """Same pass against the C oracle's own noise (no CUDA in the checker): fp32 values
-    within 8 ulp at scale, bf16/fp16 within 1 ulp."""
+    """Same pass against the C oracle's own noise (no CUDA in the checker). The two noise
+    sources differ by at most 4 fp32 ulp of z (|z| < 8), so each coefficient c carries an
+    absolute difference of at most 4 * 2^-21 * |c|: fp32 values within 8 ulp at scale
+    plus that bound, bf16/fp16 within 1 ulp."""
     l = L()
     f = lambda x: float(np.float32(x))  # noqa: E731
     cfg = K.PassCfg(ge_mode=l.ZT_GE_ACCUM, update=True, lr=f(1e-2))
@@ -168,12 +170,17 @@ def test_pass_with_independent_oracle_noise(K):
     tab.run(cfg, streams)
     torch.cuda.synchronize()
     run_pass(host, N_PARAMS, cfg, streams, noise=ph.randn)
+    noise_atol = 4 * 2.0 ** -21 * (1e-3 + 1e-2 * (0.4 + 0.9))
     for i, t in enumerate(host):
         got = dev["data"][i].float().cpu().numpy()
         scale = np.maximum(np.abs(before[i]), np.abs(t["data"])) + 1e-6
         mant = 23 if t["dtype"] == ph.F32 else (7 if t["dtype"] == ph.BF16 else 10)
-        ulps = np.abs(got.astype(np.float64) - t["data"]) / np.exp2(np.floor(np.log2(scale)) - mant)
-        assert ulps.max() <= (8 if t["dtype"] == ph.F32 else 1), (i, ulps.max())
+        ulp = np.exp2(np.floor(np.log2(scale)) - mant)
+        diff = np.abs(got.astype(np.float64) - t["data"])
+        if t["dtype"] == ph.F32:
+            assert np.all(diff <= 8 * ulp + noise_atol), (i, float(diff.max()))
+        else:
+            assert np.all(diff <= ulp), (i, float((diff / ulp).max()))
 
 
 def test_empty_and_large_stream_lists(K):

@@ -5,9 +5,13 @@
     parameters after every step must be bit-identical to the oracle's op-by-op step
     (CUDA scalar semantics) fed the same Gaussians: 0 ulp.
 (2) Against the reference itself (golden, CPU torch): fp32 configurations within 8 fp32
-    ulp at scale; bf16 configurations whose CPU run has no bf16 scalar rounding within
-    2 bf16 ulp (torch's CPU kernels round some Python scalars to bf16; its CUDA kernels,
-    which this path follows, keep them in fp32).
+    ulp at scale, or within an absolute 2e-8 (the reference ran its noise kernel under
+    Triton's CPU interpreter, whose Gaussians differ from the device's by up to 4 ulp of z,
+    i.e. 4 * 2^-21 for |z| < 8; an update term of size lr * z, lr <= 1e-2 in these
+    configurations and Adam's normalised step included, carries up to
+    1e-2 * 4 * 2^-21 = 1.9e-8 of that); bf16 configurations whose CPU run has no bf16 scalar
+    rounding within 2 bf16 ulp (torch's CPU kernels round some Python scalars to bf16; its
+    CUDA kernels, which this path follows, keep them in fp32).
 (3) Real forward: the GPU losses of a toy Llama equal the reference's CPU losses for
     the same perturbed parameters within 1e-3 relative (the task's loss bar).
 """
@@ -93,14 +97,17 @@ def test_step_vs_reference_golden(name):
     a_gpu, _, snaps = run_gpu(case)
     dts = np.concatenate([[d] * n for d, n in zip(case.dtypes, case.numels)])
     # forwards see the reference's perturbed parameters up to the noise ulps
+    bf = dts == ph.BF16
     for got, ref in ((snaps[0], case.snap_pos), (snaps[1], case.snap_neg)):
-        assert scale_ulps(got, ref, case.init, dts).max() <= 8
+        u = scale_ulps(got, ref, case.init, dts)
+        assert np.all((u <= 8) | (~bf & (np.abs(got.astype(np.float64) - ref) <= 2e-8)))
     before = case.init
     for s, ref in enumerate(case.after):
         u = scale_ulps(a_gpu[s], ref, before, dts)
-        bf = dts == ph.BF16
+        absd = np.abs(a_gpu[s].astype(np.float64) - ref)
         assert (u[bf].max() if bf.any() else 0) <= 2, (s, u[bf].max())
-        assert (u[~bf].max() if (~bf).any() else 0) <= 8, (s, u[~bf].max())
+        ok32 = (u <= 8) | (absd <= 2e-8)
+        assert np.all(ok32[~bf]), (s, float(absd[~bf & ~ok32].max()) if np.any(~bf & ~ok32) else 0)
         before = ref
 
 

@@ -10,6 +10,7 @@
 // the fp32 opmath scalars torch's CUDA kernels use, one rounding to the parameter
 // dtype per torch op. Products, quotients and sums whose rounding matters are
 // written with __f*_rn intrinsics so the compiler cannot contract them.
+#include <atomic>
 #include <vector>
 
 #include "zt_common.cuh"
@@ -17,9 +18,21 @@
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kEpt = 8;  // elements per thread per unit
-static_assert(kThreads * kEpt == ZT_UNIT_ELEMS, "unit size");
+#ifndef ZT_CHAIN_EPT
+#define ZT_CHAIN_EPT 8  // elements per thread, perturb/restore passes
+#endif
+#ifndef ZT_CHAIN_MINB
+#define ZT_CHAIN_MINB 3  // resident blocks per SM the chain kernel is compiled for
+#endif
+#ifndef ZT_FULL_EPT
+#define ZT_FULL_EPT 8  // elements per thread, passes with gradient / optimizer stages
+#endif
+#ifndef ZT_FULL_MINB
+#define ZT_FULL_MINB 2
+#endif
+constexpr int kChainEpt = ZT_CHAIN_EPT;
+constexpr int kFullEpt = ZT_FULL_EPT;
+static_assert(ZT_UNIT_ELEMS % (kChainEpt * 32) == 0 && ZT_UNIT_ELEMS % (kFullEpt * 32) == 0, "unit size");
 
 struct KStream {
   uint64_t seed;
@@ -43,165 +56,200 @@ struct PassParams {
   KStream streams[ZT_MAX_STREAMS];
 };
 
-// ---- 8-element loads and stores ------------------------------------------------
+// ---- per-thread element group loads and stores ------------------------------------
+// A thread owns kEpt consecutive elements; the vector path moves them with one or two
+// 8/16-byte accesses per buffer (tensor bases 16-byte aligned, offsets multiples of kEpt).
 
-template <int DT> struct Io;
+template <int DT> struct Elem;
+template <> struct Elem<ZT_F32> { static constexpr int kBytes = 4; };
+template <> struct Elem<ZT_BF16> { static constexpr int kBytes = 2; };
+template <> struct Elem<ZT_F16> { static constexpr int kBytes = 2; };
 
-template <> struct Io<ZT_F32> {
-  __device__ static __forceinline__ void load(const void* base, int64_t e0, int nvalid, bool vec, float v[kEpt]) {
-    const float* p = static_cast<const float*>(base) + e0;
+template <int NW>
+__device__ __forceinline__ void ld_words(const void* p, uint32_t (&w)[NW]) {
+  if constexpr (NW % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < NW / 4; ++i) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(p) + i);
+      w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+    }
+  } else {
+    static_assert(NW == 2, "vector width");
+    const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+    w[0] = v.x; w[1] = v.y;
+  }
+}
+
+template <int NW>
+__device__ __forceinline__ void st_words(void* p, const uint32_t (&w)[NW]) {
+  if constexpr (NW % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < NW / 4; ++i)
+      reinterpret_cast<uint4*>(p)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+  } else {
+    reinterpret_cast<uint2*>(p)[0] = make_uint2(w[0], w[1]);
+  }
+}
+
+template <int DT, int EPT> struct Io {
+  static constexpr int kNW = EPT * Elem<DT>::kBytes / 4;
+  __device__ static __forceinline__ float scalar_ld(const void* base, int64_t i) {
+    if constexpr (DT == ZT_F32) return static_cast<const float*>(base)[i];
+    else if constexpr (DT == ZT_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i]);
+    else return __half2float(static_cast<const __half*>(base)[i]);
+  }
+  __device__ static __forceinline__ void scalar_st(void* base, int64_t i, float v) {
+    if constexpr (DT == ZT_F32) static_cast<float*>(base)[i] = v;
+    else if constexpr (DT == ZT_BF16) static_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(v);
+    else static_cast<__half*>(base)[i] = __float2half_rn(v);
+  }
+  __device__ static __forceinline__ void load(const void* base, int64_t e0, int nvalid, bool vec, float (&v)[EPT]) {
     if (vec) {
-      const float4 a = __ldg(reinterpret_cast<const float4*>(p));
-      const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
-      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      uint32_t w[kNW];
+      ld_words<kNW>(static_cast<const char*>(base) + e0 * Elem<DT>::kBytes, w);
+#pragma unroll
+      for (int k = 0; k < kNW; ++k) {
+        if constexpr (DT == ZT_F32) {
+          v[k] = __uint_as_float(w[k]);
+        } else if constexpr (DT == ZT_BF16) {
+          v[2 * k] = __uint_as_float(w[k] << 16);
+          v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+        } else {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+          v[2 * k] = f.x;
+          v[2 * k + 1] = f.y;
+        }
+      }
     } else {
 #pragma unroll
-      for (int e = 0; e < kEpt; ++e) v[e] = e < nvalid ? p[e] : 0.0f;
+      for (int e = 0; e < EPT; ++e) v[e] = e < nvalid ? scalar_ld(base, e0 + e) : 0.0f;
     }
   }
-  __device__ static __forceinline__ void store(void* base, int64_t e0, int nvalid, bool vec, const float v[kEpt]) {
-    float* p = static_cast<float*>(base) + e0;
+  __device__ static __forceinline__ void store(void* base, int64_t e0, int nvalid, bool vec, const float (&v)[EPT]) {
     if (vec) {
-      reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
-      reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+      uint32_t w[kNW];
+#pragma unroll
+      for (int k = 0; k < kNW; ++k) {
+        if constexpr (DT == ZT_F32) {
+          w[k] = __float_as_uint(v[k]);
+        } else if constexpr (DT == ZT_BF16) {
+          const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+          w[k] = *reinterpret_cast<const uint32_t*>(&h);
+        } else {
+          const __half2 h = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+          w[k] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+      }
+      st_words<kNW>(static_cast<char*>(base) + e0 * Elem<DT>::kBytes, w);
     } else {
 #pragma unroll
-      for (int e = 0; e < kEpt; ++e)
-        if (e < nvalid) p[e] = v[e];
+      for (int e = 0; e < EPT; ++e)
+        if (e < nvalid) scalar_st(base, e0 + e, v[e]);
     }
   }
 };
 
-template <> struct Io<ZT_BF16> {
-  __device__ static __forceinline__ void load(const void* base, int64_t e0, int nvalid, bool vec, float v[kEpt]) {
-    const __nv_bfloat16* p = static_cast<const __nv_bfloat16*>(base) + e0;
-    if (vec) {
-      const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
-      const uint32_t w[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        v[2 * k] = __uint_as_float(w[k] << 16);
-        v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < kEpt; ++e) v[e] = e < nvalid ? __bfloat162float(p[e]) : 0.0f;
-    }
-  }
-  __device__ static __forceinline__ void store(void* base, int64_t e0, int nvalid, bool vec, const float v[kEpt]) {
-    __nv_bfloat16* p = static_cast<__nv_bfloat16*>(base) + e0;
-    if (vec) {
-      uint32_t w[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
-        w[k] = *reinterpret_cast<const uint32_t*>(&h);
-      }
-      *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < kEpt; ++e)
-        if (e < nvalid) p[e] = __float2bfloat16_rn(v[e]);
-    }
-  }
-};
+// ---- one thread's element group -------------------------------------------------
 
-template <> struct Io<ZT_F16> {
-  __device__ static __forceinline__ void load(const void* base, int64_t e0, int nvalid, bool vec, float v[kEpt]) {
-    const __half* p = static_cast<const __half*>(base) + e0;
-    if (vec) {
-      const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
-      const uint32_t w[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const __half2 h = *reinterpret_cast<const __half2*>(&w[k]);
-        const float2 f = __half22float2(h);
-        v[2 * k] = f.x;
-        v[2 * k + 1] = f.y;
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < kEpt; ++e) v[e] = e < nvalid ? __half2float(p[e]) : 0.0f;
-    }
-  }
-  __device__ static __forceinline__ void store(void* base, int64_t e0, int nvalid, bool vec, const float v[kEpt]) {
-    __half* p = static_cast<__half*>(base) + e0;
-    if (vec) {
-      uint32_t w[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const __half2 h = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
-        w[k] = *reinterpret_cast<const uint32_t*>(&h);
-      }
-      *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < kEpt; ++e)
-        if (e < nvalid) p[e] = __float2half_rn(v[e]);
-    }
-  }
-};
-
-// ---- one thread's 8-element group ---------------------------------------------------
-
-template <int DT>
-__device__ __forceinline__ void run_group(const PassParams& P, const zt_tensor& t, int64_t e0, int nvalid, bool vec) {
+// Perturb / restore passes: theta <- round(theta + a*z) for each chained coefficient of
+// each stream (train_zo.py:350-351), nothing else.
+template <int DT, int EPT>
+__device__ __forceinline__ void run_chain(const PassParams& P, const zt_tensor& t, int64_t e0, int nvalid, bool vec) {
   using R = zt::Dt<DT>;
-  using IO = Io<DT>;
+  using IO = Io<DT, EPT>;
+  const zt_pass_cfg& c = P.cfg;
+  float th[EPT];
+  IO::load(c.src == ZT_BUF_LIVE ? t.live : t.data, e0, nvalid, vec, th);
+  const uint32_t ctr0 = (uint32_t)e0;
+  for (int s = 0; s < P.n_streams; ++s) {
+    const KStream& S = P.streams[s];
+    const zt::RoundKeys rk = zt::round_keys(zt::param_key(S.seed, P.n_params, (uint32_t)t.index));
+    const float a0 = S.chain[0], a1 = S.chain[1], a2 = S.chain[2];
+    switch (S.n_chain) {  // the chain length is uniform: branch once, not per element
+      case 1:
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) th[e] = R::round(__fmaf_rn(zt::gauss_rk(ctr0 + (uint32_t)e, rk), a0, th[e]));
+        break;
+      case 2:
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) {
+          const float z = zt::gauss_rk(ctr0 + (uint32_t)e, rk);
+          th[e] = R::round(__fmaf_rn(z, a1, R::round(__fmaf_rn(z, a0, th[e]))));
+        }
+        break;
+      case 3:
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) {
+          const float z = zt::gauss_rk(ctr0 + (uint32_t)e, rk);
+          th[e] = R::round(__fmaf_rn(z, a2, R::round(__fmaf_rn(z, a1, R::round(__fmaf_rn(z, a0, th[e]))))));
+        }
+        break;
+      default:
+        break;
+    }
+  }
+  if (c.dst & ZT_BUF_DATA) IO::store(t.data, e0, nvalid, vec, th);
+  if (c.dst & ZT_BUF_LIVE) IO::store(t.live, e0, nvalid, vec, th);
+}
+
+template <int DT, int EPT>
+__device__ __forceinline__ void run_full(const PassParams& P, const zt_tensor& t, int64_t e0, int nvalid, bool vec) {
+  using R = zt::Dt<DT>;
+  using IO = Io<DT, EPT>;
   const zt_pass_cfg& c = P.cfg;
 
-  float th[kEpt], ge[kEpt], mom[kEpt];
+  float th[EPT], ge[EPT], mom[EPT];
   IO::load(c.src == ZT_BUF_LIVE ? t.live : t.data, e0, nvalid, vec, th);
 #pragma unroll
-  for (int e = 0; e < kEpt; ++e) { ge[e] = 0.0f; mom[e] = 0.0f; }
+  for (int e = 0; e < EPT; ++e) { ge[e] = 0.0f; mom[e] = 0.0f; }
 
   const uint32_t ctr0 = (uint32_t)e0;
   for (int s = 0; s < P.n_streams; ++s) {
     const KStream& S = P.streams[s];
-    const uint32_t key = zt::param_key(S.seed, P.n_params, (uint32_t)t.index);
-    float z[kEpt];
+    const zt::RoundKeys rk = zt::round_keys(zt::param_key(S.seed, P.n_params, (uint32_t)t.index));
+    float z[EPT];
 #pragma unroll
-    for (int e = 0; e < kEpt; ++e) z[e] = zt::gauss(ctr0 + (uint32_t)e, key);
+    for (int e = 0; e < EPT; ++e) z[e] = zt::gauss_rk(ctr0 + (uint32_t)e, rk);
     // _apply_z: theta <- round(theta + a*z), one rounding per call (train_zo.py:350-351)
     for (int k = 0; k < S.n_chain; ++k) {
       const float a = S.chain[k];
 #pragma unroll
-      for (int e = 0; e < kEpt; ++e) th[e] = R::round(__fmaf_rn(z[e], a, th[e]));
+      for (int e = 0; e < EPT; ++e) th[e] = R::round(__fmaf_rn(z[e], a, th[e]));
     }
     if (S.flags & ZT_STREAM_GE) {
       const float a = S.ge_coef;
       if (c.ge_mode == ZT_GE_PRODUCT) {
 #pragma unroll
-        for (int e = 0; e < kEpt; ++e) ge[e] = __fmul_rn(z[e], a);  // fp32 (train_zo.py:552)
+        for (int e = 0; e < EPT; ++e) ge[e] = __fmul_rn(z[e], a);  // fp32 (train_zo.py:552)
       } else {
 #pragma unroll
-        for (int e = 0; e < kEpt; ++e) ge[e] = R::round(__fmaf_rn(z[e], a, ge[e]));  // (:556, :577)
+        for (int e = 0; e < EPT; ++e) ge[e] = R::round(__fmaf_rn(z[e], a, ge[e]));  // (:556, :577)
       }
     }
     if (S.flags & ZT_STREAM_MOM) {
       const float a = S.mom_coef;
 #pragma unroll
-      for (int e = 0; e < kEpt; ++e) mom[e] = R::round(__fmaf_rn(z[e], a, mom[e]));  // (:345)
+      for (int e = 0; e < EPT; ++e) mom[e] = R::round(__fmaf_rn(z[e], a, mom[e]));  // (:345)
     }
   }
 
   if (c.ge_scale_on) {  // norm clipping rescales grad_est (train_zo.py:457)
     if (c.ge_mode == ZT_GE_PRODUCT) {
 #pragma unroll
-      for (int e = 0; e < kEpt; ++e) ge[e] = __fmul_rn(ge[e], c.ge_scale);
+      for (int e = 0; e < EPT; ++e) ge[e] = __fmul_rn(ge[e], c.ge_scale);
     } else {
 #pragma unroll
-      for (int e = 0; e < kEpt; ++e) ge[e] = R::round(__fmul_rn(ge[e], c.ge_scale));
+      for (int e = 0; e < EPT; ++e) ge[e] = R::round(__fmul_rn(ge[e], c.ge_scale));
     }
   }
 
   if (c.update) {
-    float g[kEpt];
+    float g[EPT];
     if (c.momentum == ZT_MOM_STORED_EMA) {  // (:418-419, :330-331)
-      float m[kEpt];
+      float m[EPT];
       IO::load(t.m, e0, nvalid, vec, m);
 #pragma unroll
-      for (int e = 0; e < kEpt; ++e) {
+      for (int e = 0; e < EPT; ++e) {
         m[e] = R::round(__fmul_rn(m[e], c.beta1));
         m[e] = R::round(__fmaf_rn(ge[e], c.one_minus_beta1, m[e]));
         g[e] = R::round(__fmul_rn(m[e], c.m_scale));
@@ -209,17 +257,17 @@ __device__ __forceinline__ void run_group(const PassParams& P, const zt_tensor& 
       IO::store(t.m, e0, nvalid, vec, m);
     } else if (c.momentum == ZT_MOM_SEED_WINDOW) {
 #pragma unroll
-      for (int e = 0; e < kEpt; ++e) g[e] = mom[e];
+      for (int e = 0; e < EPT; ++e) g[e] = mom[e];
     } else {
 #pragma unroll
-      for (int e = 0; e < kEpt; ++e) g[e] = ge[e];
+      for (int e = 0; e < EPT; ++e) g[e] = ge[e];
     }
     if (c.second_moment) {  // (:423-425, :392-397)
-      float v[kEpt];
+      float v[EPT];
       IO::load(t.v, e0, nvalid, vec, v);
       const float nlr = -c.lr;
 #pragma unroll
-      for (int e = 0; e < kEpt; ++e) {
+      for (int e = 0; e < EPT; ++e) {
         v[e] = R::round(__fmul_rn(v[e], c.beta2));
         v[e] = R::round(__fmaf_rn(__fmul_rn(c.one_minus_beta2, ge[e]), ge[e], v[e]));
         float vh = R::round(__fdiv_rn(v[e], c.bc2));
@@ -231,18 +279,18 @@ __device__ __forceinline__ void run_group(const PassParams& P, const zt_tensor& 
     } else {
       const float nlr = -c.lr;
 #pragma unroll
-      for (int e = 0; e < kEpt; ++e) th[e] = R::round(__fmaf_rn(g[e], nlr, th[e]));  // (:399)
+      for (int e = 0; e < EPT; ++e) th[e] = R::round(__fmaf_rn(g[e], nlr, th[e]));  // (:399)
     }
     if (c.wd == ZT_WD_STANDARD) {  // (:401-402)
 #pragma unroll
-      for (int e = 0; e < kEpt; ++e) th[e] = R::round(__fmul_rn(th[e], c.wd_factor));
+      for (int e = 0; e < EPT; ++e) th[e] = R::round(__fmul_rn(th[e], c.wd_factor));
     } else if (c.wd == ZT_WD_ANCHORED_L2 || c.wd == ZT_WD_ANCHORED_L1) {  // (:403-407)
-      float a0[kEpt];
+      float a0[EPT];
       IO::load(t.anchor, e0, nvalid, vec, a0);
       const float nlam = -c.wd_lam;
       const bool l1 = c.wd == ZT_WD_ANCHORED_L1;
 #pragma unroll
-      for (int e = 0; e < kEpt; ++e) {
+      for (int e = 0; e < EPT; ++e) {
         const float d = R::round(__fsub_rn(th[e], a0[e]));
         const float x = l1 ? (float)((d > 0.0f) - (d < 0.0f)) : d;
         th[e] = R::round(__fmaf_rn(x, nlam, th[e]));
@@ -265,36 +313,68 @@ __device__ __forceinline__ int find_tensor(const int64_t* __restrict__ prefix, i
 
 __device__ __forceinline__ bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
-__global__ void __launch_bounds__(kThreads) pass_kernel(const __grid_constant__ PassParams P) {
+// Persistent grid over work units. The owning tensor is looked up only when a unit
+// leaves the current tensor's unit range (grid-stride steps rarely do).
+template <bool kFull, int EPT>
+__device__ __forceinline__ void walk_units(const PassParams& P) {
+  constexpr int kThreadsT = ZT_UNIT_ELEMS / EPT;
+  const zt_pass_cfg& c = P.cfg;
+  int64_t lo = 0, hi = -1;  // unit range of the cached tensor
+  zt_tensor t{};
+  bool base_vec = false;
   for (int64_t u = blockIdx.x; u < P.n_units; u += gridDim.x) {
-    const int ti = find_tensor(P.unit_prefix, P.n_tensors, u);
-    const zt_tensor t = P.tensors[ti];
-    const int64_t e0 = (u - __ldg(P.unit_prefix + ti)) * ZT_UNIT_ELEMS + (int64_t)threadIdx.x * kEpt;
+    if (u < lo || u >= hi) {
+      const int ti = find_tensor(P.unit_prefix, P.n_tensors, u);
+      lo = __ldg(P.unit_prefix + ti);
+      hi = __ldg(P.unit_prefix + ti + 1);
+      t = P.tensors[ti];
+      base_vec = aligned16(t.data);
+      if (c.src == ZT_BUF_LIVE || (c.dst & ZT_BUF_LIVE)) base_vec = base_vec && aligned16(t.live);
+      if (kFull && c.update && c.momentum == ZT_MOM_STORED_EMA) base_vec = base_vec && aligned16(t.m);
+      if (kFull && c.update && c.second_moment) base_vec = base_vec && aligned16(t.v);
+      if (kFull && c.update && (c.wd == ZT_WD_ANCHORED_L1 || c.wd == ZT_WD_ANCHORED_L2))
+        base_vec = base_vec && aligned16(t.anchor);
+    }
+    const int64_t e0 = (u - lo) * ZT_UNIT_ELEMS + (int64_t)(threadIdx.x % kThreadsT) * EPT;
     if (e0 >= t.numel) continue;
     const int64_t rem = t.numel - e0;
-    const int nvalid = rem < kEpt ? (int)rem : kEpt;
-    bool vec = nvalid == kEpt && aligned16(t.data);
-    const zt_pass_cfg& c = P.cfg;
-    if (c.src == ZT_BUF_LIVE || (c.dst & ZT_BUF_LIVE)) vec = vec && aligned16(t.live);
-    if (c.update && c.momentum == ZT_MOM_STORED_EMA) vec = vec && aligned16(t.m);
-    if (c.update && c.second_moment) vec = vec && aligned16(t.v);
-    if (c.update && (c.wd == ZT_WD_ANCHORED_L1 || c.wd == ZT_WD_ANCHORED_L2)) vec = vec && aligned16(t.anchor);
-    if (t.dtype == ZT_BF16) run_group<ZT_BF16>(P, t, e0, nvalid, vec);
-    else if (t.dtype == ZT_F32) run_group<ZT_F32>(P, t, e0, nvalid, vec);
-    else run_group<ZT_F16>(P, t, e0, nvalid, vec);
+    const int nvalid = rem < EPT ? (int)rem : EPT;
+    const bool vec = base_vec && nvalid == EPT;
+    if (kFull) {
+      if (t.dtype == ZT_BF16) run_full<ZT_BF16, EPT>(P, t, e0, nvalid, vec);
+      else if (t.dtype == ZT_F32) run_full<ZT_F32, EPT>(P, t, e0, nvalid, vec);
+      else run_full<ZT_F16, EPT>(P, t, e0, nvalid, vec);
+    } else {
+      if (t.dtype == ZT_BF16) run_chain<ZT_BF16, EPT>(P, t, e0, nvalid, vec);
+      else if (t.dtype == ZT_F32) run_chain<ZT_F32, EPT>(P, t, e0, nvalid, vec);
+      else run_chain<ZT_F16, EPT>(P, t, e0, nvalid, vec);
+    }
   }
 }
 
-int pass_grid(int64_t n_units) {
-  static int occ = 0;
-  if (occ == 0) {
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, pass_kernel, kThreads, 0) != cudaSuccess || n <= 0) n = 1;
-    occ = n;
+__global__ void __launch_bounds__(ZT_UNIT_ELEMS / kChainEpt, ZT_CHAIN_MINB)
+chain_kernel(const __grid_constant__ PassParams P) {
+  walk_units<false, kChainEpt>(P);
+}
+
+__global__ void __launch_bounds__(ZT_UNIT_ELEMS / kFullEpt, ZT_FULL_MINB)
+full_kernel(const __grid_constant__ PassParams P) {
+  walk_units<true, kFullEpt>(P);
+}
+
+// Grid = SMs x resident blocks per SM (occupancy queried once per kernel).
+template <typename K>
+int grid_for(K kernel, int threads, int64_t n_units, std::atomic<int>& occ_cache) {
+  int occ = occ_cache.load(std::memory_order_relaxed);
+  if (occ <= 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, 0) != cudaSuccess || occ <= 0) occ = 1;
+    occ_cache.store(occ, std::memory_order_relaxed);
   }
   const int64_t cap = (int64_t)zt::sm_count() * occ;
   return (int)(n_units < cap ? n_units : cap);
 }
+
+std::atomic<int> g_occ_chain{0}, g_occ_full{0};
 
 }  // namespace
 
@@ -418,7 +498,15 @@ int zt_pass(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* stream
     K.pad[0] = K.pad[1] = 0;
   }
   for (int s = n_streams; s < ZT_MAX_STREAMS; ++s) P.streams[s] = KStream{};
-  pass_kernel<<<pass_grid(plan->n_units), kThreads, 0, zt::as_stream(stream)>>>(P);
+  bool full = cfg->update || cfg->ge_scale_on;
+  for (int s = 0; s < n_streams; ++s) full = full || streams[s].flags != 0;
+  if (full) {
+    constexpr int th = ZT_UNIT_ELEMS / kFullEpt;
+    full_kernel<<<grid_for(full_kernel, th, plan->n_units, g_occ_full), th, 0, zt::as_stream(stream)>>>(P);
+  } else {
+    constexpr int th = ZT_UNIT_ELEMS / kChainEpt;
+    chain_kernel<<<grid_for(chain_kernel, th, plan->n_units, g_occ_chain), th, 0, zt::as_stream(stream)>>>(P);
+  }
   return zt::check_cuda(cudaGetLastError(), "zt_pass launch");
 }
 

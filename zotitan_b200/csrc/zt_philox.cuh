@@ -54,6 +54,38 @@ __device__ __forceinline__ void philox_w01(uint32_t ctr, uint32_t key, uint32_t&
   w1 = c1;
 }
 
+// Round keys of the key-schedule word 0: rk[r] = key + r * kPhiloxW0. Word 1 of the key
+// is 0, so its schedule r * kPhiloxW1 is a compile-time constant. Computing rk once per
+// (stream, tensor) and sharing it across a thread's elements removes the per-element
+// key additions.
+struct RoundKeys {
+  uint32_t k[10];
+};
+
+__device__ __forceinline__ RoundKeys round_keys(uint32_t key) {
+  RoundKeys rk;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) rk.k[r] = key + (uint32_t)r * kPhiloxW0;
+  return rk;
+}
+
+__device__ __forceinline__ void philox_w01_rk(uint32_t ctr, const RoundKeys& rk, uint32_t& w0, uint32_t& w1) {
+  uint32_t c0 = ctr, c1 = 0u, c2 = 0u, c3 = 0u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint64_t p0 = (uint64_t)kPhiloxM0 * c0;
+    const uint64_t p1 = (uint64_t)kPhiloxM1 * c2;
+    const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c1 ^ rk.k[r];
+    const uint32_t n2 = (uint32_t)(p0 >> 32) ^ c3 ^ ((uint32_t)r * kPhiloxW1);
+    c1 = (uint32_t)p1;
+    c3 = (uint32_t)p0;
+    c0 = n0;
+    c2 = n2;
+  }
+  w0 = c0;
+  w1 = c1;
+}
+
 // All four words (test entry points only).
 __device__ __forceinline__ void philox_w4(uint32_t ctr, uint32_t key, uint32_t w[4]) {
   uint32_t c0 = ctr, c1 = 0u, c2 = 0u, c3 = 0u;
@@ -107,6 +139,12 @@ __device__ __forceinline__ float box_muller_cos(float u1, float u2) {
 __device__ __forceinline__ float gauss(uint32_t ctr, uint32_t key) {
   uint32_t w0, w1;
   philox_w01(ctr, key, w0, w1);
+  return box_muller_cos(word_to_uniform(w0), word_to_uniform(w1));
+}
+
+__device__ __forceinline__ float gauss_rk(uint32_t ctr, const RoundKeys& rk) {
+  uint32_t w0, w1;
+  philox_w01_rk(ctr, rk, w0, w1);
   return box_muller_cos(word_to_uniform(w0), word_to_uniform(w1));
 }
 
