@@ -199,6 +199,30 @@ typedef struct zt_pass_cfg {
 ZT_API int zt_pass(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* streams, int32_t n_streams,
             void* stream);
 
+/* ---- the fused pass without a caller-provided workspace -------------------------- */
+
+#define ZT_STATIC_MAX_TENSORS 1024
+
+/* zt_pass for callers that cannot allocate device memory. This entry point has no
+ * counterpart in the reference. It serves callers that cannot hand the library a
+ * workspace: a process whose device memory is held by another allocator that reserved
+ * it up front, or host code that must not call cudaMalloc/cudaFree while a step is in
+ * flight (those calls synchronise the device and fragment the owner's memory pool).
+ *
+ * Instead of a zt_plan, it takes the host descriptor table directly, copies it into a
+ * fixed array compiled into the library (about 64 KB, kept on every GPU that loads the
+ * library until the process exits) and runs the same pass as zt_pass. At most
+ * ZT_STATIC_MAX_TENSORS tensors per call; more are rejected with ZT_ERR_LIMIT. It calls
+ * no cudaMalloc, cudaFree or other allocating routine.
+ *
+ * The first call on a device resolves the array's device address (once per device, with
+ * that device current); make that first call before any stream capture. Every call
+ * copies its table into the same array, on `stream`, before its pass, and the array keeps
+ * the last call's table: calls whose work can overlap on the GPU (different streams, or
+ * unordered host threads on one device) race on it. Order such calls on one stream. */
+ZT_API int zt_pass_static(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_params,
+                          const zt_pass_cfg* cfg, const zt_stream* streams, int32_t n_streams, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -25,7 +25,8 @@ ZT_BUF_DATA, ZT_BUF_LIVE = 1, 2
 
 # every function include/zotitan_b200.h declares
 EXPORTS = ("zt_last_error", "zt_abi_version", "zt_param_key", "zt_philox_words", "zt_randn",
-           "zt_randn_at", "zt_plan_workspace_bytes", "zt_plan_init", "zt_pass")
+           "zt_randn_at", "zt_plan_workspace_bytes", "zt_plan_init", "zt_pass", "zt_pass_static")
+ZT_STATIC_MAX_TENSORS = 1024
 
 
 class ZtTensor(ctypes.Structure):
@@ -83,7 +84,9 @@ def load():
                        ("zt_plan_init", [ctypes.POINTER(ZtTensor), I32, U32, P, ctypes.c_size_t,
                                          ctypes.POINTER(ZtPlan), P]),
                        ("zt_pass", [ctypes.POINTER(ZtPlan), ctypes.POINTER(ZtPassCfg), ctypes.POINTER(ZtStream),
-                                    I32, P])]:
+                                    I32, P]),
+                       ("zt_pass_static", [ctypes.POINTER(ZtTensor), I32, U32, ctypes.POINTER(ZtPassCfg),
+                                           ctypes.POINTER(ZtStream), I32, P])]:
         fn = getattr(lib, name)
         fn.restype = ctypes.c_int
         fn.argtypes = args

@@ -21,6 +21,15 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 // SM count of the current device (cached per device).
 int sm_count();
 
+// Validate a tensor table and copy it (with its work-unit prefix) into `workspace`;
+// the body of zt_plan_init. sync_copies: wait for the copies before returning.
+int plan_build(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_params, void* workspace,
+               size_t workspace_bytes, zt_plan* plan, void* stream, bool sync_copies);
+
+// Validate a pass and launch it; the body of zt_pass.
+int pass_launch(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* streams, int32_t n_streams,
+                void* stream);
+
 // --- parameter-dtype rounding ----------------------------------------------------
 template <int DT> struct Dt;
 template <> struct Dt<ZT_F32> {

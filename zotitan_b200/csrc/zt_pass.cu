@@ -390,6 +390,20 @@ size_t zt_plan_workspace_bytes(int32_t n_tensors) {
 int zt_plan_init(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_params, void* workspace,
                  size_t workspace_bytes, zt_plan* plan, void* stream) {
   zt::clear_error();
+  return zt::plan_build(host_tensors, n_tensors, n_params, workspace, workspace_bytes, plan, stream, true);
+}
+
+int zt_pass(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* streams, int32_t n_streams, void* stream) {
+  zt::clear_error();
+  return zt::pass_launch(plan, cfg, streams, n_streams, stream);
+}
+
+}  // extern "C"
+
+namespace zt {
+
+int plan_build(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_params, void* workspace,
+               size_t workspace_bytes, zt_plan* plan, void* stream, bool sync_copies) {
   if (!plan || (n_tensors > 0 && (!host_tensors || !workspace)))
     return zt::set_error(ZT_ERR_INVALID, "zt_plan_init: null pointer");
   if (n_tensors < 0) return zt::set_error(ZT_ERR_INVALID, "zt_plan_init: n_tensors < 0");
@@ -429,9 +443,12 @@ int zt_plan_init(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_pa
   }
   if (int rc = zt::check_cuda(cudaMemcpyAsync(ws + off, prefix.data(), sizeof(int64_t) * prefix.size(),
                                               cudaMemcpyHostToDevice, s), "zt_plan_init: copy prefix")) return rc;
-  // The host staging buffers are released when this function returns; make the
-  // copies complete first so the caller's arrays and `prefix` may be freed.
-  if (int rc = zt::check_cuda(cudaStreamSynchronize(s), "zt_plan_init: synchronize")) return rc;
+  // Copies from pageable host memory are staged before cudaMemcpyAsync returns, so the
+  // host arrays may be freed right away; zt_plan_init still waits for the copies so a
+  // plan is complete on the device when it returns.
+  if (sync_copies) {
+    if (int rc = zt::check_cuda(cudaStreamSynchronize(s), "zt_plan_init: synchronize")) return rc;
+  }
   plan->tensors = reinterpret_cast<const zt_tensor*>(ws);
   plan->unit_prefix = reinterpret_cast<const int64_t*>(ws + off);
   plan->n_units = prefix[n_tensors];
@@ -443,8 +460,8 @@ int zt_plan_init(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_pa
   return ZT_OK;
 }
 
-int zt_pass(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* streams, int32_t n_streams, void* stream) {
-  zt::clear_error();
+int pass_launch(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* streams, int32_t n_streams,
+                void* stream) {
   if (!plan || !cfg) return zt::set_error(ZT_ERR_INVALID, "zt_pass: null plan or cfg");
   if (n_streams < 0 || (n_streams > 0 && !streams)) return zt::set_error(ZT_ERR_INVALID, "zt_pass: bad stream list");
   if (n_streams > ZT_MAX_STREAMS)
@@ -510,4 +527,4 @@ int zt_pass(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* stream
   return zt::check_cuda(cudaGetLastError(), "zt_pass launch");
 }
 
-}  // extern "C"
+}  // namespace zt

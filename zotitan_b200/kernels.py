@@ -111,6 +111,32 @@ class PassCfg:
         return c
 
 
+def _streams_array(streams):
+    if len(streams) > L.ZT_MAX_STREAMS:
+        raise ValueError(f"{len(streams)} noise streams > {L.ZT_MAX_STREAMS}")
+    arr = (L.ZtStream * max(1, len(streams)))()
+    for i, s in enumerate(streams):
+        arr[i] = s.to_c()
+    return arr
+
+
+def pass_static(params, cfg: PassCfg, streams: list, n_params=None, indices=None, live=None, m=None, v=None,
+                anchor=None) -> None:
+    """One fused pass through zt_pass_static: no workspace, nothing allocated on the device.
+
+    For callers that cannot allocate device memory (see include/zotitan_b200.h). Same
+    arguments and result as ParamTable(...).run(cfg, streams); at most
+    ZT_STATIC_MAX_TENSORS tensors. Calls that can overlap on the GPU race on the
+    library's one descriptor array, so keep them on one stream."""
+    desc = ParamTable.__new__(ParamTable)
+    desc._describe(params, n_params, indices, live, m, v, anchor)
+    arr = _streams_array(streams)
+    c = cfg.to_c()
+    with torch.cuda.device(desc.device):
+        L.check(L.load().zt_pass_static(desc._host, len(desc.params), desc.n_params, ctypes.byref(c), arr,
+                                        len(streams), _stream_ptr(desc.device)), "zt_pass_static")
+
+
 class ParamTable:
     """A zt_plan over trainable tensors, resident on their device.
 
@@ -121,6 +147,19 @@ class ParamTable:
     """
 
     def __init__(self, params, n_params=None, indices=None, live=None, m=None, v=None, anchor=None):
+        self._describe(params, n_params, indices, live, m, v, anchor)
+        lib = L.load()
+        n = len(self.params)
+        nbytes = lib.zt_plan_workspace_bytes(n)
+        self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        self.plan = L.ZtPlan()
+        with torch.cuda.device(self.device):
+            L.check(lib.zt_plan_init(self._host, n, self.n_params, self.workspace.data_ptr(), nbytes,
+                                     ctypes.byref(self.plan), _stream_ptr(self.device)), "zt_plan_init")
+        self.numel = int(self.plan.numel_total)
+
+    def _describe(self, params, n_params, indices, live, m, v, anchor):
+        """Validate the tensors and build the host zt_tensor array."""
         params = list(params)
         if not params:
             raise ValueError("empty parameter list")
@@ -143,14 +182,6 @@ class ParamTable:
             arr[i].dtype = _DT[p.dtype]
             arr[i].index = self.indices[i]
         self._host = arr
-        lib = L.load()
-        nbytes = lib.zt_plan_workspace_bytes(len(params))
-        self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
-        self.plan = L.ZtPlan()
-        with torch.cuda.device(self.device):
-            L.check(lib.zt_plan_init(arr, len(params), self.n_params, self.workspace.data_ptr(), nbytes,
-                                     ctypes.byref(self.plan), _stream_ptr(self.device)), "zt_plan_init")
-        self.numel = int(self.plan.numel_total)
 
     def _check(self, t: torch.Tensor, like: torch.Tensor, name: str):
         if t.device != self.device:
@@ -164,11 +195,7 @@ class ParamTable:
 
     def run(self, cfg: PassCfg, streams: list[Stream]) -> None:
         """One fused pass (zt_pass) on torch's current stream."""
-        if len(streams) > L.ZT_MAX_STREAMS:
-            raise ValueError(f"{len(streams)} noise streams > {L.ZT_MAX_STREAMS}")
-        arr = (L.ZtStream * max(1, len(streams)))()
-        for i, s in enumerate(streams):
-            arr[i] = s.to_c()
+        arr = _streams_array(streams)
         c = cfg.to_c()
         with torch.cuda.device(self.device):
             L.check(L.load().zt_pass(ctypes.byref(self.plan), ctypes.byref(c), arr, len(streams),
