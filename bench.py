@@ -42,7 +42,41 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seeds", type=int, default=N_SEEDS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", choices=["chain", "full"], default=None,
+                    help="small case for ncu: one bf16 tensor of 2^28 elements, 3 launches of the "
+                         "-2eps pass (chain) or of the restore+accumulate+perturb pass (full)")
     return ap.parse_args()
+
+
+def profile_case(kind: str):
+    """A few launches of one pass kind on a 512 MB bf16 tensor (larger than L2)."""
+    import torch
+
+    from zotitan_b200 import _lib as L
+    from zotitan_b200 import kernels as K
+    n = 1 << 28
+    p = (torch.randn(n, device="cuda") * 0.02).bfloat16()
+    f = lambda x: float(np.float32(x))  # noqa: E731
+    if kind == "chain":
+        tab = K.ParamTable([p])
+        cfg, streams = K.PassCfg(), [K.Stream(5, (f(-2e-3),))]
+    else:
+        ge = torch.zeros_like(p)
+        vals = torch.tensor([2.01, 2.0], device="cuda")
+        tab = K.ParamTable([p], ge=[ge])
+        cfg = K.PassCfg(ge_mode=L.ZT_GE_ACCUM, ge_load=True, ge_store=True, dev_vals=vals.data_ptr(),
+                        dev_inv2eps=f(500.0), dev_invz=f(1 / 64), dev_tau=float("inf"))
+        streams = [K.Stream(4, (f(1e-3),), ge_dev=True), K.Stream(5, (f(1e-3),))]
+    for _ in range(3):
+        tab.run(cfg, streams)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    tab.run(cfg, streams)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    print(json.dumps({"profile_case": kind, "elements": n, "ms": ms, "G_elem_per_s": n / ms / 1e6}))
 
 
 def env_rank():
@@ -329,6 +363,9 @@ def run_ours(args, rank, local_rank, world):
 def main():
     args = parse()
     rank, local_rank, world = env_rank()
+    if args.profile_case:
+        profile_case(args.profile_case)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         return

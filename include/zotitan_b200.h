@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define ZT_ABI_VERSION 1
+#define ZT_ABI_VERSION 2
 
 /* dtypes of parameter tensors */
 #define ZT_F32 0
@@ -78,13 +78,16 @@ ZT_API int zt_randn_at(uint32_t key, const uint32_t* offsets, int64_t n, float* 
  *          (seed-sharded multi-GPU mode);
  *   m      stored-EMA first moment   (ZOOptimizer.m,  zotitan/train_zo.py:257-258)
  *   v      second moment             (ZOOptimizer.v,  zotitan/train_zo.py:265-266)
- *   anchor theta_0 for anchored weight decay (zotitan/train_zo.py:273-274). */
+ *   anchor theta_0 for anchored weight decay (zotitan/train_zo.py:273-274)
+ *   ge     the gradient estimate accumulated across a step's passes, in the
+ *          parameter dtype (grad_est of zotitan/train_zo.py:555-556). */
 typedef struct zt_tensor {
   void* data;
   void* live;
   void* m;
   void* v;
   const void* anchor;
+  void* ge;
   int64_t numel;
   int32_t dtype;   /* ZT_F32 / ZT_BF16 / ZT_F16 */
   int32_t index;   /* position in the reference's named-parameter list */
@@ -106,6 +109,7 @@ typedef struct zt_plan {
 #define ZT_HAS_M 2
 #define ZT_HAS_V 4
 #define ZT_HAS_ANCHOR 8
+#define ZT_HAS_GE 16
 
 #define ZT_UNIT_ELEMS 2048
 
@@ -123,6 +127,8 @@ ZT_API int zt_plan_init(const zt_tensor* host_tensors, int32_t n_tensors, uint32
 /* Roles of a noise stream inside one pass (flags). */
 #define ZT_STREAM_GE 1   /* contributes ge_coef * z to the gradient estimate */
 #define ZT_STREAM_MOM 2  /* contributes mom_coef * z to the reconstructed momentum */
+#define ZT_STREAM_GE_DEV 4 /* with ZT_STREAM_GE: ge_coef is computed on the device from
+                              cfg->dev_vals (see zt_pass_cfg) instead of taken from ge_coef */
 
 /* One noise stream: z = the Gaussian field of pair seed `seed`. Streams are applied in
  * array order. For each stream, the n_chain perturbations theta <- theta + chain[c] * z
@@ -180,6 +186,21 @@ typedef struct zt_pass_cfg {
   int32_t wd;           /* ZT_WD_* */
   float wd_lam;         /* fp32(fp32(lambda) * lr) (:390) */
   float wd_factor;      /* fp32(1 - wd_lam) (:402) */
+  /* Gradient-estimate buffer (ZT_GE_ACCUM only): ge_load starts ge from the tensors' ge
+   * buffers instead of zero; ge_store writes ge back after the streams. */
+  int32_t ge_load;
+  int32_t ge_store;
+  /* Device-side coefficient of a ZT_STREAM_GE_DEV stream, from the pair's two values
+   * v+ = dev_vals[0], v- = dev_vals[1] (device fp32), with the reference's arithmetic:
+   *   pg = fp32(v+ - v-) * dev_inv2eps           (train_zo.py:544, CUDA scalar division)
+   *   pgc = clamp(pg, -dev_tau, dev_tau)          (:545; dev_tau = +inf when not clipping)
+   *   coef = pgc * dev_invz                       (:556, alpha = pgc / z_batch)
+   * so passes can accumulate grad_est before the host has read any value. */
+  const float* dev_vals;
+  float dev_inv2eps;
+  float dev_invz;
+  float dev_tau;
+  int32_t reserved;
 } zt_pass_cfg;
 
 /* A pass is rejected (ZT_ERR_INVALID) when cfg reads or writes a buffer (live, m, v,

@@ -6,9 +6,10 @@ materialised. Used to check (a) on CPU, that the host planner's pass schedule
 reproduces the op-by-op optimizer step (oracle/zo_step.py), and (b) on GPU, that the
 CUDA pass computes bit-identical results given the same noise.
 
-tensors: list of dicts with keys data, live, m, v, anchor (numpy fp32 carriers or
+tensors: list of dicts with keys data, live, m, v, anchor, ge (numpy fp32 carriers or
 None), dtype (oracle.philox code) and index. cfg / streams: any objects with the
-attribute names of zotitan_b200.kernels.PassCfg / Stream.
+attribute names of zotitan_b200.kernels.PassCfg / Stream. dev_values: the (v+, v-) pair
+a ge_dev stream reads (what cfg.dev_vals points at on the device).
 """
 from __future__ import annotations
 
@@ -22,26 +23,40 @@ WD_NONE, WD_STANDARD, WD_ANCHORED_L2, WD_ANCHORED_L1 = 0, 1, 2, 3
 BUF_DATA, BUF_LIVE = 1, 2
 
 
-def run_pass(tensors, n_params, cfg, streams, noise=ph.randn):
+def dev_coefficient(cfg, dev_values):
+    """(v+ - v-) * inv2eps, clamp to +-tau, * invz, each step in fp32."""
+    vp, vn = (np.float32(x) for x in dev_values)
+    pg = np.float32(np.float32(vp - vn) * np.float32(cfg.dev_inv2eps))
+    tau = np.float32(cfg.dev_tau)
+    pg = -tau if pg < -tau else (tau if pg > tau else pg)
+    return float(np.float32(pg * np.float32(cfg.dev_invz)))
+
+
+def run_pass(tensors, n_params, cfg, streams, noise=ph.randn, dev_values=None):
+    dev_coef = dev_coefficient(cfg, dev_values) if dev_values is not None else None
     for t in tensors:
         dt, n = t["dtype"], t["data"].size
         src = t["live"] if cfg.src == BUF_LIVE else t["data"]
         th = np.ascontiguousarray(src, dtype=np.float32).reshape(-1).copy()
-        ge = np.zeros(n, np.float32)
+        ge = (t["ge"].reshape(-1).astype(np.float32).copy() if getattr(cfg, "ge_load", False)
+              else np.zeros(n, np.float32))
         mom = np.zeros(n, np.float32)
         for s in streams:
             z = noise(ph.param_key(s.seed, n_params, t["index"]), n)
             for a in s.chain:
                 ph.add_scaled_(dt, th, z, a)
-            if s.ge is not None:
+            if s.ge is not None or getattr(s, "ge_dev", False):
+                c = dev_coef if getattr(s, "ge_dev", False) else s.ge
                 if cfg.ge_mode == GE_PRODUCT:
-                    ge = ph.mul_scalar(ph.F32, z, s.ge)
+                    ge = ph.mul_scalar(ph.F32, z, c)
                 else:
-                    ph.add_scaled_(dt, ge, z, s.ge)
+                    ph.add_scaled_(dt, ge, z, c)
             if s.mom is not None:
                 ph.add_scaled_(dt, mom, z, s.mom)
         if cfg.ge_scale is not None:
             ge = ph.mul_scalar(ph.F32 if cfg.ge_mode == GE_PRODUCT else dt, ge, cfg.ge_scale)
+        if getattr(cfg, "ge_store", False):
+            t["ge"][...] = ge.reshape(t["ge"].shape)
         if cfg.update:
             if cfg.momentum == MOM_STORED_EMA:
                 m = ph.mul_scalar(dt, t["m"].reshape(-1).astype(np.float32), cfg.beta1)

@@ -37,9 +37,9 @@ def cuda_noise(K):
     return noise
 
 
-def make_case(seed, with_live=False, with_m=False, with_v=False, with_anchor=False):
+def make_case(seed, with_live=False, with_m=False, with_v=False, with_anchor=False, with_ge=False):
     rng = np.random.default_rng(seed)
-    host, dev, keep = [], {"data": [], "live": [], "m": [], "v": [], "anchor": []}, []
+    host, dev, keep = [], {"data": [], "live": [], "m": [], "v": [], "anchor": [], "ge": []}, []
     for i, (n, dt) in enumerate(SPECS):
         unaligned = dt == "unaligned"
         dt = ph.BF16 if unaligned else dt
@@ -50,7 +50,8 @@ def make_case(seed, with_live=False, with_m=False, with_v=False, with_anchor=Fal
              "live": arr(0.02) if with_live else None,
              "m": arr(0.5) if with_m else None,
              "v": arr(0.01, positive=True) if with_v else None,
-             "anchor": arr(0.02) if with_anchor else None}
+             "anchor": arr(0.02) if with_anchor else None,
+             "ge": arr(0.3) if with_ge else None}
         host.append(t)
         for k in dev:
             if t[k] is None:
@@ -68,11 +69,11 @@ def make_case(seed, with_live=False, with_m=False, with_v=False, with_anchor=Fal
 
 
 def table(K, dev, n_params):
-    opt = {k: (dev[k] if any(x is not None for x in dev[k]) else None) for k in ("live", "m", "v", "anchor")}
+    opt = {k: (dev[k] if any(x is not None for x in dev[k]) else None) for k in ("live", "m", "v", "anchor", "ge")}
     return K.ParamTable(dev["data"], n_params=n_params, **opt)
 
 
-def compare(host, dev, keys=("data", "live", "m", "v")):
+def compare(host, dev, keys=("data", "live", "m", "v", "ge")):
     for i, t in enumerate(host):
         for k in keys:
             if t[k] is None:
@@ -84,13 +85,34 @@ def compare(host, dev, keys=("data", "live", "m", "v")):
 N_PARAMS = 40  # tensors sit at indices 0..9 of a 40-long parameter list
 
 
-def run_both(K, cfg, streams, **case_kw):
+def run_both(K, cfg, streams, dev_values=None, **case_kw):
     host, dev, keep = make_case(3, **case_kw)
     tab = table(K, dev, N_PARAMS)
+    if dev_values is not None:
+        vals = torch.tensor(dev_values, dtype=torch.float32, device="cuda")
+        cfg.dev_vals = vals.data_ptr()
     tab.run(cfg, streams)
     torch.cuda.synchronize()
-    run_pass(host, N_PARAMS, cfg, streams, noise=cuda_noise(K))
+    run_pass(host, N_PARAMS, cfg, streams, noise=cuda_noise(K), dev_values=dev_values)
     compare(host, dev)
+
+
+@pytest.mark.parametrize("tau", [float("inf"), 3.0])
+def test_onthefly_accumulation_with_device_coefficient(K, tau):
+    """Restore pass of a pair that also accumulates its grad_est term, the coefficient
+    computed on the device from the pair's two values (and clamped when clipping), then
+    perturbs the next pair; and the first such pass, which starts grad_est from zero."""
+    l = L()
+    f = lambda x: float(np.float32(x))  # noqa: E731
+    e = f(1e-3)
+    for load in (True, False):
+        cfg = K.PassCfg(ge_mode=l.ZT_GE_ACCUM, ge_load=load, ge_store=True, dev_inv2eps=f(1 / f(2e-3)),
+                        dev_invz=f(1 / f(3)), dev_tau=f(tau) if tau != float("inf") else tau)
+        streams = [K.Stream(50, (e,), ge_dev=True), K.Stream(51, (e,))]
+        run_both(K, cfg, streams, dev_values=(2.0137, 2.0051), with_ge=True)
+    # the last pass: loads grad_est, adds the last term with a host coefficient, updates
+    cfg = K.PassCfg(ge_mode=l.ZT_GE_ACCUM, ge_load=True, update=True, lr=f(1e-2))
+    run_both(K, cfg, [K.Stream(52, (e,), ge=f(0.7))], with_ge=True)
 
 
 def L():

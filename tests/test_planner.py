@@ -27,6 +27,7 @@ def make_tensors(params, dtypes, planner, sharded):
                    "m": np.zeros_like(p) if planner.needs_m else None,
                    "v": np.zeros_like(p) if planner.needs_v else None,
                    "anchor": p.copy() if planner.needs_anchor else None,
+                   "ge": np.zeros_like(p) if planner.ge_onthefly else None,
                    "dtype": dt, "index": i})
     return ts
 
@@ -44,7 +45,7 @@ def run_planner(case, world, rank=0):
         vals = [next(vals_all) for _ in range(2 * Z)]
         prev = None
         for j in local:
-            run_pass(ts, n, *_spec(pl.plus_pass(j, prev)))
+            run_pass(ts, n, *_spec(pl.plus_pass(j, prev)), dev_values=_dev(pl.plus_pass(j, prev), vals))
             snaps.append(flat([t["live"] if world > 1 else t["data"] for t in ts]))
             run_pass(ts, n, *_spec(pl.minus_pass(j)))
             snaps.append(flat([t["live"] if world > 1 else t["data"] for t in ts]))
@@ -60,6 +61,11 @@ def run_planner(case, world, rank=0):
 
 def _spec(s):
     return s.cfg, s.streams
+
+
+def _dev(s, vals):
+    p = s.cfg.dev_pair
+    return None if p is None else (vals[2 * p], vals[2 * p + 1])
 
 
 def run_oracle(case):
@@ -129,13 +135,22 @@ def test_planner_rejects_unsupported():
 
 
 def test_planner_stream_limit():
+    """Seed-window momentum regenerates every pair in the last pass: more than 256
+    streams is refused. Plain MeZO accumulates on the fly and needs one stream."""
     from helpers import ns
-    cfg = StepCase(_G, "mezo_f32_z1").cfg_dict
+    cfg = StepCase(_G, "seedwin_f32_z1").cfg_dict
     cfg["z_batch"] = 300
     pl = StepPlanner(ns(cfg))
     pl.start()
     with pytest.raises(ValueError, match="noise streams"):
         pl.finish([1.0, 0.5] * 300)
+    cfg = StepCase(_G, "mezo_f32_z1").cfg_dict
+    cfg["z_batch"] = 300
+    pl = StepPlanner(ns(cfg))
+    assert pl.ge_onthefly
+    pl.start()
+    spec, _ = pl.finish([1.0, 0.5] * 300)
+    assert len(spec.streams) == 1 and spec.cfg.ge_load
 
 
 def test_planner_state_dict_roundtrip():

@@ -17,7 +17,7 @@ ZT_MAX_STREAMS = 256
 ZT_MAX_CHAIN = 3
 ZT_MAX_NUMEL = 2**31 - 1
 ZT_UNIT_ELEMS = 2048
-ZT_STREAM_GE, ZT_STREAM_MOM = 1, 2
+ZT_STREAM_GE, ZT_STREAM_MOM, ZT_STREAM_GE_DEV = 1, 2, 4
 ZT_GE_NONE, ZT_GE_PRODUCT, ZT_GE_ACCUM = 0, 1, 2
 ZT_MOM_NONE, ZT_MOM_STORED_EMA, ZT_MOM_SEED_WINDOW = 0, 1, 2
 ZT_WD_NONE, ZT_WD_STANDARD, ZT_WD_ANCHORED_L2, ZT_WD_ANCHORED_L1 = 0, 1, 2, 3
@@ -31,7 +31,7 @@ ZT_STATIC_MAX_TENSORS = 1024
 
 class ZtTensor(ctypes.Structure):
     _fields_ = [("data", ctypes.c_void_p), ("live", ctypes.c_void_p), ("m", ctypes.c_void_p),
-                ("v", ctypes.c_void_p), ("anchor", ctypes.c_void_p), ("numel", ctypes.c_int64),
+                ("v", ctypes.c_void_p), ("anchor", ctypes.c_void_p), ("ge", ctypes.c_void_p), ("numel", ctypes.c_int64),
                 ("dtype", ctypes.c_int32), ("index", ctypes.c_int32)]
 
 
@@ -54,7 +54,9 @@ class ZtPassCfg(ctypes.Structure):
                 ("second_moment", ctypes.c_int32), ("beta2", ctypes.c_float), ("one_minus_beta2", ctypes.c_float),
                 ("bc2", ctypes.c_float), ("denom_eps", ctypes.c_float), ("update", ctypes.c_int32),
                 ("lr", ctypes.c_float), ("wd", ctypes.c_int32), ("wd_lam", ctypes.c_float),
-                ("wd_factor", ctypes.c_float)]
+                ("wd_factor", ctypes.c_float), ("ge_load", ctypes.c_int32), ("ge_store", ctypes.c_int32),
+                ("dev_vals", ctypes.c_void_p), ("dev_inv2eps", ctypes.c_float), ("dev_invz", ctypes.c_float),
+                ("dev_tau", ctypes.c_float), ("reserved", ctypes.c_int32)]
 
 
 class ZtError(RuntimeError):
@@ -92,8 +94,8 @@ def load():
         fn.argtypes = args
     lib.zt_plan_workspace_bytes.restype = ctypes.c_size_t
     lib.zt_plan_workspace_bytes.argtypes = [I32]
-    if lib.zt_abi_version() != 1:
-        raise ZtError(f"{LIB_PATH}: ABI version {lib.zt_abi_version()} != 1")
+    if lib.zt_abi_version() != 2:
+        raise ZtError(f"{LIB_PATH}: ABI version {lib.zt_abi_version()} != 2")
     _lib = lib
     return lib
 

@@ -193,15 +193,22 @@ __device__ __forceinline__ void run_chain(const PassParams& P, const zt_tensor& 
 }
 
 template <int DT, int EPT>
-__device__ __forceinline__ void run_full(const PassParams& P, const zt_tensor& t, int64_t e0, int nvalid, bool vec) {
+__device__ __forceinline__ void run_full(const PassParams& P, const zt_tensor& t, int64_t e0, int nvalid, bool vec,
+                                         float dev_coef) {
   using R = zt::Dt<DT>;
   using IO = Io<DT, EPT>;
   const zt_pass_cfg& c = P.cfg;
 
   float th[EPT], ge[EPT], mom[EPT];
   IO::load(c.src == ZT_BUF_LIVE ? t.live : t.data, e0, nvalid, vec, th);
+  if (c.ge_load) {
+    IO::load(t.ge, e0, nvalid, vec, ge);
+  } else {
 #pragma unroll
-  for (int e = 0; e < EPT; ++e) { ge[e] = 0.0f; mom[e] = 0.0f; }
+    for (int e = 0; e < EPT; ++e) ge[e] = 0.0f;
+  }
+#pragma unroll
+  for (int e = 0; e < EPT; ++e) mom[e] = 0.0f;
 
   const uint32_t ctr0 = (uint32_t)e0;
   for (int s = 0; s < P.n_streams; ++s) {
@@ -217,7 +224,7 @@ __device__ __forceinline__ void run_full(const PassParams& P, const zt_tensor& t
       for (int e = 0; e < EPT; ++e) th[e] = R::round(__fmaf_rn(z[e], a, th[e]));
     }
     if (S.flags & ZT_STREAM_GE) {
-      const float a = S.ge_coef;
+      const float a = (S.flags & ZT_STREAM_GE_DEV) ? dev_coef : S.ge_coef;
       if (c.ge_mode == ZT_GE_PRODUCT) {
 #pragma unroll
         for (int e = 0; e < EPT; ++e) ge[e] = __fmul_rn(z[e], a);  // fp32 (train_zo.py:552)
@@ -242,6 +249,8 @@ __device__ __forceinline__ void run_full(const PassParams& P, const zt_tensor& t
       for (int e = 0; e < EPT; ++e) ge[e] = R::round(__fmul_rn(ge[e], c.ge_scale));
     }
   }
+
+  if (c.ge_store) IO::store(t.ge, e0, nvalid, vec, ge);
 
   if (c.update) {
     float g[EPT];
@@ -322,6 +331,16 @@ __device__ __forceinline__ void walk_units(const PassParams& P) {
   int64_t lo = 0, hi = -1;  // unit range of the cached tensor
   zt_tensor t{};
   bool base_vec = false;
+  // Coefficient of a ZT_STREAM_GE_DEV stream: the reference's (v+ - v-)/(2 eps), clamp
+  // and /z_batch in fp32 (train_zo.py:544-556), from the two device values. A NaN value
+  // propagates through the comparisons unchanged, as torch.clamp does.
+  float dev_coef = 0.0f;
+  if (kFull && c.dev_vals) {
+    const float d = __fsub_rn(__ldg(c.dev_vals), __ldg(c.dev_vals + 1));
+    float pg = __fmul_rn(d, c.dev_inv2eps);
+    pg = pg < -c.dev_tau ? -c.dev_tau : (pg > c.dev_tau ? c.dev_tau : pg);
+    dev_coef = __fmul_rn(pg, c.dev_invz);
+  }
   for (int64_t u = blockIdx.x; u < P.n_units; u += gridDim.x) {
     if (u < lo || u >= hi) {
       const int ti = find_tensor(P.unit_prefix, P.n_tensors, u);
@@ -334,6 +353,7 @@ __device__ __forceinline__ void walk_units(const PassParams& P) {
       if (kFull && c.update && c.second_moment) base_vec = base_vec && aligned16(t.v);
       if (kFull && c.update && (c.wd == ZT_WD_ANCHORED_L1 || c.wd == ZT_WD_ANCHORED_L2))
         base_vec = base_vec && aligned16(t.anchor);
+      if (kFull && (c.ge_load || c.ge_store)) base_vec = base_vec && aligned16(t.ge);
     }
     const int64_t e0 = (u - lo) * ZT_UNIT_ELEMS + (int64_t)(threadIdx.x % kThreadsT) * EPT;
     if (e0 >= t.numel) continue;
@@ -341,9 +361,9 @@ __device__ __forceinline__ void walk_units(const PassParams& P) {
     const int nvalid = rem < EPT ? (int)rem : EPT;
     const bool vec = base_vec && nvalid == EPT;
     if (kFull) {
-      if (t.dtype == ZT_BF16) run_full<ZT_BF16, EPT>(P, t, e0, nvalid, vec);
-      else if (t.dtype == ZT_F32) run_full<ZT_F32, EPT>(P, t, e0, nvalid, vec);
-      else run_full<ZT_F16, EPT>(P, t, e0, nvalid, vec);
+      if (t.dtype == ZT_BF16) run_full<ZT_BF16, EPT>(P, t, e0, nvalid, vec, dev_coef);
+      else if (t.dtype == ZT_F32) run_full<ZT_F32, EPT>(P, t, e0, nvalid, vec, dev_coef);
+      else run_full<ZT_F16, EPT>(P, t, e0, nvalid, vec, dev_coef);
     } else {
       if (t.dtype == ZT_BF16) run_chain<ZT_BF16, EPT>(P, t, e0, nvalid, vec);
       else if (t.dtype == ZT_F32) run_chain<ZT_F32, EPT>(P, t, e0, nvalid, vec);
@@ -412,7 +432,7 @@ int plan_build(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_para
   if (((uintptr_t)workspace & 15) != 0) return zt::set_error(ZT_ERR_INVALID, "zt_plan_init: workspace not 16-byte aligned");
   std::vector<int64_t> prefix((size_t)n_tensors + 1, 0);
   int64_t total = 0;
-  int32_t buffers = ZT_HAS_LIVE | ZT_HAS_M | ZT_HAS_V | ZT_HAS_ANCHOR;
+  int32_t buffers = ZT_HAS_LIVE | ZT_HAS_M | ZT_HAS_V | ZT_HAS_ANCHOR | ZT_HAS_GE;
   for (int32_t i = 0; i < n_tensors; ++i) {
     const zt_tensor& t = host_tensors[i];
     if (t.numel < 0 || t.numel > (int64_t)ZT_MAX_NUMEL)
@@ -428,6 +448,7 @@ int plan_build(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_para
       if (!t.m) buffers &= ~ZT_HAS_M;
       if (!t.v) buffers &= ~ZT_HAS_V;
       if (!t.anchor) buffers &= ~ZT_HAS_ANCHOR;
+      if (!t.ge) buffers &= ~ZT_HAS_GE;
     }
     prefix[i + 1] = prefix[i] + (t.numel + ZT_UNIT_ELEMS - 1) / ZT_UNIT_ELEMS;
     total += t.numel;
@@ -483,6 +504,10 @@ int pass_launch(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* st
       return zt::set_error(ZT_ERR_INVALID, "zt_pass: second moment needs v buffers");
     if (cfg->update && anchored && !(plan->buffers & ZT_HAS_ANCHOR))
       return zt::set_error(ZT_ERR_INVALID, "zt_pass: anchored weight decay needs anchor buffers");
+    if ((cfg->ge_load || cfg->ge_store) && !(plan->buffers & ZT_HAS_GE))
+      return zt::set_error(ZT_ERR_INVALID, "zt_pass: ge_load/ge_store need ge buffers");
+    if ((cfg->ge_load || cfg->ge_store) && cfg->ge_mode != ZT_GE_ACCUM)
+      return zt::set_error(ZT_ERR_INVALID, "zt_pass: ge_load/ge_store need ge_mode ACCUM");
   }
   int dev = 0;
   if (int rc = zt::check_cuda(cudaGetDevice(&dev), "zt_pass: cudaGetDevice")) return rc;
@@ -500,7 +525,10 @@ int pass_launch(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* st
   for (int s = 0; s < n_streams; ++s) {
     const zt_stream& S = streams[s];
     if (S.n_chain < 0 || S.n_chain > ZT_MAX_CHAIN) return zt::set_error(ZT_ERR_INVALID, "zt_pass: n_chain outside [0, 3]");
-    if ((S.flags & ~(ZT_STREAM_GE | ZT_STREAM_MOM)) != 0) return zt::set_error(ZT_ERR_INVALID, "zt_pass: bad stream flags");
+    if ((S.flags & ~(ZT_STREAM_GE | ZT_STREAM_MOM | ZT_STREAM_GE_DEV)) != 0)
+      return zt::set_error(ZT_ERR_INVALID, "zt_pass: bad stream flags");
+    if ((S.flags & ZT_STREAM_GE_DEV) && (!(S.flags & ZT_STREAM_GE) || !cfg->dev_vals || cfg->ge_mode != ZT_GE_ACCUM))
+      return zt::set_error(ZT_ERR_INVALID, "zt_pass: GE_DEV stream needs GE, dev_vals and ge_mode ACCUM");
     if ((S.flags & ZT_STREAM_GE) && cfg->ge_mode == ZT_GE_NONE)
       return zt::set_error(ZT_ERR_INVALID, "zt_pass: GE stream with ge_mode NONE");
     if ((S.flags & ZT_STREAM_MOM) && cfg->momentum != ZT_MOM_SEED_WINDOW)
@@ -515,7 +543,7 @@ int pass_launch(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* st
     K.pad[0] = K.pad[1] = 0;
   }
   for (int s = n_streams; s < ZT_MAX_STREAMS; ++s) P.streams[s] = KStream{};
-  bool full = cfg->update || cfg->ge_scale_on;
+  bool full = cfg->update || cfg->ge_scale_on || cfg->ge_load || cfg->ge_store;
   for (int s = 0; s < n_streams; ++s) full = full || streams[s].flags != 0;
   if (full) {
     constexpr int th = ZT_UNIT_ELEMS / kFullEpt;

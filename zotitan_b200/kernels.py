@@ -62,6 +62,7 @@ class Stream:
     chain: tuple = ()
     ge: float | None = None
     mom: float | None = None
+    ge_dev: bool = False      # ge coefficient computed on the device from the pass's dev values
 
     def to_c(self) -> L.ZtStream:
         if len(self.chain) > L.ZT_MAX_CHAIN:
@@ -71,7 +72,9 @@ class Stream:
         for k, a in enumerate(self.chain):
             s.chain[k] = a
         s.n_chain = len(self.chain)
-        s.flags = (L.ZT_STREAM_GE if self.ge is not None else 0) | (L.ZT_STREAM_MOM if self.mom is not None else 0)
+        s.flags = ((L.ZT_STREAM_GE if (self.ge is not None or self.ge_dev) else 0)
+                   | (L.ZT_STREAM_MOM if self.mom is not None else 0)
+                   | (L.ZT_STREAM_GE_DEV if self.ge_dev else 0))
         s.ge_coef = self.ge if self.ge is not None else 0.0
         s.mom_coef = self.mom if self.mom is not None else 0.0
         return s
@@ -98,6 +101,13 @@ class PassCfg:
     wd: int = L.ZT_WD_NONE
     wd_lam: float = 0.0
     wd_factor: float = 1.0
+    ge_load: bool = False
+    ge_store: bool = False
+    dev_pair: int | None = None     # pair whose device values feed a ge_dev stream
+    dev_vals: int = 0               # device address of that pair's (v+, v-), set at launch
+    dev_inv2eps: float = 0.0
+    dev_invz: float = 0.0
+    dev_tau: float = float("inf")
 
     def to_c(self) -> L.ZtPassCfg:
         c = L.ZtPassCfg()
@@ -108,6 +118,9 @@ class PassCfg:
         c.second_moment, c.beta2, c.one_minus_beta2 = int(self.second_moment), self.beta2, self.one_minus_beta2
         c.bc2, c.denom_eps, c.update, c.lr = self.bc2, self.denom_eps, int(self.update), self.lr
         c.wd, c.wd_lam, c.wd_factor = self.wd, self.wd_lam, self.wd_factor
+        c.ge_load, c.ge_store = int(self.ge_load), int(self.ge_store)
+        c.dev_vals = self.dev_vals or None
+        c.dev_inv2eps, c.dev_invz, c.dev_tau = self.dev_inv2eps, self.dev_invz, self.dev_tau
         return c
 
 
@@ -121,7 +134,7 @@ def _streams_array(streams):
 
 
 def pass_static(params, cfg: PassCfg, streams: list, n_params=None, indices=None, live=None, m=None, v=None,
-                anchor=None) -> None:
+                anchor=None, ge=None) -> None:
     """One fused pass through zt_pass_static: no workspace, nothing allocated on the device.
 
     For callers that cannot allocate device memory (see include/zotitan_b200.h). Same
@@ -129,7 +142,7 @@ def pass_static(params, cfg: PassCfg, streams: list, n_params=None, indices=None
     ZT_STATIC_MAX_TENSORS tensors. Calls that can overlap on the GPU race on the
     library's one descriptor array, so keep them on one stream."""
     desc = ParamTable.__new__(ParamTable)
-    desc._describe(params, n_params, indices, live, m, v, anchor)
+    desc._describe(params, n_params, indices, live, m, v, anchor, ge)
     arr = _streams_array(streams)
     c = cfg.to_c()
     with torch.cuda.device(desc.device):
@@ -146,8 +159,8 @@ class ParamTable:
     The table keeps references to every tensor, so the pointers stay valid.
     """
 
-    def __init__(self, params, n_params=None, indices=None, live=None, m=None, v=None, anchor=None):
-        self._describe(params, n_params, indices, live, m, v, anchor)
+    def __init__(self, params, n_params=None, indices=None, live=None, m=None, v=None, anchor=None, ge=None):
+        self._describe(params, n_params, indices, live, m, v, anchor, ge)
         lib = L.load()
         n = len(self.params)
         nbytes = lib.zt_plan_workspace_bytes(n)
@@ -158,7 +171,7 @@ class ParamTable:
                                      ctypes.byref(self.plan), _stream_ptr(self.device)), "zt_plan_init")
         self.numel = int(self.plan.numel_total)
 
-    def _describe(self, params, n_params, indices, live, m, v, anchor):
+    def _describe(self, params, n_params, indices, live, m, v, anchor, ge=None):
         """Validate the tensors and build the host zt_tensor array."""
         params = list(params)
         if not params:
@@ -168,12 +181,12 @@ class ParamTable:
             raise ValueError("ParamTable needs CUDA tensors (no CPU fallback)")
         self.n_params = len(params) if n_params is None else n_params
         self.indices = list(range(len(params))) if indices is None else list(indices)
-        self.params, self.live, self.m, self.v, self.anchor = params, live, m, v, anchor
+        self.params, self.live, self.m, self.v, self.anchor, self.ge = params, live, m, v, anchor, ge
         arr = (L.ZtTensor * len(params))()
         for i, p in enumerate(params):
             self._check(p, p, f"param {i}")
             arr[i].data = p.data_ptr()
-            for name in ("live", "m", "v", "anchor"):
+            for name in ("live", "m", "v", "anchor", "ge"):
                 lst = getattr(self, name)
                 if lst is not None and lst[i] is not None:
                     self._check(lst[i], p, f"{name}[{i}]")

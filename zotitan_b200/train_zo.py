@@ -10,11 +10,11 @@ grad_est buffer, momentum replay and the update). Here every pass is one
 ``zt_pass`` launch over all trainable tensors that regenerates the noise in
 registers (include/zotitan_b200.h):
 
-  pair j:    [restore of pair j-1 (+eps z_{j-1}) fused with] +eps z_j ; score ;
-             -2eps z_j ; score
-  step end:  restore of the last pair + gradient estimate from all pair seeds +
+  pair j:    [restore of pair j-1 (+eps z_{j-1}), its grad_est term] fused with
+             +eps z_j ; score ; -2eps z_j ; score
+  step end:  restore of the last pair + the remaining gradient-estimate terms +
              momentum replay + (m, v) update + parameter update + weight decay,
-             one pass, no noise or grad_est in memory.
+             one pass; noise is never stored.
 
 Arithmetic follows the reference's eager op order with the fp32 opmath scalars of
 torch's CUDA kernels (tensor / Python scalar multiplies by the fp32 reciprocal),
@@ -162,6 +162,17 @@ class StepPlanner:
         self.needs_m = cfg.mom.momentum_method == "stored_ema"
         self.needs_v = cfg.mom.second_moment
         self.needs_anchor = wd.strategy == "anchored" and self.wd_enabled
+        # grad_est is consumed by the update itself (no momentum), the stored EMA, or v.
+        self.need_ge = (not self.has_momentum) or cfg.mom.momentum_method == "stored_ema" or cfg.mom.second_moment
+        # Single-GPU, several pairs, coefficients known pair by pair: each restore pass
+        # also accumulates its pair into a grad_est buffer in the parameter dtype (the
+        # reference's own accumulation, train_zo.py:555-556), with the coefficient computed
+        # on the device from the pair's values, so the last pass needs one noise stream
+        # instead of z_batch. Fitness shaping needs the whole population first and seed-
+        # window momentum regenerates every seed anyway; the sharded schedule must replay
+        # the pairs in order on the master.
+        self.ge_onthefly = (not self.sharded and cfg.z_batch > 1 and not self.shaping and self.need_ge
+                            and cfg.mom.momentum_method != "seed_window")
 
     # -- reference helpers (zotitan/train_zo.py:287-293, 427-508) ----------------
     def _draw_seeds(self, n):
@@ -213,10 +224,17 @@ class StepPlanner:
         return self.local
 
     def plus_pass(self, j: int, prev: int | None) -> PassSpec:
-        """+eps z_j; single-GPU mode also restores the previous pair (+eps z_prev) first."""
+        """+eps z_j; single-GPU mode also restores the previous pair (+eps z_prev) first and,
+        when accumulating on the fly, adds prev's grad_est contribution."""
         a = f32(self.cfg.eps)
         if self.sharded:
             return PassSpec(PassCfg(src=L.ZT_BUF_DATA, dst=L.ZT_BUF_LIVE), [Stream(self.seeds[j], (a,))])
+        if self.ge_onthefly and prev is not None:
+            cfg = PassCfg(src=L.ZT_BUF_DATA, dst=L.ZT_BUF_DATA, ge_mode=L.ZT_GE_ACCUM, ge_load=prev > 0,
+                          ge_store=True, dev_pair=prev, dev_inv2eps=f32_recip(2 * self.cfg.eps),
+                          dev_invz=f32_recip(self.cfg.z_batch),
+                          dev_tau=f32(self.tau) if self.clip_in_loop else float("inf"))
+            return PassSpec(cfg, [Stream(self.seeds[prev], (a,), ge_dev=True), Stream(self.seeds[j], (a,))])
         streams = ([Stream(self.seeds[prev], (a,))] if prev is not None else []) + [Stream(self.seeds[j], (a,))]
         return PassSpec(PassCfg(src=L.ZT_BUF_DATA, dst=L.ZT_BUF_DATA), streams)
 
@@ -275,9 +293,7 @@ class StepPlanner:
             else:
                 clip_frac = 0.0
 
-        # grad_est is consumed by: the update itself (no momentum), the stored EMA, or v.
-        need_ge = (not self.has_momentum) or mc.momentum_method == "stored_ema" or mc.second_moment
-        if not need_ge:
+        if not self.need_ge:
             ge_mode = L.ZT_GE_NONE
             ge_scale = None
 
@@ -299,6 +315,8 @@ class StepPlanner:
                 chain = (a_pos, a_neg, a_pos)   # replay pair j's rounding chain on the master
             else:
                 chain = (a_pos,) if j == Z - 1 else ()   # restore of the last pair (:371)
+                if self.ge_onthefly and j < Z - 1:
+                    continue                      # already restored and accumulated
             streams.append(Stream(self.seeds[j], chain,
                                   ge_coefs[j] if ge_mode != L.ZT_GE_NONE else None,
                                   mom_coefs[0][j] if mom_coefs else None))
@@ -328,7 +346,8 @@ class StepPlanner:
             m_scale=f32_recip(f32((1.0 - mc.beta1 ** t) + mc.denom_eps)) if mc.momentum_method == "stored_ema" else 1.0,
             second_moment=mc.second_moment, beta2=f32(mc.beta2), one_minus_beta2=f32(1 - mc.beta2),
             bc2=f32(1.0 - mc.beta2 ** t), denom_eps=f32(mc.denom_eps),
-            update=True, lr=lr32, wd=wd_code, wd_lam=wd_lam, wd_factor=f32(1.0 - wd_lam))
+            update=True, lr=lr32, wd=wd_code, wd_lam=wd_lam, wd_factor=f32(1.0 - wd_lam),
+            ge_load=self.ge_onthefly)
         metrics = {
             "loss": mean_loss,
             "proj_grad": sum(pg) / Z,
@@ -402,13 +421,18 @@ class ZOOptimizer:
         # theta_0 for anchored decay stays in HBM (the reference pins it in host
         # memory and copies it every step, train_zo.py:274, :406)
         self.theta_0 = [p.clone() for p in self.params] if pl.needs_anchor else None
+        # grad_est buffer of the on-the-fly accumulation (same size as the reference's
+        # zeros_like grad_est for z_batch > 1)
+        self.ge = [torch.zeros_like(p) for p in self.params] if pl.ge_onthefly else None
+        dev = self.params[0].device
+        self.vals_buf = torch.zeros(2 * max(1, cfg.z_batch), dtype=torch.float32, device=dev)
         if pl.sharded:
             # model reads `live` (the parameters' own storage); `master` stays unperturbed
             self.master = [p.clone() for p in self.params]
             self.table = ParamTable(self.master, live=self.params, m=self.m, v=self.v, anchor=self.theta_0)
         else:
             self.master = None
-            self.table = ParamTable(self.params, m=self.m, v=self.v, anchor=self.theta_0)
+            self.table = ParamTable(self.params, m=self.m, v=self.v, anchor=self.theta_0, ge=self.ge)
         self._metric_keys = None
 
     # properties mirroring the reference's attributes
@@ -425,6 +449,8 @@ class ZOOptimizer:
         self.planner._seed_ctr = int(v)
 
     def _run(self, spec: PassSpec) -> None:
+        if spec.cfg.dev_pair is not None:
+            spec.cfg.dev_vals = self.vals_buf.data_ptr() + 8 * spec.cfg.dev_pair
         self.table.run(spec.cfg, spec.streams)
 
     def _acquire(self, model, batch):
@@ -448,12 +474,17 @@ class ZOOptimizer:
                 self._run(pl.minus_pass(j))
                 vn, mn = self._acquire(model, batches[j])
                 prev = j
-                vals_t += [vp.detach().float().reshape(()).to(dev), vn.detach().float().reshape(()).to(dev)]
+                vp = vp.detach().float().reshape(()).to(dev)
+                vn = vn.detach().float().reshape(()).to(dev)
+                if not pl.sharded:   # read by the next restore pass (device coefficient)
+                    self.vals_buf[2 * j].copy_(vp)
+                    self.vals_buf[2 * j + 1].copy_(vn)
+                vals_t += [vp, vn]
                 metric_dicts += [mp, mn]
         if pl.sharded:
             vals, metrics_avg = self._gather(vals_t, metric_dicts, local)
         else:
-            vals = torch.stack(vals_t).tolist()          # the step's one host sync (:564-565)
+            vals = self.vals_buf[: 2 * Z].tolist()      # the step's one host sync (:564-565)
             metrics_avg = _aggregate_metrics(metric_dicts)
         spec, metrics = pl.finish(vals)
         with torch.inference_mode():
