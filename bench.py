@@ -4,9 +4,9 @@
 Workload (N=1 default): the kernel microbench on the full parameter set of a
 Llama-3.2-1B-shaped model (146 bf16 tensors, 1,235,814,400 params, N(0,0.02)),
 64 seeds per step drawn from a seeded uint64 stream, eps = 1e-3. One step = for each
-seed: +eps (fused with the previous seed's restore), -2eps; then the last restore,
-the 64-stream gradient estimate and the update in one pass: 129 fused passes, no
-forward (synthetic pair values). ``value`` = ZO steps/s over all ranks (seeds sharded
+seed: +eps (fused with the previous seed's restore and its grad_est term), -2eps; then
+the last restore, the last grad_est term and the update in one pass: 129 fused passes,
+no forward (synthetic pair values). ``value`` = ZO steps/s over all ranks (seeds sharded
 round-robin over ranks, one all-gather of the pair values, replicated final pass).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
@@ -129,7 +129,7 @@ class ClockSampler:
 
 # ── CPU baseline: the oracle port on host cores ───────────────────────────────────────
 
-def cpu_sample_step_rate(total_numel: int, n_seeds: int, sample_elems: int = 1 << 24, pairs: int = 2):
+def cpu_sample_step_rate(total_numel: int, n_seeds: int, sample_elems: int = 1 << 26, pairs: int = 16):
     """Time the reference's per-pair algorithm (materialise z, three perturb ops, one
     grad_est accumulation, zotitan/train_zo.py:534-556) on `sample_elems` bf16 elements
     for `pairs` pairs plus the update, with one thread per core (ctypes releases the GIL),
@@ -184,7 +184,7 @@ def run_reference(args, rank, world):
     total = numel(llama_param_shapes(LLAMA_1B))
     vals = []
     for i in range(args.warmup + args.steps):
-        r = cpu_sample_step_rate(total, args.seeds, sample_elems=1 << 24, pairs=2)
+        r = cpu_sample_step_rate(total, args.seeds, sample_elems=1 << 25, pairs=4)
         if i >= args.warmup:
             vals.append(r["value"])
     v = statistics.median(vals)
