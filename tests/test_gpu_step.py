@@ -179,11 +179,8 @@ def test_sharded_optimizer_single_process_group():
     dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device("cuda", 0))
     try:
         ps = [torch.nn.Parameter(torch.from_numpy(p).to(TDT[d]).cuda()) for p, d in zip(case.params(), case.dtypes)]
-        opt = ZOOptimizer(list(zip(case.names, ps)), case.cfg, ReplayScore(case.values, ps))
-        opt.planner.sharded = True  # force the sharded schedule on one rank
-        opt.master = [p.detach().clone() for p in ps]
-        from zotitan_b200.kernels import ParamTable
-        opt.table = ParamTable(opt.master, live=[p.data for p in ps])
+        opt = ZOOptimizer(list(zip(case.names, ps)), case.cfg, ReplayScore(case.values, ps), sharded=True)
+        assert opt.master is not None and opt.ge is None
         for s in range(case.spec["steps"]):
             opt.step(None, [None] * case.cfg.z_batch)
             assert np.array_equal(flat([p.detach().float().cpu().numpy() for p in ps]), a1[s])

@@ -128,9 +128,11 @@ class StepPlanner:
     """Host half of ``ZOOptimizer.step``: seed counter, clip history, seed window,
     fitness shaping, the pass schedule and every scalar the passes take.
 
-    ``world > 1`` selects the seed-sharded schedule (master/live copies)."""
+    ``world > 1`` selects the seed-sharded schedule (master/live copies); ``sharded``
+    forces it on or off (a one-rank group can run the sharded schedule)."""
 
-    def __init__(self, cfg: ZOConfig, total_steps: int = 0, rank: int = 0, world: int = 1):
+    def __init__(self, cfg: ZOConfig, total_steps: int = 0, rank: int = 0, world: int = 1,
+                 sharded: bool | None = None):
         if cfg.perturbation.distribution != "gaussian":
             # The fused passes regenerate Gaussian fields; low-rank / polar directions
             # (train_zo.py:304-320) are not part of this path.
@@ -142,7 +144,7 @@ class StepPlanner:
         self._total_steps = total_steps
         self._seed_ctr = 0
         self.rank, self.world = rank, world
-        self.sharded = world > 1
+        self.sharded = world > 1 if sharded is None else bool(sharded)
         self.has_momentum = cfg.mom.momentum_method != "none"
         self._pg_hist = (collections.deque(maxlen=cfg.clip.window)
                          if cfg.clip.strategy != "none" and cfg.clip.clip_pct > 0 else None)
@@ -399,9 +401,11 @@ class ZOOptimizer:
     """``ZOOptimizer`` (zotitan/train_zo.py:242-606) on fused CUDA passes.
 
     ``process_group``: torch.distributed group to shard pairs over; default: the
-    default group when it is initialised with more than one rank."""
+    default group when it is initialised with more than one rank. ``sharded``: force the
+    seed-sharded schedule on (it then needs an initialised process group) or off."""
 
-    def __init__(self, named_params: list, cfg: ZOConfig, score_fn, total_steps: int = 0, process_group=None):
+    def __init__(self, named_params: list, cfg: ZOConfig, score_fn, total_steps: int = 0, process_group=None,
+                 sharded: bool | None = None):
         self.named_params = named_params
         self.params = [p.data for _, p in named_params]
         self.cfg = cfg
@@ -413,7 +417,7 @@ class ZOOptimizer:
                 raise ValueError(f"{n}: trainable tensors must be contiguous")
         self.group = process_group
         rank, world = world_info(process_group)
-        self.planner = StepPlanner(cfg, total_steps, rank, world)
+        self.planner = StepPlanner(cfg, total_steps, rank, world, sharded=sharded)
         self.rank, self.world = rank, world
         pl = self.planner
         self.m = [torch.zeros_like(p) for p in self.params] if pl.needs_m else None
