@@ -250,21 +250,29 @@ def run_ours(args, rank, local_rank, world):
     rng = np.random.default_rng(12345)   # seeded uint64 seed stream, identical on every rank
     opt.planner._draw_seeds = lambda n: [int(x) for x in rng.integers(0, 2**64 - 1, n, dtype=np.uint64)]
 
-    # per-launch events on the -2eps passes (one noise stream, read+write of every element)
-    events, counter = [], {"launches": 0, "on": False}
+    # Per-launch CUDA events on the launching (current) stream for the two pass kinds:
+    #  - "perturb": the -2eps pass, one noise stream, read + write of theta (4 B/element bf16);
+    #  - "accum": restore of pair j-1 + its grad_est term + perturb of pair j, two noise
+    #    streams, theta and grad_est read + written (8 B/element) - the dominant kernel.
+    events, counter = {"perturb": [], "accum": []}, {"launches": 0, "on": False}
     orig_run = opt.table.run
 
     def run(cfg_, streams):
         if counter["on"]:
             counter["launches"] += 1
-        rec = counter["on"] and len(streams) == 1 and streams[0].chain and streams[0].chain[0] < 0
-        if rec:
+        kind = None
+        if counter["on"]:
+            if len(streams) == 1 and streams[0].chain and streams[0].chain[0] < 0:
+                kind = "perturb"
+            elif any(s.ge_dev for s in streams):
+                kind = "accum"
+        if kind:
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
         orig_run(cfg_, streams)
-        if rec:
+        if kind:
             b.record()
-            events.append((a, b))
+            events[kind].append((a, b))
     opt.table.run = run
 
     batches = [None] * args.seeds
@@ -290,7 +298,8 @@ def run_ours(args, rank, local_rank, world):
     counter["on"] = False
     clk = clocks.stop()
     ms = t0.elapsed_time(t1)
-    kern_ms = [a.elapsed_time(b) for a, b in events]
+    pert_ms = [a.elapsed_time(b) for a, b in events["perturb"]]
+    acc_ms = [a.elapsed_time(b) for a, b in events["accum"]]
     launches = counter["launches"]
 
     # e2e: same steps through the public API with every pair value copied from pinned host memory
@@ -306,12 +315,12 @@ def run_ours(args, rank, local_rank, world):
     wall_e2e = time.perf_counter() - w0
     e2e_ms = e0.elapsed_time(e1)
 
+    pmean = float(np.mean(pert_ms)) if pert_ms else 0.0
+    amean = float(np.mean(acc_ms)) if acc_ms else 0.0
     if world > 1:
-        t = torch.tensor([ms, e2e_ms, float(np.mean(kern_ms)) if kern_ms else 0.0], device=dev)
+        t = torch.tensor([ms, e2e_ms, pmean, amean], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms, kmean = t.tolist()
-    else:
-        kmean = float(np.mean(kern_ms)) if kern_ms else 0.0
+        ms, e2e_ms, pmean, amean = t.tolist()
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
@@ -323,11 +332,17 @@ def run_ours(args, rank, local_rank, world):
     except (OSError, ValueError):
         pass
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
-    bytes_per_launch = 2 * 2 * numel          # bf16 read + write of every element
-    achieved = bytes_per_launch / (kmean * 1e-3) / 1e9 if kmean else None
+    perturb_bytes = 2 * 2 * numel            # bf16 theta read + write
+    accum_bytes = 2 * 2 * 2 * numel          # bf16 theta and grad_est read + write
+    perturb_gbs = perturb_bytes / (pmean * 1e-3) / 1e9 if pmean else None
+    if amean:   # single-GPU schedule: the restore/accumulate/perturb pass dominates
+        achieved, kname, kbytes = accum_bytes / (amean * 1e-3) / 1e9, \
+            "full_kernel: restore + grad_est accumulation + perturb (2 noise streams)", accum_bytes
+    else:       # sharded schedule: the +eps / -2eps passes on the live copy dominate
+        achieved, kname, kbytes = perturb_gbs, "chain_kernel: -2eps perturb pass (1 noise stream)", perturb_bytes
     traffic = None
     prof = os.path.join(HERE, "profiles", "pass_kernel_traffic.json")
-    if os.path.exists(prof):
+    if amean and os.path.exists(prof):
         try:
             traffic = json.load(open(prof)).get("dram_bytes_per_launch")
         except ValueError:
@@ -341,11 +356,13 @@ def run_ours(args, rank, local_rank, world):
                    "params": numel, "tensors": len(named), "seeds_per_step": args.seeds, "eps": EPS,
                    "passes_per_step": 2 * args.seeds + 1, "parallelism": f"seed-sharded x{world}",
                    "l2": "inputs (2.47 GB of bf16 parameters) larger than L2"},
-        "perturb_pass_gbs": achieved, "perturb_pass_ms": kmean,
-        "philox_gelem_per_s": numel / (kmean * 1e-3) / 1e9 if kmean else None,
+        "perturb_pass_gbs": perturb_gbs, "perturb_pass_ms": pmean, "accum_pass_ms": amean,
+        "philox_gelem_per_s": numel / (pmean * 1e-3) / 1e9 if pmean else None,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": (achieved / hbm_peak) if achieved else None, "traffic": traffic,
-                     "kernel": "pass_kernel, -2eps pass (1 noise stream)",
+                     "kernel": kname, "algorithmic_bytes_per_launch": kbytes,
+                     "note": "instruction-bound (Philox4x32-10 + logf/cosf per element per noise stream); "
+                             "see profiles/",
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback 6650 GB/s"},
         "clocks": clk,
         "gpu_launches": launches,
