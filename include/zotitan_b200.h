@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define ZT_ABI_VERSION 2
+#define ZT_ABI_VERSION 3
 
 /* dtypes of parameter tensors */
 #define ZT_F32 0
@@ -201,6 +201,13 @@ typedef struct zt_pass_cfg {
   float dev_invz;
   float dev_tau;
   int32_t reserved;
+  /* Work-unit range [unit_begin, unit_end) of the plan this pass covers; unit_end <= 0
+   * means every unit. Units number the plan's tensors' 2048-element blocks in table
+   * order, so a range is a contiguous slice when tensors are laid out back to back with
+   * each padded to a multiple of ZT_UNIT_ELEMS (the sharded update splits the last pass
+   * of a step this way across ranks). */
+  int64_t unit_begin;
+  int64_t unit_end;
 } zt_pass_cfg;
 
 /* A pass is rejected (ZT_ERR_INVALID) when cfg reads or writes a buffer (live, m, v,

@@ -32,55 +32,86 @@ def dev_coefficient(cfg, dev_values):
     return float(np.float32(pg * np.float32(cfg.dev_invz)))
 
 
+UNIT = 2048
+
+
 def run_pass(tensors, n_params, cfg, streams, noise=ph.randn, dev_values=None):
+    """A unit range (cfg.unit_begin, cfg.unit_end) restricts the pass to those 2048-element
+    units of the table (numbered in table order); elements outside are left untouched."""
     dev_coef = dev_coefficient(cfg, dev_values) if dev_values is not None else None
+    ub, ue = getattr(cfg, "unit_begin", 0), getattr(cfg, "unit_end", 0)
+    base = 0
     for t in tensors:
-        dt, n = t["dtype"], t["data"].size
-        src = t["live"] if cfg.src == BUF_LIVE else t["data"]
-        th = np.ascontiguousarray(src, dtype=np.float32).reshape(-1).copy()
-        ge = (t["ge"].reshape(-1).astype(np.float32).copy() if getattr(cfg, "ge_load", False)
-              else np.zeros(n, np.float32))
-        mom = np.zeros(n, np.float32)
-        for s in streams:
-            z = noise(ph.param_key(s.seed, n_params, t["index"]), n)
-            for a in s.chain:
-                ph.add_scaled_(dt, th, z, a)
-            if s.ge is not None or getattr(s, "ge_dev", False):
-                c = dev_coef if getattr(s, "ge_dev", False) else s.ge
-                if cfg.ge_mode == GE_PRODUCT:
-                    ge = ph.mul_scalar(ph.F32, z, c)
-                else:
-                    ph.add_scaled_(dt, ge, z, c)
-            if s.mom is not None:
-                ph.add_scaled_(dt, mom, z, s.mom)
-        if cfg.ge_scale is not None:
-            ge = ph.mul_scalar(ph.F32 if cfg.ge_mode == GE_PRODUCT else dt, ge, cfg.ge_scale)
-        if getattr(cfg, "ge_store", False):
-            t["ge"][...] = ge.reshape(t["ge"].shape)
-        if cfg.update:
-            if cfg.momentum == MOM_STORED_EMA:
-                m = ph.mul_scalar(dt, t["m"].reshape(-1).astype(np.float32), cfg.beta1)
-                ph.add_scaled_(dt, m, ge, cfg.one_minus_beta1)
-                t["m"][...] = m.reshape(t["m"].shape)
-                g = ph.mul_scalar(dt, m, cfg.m_scale)
-            elif cfg.momentum == MOM_SEED_WINDOW:
-                g = mom
+        units = (t["data"].size + UNIT - 1) // UNIT
+        lo_u, hi_u = base, base + units
+        base += units
+        if ue > 0:
+            a, b = max(ub, lo_u), min(ue, hi_u)
+            if a >= b:
+                continue
+            sub = {k: (v.reshape(-1)[(a - lo_u) * UNIT: min((b - lo_u) * UNIT, v.size)]
+                       if isinstance(v, np.ndarray) else v) for k, v in t.items()}
+            _run_tensor(sub, n_params, cfg, streams, noise, dev_coef, ctr_offset=(a - lo_u) * UNIT)
+        else:
+            _run_tensor(t, n_params, cfg, streams, noise, dev_coef, ctr_offset=0)
+
+
+def _run_tensor(t, n_params, cfg, streams, noise, dev_coef, ctr_offset):
+    dt, n = t["dtype"], t["data"].size
+    src = t["live"] if cfg.src == BUF_LIVE else t["data"]
+    th = np.ascontiguousarray(src, dtype=np.float32).reshape(-1).copy()
+    ge = (t["ge"].reshape(-1).astype(np.float32).copy() if getattr(cfg, "ge_load", False)
+          else np.zeros(n, np.float32))
+    mom = np.zeros(n, np.float32)
+    for s in streams:
+        key = ph.param_key(s.seed, n_params, t["index"])
+        z = noise(key, n) if ctr_offset == 0 else _noise_at(noise, key, ctr_offset, n)
+        for a in s.chain:
+            ph.add_scaled_(dt, th, z, a)
+        if s.ge is not None or getattr(s, "ge_dev", False):
+            c = dev_coef if getattr(s, "ge_dev", False) else s.ge
+            if cfg.ge_mode == GE_PRODUCT:
+                ge = ph.mul_scalar(ph.F32, z, c)
             else:
-                g = ge
-            if cfg.second_moment:
-                v = ph.mul_scalar(dt, t["v"].reshape(-1).astype(np.float32), cfg.beta2)
-                ph.addcmul_(dt, v, ge, ge, cfg.one_minus_beta2)
-                t["v"][...] = v.reshape(t["v"].shape)
-                vh = ph.div_scalar(dt, v, cfg.bc2)
-                ph.sqrt_add_(dt, vh, cfg.denom_eps)
-                ph.addcdiv_(dt, th, g, vh, -cfg.lr)
-            else:
-                ph.add_scaled_(dt, th, np.ascontiguousarray(g, dtype=np.float32), -cfg.lr)
-            if cfg.wd == WD_STANDARD:
-                th = ph.mul_scalar(dt, th, cfg.wd_factor)
-            elif cfg.wd in (WD_ANCHORED_L1, WD_ANCHORED_L2):
-                ph.anchored_(dt, th, t["anchor"].reshape(-1).astype(np.float32), cfg.wd_lam, cfg.wd == WD_ANCHORED_L1)
-        if cfg.dst & BUF_DATA:
-            t["data"][...] = th.reshape(t["data"].shape)
-        if cfg.dst & BUF_LIVE:
-            t["live"][...] = th.reshape(t["live"].shape)
+                ph.add_scaled_(dt, ge, z, c)
+        if s.mom is not None:
+            ph.add_scaled_(dt, mom, z, s.mom)
+    if cfg.ge_scale is not None:
+        ge = ph.mul_scalar(ph.F32 if cfg.ge_mode == GE_PRODUCT else dt, ge, cfg.ge_scale)
+    if getattr(cfg, "ge_store", False):
+        t["ge"][...] = ge.reshape(t["ge"].shape)
+    if cfg.update:
+        if cfg.momentum == MOM_STORED_EMA:
+            m = ph.mul_scalar(dt, t["m"].reshape(-1).astype(np.float32), cfg.beta1)
+            ph.add_scaled_(dt, m, ge, cfg.one_minus_beta1)
+            t["m"][...] = m.reshape(t["m"].shape)
+            g = ph.mul_scalar(dt, m, cfg.m_scale)
+        elif cfg.momentum == MOM_SEED_WINDOW:
+            g = mom
+        else:
+            g = ge
+        if cfg.second_moment:
+            v = ph.mul_scalar(dt, t["v"].reshape(-1).astype(np.float32), cfg.beta2)
+            ph.addcmul_(dt, v, ge, ge, cfg.one_minus_beta2)
+            t["v"][...] = v.reshape(t["v"].shape)
+            vh = ph.div_scalar(dt, v, cfg.bc2)
+            ph.sqrt_add_(dt, vh, cfg.denom_eps)
+            ph.addcdiv_(dt, th, g, vh, -cfg.lr)
+        else:
+            ph.add_scaled_(dt, th, np.ascontiguousarray(g, dtype=np.float32), -cfg.lr)
+        if cfg.wd == WD_STANDARD:
+            th = ph.mul_scalar(dt, th, cfg.wd_factor)
+        elif cfg.wd in (WD_ANCHORED_L1, WD_ANCHORED_L2):
+            ph.anchored_(dt, th, t["anchor"].reshape(-1).astype(np.float32), cfg.wd_lam, cfg.wd == WD_ANCHORED_L1)
+    if cfg.dst & BUF_DATA:
+        t["data"][...] = th.reshape(t["data"].shape)
+    if cfg.dst & BUF_LIVE:
+        t["live"][...] = th.reshape(t["live"].shape)
+
+
+def _noise_at(noise, key, off0, n):
+    """Gaussians at element offsets off0 .. off0+n-1 of a tensor."""
+    try:
+        return noise(key, n, off0)
+    except TypeError:
+        return noise(key, off0 + n)[off0:]

@@ -34,7 +34,7 @@ def _init(rank, world, port, timeout_s):
     return dist
 
 
-def _sharded_worker(rank, world, port, name, out_dir):
+def _sharded_worker(rank, world, port, name, out_dir, shard_update=False):
     sys.path[:0] = [os.path.dirname(HERE), HERE]
     import torch
     from helpers import StepCase, flat, step_cases
@@ -47,6 +47,11 @@ def _sharded_worker(rank, world, port, name, out_dir):
     params = case.params()
     pl = StepPlanner(case.cfg, total_steps=case.spec["total_steps"], rank=rank, world=world)
     assert pl.sharded
+    layout = None
+    if shard_update:   # last pass on this rank's unit range, then all-gather the flat master
+        from zotitan_b200.flat import FlatLayout
+        layout = FlatLayout([p.size for p in params], world)
+        pl.unit_range = layout.shard_units(rank)
     ts = [{"data": p, "live": p.copy(), "m": np.zeros_like(p) if pl.needs_m else None,
            "v": np.zeros_like(p) if pl.needs_v else None, "anchor": p.copy() if pl.needs_anchor else None,
            "ge": None, "dtype": dt, "index": i} for i, (p, dt) in enumerate(zip(params, case.dtypes))]
@@ -67,16 +72,32 @@ def _sharded_worker(rank, world, port, name, out_dir):
         vals = [x for row in gathered for x in row]
         spec, _ = pl.finish(vals)
         run_pass(ts, len(ts), spec.cfg, spec.streams)
+        if layout is not None:
+            buf = np.zeros(layout.numel, np.float32)
+            for o, p in zip(layout.offsets, params):
+                buf[o:o + p.size] = p.reshape(-1)
+            ub, ue = layout.shard_units(rank)
+            mine = torch.from_numpy(buf[ub * 2048: ue * 2048].copy())
+            full = torch.zeros(layout.numel, dtype=torch.float32)
+            dist.all_gather_into_tensor(full, mine)
+            full = full.numpy()
+            for o, p, t in zip(layout.offsets, params, ts):
+                p.reshape(-1)[:] = full[o:o + p.size]
+                t["live"].reshape(-1)[:] = full[o:o + p.size]
     np.save(os.path.join(out_dir, f"rank{rank}.npy"), flat(params))
     dist.barrier()
     dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("shard_update", [False, True])
 @pytest.mark.parametrize("name", ["mezo_bf16_z3", "seedwin_adam_bf16_z2", "es_rank_f32"])
-def test_sharded_gloo_ranks_match_single_gpu(name, tmp_path):
+def test_sharded_gloo_ranks_match_single_gpu(name, shard_update, tmp_path):
+    """Both the replicated last pass and the sharded update (each rank updates its unit
+    range, one all-gather completes the parameters) end bit-identical to one GPU."""
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_sharded_worker, args=(r, 2, port, name, str(tmp_path))) for r in range(2)]
+    procs = [ctx.Process(target=_sharded_worker, args=(r, 2, port, name, str(tmp_path), shard_update))
+             for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:

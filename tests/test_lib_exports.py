@@ -32,7 +32,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version_and_key(lib):
-    assert lib.zt_abi_version() == 2
+    assert lib.zt_abi_version() == 3
     from oracle import philox as ph
     for seed, n, i in [(0, 1, 0), (1234, 39, 7), (2**40 + 3, 146, 145), (2**64 - 1, 448, 3)]:
         assert lib.zt_param_key(seed, n, i) == ph.param_key(seed, n, i) == (seed * n + i) & 0x7FFFFFFF
@@ -42,7 +42,7 @@ def test_struct_layouts_match_header(lib):
     assert ctypes.sizeof(L.ZtTensor) == 64
     assert ctypes.sizeof(L.ZtStream) == 40
     assert ctypes.sizeof(L.ZtPlan) == 48
-    assert ctypes.sizeof(L.ZtPassCfg) == 112 and L.ZtPassCfg.dev_vals.offset == 88
+    assert ctypes.sizeof(L.ZtPassCfg) == 128 and L.ZtPassCfg.dev_vals.offset == 88 and L.ZtPassCfg.unit_begin.offset == 112
     assert lib.zt_plan_workspace_bytes(0) == 8
     assert lib.zt_plan_workspace_bytes(3) == 256 + 8 * 4
     assert lib.zt_plan_workspace_bytes(5) == 512 + 8 * 6

@@ -56,7 +56,8 @@ class ZtPassCfg(ctypes.Structure):
                 ("lr", ctypes.c_float), ("wd", ctypes.c_int32), ("wd_lam", ctypes.c_float),
                 ("wd_factor", ctypes.c_float), ("ge_load", ctypes.c_int32), ("ge_store", ctypes.c_int32),
                 ("dev_vals", ctypes.c_void_p), ("dev_inv2eps", ctypes.c_float), ("dev_invz", ctypes.c_float),
-                ("dev_tau", ctypes.c_float), ("reserved", ctypes.c_int32)]
+                ("dev_tau", ctypes.c_float), ("reserved", ctypes.c_int32), ("unit_begin", ctypes.c_int64),
+                ("unit_end", ctypes.c_int64)]
 
 
 class ZtError(RuntimeError):
@@ -94,8 +95,8 @@ def load():
         fn.argtypes = args
     lib.zt_plan_workspace_bytes.restype = ctypes.c_size_t
     lib.zt_plan_workspace_bytes.argtypes = [I32]
-    if lib.zt_abi_version() != 2:
-        raise ZtError(f"{LIB_PATH}: ABI version {lib.zt_abi_version()} != 2")
+    if lib.zt_abi_version() != 3:
+        raise ZtError(f"{LIB_PATH}: ABI version {lib.zt_abi_version()} != 3")
     _lib = lib
     return lib
 

@@ -48,7 +48,8 @@ static_assert(sizeof(KStream) == 32, "KStream layout");
 struct PassParams {
   const zt_tensor* tensors;
   const int64_t* unit_prefix;
-  int64_t n_units;
+  int64_t unit_begin;  // first unit of this launch
+  int64_t n_units;     // one past the last unit of this launch
   int32_t n_tensors;
   uint32_t n_params;
   zt_pass_cfg cfg;
@@ -341,7 +342,7 @@ __device__ __forceinline__ void walk_units(const PassParams& P) {
     pg = pg < -c.dev_tau ? -c.dev_tau : (pg > c.dev_tau ? c.dev_tau : pg);
     dev_coef = __fmul_rn(pg, c.dev_invz);
   }
-  for (int64_t u = blockIdx.x; u < P.n_units; u += gridDim.x) {
+  for (int64_t u = P.unit_begin + blockIdx.x; u < P.n_units; u += gridDim.x) {
     if (u < lo || u >= hi) {
       const int ti = find_tensor(P.unit_prefix, P.n_tensors, u);
       lo = __ldg(P.unit_prefix + ti);
@@ -514,10 +515,15 @@ int pass_launch(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* st
   if (dev != plan->device) return zt::set_error(ZT_ERR_INVALID, "zt_pass: plan belongs to another device");
   if (plan->n_units == 0) return ZT_OK;
 
+  int64_t ub = cfg->unit_begin, ue = cfg->unit_end;
+  if (ue <= 0 || ue > plan->n_units) ue = plan->n_units;
+  if (ub < 0) return zt::set_error(ZT_ERR_INVALID, "zt_pass: unit_begin < 0");
+  if (ub >= ue) return ZT_OK;
   PassParams P;
   P.tensors = plan->tensors;
   P.unit_prefix = plan->unit_prefix;
-  P.n_units = plan->n_units;
+  P.unit_begin = ub;
+  P.n_units = ue;
   P.n_tensors = plan->n_tensors;
   P.n_params = plan->n_params;
   P.cfg = *cfg;
@@ -547,10 +553,10 @@ int pass_launch(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* st
   for (int s = 0; s < n_streams; ++s) full = full || streams[s].flags != 0;
   if (full) {
     constexpr int th = ZT_UNIT_ELEMS / kFullEpt;
-    full_kernel<<<grid_for(full_kernel, th, plan->n_units, g_occ_full), th, 0, zt::as_stream(stream)>>>(P);
+    full_kernel<<<grid_for(full_kernel, th, ue - ub, g_occ_full), th, 0, zt::as_stream(stream)>>>(P);
   } else {
     constexpr int th = ZT_UNIT_ELEMS / kChainEpt;
-    chain_kernel<<<grid_for(chain_kernel, th, plan->n_units, g_occ_chain), th, 0, zt::as_stream(stream)>>>(P);
+    chain_kernel<<<grid_for(chain_kernel, th, ue - ub, g_occ_chain), th, 0, zt::as_stream(stream)>>>(P);
   }
   return zt::check_cuda(cudaGetLastError(), "zt_pass launch");
 }

@@ -108,6 +108,8 @@ class PassCfg:
     dev_inv2eps: float = 0.0
     dev_invz: float = 0.0
     dev_tau: float = float("inf")
+    unit_begin: int = 0             # work-unit range of the pass (unit_end 0: all units)
+    unit_end: int = 0
 
     def to_c(self) -> L.ZtPassCfg:
         c = L.ZtPassCfg()
@@ -121,6 +123,7 @@ class PassCfg:
         c.ge_load, c.ge_store = int(self.ge_load), int(self.ge_store)
         c.dev_vals = self.dev_vals or None
         c.dev_inv2eps, c.dev_invz, c.dev_tau = self.dev_inv2eps, self.dev_invz, self.dev_tau
+        c.unit_begin, c.unit_end = self.unit_begin, self.unit_end
         return c
 
 

@@ -145,6 +145,10 @@ class StepPlanner:
         self._seed_ctr = 0
         self.rank, self.world = rank, world
         self.sharded = world > 1 if sharded is None else bool(sharded)
+        # Sharded update: the step's last pass covers only this rank's unit range of a
+        # flat parameter layout, followed by an all-gather of the updated master (set by
+        # ZOOptimizer when the layout is in place).
+        self.unit_range: tuple[int, int] | None = None
         self.has_momentum = cfg.mom.momentum_method != "none"
         self._pg_hist = (collections.deque(maxlen=cfg.clip.window)
                          if cfg.clip.strategy != "none" and cfg.clip.clip_pct > 0 else None)
@@ -338,9 +342,15 @@ class StepPlanner:
             wd_code = L.ZT_WD_STANDARD
         elif wd.strategy == "anchored" and self.wd_enabled:
             wd_code = L.ZT_WD_ANCHORED_L1 if wd.penalty == "l1" else L.ZT_WD_ANCHORED_L2
+        if self.sharded and self.unit_range is not None:
+            dst = L.ZT_BUF_DATA                       # this rank's slice of the master only
+        elif self.sharded:
+            dst = L.ZT_BUF_DATA | L.ZT_BUF_LIVE
+        else:
+            dst = L.ZT_BUF_DATA
         pcfg = PassCfg(
             src=L.ZT_BUF_DATA,
-            dst=(L.ZT_BUF_DATA | L.ZT_BUF_LIVE) if self.sharded else L.ZT_BUF_DATA,
+            dst=dst,
             ge_mode=ge_mode, ge_scale=ge_scale,
             momentum={"none": L.ZT_MOM_NONE, "stored_ema": L.ZT_MOM_STORED_EMA,
                       "seed_window": L.ZT_MOM_SEED_WINDOW}[mc.momentum_method],
@@ -350,6 +360,8 @@ class StepPlanner:
             bc2=f32(1.0 - mc.beta2 ** t), denom_eps=f32(mc.denom_eps),
             update=True, lr=lr32, wd=wd_code, wd_lam=wd_lam, wd_factor=f32(1.0 - wd_lam),
             ge_load=self.ge_onthefly)
+        if self.sharded and self.unit_range is not None:
+            pcfg.unit_begin, pcfg.unit_end = self.unit_range
         metrics = {
             "loss": mean_loss,
             "proj_grad": sum(pg) / Z,
@@ -402,10 +414,15 @@ class ZOOptimizer:
 
     ``process_group``: torch.distributed group to shard pairs over; default: the
     default group when it is initialised with more than one rank. ``sharded``: force the
-    seed-sharded schedule on (it then needs an initialised process group) or off."""
+    seed-sharded schedule on (it then needs an initialised process group) or off.
+    ``shard_update`` (sharded schedule, trainable tensors of one dtype): each rank runs
+    the step's last pass on 1/W of the elements and one in-place all-gather of the
+    updated parameters completes them, instead of every rank regenerating every pair's
+    noise over all elements. The trainable tensors are then re-homed into one flat
+    buffer (the Parameters keep their identity; ``p.data`` becomes a view)."""
 
     def __init__(self, named_params: list, cfg: ZOConfig, score_fn, total_steps: int = 0, process_group=None,
-                 sharded: bool | None = None):
+                 sharded: bool | None = None, shard_update: bool = True):
         self.named_params = named_params
         self.params = [p.data for _, p in named_params]
         self.cfg = cfg
@@ -430,7 +447,25 @@ class ZOOptimizer:
         self.ge = [torch.zeros_like(p) for p in self.params] if pl.ge_onthefly else None
         dev = self.params[0].device
         self.vals_buf = torch.zeros(2 * max(1, cfg.z_batch), dtype=torch.float32, device=dev)
-        if pl.sharded:
+        self.layout = None
+        one_dtype = len({p.dtype for p in self.params}) == 1
+        if pl.sharded and shard_update and one_dtype:
+            from .flat import FlatLayout
+            self.layout = FlatLayout([p.numel() for p in self.params], world)
+            dt = self.params[0].dtype
+            shapes = [p.shape for p in self.params]
+            self.flat_live, live = self.layout.alloc(dt, dev, like=self.params)
+            for (_, p), view in zip(named_params, live):
+                p.data = view                      # the model now reads the flat live copy
+            self.params = live
+            self.flat_master, self.master = self.layout.alloc(dt, dev, like=self.params)
+            flat_view = lambda: self.layout.views(torch.zeros(self.layout.numel, dtype=dt, device=dev), shapes)  # noqa: E731
+            self.m = flat_view() if pl.needs_m else None
+            self.v = flat_view() if pl.needs_v else None
+            self.theta_0 = self.layout.views(self.flat_master.clone(), shapes) if pl.needs_anchor else None
+            self.table = ParamTable(self.master, live=self.params, m=self.m, v=self.v, anchor=self.theta_0)
+            pl.unit_range = self.layout.shard_units(rank)
+        elif pl.sharded:
             # model reads `live` (the parameters' own storage); `master` stays unperturbed
             self.master = [p.clone() for p in self.params]
             self.table = ParamTable(self.master, live=self.params, m=self.m, v=self.v, anchor=self.theta_0)
@@ -493,6 +528,11 @@ class ZOOptimizer:
         spec, metrics = pl.finish(vals)
         with torch.inference_mode():
             self._run(spec)
+            if self.layout is not None:
+                import torch.distributed as dist
+                dist.all_gather_into_tensor(self.flat_master, self.layout.shard_slice(self.flat_master, self.rank),
+                                            group=self.group)
+                self.flat_live.copy_(self.flat_master)
         metrics.update(metrics_avg)
         return metrics
 
