@@ -227,6 +227,36 @@ typedef struct zt_pass_cfg {
 ZT_API int zt_pass(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* streams, int32_t n_streams,
             void* stream);
 
+/* ---- EGGROLL population linear layer -------------------------------------------- */
+
+/* One linear layer of a population forward in which member i's weight is perturbed by a
+ * rank-4 term: W + sigma_i * A_i B_i^T. With X holding all members' activations (member i
+ * owns rows [i*rows_per_member, (i+1)*rows_per_member)):
+ *   Y[m, :] = X[m, :] W^T + sigma_i * (X[m, :] B_i) A_i^T,   i = m / rows_per_member.
+ * The base GEMM runs on tcgen05 tensor cores (bf16 in, fp32 accumulate, bf16 out); the
+ * rank-4 term is added in the GEMM epilogue, so W is shared and never copied per member.
+ * The reference has no EGGROLL implementation (it is only named in README.md:11); the
+ * perturbation follows its low-rank branch, z = P Psi (zotitan/train_zo.py:304-320),
+ * with A_i = P and B_i = Psi^T and the normalisation folded into sigma_i. */
+typedef struct zt_eggroll_args {
+  const void* x;          /* [m, k] bf16, row-major, 16-byte aligned */
+  const void* w;          /* [n, k] bf16, row-major (the layer's weight as torch stores it) */
+  const float* a;         /* [members, n, 4] fp32: A_i */
+  const float* b;         /* [members, k, 4] fp32: B_i */
+  const float* sigma;     /* [members] fp32: signed per-member scale */
+  float* xb;              /* [m, 4] fp32 workspace, written by the call: X B_i */
+  void* y;                /* [m, n] bf16 output */
+  int64_t m, n, k;        /* m % 128 == 0, n % 256 == 0, k % 64 == 0 */
+  int32_t rows_per_member;  /* multiple of 128 dividing m */
+  int32_t rank;           /* must be 4 */
+} zt_eggroll_args;
+
+ZT_API int zt_eggroll_linear(const zt_eggroll_args* args, void* stream);
+
+/* Reads and clears the device-side error code of the EGGROLL kernels (0: none; nonzero:
+ * a bounded wait inside the GEMM expired and that launch returned early). Synchronous. */
+ZT_API int zt_eggroll_take_error(int32_t* code);
+
 /* ---- the fused pass without a caller-provided workspace -------------------------- */
 
 #define ZT_STATIC_MAX_TENSORS 1024

@@ -25,7 +25,8 @@ ZT_BUF_DATA, ZT_BUF_LIVE = 1, 2
 
 # every function include/zotitan_b200.h declares
 EXPORTS = ("zt_last_error", "zt_abi_version", "zt_param_key", "zt_philox_words", "zt_randn",
-           "zt_randn_at", "zt_plan_workspace_bytes", "zt_plan_init", "zt_pass", "zt_pass_static")
+           "zt_randn_at", "zt_plan_workspace_bytes", "zt_plan_init", "zt_pass", "zt_pass_static",
+           "zt_eggroll_linear", "zt_eggroll_take_error")
 ZT_STATIC_MAX_TENSORS = 1024
 
 
@@ -58,6 +59,13 @@ class ZtPassCfg(ctypes.Structure):
                 ("dev_vals", ctypes.c_void_p), ("dev_inv2eps", ctypes.c_float), ("dev_invz", ctypes.c_float),
                 ("dev_tau", ctypes.c_float), ("reserved", ctypes.c_int32), ("unit_begin", ctypes.c_int64),
                 ("unit_end", ctypes.c_int64)]
+
+
+class ZtEggrollArgs(ctypes.Structure):
+    _fields_ = [("x", ctypes.c_void_p), ("w", ctypes.c_void_p), ("a", ctypes.c_void_p), ("b", ctypes.c_void_p),
+                ("sigma", ctypes.c_void_p), ("xb", ctypes.c_void_p), ("y", ctypes.c_void_p),
+                ("m", ctypes.c_int64), ("n", ctypes.c_int64), ("k", ctypes.c_int64),
+                ("rows_per_member", ctypes.c_int32), ("rank", ctypes.c_int32)]
 
 
 class ZtError(RuntimeError):
@@ -93,6 +101,10 @@ def load():
         fn = getattr(lib, name)
         fn.restype = ctypes.c_int
         fn.argtypes = args
+    lib.zt_eggroll_linear.restype = ctypes.c_int
+    lib.zt_eggroll_linear.argtypes = [ctypes.POINTER(ZtEggrollArgs), P]
+    lib.zt_eggroll_take_error.restype = ctypes.c_int
+    lib.zt_eggroll_take_error.argtypes = [ctypes.POINTER(ctypes.c_int32)]
     lib.zt_plan_workspace_bytes.restype = ctypes.c_size_t
     lib.zt_plan_workspace_bytes.argtypes = [I32]
     if lib.zt_abi_version() != 3:

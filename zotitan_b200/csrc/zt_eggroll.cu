@@ -1,0 +1,428 @@
+// EGGROLL population linear layer on the 5th-generation tensor cores.
+//
+//   Y[m, :] = X[m, :] W^T + sigma_i * (X[m, :] B_i) A_i^T,   i = m / rows_per_member
+//
+// X [M, K] bf16 holds the activations of a whole population chunk (member i owns rows
+// [i*T, (i+1)*T)), W [N, K] bf16 is the shared base weight, A_i [N, 4] and B_i [K, 4]
+// (fp32) are member i's rank-4 factors and sigma_i its signed scale. The base GEMM runs
+// on tcgen05 tensor cores with TMA-staged tiles; the rank-4 correction is added in the
+// epilogue from X B_i (computed by a bandwidth-bound pre-pass) and the member's A_i
+// tile, so W is never perturbed or copied per member.
+//
+// GEMM structure (one persistent CTA per SM, 6 warps):
+//   warp 0      TMA producer: 128x64 X tile + 256x64 W tile per stage, 4 stages,
+//               128-byte swizzle, completion tracked by mbarrier transaction bytes;
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=256, K=16, bf16 in,
+//               fp32 accumulate in tensor memory) and tcgen05.commit to free stages;
+//   warps 2..5  epilogue: tcgen05.ld of the 128x256 fp32 accumulator (each warp reads
+//               its 32-lane quarter), rank-4 correction, bf16 store. The accumulator is
+//               double-buffered in tensor memory (2 x 256 columns) so the epilogue of one
+//               tile overlaps the MMAs of the next.
+// Every mbarrier wait is bounded by a clock deadline; on expiry the kernel records an
+// error code, stops issuing, drains its own copies and MMAs (again bounded), frees its
+// tensor memory and returns.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "zt_common.cuh"
+
+namespace {
+
+constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
+constexpr int kUmmaK = 16;
+constexpr int kThreadsEgg = 192;  // 6 warps
+constexpr uint32_t kStageA = kBM * kBK * 2;   // 16 KB
+constexpr uint32_t kStageB = kBN * kBK * 2;   // 32 KB
+constexpr uint32_t kStageBytes = kStageA + kStageB;
+constexpr uint32_t kTmemCols = 2 * kBN;       // two fp32 accumulators of 128 x 256
+constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + kStages * kStageBytes + 256 /*barriers, flags*/;
+constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
+
+__device__ int g_eggroll_error = 0;
+
+struct EggParams {
+  CUtensorMap tmap_x;  // X [M, K], box {64, 128}
+  CUtensorMap tmap_w;  // W [N, K], box {64, 256}
+  const float* a;      // [members, N, 4]
+  const float* sigma;  // [members]
+  const float* xb;     // [M, 4]
+  __nv_bfloat16* y;    // [M, N]
+  int32_t m_blocks, n_blocks, k_blocks;
+  int32_t n;
+  int32_t rows_per_member;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the completion of the phase with the given parity. Returns false if
+// the deadline passes or another role already aborted (*abort != 0).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int code) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      atomicExch(&g_eggroll_error, code);
+      *abort = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tmap, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (stride byte offset), leading byte offset unused (1), descriptor
+// version 1, layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor: fp32 accumulator, bf16 A and B, both K-major, N = 256, M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
+                            ((uint32_t)(kBM >> 4) << 24);
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kThreadsEgg, 1) eggroll_gemm_kernel(const __grid_constant__ EggParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t* stage_base = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* full = bars;                 // [kStages]
+  uint64_t* empty = bars + kStages;      // [kStages]
+  uint64_t* accf = bars + 2 * kStages;   // [2]
+  uint64_t* acce = bars + 2 * kStages + 2;  // [2]
+  uint64_t* drain = bars + 2 * kStages + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 5);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&accf[b], 1); mbar_init(&acce[b], 4 * 32); }
+    mbar_init(drain, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {  // the whole warp allocates tensor memory
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int n_tiles = P.m_blocks * P.n_blocks;
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer
+      int last_phase[kStages];
+      for (int s = 0; s < kStages; ++s) last_phase[s] = -1;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+        const int nb = tile % P.n_blocks, mb = tile / P.n_blocks;
+        for (int kb = 0; kb < P.k_blocks; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t round = it / kStages;
+          if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort, 1)) { ok = false; break; }
+          uint8_t* sa = stage_base + s * kStageBytes;
+          mbar_expect_tx(&full[s], kStageBytes);
+          tma_load_2d(sa, &P.tmap_x, &full[s], kb * kBK, mb * kBM);
+          tma_load_2d(sa + kStageA, &P.tmap_w, &full[s], kb * kBK, nb * kBN);
+          last_phase[s] = (int)(round & 1);
+        }
+      }
+      // Drain: every issued copy must have landed before the CTA can exit.
+      for (int s = 0; s < kStages; ++s)
+        if (last_phase[s] >= 0) {
+          const long long t0 = clock64();
+          while (!mbar_try_wait(&full[s], (uint32_t)last_phase[s]) && clock64() - t0 < kWaitCycles) {
+          }
+        }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---- MMA issuer
+      uint32_t it = 0, tcount = 0;
+      bool ok = true, issued = false;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++tcount) {
+        const uint32_t b = tcount & 1;
+        if (!mbar_wait(&acce[b], ((tcount >> 1) & 1) ^ 1, abort, 2)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t tmem_d = tmem_base + b * kBN;
+        for (int kb = 0; kb < P.k_blocks; ++kb, ++it) {
+          const int s = it % kStages;
+          if (!mbar_wait(&full[s], (it / kStages) & 1, abort, 3)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t sa = smem_u32(stage_base + s * kStageBytes);
+          const uint32_t sb = sa + kStageA;
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k)
+            umma_bf16(tmem_d, umma_desc(sa + k * kUmmaK * 2), umma_desc(sb + k * kUmmaK * 2), (kb | k) != 0);
+          issued = true;
+          umma_commit(&empty[s]);  // stage s is free once these MMAs have read it
+        }
+        if (!ok) break;
+        umma_commit(&accf[b]);  // accumulator b is complete
+      }
+      if (issued) {  // wait (bounded) for every MMA issued by this thread before exit
+        umma_commit(drain);
+        const long long t0 = clock64();
+        while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitCycles) {
+        }
+      }
+    }
+  } else {  // ---- epilogue: warps 2..5
+    // No barrier among the epilogue threads: each reads the member's A_i columns from
+    // global memory at warp-uniform addresses (one L1 broadcast per load), so a thread
+    // that gives up on a wait can leave without stranding the others.
+    const int q = warp & 3;            // tensor-memory lane quarter this warp may read
+    const int row = q * 32 + lane;     // row of the 128-row tile
+    uint32_t tcount = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++tcount) {
+      const int nb = tile % P.n_blocks, mb = tile / P.n_blocks;
+      const uint32_t b = tcount & 1;
+      const int m = mb * kBM + row;
+      const int member = (mb * kBM) / P.rows_per_member;
+      const float4* a_tile = reinterpret_cast<const float4*>(P.a + ((size_t)member * P.n + (size_t)nb * kBN) * 4);
+      const float sg = __ldg(P.sigma + member);
+      const float4 xb = __ldg(reinterpret_cast<const float4*>(P.xb) + m);
+      const float x0 = sg * xb.x, x1 = sg * xb.y, x2 = sg * xb.z, x3 = sg * xb.w;
+      // One lane waits and the warp follows its verdict, so the warp stays converged for
+      // the .sync.aligned tensor-memory loads even when a wait gives up.
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(&accf[b], (tcount >> 1) & 1, abort, 4) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      __syncwarp();
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      __nv_bfloat16* yrow = P.y + (size_t)m * P.n + (size_t)nb * kBN;
+      for (int c0 = 0; c0 < kBN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + b * kBN + c0, r);
+        uint32_t packed[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const float4 a0 = __ldg(a_tile + c0 + j);
+          const float4 a1 = __ldg(a_tile + c0 + j + 1);
+          const float v0 = __uint_as_float(r[j]) + (x0 * a0.x + x1 * a0.y + x2 * a0.z + x3 * a0.w);
+          const float v1 = __uint_as_float(r[j + 1]) + (x0 * a1.x + x1 * a1.y + x2 * a1.z + x3 * a1.w);
+          const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
+          packed[j / 2] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(yrow + c0);
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(&acce[b]);  // accumulator b may be overwritten
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (warp == 0) {
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+  }
+}
+
+// XB[m, r] = sum_k X[m, k] * B_i[k, r] (fp32), one warp per row: bandwidth-bound read of X.
+__global__ void __launch_bounds__(256) eggroll_xb_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ b,
+                                                         float* __restrict__ xb, int64_t m_rows, int32_t k,
+                                                         int32_t rows_per_member) {
+  const int64_t m = (int64_t)blockIdx.x * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (m >= m_rows) return;
+  const int member = (int)(m / rows_per_member);
+  const __nv_bfloat16* xr = x + m * k;
+  const float4* br = reinterpret_cast<const float4*>(b + (size_t)member * k * 4);
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  for (int k0 = lane * 8; k0 < k; k0 += 32 * 8) {
+    const uint4 xv = __ldg(reinterpret_cast<const uint4*>(xr + k0));
+    const uint32_t w[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float xf = __uint_as_float((j & 1) ? (w[j / 2] & 0xffff0000u) : (w[j / 2] << 16));
+      const float4 bb = __ldg(br + k0 + j);
+      s0 = fmaf(xf, bb.x, s0); s1 = fmaf(xf, bb.y, s1); s2 = fmaf(xf, bb.z, s2); s3 = fmaf(xf, bb.w, s3);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    s3 += __shfl_xor_sync(0xffffffffu, s3, o);
+  }
+  if (lane == 0) reinterpret_cast<float4*>(xb)[m] = make_float4(s0, s1, s2, s3);
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encode(EncodeFn* fn) {
+  static std::mutex mu;
+  static EncodeFn cached = nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cached) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (int rc = zt::check_cuda(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q),
+                                "zt_eggroll_linear: cudaGetDriverEntryPoint"))
+      return rc;
+    if (!p || q != cudaDriverEntryPointSuccess)
+      return zt::set_error(ZT_ERR_CUDA, "zt_eggroll_linear: cuTensorMapEncodeTiled unavailable");
+    cached = reinterpret_cast<EncodeFn>(p);
+  }
+  *fn = cached;
+  return ZT_OK;
+}
+
+int make_map(EncodeFn enc, CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kBK, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return zt::set_error(ZT_ERR_CUDA, "zt_eggroll_linear: cuTensorMapEncodeTiled failed");
+  return ZT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int zt_eggroll_linear(const zt_eggroll_args* args, void* stream) {
+  zt::clear_error();
+  if (!args) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: null args");
+  const zt_eggroll_args& A = *args;
+  if (!A.x || !A.w || !A.a || !A.b || !A.sigma || !A.xb || !A.y)
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: null pointer");
+  if (A.rank != 4) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: rank must be 4");
+  if (A.m <= 0 || A.n <= 0 || A.k <= 0) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: empty shape");
+  if (A.m % kBM || A.n % kBN || A.k % kBK)
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: need M % 128 == 0, N % 256 == 0, K % 64 == 0");
+  if (A.rows_per_member <= 0 || A.rows_per_member % kBM || A.m % A.rows_per_member)
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: rows_per_member must divide M and be a multiple of 128");
+  if (A.m > (int64_t)INT32_MAX || A.n > (int64_t)INT32_MAX || A.k > (int64_t)INT32_MAX)
+    return zt::set_error(ZT_ERR_LIMIT, "zt_eggroll_linear: dimension above 2^31-1");
+  for (const void* p : {A.x, A.w, (const void*)A.a, (const void*)A.b, (const void*)A.xb, (const void*)A.y})
+    if (((uintptr_t)p & 15) != 0) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: pointers must be 16-byte aligned");
+  EncodeFn enc = nullptr;
+  if (int rc = get_encode(&enc)) return rc;
+  EggParams P;
+  if (int rc = make_map(enc, &P.tmap_x, A.x, (uint64_t)A.m, (uint64_t)A.k, kBM)) return rc;
+  if (int rc = make_map(enc, &P.tmap_w, A.w, (uint64_t)A.n, (uint64_t)A.k, kBN)) return rc;
+  P.a = A.a;
+  P.sigma = A.sigma;
+  P.xb = A.xb;
+  P.y = static_cast<__nv_bfloat16*>(A.y);
+  P.m_blocks = (int32_t)(A.m / kBM);
+  P.n_blocks = (int32_t)(A.n / kBN);
+  P.k_blocks = (int32_t)(A.k / kBK);
+  P.n = (int32_t)A.n;
+  P.rows_per_member = A.rows_per_member;
+  cudaStream_t s = zt::as_stream(stream);
+  eggroll_xb_kernel<<<(unsigned)((A.m + 7) / 8), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(A.x), A.b, A.xb, A.m,
+                                                              (int32_t)A.k, A.rows_per_member);
+  if (int rc = zt::check_cuda(cudaGetLastError(), "zt_eggroll_linear: xb launch")) return rc;
+  {  // the dynamic shared-memory limit is a per-device function attribute
+    static std::mutex mu;
+    static bool done[64] = {false};
+    int dev = 0;
+    if (int rc = zt::check_cuda(cudaGetDevice(&dev), "zt_eggroll_linear: cudaGetDevice")) return rc;
+    if (dev < 0 || dev >= 64) return zt::set_error(ZT_ERR_LIMIT, "zt_eggroll_linear: device ordinal >= 64");
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev]) {
+      if (int rc = zt::check_cuda(cudaFuncSetAttribute(eggroll_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       (int)kSmemBytes), "zt_eggroll_linear: shared memory attribute"))
+        return rc;
+      done[dev] = true;
+    }
+  }
+  const int tiles = P.m_blocks * P.n_blocks;
+  const int grid = tiles < zt::sm_count() ? tiles : zt::sm_count();
+  eggroll_gemm_kernel<<<grid, kThreadsEgg, kSmemBytes, s>>>(P);
+  return zt::check_cuda(cudaGetLastError(), "zt_eggroll_linear: gemm launch");
+}
+
+int zt_eggroll_take_error(int32_t* code) {
+  zt::clear_error();
+  if (!code) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_take_error: null pointer");
+  int v = 0;
+  if (int rc = zt::check_cuda(cudaMemcpyFromSymbol(&v, g_eggroll_error, sizeof(int)), "zt_eggroll_take_error: read"))
+    return rc;
+  const int zero = 0;
+  if (v != 0) {
+    if (int rc = zt::check_cuda(cudaMemcpyToSymbol(g_eggroll_error, &zero, sizeof(int)), "zt_eggroll_take_error: clear"))
+      return rc;
+  }
+  *code = v;
+  return ZT_OK;
+}
+
+}  // extern "C"

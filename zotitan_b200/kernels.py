@@ -216,3 +216,42 @@ class ParamTable:
         with torch.cuda.device(self.device):
             L.check(L.load().zt_pass(ctypes.byref(self.plan), ctypes.byref(c), arr, len(streams),
                                      _stream_ptr(self.device)), "zt_pass")
+
+
+def eggroll_linear(x: torch.Tensor, w: torch.Tensor, a: torch.Tensor, b: torch.Tensor, sigma: torch.Tensor,
+                   rows_per_member: int, out: torch.Tensor | None = None, xb: torch.Tensor | None = None) -> torch.Tensor:
+    """EGGROLL population linear layer (zt_eggroll_linear):
+    Y = X W^T + sigma_i (X B_i) A_i^T for the rows of member i.
+
+    x [M, K] bf16, w [N, K] bf16, a [members, N, 4] fp32, b [members, K, 4] fp32,
+    sigma [members] fp32; returns Y [M, N] bf16. M % 128, N % 256, K % 64 must be 0 and
+    rows_per_member a multiple of 128 dividing M."""
+    for t, name in ((x, "x"), (w, "w"), (a, "a"), (b, "b"), (sigma, "sigma")):
+        _check_cuda(t, name)
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise ValueError("x and w must be bf16")
+    if a.dtype != torch.float32 or b.dtype != torch.float32 or sigma.dtype != torch.float32:
+        raise ValueError("a, b and sigma must be fp32")
+    M, K = x.shape
+    N = w.shape[0]
+    members = M // rows_per_member
+    if w.shape[1] != K or a.shape != (members, N, 4) or b.shape != (members, K, 4) or sigma.shape != (members,):
+        raise ValueError("inconsistent shapes")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    if xb is None:
+        xb = torch.empty((M, 4), dtype=torch.float32, device=x.device)
+    args = L.ZtEggrollArgs(x.data_ptr(), w.data_ptr(), a.data_ptr(), b.data_ptr(), sigma.data_ptr(), xb.data_ptr(),
+                           out.data_ptr(), M, N, K, rows_per_member, 4)
+    with torch.cuda.device(x.device):
+        L.check(L.load().zt_eggroll_linear(ctypes.byref(args), _stream_ptr(x.device)), "zt_eggroll_linear")
+    return out
+
+
+def eggroll_take_error() -> int:
+    """Read and clear the EGGROLL kernels' device error code (synchronous)."""
+    code = ctypes.c_int32(0)
+    L.check(L.load().zt_eggroll_take_error(ctypes.byref(code)), "zt_eggroll_take_error")
+    return int(code.value)
