@@ -42,10 +42,67 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seeds", type=int, default=N_SEEDS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile-case", choices=["chain", "full"], default=None,
+    ap.add_argument("--profile-case", choices=["chain", "full", "eggroll"], default=None,
                     help="small case for ncu: one bf16 tensor of 2^28 elements, 3 launches of the "
-                         "-2eps pass (chain) or of the restore+accumulate+perturb pass (full)")
+                         "-2eps pass (chain) or of the restore+accumulate+perturb pass (full); or 3 "
+                         "EGGROLL linear launches on an 8B gate_proj shape, 16 members x 1024 rows (eggroll)")
+    ap.add_argument("--eggroll-gemm", action="store_true",
+                    help="time the EGGROLL population linear layer on the Llama-3-8B layer shapes")
     return ap.parse_args()
+
+
+EGG_SHAPES = {  # Llama-3-8B linear layers (N, K): out x in
+    "q_proj/o_proj": (4096, 4096), "k_proj/v_proj": (1024, 4096), "gate_proj/up_proj": (14336, 4096),
+    "down_proj": (4096, 14336)}
+
+
+def eggroll_inputs(M, N, K, T, dev, seed=0):
+    import torch
+    g = torch.Generator(device=dev).manual_seed(seed)
+    members = M // T
+    x = (torch.randn(M, K, device=dev, generator=g)).bfloat16()
+    w = (torch.randn(N, K, device=dev, generator=g) * 0.02).bfloat16()
+    a = torch.randn(members, N, 4, device=dev, generator=g)
+    b = torch.randn(members, K, 4, device=dev, generator=g)
+    sigma = torch.full((members,), 1e-3, device=dev)
+    return x, w, a, b, sigma
+
+
+def eggroll_gemm_bench(rows: int = 16384, T: int = 1024, reps: int = 10):
+    """TFLOP/s of zt_eggroll_linear (base GEMM FLOPs 2*M*N*K) per Llama-3-8B layer shape,
+    with torch.matmul (cuBLAS) of the plain GEMM on the same shapes for context."""
+    import torch
+
+    from zotitan_b200 import kernels as K_
+    dev = torch.device("cuda")
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(HERE, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    peak = peaks.get("bf16_tflops", 1590.0)
+    res = {}
+    for name, (N, Kd) in EGG_SHAPES.items():
+        x, w, a, b, sigma = eggroll_inputs(rows, N, Kd, T, dev)
+        y = torch.empty(rows, N, dtype=torch.bfloat16, device=dev)
+        xb = torch.empty(rows, 4, dtype=torch.float32, device=dev)
+
+        def timed(fn):
+            fn(); torch.cuda.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(reps):
+                fn()
+            e.record(); torch.cuda.synchronize()
+            return s.elapsed_time(e) / reps
+        ms = timed(lambda: K_.eggroll_linear(x, w, a, b, sigma, T, out=y, xb=xb))
+        ms_cublas = timed(lambda: torch.matmul(x, w.T))
+        flops = 2.0 * rows * N * Kd
+        res[name] = {"M": rows, "N": N, "K": Kd, "ms": ms, "tflops": flops / ms / 1e9,
+                     "frac_of_peak": flops / ms / 1e9 / peak, "cublas_plain_gemm_tflops": flops / ms_cublas / 1e9}
+    assert K_.eggroll_take_error() == 0
+    print(json.dumps({"eggroll_gemm": res, "peak_tflops": peak,
+                      "peak_source": "MEASURED_PEAKS.json bf16_tflops" if "bf16_tflops" in peaks else "fallback"}))
 
 
 def profile_case(kind: str):
@@ -57,6 +114,15 @@ def profile_case(kind: str):
     n = 1 << 28
     p = (torch.randn(n, device="cuda") * 0.02).bfloat16()
     f = lambda x: float(np.float32(x))  # noqa: E731
+    if kind == "eggroll":
+        x, w, a, b, sigma = eggroll_inputs(16384, 14336, 4096, 1024, "cuda")
+        y = torch.empty(16384, 14336, dtype=torch.bfloat16, device="cuda")
+        xb = torch.empty(16384, 4, dtype=torch.float32, device="cuda")
+        for _ in range(3):
+            K.eggroll_linear(x, w, a, b, sigma, 1024, out=y, xb=xb)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": kind, "error": K.eggroll_take_error()}))
+        return
     if kind == "chain":
         tab = K.ParamTable([p])
         cfg, streams = K.PassCfg(), [K.Stream(5, (f(-2e-3),))]
@@ -382,6 +448,9 @@ def main():
     rank, local_rank, world = env_rank()
     if args.profile_case:
         profile_case(args.profile_case)
+        return
+    if args.eggroll_gemm:
+        eggroll_gemm_bench()
         return
     if args.impl == "reference":
         run_reference(args, rank, world)
