@@ -38,6 +38,20 @@ constexpr uint32_t kStageBytes = kStageA + kStageB;
 constexpr uint32_t kTmemCols = 2 * kBN;       // two fp32 accumulators of 128 x 256
 constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + kStages * kStageBytes + 256 /*barriers, flags*/;
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
+constexpr int kGroupN = 16;  // N-blocks per rasterisation group
+
+// Tile order: groups of kGroupN N-blocks; inside a group the M-blocks are swept with the
+// N-block fastest. The ~150 tiles in flight then touch ~10 M-blocks of X and one group's
+// slice of W, both of which stay in L2, instead of streaming all of W per wave.
+__device__ __forceinline__ void tile_coords(int tile, int m_blocks, int n_blocks, int& mb, int& nb) {
+  const int per_group = kGroupN * m_blocks;
+  const int g = tile / per_group;
+  const int r = tile - g * per_group;
+  const int rem = n_blocks - g * kGroupN;
+  const int gn = rem < kGroupN ? rem : kGroupN;
+  mb = r / gn;
+  nb = g * kGroupN + r % gn;
+}
 
 __device__ int g_eggroll_error = 0;
 
@@ -179,7 +193,8 @@ __global__ void __launch_bounds__(kThreadsEgg, 1) eggroll_gemm_kernel(const __gr
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
-        const int nb = tile % P.n_blocks, mb = tile / P.n_blocks;
+        int mb, nb;
+        tile_coords(tile, P.m_blocks, P.n_blocks, mb, nb);
         for (int kb = 0; kb < P.k_blocks; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t round = it / kStages;
@@ -238,7 +253,8 @@ __global__ void __launch_bounds__(kThreadsEgg, 1) eggroll_gemm_kernel(const __gr
     const int row = q * 32 + lane;     // row of the 128-row tile
     uint32_t tcount = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++tcount) {
-      const int nb = tile % P.n_blocks, mb = tile / P.n_blocks;
+      int mb, nb;
+      tile_coords(tile, P.m_blocks, P.n_blocks, mb, nb);
       const uint32_t b = tcount & 1;
       const int m = mb * kBM + row;
       const int member = (mb * kBM) / P.rows_per_member;
@@ -286,35 +302,61 @@ __global__ void __launch_bounds__(kThreadsEgg, 1) eggroll_gemm_kernel(const __gr
   }
 }
 
-// XB[m, r] = sum_k X[m, k] * B_i[k, r] (fp32), one warp per row: bandwidth-bound read of X.
+// XB[m, r] = sum_k X[m, k] * B_i[k, r] (fp32). One CTA per 64 rows of one member: B_i is
+// staged in shared memory transposed (4 x kXbChunk floats per chunk); each warp owns 8
+// rows and its lanes read consecutive bf16 pairs of X (coalesced 128-byte rows) and the
+// matching float2 of each B_i row (consecutive 8-byte words: no bank conflicts).
+constexpr int kXbRows = 64, kXbChunk = 1024;
+
 __global__ void __launch_bounds__(256) eggroll_xb_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ b,
-                                                         float* __restrict__ xb, int64_t m_rows, int32_t k,
-                                                         int32_t rows_per_member) {
-  const int64_t m = (int64_t)blockIdx.x * 8 + threadIdx.x / 32;
-  const int lane = threadIdx.x % 32;
-  if (m >= m_rows) return;
-  const int member = (int)(m / rows_per_member);
-  const __nv_bfloat16* xr = x + m * k;
-  const float4* br = reinterpret_cast<const float4*>(b + (size_t)member * k * 4);
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-  for (int k0 = lane * 8; k0 < k; k0 += 32 * 8) {
-    const uint4 xv = __ldg(reinterpret_cast<const uint4*>(xr + k0));
-    const uint32_t w[4] = {xv.x, xv.y, xv.z, xv.w};
+                                                         float* __restrict__ xb, int32_t k, int32_t rows_per_member) {
+  __shared__ float bt[4][kXbChunk];
+  const int64_t row0 = (int64_t)blockIdx.x * kXbRows;
+  const int member = (int)(row0 / rows_per_member);
+  const float4* bm = reinterpret_cast<const float4*>(b + (size_t)member * k * 4);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  float acc[8][4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float xf = __uint_as_float((j & 1) ? (w[j / 2] & 0xffff0000u) : (w[j / 2] << 16));
-      const float4 bb = __ldg(br + k0 + j);
-      s0 = fmaf(xf, bb.x, s0); s1 = fmaf(xf, bb.y, s1); s2 = fmaf(xf, bb.z, s2); s3 = fmaf(xf, bb.w, s3);
+  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  for (int kc = 0; kc < k; kc += kXbChunk) {
+    const int len = (k - kc) < kXbChunk ? (k - kc) : kXbChunk;
+    __syncthreads();
+    for (int t = threadIdx.x; t < len; t += 256) {
+      const float4 v = __ldg(bm + kc + t);
+      bt[0][t] = v.x; bt[1][t] = v.y; bt[2][t] = v.z; bt[3][t] = v.w;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const __nv_bfloat16* xr = x + (row0 + warp * 8 + i) * (int64_t)k + kc;
+      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+      for (int t = 2 * lane; t < len; t += 64) {
+        const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(xr + t));
+        const float xa = __uint_as_float(w << 16), xc = __uint_as_float(w & 0xffff0000u);
+        const float2 b0 = *reinterpret_cast<const float2*>(&bt[0][t]);
+        const float2 b1 = *reinterpret_cast<const float2*>(&bt[1][t]);
+        const float2 b2 = *reinterpret_cast<const float2*>(&bt[2][t]);
+        const float2 b3 = *reinterpret_cast<const float2*>(&bt[3][t]);
+        s0 = fmaf(xa, b0.x, fmaf(xc, b0.y, s0));
+        s1 = fmaf(xa, b1.x, fmaf(xc, b1.y, s1));
+        s2 = fmaf(xa, b2.x, fmaf(xc, b2.y, s2));
+        s3 = fmaf(xa, b3.x, fmaf(xc, b3.y, s3));
+      }
+      acc[i][0] += s0; acc[i][1] += s1; acc[i][2] += s2; acc[i][3] += s3;
     }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-    s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-    s3 += __shfl_xor_sync(0xffffffffu, s3, o);
+  for (int i = 0; i < 8; ++i) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      acc[i][0] += __shfl_xor_sync(0xffffffffu, acc[i][0], o);
+      acc[i][1] += __shfl_xor_sync(0xffffffffu, acc[i][1], o);
+      acc[i][2] += __shfl_xor_sync(0xffffffffu, acc[i][2], o);
+      acc[i][3] += __shfl_xor_sync(0xffffffffu, acc[i][3], o);
+    }
+    if (lane == 0)
+      reinterpret_cast<float4*>(xb)[row0 + warp * 8 + i] = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
   }
-  if (lane == 0) reinterpret_cast<float4*>(xb)[m] = make_float4(s0, s1, s2, s3);
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
@@ -387,8 +429,9 @@ int zt_eggroll_linear(const zt_eggroll_args* args, void* stream) {
   P.n = (int32_t)A.n;
   P.rows_per_member = A.rows_per_member;
   cudaStream_t s = zt::as_stream(stream);
-  eggroll_xb_kernel<<<(unsigned)((A.m + 7) / 8), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(A.x), A.b, A.xb, A.m,
-                                                              (int32_t)A.k, A.rows_per_member);
+  // m % 128 == 0 and rows_per_member % 128 == 0, so each 64-row block lies in one member
+  eggroll_xb_kernel<<<(unsigned)(A.m / kXbRows), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(A.x), A.b, A.xb,
+                                                             (int32_t)A.k, A.rows_per_member);
   if (int rc = zt::check_cuda(cudaGetLastError(), "zt_eggroll_linear: xb launch")) return rc;
   {  // the dynamic shared-memory limit is a per-device function attribute
     static std::mutex mu;
