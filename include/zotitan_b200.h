@@ -70,6 +70,11 @@ ZT_API int zt_randn(uint32_t key, int64_t off0, int64_t n, float* out, void* str
 /* out[i] = N(0,1) sample at offsets[i]. */
 ZT_API int zt_randn_at(uint32_t key, const uint32_t* offsets, int64_t n, float* out, void* stream);
 
+/* out[j*n + t] = N(0,1) sample at offset t for key keys[j] (host array), j < n_keys <= 1024:
+ * many tensors' fields in one launch (the EGGROLL factors of a population chunk). Each
+ * row equals zt_randn(keys[j], 0, n). */
+ZT_API int zt_randn_keys(const uint32_t* keys, int32_t n_keys, int64_t n, float* out, void* stream);
+
 /* ---- parameter tables -------------------------------------------------------------- */
 
 /* One trainable tensor. `data` is the parameter; the other buffers are optional

@@ -26,7 +26,7 @@ ZT_BUF_DATA, ZT_BUF_LIVE = 1, 2
 # every function include/zotitan_b200.h declares
 EXPORTS = ("zt_last_error", "zt_abi_version", "zt_param_key", "zt_philox_words", "zt_randn",
            "zt_randn_at", "zt_plan_workspace_bytes", "zt_plan_init", "zt_pass", "zt_pass_static",
-           "zt_eggroll_linear", "zt_eggroll_take_error")
+           "zt_eggroll_linear", "zt_eggroll_take_error", "zt_randn_keys")
 ZT_STATIC_MAX_TENSORS = 1024
 
 
@@ -101,6 +101,8 @@ def load():
         fn = getattr(lib, name)
         fn.restype = ctypes.c_int
         fn.argtypes = args
+    lib.zt_randn_keys.restype = ctypes.c_int
+    lib.zt_randn_keys.argtypes = [ctypes.POINTER(ctypes.c_uint32), I32, I64, P, P]
     lib.zt_eggroll_linear.restype = ctypes.c_int
     lib.zt_eggroll_linear.argtypes = [ctypes.POINTER(ZtEggrollArgs), P]
     lib.zt_eggroll_take_error.restype = ctypes.c_int

@@ -302,11 +302,12 @@ __global__ void __launch_bounds__(kThreadsEgg, 1) eggroll_gemm_kernel(const __gr
   }
 }
 
-// XB[m, r] = sum_k X[m, k] * B_i[k, r] (fp32). One CTA per 64 rows of one member: B_i is
-// staged in shared memory transposed (4 x kXbChunk floats per chunk); each warp owns 8
+// XB[m, r] = sum_k X[m, k] * B_i[k, r] (fp32). One CTA per 16 rows of one member: B_i is
+// staged in shared memory transposed (4 x kXbChunk floats per chunk); each warp owns 2
 // rows and its lanes read consecutive bf16 pairs of X (coalesced 128-byte rows) and the
 // matching float2 of each B_i row (consecutive 8-byte words: no bank conflicts).
-constexpr int kXbRows = 64, kXbChunk = 1024;
+constexpr int kXbRows = 16, kXbRowsPerWarp = 2, kXbChunk = 1024;
+static_assert(kXbRows == 8 * kXbRowsPerWarp, "8 warps per CTA");
 
 __global__ void __launch_bounds__(256) eggroll_xb_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ b,
                                                          float* __restrict__ xb, int32_t k, int32_t rows_per_member) {
@@ -315,9 +316,9 @@ __global__ void __launch_bounds__(256) eggroll_xb_kernel(const __nv_bfloat16* __
   const int member = (int)(row0 / rows_per_member);
   const float4* bm = reinterpret_cast<const float4*>(b + (size_t)member * k * 4);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  float acc[8][4];
+  float acc[kXbRowsPerWarp][4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  for (int i = 0; i < kXbRowsPerWarp; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   for (int kc = 0; kc < k; kc += kXbChunk) {
     const int len = (k - kc) < kXbChunk ? (k - kc) : kXbChunk;
     __syncthreads();
@@ -327,8 +328,8 @@ __global__ void __launch_bounds__(256) eggroll_xb_kernel(const __nv_bfloat16* __
     }
     __syncthreads();
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const __nv_bfloat16* xr = x + (row0 + warp * 8 + i) * (int64_t)k + kc;
+    for (int i = 0; i < kXbRowsPerWarp; ++i) {
+      const __nv_bfloat16* xr = x + (row0 + warp * kXbRowsPerWarp + i) * (int64_t)k + kc;
       float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
       for (int t = 2 * lane; t < len; t += 64) {
         const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(xr + t));
@@ -346,7 +347,7 @@ __global__ void __launch_bounds__(256) eggroll_xb_kernel(const __nv_bfloat16* __
     }
   }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < kXbRowsPerWarp; ++i) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       acc[i][0] += __shfl_xor_sync(0xffffffffu, acc[i][0], o);
@@ -355,7 +356,7 @@ __global__ void __launch_bounds__(256) eggroll_xb_kernel(const __nv_bfloat16* __
       acc[i][3] += __shfl_xor_sync(0xffffffffu, acc[i][3], o);
     }
     if (lane == 0)
-      reinterpret_cast<float4*>(xb)[row0 + warp * 8 + i] = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+      reinterpret_cast<float4*>(xb)[row0 + warp * kXbRowsPerWarp + i] = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
   }
 }
 
@@ -429,7 +430,7 @@ int zt_eggroll_linear(const zt_eggroll_args* args, void* stream) {
   P.n = (int32_t)A.n;
   P.rows_per_member = A.rows_per_member;
   cudaStream_t s = zt::as_stream(stream);
-  // m % 128 == 0 and rows_per_member % 128 == 0, so each 64-row block lies in one member
+  // m % 128 == 0 and rows_per_member % 128 == 0, so each 16-row block lies in one member
   eggroll_xb_kernel<<<(unsigned)(A.m / kXbRows), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(A.x), A.b, A.xb,
                                                              (int32_t)A.k, A.rows_per_member);
   if (int rc = zt::check_cuda(cudaGetLastError(), "zt_eggroll_linear: xb launch")) return rc;

@@ -46,6 +46,16 @@ def randn(key: int, n: int, device, off0: int = 0) -> torch.Tensor:
     return out
 
 
+def randn_keys(keys: list[int], n: int, device) -> torch.Tensor:
+    """[len(keys), n] fp32: row j is the Gaussian field of key keys[j] at offsets 0..n-1."""
+    device = torch.device(device)
+    out = torch.empty((len(keys), n), dtype=torch.float32, device=device)
+    arr = (ctypes.c_uint32 * max(1, len(keys)))(*keys)
+    L.check(L.load().zt_randn_keys(arr, len(keys), n, out.data_ptr() if out.numel() else None, _stream_ptr(device)),
+            "zt_randn_keys")
+    return out
+
+
 def randn_at(key: int, offsets: torch.Tensor) -> torch.Tensor:
     _check_cuda(offsets, "offsets")
     offs = offsets.to(torch.int32).contiguous()
