@@ -42,6 +42,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seeds", type=int, default=N_SEEDS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-eggroll", action="store_true", help="skip the EGGROLL population measurement")
     ap.add_argument("--profile-case", choices=["chain", "full", "eggroll"], default=None,
                     help="small case for ncu: one bf16 tensor of 2^28 elements, 3 launches of the "
                          "-2eps pass (chain) or of the restore+accumulate+perturb pass (full); or 3 "
@@ -264,6 +265,58 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# ── EGGROLL population evaluation (Llama-3-8B shape) ─────────────────────────────────────
+
+def eggroll_member_evals(dev, rank: int, world: int, pairs_per_rank: int = 16, pairs_per_chunk: int = 8):
+    """Member-evals/s of the EGGROLL population forward on the Llama-3-8B-shaped bf16 model:
+    members in antithetic pairs (seeds from the pair counter, rank r takes pairs r, r+W, ...),
+    each scored with cross-entropy on a shared 4 x 256-token batch, sigma = 1e-3, rank-4
+    perturbations regenerated from Philox seeds; one all-gather of the member losses.
+    Weak scaling: fixed members per rank. Timed with CUDA events, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from zotitan_b200 import kernels as K
+    from zotitan_b200.eggroll import EggrollConfig, EggrollPopulation
+    from zotitan_b200.synthetic import LLAMA_8B, build_llama, linear_flops_per_token
+    model = build_llama(LLAMA_8B, device=dev, seed=0, max_positions=1024)
+    pop = EggrollPopulation(model, EggrollConfig(sigma=1e-3))
+    g = torch.Generator().manual_seed(7)
+    tokens = torch.randint(0, LLAMA_8B.vocab, (4, 256), generator=g).to(dev)
+    my_pairs = list(range(rank, world * pairs_per_rank, world))
+    pop.evaluate(tokens, my_pairs[:pairs_per_chunk])          # warm-up chunk
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    losses = []
+    for c in range(0, len(my_pairs), pairs_per_chunk):
+        losses.append(pop.evaluate(tokens, my_pairs[c:c + pairs_per_chunk]))
+    mine = torch.cat(losses)
+    if world > 1:
+        allv = torch.empty(world * mine.numel(), device=dev)
+        dist.all_gather_into_tensor(allv, mine)
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    err = K.eggroll_take_error()
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    members = 2 * pairs_per_rank * world
+    tokens_per_member = tokens.numel()
+    lin_flops = linear_flops_per_token(LLAMA_8B) * tokens_per_member * members
+    del pop, model
+    torch.cuda.empty_cache()
+    return {"metric": "EGGROLL member-evals/s (Llama-3-8B shape)", "value": members / (ms * 1e-3),
+            "unit": "member-evals/s", "members": members, "members_per_rank": 2 * pairs_per_rank,
+            "tokens_per_member": tokens_per_member, "sigma": 1e-3, "rank": 4, "scaling": "weak",
+            "ms": ms, "linear_tflops": lin_flops / (ms * 1e-3) / 1e12, "device_error": err,
+            "mean_loss": float(mine.mean())}
+
+
 # ── our arm ─────────────────────────────────────────────────────────────────────────
 
 def run_ours(args, rank, local_rank, world):
@@ -288,6 +341,7 @@ def run_ours(args, rank, local_rank, world):
     shapes = llama_param_shapes(LLAMA_1B)
     named = make_params(shapes, torch.bfloat16, dev, seed=0)
     numel = sum(p.numel() for _, p in named)
+    n_tensors = len(named)
     cfg = ZOConfig()
     cfg.eps, cfg.z_batch, cfg.base.lr = EPS, args.seeds, LR
 
@@ -387,6 +441,10 @@ def run_ours(args, rank, local_rank, world):
         t = torch.tensor([ms, e2e_ms, pmean, amean], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e2e_ms, pmean, amean = t.tolist()
+    # release the microbench's buffers, then the EGGROLL population measurement (all ranks)
+    del opt, named
+    torch.cuda.empty_cache()
+    egg = eggroll_member_evals(dev, rank, world) if not args.no_eggroll else None
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
@@ -419,7 +477,7 @@ def run_ours(args, rank, local_rank, world):
         "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "Llama-3.2-1B-shaped parameter set, 64 seeds/step (kernel microbench)",
-                   "params": numel, "tensors": len(named), "seeds_per_step": args.seeds, "eps": EPS,
+                   "params": numel, "tensors": n_tensors, "seeds_per_step": args.seeds, "eps": EPS,
                    "passes_per_step": 2 * args.seeds + 1, "parallelism": f"seed-sharded x{world}",
                    "l2": "inputs (2.47 GB of bf16 parameters) larger than L2"},
         "perturb_pass_gbs": perturb_gbs, "perturb_pass_ms": pmean, "accum_pass_ms": amean,
@@ -438,6 +496,8 @@ def run_ours(args, rank, local_rank, world):
     }
     if cpu_line is not None:
         line["cpu_baseline"] = cpu_line
+    if egg is not None:
+        line["eggroll"] = egg
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

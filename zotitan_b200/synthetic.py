@@ -49,6 +49,30 @@ def llama_param_shapes(s: LlamaShape) -> list[tuple[str, tuple[int, ...]]]:
     return out
 
 
+def build_llama(s: LlamaShape, device="cuda", dtype=None, seed: int = 0, max_positions: int = 2048):
+    """A transformers LlamaForCausalLM of this shape built directly on `device` in `dtype`
+    (bf16 default), every parameter re-drawn N(0, 0.02) from a seeded generator."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+    dtype = dtype or torch.bfloat16
+    cfg = LlamaConfig(vocab_size=s.vocab, hidden_size=s.d_model, intermediate_size=s.ffn, num_hidden_layers=s.layers,
+                      num_attention_heads=s.heads, num_key_value_heads=s.kv_heads, tie_word_embeddings=s.tied,
+                      max_position_embeddings=max_positions, attn_implementation="sdpa")
+    with torch.device(device):
+        model = LlamaForCausalLM._from_config(cfg, dtype=dtype)
+    g = torch.Generator(device=device).manual_seed(seed)
+    with torch.no_grad():
+        for _, p in model.named_parameters():
+            p.normal_(0.0, 0.02, generator=g)
+    return model.eval()
+
+
+def linear_flops_per_token(s: LlamaShape) -> float:
+    """2 * (sum of in*out over the linear layers, lm_head included): base GEMM FLOPs per token."""
+    d, kv = s.d_model, s.kv_heads * s.head_dim
+    per_layer = d * d * 2 + d * kv * 2 + 3 * d * s.ffn
+    return 2.0 * (s.layers * per_layer + s.vocab * d)
+
+
 def lora_param_shapes(s: LlamaShape, r: int = 16) -> list[tuple[str, tuple[int, ...]]]:
     """Trainable LoRA adapters (A: [r, in], B: [out, r]) on every q/k/v/o/gate/up/down."""
     out = []
