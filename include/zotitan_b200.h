@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define ZT_ABI_VERSION 3
+#define ZT_ABI_VERSION 4
 
 /* dtypes of parameter tensors */
 #define ZT_F32 0
@@ -261,6 +261,75 @@ ZT_API int zt_eggroll_linear(const zt_eggroll_args* args, void* stream);
 /* Reads and clears the device-side error code of the EGGROLL kernels (0: none; nonzero:
  * a bounded wait inside the GEMM expired and that launch returned early). Synchronous. */
 ZT_API int zt_eggroll_take_error(int32_t* code);
+
+/* ---- EGGROLL population forward: factors and element-wise layers ------------------ */
+
+#define ZT_EGGROLL_MAX_PAIRS 512
+#define ZT_EGGROLL_FACTOR_BLOCKS 64
+#define ZT_EGGROLL_FACTOR_WORK_FLOATS (ZT_EGGROLL_FACTOR_BLOCKS * 20) /* workspace floats per pair */
+
+/* The rank-4 factors of one 2-D tensor [n, k] for a chunk of antithetic pairs: pair j
+ * gives members 2j (+sigma) and 2j+1 (-sigma). Replaces the low_rank branch of
+ * _sample_z (zotitan/train_zo.py:304-320) for the population forward:
+ *   P   = randn(keys_a[j], n*4).view(n, 4)  rounded to dtype  -> A_{2j} = A_{2j+1} = P
+ *   Psi = randn(keys_b[j], 4*k).view(4, k)  rounded to dtype  -> B_{2j} = B_{2j+1} = Psi^T
+ *   c_j = sqrt(n*k) / (||P Psi||_F + 1e-7), the norm, the sum and the quotient each
+ *         rounded to dtype as the reference evaluates them,
+ *   scale[2j] = sigma * c_j, scale[2j+1] = -sigma * c_j.
+ * The outputs are zt_eggroll_linear's a, b and sigma operands. ||P Psi||_F^2 is
+ * evaluated as sum_{r,s} (P^T P)_{rs} (Psi Psi^T)_{rs} from fixed-order partial sums
+ * (deterministic); the reference takes the norm of the rounded product P Psi. */
+typedef struct zt_eggroll_factor_args {
+  const uint32_t* keys_a; /* host [pairs]: key of P = zt_param_key(seed, n_params, index + 2*n_params) */
+  const uint32_t* keys_b; /* host [pairs]: key of Psi = zt_param_key(seed, n_params, index + n_params) */
+  int32_t pairs;          /* 1 .. ZT_EGGROLL_MAX_PAIRS */
+  int32_t rank;           /* must be 4 */
+  int64_t n, k;           /* the weight's out_features and in_features; 4*n, 4*k <= ZT_MAX_NUMEL */
+  int32_t dtype;          /* parameter dtype (ZT_F32 / ZT_BF16 / ZT_F16) */
+  int32_t normalize;      /* 0: c_j = 1 */
+  float sigma;
+  int32_t reserved;
+  float* a;               /* out [2*pairs, n, 4] fp32, 16-byte aligned */
+  float* b;               /* out [2*pairs, k, 4] fp32, 16-byte aligned */
+  float* scale;           /* out [2*pairs] fp32 */
+  float* work;            /* workspace: pairs * ZT_EGGROLL_FACTOR_WORK_FLOATS floats */
+} zt_eggroll_factor_args;
+
+ZT_API int zt_eggroll_factors(const zt_eggroll_factor_args* args, void* stream);
+
+/* Llama RMSNorm of a population chunk with member-perturbed weights (a 1-D tensor gets
+ * full Gaussian noise, zotitan/train_zo.py:303, applied as p + alpha*z, :350-351):
+ *   w_members[2j]   = bf16(w + sigma * z_j),  w_members[2j+1] = bf16(w - sigma * z_j),
+ *   z_j[t] = randn(keys[j], t) (fp32),
+ *   y[r] = w_members[r / rows_per_member] * bf16(x[r] * rsqrt(mean(x[r]^2) + eps))
+ * in fp32 with bf16 rounding where the transformers LlamaRMSNorm on bf16 rounds. All
+ * tensors bf16, rows contiguous, d % 8 == 0, m == rows_per_member * 2 * pairs. */
+typedef struct zt_eggroll_norm_args {
+  const void* x;          /* [m, d] bf16, 16-byte aligned */
+  const void* w;          /* [d] bf16: the norm's unperturbed weight */
+  const uint32_t* keys;   /* host [pairs]: zt_param_key(seed, n_params, index) */
+  void* w_members;        /* [2*pairs, d] bf16 workspace, written by the call */
+  void* y;                /* [m, d] bf16 out (may not alias x) */
+  int64_t m, d;
+  int32_t pairs;
+  int32_t rows_per_member;
+  float sigma;
+  float eps;
+} zt_eggroll_norm_args;
+
+ZT_API int zt_eggroll_rmsnorm(const zt_eggroll_norm_args* args, void* stream);
+
+/* In-place rotary position embedding of q [rows, q_heads*head_dim] and k [rows,
+ * k_heads*head_dim] (bf16, rows contiguous; row r is at position r % seq):
+ *   x = x * cos[pos] + rotate_half(x) * sin[pos],  cos, sin [seq, head_dim] bf16,
+ * each product and the sum rounded to bf16 (apply_rotary_pos_emb of transformers'
+ * Llama on bf16 tensors). head_dim % 16 == 0. */
+ZT_API int zt_eggroll_rope(void* q, void* k, const void* cos, const void* sin, int64_t rows, int32_t seq,
+                           int32_t q_heads, int32_t k_heads, int32_t head_dim, void* stream);
+
+/* out = bf16(bf16(silu(gate)) * up) over n bf16 elements (n % 8 == 0): the Llama MLP's
+ * act_fn(gate_proj(x)) * up_proj(x). */
+ZT_API int zt_eggroll_swiglu(const void* gate, const void* up, void* out, int64_t n, void* stream);
 
 /* ---- the fused pass without a caller-provided workspace -------------------------- */
 

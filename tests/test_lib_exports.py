@@ -32,7 +32,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version_and_key(lib):
-    assert lib.zt_abi_version() == 3
+    assert lib.zt_abi_version() == L.ABI_VERSION == 4
     from oracle import philox as ph
     for seed, n, i in [(0, 1, 0), (1234, 39, 7), (2**40 + 3, 146, 145), (2**64 - 1, 448, 3)]:
         assert lib.zt_param_key(seed, n, i) == ph.param_key(seed, n, i) == (seed * n + i) & 0x7FFFFFFF
@@ -43,6 +43,9 @@ def test_struct_layouts_match_header(lib):
     assert ctypes.sizeof(L.ZtStream) == 40
     assert ctypes.sizeof(L.ZtPlan) == 48
     assert ctypes.sizeof(L.ZtPassCfg) == 128 and L.ZtPassCfg.dev_vals.offset == 88 and L.ZtPassCfg.unit_begin.offset == 112
+    assert ctypes.sizeof(L.ZtEggrollArgs) == 88
+    assert ctypes.sizeof(L.ZtEggrollFactorArgs) == 88 and L.ZtEggrollFactorArgs.a.offset == 56
+    assert ctypes.sizeof(L.ZtEggrollNormArgs) == 72 and L.ZtEggrollNormArgs.m.offset == 40
     assert lib.zt_plan_workspace_bytes(0) == 8
     assert lib.zt_plan_workspace_bytes(3) == 256 + 8 * 4
     assert lib.zt_plan_workspace_bytes(5) == 512 + 8 * 6
@@ -94,3 +97,27 @@ def test_optimizer_refuses_cpu_tensors():
     p = torch.nn.Parameter(torch.zeros(4))
     with pytest.raises(ValueError, match="CUDA"):
         ZOOptimizer([("w", p)], ZOConfig(), score_fn=None)
+
+
+def test_eggroll_companions_validate_before_launch(lib):
+    """Shape checks of the population element-wise entry points fail on the host."""
+    import numpy as np
+    keys = (ctypes.c_uint32 * 2)(1, 2)
+    fa = L.ZtEggrollFactorArgs(ctypes.addressof(keys), ctypes.addressof(keys), 2, 3, 256, 256, L.ZT_BF16, 1, 1e-3, 0,
+                               16, 16, 16, 16)
+    assert lib.zt_eggroll_factors(ctypes.byref(fa), None) == L.ZT_ERR_INVALID and b"rank" in lib.zt_last_error()
+    fa.rank, fa.pairs = 4, L.ZT_EGGROLL_MAX_PAIRS + 1
+    assert lib.zt_eggroll_factors(ctypes.byref(fa), None) == L.ZT_ERR_LIMIT
+    fa.pairs, fa.n = 2, 2**30
+    assert lib.zt_eggroll_factors(ctypes.byref(fa), None) == L.ZT_ERR_LIMIT
+    fa.n, fa.a = 256, 8
+    assert lib.zt_eggroll_factors(ctypes.byref(fa), None) == L.ZT_ERR_INVALID and b"aligned" in lib.zt_last_error()
+    na = L.ZtEggrollNormArgs(16, 16, ctypes.addressof(keys), 16, 16, 1000, 64, 2, 128, 1e-3, 1e-5)
+    assert lib.zt_eggroll_rmsnorm(ctypes.byref(na), None) == L.ZT_ERR_INVALID and b"rows_per_member" in lib.zt_last_error()
+    na.m, na.d = 512, 60
+    assert lib.zt_eggroll_rmsnorm(ctypes.byref(na), None) == L.ZT_ERR_INVALID
+    assert lib.zt_eggroll_rope(16, 16, 16, 16, 64, 64, 4, 4, 24, None) == L.ZT_ERR_INVALID
+    assert lib.zt_eggroll_rope(16, 16, 16, 16, 65, 64, 4, 4, 64, None) == L.ZT_ERR_INVALID
+    assert lib.zt_eggroll_swiglu(16, 16, 16, 12, None) == L.ZT_ERR_INVALID
+    assert lib.zt_eggroll_swiglu(None, None, None, 0, None) == L.ZT_OK
+    del np

@@ -26,8 +26,12 @@ ZT_BUF_DATA, ZT_BUF_LIVE = 1, 2
 # every function include/zotitan_b200.h declares
 EXPORTS = ("zt_last_error", "zt_abi_version", "zt_param_key", "zt_philox_words", "zt_randn",
            "zt_randn_at", "zt_plan_workspace_bytes", "zt_plan_init", "zt_pass", "zt_pass_static",
-           "zt_eggroll_linear", "zt_eggroll_take_error", "zt_randn_keys")
+           "zt_eggroll_linear", "zt_eggroll_take_error", "zt_randn_keys", "zt_eggroll_factors",
+           "zt_eggroll_rmsnorm", "zt_eggroll_rope", "zt_eggroll_swiglu")
 ZT_STATIC_MAX_TENSORS = 1024
+ZT_EGGROLL_MAX_PAIRS = 512
+ZT_EGGROLL_FACTOR_WORK_FLOATS = 64 * 20
+ABI_VERSION = 4
 
 
 class ZtTensor(ctypes.Structure):
@@ -66,6 +70,20 @@ class ZtEggrollArgs(ctypes.Structure):
                 ("sigma", ctypes.c_void_p), ("xb", ctypes.c_void_p), ("y", ctypes.c_void_p),
                 ("m", ctypes.c_int64), ("n", ctypes.c_int64), ("k", ctypes.c_int64),
                 ("rows_per_member", ctypes.c_int32), ("rank", ctypes.c_int32)]
+
+
+class ZtEggrollFactorArgs(ctypes.Structure):
+    _fields_ = [("keys_a", ctypes.c_void_p), ("keys_b", ctypes.c_void_p), ("pairs", ctypes.c_int32),
+                ("rank", ctypes.c_int32), ("n", ctypes.c_int64), ("k", ctypes.c_int64), ("dtype", ctypes.c_int32),
+                ("normalize", ctypes.c_int32), ("sigma", ctypes.c_float), ("reserved", ctypes.c_int32),
+                ("a", ctypes.c_void_p), ("b", ctypes.c_void_p), ("scale", ctypes.c_void_p), ("work", ctypes.c_void_p)]
+
+
+class ZtEggrollNormArgs(ctypes.Structure):
+    _fields_ = [("x", ctypes.c_void_p), ("w", ctypes.c_void_p), ("keys", ctypes.c_void_p),
+                ("w_members", ctypes.c_void_p), ("y", ctypes.c_void_p), ("m", ctypes.c_int64), ("d", ctypes.c_int64),
+                ("pairs", ctypes.c_int32), ("rows_per_member", ctypes.c_int32), ("sigma", ctypes.c_float),
+                ("eps", ctypes.c_float)]
 
 
 class ZtError(RuntimeError):
@@ -107,10 +125,18 @@ def load():
     lib.zt_eggroll_linear.argtypes = [ctypes.POINTER(ZtEggrollArgs), P]
     lib.zt_eggroll_take_error.restype = ctypes.c_int
     lib.zt_eggroll_take_error.argtypes = [ctypes.POINTER(ctypes.c_int32)]
+    lib.zt_eggroll_factors.restype = ctypes.c_int
+    lib.zt_eggroll_factors.argtypes = [ctypes.POINTER(ZtEggrollFactorArgs), P]
+    lib.zt_eggroll_rmsnorm.restype = ctypes.c_int
+    lib.zt_eggroll_rmsnorm.argtypes = [ctypes.POINTER(ZtEggrollNormArgs), P]
+    lib.zt_eggroll_rope.restype = ctypes.c_int
+    lib.zt_eggroll_rope.argtypes = [P, P, P, P, I64, I32, I32, I32, I32, P]
+    lib.zt_eggroll_swiglu.restype = ctypes.c_int
+    lib.zt_eggroll_swiglu.argtypes = [P, P, P, I64, P]
     lib.zt_plan_workspace_bytes.restype = ctypes.c_size_t
     lib.zt_plan_workspace_bytes.argtypes = [I32]
-    if lib.zt_abi_version() != 3:
-        raise ZtError(f"{LIB_PATH}: ABI version {lib.zt_abi_version()} != 3")
+    if lib.zt_abi_version() != ABI_VERSION:
+        raise ZtError(f"{LIB_PATH}: ABI version {lib.zt_abi_version()} != {ABI_VERSION}")
     _lib = lib
     return lib
 

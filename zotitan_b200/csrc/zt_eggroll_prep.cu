@@ -1,0 +1,352 @@
+// Element-wise companions of the EGGROLL population linear: the per-member rank-4
+// factors, the per-member RMSNorm, rotary position embedding and SwiGLU of a Llama
+// population forward. Each is one or two bandwidth-bound launches over rows that the
+// population GEMM reads or writes; together they replace ~20 torch launches per layer.
+#include "zt_common.cuh"
+#include "zt_philox.cuh"
+
+namespace {
+
+constexpr int kMaxPairs = ZT_EGGROLL_MAX_PAIRS;
+constexpr int kFacThreads = 256;
+constexpr int kFacBlocks = ZT_EGGROLL_FACTOR_BLOCKS;
+constexpr int kGram = 10;  // upper triangle of a symmetric 4 x 4 Gram matrix
+
+struct PairKeys {
+  uint32_t ka[kMaxPairs];
+  uint32_t kb[kMaxPairs];
+};
+
+__device__ __forceinline__ void gram_add(float g[kGram], const float v[4]) {
+  g[0] = fmaf(v[0], v[0], g[0]); g[1] = fmaf(v[0], v[1], g[1]); g[2] = fmaf(v[0], v[2], g[2]);
+  g[3] = fmaf(v[0], v[3], g[3]); g[4] = fmaf(v[1], v[1], g[4]); g[5] = fmaf(v[1], v[2], g[5]);
+  g[6] = fmaf(v[1], v[3], g[6]); g[7] = fmaf(v[2], v[2], g[7]); g[8] = fmaf(v[2], v[3], g[8]);
+  g[9] = fmaf(v[3], v[3], g[9]);
+}
+
+// Pair j (blockIdx.y) draws P (n x 4, stream order o*4 + r under key ka[j]) and Psi
+// (4 x k, stream order r*k + t under key kb[j]), rounds both to the parameter dtype and
+// writes A = P and B = Psi^T for both members 2j and 2j+1. Items 0..n-1 are rows of P,
+// items n..n+k-1 columns of Psi. Each block also writes its partial Gram matrices P^T P
+// and Psi Psi^T (fixed-order block reduction) for the normalisation.
+template <int DT>
+__global__ void __launch_bounds__(kFacThreads) factor_kernel(const __grid_constant__ PairKeys K, int32_t n, int32_t k,
+                                                              float4* __restrict__ a, float4* __restrict__ b,
+                                                              float* __restrict__ part) {
+  const int j = blockIdx.y;
+  const uint32_t ka = K.ka[j], kb = K.kb[j];
+  const int items = n + k;
+  float gp[kGram], gq[kGram];
+#pragma unroll
+  for (int e = 0; e < kGram; ++e) gp[e] = gq[e] = 0.f;
+  float4* a0 = a + (size_t)(2 * j) * n;
+  float4* b0 = b + (size_t)(2 * j) * k;
+  for (int i = blockIdx.x * kFacThreads + threadIdx.x; i < items; i += gridDim.x * kFacThreads) {
+    float v[4];
+    if (i < n) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) v[r] = zt::Dt<DT>::round(zt::gauss((uint32_t)(4 * i + r), ka));
+      const float4 f = make_float4(v[0], v[1], v[2], v[3]);
+      a0[i] = f;
+      a0[i + n] = f;
+      gram_add(gp, v);
+    } else {
+      const int t = i - n;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) v[r] = zt::Dt<DT>::round(zt::gauss((uint32_t)(r * k + t), kb));
+      const float4 f = make_float4(v[0], v[1], v[2], v[3]);
+      b0[t] = f;
+      b0[t + k] = f;
+      gram_add(gq, v);
+    }
+  }
+  __shared__ float red[kFacThreads / 32][2 * kGram];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+#pragma unroll
+  for (int e = 0; e < kGram; ++e) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      gp[e] += __shfl_xor_sync(0xffffffffu, gp[e], o);
+      gq[e] += __shfl_xor_sync(0xffffffffu, gq[e], o);
+    }
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int e = 0; e < kGram; ++e) {
+      red[warp][e] = gp[e];
+      red[warp][kGram + e] = gq[e];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 2 * kGram) {
+    float s = 0.f;
+    for (int w = 0; w < kFacThreads / 32; ++w) s += red[w][threadIdx.x];
+    part[((size_t)j * gridDim.x + blockIdx.x) * (2 * kGram) + threadIdx.x] = s;
+  }
+}
+
+// Signed scale of both members of pair j: +-sigma * c_j with
+// c_j = sqrt(n*k) / (||P Psi||_F + 1e-7), each step rounded to the parameter dtype as
+// the reference's low_rank branch evaluates `z * (numel**0.5 / (z.norm() + 1e-7))`.
+// ||P Psi||_F^2 = sum_{r,s} (P^T P)_{rs} (Psi Psi^T)_{rs}.
+template <int DT>
+__global__ void __launch_bounds__(128) factor_scale_kernel(const float* __restrict__ part, int32_t pairs, int32_t nblk,
+                                                           float sqrt_numel, float sigma, int32_t normalize,
+                                                           float* __restrict__ scale) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= pairs) return;
+  double g[2 * kGram];
+  for (int e = 0; e < 2 * kGram; ++e) g[e] = 0.0;
+  for (int bi = 0; bi < nblk; ++bi)
+    for (int e = 0; e < 2 * kGram; ++e) g[e] += (double)part[((size_t)j * nblk + bi) * (2 * kGram) + e];
+  float c = 1.f;
+  if (normalize) {
+    double fro2 = 0.0;
+    for (int e = 0; e < kGram; ++e) {
+      const bool diag = (e == 0 || e == 4 || e == 7 || e == 9);
+      fro2 += (diag ? 1.0 : 2.0) * g[e] * g[kGram + e];
+    }
+    const float norm = zt::Dt<DT>::round((float)sqrt(fro2 > 0.0 ? fro2 : 0.0));
+    const float t = zt::Dt<DT>::round(norm + 1e-7f);
+    c = zt::Dt<DT>::round(__fmul_rn(__fdiv_rn(1.0f, t), sqrt_numel));
+  }
+  const float s = sigma * c;
+  scale[2 * j] = s;
+  scale[2 * j + 1] = -s;
+}
+
+// ---- RMSNorm with per-member weights -------------------------------------------------
+
+// wm[2j][t] = w[t] + sigma z_j[t], wm[2j+1][t] = w[t] - sigma z_j[t] (fp32 fused
+// multiply-add, rounded to bf16), z_j[t] the N(0,1) sample at offset t for key keys[j].
+__global__ void __launch_bounds__(256) norm_weights_kernel(const __grid_constant__ PairKeys K, const __nv_bfloat16* __restrict__ w,
+                                                           int32_t d, float sigma, __nv_bfloat16* __restrict__ wm) {
+  const int j = blockIdx.y;
+  const uint32_t key = K.ka[j];
+  for (int t = blockIdx.x * 256 + threadIdx.x; t < d; t += gridDim.x * 256) {
+    const float z = zt::gauss((uint32_t)t, key);
+    const float wf = __bfloat162float(w[t]);
+    wm[(size_t)(2 * j) * d + t] = __float2bfloat16_rn(fmaf(sigma, z, wf));
+    wm[(size_t)(2 * j + 1) * d + t] = __float2bfloat16_rn(fmaf(-sigma, z, wf));
+  }
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float f[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  const uint32_t l = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
+  const uint32_t h = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
+  return l | (h << 16);
+}
+
+__device__ __forceinline__ uint4 pack8(const float f[8]) {
+  return make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
+}
+
+__device__ __forceinline__ float bf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// One warp per row: y = wm[member] * bf16(x * rsqrt(mean(x^2) + eps)), the Llama RMSNorm
+// (fp32 statistics, normalised row rounded to bf16 before the weight product).
+constexpr int kNormRows = 8;
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const uint4* __restrict__ x, const uint4* __restrict__ wm,
+                                                      uint4* __restrict__ y, int64_t rows, int32_t d8,
+                                                      int32_t rows_per_member, float inv_d, float eps) {
+  const int64_t row = (int64_t)blockIdx.x * kNormRows + threadIdx.x / 32;
+  if (row >= rows) return;
+  const int lane = threadIdx.x % 32;
+  const uint4* xr = x + row * d8;
+  float ss = 0.f;
+  for (int c = lane; c < d8; c += 32) {
+    float f[8];
+    unpack8(xr[c], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float inv = rsqrtf(ss * inv_d + eps);
+  const uint4* wr = wm + (int64_t)(row / rows_per_member) * d8;
+  uint4* yr = y + row * d8;
+  for (int c = lane; c < d8; c += 32) {
+    float f[8], g[8];
+    unpack8(xr[c], f);
+    unpack8(wr[c], g);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] = g[e] * bf(f[e] * inv);
+    yr[c] = pack8(f);
+  }
+}
+
+// ---- rotary position embedding, in place --------------------------------------------
+
+// x_embed = x * cos + rotate_half(x) * sin with every product and the sum rounded to bf16
+// (the torch evaluation of the Llama rotary embedding on bf16 tensors). One thread owns 8
+// consecutive dims i of one head's first half and the matching 8 of its second half.
+__global__ void __launch_bounds__(256) rope_kernel(uint4* __restrict__ q, uint4* __restrict__ k,
+                                                   const uint4* __restrict__ cs, const uint4* __restrict__ sn,
+                                                   int64_t rows, int32_t seq, int32_t hq, int32_t hk, int32_t hd) {
+  const int half8 = hd / 16;               // 8-element chunks per half head
+  const int per_row = (hq + hk) * half8;
+  const int64_t total = rows * per_row;
+  const int hd8 = hd / 8;
+  for (int64_t it = (int64_t)blockIdx.x * 256 + threadIdx.x; it < total; it += (int64_t)gridDim.x * 256) {
+    const int64_t row = it / per_row;
+    const int rem = (int)(it - row * per_row);
+    const int head = rem / half8, c = rem - head * half8;
+    uint4* base = head < hq ? q + (row * hq + head) * hd8 : k + (row * hk + (head - hq)) * hd8;
+    const int64_t pos = row % seq;
+    float x1[8], x2[8], c1[8], c2[8], s1[8], s2[8];
+    unpack8(base[c], x1);
+    unpack8(base[c + half8], x2);
+    unpack8(cs[pos * hd8 + c], c1);
+    unpack8(cs[pos * hd8 + c + half8], c2);
+    unpack8(sn[pos * hd8 + c], s1);
+    unpack8(sn[pos * hd8 + c + half8], s2);
+    float o1[8], o2[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      o1[e] = bf(x1[e] * c1[e]) + bf(-x2[e] * s1[e]);
+      o2[e] = bf(x2[e] * c2[e]) + bf(x1[e] * s2[e]);
+    }
+    base[c] = pack8(o1);
+    base[c + half8] = pack8(o2);
+  }
+}
+
+// ---- SwiGLU ---------------------------------------------------------------------------
+
+// y = bf16(bf16(silu(g)) * u), silu(x) = x / (1 + exp(-x)) in fp32 (torch's bf16 SiLU
+// followed by a bf16 product).
+__global__ void __launch_bounds__(256) swiglu_kernel(const uint4* __restrict__ g, const uint4* __restrict__ u,
+                                                     uint4* __restrict__ y, int64_t n8) {
+  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n8; i += (int64_t)gridDim.x * 256) {
+    float a[8], b[8];
+    unpack8(g[i], a);
+    unpack8(u[i], b);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) a[e] = bf(a[e] / (1.0f + expf(-a[e]))) * b[e];
+    y[i] = pack8(a);
+  }
+}
+
+int stream_grid(int64_t items, int per_sm) {
+  const int64_t want = (items + 255) / 256;
+  const int64_t cap = (int64_t)zt::sm_count() * per_sm;
+  return (int)(want < 1 ? 1 : (want < cap ? want : cap));
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int zt_eggroll_factors(const zt_eggroll_factor_args* args, void* stream) {
+  zt::clear_error();
+  if (!args) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_factors: null args");
+  const zt_eggroll_factor_args& A = *args;
+  if (A.rank != 4) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_factors: rank must be 4");
+  if (A.pairs <= 0 || A.n <= 0 || A.k <= 0) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_factors: empty shape");
+  if (A.pairs > kMaxPairs) return zt::set_error(ZT_ERR_LIMIT, "zt_eggroll_factors: more than ZT_EGGROLL_MAX_PAIRS pairs");
+  if (A.n * 4 > (int64_t)ZT_MAX_NUMEL || A.k * 4 > (int64_t)ZT_MAX_NUMEL)
+    return zt::set_error(ZT_ERR_LIMIT, "zt_eggroll_factors: factor fields beyond 2^31 elements");
+  if (!A.keys_a || !A.keys_b || !A.a || !A.b || !A.scale || !A.work)
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_factors: null pointer");
+  if (!aligned16(A.a) || !aligned16(A.b)) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_factors: a, b not 16-byte aligned");
+  if (A.dtype != ZT_F32 && A.dtype != ZT_BF16 && A.dtype != ZT_F16)
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_factors: unknown dtype");
+  PairKeys K;
+  for (int j = 0; j < kMaxPairs; ++j) {
+    K.ka[j] = j < A.pairs ? A.keys_a[j] : 0u;
+    K.kb[j] = j < A.pairs ? A.keys_b[j] : 0u;
+  }
+  const int64_t items = A.n + A.k;
+  int64_t nblk = (items + 4 * kFacThreads - 1) / (4 * kFacThreads);
+  if (nblk > kFacBlocks) nblk = kFacBlocks;
+  const dim3 grid((unsigned)nblk, (unsigned)A.pairs);
+  cudaStream_t s = zt::as_stream(stream);
+  float4* a4 = reinterpret_cast<float4*>(A.a);
+  float4* b4 = reinterpret_cast<float4*>(A.b);
+  const float sqrt_numel = (float)sqrt((double)A.n * (double)A.k);
+  const unsigned sgrid = (unsigned)((A.pairs + 127) / 128);
+  switch (A.dtype) {
+    case ZT_F32:
+      factor_kernel<ZT_F32><<<grid, kFacThreads, 0, s>>>(K, (int32_t)A.n, (int32_t)A.k, a4, b4, A.work);
+      factor_scale_kernel<ZT_F32><<<sgrid, 128, 0, s>>>(A.work, A.pairs, (int32_t)nblk, sqrt_numel, A.sigma, A.normalize, A.scale);
+      break;
+    case ZT_BF16:
+      factor_kernel<ZT_BF16><<<grid, kFacThreads, 0, s>>>(K, (int32_t)A.n, (int32_t)A.k, a4, b4, A.work);
+      factor_scale_kernel<ZT_BF16><<<sgrid, 128, 0, s>>>(A.work, A.pairs, (int32_t)nblk, sqrt_numel, A.sigma, A.normalize, A.scale);
+      break;
+    default:
+      factor_kernel<ZT_F16><<<grid, kFacThreads, 0, s>>>(K, (int32_t)A.n, (int32_t)A.k, a4, b4, A.work);
+      factor_scale_kernel<ZT_F16><<<sgrid, 128, 0, s>>>(A.work, A.pairs, (int32_t)nblk, sqrt_numel, A.sigma, A.normalize, A.scale);
+      break;
+  }
+  return zt::check_cuda(cudaGetLastError(), "zt_eggroll_factors launch");
+}
+
+int zt_eggroll_rmsnorm(const zt_eggroll_norm_args* args, void* stream) {
+  zt::clear_error();
+  if (!args) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_rmsnorm: null args");
+  const zt_eggroll_norm_args& A = *args;
+  if (A.pairs <= 0 || A.m <= 0 || A.d <= 0) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_rmsnorm: empty shape");
+  if (A.pairs > kMaxPairs) return zt::set_error(ZT_ERR_LIMIT, "zt_eggroll_rmsnorm: more than ZT_EGGROLL_MAX_PAIRS pairs");
+  if (A.d % 8 || A.d > (int64_t)ZT_MAX_NUMEL) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_rmsnorm: d must be a multiple of 8");
+  if (A.rows_per_member <= 0 || A.m != (int64_t)A.rows_per_member * 2 * A.pairs)
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_rmsnorm: m must equal rows_per_member * 2 * pairs");
+  if (!A.keys || !A.x || !A.w || !A.w_members || !A.y) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_rmsnorm: null pointer");
+  if (!aligned16(A.x) || !aligned16(A.w_members) || !aligned16(A.y))
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_rmsnorm: x, w_members, y not 16-byte aligned");
+  PairKeys K;
+  for (int j = 0; j < kMaxPairs; ++j) K.ka[j] = j < A.pairs ? A.keys[j] : 0u;
+  for (int j = 0; j < kMaxPairs; ++j) K.kb[j] = 0u;
+  cudaStream_t s = zt::as_stream(stream);
+  const dim3 wgrid((unsigned)((A.d + 255) / 256), (unsigned)A.pairs);
+  norm_weights_kernel<<<wgrid, 256, 0, s>>>(K, static_cast<const __nv_bfloat16*>(A.w), (int32_t)A.d, A.sigma,
+                                            static_cast<__nv_bfloat16*>(A.w_members));
+  if (int rc = zt::check_cuda(cudaGetLastError(), "zt_eggroll_rmsnorm: weights launch")) return rc;
+  const unsigned grid = (unsigned)((A.m + kNormRows - 1) / kNormRows);
+  rmsnorm_kernel<<<grid, 256, 0, s>>>(static_cast<const uint4*>(A.x), static_cast<const uint4*>(A.w_members),
+                                      static_cast<uint4*>(A.y), A.m, (int32_t)(A.d / 8), A.rows_per_member,
+                                      1.0f / (float)A.d, A.eps);
+  return zt::check_cuda(cudaGetLastError(), "zt_eggroll_rmsnorm launch");
+}
+
+int zt_eggroll_rope(void* q, void* k, const void* cos, const void* sin, int64_t rows, int32_t seq, int32_t q_heads,
+                    int32_t k_heads, int32_t head_dim, void* stream) {
+  zt::clear_error();
+  if (rows <= 0 || seq <= 0 || q_heads <= 0 || k_heads < 0 || head_dim <= 0)
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_rope: empty shape");
+  if (head_dim % 16) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_rope: head_dim must be a multiple of 16");
+  if (rows % seq) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_rope: rows must be a multiple of seq");
+  if (!q || (k_heads > 0 && !k) || !cos || !sin) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_rope: null pointer");
+  if (!aligned16(q) || (k && !aligned16(k)) || !aligned16(cos) || !aligned16(sin))
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_rope: pointers must be 16-byte aligned");
+  const int64_t items = rows * (int64_t)(q_heads + k_heads) * (head_dim / 16);
+  rope_kernel<<<stream_grid(items, 16), 256, 0, zt::as_stream(stream)>>>(
+      static_cast<uint4*>(q), static_cast<uint4*>(k), static_cast<const uint4*>(cos), static_cast<const uint4*>(sin),
+      rows, seq, q_heads, k_heads, head_dim);
+  return zt::check_cuda(cudaGetLastError(), "zt_eggroll_rope launch");
+}
+
+int zt_eggroll_swiglu(const void* gate, const void* up, void* out, int64_t n, void* stream) {
+  zt::clear_error();
+  if (n < 0 || n % 8) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_swiglu: n must be a non-negative multiple of 8");
+  if (n == 0) return ZT_OK;
+  if (!gate || !up || !out) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_swiglu: null pointer");
+  if (!aligned16(gate) || !aligned16(up) || !aligned16(out))
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_swiglu: pointers must be 16-byte aligned");
+  swiglu_kernel<<<stream_grid(n / 8, 16), 256, 0, zt::as_stream(stream)>>>(
+      static_cast<const uint4*>(gate), static_cast<const uint4*>(up), static_cast<uint4*>(out), n / 8);
+  return zt::check_cuda(cudaGetLastError(), "zt_eggroll_swiglu launch");
+}
+
+}  // extern "C"

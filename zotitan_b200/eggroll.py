@@ -14,8 +14,12 @@ pair sharing s_j with signs +1 / -1). The perturbation follows the reference's
 The linear layers never materialise p_i: ``zt_eggroll_linear`` computes
 x p^T + (sign sigma c) (x B_i) A_i^T with the base GEMM on the tensor cores and the
 rank-4 term in its epilogue, for all members of a chunk at once (member i owns a
-contiguous block of rows). ||P Psi||_F^2 = sum((P^T P) * (Psi Psi^T)) is a 4x4 product.
-Norm weights and the embedding rows are perturbed per member directly.
+contiguous block of rows). ``zt_eggroll_factors`` draws A_i, B_i and c for every pair of
+a chunk in one launch (||P Psi||_F^2 = sum((P^T P) * (Psi Psi^T)), a 4x4 product).
+The rest of a decoder layer runs as fused bandwidth-bound kernels on the population rows:
+RMSNorm with per-member weights (``zt_eggroll_rmsnorm``), the rotary embedding in place
+(``zt_eggroll_rope``) and the SwiGLU product (``zt_eggroll_swiglu``); attention is the
+model's own configured implementation. Embedding rows are perturbed per member directly.
 
 The reference names EGGROLL (README.md:11) but has no implementation; this module is
 the population forward the optimizer's fitness-shaping path (train_zo.py:474-508,
@@ -47,41 +51,27 @@ def _key(seed: int, n: int, idx: int) -> int:
 
 
 class _Population:
-    """The member chunk being evaluated: pair seeds, signs and per-tensor caches."""
+    """The member chunk being evaluated: its pair seeds and rows per member."""
 
     def __init__(self, n_params: int, cfg: EggrollConfig):
         self.n_params = n_params
         self.cfg = cfg
         self.pair_seeds: list[int] = []
         self.rows_per_member = 0
-        self.signs = None            # [members] fp32 (+1, -1, +1, -1, ...)
 
     @property
     def members(self) -> int:
         return 2 * len(self.pair_seeds)
 
-    def low_rank(self, idx: int, out_f: int, in_f: int, device):
-        """A [members, out, 4], B [members, in, 4] (fp32 holding bf16 values) and the signed
-        scale [members] of tensor idx for the current chunk."""
-        n = self.n_params
-        kp = [_key(s, n, idx + 2 * n) for s in self.pair_seeds]
-        kq = [_key(s, n, idx + n) for s in self.pair_seeds]
-        P = K.randn_keys(kp, out_f * RANK, device).view(-1, out_f, RANK).bfloat16().float()
-        Psi = K.randn_keys(kq, RANK * in_f, device).view(-1, RANK, in_f).bfloat16().float()
-        if self.cfg.normalize:
-            fro2 = torch.einsum("prs,prs->p", P.transpose(1, 2) @ P, Psi @ Psi.transpose(1, 2))
-            c = (out_f * in_f) ** 0.5 / (fro2.clamp_min(0).sqrt() + 1e-7)
-        else:
-            c = torch.ones(len(self.pair_seeds), device=device)
-        A = P.repeat_interleave(2, dim=0).contiguous()
-        B = Psi.transpose(1, 2).repeat_interleave(2, dim=0).contiguous()
-        scale = (self.cfg.sigma * c).repeat_interleave(2) * self.signs
-        return A, B, scale.float().contiguous()
+    def keys(self, idx: int) -> list[int]:
+        return [_key(s, self.n_params, idx) for s in self.pair_seeds]
 
-    def dense(self, idx: int, numel: int, device):
-        """Full Gaussian field [members, numel] of a 1-D tensor, signs and sigma applied."""
-        z = K.randn_keys([_key(s, self.n_params, idx) for s in self.pair_seeds], numel, device)
-        return z.repeat_interleave(2, dim=0) * (self.cfg.sigma * self.signs)[:, None]
+    def low_rank(self, idx: int, out_f: int, in_f: int, device, dtype=torch.bfloat16):
+        """A [members, out, 4], B [members, in, 4] (fp32 holding dtype-rounded values) and
+        the signed scale [members] of tensor idx for the current chunk (zt_eggroll_factors:
+        one launch for the factors of every pair plus one for the normalisation)."""
+        return K.eggroll_factors(self.keys(idx + 2 * self.n_params), self.keys(idx + self.n_params), out_f, in_f,
+                                 self.cfg.sigma, device, dtype, self.cfg.normalize)
 
 
 class PopLinear(nn.Module):
@@ -96,13 +86,14 @@ class PopLinear(nn.Module):
         shp = x.shape
         x2 = x.reshape(-1, shp[-1]).contiguous()
         out_f, in_f = self.weight.shape
-        A, B, sig = self.pop.low_rank(self.idx, out_f, in_f, x.device)
+        A, B, sig = self.pop.low_rank(self.idx, out_f, in_f, x.device, self.weight.dtype)
         y = K.eggroll_linear(x2, self.weight.data, A, B, sig, self.pop.rows_per_member)
         return y.view(*shp[:-1], out_f)
 
 
 class PopRMSNorm(nn.Module):
-    """Llama RMSNorm with member i's weight w + sign_i sigma z_i on member i's rows."""
+    """Llama RMSNorm with member i's weight w + sign_i sigma z_i on member i's rows
+    (zt_eggroll_rmsnorm: the member weights and the normalisation in two launches)."""
 
     def __init__(self, base, idx: int, pop: _Population):
         super().__init__()
@@ -111,13 +102,54 @@ class PopRMSNorm(nn.Module):
         self.idx, self.pop = idx, pop
 
     def forward(self, x):
-        dt = x.dtype
-        h = x.float()
-        h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + self.eps)
-        d = self.weight.shape[0]
-        w = (self.weight.float()[None, :] + self.pop.dense(self.idx, d, x.device)).to(self.weight.dtype)
-        P = self.pop.members
-        return (w[:, None, :] * h.to(dt).reshape(P, -1, d)).reshape(x.shape)
+        return K.eggroll_rmsnorm(x.contiguous(), self.weight.data, self.pop.keys(self.idx), self.pop.cfg.sigma,
+                                 self.eps, self.pop.rows_per_member)
+
+
+class PopAttention(nn.Module):
+    """transformers' LlamaAttention with population projections and the rotary embedding
+    applied in place by zt_eggroll_rope; the attention itself is the model's configured
+    implementation, called exactly as LlamaAttention.forward calls it."""
+
+    _ATTRS = ("config", "layer_idx", "head_dim", "num_key_value_groups", "scaling", "attention_dropout", "is_causal")
+
+    def __init__(self, base, q_proj, k_proj, v_proj, o_proj):
+        super().__init__()
+        for a in self._ATTRS:
+            setattr(self, a, getattr(base, a))
+        self.q_proj, self.k_proj, self.v_proj, self.o_proj = q_proj, k_proj, v_proj, o_proj
+
+    def forward(self, hidden_states, position_embeddings=None, attention_mask=None, past_key_values=None, **kwargs):
+        from transformers.models.llama.modeling_llama import ALL_ATTENTION_FUNCTIONS, eager_attention_forward
+        bsz, T, _ = hidden_states.shape
+        hd = self.head_dim
+        q = self.q_proj(hidden_states)
+        k = self.k_proj(hidden_states)
+        v = self.v_proj(hidden_states)
+        cos, sin = position_embeddings
+        if cos.shape[0] != 1:
+            raise NotImplementedError("per-sequence position ids")
+        K.eggroll_rope_(q, k, cos[0].contiguous(), sin[0].contiguous(), T, hd)
+        q = q.view(bsz, T, -1, hd).transpose(1, 2)
+        k = k.view(bsz, T, -1, hd).transpose(1, 2)
+        v = v.view(bsz, T, -1, hd).transpose(1, 2)
+        if past_key_values is not None:
+            k, v = past_key_values.update(k, v, self.layer_idx)
+        attn = ALL_ATTENTION_FUNCTIONS.get_interface(self.config._attn_implementation, eager_attention_forward)
+        out, weights = attn(self, q, k, v, attention_mask, dropout=0.0, scaling=self.scaling, **kwargs)
+        return self.o_proj(out.reshape(bsz, T, -1).contiguous()), weights
+
+
+class PopMLP(nn.Module):
+    """Llama MLP down(silu(gate(x)) * up(x)) with population projections and the SwiGLU
+    product in one launch (zt_eggroll_swiglu)."""
+
+    def __init__(self, gate_proj, up_proj, down_proj):
+        super().__init__()
+        self.gate_proj, self.up_proj, self.down_proj = gate_proj, up_proj, down_proj
+
+    def forward(self, x):
+        return self.down_proj(K.eggroll_swiglu(self.gate_proj(x), self.up_proj(x)))
 
 
 class PopEmbedding(nn.Module):
@@ -130,7 +162,7 @@ class PopEmbedding(nn.Module):
 
     def forward(self, ids):
         V, d = self.weight.shape
-        A, B, sig = self.pop.low_rank(self.idx, V, d, ids.device)   # A [m, V, 4], B [m, d, 4]
+        A, B, sig = self.pop.low_rank(self.idx, V, d, ids.device, self.weight.dtype)   # A [m, V, 4], B [m, d, 4]
         P = self.pop.members
         ids_m = ids.reshape(P, -1)                                  # member i's token ids
         rows = torch.gather(A, 1, ids_m[..., None].expand(-1, -1, RANK))   # [m, tokens, 4]
@@ -151,25 +183,40 @@ class EggrollPopulation:
         named = [(n, p) for n, p in model.named_parameters() if p.requires_grad]
         index = {id(p): i for i, (_, p) in enumerate(named)}
         self.pop = _Population(len(named), self.cfg)
-        norm_types = tuple(t for t in (getattr(__import__("transformers.models.llama.modeling_llama", fromlist=["x"]),
-                                               "LlamaRMSNorm", None),) if t is not None)
+        from transformers.models.llama import modeling_llama as ml
         replaced = set()
+
+        def lin(mod):
+            replaced.add(index[id(mod.weight)])
+            return PopLinear(mod, index[id(mod.weight)], self.pop)
+
+        done_prefixes: list[str] = []
         for name, mod in list(model.named_modules()):
+            if any(name.startswith(p) for p in done_prefixes):
+                continue
             new = None
-            if isinstance(mod, nn.Linear) and id(mod.weight) in index:
-                new = PopLinear(mod, index[id(mod.weight)], self.pop)
+            if isinstance(mod, ml.LlamaAttention):
+                new = PopAttention(mod, *(lin(getattr(mod, a)) for a in ("q_proj", "k_proj", "v_proj", "o_proj")))
+            elif isinstance(mod, ml.LlamaMLP):
+                if getattr(mod.config, "hidden_act", "silu") != "silu":
+                    raise NotImplementedError("EGGROLL MLP: SiLU gating only")
+                new = PopMLP(*(lin(getattr(mod, a)) for a in ("gate_proj", "up_proj", "down_proj")))
+            elif isinstance(mod, nn.Linear) and id(mod.weight) in index:
+                new = lin(mod)
             elif isinstance(mod, nn.Embedding) and id(mod.weight) in index:
                 new = PopEmbedding(mod, index[id(mod.weight)], self.pop)
-            elif norm_types and isinstance(mod, norm_types) and id(mod.weight) in index:
+                replaced.add(index[id(mod.weight)])
+            elif isinstance(mod, ml.LlamaRMSNorm) and id(mod.weight) in index:
                 new = PopRMSNorm(mod, index[id(mod.weight)], self.pop)
+                replaced.add(index[id(mod.weight)])
             if new is None:
                 continue
+            done_prefixes.append(name + ".")
             parent = model
             *path, leaf = name.split(".")
             for p in path:
                 parent = getattr(parent, p)
             setattr(parent, leaf, new)
-            replaced.add(index[id(mod.weight)])
         missing = [n for i, (n, _) in enumerate(named) if i not in replaced]
         if missing:
             raise NotImplementedError(f"no population module for trainable tensors: {missing[:4]}")
@@ -184,9 +231,8 @@ class EggrollPopulation:
         pop.pair_seeds = list(pair_seeds)
         P = pop.members
         pop.rows_per_member = S * T
-        pop.signs = torch.tensor([1.0, -1.0] * len(pair_seeds), device=tokens.device)
         ids = tokens.repeat(P, 1)                                   # [P*S, T]
-        hidden = self.model.model(input_ids=ids).last_hidden_state   # [P*S, T, d]
+        hidden = self.model.model(input_ids=ids, use_cache=False).last_hidden_state   # [P*S, T, d]
         logits = self.model.lm_head(hidden)                          # [P*S, T, V] bf16
         V = logits.shape[-1]
         ce = F.cross_entropy(logits[:, :-1, :].reshape(-1, V).float(), ids[:, 1:].reshape(-1), reduction="none")

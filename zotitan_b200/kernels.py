@@ -265,3 +265,90 @@ def eggroll_take_error() -> int:
     code = ctypes.c_int32(0)
     L.check(L.load().zt_eggroll_take_error(ctypes.byref(code)), "zt_eggroll_take_error")
     return int(code.value)
+
+
+_DT = {torch.float32: L.ZT_F32, torch.bfloat16: L.ZT_BF16, torch.float16: L.ZT_F16}
+
+
+def _keys_array(keys):
+    arr = (ctypes.c_uint32 * max(1, len(keys)))(*[int(k) & 0xFFFFFFFF for k in keys])
+    return arr
+
+
+def eggroll_factors(keys_a: list[int], keys_b: list[int], n: int, k: int, sigma: float, device,
+                    dtype: torch.dtype = torch.bfloat16, normalize: bool = True):
+    """Rank-4 factors of an [n, k] tensor for antithetic pairs (zt_eggroll_factors):
+    returns A [2p, n, 4], B [2p, k, 4] (fp32 holding dtype-rounded values) and the signed
+    scale [2p] (+sigma c_j, -sigma c_j), ready for eggroll_linear."""
+    pairs = len(keys_a)
+    if pairs != len(keys_b) or pairs == 0:
+        raise ValueError("keys_a and keys_b must be non-empty and of equal length")
+    if pairs > L.ZT_EGGROLL_MAX_PAIRS:
+        raise ValueError(f"at most {L.ZT_EGGROLL_MAX_PAIRS} pairs per call")
+    device = torch.device(device)
+    a = torch.empty((2 * pairs, n, 4), dtype=torch.float32, device=device)
+    b = torch.empty((2 * pairs, k, 4), dtype=torch.float32, device=device)
+    scale = torch.empty(2 * pairs, dtype=torch.float32, device=device)
+    work = torch.empty(pairs * L.ZT_EGGROLL_FACTOR_WORK_FLOATS, dtype=torch.float32, device=device)
+    ka, kb = _keys_array(keys_a), _keys_array(keys_b)
+    args = L.ZtEggrollFactorArgs(ctypes.addressof(ka), ctypes.addressof(kb), pairs, 4, n, k, _DT[dtype],
+                                 1 if normalize else 0, float(sigma), 0, a.data_ptr(), b.data_ptr(), scale.data_ptr(),
+                                 work.data_ptr())
+    with torch.cuda.device(device):
+        L.check(L.load().zt_eggroll_factors(ctypes.byref(args), _stream_ptr(device)), "zt_eggroll_factors")
+    return a, b, scale
+
+
+def eggroll_rmsnorm(x: torch.Tensor, w: torch.Tensor, keys: list[int], sigma: float, eps: float,
+                    rows_per_member: int) -> torch.Tensor:
+    """Llama RMSNorm of population rows x [M, d] with member-perturbed weights
+    (zt_eggroll_rmsnorm): members 2j / 2j+1 use bf16(w +- sigma randn(keys[j]))."""
+    _check_cuda(x, "x")
+    _check_cuda(w, "w")
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise ValueError("x and w must be bf16")
+    if not x.is_contiguous() or not w.is_contiguous():
+        raise ValueError("x and w must be contiguous")
+    d = w.shape[0]
+    x2 = x.reshape(-1, d)
+    pairs = len(keys)
+    wm = torch.empty((2 * pairs, d), dtype=torch.bfloat16, device=x.device)
+    y = torch.empty_like(x2)
+    ka = _keys_array(keys)
+    args = L.ZtEggrollNormArgs(x2.data_ptr(), w.data_ptr(), ctypes.addressof(ka), wm.data_ptr(), y.data_ptr(),
+                               x2.shape[0], d, pairs, rows_per_member, float(sigma), float(eps))
+    with torch.cuda.device(x.device):
+        L.check(L.load().zt_eggroll_rmsnorm(ctypes.byref(args), _stream_ptr(x.device)), "zt_eggroll_rmsnorm")
+    return y.view(x.shape)
+
+
+def eggroll_rope_(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, seq: int, head_dim: int):
+    """In-place rotary embedding of q [rows, Hq*hd] and k [rows, Hk*hd] (bf16, row r at
+    position r % seq) with cos, sin [seq, hd] bf16 (zt_eggroll_rope)."""
+    for t, name in ((q, "q"), (k, "k"), (cos, "cos"), (sin, "sin")):
+        _check_cuda(t, name)
+        if t.dtype != torch.bfloat16 or not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous bf16")
+    rows = q.numel() // q.shape[-1]
+    if cos.shape != (seq, head_dim) or sin.shape != (seq, head_dim):
+        raise ValueError("cos and sin must be [seq, head_dim]")
+    hq, hk = q.shape[-1] // head_dim, k.shape[-1] // head_dim
+    with torch.cuda.device(q.device):
+        L.check(L.load().zt_eggroll_rope(q.data_ptr(), k.data_ptr(), cos.data_ptr(), sin.data_ptr(), rows, seq, hq, hk,
+                                         head_dim, _stream_ptr(q.device)), "zt_eggroll_rope")
+    return q, k
+
+
+def eggroll_swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """bf16(bf16(silu(gate)) * up) (zt_eggroll_swiglu)."""
+    for t, name in ((gate, "gate"), (up, "up")):
+        _check_cuda(t, name)
+        if t.dtype != torch.bfloat16 or not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous bf16")
+    if gate.shape != up.shape:
+        raise ValueError("gate and up must have the same shape")
+    out = torch.empty_like(gate)
+    with torch.cuda.device(gate.device):
+        L.check(L.load().zt_eggroll_swiglu(gate.data_ptr(), up.data_ptr(), out.data_ptr(), gate.numel(),
+                                           _stream_ptr(gate.device)), "zt_eggroll_swiglu")
+    return out
