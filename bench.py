@@ -43,6 +43,7 @@ def parse():
     ap.add_argument("--seeds", type=int, default=N_SEEDS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-eggroll", action="store_true", help="skip the EGGROLL population measurement")
+    ap.add_argument("--no-mezo", action="store_true", help="skip the MeZO full fine-tune step measurement")
     ap.add_argument("--profile-case", choices=["chain", "full", "eggroll"], default=None,
                     help="small case for ncu: one bf16 tensor of 2^28 elements, 3 launches of the "
                          "-2eps pass (chain) or of the restore+accumulate+perturb pass (full); or 3 "
@@ -317,6 +318,64 @@ def eggroll_member_evals(dev, rank: int, world: int, pairs_per_rank: int = 16, p
             "mean_loss": float(mine.mean())}
 
 
+def mezo_full_ft_steps(dev, rank: int, world: int, steps: int = 3, warmup: int = 2, pairs: int = 8):
+    """ZO steps/s of MeZO full fine-tuning on the Llama-3.2-1B-shaped bf16 model (tied
+    embeddings, N(0,0.02) weights from seed 0): 8 antithetic pairs per step sharded over
+    the ranks (rank r scores pairs r, r+W, ...), each pair on its own 16 x 512 batch of
+    uniform random tokens (batch of pair j at step t from seed 1000*t + j), next-token
+    CE + 1e-4 z-loss through the fused CUDA scorer, eps = 1e-3, lr = 1e-5. One step =
+    2 forwards per local pair + the fused perturb/restore/update passes + the all-gather
+    of the pair losses (and, with W > 1, the sharded update's parameter all-gather).
+    Batches are built on the device before the timed region. Timed with CUDA events
+    over `steps` steps, max over ranks; weak in pairs per rank only when W divides 8."""
+    import torch
+    import torch.distributed as dist
+
+    from zotitan_b200.data import synthetic_token_batch
+    from zotitan_b200.objective import SyntheticTokensObjective
+    from zotitan_b200.synthetic import LLAMA_1B, build_llama
+    from zotitan_b200.train_zo import ZOConfig, ZOOptimizer
+    B, S = 16, 512
+    model = build_llama(LLAMA_1B, device=dev, seed=0, max_positions=S)
+    objective = SyntheticTokensObjective(LLAMA_1B.vocab, S, z_loss_weight=1e-4)
+    cfg = ZOConfig()
+    cfg.eps, cfg.z_batch, cfg.base.lr = EPS, pairs, 1e-5
+    named = [(n, p) for n, p in model.named_parameters() if p.requires_grad]
+    opt = ZOOptimizer(named, cfg, objective.score, total_steps=steps + warmup)
+    mine = set(range(rank, pairs, world))
+
+    def batches_for(t):
+        return [synthetic_token_batch(LLAMA_1B.vocab, B, S, 1000 * t + j, device=dev) if j in mine else None
+                for j in range(pairs)]
+
+    plan = [batches_for(t) for t in range(warmup + steps)]
+    for t in range(warmup):
+        opt.step(model, plan[t])
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for t in range(warmup, warmup + steps):
+        m = opt.step(model, plan[t])
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    n_params = sum(p.numel() for _, p in named)
+    del opt, model, named, plan
+    torch.cuda.empty_cache()
+    return {"metric": "ZO steps/s (MeZO full fine-tune, Llama-3.2-1B shape)", "value": steps / (ms * 1e-3),
+            "unit": "ZO steps/s", "ms_per_step": ms / steps, "steps": steps, "warmup": warmup,
+            "pairs_per_step": pairs, "forwards_per_step": 2 * pairs, "batch": B, "seq_len": S,
+            "tokens_per_step": 2 * pairs * B * S, "params": n_params, "z_loss": 1e-4,
+            "scorer": "fused CUDA cross-entropy (zt_xent_rows)", "parallelism": f"pair-sharded x{world}",
+            "loss_last_step": m["loss"], "proj_grad_last_step": m["proj_grad"]}
+
+
 # ── our arm ─────────────────────────────────────────────────────────────────────────
 
 def run_ours(args, rank, local_rank, world):
@@ -445,6 +504,7 @@ def run_ours(args, rank, local_rank, world):
     del opt, named
     torch.cuda.empty_cache()
     egg = eggroll_member_evals(dev, rank, world) if not args.no_eggroll else None
+    mezo = mezo_full_ft_steps(dev, rank, world) if not args.no_mezo else None
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
@@ -498,6 +558,8 @@ def run_ours(args, rank, local_rank, world):
         line["cpu_baseline"] = cpu_line
     if egg is not None:
         line["eggroll"] = egg
+    if mezo is not None:
+        line["mezo_full_ft"] = mezo
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

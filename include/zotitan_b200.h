@@ -331,6 +331,20 @@ ZT_API int zt_eggroll_rope(void* q, void* k, const void* cos, const void* sin, i
  * act_fn(gate_proj(x)) * up_proj(x). */
 ZT_API int zt_eggroll_swiglu(const void* gate, const void* up, void* out, int64_t n, void* stream);
 
+/* ---- the scorer: next-token cross-entropy statistics ------------------------------ */
+
+/* Per-row statistics of bf16 logits [rows, vocab] (row stride ld elements, ld % 8 == 0,
+ * 16-byte aligned) against int64 targets[rows] (negative = ignored):
+ *   lse[r]     = log(sum_v exp(x[r, v]))        (fp32, max-shifted; the z-loss term)
+ *   loss[r]    = -((x[r, t] - max_r) - log(sum_v exp(x[r, v] - max_r)))
+ *   correct[r] = (first argmax of x[r, :] == t)
+ * as torch's cross_entropy / logsumexp / argmax evaluate them on the fp32 upcast of the
+ * logits (zotitan/losses.py:55-79; transformers' ForCausalLMLoss). Ignored rows get
+ * 0 in all three; a target >= vocab gives NaN. lse and correct may be NULL. Replaces the
+ * reference's Liger fused cross-entropy (zotitan/losses.py:17-52) after the lm_head GEMM. */
+ZT_API int zt_xent_rows(const void* logits, int64_t ld, int64_t rows, int64_t vocab, const int64_t* targets,
+                        float* loss, float* lse, int32_t* correct, void* stream);
+
 /* ---- the fused pass without a caller-provided workspace -------------------------- */
 
 #define ZT_STATIC_MAX_TENSORS 1024

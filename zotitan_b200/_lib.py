@@ -27,7 +27,7 @@ ZT_BUF_DATA, ZT_BUF_LIVE = 1, 2
 EXPORTS = ("zt_last_error", "zt_abi_version", "zt_param_key", "zt_philox_words", "zt_randn",
            "zt_randn_at", "zt_plan_workspace_bytes", "zt_plan_init", "zt_pass", "zt_pass_static",
            "zt_eggroll_linear", "zt_eggroll_take_error", "zt_randn_keys", "zt_eggroll_factors",
-           "zt_eggroll_rmsnorm", "zt_eggroll_rope", "zt_eggroll_swiglu")
+           "zt_eggroll_rmsnorm", "zt_eggroll_rope", "zt_eggroll_swiglu", "zt_xent_rows")
 ZT_STATIC_MAX_TENSORS = 1024
 ZT_EGGROLL_MAX_PAIRS = 512
 ZT_EGGROLL_FACTOR_WORK_FLOATS = 64 * 20
@@ -133,6 +133,8 @@ def load():
     lib.zt_eggroll_rope.argtypes = [P, P, P, P, I64, I32, I32, I32, I32, P]
     lib.zt_eggroll_swiglu.restype = ctypes.c_int
     lib.zt_eggroll_swiglu.argtypes = [P, P, P, I64, P]
+    lib.zt_xent_rows.restype = ctypes.c_int
+    lib.zt_xent_rows.argtypes = [P, I64, I64, I64, P, P, P, P, P]
     lib.zt_plan_workspace_bytes.restype = ctypes.c_size_t
     lib.zt_plan_workspace_bytes.argtypes = [I32]
     if lib.zt_abi_version() != ABI_VERSION:

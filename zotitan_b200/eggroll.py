@@ -31,7 +31,6 @@ from dataclasses import dataclass
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
 from . import kernels as K
 
@@ -235,5 +234,7 @@ class EggrollPopulation:
         hidden = self.model.model(input_ids=ids, use_cache=False).last_hidden_state   # [P*S, T, d]
         logits = self.model.lm_head(hidden)                          # [P*S, T, V] bf16
         V = logits.shape[-1]
-        ce = F.cross_entropy(logits[:, :-1, :].reshape(-1, V).float(), ids[:, 1:].reshape(-1), reduction="none")
-        return ce.view(P, -1).mean(dim=1)
+        tgt = torch.full_like(ids, -100)
+        tgt[:, :-1] = ids[:, 1:]
+        ce, _, _ = K.xent_rows(logits.view(-1, V), tgt.view(-1), want_lse=False, want_correct=False)
+        return ce.view(P, -1).sum(dim=1) / (S * (T - 1))

@@ -352,3 +352,26 @@ def eggroll_swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
         L.check(L.load().zt_eggroll_swiglu(gate.data_ptr(), up.data_ptr(), out.data_ptr(), gate.numel(),
                                            _stream_ptr(gate.device)), "zt_eggroll_swiglu")
     return out
+
+
+def xent_rows(logits: torch.Tensor, targets: torch.Tensor, want_lse: bool = True, want_correct: bool = True):
+    """Per-row cross-entropy statistics of bf16 logits [rows, vocab] against int64
+    targets [rows] (negative = ignored), zt_xent_rows: returns (loss, lse | None,
+    correct | None) as fp32, fp32, int32 [rows]."""
+    _check_cuda(logits, "logits")
+    _check_cuda(targets, "targets")
+    if logits.dtype != torch.bfloat16 or logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be a bf16 [rows, vocab] matrix with unit column stride")
+    if targets.dtype != torch.int64 or targets.shape != (logits.shape[0],) or not targets.is_contiguous():
+        raise ValueError("targets must be a contiguous int64 [rows] vector")
+    rows, vocab = logits.shape
+    dev = logits.device
+    loss = torch.empty(rows, dtype=torch.float32, device=dev)
+    lse = torch.empty(rows, dtype=torch.float32, device=dev) if want_lse else None
+    correct = torch.empty(rows, dtype=torch.int32, device=dev) if want_correct else None
+    with torch.cuda.device(dev):
+        L.check(L.load().zt_xent_rows(logits.data_ptr(), logits.stride(0), rows, vocab, targets.data_ptr(),
+                                      loss.data_ptr(), lse.data_ptr() if lse is not None else None,
+                                      correct.data_ptr() if correct is not None else None, _stream_ptr(dev)),
+                "zt_xent_rows")
+    return loss, lse, correct

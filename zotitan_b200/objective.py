@@ -2,8 +2,9 @@
 
 Mirrors zotitan/objective.py: ``Score`` (:36-39), the ``Objective`` protocol
 (:154-163), ``CrossEntropyCriterion`` (:59-95), ``RubricObjective`` (:186-217) and the
-``register_objective`` registry (:170-181). Cross-entropy is the reference's torch
-path (zotitan/losses.py:55-79); the Liger/Triton fused path is not used here.
+``register_objective`` registry (:170-181). Cross-entropy comes from ``losses``: the
+CUDA fused scorer by default (the reference's default is its fused Liger path), or the
+reference's torch path with fused=False.
 Dataset-backed objectives need network datasets and are out of scope; a
 synthetic-token objective stands in for them.
 """
@@ -15,6 +16,7 @@ from typing import Iterator, Protocol
 import torch
 
 from .data import synthetic_token_batches
+from .losses import get_xentropy, torch_xentropy  # noqa: F401  (torch_xentropy re-exported)
 
 Metric = torch.Tensor | float
 
@@ -47,37 +49,21 @@ def register_objective(name: str):
     return deco
 
 
-def torch_xentropy(model, batch, z_loss_weight: float, compute_accuracy: bool):
-    """Full forward, CE from materialised logits, optional z-loss and accuracy
-    (zotitan/losses.py:55-79). Returns (loss, z_loss | None, extra | None)."""
-    out = model(**batch)
-    loss = out.loss
-    extra = None
-    if compute_accuracy:
-        logits = out.logits[:, :-1, :]
-        labels = batch["labels"][:, 1:]
-        mask = labels != -100
-        correct = (logits.argmax(-1) == labels) & mask
-        extra = {"acc": correct.sum() / mask.sum().clamp_min(1)}
-    if z_loss_weight == 0.0:
-        return loss, None, extra
-    logits = out.logits[:, :-1, :].float()
-    labels = batch["labels"][:, 1:]
-    mask = labels != -100
-    lse = torch.logsumexp(logits, dim=-1)
-    z_loss = z_loss_weight * (lse.square() * mask).sum() / mask.sum().clamp_min(1)
-    return loss, z_loss, extra
-
-
 class CrossEntropyCriterion:
-    """value = ce + z_loss; metrics {"ce", "z_loss", "acc"} (zotitan/objective.py:59-95)."""
+    """value = ce + z_loss; metrics {"ce", "z_loss", "acc"} (zotitan/objective.py:59-95).
+    fused=True (the reference's default) scores with the CUDA cross-entropy
+    (losses.fused_xentropy); fused=False with the reference's torch path."""
     name = "ce"
     differentiable = True
 
-    def __init__(self, z_loss_weight: float = 0.0, compute_accuracy: bool = True, fn=None):
+    def __init__(self, compile_enabled: bool = False, compile_mode: str | None = None, z_loss_weight: float = 0.0,
+                 fused: bool = True, compute_accuracy: bool = True, fn=None):
+        self.compile_enabled = compile_enabled
+        self.compile_mode = compile_mode
         self.z_loss_weight = z_loss_weight
+        self.fused = fused
         self.compute_accuracy = compute_accuracy
-        self.fn = fn or torch_xentropy
+        self.fn = fn or get_xentropy(fused=fused, compile_mode=compile_mode)
 
     def __call__(self, model, batch):
         loss, z_loss, extra = self.fn(model, batch, self.z_loss_weight, self.compute_accuracy)
@@ -122,8 +108,8 @@ class RubricObjective:
 class SyntheticTokensObjective(RubricObjective):
     """Next-token CE (+ z-loss) on uniform random token ids of a fixed length."""
 
-    def __init__(self, vocab_size: int, seq_len: int, z_loss_weight: float = 0.0):
-        super().__init__([(CrossEntropyCriterion(z_loss_weight=z_loss_weight), 1.0)])
+    def __init__(self, vocab_size: int, seq_len: int, z_loss_weight: float = 0.0, fused: bool = True):
+        super().__init__([(CrossEntropyCriterion(z_loss_weight=z_loss_weight, fused=fused), 1.0)])
         self.vocab_size, self.seq_len = vocab_size, seq_len
 
     def train_batches(self, tokenizer, seed: int, batch_size: int):
