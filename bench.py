@@ -44,10 +44,12 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-eggroll", action="store_true", help="skip the EGGROLL population measurement")
     ap.add_argument("--no-mezo", action="store_true", help="skip the MeZO full fine-tune step measurement")
-    ap.add_argument("--profile-case", choices=["chain", "full", "eggroll"], default=None,
+    ap.add_argument("--profile-case", choices=["chain", "full", "eggroll", "eggroll-forward"], default=None,
                     help="small case for ncu: one bf16 tensor of 2^28 elements, 3 launches of the "
                          "-2eps pass (chain) or of the restore+accumulate+perturb pass (full); or 3 "
-                         "EGGROLL linear launches on an 8B gate_proj shape, 16 members x 1024 rows (eggroll)")
+                         "EGGROLL linear launches on an 8B gate_proj shape, 16 members x 1024 rows (eggroll); "
+                         "or one 16-member EGGROLL population chunk of the 8B model inside the NVTX range "
+                         "'egg_chunk' (eggroll-forward)")
     ap.add_argument("--eggroll-gemm", action="store_true",
                     help="time the EGGROLL population linear layer on the Llama-3-8B layer shapes")
     return ap.parse_args()
@@ -113,6 +115,24 @@ def profile_case(kind: str):
 
     from zotitan_b200 import _lib as L
     from zotitan_b200 import kernels as K
+    if kind == "eggroll-forward":
+        from zotitan_b200.eggroll import EggrollConfig, EggrollPopulation
+        from zotitan_b200.synthetic import LLAMA_8B, build_llama
+        model = build_llama(LLAMA_8B, device="cuda", seed=0, max_positions=1024)
+        pop = EggrollPopulation(model, EggrollConfig(sigma=1e-3))
+        tokens = torch.randint(0, LLAMA_8B.vocab, (4, 256), generator=torch.Generator().manual_seed(7)).cuda()
+        pop.evaluate(tokens, list(range(8)))      # warm-up chunk
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("egg_chunk")
+        a.record()
+        losses = pop.evaluate(tokens, list(range(8, 16)))
+        b.record()
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": kind, "members": 16, "ms": a.elapsed_time(b),
+                          "mean_loss": float(losses.mean()), "error": K.eggroll_take_error()}))
+        return
     n = 1 << 28
     p = (torch.randn(n, device="cuda") * 0.02).bfloat16()
     f = lambda x: float(np.float32(x))  # noqa: E731

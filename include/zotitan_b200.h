@@ -254,9 +254,25 @@ typedef struct zt_eggroll_args {
   int64_t m, n, k;        /* m % 128 == 0, n % 256 == 0, k % 64 == 0 */
   int32_t rows_per_member;  /* multiple of 128 dividing m */
   int32_t rank;           /* must be 4 */
+  int32_t xb_ready;       /* nonzero: xb already holds X B_i (zt_eggroll_xb) and is only read */
+  int32_t reserved;
 } zt_eggroll_args;
 
 ZT_API int zt_eggroll_linear(const zt_eggroll_args* args, void* stream);
+
+/* X B_s for up to three factor sets that share the activations X (q/k/v projections,
+ * or gate/up), in one read of X: xb[s][m, :] = X[m, :] B_{s,i}, i = m / rows_per_member,
+ * fp32. The outputs feed zt_eggroll_linear with xb_ready = 1. */
+typedef struct zt_eggroll_xb_args {
+  const void* x;          /* [m, k] bf16, 16-byte aligned */
+  const float* b[3];      /* per set: [members, k, 4] fp32 (entries >= n_seg unused) */
+  float* xb[3];           /* per set: [m, 4] fp32 out */
+  int64_t m, k;           /* m % 64 == 0, k % 4 == 0 */
+  int32_t n_seg;          /* 1, 2 or 3 */
+  int32_t rows_per_member;  /* multiple of 64 dividing m */
+} zt_eggroll_xb_args;
+
+ZT_API int zt_eggroll_xb(const zt_eggroll_xb_args* args, void* stream);
 
 /* Reads and clears the device-side error code of the EGGROLL kernels (0: none; nonzero:
  * a bounded wait inside the GEMM expired and that launch returned early). Synchronous. */

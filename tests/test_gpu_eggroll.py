@@ -21,7 +21,7 @@ def reference(x, w, a, b, sigma, T):
     return y
 
 
-@pytest.mark.parametrize("M,N,K,T", [(256, 512, 128, 128), (2048, 4096, 512, 512), (512, 256, 4096, 256),
+@pytest.mark.parametrize("M,N,K,T", [(256, 512, 128, 128), (2048, 4096, 512, 512), (512, 256, 4096, 256), (384, 512, 256, 128),
                                      (1024, 1024, 1024, 1024)])
 def test_eggroll_linear_matches_reference(M, N, K, T):
     from zotitan_b200 import kernels as K_
@@ -54,3 +54,42 @@ def test_eggroll_rejects_bad_shapes():
     with pytest.raises(L.ZtError, match="K % 64"):
         K_.eggroll_linear(x, w, torch.zeros(1, 256, 4, device="cuda"), torch.zeros(1, 100, 4, device="cuda"),
                           torch.zeros(1, device="cuda"), 128)
+
+
+@pytest.mark.parametrize("M,K,T,nseg", [(256, 4096, 128, 3), (1024, 14336, 512, 1), (512, 4100, 256, 2),
+                                        (128, 64, 64, 3)])
+def test_shared_xb_matches_reference_and_single_set(M, K, T, nseg):
+    """zt_eggroll_xb: X B_s for several factor sets in one read of X, within fp32
+    accumulation-order error of the fp64 product; each set's result is bit-identical to the
+    single-set pass that zt_eggroll_linear runs internally (same per-set accumulation order)."""
+    from zotitan_b200 import kernels as K_
+    g = torch.Generator(device="cuda").manual_seed(M + K + nseg)
+    members = M // T
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    bs = [torch.randn(members, K, 4, device="cuda", generator=g) for _ in range(nseg)]
+    xbs = K_.eggroll_xb(x, bs, T)
+    for b, xb in zip(bs, xbs):
+        ref = torch.cat([x[i * T:(i + 1) * T].double() @ b[i].double() for i in range(members)])
+        scale = (x.double().abs() @ b.abs().double().amax(0)).amax()
+        assert float((xb.double() - ref).abs().max()) <= 1e-5 * float(scale)
+        single = K_.eggroll_xb(x, [b], T)[0]
+        assert torch.equal(single, xb)
+
+
+def test_linear_with_precomputed_xb_is_identical():
+    from zotitan_b200 import kernels as K_
+    M, N, K, T = 512, 1024, 2048, 256
+    g = torch.Generator(device="cuda").manual_seed(11)
+    members = M // T
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    ws = [(torch.randn(N, K, device="cuda", generator=g) * 0.02).bfloat16() for _ in range(3)]
+    as_ = [torch.randn(members, N, 4, device="cuda", generator=g) for _ in range(3)]
+    bs = [torch.randn(members, K, 4, device="cuda", generator=g) for _ in range(3)]
+    sigma = torch.randn(members, device="cuda", generator=g) * 1e-2
+    xbs = K_.eggroll_xb(x, bs, T)
+    for w, a, b, xb in zip(ws, as_, bs, xbs):
+        y_shared = K_.eggroll_linear(x, w, a, None, sigma, T, xb=xb, xb_ready=True)
+        y_own = K_.eggroll_linear(x, w, a, b, sigma, T)
+        assert torch.equal(y_shared, y_own)
+    torch.cuda.synchronize()
+    assert K_.eggroll_take_error() == 0

@@ -43,7 +43,8 @@ def test_struct_layouts_match_header(lib):
     assert ctypes.sizeof(L.ZtStream) == 40
     assert ctypes.sizeof(L.ZtPlan) == 48
     assert ctypes.sizeof(L.ZtPassCfg) == 128 and L.ZtPassCfg.dev_vals.offset == 88 and L.ZtPassCfg.unit_begin.offset == 112
-    assert ctypes.sizeof(L.ZtEggrollArgs) == 88
+    assert ctypes.sizeof(L.ZtEggrollArgs) == 96 and L.ZtEggrollArgs.xb_ready.offset == 88
+    assert ctypes.sizeof(L.ZtEggrollXbArgs) == 80 and L.ZtEggrollXbArgs.m.offset == 56
     assert ctypes.sizeof(L.ZtEggrollFactorArgs) == 88 and L.ZtEggrollFactorArgs.a.offset == 56
     assert ctypes.sizeof(L.ZtEggrollNormArgs) == 72 and L.ZtEggrollNormArgs.m.offset == 40
     assert lib.zt_plan_workspace_bytes(0) == 8

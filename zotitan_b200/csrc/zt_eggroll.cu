@@ -302,62 +302,355 @@ __global__ void __launch_bounds__(kThreadsEgg, 1) eggroll_gemm_kernel(const __gr
   }
 }
 
-// XB[m, r] = sum_k X[m, k] * B_i[k, r] (fp32). One CTA per 16 rows of one member: B_i is
-// staged in shared memory transposed (4 x kXbChunk floats per chunk); each warp owns 2
-// rows and its lanes read consecutive bf16 pairs of X (coalesced 128-byte rows) and the
-// matching float2 of each B_i row (consecutive 8-byte words: no bank conflicts).
-constexpr int kXbRows = 16, kXbRowsPerWarp = 2, kXbChunk = 1024;
+// ---- the same GEMM on CTA pairs (tcgen05 cta_group::2) ------------------------------
+//
+// A cluster of two CTAs on two SMs computes a 256 x 256 tile: CTA r (r = 0, 1) loads rows
+// [r*128, r*128+128) of the X tile and rows [r*128, r*128+128) of the W tile into its own
+// shared memory, and the leader (r = 0) issues tcgen05.mma.cta_group::2 (M = 256, N = 256),
+// which reads A from each CTA's own half and B from both halves and writes each CTA's 128
+// accumulator rows into that CTA's tensor memory. Per SM this moves half the W bytes of
+// the single-CTA tile through shared memory for the same tensor work. The loads carry no
+// multicast: each CTA fetches its own halves, and the copies' byte counts land on the
+// leader's full barrier, which the leader alone arms with both CTAs' bytes. The leader's
+// commits free each stage and publish each accumulator in both CTAs (commit multicast);
+// both CTAs' epilogue warps release an accumulator on the leader's barrier.
+constexpr int kStages2 = 6;
+constexpr uint32_t kHalfRows = 128;
+constexpr uint32_t kStageA2 = kHalfRows * kBK * 2;  // 16 KB of X
+constexpr uint32_t kStageB2 = kHalfRows * kBK * 2;  // 16 KB of W (this CTA's half of the N tile)
+constexpr uint32_t kStageBytes2 = kStageA2 + kStageB2;
+constexpr size_t kSmemBytes2 = 1024 + kStages2 * kStageBytes2 + 256;
+constexpr uint32_t kIdesc2 = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
+                             ((uint32_t)(256 >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t n_clusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* tmap, uint32_t leader_bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(leader_bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc2), "r"(accumulate)
+      : "memory");
+}
+
+// arrive once on the barrier at this offset in both CTAs of the pair
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+      ::"r"(smem_u32(bar)), "h"((uint16_t)0x3) : "memory");
+}
+
+__device__ __forceinline__ void umma_commit_pair_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// Bounded wait that also raises the peer CTA's abort flag when it gives up.
+__device__ __forceinline__ bool mbar_wait_pair(uint64_t* bar, uint32_t parity, volatile int* abort, uint32_t peer_abort,
+                                               int code) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      atomicExch(&g_eggroll_error, code);
+      *abort = 1;
+      asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer_abort), "r"(1) : "memory");
+      return false;
+    }
+  }
+  return true;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
+    eggroll_gemm_pair_kernel(const __grid_constant__ EggParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t* stage_base = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages2 * kStageBytes2);
+  uint64_t* full = bars;                    // [kStages2], used in the leader
+  uint64_t* empty = bars + kStages2;        // [kStages2]
+  uint64_t* accf = bars + 2 * kStages2;     // [2]
+  uint64_t* acce = bars + 2 * kStages2 + 2; // [2], used in the leader
+  uint64_t* drain = bars + 2 * kStages2 + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages2 + 5);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages2; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&accf[b], 1); mbar_init(&acce[b], 2 * 4); }
+    mbar_init(drain, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {  // warp 0 of both CTAs allocates the pair's tensor memory
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncwarp();
+  cluster_sync_all();  // barriers of both CTAs initialised before any cross-CTA signal
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t peer_abort = peer_addr((const void*)abort, rank ^ 1u);
+
+  const int m_tiles = P.m_blocks / 2;  // 256-row tiles
+  const int n_tiles = m_tiles * P.n_blocks;
+  const int cid = (int)cluster_id_x(), ncl = (int)n_clusters_x();
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer (both CTAs)
+      int last_phase[kStages2];
+      for (int s = 0; s < kStages2; ++s) last_phase[s] = -1;
+      uint32_t it = 0;
+      for (int tile = cid; tile < n_tiles; tile += ncl) {
+        int mb, nb;
+        tile_coords(tile, m_tiles, P.n_blocks, mb, nb);
+        bool ok = true;
+        for (int kb = 0; kb < P.k_blocks; ++kb, ++it) {
+          const int s = it % kStages2;
+          const uint32_t round = it / kStages2;
+          if (!mbar_wait_pair(&empty[s], (round & 1) ^ 1, abort, peer_abort, 1)) { ok = false; break; }
+          uint8_t* sa = stage_base + s * kStageBytes2;
+          const uint32_t leader_full = peer_addr(&full[s], 0);
+          if (leader) mbar_expect_tx(&full[s], 2 * kStageBytes2);
+          tma_load_2d_pair(sa, &P.tmap_x, leader_full, kb * kBK, mb * 256 + (int)rank * 128);
+          tma_load_2d_pair(sa + kStageA2, &P.tmap_w, leader_full, kb * kBK, nb * kBN + (int)rank * 128);
+          last_phase[s] = (int)(round & 1);
+        }
+        if (!ok) break;
+      }
+      // Drain (leader): each armed phase of a full barrier completes only when both CTAs'
+      // copies for it have landed, so no copy is in flight when the pair leaves.
+      if (leader)
+        for (int s = 0; s < kStages2; ++s)
+          if (last_phase[s] >= 0) {
+            const long long t0 = clock64();
+            while (!mbar_try_wait(&full[s], (uint32_t)last_phase[s]) && clock64() - t0 < kWaitCycles) {
+            }
+          }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {  // ---- MMA issuer (leader CTA only)
+      uint32_t it = 0, tcount = 0;
+      bool ok = true, issued = false;
+      for (int tile = cid; ok && tile < n_tiles; tile += ncl, ++tcount) {
+        const uint32_t b = tcount & 1;
+        if (!mbar_wait_pair(&acce[b], ((tcount >> 1) & 1) ^ 1, abort, peer_abort, 2)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t tmem_d = tmem_base + b * kBN;
+        for (int kb = 0; kb < P.k_blocks; ++kb, ++it) {
+          const int s = it % kStages2;
+          if (!mbar_wait_pair(&full[s], (it / kStages2) & 1, abort, peer_abort, 3)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t sa = smem_u32(stage_base + s * kStageBytes2);
+          const uint32_t sb = sa + kStageA2;
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k)
+            umma_bf16_pair(tmem_d, umma_desc(sa + k * kUmmaK * 2), umma_desc(sb + k * kUmmaK * 2), (kb | k) != 0);
+          issued = true;
+          umma_commit_pair(&empty[s]);  // stage s is free in both CTAs once these MMAs have read it
+        }
+        if (!ok) break;
+        umma_commit_pair(&accf[b]);  // accumulator b is complete in both CTAs
+      }
+      if (issued) {  // wait (bounded) for every MMA issued by this thread before exit
+        umma_commit_pair_local(drain);
+        const long long t0 = clock64();
+        while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitCycles) {
+        }
+      }
+    }
+  } else {  // ---- epilogue: warps 2..5 of both CTAs, each on its own 128 rows
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t leader_acce0 = peer_addr(&acce[0], 0), leader_acce1 = peer_addr(&acce[1], 0);
+    uint32_t tcount = 0;
+    for (int tile = cid; tile < n_tiles; tile += ncl, ++tcount) {
+      int mb, nb;
+      tile_coords(tile, m_tiles, P.n_blocks, mb, nb);
+      const uint32_t b = tcount & 1;
+      const int row0 = mb * 256 + (int)rank * 128;
+      const int m = row0 + row;
+      const int member = row0 / P.rows_per_member;
+      const float4* a_tile = reinterpret_cast<const float4*>(P.a + ((size_t)member * P.n + (size_t)nb * kBN) * 4);
+      const float sg = __ldg(P.sigma + member);
+      const float4 xb = __ldg(reinterpret_cast<const float4*>(P.xb) + m);
+      const float x0 = sg * xb.x, x1 = sg * xb.y, x2 = sg * xb.z, x3 = sg * xb.w;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait_pair(&accf[b], (tcount >> 1) & 1, abort, peer_abort, 4) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      __syncwarp();
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      __nv_bfloat16* yrow = P.y + (size_t)m * P.n + (size_t)nb * kBN;
+      for (int c0 = 0; c0 < kBN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + b * kBN + c0, r);
+        uint32_t packed[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const float4 a0 = __ldg(a_tile + c0 + j);
+          const float4 a1 = __ldg(a_tile + c0 + j + 1);
+          const float v0 = __uint_as_float(r[j]) + (x0 * a0.x + x1 * a0.y + x2 * a0.z + x3 * a0.w);
+          const float v1 = __uint_as_float(r[j + 1]) + (x0 * a1.x + x1 * a1.y + x2 * a1.z + x3 * a1.w);
+          const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
+          packed[j / 2] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(yrow + c0);
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(b ? leader_acce1 : leader_acce0);  // accumulator b may be overwritten
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncwarp();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal it or read its shared memory
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (warp == 0) {
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+  }
+}
+
+// XB_s[m, r] = sum_k X[m, k] * B_{s,i}[k, r] (fp32) for up to 3 factor sets s that share
+// X (q/k/v, or gate/up): X is read once for all of them. One CTA per 64 rows of one
+// member (8 warps x 8 rows). B_{s,i} is staged in shared memory in chunks of 512 k,
+// transposed to [s][r][k], so lane l reads the float4 at k = 4l + 128j (consecutive
+// 16-byte words across the warp: no bank conflicts) and the same B values serve the
+// warp's 8 rows. X moves as 8-byte loads of 4 bf16 (256 contiguous bytes per warp and row).
+constexpr int kXbRows = 64, kXbRowsPerWarp = 8, kXbChunk = 512, kXbMaxSeg = 3;
 static_assert(kXbRows == 8 * kXbRowsPerWarp, "8 warps per CTA");
 
-__global__ void __launch_bounds__(256) eggroll_xb_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ b,
-                                                         float* __restrict__ xb, int32_t k, int32_t rows_per_member) {
-  __shared__ float bt[4][kXbChunk];
+struct XbSegs {
+  const float* b[kXbMaxSeg];  // [members, k, 4]
+  float* xb[kXbMaxSeg];       // [m, 4]
+};
+
+template <int NSEG>
+__global__ void __launch_bounds__(256, 1) eggroll_xb_kernel(const __nv_bfloat16* __restrict__ x,
+                                                            const __grid_constant__ XbSegs S, int32_t k,
+                                                            int32_t rows_per_member) {
+  __shared__ __align__(16) float bt[NSEG][4][kXbChunk];
   const int64_t row0 = (int64_t)blockIdx.x * kXbRows;
   const int member = (int)(row0 / rows_per_member);
-  const float4* bm = reinterpret_cast<const float4*>(b + (size_t)member * k * 4);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  float acc[kXbRowsPerWarp][4];
+  const int64_t wrow = row0 + warp * kXbRowsPerWarp;
+  float acc[NSEG][kXbRowsPerWarp][4];
 #pragma unroll
-  for (int i = 0; i < kXbRowsPerWarp; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  for (int s = 0; s < NSEG; ++s)
+#pragma unroll
+    for (int i = 0; i < kXbRowsPerWarp; ++i) acc[s][i][0] = acc[s][i][1] = acc[s][i][2] = acc[s][i][3] = 0.f;
   for (int kc = 0; kc < k; kc += kXbChunk) {
     const int len = (k - kc) < kXbChunk ? (k - kc) : kXbChunk;
     __syncthreads();
-    for (int t = threadIdx.x; t < len; t += 256) {
-      const float4 v = __ldg(bm + kc + t);
-      bt[0][t] = v.x; bt[1][t] = v.y; bt[2][t] = v.z; bt[3][t] = v.w;
+#pragma unroll
+    for (int s = 0; s < NSEG; ++s) {
+      const float4* bm = reinterpret_cast<const float4*>(S.b[s] + (size_t)member * k * 4) + kc;
+      for (int t = threadIdx.x; t < len; t += 256) {
+        const float4 v = __ldg(bm + t);
+        bt[s][0][t] = v.x; bt[s][1][t] = v.y; bt[s][2][t] = v.z; bt[s][3][t] = v.w;
+      }
     }
     __syncthreads();
 #pragma unroll
-    for (int i = 0; i < kXbRowsPerWarp; ++i) {
-      const __nv_bfloat16* xr = x + (row0 + warp * kXbRowsPerWarp + i) * (int64_t)k + kc;
-      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-      for (int t = 2 * lane; t < len; t += 64) {
-        const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(xr + t));
-        const float xa = __uint_as_float(w << 16), xc = __uint_as_float(w & 0xffff0000u);
-        const float2 b0 = *reinterpret_cast<const float2*>(&bt[0][t]);
-        const float2 b1 = *reinterpret_cast<const float2*>(&bt[1][t]);
-        const float2 b2 = *reinterpret_cast<const float2*>(&bt[2][t]);
-        const float2 b3 = *reinterpret_cast<const float2*>(&bt[3][t]);
-        s0 = fmaf(xa, b0.x, fmaf(xc, b0.y, s0));
-        s1 = fmaf(xa, b1.x, fmaf(xc, b1.y, s1));
-        s2 = fmaf(xa, b2.x, fmaf(xc, b2.y, s2));
-        s3 = fmaf(xa, b3.x, fmaf(xc, b3.y, s3));
+    for (int j = 0; j < kXbChunk / 128; ++j) {
+      const int t = 4 * lane + 128 * j;
+      if (t < len) {  // len % 4 == 0
+        float xf[kXbRowsPerWarp][4];
+#pragma unroll
+        for (int i = 0; i < kXbRowsPerWarp; ++i) {
+          const uint2 w = __ldcs(reinterpret_cast<const uint2*>(x + (wrow + i) * (int64_t)k + kc + t));
+          xf[i][0] = __uint_as_float(w.x << 16);
+          xf[i][1] = __uint_as_float(w.x & 0xffff0000u);
+          xf[i][2] = __uint_as_float(w.y << 16);
+          xf[i][3] = __uint_as_float(w.y & 0xffff0000u);
+        }
+#pragma unroll
+        for (int s = 0; s < NSEG; ++s)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const float4 bv = *reinterpret_cast<const float4*>(&bt[s][r][t]);
+#pragma unroll
+            for (int i = 0; i < kXbRowsPerWarp; ++i)
+              acc[s][i][r] = fmaf(xf[i][0], bv.x, fmaf(xf[i][1], bv.y, fmaf(xf[i][2], bv.z, fmaf(xf[i][3], bv.w, acc[s][i][r]))));
+          }
       }
-      acc[i][0] += s0; acc[i][1] += s1; acc[i][2] += s2; acc[i][3] += s3;
     }
   }
 #pragma unroll
-  for (int i = 0; i < kXbRowsPerWarp; ++i) {
+  for (int s = 0; s < NSEG; ++s)
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      acc[i][0] += __shfl_xor_sync(0xffffffffu, acc[i][0], o);
-      acc[i][1] += __shfl_xor_sync(0xffffffffu, acc[i][1], o);
-      acc[i][2] += __shfl_xor_sync(0xffffffffu, acc[i][2], o);
-      acc[i][3] += __shfl_xor_sync(0xffffffffu, acc[i][3], o);
+    for (int i = 0; i < kXbRowsPerWarp; ++i) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[s][i][r] += __shfl_xor_sync(0xffffffffu, acc[s][i][r], o);
+      if (lane == 0)
+        reinterpret_cast<float4*>(S.xb[s])[wrow + i] = make_float4(acc[s][i][0], acc[s][i][1], acc[s][i][2], acc[s][i][3]);
     }
-    if (lane == 0)
-      reinterpret_cast<float4*>(xb)[row0 + warp * kXbRowsPerWarp + i] = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+}
+
+int launch_xb(const void* x, const float* const* b, float* const* xb, int nseg, int64_t m, int64_t k,
+              int32_t rows_per_member, cudaStream_t s) {
+  XbSegs S{};
+  for (int i = 0; i < nseg; ++i) {
+    S.b[i] = b[i];
+    S.xb[i] = xb[i];
   }
+  const unsigned grid = (unsigned)(m / kXbRows);
+  const __nv_bfloat16* xp = static_cast<const __nv_bfloat16*>(x);
+  switch (nseg) {
+    case 1: eggroll_xb_kernel<1><<<grid, 256, 0, s>>>(xp, S, (int32_t)k, rows_per_member); break;
+    case 2: eggroll_xb_kernel<2><<<grid, 256, 0, s>>>(xp, S, (int32_t)k, rows_per_member); break;
+    default: eggroll_xb_kernel<3><<<grid, 256, 0, s>>>(xp, S, (int32_t)k, rows_per_member); break;
+  }
+  return zt::check_cuda(cudaGetLastError(), "eggroll xb launch");
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
@@ -403,7 +696,7 @@ int zt_eggroll_linear(const zt_eggroll_args* args, void* stream) {
   zt::clear_error();
   if (!args) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: null args");
   const zt_eggroll_args& A = *args;
-  if (!A.x || !A.w || !A.a || !A.b || !A.sigma || !A.xb || !A.y)
+  if (!A.x || !A.w || !A.a || (!A.b && !A.xb_ready) || !A.sigma || !A.xb || !A.y)
     return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: null pointer");
   if (A.rank != 4) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: rank must be 4");
   if (A.m <= 0 || A.n <= 0 || A.k <= 0) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: empty shape");
@@ -417,9 +710,11 @@ int zt_eggroll_linear(const zt_eggroll_args* args, void* stream) {
     if (((uintptr_t)p & 15) != 0) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: pointers must be 16-byte aligned");
   EncodeFn enc = nullptr;
   if (int rc = get_encode(&enc)) return rc;
+  // CTA pairs (cta_group::2) whenever the rows split into 256-row tiles
+  const bool pair = (A.m % 256) == 0;
   EggParams P;
   if (int rc = make_map(enc, &P.tmap_x, A.x, (uint64_t)A.m, (uint64_t)A.k, kBM)) return rc;
-  if (int rc = make_map(enc, &P.tmap_w, A.w, (uint64_t)A.n, (uint64_t)A.k, kBN)) return rc;
+  if (int rc = make_map(enc, &P.tmap_w, A.w, (uint64_t)A.n, (uint64_t)A.k, pair ? kHalfRows : kBN)) return rc;
   P.a = A.a;
   P.sigma = A.sigma;
   P.xb = A.xb;
@@ -430,10 +725,11 @@ int zt_eggroll_linear(const zt_eggroll_args* args, void* stream) {
   P.n = (int32_t)A.n;
   P.rows_per_member = A.rows_per_member;
   cudaStream_t s = zt::as_stream(stream);
-  // m % 128 == 0 and rows_per_member % 128 == 0, so each 16-row block lies in one member
-  eggroll_xb_kernel<<<(unsigned)(A.m / kXbRows), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(A.x), A.b, A.xb,
-                                                             (int32_t)A.k, A.rows_per_member);
-  if (int rc = zt::check_cuda(cudaGetLastError(), "zt_eggroll_linear: xb launch")) return rc;
+  if (!A.xb_ready) {  // m % 128 == 0 and rows_per_member % 128 == 0: each 64-row block lies in one member
+    const float* bb[1] = {A.b};
+    float* xx[1] = {A.xb};
+    if (int rc = launch_xb(A.x, bb, xx, 1, A.m, A.k, A.rows_per_member, s)) return rc;
+  }
   {  // the dynamic shared-memory limit is a per-device function attribute
     static std::mutex mu;
     static bool done[64] = {false};
@@ -445,13 +741,62 @@ int zt_eggroll_linear(const zt_eggroll_args* args, void* stream) {
       if (int rc = zt::check_cuda(cudaFuncSetAttribute(eggroll_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                        (int)kSmemBytes), "zt_eggroll_linear: shared memory attribute"))
         return rc;
+      if (int rc = zt::check_cuda(cudaFuncSetAttribute(eggroll_gemm_pair_kernel,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes2),
+                                  "zt_eggroll_linear: shared memory attribute (pair)"))
+        return rc;
       done[dev] = true;
     }
+  }
+  if (pair) {
+    static std::mutex cmu;
+    static int max_clusters_dev[64] = {0};
+    int dev = 0;
+    if (int rc = zt::check_cuda(cudaGetDevice(&dev), "zt_eggroll_linear: cudaGetDevice")) return rc;
+    int max_clusters = 0;
+    {
+      std::lock_guard<std::mutex> lock(cmu);
+      if (max_clusters_dev[dev] == 0) {  // pairs that fit on the GPU at once (GPC boundaries)
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (unsigned)(zt::sm_count() / 2));
+        cfg.blockDim = dim3(kThreadsEgg);
+        cfg.dynamicSmemBytes = kSmemBytes2;
+        int n = 0;
+        if (int rc = zt::check_cuda(cudaOccupancyMaxActiveClusters(&n, eggroll_gemm_pair_kernel, &cfg),
+                                    "zt_eggroll_linear: cudaOccupancyMaxActiveClusters"))
+          return rc;
+        if (n <= 0) return zt::set_error(ZT_ERR_CUDA, "zt_eggroll_linear: no CTA pair fits on this GPU");
+        max_clusters_dev[dev] = n;
+      }
+      max_clusters = max_clusters_dev[dev];
+    }
+    const int tiles = (P.m_blocks / 2) * P.n_blocks;
+    const int clusters = tiles < max_clusters ? tiles : max_clusters;
+    eggroll_gemm_pair_kernel<<<2 * clusters, kThreadsEgg, kSmemBytes2, s>>>(P);
+    return zt::check_cuda(cudaGetLastError(), "zt_eggroll_linear: gemm launch (pair)");
   }
   const int tiles = P.m_blocks * P.n_blocks;
   const int grid = tiles < zt::sm_count() ? tiles : zt::sm_count();
   eggroll_gemm_kernel<<<grid, kThreadsEgg, kSmemBytes, s>>>(P);
   return zt::check_cuda(cudaGetLastError(), "zt_eggroll_linear: gemm launch");
+}
+
+int zt_eggroll_xb(const zt_eggroll_xb_args* args, void* stream) {
+  zt::clear_error();
+  if (!args) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: null args");
+  const zt_eggroll_xb_args& A = *args;
+  if (A.n_seg < 1 || A.n_seg > kXbMaxSeg) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: n_seg must be 1, 2 or 3");
+  if (A.m <= 0 || A.k <= 0) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: empty shape");
+  if (A.m % kXbRows || A.k % 4) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: need m % 64 == 0 and k % 4 == 0");
+  if (A.rows_per_member <= 0 || A.rows_per_member % kXbRows || A.m % A.rows_per_member)
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: rows_per_member must divide m and be a multiple of 64");
+  if (A.m > (int64_t)INT32_MAX * kXbRows || A.k > (int64_t)INT32_MAX)
+    return zt::set_error(ZT_ERR_LIMIT, "zt_eggroll_xb: dimension too large");
+  if (!A.x || ((uintptr_t)A.x & 15)) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: x null or not 16-byte aligned");
+  for (int i = 0; i < A.n_seg; ++i)
+    if (!A.b[i] || !A.xb[i] || ((uintptr_t)A.b[i] & 15) || ((uintptr_t)A.xb[i] & 15))
+      return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: b/xb null or not 16-byte aligned");
+  return launch_xb(A.x, A.b, A.xb, A.n_seg, A.m, A.k, A.rows_per_member, zt::as_stream(stream));
 }
 
 int zt_eggroll_take_error(int32_t* code) {

@@ -81,13 +81,27 @@ class PopLinear(nn.Module):
         self.weight = base.weight
         self.idx, self.pop = idx, pop
 
-    def forward(self, x):
+    def factors(self, device):
+        out_f, in_f = self.weight.shape
+        return self.pop.low_rank(self.idx, out_f, in_f, device, self.weight.dtype)
+
+    def forward(self, x, fac=None, xb=None):
+        """fac = (A, B, scale) and xb = X B from a shared zt_eggroll_xb call, or None."""
         shp = x.shape
         x2 = x.reshape(-1, shp[-1]).contiguous()
-        out_f, in_f = self.weight.shape
-        A, B, sig = self.pop.low_rank(self.idx, out_f, in_f, x.device, self.weight.dtype)
-        y = K.eggroll_linear(x2, self.weight.data, A, B, sig, self.pop.rows_per_member)
+        out_f = self.weight.shape[0]
+        A, B, sig = fac if fac is not None else self.factors(x.device)
+        y = K.eggroll_linear(x2, self.weight.data, A, B, sig, self.pop.rows_per_member, xb=xb,
+                             xb_ready=xb is not None)
         return y.view(*shp[:-1], out_f)
+
+
+def _shared_input(x, linears, pop):
+    """Factors of every linear reading x and their X B in one pass over x."""
+    x2 = x.reshape(-1, x.shape[-1]).contiguous()
+    facs = [lin.factors(x.device) for lin in linears]
+    xbs = K.eggroll_xb(x2, [f[1] for f in facs], pop.rows_per_member)
+    return x2, facs, xbs
 
 
 class PopRMSNorm(nn.Module):
@@ -122,9 +136,12 @@ class PopAttention(nn.Module):
         from transformers.models.llama.modeling_llama import ALL_ATTENTION_FUNCTIONS, eager_attention_forward
         bsz, T, _ = hidden_states.shape
         hd = self.head_dim
-        q = self.q_proj(hidden_states)
-        k = self.k_proj(hidden_states)
-        v = self.v_proj(hidden_states)
+        projs = (self.q_proj, self.k_proj, self.v_proj)
+        if all(isinstance(p, PopLinear) for p in projs):
+            x2, facs, xbs = _shared_input(hidden_states, projs, projs[0].pop)
+            q, k, v = (p(x2, f, xb).view(bsz, T, -1) for p, f, xb in zip(projs, facs, xbs))
+        else:
+            q, k, v = (p(hidden_states) for p in projs)
         cos, sin = position_embeddings
         if cos.shape[0] != 1:
             raise NotImplementedError("per-sequence position ids")
@@ -148,7 +165,13 @@ class PopMLP(nn.Module):
         self.gate_proj, self.up_proj, self.down_proj = gate_proj, up_proj, down_proj
 
     def forward(self, x):
-        return self.down_proj(K.eggroll_swiglu(self.gate_proj(x), self.up_proj(x)))
+        projs = (self.gate_proj, self.up_proj)
+        if all(isinstance(p, PopLinear) for p in projs):
+            x2, facs, xbs = _shared_input(x, projs, projs[0].pop)
+            g, u = (p(x2, f, xb).view(*x.shape[:-1], -1) for p, f, xb in zip(projs, facs, xbs))
+        else:
+            g, u = (p(x) for p in projs)
+        return self.down_proj(K.eggroll_swiglu(g, u))
 
 
 class PopEmbedding(nn.Module):

@@ -228,36 +228,67 @@ class ParamTable:
                                      _stream_ptr(self.device)), "zt_pass")
 
 
-def eggroll_linear(x: torch.Tensor, w: torch.Tensor, a: torch.Tensor, b: torch.Tensor, sigma: torch.Tensor,
-                   rows_per_member: int, out: torch.Tensor | None = None, xb: torch.Tensor | None = None) -> torch.Tensor:
+def eggroll_linear(x: torch.Tensor, w: torch.Tensor, a: torch.Tensor, b: torch.Tensor | None, sigma: torch.Tensor,
+                   rows_per_member: int, out: torch.Tensor | None = None, xb: torch.Tensor | None = None,
+                   xb_ready: bool = False) -> torch.Tensor:
     """EGGROLL population linear layer (zt_eggroll_linear):
     Y = X W^T + sigma_i (X B_i) A_i^T for the rows of member i.
 
     x [M, K] bf16, w [N, K] bf16, a [members, N, 4] fp32, b [members, K, 4] fp32,
     sigma [members] fp32; returns Y [M, N] bf16. M % 128, N % 256, K % 64 must be 0 and
-    rows_per_member a multiple of 128 dividing M."""
-    for t, name in ((x, "x"), (w, "w"), (a, "a"), (b, "b"), (sigma, "sigma")):
+    rows_per_member a multiple of 128 dividing M. With xb_ready, xb already holds X B_i
+    (from eggroll_xb) and b may be None."""
+    if xb_ready and xb is None:
+        raise ValueError("xb_ready needs xb")
+    named = [(x, "x"), (w, "w"), (a, "a"), (sigma, "sigma")] + ([] if xb_ready else [(b, "b")])
+    for t, name in named:
         _check_cuda(t, name)
         if not t.is_contiguous():
             raise ValueError(f"{name} must be contiguous")
     if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
         raise ValueError("x and w must be bf16")
-    if a.dtype != torch.float32 or b.dtype != torch.float32 or sigma.dtype != torch.float32:
+    if a.dtype != torch.float32 or sigma.dtype != torch.float32 or (b is not None and b.dtype != torch.float32):
         raise ValueError("a, b and sigma must be fp32")
     M, K = x.shape
     N = w.shape[0]
     members = M // rows_per_member
-    if w.shape[1] != K or a.shape != (members, N, 4) or b.shape != (members, K, 4) or sigma.shape != (members,):
+    if w.shape[1] != K or a.shape != (members, N, 4) or sigma.shape != (members,):
+        raise ValueError("inconsistent shapes")
+    if b is not None and b.shape != (members, K, 4):
         raise ValueError("inconsistent shapes")
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
     if xb is None:
         xb = torch.empty((M, 4), dtype=torch.float32, device=x.device)
-    args = L.ZtEggrollArgs(x.data_ptr(), w.data_ptr(), a.data_ptr(), b.data_ptr(), sigma.data_ptr(), xb.data_ptr(),
-                           out.data_ptr(), M, N, K, rows_per_member, 4)
+    args = L.ZtEggrollArgs(x.data_ptr(), w.data_ptr(), a.data_ptr(), b.data_ptr() if b is not None else None,
+                           sigma.data_ptr(), xb.data_ptr(), out.data_ptr(), M, N, K, rows_per_member, 4,
+                           1 if xb_ready else 0, 0)
     with torch.cuda.device(x.device):
         L.check(L.load().zt_eggroll_linear(ctypes.byref(args), _stream_ptr(x.device)), "zt_eggroll_linear")
     return out
+
+
+def eggroll_xb(x: torch.Tensor, bs: list, rows_per_member: int) -> list:
+    """X B_s for 1-3 factor sets sharing x [M, K] bf16 (zt_eggroll_xb): returns one
+    [M, 4] fp32 tensor per b in bs ([members, K, 4] fp32 each)."""
+    if not 1 <= len(bs) <= 3:
+        raise ValueError("one to three factor sets")
+    _check_cuda(x, "x")
+    if x.dtype != torch.bfloat16 or not x.is_contiguous() or x.dim() != 2:
+        raise ValueError("x must be a contiguous bf16 matrix")
+    M, K = x.shape
+    for b in bs:
+        _check_cuda(b, "b")
+        if b.dtype != torch.float32 or not b.is_contiguous() or b.shape != (M // rows_per_member, K, 4):
+            raise ValueError("each b must be a contiguous fp32 [members, K, 4] tensor")
+    xbs = [torch.empty((M, 4), dtype=torch.float32, device=x.device) for _ in bs]
+    bp = [b.data_ptr() for b in bs] + [0] * (3 - len(bs))
+    xp = [t.data_ptr() for t in xbs] + [0] * (3 - len(bs))
+    args = L.ZtEggrollXbArgs(x.data_ptr(), (ctypes.c_void_p * 3)(*bp), (ctypes.c_void_p * 3)(*xp), M, K, len(bs),
+                             rows_per_member)
+    with torch.cuda.device(x.device):
+        L.check(L.load().zt_eggroll_xb(ctypes.byref(args), _stream_ptr(x.device)), "zt_eggroll_xb")
+    return xbs
 
 
 def eggroll_take_error() -> int:
