@@ -57,7 +57,8 @@ __device__ int g_eggroll_error = 0;
 
 struct EggParams {
   CUtensorMap tmap_x;  // X [M, K], box {64, 128}
-  CUtensorMap tmap_w;  // W [N, K], box {64, 256}
+  CUtensorMap tmap_w;  // W [N, K], box {64, 256} (single CTA) or {64, 128} (CTA pair)
+  CUtensorMap tmap_y;  // Y [M, N], box {32, 32}, 64-byte swizzle (CTA-pair epilogue stores)
   const float* a;      // [members, N, 4]
   const float* sigma;  // [members]
   const float* xb;     // [M, 4]
@@ -319,7 +320,9 @@ constexpr uint32_t kHalfRows = 128;
 constexpr uint32_t kStageA2 = kHalfRows * kBK * 2;  // 16 KB of X
 constexpr uint32_t kStageB2 = kHalfRows * kBK * 2;  // 16 KB of W (this CTA's half of the N tile)
 constexpr uint32_t kStageBytes2 = kStageA2 + kStageB2;
-constexpr size_t kSmemBytes2 = 1024 + kStages2 * kStageBytes2 + 256;
+constexpr uint32_t kOutChunk = 32 * 32 * 2;           // one warp's 32 x 32 bf16 output chunk
+constexpr uint32_t kOutBytes2 = 4 * 2 * kOutChunk;     // 4 epilogue warps x 2 buffers
+constexpr size_t kSmemBytes2 = 1024 + kStages2 * kStageBytes2 + kOutBytes2 + 256;
 constexpr uint32_t kIdesc2 = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
                              ((uint32_t)(256 >> 4) << 24);
 
@@ -405,7 +408,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t* stage_base = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages2 * kStageBytes2);
+  uint8_t* out_base = smem + kStages2 * kStageBytes2;  // 1024-byte aligned
+  uint64_t* bars = reinterpret_cast<uint64_t*>(out_base + kOutBytes2);
   uint64_t* full = bars;                    // [kStages2], used in the leader
   uint64_t* empty = bars + kStages2;        // [kStages2]
   uint64_t* accf = bars + 2 * kStages2;     // [2]
@@ -503,10 +507,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
       }
     }
   } else {  // ---- epilogue: warps 2..5 of both CTAs, each on its own 128 rows
+    // Each warp turns its 32 rows x 32 columns of the accumulator into bf16 in a shared
+    // buffer (64-byte swizzle: conflict-free 16-byte writes) and one lane stores the chunk
+    // with a TMA bulk tensor store; two buffers per warp let a store drain while the next
+    // chunk is converted.
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const uint32_t leader_acce0 = peer_addr(&acce[0], 0), leader_acce1 = peer_addr(&acce[1], 0);
-    uint32_t tcount = 0;
+    uint8_t* obuf = out_base + q * 2 * kOutChunk;
+    uint32_t tcount = 0, chunk = 0;
     for (int tile = cid; tile < n_tiles; tile += ncl, ++tcount) {
       int mb, nb;
       tile_coords(tile, m_tiles, P.n_blocks, mb, nb);
@@ -524,8 +533,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
       if (!ok) break;
       __syncwarp();
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      __nv_bfloat16* yrow = P.y + (size_t)m * P.n + (size_t)nb * kBN;
-      for (int c0 = 0; c0 < kBN; c0 += 32) {
+      for (int c0 = 0; c0 < kBN; c0 += 32, ++chunk) {
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + b * kBN + c0, r);
         uint32_t packed[16];
@@ -538,15 +546,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
           const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
           packed[j / 2] = *reinterpret_cast<const uint32_t*>(&h);
         }
-        uint4* dst = reinterpret_cast<uint4*>(yrow + c0);
+        uint8_t* buf = obuf + (chunk & 1) * kOutChunk;
+        if (chunk >= 2) {  // the store issued from this buffer two chunks ago has read it
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          __syncwarp();
+        }
 #pragma unroll
-        for (int v = 0; v < 4; ++v)
-          dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+        for (int v = 0; v < 4; ++v) {  // 16-byte piece v of this row, 64-byte swizzle
+          const uint32_t off = (uint32_t)lane * 64 + (uint32_t)((v ^ ((lane >> 1) & 3)) * 16);
+          *reinterpret_cast<uint4*>(buf + off) =
+              make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          asm volatile(
+              "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];\n\t"
+              "cp.async.bulk.commit_group;"
+              ::"l"(reinterpret_cast<uint64_t>(&P.tmap_y)), "r"(nb * kBN + c0), "r"(row0 + q * 32), "r"(smem_u32(buf))
+              : "memory");
+        }
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(b ? leader_acce1 : leader_acce0);  // accumulator b may be overwritten
     }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // all stores complete
+    __syncwarp();
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncwarp();
@@ -715,6 +741,15 @@ int zt_eggroll_linear(const zt_eggroll_args* args, void* stream) {
   EggParams P;
   if (int rc = make_map(enc, &P.tmap_x, A.x, (uint64_t)A.m, (uint64_t)A.k, kBM)) return rc;
   if (int rc = make_map(enc, &P.tmap_w, A.w, (uint64_t)A.n, (uint64_t)A.k, pair ? kHalfRows : kBN)) return rc;
+  if (pair) {
+    const cuuint64_t dims[2] = {(cuuint64_t)A.n, (cuuint64_t)A.m};
+    const cuuint64_t strides[1] = {(cuuint64_t)A.n * 2};
+    const cuuint32_t box[2] = {32, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&P.tmap_y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A.y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return zt::set_error(ZT_ERR_CUDA, "zt_eggroll_linear: cuTensorMapEncodeTiled (output) failed");
+  }
   P.a = A.a;
   P.sigma = A.sigma;
   P.xb = A.xb;
