@@ -274,6 +274,30 @@ typedef struct zt_eggroll_xb_args {
 
 ZT_API int zt_eggroll_xb(const zt_eggroll_xb_args* args, void* stream);
 
+/* The Llama MLP's gated product of a population chunk in one GEMM:
+ *   G = X W_gate^T + sigma_gate_i (X B_gate,i) A_gate,i^T,  U likewise with the up factors,
+ *   y = bf16(bf16(silu(bf16(G))) * bf16(U)),  silu(g) = g / (1 + exp(-g)),
+ * the rounding torch applies to act_fn(gate_proj(x)) * up_proj(x) in bf16. G and U are
+ * never written: a pair of CTAs computes both for the same 128 features and the epilogue
+ * combines them. xb_gate / xb_up come from zt_eggroll_xb (one pass over X for both). */
+typedef struct zt_eggroll_gated_args {
+  const void* x;          /* [m, k] bf16 */
+  const void* w_gate;     /* [n, k] bf16 */
+  const void* w_up;       /* [n, k] bf16 */
+  const float* a_gate;    /* [members, n, 4] */
+  const float* a_up;      /* [members, n, 4] */
+  const float* sigma_gate;  /* [members] */
+  const float* sigma_up;    /* [members] */
+  const float* xb_gate;   /* [m, 4] */
+  const float* xb_up;     /* [m, 4] */
+  void* y;                /* [m, n] bf16 out */
+  int64_t m, n, k;        /* m % 256 == 0, n % 128 == 0, k % 64 == 0 */
+  int32_t rows_per_member;  /* multiple of 128 dividing m */
+  int32_t rank;           /* must be 4 */
+} zt_eggroll_gated_args;
+
+ZT_API int zt_eggroll_gated(const zt_eggroll_gated_args* args, void* stream);
+
 /* Reads and clears the device-side error code of the EGGROLL kernels (0: none; nonzero:
  * a bounded wait inside the GEMM expired and that launch returned early). Synchronous. */
 ZT_API int zt_eggroll_take_error(int32_t* code);

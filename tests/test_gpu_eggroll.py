@@ -93,3 +93,41 @@ def test_linear_with_precomputed_xb_is_identical():
         assert torch.equal(y_shared, y_own)
     torch.cuda.synchronize()
     assert K_.eggroll_take_error() == 0
+
+
+@pytest.mark.parametrize("M,N,K,T", [(512, 256, 512, 256), (1024, 1408, 1024, 512)])
+def test_gated_pair_matches_unfused_path(M, N, K, T):
+    """zt_eggroll_gated (gate and up in one pair GEMM, SwiGLU in the epilogue) against two
+    EGGROLL linears and zt_eggroll_swiglu: the same rounding steps, so outputs agree to the
+    bit except where the two GEMMs' accumulation orders differ (at most one bf16 step)."""
+    from zotitan_b200 import kernels as K_
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    members = M // T
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    wg = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
+    wu = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
+    fg = (torch.randn(members, N, 4, device="cuda", generator=g), torch.randn(members, K, 4, device="cuda", generator=g),
+          torch.randn(members, device="cuda", generator=g) * 1e-2)
+    fu = (torch.randn(members, N, 4, device="cuda", generator=g), torch.randn(members, K, 4, device="cuda", generator=g),
+          torch.randn(members, device="cuda", generator=g) * 1e-2)
+    xbg, xbu = K_.eggroll_xb(x, [fg[1], fu[1]], T)
+    y = K_.eggroll_gated(x, wg, wu, fg, fu, xbg, xbu, T)
+    if N % 256 == 0:
+        gate = K_.eggroll_linear(x, wg, fg[0], None, fg[2], T, xb=xbg, xb_ready=True)
+        up = K_.eggroll_linear(x, wu, fu[0], None, fu[2], T, xb=xbu, xb_ready=True)
+        want = K_.eggroll_swiglu(gate, up)
+    else:  # torch evaluation of the same rounding chain
+        def lin(w, f, xb):
+            y_ = x.float() @ w.float().T
+            for i in range(members):
+                r = slice(i * T, (i + 1) * T)
+                y_[r] += f[2][i] * (xb[r] @ f[0][i].T)
+            return y_.bfloat16()
+        want = K_.eggroll_swiglu(lin(wg, fg, xbg), lin(wu, fu, xbu))
+    torch.cuda.synchronize()
+    assert K_.eggroll_take_error() == 0
+    d = (y.float() - want.float()).abs()
+    tol = 2 ** -7 * want.float().abs() + 1e-6 if N % 256 == 0 else 2 ** -6 * want.float().abs() + 1e-3
+    assert bool((d <= tol).all()), float(d.max())
+    if N % 256 == 0:
+        assert float((d == 0).float().mean()) >= 0.999

@@ -59,6 +59,10 @@ struct EggParams {
   CUtensorMap tmap_x;  // X [M, K], box {64, 128}
   CUtensorMap tmap_w;  // W [N, K], box {64, 256} (single CTA) or {64, 128} (CTA pair)
   CUtensorMap tmap_y;  // Y [M, N], box {32, 32}, 64-byte swizzle (CTA-pair epilogue stores)
+  CUtensorMap tmap_w2; // gated pair: W_up [N, K], box {64, 128} (tmap_w holds W_gate)
+  const float* a2;     // gated: A of the up projection [members, N, 4]
+  const float* sigma2; // gated: [members]
+  const float* xb2;    // gated: X B_up [M, 4]
   const float* a;      // [members, N, 4]
   const float* sigma;  // [members]
   const float* xb;     // [M, 4]
@@ -403,6 +407,12 @@ __device__ __forceinline__ bool mbar_wait_pair(uint64_t* bar, uint32_t parity, v
   return true;
 }
 
+// GATED: the pair computes the Llama MLP's gate and up projections of the same 128
+// output features at once: CTA 0 stages W_gate rows and CTA 1 W_up rows, so accumulator
+// columns 0..127 hold G and 128..255 hold U for features [nb*128, nb*128+128), and the
+// epilogue writes bf16(bf16(silu(bf16(G))) * bf16(U)) -- the rounding torch applies to
+// act_fn(gate_proj(x)) * up_proj(x) -- without G or U ever reaching global memory.
+template <bool GATED>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
     eggroll_gemm_pair_kernel(const __grid_constant__ EggParams P) {
   extern __shared__ uint8_t smem_raw[];
@@ -460,7 +470,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
           const uint32_t leader_full = peer_addr(&full[s], 0);
           if (leader) mbar_expect_tx(&full[s], 2 * kStageBytes2);
           tma_load_2d_pair(sa, &P.tmap_x, leader_full, kb * kBK, mb * 256 + (int)rank * 128);
-          tma_load_2d_pair(sa + kStageA2, &P.tmap_w, leader_full, kb * kBK, nb * kBN + (int)rank * 128);
+          if (GATED)
+            tma_load_2d_pair(sa + kStageA2, rank ? &P.tmap_w2 : &P.tmap_w, leader_full, kb * kBK, nb * 128);
+          else
+            tma_load_2d_pair(sa + kStageA2, &P.tmap_w, leader_full, kb * kBK, nb * kBN + (int)rank * 128);
           last_phase[s] = (int)(round & 1);
         }
         if (!ok) break;
@@ -523,7 +536,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
       const int row0 = mb * 256 + (int)rank * 128;
       const int m = row0 + row;
       const int member = row0 / P.rows_per_member;
-      const float4* a_tile = reinterpret_cast<const float4*>(P.a + ((size_t)member * P.n + (size_t)nb * kBN) * 4);
+      const int col0 = nb * (GATED ? 128 : kBN);  // first output column of the tile
+      const float4* a_tile = reinterpret_cast<const float4*>(P.a + ((size_t)member * P.n + (size_t)col0) * 4);
       const float sg = __ldg(P.sigma + member);
       const float4 xb = __ldg(reinterpret_cast<const float4*>(P.xb) + m);
       const float x0 = sg * xb.x, x1 = sg * xb.y, x2 = sg * xb.z, x3 = sg * xb.w;
@@ -533,18 +547,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
       if (!ok) break;
       __syncwarp();
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      for (int c0 = 0; c0 < kBN; c0 += 32, ++chunk) {
+      const int out_cols = GATED ? 128 : kBN;
+      const float4* a2_tile = nullptr;
+      float u0 = 0.f, u1 = 0.f, u2 = 0.f, u3 = 0.f;
+      if (GATED) {
+        a2_tile = reinterpret_cast<const float4*>(P.a2 + ((size_t)member * P.n + (size_t)nb * 128) * 4);
+        const float sg2 = __ldg(P.sigma2 + member);
+        const float4 xb2 = __ldg(reinterpret_cast<const float4*>(P.xb2) + m);
+        u0 = sg2 * xb2.x; u1 = sg2 * xb2.y; u2 = sg2 * xb2.z; u3 = sg2 * xb2.w;
+      }
+      for (int c0 = 0; c0 < out_cols; c0 += 32, ++chunk) {
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + b * kBN + c0, r);
         uint32_t packed[16];
+        if (GATED) {
+          uint32_t ru[32];
+          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + b * kBN + 128 + c0, ru);
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const float4 a0 = __ldg(a_tile + c0 + j);
-          const float4 a1 = __ldg(a_tile + c0 + j + 1);
-          const float v0 = __uint_as_float(r[j]) + (x0 * a0.x + x1 * a0.y + x2 * a0.z + x3 * a0.w);
-          const float v1 = __uint_as_float(r[j + 1]) + (x0 * a1.x + x1 * a1.y + x2 * a1.z + x3 * a1.w);
-          const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
-          packed[j / 2] = *reinterpret_cast<const uint32_t*>(&h);
+          for (int j = 0; j < 32; j += 2) {
+            float h[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const float4 ag = __ldg(a_tile + c0 + j + e);
+              const float4 au = __ldg(a2_tile + c0 + j + e);
+              const float g = __bfloat162float(__float2bfloat16_rn(
+                  __uint_as_float(r[j + e]) + (x0 * ag.x + x1 * ag.y + x2 * ag.z + x3 * ag.w)));
+              const float u = __bfloat162float(__float2bfloat16_rn(
+                  __uint_as_float(ru[j + e]) + (u0 * au.x + u1 * au.y + u2 * au.z + u3 * au.w)));
+              h[e] = __bfloat162float(__float2bfloat16_rn(g / (1.0f + expf(-g)))) * u;
+            }
+            const __nv_bfloat162 hv = __floats2bfloat162_rn(h[0], h[1]);
+            packed[j / 2] = *reinterpret_cast<const uint32_t*>(&hv);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const float4 a0 = __ldg(a_tile + c0 + j);
+            const float4 a1 = __ldg(a_tile + c0 + j + 1);
+            const float v0 = __uint_as_float(r[j]) + (x0 * a0.x + x1 * a0.y + x2 * a0.z + x3 * a0.w);
+            const float v1 = __uint_as_float(r[j + 1]) + (x0 * a1.x + x1 * a1.y + x2 * a1.z + x3 * a1.w);
+            const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
+            packed[j / 2] = *reinterpret_cast<const uint32_t*>(&h);
+          }
         }
         uint8_t* buf = obuf + (chunk & 1) * kOutChunk;
         if (chunk >= 2) {  // the store issued from this buffer two chunks ago has read it
@@ -563,7 +607,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
           asm volatile(
               "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];\n\t"
               "cp.async.bulk.commit_group;"
-              ::"l"(reinterpret_cast<uint64_t>(&P.tmap_y)), "r"(nb * kBN + c0), "r"(row0 + q * 32), "r"(smem_u32(buf))
+              ::"l"(reinterpret_cast<uint64_t>(&P.tmap_y)), "r"(col0 + c0), "r"(row0 + q * 32), "r"(smem_u32(buf))
               : "memory");
         }
       }
@@ -714,6 +758,65 @@ int make_map(EncodeFn enc, CUtensorMap* map, const void* base, uint64_t rows, ui
   return ZT_OK;
 }
 
+int make_out_map(EncodeFn enc, CUtensorMap* map, void* base, uint64_t rows, uint64_t cols) {
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {32, 32};
+  const cuuint32_t estr[2] = {1, 1};
+  if (enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return zt::set_error(ZT_ERR_CUDA, "eggroll: cuTensorMapEncodeTiled (output) failed");
+  return ZT_OK;
+}
+
+// The dynamic shared-memory limits are per-device function attributes; the number of CTA
+// pairs that fit at once (GPC boundaries) is queried once per device.
+int g_max_pairs[64] = {0};
+
+int prepare_kernels() {
+  static std::mutex mu;
+  static bool done[64] = {false};
+  int dev = 0;
+  if (int rc = zt::check_cuda(cudaGetDevice(&dev), "eggroll: cudaGetDevice")) return rc;
+  if (dev < 0 || dev >= 64) return zt::set_error(ZT_ERR_LIMIT, "eggroll: device ordinal >= 64");
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[dev]) return ZT_OK;
+  if (int rc = zt::check_cuda(cudaFuncSetAttribute(eggroll_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)kSmemBytes), "eggroll: shared memory attribute"))
+    return rc;
+  if (int rc = zt::check_cuda(cudaFuncSetAttribute(eggroll_gemm_pair_kernel<false>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes2),
+                              "eggroll: shared memory attribute (pair)"))
+    return rc;
+  if (int rc = zt::check_cuda(cudaFuncSetAttribute(eggroll_gemm_pair_kernel<true>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes2),
+                              "eggroll: shared memory attribute (gated pair)"))
+    return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * (unsigned)(zt::sm_count() / 2));
+  cfg.blockDim = dim3(kThreadsEgg);
+  cfg.dynamicSmemBytes = kSmemBytes2;
+  int n = 0;
+  if (int rc = zt::check_cuda(cudaOccupancyMaxActiveClusters(&n, eggroll_gemm_pair_kernel<false>, &cfg),
+                              "eggroll: cudaOccupancyMaxActiveClusters"))
+    return rc;
+  if (n <= 0) return zt::set_error(ZT_ERR_CUDA, "eggroll: no CTA pair fits on this GPU");
+  g_max_pairs[dev] = n;
+  done[dev] = true;
+  return ZT_OK;
+}
+
+template <bool GATED>
+int launch_pair(const EggParams& P, cudaStream_t s) {
+  int dev = 0;
+  if (int rc = zt::check_cuda(cudaGetDevice(&dev), "eggroll: cudaGetDevice")) return rc;
+  const int max_clusters = g_max_pairs[dev];
+  const int tiles = (P.m_blocks / 2) * P.n_blocks;
+  const int clusters = tiles < max_clusters ? tiles : max_clusters;
+  eggroll_gemm_pair_kernel<GATED><<<2 * clusters, kThreadsEgg, kSmemBytes2, s>>>(P);
+  return zt::check_cuda(cudaGetLastError(), GATED ? "eggroll: gated gemm launch" : "eggroll: gemm launch (pair)");
+}
+
 }  // namespace
 
 extern "C" {
@@ -741,18 +844,14 @@ int zt_eggroll_linear(const zt_eggroll_args* args, void* stream) {
   EggParams P;
   if (int rc = make_map(enc, &P.tmap_x, A.x, (uint64_t)A.m, (uint64_t)A.k, kBM)) return rc;
   if (int rc = make_map(enc, &P.tmap_w, A.w, (uint64_t)A.n, (uint64_t)A.k, pair ? kHalfRows : kBN)) return rc;
-  if (pair) {
-    const cuuint64_t dims[2] = {(cuuint64_t)A.n, (cuuint64_t)A.m};
-    const cuuint64_t strides[1] = {(cuuint64_t)A.n * 2};
-    const cuuint32_t box[2] = {32, 32};
-    const cuuint32_t estr[2] = {1, 1};
-    if (enc(&P.tmap_y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A.y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return zt::set_error(ZT_ERR_CUDA, "zt_eggroll_linear: cuTensorMapEncodeTiled (output) failed");
-  }
+  if (pair)
+    if (int rc = make_out_map(enc, &P.tmap_y, A.y, (uint64_t)A.m, (uint64_t)A.n)) return rc;
   P.a = A.a;
   P.sigma = A.sigma;
   P.xb = A.xb;
+  P.a2 = nullptr;
+  P.sigma2 = nullptr;
+  P.xb2 = nullptr;
   P.y = static_cast<__nv_bfloat16*>(A.y);
   P.m_blocks = (int32_t)(A.m / kBM);
   P.n_blocks = (int32_t)(A.n / kBN);
@@ -765,55 +864,53 @@ int zt_eggroll_linear(const zt_eggroll_args* args, void* stream) {
     float* xx[1] = {A.xb};
     if (int rc = launch_xb(A.x, bb, xx, 1, A.m, A.k, A.rows_per_member, s)) return rc;
   }
-  {  // the dynamic shared-memory limit is a per-device function attribute
-    static std::mutex mu;
-    static bool done[64] = {false};
-    int dev = 0;
-    if (int rc = zt::check_cuda(cudaGetDevice(&dev), "zt_eggroll_linear: cudaGetDevice")) return rc;
-    if (dev < 0 || dev >= 64) return zt::set_error(ZT_ERR_LIMIT, "zt_eggroll_linear: device ordinal >= 64");
-    std::lock_guard<std::mutex> lock(mu);
-    if (!done[dev]) {
-      if (int rc = zt::check_cuda(cudaFuncSetAttribute(eggroll_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                       (int)kSmemBytes), "zt_eggroll_linear: shared memory attribute"))
-        return rc;
-      if (int rc = zt::check_cuda(cudaFuncSetAttribute(eggroll_gemm_pair_kernel,
-                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes2),
-                                  "zt_eggroll_linear: shared memory attribute (pair)"))
-        return rc;
-      done[dev] = true;
-    }
-  }
-  if (pair) {
-    static std::mutex cmu;
-    static int max_clusters_dev[64] = {0};
-    int dev = 0;
-    if (int rc = zt::check_cuda(cudaGetDevice(&dev), "zt_eggroll_linear: cudaGetDevice")) return rc;
-    int max_clusters = 0;
-    {
-      std::lock_guard<std::mutex> lock(cmu);
-      if (max_clusters_dev[dev] == 0) {  // pairs that fit on the GPU at once (GPC boundaries)
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(2 * (unsigned)(zt::sm_count() / 2));
-        cfg.blockDim = dim3(kThreadsEgg);
-        cfg.dynamicSmemBytes = kSmemBytes2;
-        int n = 0;
-        if (int rc = zt::check_cuda(cudaOccupancyMaxActiveClusters(&n, eggroll_gemm_pair_kernel, &cfg),
-                                    "zt_eggroll_linear: cudaOccupancyMaxActiveClusters"))
-          return rc;
-        if (n <= 0) return zt::set_error(ZT_ERR_CUDA, "zt_eggroll_linear: no CTA pair fits on this GPU");
-        max_clusters_dev[dev] = n;
-      }
-      max_clusters = max_clusters_dev[dev];
-    }
-    const int tiles = (P.m_blocks / 2) * P.n_blocks;
-    const int clusters = tiles < max_clusters ? tiles : max_clusters;
-    eggroll_gemm_pair_kernel<<<2 * clusters, kThreadsEgg, kSmemBytes2, s>>>(P);
-    return zt::check_cuda(cudaGetLastError(), "zt_eggroll_linear: gemm launch (pair)");
-  }
+  if (int rc = prepare_kernels()) return rc;
+  if (pair) return launch_pair<false>(P, s);
   const int tiles = P.m_blocks * P.n_blocks;
   const int grid = tiles < zt::sm_count() ? tiles : zt::sm_count();
   eggroll_gemm_kernel<<<grid, kThreadsEgg, kSmemBytes, s>>>(P);
   return zt::check_cuda(cudaGetLastError(), "zt_eggroll_linear: gemm launch");
+}
+
+int zt_eggroll_gated(const zt_eggroll_gated_args* args, void* stream) {
+  zt::clear_error();
+  if (!args) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_gated: null args");
+  const zt_eggroll_gated_args& A = *args;
+  if (!A.x || !A.w_gate || !A.w_up || !A.a_gate || !A.a_up || !A.sigma_gate || !A.sigma_up || !A.xb_gate ||
+      !A.xb_up || !A.y)
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_gated: null pointer");
+  if (A.rank != 4) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_gated: rank must be 4");
+  if (A.m <= 0 || A.n <= 0 || A.k <= 0) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_gated: empty shape");
+  if (A.m % 256 || A.n % 128 || A.k % kBK)
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_gated: need M % 256 == 0, N % 128 == 0, K % 64 == 0");
+  if (A.rows_per_member <= 0 || A.rows_per_member % kBM || A.m % A.rows_per_member)
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_gated: rows_per_member must divide M and be a multiple of 128");
+  if (A.m > (int64_t)INT32_MAX || A.n > (int64_t)INT32_MAX || A.k > (int64_t)INT32_MAX)
+    return zt::set_error(ZT_ERR_LIMIT, "zt_eggroll_gated: dimension above 2^31-1");
+  for (const void* p : {A.x, A.w_gate, A.w_up, (const void*)A.a_gate, (const void*)A.a_up, (const void*)A.xb_gate,
+                        (const void*)A.xb_up, (const void*)A.y})
+    if (((uintptr_t)p & 15) != 0) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_gated: pointers must be 16-byte aligned");
+  EncodeFn enc = nullptr;
+  if (int rc = get_encode(&enc)) return rc;
+  EggParams P;
+  if (int rc = make_map(enc, &P.tmap_x, A.x, (uint64_t)A.m, (uint64_t)A.k, kBM)) return rc;
+  if (int rc = make_map(enc, &P.tmap_w, A.w_gate, (uint64_t)A.n, (uint64_t)A.k, kHalfRows)) return rc;
+  if (int rc = make_map(enc, &P.tmap_w2, A.w_up, (uint64_t)A.n, (uint64_t)A.k, kHalfRows)) return rc;
+  if (int rc = make_out_map(enc, &P.tmap_y, A.y, (uint64_t)A.m, (uint64_t)A.n)) return rc;
+  P.a = A.a_gate;
+  P.sigma = A.sigma_gate;
+  P.xb = A.xb_gate;
+  P.a2 = A.a_up;
+  P.sigma2 = A.sigma_up;
+  P.xb2 = A.xb_up;
+  P.y = static_cast<__nv_bfloat16*>(A.y);
+  P.m_blocks = (int32_t)(A.m / kBM);
+  P.n_blocks = (int32_t)(A.n / 128);  // tiles of 128 output features
+  P.k_blocks = (int32_t)(A.k / kBK);
+  P.n = (int32_t)A.n;
+  P.rows_per_member = A.rows_per_member;
+  if (int rc = prepare_kernels()) return rc;
+  return launch_pair<true>(P, zt::as_stream(stream));
 }
 
 int zt_eggroll_xb(const zt_eggroll_xb_args* args, void* stream) {

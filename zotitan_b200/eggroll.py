@@ -157,8 +157,9 @@ class PopAttention(nn.Module):
 
 
 class PopMLP(nn.Module):
-    """Llama MLP down(silu(gate(x)) * up(x)) with population projections and the SwiGLU
-    product in one launch (zt_eggroll_swiglu)."""
+    """Llama MLP down(silu(gate(x)) * up(x)) with population projections. Gate, up and
+    the SwiGLU product run as one GEMM (zt_eggroll_gated) when the rows split into
+    256-row tiles, else as two EGGROLL linears and zt_eggroll_swiglu."""
 
     def __init__(self, gate_proj, up_proj, down_proj):
         super().__init__()
@@ -168,6 +169,10 @@ class PopMLP(nn.Module):
         projs = (self.gate_proj, self.up_proj)
         if all(isinstance(p, PopLinear) for p in projs):
             x2, facs, xbs = _shared_input(x, projs, projs[0].pop)
+            if x2.shape[0] % 256 == 0:   # gate, up and SwiGLU in one GEMM (zt_eggroll_gated)
+                h = K.eggroll_gated(x2, self.gate_proj.weight.data, self.up_proj.weight.data, facs[0], facs[1],
+                                    xbs[0], xbs[1], projs[0].pop.rows_per_member)
+                return self.down_proj(h.view(*x.shape[:-1], -1))
             g, u = (p(x2, f, xb).view(*x.shape[:-1], -1) for p, f, xb in zip(projs, facs, xbs))
         else:
             g, u = (p(x) for p in projs)

@@ -291,6 +291,32 @@ def eggroll_xb(x: torch.Tensor, bs: list, rows_per_member: int) -> list:
     return xbs
 
 
+def eggroll_gated(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, fac_gate, fac_up, xb_gate, xb_up,
+                  rows_per_member: int) -> torch.Tensor:
+    """bf16(bf16(silu(G)) * U) for the population rows x [M, K] (zt_eggroll_gated):
+    G, U the EGGROLL linear outputs of the gate and up projections. fac_* = (A, B, scale)
+    from eggroll_factors; xb_* = X B from eggroll_xb. M % 256 == 0."""
+    for t, name in ((x, "x"), (w_gate, "w_gate"), (w_up, "w_up"), (xb_gate, "xb_gate"), (xb_up, "xb_up")):
+        _check_cuda(t, name)
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    M, K = x.shape
+    N = w_gate.shape[0]
+    if w_up.shape != (N, K) or w_gate.shape[1] != K:
+        raise ValueError("inconsistent shapes")
+    members = M // rows_per_member
+    for a, _, sg in (fac_gate, fac_up):
+        if a.shape != (members, N, 4) or sg.shape != (members,):
+            raise ValueError("inconsistent factor shapes")
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    args = L.ZtEggrollGatedArgs(x.data_ptr(), w_gate.data_ptr(), w_up.data_ptr(), fac_gate[0].data_ptr(),
+                                fac_up[0].data_ptr(), fac_gate[2].data_ptr(), fac_up[2].data_ptr(), xb_gate.data_ptr(),
+                                xb_up.data_ptr(), y.data_ptr(), M, N, K, rows_per_member, 4)
+    with torch.cuda.device(x.device):
+        L.check(L.load().zt_eggroll_gated(ctypes.byref(args), _stream_ptr(x.device)), "zt_eggroll_gated")
+    return y
+
+
 def eggroll_take_error() -> int:
     """Read and clear the EGGROLL kernels' device error code (synchronous)."""
     code = ctypes.c_int32(0)
