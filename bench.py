@@ -44,6 +44,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-eggroll", action="store_true", help="skip the EGGROLL population measurement")
     ap.add_argument("--no-mezo", action="store_true", help="skip the MeZO full fine-tune step measurement")
+    ap.add_argument("--no-lora", action="store_true", help="skip the MeZO-Adam LoRA step measurement")
     ap.add_argument("--profile-case", choices=["chain", "full", "eggroll", "eggroll-forward"], default=None,
                     help="small case for ncu: one bf16 tensor of 2^28 elements, 3 launches of the "
                          "-2eps pass (chain) or of the restore+accumulate+perturb pass (full); or 3 "
@@ -396,6 +397,71 @@ def mezo_full_ft_steps(dev, rank: int, world: int, steps: int = 3, warmup: int =
             "loss_last_step": m["loss"], "proj_grad_last_step": m["proj_grad"]}
 
 
+def mezo_adam_lora_steps(dev, rank: int, world: int, steps: int = 3, warmup: int = 2):
+    """ZO steps/s of MeZO-Adam with seed-window momentum (K = 16 past seeds) and second
+    moment on rank-16 LoRA adapters (q/k/v/o/gate/up/down, fp32, A ~ N(0, 1/r), B = 0) of
+    the Llama-3-8B-shaped bf16 model: one antithetic pair per step (z_batch = 1), next-token
+    CE on an 8 x 1024 batch of uniform random tokens (pair batch of step t from seed t),
+    eps = 1e-3, lr = 1e-5, beta1 = 0.9, beta2 = 0.999. One step = 2 forwards of the
+    LoRA-wrapped model + the fused perturb/restore passes + the last pass replaying the
+    16-step seed window (momentum rebuilt in registers) with the Adam update, over the
+    448 adapter tensors (41,943,040 fp32 parameters). z_batch = 1 gives nothing to shard:
+    with W > 1 every rank runs its own replica and the slowest rank's time is reported."""
+    import torch
+    import torch.distributed as dist
+
+    from zotitan_b200.data import synthetic_token_batch
+    from zotitan_b200.lora import LoRAConfig, make_lora, trainable_params
+    from zotitan_b200.objective import SyntheticTokensObjective
+    from zotitan_b200.synthetic import LLAMA_8B, build_llama
+    from zotitan_b200.train_zo import ZOConfig, ZOOptimizer
+    B, S, r = 8, 1024, 16
+    model = build_llama(LLAMA_8B, device=dev, seed=0, max_positions=S)
+    make_lora(model, LoRAConfig(r=r, alpha=32, dtype="fp32"))
+    g = torch.Generator(device=dev).manual_seed(1)
+    with torch.no_grad():
+        for n, p in model.named_parameters():
+            if "lora_A" in n:
+                p.normal_(0.0, (1.0 / r) ** 0.5, generator=g)
+    objective = SyntheticTokensObjective(LLAMA_8B.vocab, S)
+    cfg = ZOConfig()
+    cfg.eps, cfg.z_batch, cfg.base.lr = EPS, 1, 1e-5
+    cfg.mom.momentum_method, cfg.mom.beta1, cfg.mom.beta2, cfg.mom.second_moment = "seed_window", 0.9, 0.999, True
+    cfg.seed_window.size = 16
+    named = [(n, p) for n, p in model.named_parameters() if p.requires_grad]
+    group = None
+    if world > 1:   # a one-rank group per rank: every rank is an independent replica
+        groups = [dist.new_group([r]) for r in range(world)]
+        group = groups[rank]
+    opt = ZOOptimizer(named, cfg, objective.score, total_steps=steps + warmup + 16, process_group=group)
+    plan = [[synthetic_token_batch(LLAMA_8B.vocab, B, S, t, device=dev)] for t in range(warmup + steps)]
+    for t in range(warmup):
+        opt.step(model, plan[t])
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for t in range(warmup, warmup + steps):
+        m = opt.step(model, plan[t])
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    n_train, n_total = trainable_params(model)
+    n_tensors = len(named)
+    del opt, model, named, plan
+    torch.cuda.empty_cache()
+    return {"metric": "ZO steps/s (MeZO-Adam, seed window 16, LoRA r16 on Llama-3-8B shape)",
+            "value": steps / (ms * 1e-3), "unit": "ZO steps/s", "ms_per_step": ms / steps, "steps": steps,
+            "warmup": warmup, "batch": B, "seq_len": S, "trainable_params": n_train, "trainable_tensors": n_tensors,
+            "total_params": n_total, "parallelism": f"replicas x{world}", "loss_last_step": m["loss"],
+            "proj_grad_last_step": m["proj_grad"]}
+
+
 # ── our arm ─────────────────────────────────────────────────────────────────────────
 
 def run_ours(args, rank, local_rank, world):
@@ -525,6 +591,7 @@ def run_ours(args, rank, local_rank, world):
     torch.cuda.empty_cache()
     egg = eggroll_member_evals(dev, rank, world) if not args.no_eggroll else None
     mezo = mezo_full_ft_steps(dev, rank, world) if not args.no_mezo else None
+    lora = mezo_adam_lora_steps(dev, rank, world) if not args.no_lora else None
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
@@ -580,6 +647,8 @@ def run_ours(args, rank, local_rank, world):
         line["eggroll"] = egg
     if mezo is not None:
         line["mezo_full_ft"] = mezo
+    if lora is not None:
+        line["mezo_adam_lora"] = lora
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
