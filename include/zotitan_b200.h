@@ -256,6 +256,13 @@ typedef struct zt_eggroll_args {
   int32_t rank;           /* must be 4 */
   int32_t xb_ready;       /* nonzero: xb already holds X B_i (zt_eggroll_xb) and is only read */
   int32_t reserved;
+  /* Optional rank-4 K-slab (both non-NULL: a, b, sigma, xb are not read). The correction
+   * sigma_i (X B_i) A_i^T then runs on the tensor cores as one extra K = 16 MMA per tile:
+   * x_ext [m, 16] bf16 rows [hi(sigma_i X B_i), lo(sigma_i X B_i), 0 x 8] (zt_eggroll_xb,
+   * hi + lo = the fp32 value to ~2^-16), w_ext [members, n, 16] bf16 rows [A_i, A_i, 0 x 8]
+   * (zt_eggroll_factors). Needs m % 256 == 0 and rows_per_member % 256 == 0. */
+  const void* x_ext;
+  const void* w_ext;
 } zt_eggroll_args;
 
 ZT_API int zt_eggroll_linear(const zt_eggroll_args* args, void* stream);
@@ -266,10 +273,14 @@ ZT_API int zt_eggroll_linear(const zt_eggroll_args* args, void* stream);
 typedef struct zt_eggroll_xb_args {
   const void* x;          /* [m, k] bf16, 16-byte aligned */
   const float* b[3];      /* per set: [members, k, 4] fp32 (entries >= n_seg unused) */
-  float* xb[3];           /* per set: [m, 4] fp32 out */
+  float* xb[3];           /* per set: [m, 4] fp32 out (NULL: not written) */
   int64_t m, k;           /* m % 64 == 0, k % 4 == 0 */
   int32_t n_seg;          /* 1, 2 or 3 */
   int32_t rows_per_member;  /* multiple of 64 dividing m */
+  const float* sigma[3];  /* per set: [members] signed scale, read when xe[s] is set */
+  void* xe[3];            /* per set: optional [m, 16] bf16 K-slab rows of sigma_i X B (NULL: skip) */
+  int32_t xe_slot[3];     /* 0: write [hi, lo, 0 x 8]; 1: write [hi, lo] to columns 0-7; 2: to 8-15 */
+  int32_t reserved;
 } zt_eggroll_xb_args;
 
 ZT_API int zt_eggroll_xb(const zt_eggroll_xb_args* args, void* stream);
@@ -294,6 +305,12 @@ typedef struct zt_eggroll_gated_args {
   int64_t m, n, k;        /* m % 256 == 0, n % 128 == 0, k % 64 == 0 */
   int32_t rows_per_member;  /* multiple of 128 dividing m */
   int32_t rank;           /* must be 4 */
+  /* Optional K-slab form of both corrections (all three non-NULL; rows_per_member % 256
+   * == 0): x_ext rows [hi_g, lo_g, hi_u, lo_u] (zt_eggroll_xb slots 1 and 2), w_ext_gate
+   * rows [A_g, A_g, 0 x 8], w_ext_up rows [0 x 8, A_u, A_u] (zt_eggroll_factors slots 0, 1). */
+  const void* x_ext;
+  const void* w_ext_gate;
+  const void* w_ext_up;
 } zt_eggroll_gated_args;
 
 ZT_API int zt_eggroll_gated(const zt_eggroll_gated_args* args, void* stream);
@@ -333,6 +350,10 @@ typedef struct zt_eggroll_factor_args {
   float* b;               /* out [2*pairs, k, 4] fp32, 16-byte aligned */
   float* scale;           /* out [2*pairs] fp32 */
   float* work;            /* workspace: pairs * ZT_EGGROLL_FACTOR_WORK_FLOATS floats */
+  void* a_ext;            /* optional out [2*pairs, n, 16] bf16: A as the B operand of the GEMM's
+                             rank-4 K-slab (see zt_eggroll_args.w_ext); NULL to skip */
+  int32_t ext_slot;       /* a_ext row: 0 = [A, A, 0 x 8], 1 = [0 x 8, A, A] */
+  int32_t reserved2;
 } zt_eggroll_factor_args;
 
 ZT_API int zt_eggroll_factors(const zt_eggroll_factor_args* args, void* stream);

@@ -131,3 +131,81 @@ def test_gated_pair_matches_unfused_path(M, N, K, T):
     assert bool((d <= tol).all()), float(d.max())
     if N % 256 == 0:
         assert float((d == 0).float().mean()) >= 0.999
+
+
+def _steps(a, b):
+    a, b = a.float(), b.float()
+    e = torch.frexp(b.abs().clamp_min(2.0 ** -126))[1].float()
+    return (a - b).abs() / torch.ldexp(torch.ones_like(e), (e - 8).int())
+
+
+def test_ksliced_factor_and_xb_rows():
+    """A_ext rows are the bf16 factors in the documented slots; X_ext rows hold
+    hi + lo = sigma_i X B_i to ~2^-16 relative."""
+    from zotitan_b200 import kernels as K_
+    n, k, T = 512, 1024, 256
+    keys_a, keys_b = [11, 12], [21, 22]
+    a, b, sc, ae0 = K_.eggroll_factors(keys_a, keys_b, n, k, 1e-3, "cuda", ext_slot=0)
+    _, _, _, ae1 = K_.eggroll_factors(keys_a, keys_b, n, k, 1e-3, "cuda", ext_slot=1)
+    ab = a.bfloat16()
+    assert torch.equal(ae0[..., 0:4], ab) and torch.equal(ae0[..., 4:8], ab) and not ae0[..., 8:].any()
+    assert torch.equal(ae1[..., 8:12], ab) and torch.equal(ae1[..., 12:16], ab) and not ae1[..., :8].any()
+    x = torch.randn(4 * T, k, device="cuda").bfloat16()
+    xb = K_.eggroll_xb(x, [b], T)[0]
+    xe = K_.eggroll_xb_ext(x, [b], [sc], [0], T)[0]
+    want = xb * sc.repeat_interleave(T)[:, None]
+    got = xe[:, 0:4].float() + xe[:, 4:8].float()
+    assert float(((got - want).abs() / want.abs().clamp_min(1e-30)).max()) < 2 ** -15
+    assert not xe[:, 8:].any()
+    g1, g2 = K_.eggroll_xb_ext(x, [b, b], [sc, sc], [1, 2], T)
+    assert g1.data_ptr() == g2.data_ptr() and torch.equal(g1[:, 0:8], xe[:, 0:8]) and torch.equal(g1[:, 8:], xe[:, 0:8])
+
+
+@pytest.mark.parametrize("M,N,K,T,sigma", [(512, 1024, 1024, 256, 1e-3), (2048, 4096, 4096, 1024, 1e-3),
+                                           (512, 1024, 1024, 256, 5e-2)])
+def test_ksliced_linear_matches_fp32_epilogue(M, N, K, T, sigma):
+    """The rank-4 term as a tensor-core K-slab against the fp32 epilogue. The slab carries
+    sigma X B as hi + lo bf16 (~2^-16 relative), so the outputs agree within one bf16 step
+    plus 2^-14 of the term's magnitude sum_r |sigma X B_r| |A_r| (absolute: where the term
+    cancels the base product the output is small and the bound is loose in bf16 steps)."""
+    from zotitan_b200 import kernels as K_
+    g = torch.Generator(device="cuda").manual_seed(M + K)
+    members = M // T
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).bfloat16()
+    a, b, sc, ae = K_.eggroll_factors(list(range(1, members // 2 + 1)), list(range(50, 50 + members // 2)), N, K,
+                                      sigma, "cuda", ext_slot=0)
+    y32 = K_.eggroll_linear(x, w, a, b, sc, T)
+    xe = K_.eggroll_xb_ext(x, [b], [sc], [0], T)[0]
+    yk = K_.eggroll_linear(x, w, a, None, sc, T, x_ext=xe, w_ext=ae)
+    xb = K_.eggroll_xb(x, [b], T)[0]
+    torch.cuda.synchronize()
+    assert K_.eggroll_take_error() == 0
+    sxb = (xb * sc.repeat_interleave(T)[:, None]).abs()
+    term = torch.cat([sxb[i * T:(i + 1) * T] @ a[i].abs().T for i in range(members)])
+    ulp = torch.ldexp(torch.ones_like(y32.float()), (torch.frexp(y32.float().abs().clamp_min(2.0 ** -126))[1] - 8).int())
+    d = (yk.float() - y32.float()).abs()
+    assert bool((d <= ulp + 2.0 ** -14 * term).all()), float((d - ulp - 2.0 ** -14 * term).max())
+    if sigma <= 1e-3:
+        assert float((d == 0).float().mean()) >= 0.99
+    assert not torch.equal(y32, (x.float() @ w.float().T).bfloat16())   # the term is applied
+
+
+def test_ksliced_gated_matches_fp32_epilogue():
+    from zotitan_b200 import kernels as K_
+    M, N, K, T = 1024, 1408, 1024, 512
+    g = torch.Generator(device="cuda").manual_seed(77)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    wg = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
+    wu = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
+    fg = K_.eggroll_factors([3], [4], N, K, 1e-3, "cuda", ext_slot=0)
+    fu = K_.eggroll_factors([5], [6], N, K, 1e-3, "cuda", ext_slot=1)
+    xbg, xbu = K_.eggroll_xb(x, [fg[1], fu[1]], T)
+    y32 = K_.eggroll_gated(x, wg, wu, fg, fu, xbg, xbu, T)
+    xe = K_.eggroll_xb_ext(x, [fg[1], fu[1]], [fg[2], fu[2]], [1, 2], T)[0]
+    yk = K_.eggroll_gated(x, wg, wu, fg, fu, None, None, T, x_ext=xe)
+    torch.cuda.synchronize()
+    assert K_.eggroll_take_error() == 0
+    d = (yk.float() - y32.float()).abs()
+    assert bool((d <= 2.0 ** -7 * y32.float().abs() + 1e-3 * y32.float().abs().max()).all())
+    assert float((d == 0).float().mean()) >= 0.98

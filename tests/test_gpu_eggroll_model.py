@@ -46,11 +46,14 @@ def _member_losses_materialised(tokens, pair_seeds):
     return losses
 
 
-def test_population_forward_matches_materialised_members():
+@pytest.mark.parametrize("batch", [2, 4])
+def test_population_forward_matches_materialised_members(batch):
+    """batch 2 (128 rows per member): the rank-4 terms in fp32 epilogues; batch 4 (256 rows
+    per member): the rank-4 terms as tensor-core K-slabs. Both run the gated MLP GEMM."""
     from toy_models import build_llama
     from zotitan_b200.eggroll import EggrollConfig, EggrollPopulation
     g = torch.Generator().manual_seed(5)
-    tokens = torch.randint(0, SHAPE["vocab_size"], (2, 64), generator=g).cuda()
+    tokens = torch.randint(0, SHAPE["vocab_size"], (batch, 64), generator=g).cuda()
     pair_seeds = [3, 11]
     model = build_llama(SHAPE, dtype=torch.bfloat16, seed=0, device="cuda")
     pop = EggrollPopulation(model, EggrollConfig(sigma=SIGMA))

@@ -71,7 +71,7 @@ class ZtEggrollArgs(ctypes.Structure):
                 ("sigma", ctypes.c_void_p), ("xb", ctypes.c_void_p), ("y", ctypes.c_void_p),
                 ("m", ctypes.c_int64), ("n", ctypes.c_int64), ("k", ctypes.c_int64),
                 ("rows_per_member", ctypes.c_int32), ("rank", ctypes.c_int32), ("xb_ready", ctypes.c_int32),
-                ("reserved", ctypes.c_int32)]
+                ("reserved", ctypes.c_int32), ("x_ext", ctypes.c_void_p), ("w_ext", ctypes.c_void_p)]
 
 
 class ZtEggrollGatedArgs(ctypes.Structure):
@@ -79,20 +79,23 @@ class ZtEggrollGatedArgs(ctypes.Structure):
                 ("a_gate", ctypes.c_void_p), ("a_up", ctypes.c_void_p), ("sigma_gate", ctypes.c_void_p),
                 ("sigma_up", ctypes.c_void_p), ("xb_gate", ctypes.c_void_p), ("xb_up", ctypes.c_void_p),
                 ("y", ctypes.c_void_p), ("m", ctypes.c_int64), ("n", ctypes.c_int64), ("k", ctypes.c_int64),
-                ("rows_per_member", ctypes.c_int32), ("rank", ctypes.c_int32)]
+                ("rows_per_member", ctypes.c_int32), ("rank", ctypes.c_int32), ("x_ext", ctypes.c_void_p),
+                ("w_ext_gate", ctypes.c_void_p), ("w_ext_up", ctypes.c_void_p)]
 
 
 class ZtEggrollXbArgs(ctypes.Structure):
     _fields_ = [("x", ctypes.c_void_p), ("b", ctypes.c_void_p * 3), ("xb", ctypes.c_void_p * 3),
                 ("m", ctypes.c_int64), ("k", ctypes.c_int64), ("n_seg", ctypes.c_int32),
-                ("rows_per_member", ctypes.c_int32)]
+                ("rows_per_member", ctypes.c_int32), ("sigma", ctypes.c_void_p * 3), ("xe", ctypes.c_void_p * 3),
+                ("xe_slot", ctypes.c_int32 * 3), ("reserved", ctypes.c_int32)]
 
 
 class ZtEggrollFactorArgs(ctypes.Structure):
     _fields_ = [("keys_a", ctypes.c_void_p), ("keys_b", ctypes.c_void_p), ("pairs", ctypes.c_int32),
                 ("rank", ctypes.c_int32), ("n", ctypes.c_int64), ("k", ctypes.c_int64), ("dtype", ctypes.c_int32),
                 ("normalize", ctypes.c_int32), ("sigma", ctypes.c_float), ("reserved", ctypes.c_int32),
-                ("a", ctypes.c_void_p), ("b", ctypes.c_void_p), ("scale", ctypes.c_void_p), ("work", ctypes.c_void_p)]
+                ("a", ctypes.c_void_p), ("b", ctypes.c_void_p), ("scale", ctypes.c_void_p), ("work", ctypes.c_void_p),
+                ("a_ext", ctypes.c_void_p), ("ext_slot", ctypes.c_int32), ("reserved2", ctypes.c_int32)]
 
 
 class ZtEggrollNormArgs(ctypes.Structure):

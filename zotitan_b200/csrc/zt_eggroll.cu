@@ -63,6 +63,9 @@ struct EggParams {
   const float* a2;     // gated: A of the up projection [members, N, 4]
   const float* sigma2; // gated: [members]
   const float* xb2;    // gated: X B_up [M, 4]
+  CUtensorMap tmap_xe;  // K-slab: X_ext [M, 16] bf16, box {16, 128}, 32-byte swizzle
+  CUtensorMap tmap_we;  // K-slab: W_ext [members * N, 16] bf16 (gated: of the gate projection)
+  CUtensorMap tmap_we2; // gated K-slab: W_ext of the up projection
   const float* a;      // [members, N, 4]
   const float* sigma;  // [members]
   const float* xb;     // [M, 4]
@@ -126,6 +129,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tmap, 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Same for a 32-byte-swizzled K-major tile (rows of 16 bf16): 8-row groups 256 bytes
+// apart, layout type 6 (SWIZZLE_32B).
+__device__ __forceinline__ uint64_t umma_desc32(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(256 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)6 << 61);
 }
 
 // Instruction descriptor: fp32 accumulator, bf16 A and B, both K-major, N = 256, M = 128.
@@ -324,6 +334,7 @@ constexpr uint32_t kHalfRows = 128;
 constexpr uint32_t kStageA2 = kHalfRows * kBK * 2;  // 16 KB of X
 constexpr uint32_t kStageB2 = kHalfRows * kBK * 2;  // 16 KB of W (this CTA's half of the N tile)
 constexpr uint32_t kStageBytes2 = kStageA2 + kStageB2;
+constexpr uint32_t kExtTile = kHalfRows * 16 * 2;     // 128 rows of a 16-column bf16 K-slab
 constexpr uint32_t kOutChunk = 32 * 32 * 2;           // one warp's 32 x 32 bf16 output chunk
 constexpr uint32_t kOutBytes2 = 4 * 2 * kOutChunk;     // 4 epilogue warps x 2 buffers
 constexpr size_t kSmemBytes2 = 1024 + kStages2 * kStageBytes2 + kOutBytes2 + 256;
@@ -412,7 +423,10 @@ __device__ __forceinline__ bool mbar_wait_pair(uint64_t* bar, uint32_t parity, v
 // columns 0..127 hold G and 128..255 hold U for features [nb*128, nb*128+128), and the
 // epilogue writes bf16(bf16(silu(bf16(G))) * bf16(U)) -- the rounding torch applies to
 // act_fn(gate_proj(x)) * up_proj(x) -- without G or U ever reaching global memory.
-template <bool GATED>
+// EXT: the rank-4 term runs on the tensor cores as one more K = 16 slab per tile,
+// X_ext [hi, lo of sigma_i X B_i] against W_ext [A_i, A_i] (gated: gate columns 0-7, up
+// columns 8-15), so the epilogue only converts (and, gated, applies the SwiGLU).
+template <bool GATED, bool EXT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
     eggroll_gemm_pair_kernel(const __grid_constant__ EggParams P) {
   extern __shared__ uint8_t smem_raw[];
@@ -476,6 +490,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
             tma_load_2d_pair(sa + kStageA2, &P.tmap_w, leader_full, kb * kBK, nb * kBN + (int)rank * 128);
           last_phase[s] = (int)(round & 1);
         }
+        if (ok && EXT) {  // the rank-4 K-slab of this tile
+          const int s = it % kStages2;
+          const uint32_t round = it / kStages2;
+          if (!mbar_wait_pair(&empty[s], (round & 1) ^ 1, abort, peer_abort, 1)) {
+            ok = false;
+          } else {
+            uint8_t* sa = stage_base + s * kStageBytes2;
+            const uint32_t leader_full = peer_addr(&full[s], 0);
+            const int member = (mb * 256) / P.rows_per_member;
+            if (leader) mbar_expect_tx(&full[s], 2 * 2 * kExtTile);
+            tma_load_2d_pair(sa, &P.tmap_xe, leader_full, 0, mb * 256 + (int)rank * 128);
+            if (GATED)
+              tma_load_2d_pair(sa + kStageA2, rank ? &P.tmap_we2 : &P.tmap_we, leader_full, 0, member * P.n + nb * 128);
+            else
+              tma_load_2d_pair(sa + kStageA2, &P.tmap_we, leader_full, 0, member * P.n + nb * kBN + (int)rank * 128);
+            last_phase[s] = (int)(round & 1);
+            ++it;
+          }
+        }
         if (!ok) break;
       }
       // Drain (leader): each armed phase of a full barrier completes only when both CTAs'
@@ -509,6 +542,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
           issued = true;
           umma_commit_pair(&empty[s]);  // stage s is free in both CTAs once these MMAs have read it
         }
+        if (ok && EXT) {  // + (sigma_i X B_i) A_i^T as one K = 16 MMA
+          const int s = it % kStages2;
+          if (!mbar_wait_pair(&full[s], (it / kStages2) & 1, abort, peer_abort, 3)) {
+            ok = false;
+          } else {
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t sa = smem_u32(stage_base + s * kStageBytes2);
+            umma_bf16_pair(tmem_d, umma_desc32(sa), umma_desc32(sa + kStageA2), 1);
+            umma_commit_pair(&empty[s]);
+            ++it;
+          }
+        }
         if (!ok) break;
         umma_commit_pair(&accf[b]);  // accumulator b is complete in both CTAs
       }
@@ -537,9 +582,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
       const int m = row0 + row;
       const int member = row0 / P.rows_per_member;
       const int col0 = nb * (GATED ? 128 : kBN);  // first output column of the tile
-      const float4* a_tile = reinterpret_cast<const float4*>(P.a + ((size_t)member * P.n + (size_t)col0) * 4);
-      const float sg = __ldg(P.sigma + member);
-      const float4 xb = __ldg(reinterpret_cast<const float4*>(P.xb) + m);
+      const float4* a_tile = EXT ? nullptr : reinterpret_cast<const float4*>(P.a + ((size_t)member * P.n + (size_t)col0) * 4);
+      const float sg = EXT ? 0.f : __ldg(P.sigma + member);
+      const float4 xb = EXT ? make_float4(0.f, 0.f, 0.f, 0.f) : __ldg(reinterpret_cast<const float4*>(P.xb) + m);
       const float x0 = sg * xb.x, x1 = sg * xb.y, x2 = sg * xb.z, x3 = sg * xb.w;
       int ok = 1;
       if (lane == 0) ok = mbar_wait_pair(&accf[b], (tcount >> 1) & 1, abort, peer_abort, 4) ? 1 : 0;
@@ -550,7 +595,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
       const int out_cols = GATED ? 128 : kBN;
       const float4* a2_tile = nullptr;
       float u0 = 0.f, u1 = 0.f, u2 = 0.f, u3 = 0.f;
-      if (GATED) {
+      if (GATED && !EXT) {
         a2_tile = reinterpret_cast<const float4*>(P.a2 + ((size_t)member * P.n + (size_t)nb * 128) * 4);
         const float sg2 = __ldg(P.sigma2 + member);
         const float4 xb2 = __ldg(reinterpret_cast<const float4*>(P.xb2) + m);
@@ -568,12 +613,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
             float h[2];
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-              const float4 ag = __ldg(a_tile + c0 + j + e);
-              const float4 au = __ldg(a2_tile + c0 + j + e);
-              const float g = __bfloat162float(__float2bfloat16_rn(
-                  __uint_as_float(r[j + e]) + (x0 * ag.x + x1 * ag.y + x2 * ag.z + x3 * ag.w)));
-              const float u = __bfloat162float(__float2bfloat16_rn(
-                  __uint_as_float(ru[j + e]) + (u0 * au.x + u1 * au.y + u2 * au.z + u3 * au.w)));
+              const float4 ag = EXT ? make_float4(0.f, 0.f, 0.f, 0.f) : __ldg(a_tile + c0 + j + e);
+              const float4 au = EXT ? make_float4(0.f, 0.f, 0.f, 0.f) : __ldg(a2_tile + c0 + j + e);
+              const float cg = EXT ? 0.f : (x0 * ag.x + x1 * ag.y + x2 * ag.z + x3 * ag.w);
+              const float cu = EXT ? 0.f : (u0 * au.x + u1 * au.y + u2 * au.z + u3 * au.w);
+              const float g = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[j + e]) + cg));
+              const float u = __bfloat162float(__float2bfloat16_rn(__uint_as_float(ru[j + e]) + cu));
               h[e] = __bfloat162float(__float2bfloat16_rn(g / (1.0f + expf(-g)))) * u;
             }
             const __nv_bfloat162 hv = __floats2bfloat162_rn(h[0], h[1]);
@@ -582,10 +627,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
         } else {
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
-            const float4 a0 = __ldg(a_tile + c0 + j);
-            const float4 a1 = __ldg(a_tile + c0 + j + 1);
-            const float v0 = __uint_as_float(r[j]) + (x0 * a0.x + x1 * a0.y + x2 * a0.z + x3 * a0.w);
-            const float v1 = __uint_as_float(r[j + 1]) + (x0 * a1.x + x1 * a1.y + x2 * a1.z + x3 * a1.w);
+            float v0 = __uint_as_float(r[j]), v1 = __uint_as_float(r[j + 1]);
+            if (!EXT) {
+              const float4 a0 = __ldg(a_tile + c0 + j);
+              const float4 a1 = __ldg(a_tile + c0 + j + 1);
+              v0 += x0 * a0.x + x1 * a0.y + x2 * a0.z + x3 * a0.w;
+              v1 += x0 * a1.x + x1 * a1.y + x2 * a1.z + x3 * a1.w;
+            }
             const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
             packed[j / 2] = *reinterpret_cast<const uint32_t*>(&h);
           }
@@ -638,9 +686,35 @@ constexpr int kXbRows = 64, kXbRowsPerWarp = 8, kXbChunk = 512, kXbMaxSeg = 3;
 static_assert(kXbRows == 8 * kXbRowsPerWarp, "8 warps per CTA");
 
 struct XbSegs {
-  const float* b[kXbMaxSeg];  // [members, k, 4]
-  float* xb[kXbMaxSeg];       // [m, 4]
+  const float* b[kXbMaxSeg];      // [members, k, 4]
+  float* xb[kXbMaxSeg];           // [m, 4] fp32 (or NULL)
+  const float* sigma[kXbMaxSeg];  // [members] (read when xe is set)
+  uint4* xe[kXbMaxSeg];           // [m, 16] bf16 K-slab rows (or NULL)
+  int32_t xe_slot[kXbMaxSeg];
 };
+
+__device__ __forceinline__ uint32_t pack_bf16x2(__nv_bfloat16 lo, __nv_bfloat16 hi) {
+  return (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+}
+
+// K-slab row of sigma * X B: v = hi + lo with hi = bf16(v), lo = bf16(v - hi).
+__device__ __forceinline__ void write_xe(uint4* row, int slot, float sg, const float acc[4]) {
+  __nv_bfloat16 h[4], l[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const float v = sg * acc[r];
+    h[r] = __float2bfloat16_rn(v);
+    l[r] = __float2bfloat16_rn(v - __bfloat162float(h[r]));
+  }
+  const uint4 hl = make_uint4(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]), pack_bf16x2(l[0], l[1]),
+                              pack_bf16x2(l[2], l[3]));
+  if (slot == 0) {
+    row[0] = hl;
+    row[1] = make_uint4(0u, 0u, 0u, 0u);
+  } else {
+    row[slot - 1] = hl;
+  }
+}
 
 template <int NSEG>
 __global__ void __launch_bounds__(256, 1) eggroll_xb_kernel(const __nv_bfloat16* __restrict__ x,
@@ -701,17 +775,24 @@ __global__ void __launch_bounds__(256, 1) eggroll_xb_kernel(const __nv_bfloat16*
       for (int r = 0; r < 4; ++r)
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc[s][i][r] += __shfl_xor_sync(0xffffffffu, acc[s][i][r], o);
-      if (lane == 0)
-        reinterpret_cast<float4*>(S.xb[s])[wrow + i] = make_float4(acc[s][i][0], acc[s][i][1], acc[s][i][2], acc[s][i][3]);
+      if (lane == 0) {
+        if (S.xb[s])
+          reinterpret_cast<float4*>(S.xb[s])[wrow + i] = make_float4(acc[s][i][0], acc[s][i][1], acc[s][i][2], acc[s][i][3]);
+        if (S.xe[s]) write_xe(S.xe[s] + 2 * (wrow + i), S.xe_slot[s], __ldg(S.sigma[s] + member), acc[s][i]);
+      }
     }
 }
 
 int launch_xb(const void* x, const float* const* b, float* const* xb, int nseg, int64_t m, int64_t k,
-              int32_t rows_per_member, cudaStream_t s) {
+              int32_t rows_per_member, cudaStream_t s, const float* const* sigma = nullptr,
+              void* const* xe = nullptr, const int32_t* xe_slot = nullptr) {
   XbSegs S{};
   for (int i = 0; i < nseg; ++i) {
     S.b[i] = b[i];
     S.xb[i] = xb[i];
+    S.sigma[i] = sigma ? sigma[i] : nullptr;
+    S.xe[i] = xe ? static_cast<uint4*>(xe[i]) : nullptr;
+    S.xe_slot[i] = xe_slot ? xe_slot[i] : 0;
   }
   const unsigned grid = (unsigned)(m / kXbRows);
   const __nv_bfloat16* xp = static_cast<const __nv_bfloat16*>(x);
@@ -758,6 +839,19 @@ int make_map(EncodeFn enc, CUtensorMap* map, const void* base, uint64_t rows, ui
   return ZT_OK;
 }
 
+// A 16-column bf16 K-slab [rows, 16]: box {16, 128}, 32-byte swizzle.
+int make_ext_map(EncodeFn enc, CUtensorMap* map, const void* base, uint64_t rows) {
+  const cuuint64_t dims[2] = {16, rows};
+  const cuuint64_t strides[1] = {32};
+  const cuuint32_t box[2] = {16, kHalfRows};
+  const cuuint32_t estr[2] = {1, 1};
+  if (enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return zt::set_error(ZT_ERR_CUDA, "eggroll: cuTensorMapEncodeTiled (K-slab) failed");
+  return ZT_OK;
+}
+
 int make_out_map(EncodeFn enc, CUtensorMap* map, void* base, uint64_t rows, uint64_t cols) {
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {cols * 2};
@@ -784,20 +878,17 @@ int prepare_kernels() {
   if (int rc = zt::check_cuda(cudaFuncSetAttribute(eggroll_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    (int)kSmemBytes), "eggroll: shared memory attribute"))
     return rc;
-  if (int rc = zt::check_cuda(cudaFuncSetAttribute(eggroll_gemm_pair_kernel<false>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes2),
-                              "eggroll: shared memory attribute (pair)"))
-    return rc;
-  if (int rc = zt::check_cuda(cudaFuncSetAttribute(eggroll_gemm_pair_kernel<true>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes2),
-                              "eggroll: shared memory attribute (gated pair)"))
-    return rc;
+  for (auto fn : {eggroll_gemm_pair_kernel<false, false>, eggroll_gemm_pair_kernel<true, false>,
+                  eggroll_gemm_pair_kernel<false, true>, eggroll_gemm_pair_kernel<true, true>})
+    if (int rc = zt::check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes2),
+                                "eggroll: shared memory attribute (pair)"))
+      return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * (unsigned)(zt::sm_count() / 2));
   cfg.blockDim = dim3(kThreadsEgg);
   cfg.dynamicSmemBytes = kSmemBytes2;
   int n = 0;
-  if (int rc = zt::check_cuda(cudaOccupancyMaxActiveClusters(&n, eggroll_gemm_pair_kernel<false>, &cfg),
+  if (int rc = zt::check_cuda(cudaOccupancyMaxActiveClusters(&n, eggroll_gemm_pair_kernel<false, false>, &cfg),
                               "eggroll: cudaOccupancyMaxActiveClusters"))
     return rc;
   if (n <= 0) return zt::set_error(ZT_ERR_CUDA, "eggroll: no CTA pair fits on this GPU");
@@ -807,13 +898,16 @@ int prepare_kernels() {
 }
 
 template <bool GATED>
-int launch_pair(const EggParams& P, cudaStream_t s) {
+int launch_pair(const EggParams& P, bool ext, cudaStream_t s) {
   int dev = 0;
   if (int rc = zt::check_cuda(cudaGetDevice(&dev), "eggroll: cudaGetDevice")) return rc;
   const int max_clusters = g_max_pairs[dev];
   const int tiles = (P.m_blocks / 2) * P.n_blocks;
   const int clusters = tiles < max_clusters ? tiles : max_clusters;
-  eggroll_gemm_pair_kernel<GATED><<<2 * clusters, kThreadsEgg, kSmemBytes2, s>>>(P);
+  if (ext)
+    eggroll_gemm_pair_kernel<GATED, true><<<2 * clusters, kThreadsEgg, kSmemBytes2, s>>>(P);
+  else
+    eggroll_gemm_pair_kernel<GATED, false><<<2 * clusters, kThreadsEgg, kSmemBytes2, s>>>(P);
   return zt::check_cuda(cudaGetLastError(), GATED ? "eggroll: gated gemm launch" : "eggroll: gemm launch (pair)");
 }
 
@@ -825,8 +919,11 @@ int zt_eggroll_linear(const zt_eggroll_args* args, void* stream) {
   zt::clear_error();
   if (!args) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: null args");
   const zt_eggroll_args& A = *args;
-  if (!A.x || !A.w || !A.a || (!A.b && !A.xb_ready) || !A.sigma || !A.xb || !A.y)
+  const bool ext = A.x_ext && A.w_ext;
+  if (!A.x || !A.w || !A.y || (!ext && (!A.a || (!A.b && !A.xb_ready) || !A.sigma || !A.xb)))
     return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: null pointer");
+  if (ext && (A.m % 256 || A.rows_per_member % 256))
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: the K-slab form needs M and rows_per_member % 256 == 0");
   if (A.rank != 4) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: rank must be 4");
   if (A.m <= 0 || A.n <= 0 || A.k <= 0) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: empty shape");
   if (A.m % kBM || A.n % kBN || A.k % kBK)
@@ -835,7 +932,8 @@ int zt_eggroll_linear(const zt_eggroll_args* args, void* stream) {
     return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: rows_per_member must divide M and be a multiple of 128");
   if (A.m > (int64_t)INT32_MAX || A.n > (int64_t)INT32_MAX || A.k > (int64_t)INT32_MAX)
     return zt::set_error(ZT_ERR_LIMIT, "zt_eggroll_linear: dimension above 2^31-1");
-  for (const void* p : {A.x, A.w, (const void*)A.a, (const void*)A.b, (const void*)A.xb, (const void*)A.y})
+  for (const void* p : {A.x, A.w, (const void*)A.a, (const void*)A.b, (const void*)A.xb, (const void*)A.y, A.x_ext,
+                        A.w_ext})
     if (((uintptr_t)p & 15) != 0) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_linear: pointers must be 16-byte aligned");
   EncodeFn enc = nullptr;
   if (int rc = get_encode(&enc)) return rc;
@@ -846,6 +944,10 @@ int zt_eggroll_linear(const zt_eggroll_args* args, void* stream) {
   if (int rc = make_map(enc, &P.tmap_w, A.w, (uint64_t)A.n, (uint64_t)A.k, pair ? kHalfRows : kBN)) return rc;
   if (pair)
     if (int rc = make_out_map(enc, &P.tmap_y, A.y, (uint64_t)A.m, (uint64_t)A.n)) return rc;
+  if (ext) {
+    if (int rc = make_ext_map(enc, &P.tmap_xe, A.x_ext, (uint64_t)A.m)) return rc;
+    if (int rc = make_ext_map(enc, &P.tmap_we, A.w_ext, (uint64_t)(A.m / A.rows_per_member) * (uint64_t)A.n)) return rc;
+  }
   P.a = A.a;
   P.sigma = A.sigma;
   P.xb = A.xb;
@@ -859,13 +961,13 @@ int zt_eggroll_linear(const zt_eggroll_args* args, void* stream) {
   P.n = (int32_t)A.n;
   P.rows_per_member = A.rows_per_member;
   cudaStream_t s = zt::as_stream(stream);
-  if (!A.xb_ready) {  // m % 128 == 0 and rows_per_member % 128 == 0: each 64-row block lies in one member
+  if (!A.xb_ready && !ext) {  // m % 128 == 0 and rows_per_member % 128 == 0: each 64-row block lies in one member
     const float* bb[1] = {A.b};
     float* xx[1] = {A.xb};
     if (int rc = launch_xb(A.x, bb, xx, 1, A.m, A.k, A.rows_per_member, s)) return rc;
   }
   if (int rc = prepare_kernels()) return rc;
-  if (pair) return launch_pair<false>(P, s);
+  if (pair) return launch_pair<false>(P, ext, s);
   const int tiles = P.m_blocks * P.n_blocks;
   const int grid = tiles < zt::sm_count() ? tiles : zt::sm_count();
   eggroll_gemm_kernel<<<grid, kThreadsEgg, kSmemBytes, s>>>(P);
@@ -876,9 +978,12 @@ int zt_eggroll_gated(const zt_eggroll_gated_args* args, void* stream) {
   zt::clear_error();
   if (!args) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_gated: null args");
   const zt_eggroll_gated_args& A = *args;
-  if (!A.x || !A.w_gate || !A.w_up || !A.a_gate || !A.a_up || !A.sigma_gate || !A.sigma_up || !A.xb_gate ||
-      !A.xb_up || !A.y)
+  const bool ext = A.x_ext && A.w_ext_gate && A.w_ext_up;
+  if (!A.x || !A.w_gate || !A.w_up || !A.y ||
+      (!ext && (!A.a_gate || !A.a_up || !A.sigma_gate || !A.sigma_up || !A.xb_gate || !A.xb_up)))
     return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_gated: null pointer");
+  if (ext && A.rows_per_member % 256)
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_gated: the K-slab form needs rows_per_member % 256 == 0");
   if (A.rank != 4) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_gated: rank must be 4");
   if (A.m <= 0 || A.n <= 0 || A.k <= 0) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_gated: empty shape");
   if (A.m % 256 || A.n % 128 || A.k % kBK)
@@ -888,7 +993,7 @@ int zt_eggroll_gated(const zt_eggroll_gated_args* args, void* stream) {
   if (A.m > (int64_t)INT32_MAX || A.n > (int64_t)INT32_MAX || A.k > (int64_t)INT32_MAX)
     return zt::set_error(ZT_ERR_LIMIT, "zt_eggroll_gated: dimension above 2^31-1");
   for (const void* p : {A.x, A.w_gate, A.w_up, (const void*)A.a_gate, (const void*)A.a_up, (const void*)A.xb_gate,
-                        (const void*)A.xb_up, (const void*)A.y})
+                        (const void*)A.xb_up, (const void*)A.y, A.x_ext, A.w_ext_gate, A.w_ext_up})
     if (((uintptr_t)p & 15) != 0) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_gated: pointers must be 16-byte aligned");
   EncodeFn enc = nullptr;
   if (int rc = get_encode(&enc)) return rc;
@@ -897,6 +1002,12 @@ int zt_eggroll_gated(const zt_eggroll_gated_args* args, void* stream) {
   if (int rc = make_map(enc, &P.tmap_w, A.w_gate, (uint64_t)A.n, (uint64_t)A.k, kHalfRows)) return rc;
   if (int rc = make_map(enc, &P.tmap_w2, A.w_up, (uint64_t)A.n, (uint64_t)A.k, kHalfRows)) return rc;
   if (int rc = make_out_map(enc, &P.tmap_y, A.y, (uint64_t)A.m, (uint64_t)A.n)) return rc;
+  if (ext) {
+    const uint64_t wrows = (uint64_t)(A.m / A.rows_per_member) * (uint64_t)A.n;
+    if (int rc = make_ext_map(enc, &P.tmap_xe, A.x_ext, (uint64_t)A.m)) return rc;
+    if (int rc = make_ext_map(enc, &P.tmap_we, A.w_ext_gate, wrows)) return rc;
+    if (int rc = make_ext_map(enc, &P.tmap_we2, A.w_ext_up, wrows)) return rc;
+  }
   P.a = A.a_gate;
   P.sigma = A.sigma_gate;
   P.xb = A.xb_gate;
@@ -910,7 +1021,7 @@ int zt_eggroll_gated(const zt_eggroll_gated_args* args, void* stream) {
   P.n = (int32_t)A.n;
   P.rows_per_member = A.rows_per_member;
   if (int rc = prepare_kernels()) return rc;
-  return launch_pair<true>(P, zt::as_stream(stream));
+  return launch_pair<true>(P, ext, zt::as_stream(stream));
 }
 
 int zt_eggroll_xb(const zt_eggroll_xb_args* args, void* stream) {
@@ -925,10 +1036,15 @@ int zt_eggroll_xb(const zt_eggroll_xb_args* args, void* stream) {
   if (A.m > (int64_t)INT32_MAX * kXbRows || A.k > (int64_t)INT32_MAX)
     return zt::set_error(ZT_ERR_LIMIT, "zt_eggroll_xb: dimension too large");
   if (!A.x || ((uintptr_t)A.x & 15)) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: x null or not 16-byte aligned");
-  for (int i = 0; i < A.n_seg; ++i)
-    if (!A.b[i] || !A.xb[i] || ((uintptr_t)A.b[i] & 15) || ((uintptr_t)A.xb[i] & 15))
-      return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: b/xb null or not 16-byte aligned");
-  return launch_xb(A.x, A.b, A.xb, A.n_seg, A.m, A.k, A.rows_per_member, zt::as_stream(stream));
+  for (int i = 0; i < A.n_seg; ++i) {
+    if (!A.b[i] || ((uintptr_t)A.b[i] & 15) || ((uintptr_t)A.xb[i] & 15))
+      return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: b null or b/xb not 16-byte aligned");
+    if (!A.xb[i] && !A.xe[i]) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: a set with neither xb nor xe");
+    if (A.xe[i] && (!A.sigma[i] || ((uintptr_t)A.xe[i] & 15) || A.xe_slot[i] < 0 || A.xe_slot[i] > 2))
+      return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: xe needs sigma, 16-byte alignment and a slot 0-2");
+  }
+  return launch_xb(A.x, A.b, A.xb, A.n_seg, A.m, A.k, A.rows_per_member, zt::as_stream(stream), A.sigma, A.xe,
+                   A.xe_slot);
 }
 
 int zt_eggroll_take_error(int32_t* code) {

@@ -24,15 +24,22 @@ __device__ __forceinline__ void gram_add(float g[kGram], const float v[4]) {
   g[9] = fmaf(v[3], v[3], g[9]);
 }
 
+__device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
+  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lo)) |
+         ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi)) << 16);
+}
+
 // Pair j (blockIdx.y) draws P (n x 4, stream order o*4 + r under key ka[j]) and Psi
 // (4 x k, stream order r*k + t under key kb[j]), rounds both to the parameter dtype and
 // writes A = P and B = Psi^T for both members 2j and 2j+1. Items 0..n-1 are rows of P,
 // items n..n+k-1 columns of Psi. Each block also writes its partial Gram matrices P^T P
-// and Psi Psi^T (fixed-order block reduction) for the normalisation.
+// and Psi Psi^T (fixed-order block reduction) for the normalisation. With a_ext, A is also
+// written in bf16 as the GEMM's rank-4 K-slab operand (exact: P is bf16-valued).
 template <int DT>
 __global__ void __launch_bounds__(kFacThreads) factor_kernel(const __grid_constant__ PairKeys K, int32_t n, int32_t k,
                                                               float4* __restrict__ a, float4* __restrict__ b,
-                                                              float* __restrict__ part) {
+                                                              float* __restrict__ part, uint4* __restrict__ a_ext,
+                                                              int32_t ext_slot) {
   const int j = blockIdx.y;
   const uint32_t ka = K.ka[j], kb = K.kb[j];
   const int items = n + k;
@@ -49,6 +56,16 @@ __global__ void __launch_bounds__(kFacThreads) factor_kernel(const __grid_consta
       const float4 f = make_float4(v[0], v[1], v[2], v[3]);
       a0[i] = f;
       a0[i + n] = f;
+      if (a_ext) {  // 32-byte K-slab row: [A, A, 0 x 8] or [0 x 8, A, A]
+        const uint2 av = make_uint2(bf16x2(v[0], v[1]), bf16x2(v[2], v[3]));
+        const uint4 nz = make_uint4(av.x, av.y, av.x, av.y), z = make_uint4(0u, 0u, 0u, 0u);
+        uint4* r0 = a_ext + 2 * ((size_t)(2 * j) * n + i);
+        uint4* r1 = r0 + 2 * (size_t)n;
+        r0[0] = ext_slot ? z : nz;
+        r0[1] = ext_slot ? nz : z;
+        r1[0] = ext_slot ? z : nz;
+        r1[1] = ext_slot ? nz : z;
+      }
       gram_add(gp, v);
     } else {
       const int t = i - n;
@@ -275,18 +292,21 @@ int zt_eggroll_factors(const zt_eggroll_factor_args* args, void* stream) {
   float4* a4 = reinterpret_cast<float4*>(A.a);
   float4* b4 = reinterpret_cast<float4*>(A.b);
   const float sqrt_numel = (float)sqrt((double)A.n * (double)A.k);
+  if (A.a_ext && (!aligned16(A.a_ext) || A.ext_slot < 0 || A.ext_slot > 1))
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_factors: a_ext not 16-byte aligned or ext_slot not 0/1");
+  uint4* ae = static_cast<uint4*>(A.a_ext);
   const unsigned sgrid = (unsigned)((A.pairs + 127) / 128);
   switch (A.dtype) {
     case ZT_F32:
-      factor_kernel<ZT_F32><<<grid, kFacThreads, 0, s>>>(K, (int32_t)A.n, (int32_t)A.k, a4, b4, A.work);
+      factor_kernel<ZT_F32><<<grid, kFacThreads, 0, s>>>(K, (int32_t)A.n, (int32_t)A.k, a4, b4, A.work, ae, A.ext_slot);
       factor_scale_kernel<ZT_F32><<<sgrid, 128, 0, s>>>(A.work, A.pairs, (int32_t)nblk, sqrt_numel, A.sigma, A.normalize, A.scale);
       break;
     case ZT_BF16:
-      factor_kernel<ZT_BF16><<<grid, kFacThreads, 0, s>>>(K, (int32_t)A.n, (int32_t)A.k, a4, b4, A.work);
+      factor_kernel<ZT_BF16><<<grid, kFacThreads, 0, s>>>(K, (int32_t)A.n, (int32_t)A.k, a4, b4, A.work, ae, A.ext_slot);
       factor_scale_kernel<ZT_BF16><<<sgrid, 128, 0, s>>>(A.work, A.pairs, (int32_t)nblk, sqrt_numel, A.sigma, A.normalize, A.scale);
       break;
     default:
-      factor_kernel<ZT_F16><<<grid, kFacThreads, 0, s>>>(K, (int32_t)A.n, (int32_t)A.k, a4, b4, A.work);
+      factor_kernel<ZT_F16><<<grid, kFacThreads, 0, s>>>(K, (int32_t)A.n, (int32_t)A.k, a4, b4, A.work, ae, A.ext_slot);
       factor_scale_kernel<ZT_F16><<<sgrid, 128, 0, s>>>(A.work, A.pairs, (int32_t)nblk, sqrt_numel, A.sigma, A.normalize, A.scale);
       break;
   }

@@ -65,12 +65,18 @@ class _Population:
     def keys(self, idx: int) -> list[int]:
         return [_key(s, self.n_params, idx) for s in self.pair_seeds]
 
-    def low_rank(self, idx: int, out_f: int, in_f: int, device, dtype=torch.bfloat16):
+    def use_ext(self, rows: int) -> bool:
+        """Whether the rank-4 terms run as a tensor-core K-slab: needs 256-row GEMM tiles
+        that each lie inside one member."""
+        return rows % 256 == 0 and self.rows_per_member % 256 == 0
+
+    def low_rank(self, idx: int, out_f: int, in_f: int, device, dtype=torch.bfloat16, ext_slot=None):
         """A [members, out, 4], B [members, in, 4] (fp32 holding dtype-rounded values) and
         the signed scale [members] of tensor idx for the current chunk (zt_eggroll_factors:
-        one launch for the factors of every pair plus one for the normalisation)."""
+        one launch for the factors of every pair plus one for the normalisation); with
+        ext_slot also A's bf16 K-slab rows."""
         return K.eggroll_factors(self.keys(idx + 2 * self.n_params), self.keys(idx + self.n_params), out_f, in_f,
-                                 self.cfg.sigma, device, dtype, self.cfg.normalize)
+                                 self.cfg.sigma, device, dtype, self.cfg.normalize, ext_slot=ext_slot)
 
 
 class PopLinear(nn.Module):
@@ -81,27 +87,42 @@ class PopLinear(nn.Module):
         self.weight = base.weight
         self.idx, self.pop = idx, pop
 
-    def factors(self, device):
+    def factors(self, device, ext_slot=None):
         out_f, in_f = self.weight.shape
-        return self.pop.low_rank(self.idx, out_f, in_f, device, self.weight.dtype)
+        return self.pop.low_rank(self.idx, out_f, in_f, device, self.weight.dtype, ext_slot)
 
-    def forward(self, x, fac=None, xb=None):
-        """fac = (A, B, scale) and xb = X B from a shared zt_eggroll_xb call, or None."""
+    def forward(self, x, fac=None, xb=None, xe=None):
+        """fac = the factors and xb = X B (fp32) or xe = its K-slab rows, from a shared
+        zt_eggroll_xb call over x; or None to compute them here."""
         shp = x.shape
         x2 = x.reshape(-1, shp[-1]).contiguous()
         out_f = self.weight.shape[0]
-        A, B, sig = fac if fac is not None else self.factors(x.device)
-        y = K.eggroll_linear(x2, self.weight.data, A, B, sig, self.pop.rows_per_member, xb=xb,
-                             xb_ready=xb is not None)
+        rpm = self.pop.rows_per_member
+        if fac is None:
+            ext = self.pop.use_ext(x2.shape[0])
+            fac = self.factors(x.device, 0 if ext else None)
+            if ext:
+                xe = K.eggroll_xb_ext(x2, [fac[1]], [fac[2]], [0], rpm)[0]
+        if xe is not None:
+            y = K.eggroll_linear(x2, self.weight.data, fac[0], None, fac[2], rpm, x_ext=xe, w_ext=fac[3])
+        else:
+            y = K.eggroll_linear(x2, self.weight.data, fac[0], fac[1], fac[2], rpm, xb=xb, xb_ready=xb is not None)
         return y.view(*shp[:-1], out_f)
 
 
-def _shared_input(x, linears, pop):
-    """Factors of every linear reading x and their X B in one pass over x."""
+def _shared_input(x, linears, pop, slots=None):
+    """Factors of every linear reading x and their X B in one pass over x: fp32 X B, or
+    the K-slab rows when the tiles allow it (slots as eggroll_xb_ext takes them; slot 2,
+    the second half of a shared row, pairs with A_ext slot 1)."""
     x2 = x.reshape(-1, x.shape[-1]).contiguous()
+    if pop.use_ext(x2.shape[0]):
+        slots = slots or [0] * len(linears)
+        facs = [lin.factors(x.device, 1 if sl == 2 else 0) for lin, sl in zip(linears, slots)]
+        xes = K.eggroll_xb_ext(x2, [f[1] for f in facs], [f[2] for f in facs], slots, pop.rows_per_member)
+        return x2, facs, [None] * len(linears), xes
     facs = [lin.factors(x.device) for lin in linears]
     xbs = K.eggroll_xb(x2, [f[1] for f in facs], pop.rows_per_member)
-    return x2, facs, xbs
+    return x2, facs, xbs, [None] * len(linears)
 
 
 class PopRMSNorm(nn.Module):
@@ -138,8 +159,8 @@ class PopAttention(nn.Module):
         hd = self.head_dim
         projs = (self.q_proj, self.k_proj, self.v_proj)
         if all(isinstance(p, PopLinear) for p in projs):
-            x2, facs, xbs = _shared_input(hidden_states, projs, projs[0].pop)
-            q, k, v = (p(x2, f, xb).view(bsz, T, -1) for p, f, xb in zip(projs, facs, xbs))
+            x2, facs, xbs, xes = _shared_input(hidden_states, projs, projs[0].pop)
+            q, k, v = (p(x2, f, xb, xe).view(bsz, T, -1) for p, f, xb, xe in zip(projs, facs, xbs, xes))
         else:
             q, k, v = (p(hidden_states) for p in projs)
         cos, sin = position_embeddings
@@ -168,12 +189,15 @@ class PopMLP(nn.Module):
     def forward(self, x):
         projs = (self.gate_proj, self.up_proj)
         if all(isinstance(p, PopLinear) for p in projs):
-            x2, facs, xbs = _shared_input(x, projs, projs[0].pop)
-            if x2.shape[0] % 256 == 0:   # gate, up and SwiGLU in one GEMM (zt_eggroll_gated)
+            pop = projs[0].pop
+            rows = x.numel() // x.shape[-1]
+            if rows % 256 == 0:   # gate, up and SwiGLU in one GEMM (zt_eggroll_gated)
+                x2, facs, xbs, xes = _shared_input(x, projs, pop, slots=[1, 2])
                 h = K.eggroll_gated(x2, self.gate_proj.weight.data, self.up_proj.weight.data, facs[0], facs[1],
-                                    xbs[0], xbs[1], projs[0].pop.rows_per_member)
+                                    xbs[0], xbs[1], pop.rows_per_member, x_ext=xes[0])
                 return self.down_proj(h.view(*x.shape[:-1], -1))
-            g, u = (p(x2, f, xb).view(*x.shape[:-1], -1) for p, f, xb in zip(projs, facs, xbs))
+            x2, facs, xbs, xes = _shared_input(x, projs, pop)
+            g, u = (p(x2, f, xb, xe).view(*x.shape[:-1], -1) for p, f, xb, xe in zip(projs, facs, xbs, xes))
         else:
             g, u = (p(x) for p in projs)
         return self.down_proj(K.eggroll_swiglu(g, u))

@@ -230,14 +230,34 @@ class ParamTable:
 
 def eggroll_linear(x: torch.Tensor, w: torch.Tensor, a: torch.Tensor, b: torch.Tensor | None, sigma: torch.Tensor,
                    rows_per_member: int, out: torch.Tensor | None = None, xb: torch.Tensor | None = None,
-                   xb_ready: bool = False) -> torch.Tensor:
+                   xb_ready: bool = False, x_ext: torch.Tensor | None = None,
+                   w_ext: torch.Tensor | None = None) -> torch.Tensor:
     """EGGROLL population linear layer (zt_eggroll_linear):
     Y = X W^T + sigma_i (X B_i) A_i^T for the rows of member i.
 
     x [M, K] bf16, w [N, K] bf16, a [members, N, 4] fp32, b [members, K, 4] fp32,
     sigma [members] fp32; returns Y [M, N] bf16. M % 128, N % 256, K % 64 must be 0 and
     rows_per_member a multiple of 128 dividing M. With xb_ready, xb already holds X B_i
-    (from eggroll_xb) and b may be None."""
+    (from eggroll_xb) and b may be None. With x_ext (eggroll_xb_ext) and w_ext (the
+    factors' A_ext) the rank-4 term runs on the tensor cores as a K = 16 slab."""
+    if (x_ext is None) != (w_ext is None):
+        raise ValueError("x_ext and w_ext go together")
+    if x_ext is not None:
+        M, K = x.shape
+        N = w.shape[0]
+        for t, name in ((x, "x"), (w, "w"), (x_ext, "x_ext"), (w_ext, "w_ext")):
+            _check_cuda(t, name)
+            if not t.is_contiguous() or t.dtype != torch.bfloat16:
+                raise ValueError(f"{name} must be contiguous bf16")
+        if w.shape[1] != K or x_ext.shape != (M, 16) or w_ext.shape != (M // rows_per_member, N, 16):
+            raise ValueError("inconsistent shapes")
+        if out is None:
+            out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+        args = L.ZtEggrollArgs(x.data_ptr(), w.data_ptr(), None, None, None, None, out.data_ptr(), M, N, K,
+                               rows_per_member, 4, 0, 0, x_ext.data_ptr(), w_ext.data_ptr())
+        with torch.cuda.device(x.device):
+            L.check(L.load().zt_eggroll_linear(ctypes.byref(args), _stream_ptr(x.device)), "zt_eggroll_linear")
+        return out
     if xb_ready and xb is None:
         raise ValueError("xb_ready needs xb")
     named = [(x, "x"), (w, "w"), (a, "a"), (sigma, "sigma")] + ([] if xb_ready else [(b, "b")])
@@ -268,6 +288,44 @@ def eggroll_linear(x: torch.Tensor, w: torch.Tensor, a: torch.Tensor, b: torch.T
     return out
 
 
+def eggroll_xb_ext(x: torch.Tensor, bs: list, scales: list, slots: list, rows_per_member: int) -> list:
+    """K-slab rows of sigma_i X B_s (zt_eggroll_xb with xe outputs): slot 0 gives a set its
+    own [M, 16] bf16 buffer [hi, lo, 0 x 8]; slots 1 and 2 share one buffer (columns 0-7
+    and 8-15, the gated gate/up form). Returns one buffer per set (shared ones repeated)."""
+    if not 1 <= len(bs) <= 3 or len(scales) != len(bs) or len(slots) != len(bs):
+        raise ValueError("one to three factor sets, with a scale and a slot each")
+    _check_cuda(x, "x")
+    if x.dtype != torch.bfloat16 or not x.is_contiguous() or x.dim() != 2:
+        raise ValueError("x must be a contiguous bf16 matrix")
+    M, K = x.shape
+    shared = None
+    xes = []
+    for b, sc, slot in zip(bs, scales, slots):
+        _check_cuda(b, "b")
+        if b.dtype != torch.float32 or not b.is_contiguous() or b.shape != (M // rows_per_member, K, 4):
+            raise ValueError("each b must be a contiguous fp32 [members, K, 4] tensor")
+        if sc.dtype != torch.float32 or sc.shape != (M // rows_per_member,):
+            raise ValueError("each scale must be fp32 [members]")
+        if slot == 0:
+            xes.append(torch.empty((M, 16), dtype=torch.bfloat16, device=x.device))
+        elif slot in (1, 2):
+            if shared is None:
+                shared = torch.empty((M, 16), dtype=torch.bfloat16, device=x.device)
+            xes.append(shared)
+        else:
+            raise ValueError("slot must be 0, 1 or 2")
+    n = len(bs)
+    pad = [0] * (3 - n)
+    args = L.ZtEggrollXbArgs(x.data_ptr(), (ctypes.c_void_p * 3)(*([b.data_ptr() for b in bs] + pad)),
+                             (ctypes.c_void_p * 3)(*([0] * 3)), M, K, n, rows_per_member,
+                             (ctypes.c_void_p * 3)(*([sc.data_ptr() for sc in scales] + pad)),
+                             (ctypes.c_void_p * 3)(*([t.data_ptr() for t in xes] + pad)),
+                             (ctypes.c_int32 * 3)(*(list(slots) + pad)), 0)
+    with torch.cuda.device(x.device):
+        L.check(L.load().zt_eggroll_xb(ctypes.byref(args), _stream_ptr(x.device)), "zt_eggroll_xb")
+    return xes
+
+
 def eggroll_xb(x: torch.Tensor, bs: list, rows_per_member: int) -> list:
     """X B_s for 1-3 factor sets sharing x [M, K] bf16 (zt_eggroll_xb): returns one
     [M, 4] fp32 tensor per b in bs ([members, K, 4] fp32 each)."""
@@ -285,18 +343,24 @@ def eggroll_xb(x: torch.Tensor, bs: list, rows_per_member: int) -> list:
     bp = [b.data_ptr() for b in bs] + [0] * (3 - len(bs))
     xp = [t.data_ptr() for t in xbs] + [0] * (3 - len(bs))
     args = L.ZtEggrollXbArgs(x.data_ptr(), (ctypes.c_void_p * 3)(*bp), (ctypes.c_void_p * 3)(*xp), M, K, len(bs),
-                             rows_per_member)
+                             rows_per_member, (ctypes.c_void_p * 3)(0, 0, 0), (ctypes.c_void_p * 3)(0, 0, 0),
+                             (ctypes.c_int32 * 3)(0, 0, 0), 0)
     with torch.cuda.device(x.device):
         L.check(L.load().zt_eggroll_xb(ctypes.byref(args), _stream_ptr(x.device)), "zt_eggroll_xb")
     return xbs
 
 
 def eggroll_gated(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, fac_gate, fac_up, xb_gate, xb_up,
-                  rows_per_member: int) -> torch.Tensor:
+                  rows_per_member: int, x_ext: torch.Tensor | None = None) -> torch.Tensor:
     """bf16(bf16(silu(G)) * U) for the population rows x [M, K] (zt_eggroll_gated):
     G, U the EGGROLL linear outputs of the gate and up projections. fac_* = (A, B, scale)
-    from eggroll_factors; xb_* = X B from eggroll_xb. M % 256 == 0."""
-    for t, name in ((x, "x"), (w_gate, "w_gate"), (w_up, "w_up"), (xb_gate, "xb_gate"), (xb_up, "xb_up")):
+    from eggroll_factors; xb_* = X B from eggroll_xb. M % 256 == 0. With x_ext (the shared
+    slot-1/2 buffer of eggroll_xb_ext) the factors carry A_ext (slots 0 and 1) and both
+    rank-4 terms run on the tensor cores; xb_* may then be None."""
+    named = [(x, "x"), (w_gate, "w_gate"), (w_up, "w_up")]
+    named += [(x_ext, "x_ext"), (fac_gate[3], "gate A_ext"), (fac_up[3], "up A_ext")] if x_ext is not None else \
+        [(xb_gate, "xb_gate"), (xb_up, "xb_up")]
+    for t, name in named:
         _check_cuda(t, name)
         if not t.is_contiguous():
             raise ValueError(f"{name} must be contiguous")
@@ -305,13 +369,18 @@ def eggroll_gated(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, fac
     if w_up.shape != (N, K) or w_gate.shape[1] != K:
         raise ValueError("inconsistent shapes")
     members = M // rows_per_member
-    for a, _, sg in (fac_gate, fac_up):
-        if a.shape != (members, N, 4) or sg.shape != (members,):
+    for fac in (fac_gate, fac_up):
+        if fac[0].shape != (members, N, 4) or fac[2].shape != (members,):
             raise ValueError("inconsistent factor shapes")
+        if x_ext is not None and (len(fac) < 4 or fac[3].shape != (members, N, 16)):
+            raise ValueError("the K-slab form needs the factors' A_ext")
     y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    ext = x_ext is not None
     args = L.ZtEggrollGatedArgs(x.data_ptr(), w_gate.data_ptr(), w_up.data_ptr(), fac_gate[0].data_ptr(),
-                                fac_up[0].data_ptr(), fac_gate[2].data_ptr(), fac_up[2].data_ptr(), xb_gate.data_ptr(),
-                                xb_up.data_ptr(), y.data_ptr(), M, N, K, rows_per_member, 4)
+                                fac_up[0].data_ptr(), fac_gate[2].data_ptr(), fac_up[2].data_ptr(),
+                                None if ext else xb_gate.data_ptr(), None if ext else xb_up.data_ptr(), y.data_ptr(),
+                                M, N, K, rows_per_member, 4, x_ext.data_ptr() if ext else None,
+                                fac_gate[3].data_ptr() if ext else None, fac_up[3].data_ptr() if ext else None)
     with torch.cuda.device(x.device):
         L.check(L.load().zt_eggroll_gated(ctypes.byref(args), _stream_ptr(x.device)), "zt_eggroll_gated")
     return y
@@ -333,10 +402,11 @@ def _keys_array(keys):
 
 
 def eggroll_factors(keys_a: list[int], keys_b: list[int], n: int, k: int, sigma: float, device,
-                    dtype: torch.dtype = torch.bfloat16, normalize: bool = True):
+                    dtype: torch.dtype = torch.bfloat16, normalize: bool = True, ext_slot: int | None = None):
     """Rank-4 factors of an [n, k] tensor for antithetic pairs (zt_eggroll_factors):
     returns A [2p, n, 4], B [2p, k, 4] (fp32 holding dtype-rounded values) and the signed
-    scale [2p] (+sigma c_j, -sigma c_j), ready for eggroll_linear."""
+    scale [2p] (+sigma c_j, -sigma c_j), ready for eggroll_linear. With ext_slot (0 or 1)
+    also A_ext [2p, n, 16] bf16, the GEMM's K-slab operand, as a fourth element."""
     pairs = len(keys_a)
     if pairs != len(keys_b) or pairs == 0:
         raise ValueError("keys_a and keys_b must be non-empty and of equal length")
@@ -347,13 +417,15 @@ def eggroll_factors(keys_a: list[int], keys_b: list[int], n: int, k: int, sigma:
     b = torch.empty((2 * pairs, k, 4), dtype=torch.float32, device=device)
     scale = torch.empty(2 * pairs, dtype=torch.float32, device=device)
     work = torch.empty(pairs * L.ZT_EGGROLL_FACTOR_WORK_FLOATS, dtype=torch.float32, device=device)
+    a_ext = None if ext_slot is None else torch.empty((2 * pairs, n, 16), dtype=torch.bfloat16, device=device)
     ka, kb = _keys_array(keys_a), _keys_array(keys_b)
     args = L.ZtEggrollFactorArgs(ctypes.addressof(ka), ctypes.addressof(kb), pairs, 4, n, k, _DT[dtype],
                                  1 if normalize else 0, float(sigma), 0, a.data_ptr(), b.data_ptr(), scale.data_ptr(),
-                                 work.data_ptr())
+                                 work.data_ptr(), a_ext.data_ptr() if a_ext is not None else None,
+                                 int(ext_slot or 0), 0)
     with torch.cuda.device(device):
         L.check(L.load().zt_eggroll_factors(ctypes.byref(args), _stream_ptr(device)), "zt_eggroll_factors")
-    return a, b, scale
+    return (a, b, scale) if a_ext is None else (a, b, scale, a_ext)
 
 
 def eggroll_rmsnorm(x: torch.Tensor, w: torch.Tensor, keys: list[int], sigma: float, eps: float,
