@@ -281,6 +281,11 @@ typedef struct zt_eggroll_xb_args {
   void* xe[3];            /* per set: optional [m, 16] bf16 K-slab rows of sigma_i X B (NULL: skip) */
   int32_t xe_slot[3];     /* 0: write [hi, lo, 0 x 8]; 1: write [hi, lo] to columns 0-7; 2: to 8-15 */
   int32_t reserved;
+  /* Optional: all sets' B_s^T as one bf16 [members, 16, k] tensor (set s in rows 4s..4s+3,
+   * the other rows zero; zt_eggroll_factors.b_ext). Then X B runs on the tensor cores
+   * (N = 16 per 128-row tile) and b[] is not read; needs m, rows_per_member % 128 == 0 and
+   * k % 64 == 0. */
+  const void* bt;
 } zt_eggroll_xb_args;
 
 ZT_API int zt_eggroll_xb(const zt_eggroll_xb_args* args, void* stream);
@@ -354,6 +359,11 @@ typedef struct zt_eggroll_factor_args {
                              rank-4 K-slab (see zt_eggroll_args.w_ext); NULL to skip */
   int32_t ext_slot;       /* a_ext row: 0 = [A, A, 0 x 8], 1 = [0 x 8, A, A] */
   int32_t reserved2;
+  void* b_ext;            /* optional out, rows of [2*pairs, 16, k] bf16: B^T written to rows
+                             b_ext_row .. b_ext_row+3 of each member (zt_eggroll_xb.bt); other
+                             rows untouched (the caller zeroes the buffer once); NULL to skip */
+  int32_t b_ext_row;      /* 0, 4 or 8 */
+  int32_t reserved3;
 } zt_eggroll_factor_args;
 
 ZT_API int zt_eggroll_factors(const zt_eggroll_factor_args* args, void* stream);

@@ -209,3 +209,32 @@ def test_ksliced_gated_matches_fp32_epilogue():
     d = (yk.float() - y32.float()).abs()
     assert bool((d <= 2.0 ** -7 * y32.float().abs() + 1e-3 * y32.float().abs().max()).all())
     assert float((d == 0).float().mean()) >= 0.98
+
+
+@pytest.mark.parametrize("M,K,T,nseg", [(512, 1024, 256, 3), (2048, 4096, 1024, 2), (256, 128, 128, 1)])
+def test_tensor_core_xb_matches_cuda_core_xb(M, K, T, nseg):
+    """X B on the tensor cores (B^T in bf16 from the factor kernel) against the CUDA-core pass:
+    fp32 accumulations of the same exact products in different orders (relative 1e-5 of
+    sum |x||b|); the K-slab rows it writes agree to ~2^-15."""
+    from zotitan_b200 import kernels as K_
+    members = M // T
+    bt = torch.zeros((members, 16, K), dtype=torch.bfloat16, device="cuda")
+    facs = [K_.eggroll_factors(list(range(s * 10 + 1, s * 10 + 1 + members // 2)),
+                               list(range(s * 10 + 50, s * 10 + 50 + members // 2)), 256, K, 1e-3, "cuda",
+                               ext_slot=0, b_ext=bt, b_ext_row=4 * s) for s in range(nseg)]
+    for s, f in enumerate(facs):
+        assert torch.equal(bt[:, 4 * s:4 * s + 4, :].float(), f[1].transpose(1, 2))
+    assert not bt[:, 4 * nseg:, :].any()
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    ref = K_.eggroll_xb(x, [f[1] for f in facs], T)
+    xes_cc = K_.eggroll_xb_ext(x, [f[1] for f in facs], [f[2] for f in facs], [0] * nseg, T)
+    xes_tc = K_.eggroll_xb_ext(x, [f[1] for f in facs], [f[2] for f in facs], [0] * nseg, T, bt=bt)
+    torch.cuda.synchronize()
+    assert K_.eggroll_take_error() == 0
+    for f, r, a_, b_ in zip(facs, ref, xes_cc, xes_tc):
+        scale = float((x.float().abs() @ f[1].abs().amax(0)).amax())
+        v_cc = a_[:, 0:4].float() + a_[:, 4:8].float()
+        v_tc = b_[:, 0:4].float() + b_[:, 4:8].float()
+        sig = f[2].repeat_interleave(T)[:, None].abs()
+        assert float((v_tc - v_cc).abs().max()) <= 1e-5 * scale * float(sig.max()) + 2 ** -14 * float(v_cc.abs().max())
+        assert not b_[:, 8:].any()

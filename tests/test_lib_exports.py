@@ -44,9 +44,9 @@ def test_struct_layouts_match_header(lib):
     assert ctypes.sizeof(L.ZtPlan) == 48
     assert ctypes.sizeof(L.ZtPassCfg) == 128 and L.ZtPassCfg.dev_vals.offset == 88 and L.ZtPassCfg.unit_begin.offset == 112
     assert ctypes.sizeof(L.ZtEggrollArgs) == 112 and L.ZtEggrollArgs.xb_ready.offset == 88
-    assert ctypes.sizeof(L.ZtEggrollXbArgs) == 144 and L.ZtEggrollXbArgs.xe_slot.offset == 128
+    assert ctypes.sizeof(L.ZtEggrollXbArgs) == 152 and L.ZtEggrollXbArgs.bt.offset == 144
     assert ctypes.sizeof(L.ZtEggrollGatedArgs) == 136 and L.ZtEggrollGatedArgs.x_ext.offset == 112
-    assert ctypes.sizeof(L.ZtEggrollFactorArgs) == 104 and L.ZtEggrollFactorArgs.a.offset == 56
+    assert ctypes.sizeof(L.ZtEggrollFactorArgs) == 120 and L.ZtEggrollFactorArgs.b_ext.offset == 104
     assert ctypes.sizeof(L.ZtEggrollNormArgs) == 72 and L.ZtEggrollNormArgs.m.offset == 40
     assert lib.zt_plan_workspace_bytes(0) == 8
     assert lib.zt_plan_workspace_bytes(3) == 256 + 8 * 4
@@ -106,7 +106,7 @@ def test_eggroll_companions_validate_before_launch(lib):
     import numpy as np
     keys = (ctypes.c_uint32 * 2)(1, 2)
     fa = L.ZtEggrollFactorArgs(ctypes.addressof(keys), ctypes.addressof(keys), 2, 3, 256, 256, L.ZT_BF16, 1, 1e-3, 0,
-                               16, 16, 16, 16, None, 0, 0)
+                               16, 16, 16, 16, None, 0, 0, None, 0, 0)
     assert lib.zt_eggroll_factors(ctypes.byref(fa), None) == L.ZT_ERR_INVALID and b"rank" in lib.zt_last_error()
     fa.rank, fa.pairs = 4, L.ZT_EGGROLL_MAX_PAIRS + 1
     assert lib.zt_eggroll_factors(ctypes.byref(fa), None) == L.ZT_ERR_LIMIT

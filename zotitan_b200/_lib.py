@@ -87,7 +87,7 @@ class ZtEggrollXbArgs(ctypes.Structure):
     _fields_ = [("x", ctypes.c_void_p), ("b", ctypes.c_void_p * 3), ("xb", ctypes.c_void_p * 3),
                 ("m", ctypes.c_int64), ("k", ctypes.c_int64), ("n_seg", ctypes.c_int32),
                 ("rows_per_member", ctypes.c_int32), ("sigma", ctypes.c_void_p * 3), ("xe", ctypes.c_void_p * 3),
-                ("xe_slot", ctypes.c_int32 * 3), ("reserved", ctypes.c_int32)]
+                ("xe_slot", ctypes.c_int32 * 3), ("reserved", ctypes.c_int32), ("bt", ctypes.c_void_p)]
 
 
 class ZtEggrollFactorArgs(ctypes.Structure):
@@ -95,7 +95,8 @@ class ZtEggrollFactorArgs(ctypes.Structure):
                 ("rank", ctypes.c_int32), ("n", ctypes.c_int64), ("k", ctypes.c_int64), ("dtype", ctypes.c_int32),
                 ("normalize", ctypes.c_int32), ("sigma", ctypes.c_float), ("reserved", ctypes.c_int32),
                 ("a", ctypes.c_void_p), ("b", ctypes.c_void_p), ("scale", ctypes.c_void_p), ("work", ctypes.c_void_p),
-                ("a_ext", ctypes.c_void_p), ("ext_slot", ctypes.c_int32), ("reserved2", ctypes.c_int32)]
+                ("a_ext", ctypes.c_void_p), ("ext_slot", ctypes.c_int32), ("reserved2", ctypes.c_int32),
+                ("b_ext", ctypes.c_void_p), ("b_ext_row", ctypes.c_int32), ("reserved3", ctypes.c_int32)]
 
 
 class ZtEggrollNormArgs(ctypes.Structure):

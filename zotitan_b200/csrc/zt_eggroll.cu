@@ -783,6 +783,149 @@ __global__ void __launch_bounds__(256, 1) eggroll_xb_kernel(const __nv_bfloat16*
     }
 }
 
+// ---- X B on the tensor cores (K-slab path) ---------------------------------------------
+//
+// One CTA per 128-row tile of one member: XB[128, 16] = X[tile, K] Bt[member]^T with
+// Bt [members, 16, K] bf16 (set s in rows 4s..4s+3), tcgen05.mma M = 128, N = 16 into 16
+// tensor-memory columns; X and Bt tiles arrive by TMA (128-byte swizzle) through a
+// 4-stage ring. The epilogue turns each set's 4 columns into K-slab rows
+// [hi, lo] of sigma_i X B (and fp32 X B if asked). X is read once for all sets, at HBM rate.
+constexpr int kXtStages = 4;
+constexpr uint32_t kXtA = 128 * kBK * 2;   // 16 KB of X
+constexpr uint32_t kXtB = 16 * kBK * 2;    // 2 KB of Bt
+constexpr uint32_t kXtStage = kXtA + 2048;  // 1024-aligned stages
+constexpr size_t kXtSmem = 1024 + kXtStages * kXtStage + 256;
+constexpr uint32_t kXtIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(16 >> 3) << 17) |
+                              ((uint32_t)(128 >> 4) << 24);
+
+struct XbtParams {
+  CUtensorMap tmap_x;   // X [M, K], box {64, 128}
+  CUtensorMap tmap_bt;  // Bt [members * 16, K], box {64, 16}
+  XbSegs S;
+  int32_t n_seg;
+  int32_t k_blocks;
+  int32_t rows_per_member;
+};
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kThreadsEgg, 1) eggroll_xbt_kernel(const __grid_constant__ XbtParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kXtStages * kXtStage);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kXtStages;
+  uint64_t* accf = bars + 2 * kXtStages;
+  uint64_t* drain = accf + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int row0 = blockIdx.x * 128;
+  const int member = row0 / P.rows_per_member;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kXtStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    mbar_init(accf, 1);
+    mbar_init(drain, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(32)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_base = *tmem_slot;
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer
+      int last_phase[kXtStages];
+      for (int s = 0; s < kXtStages; ++s) last_phase[s] = -1;
+      for (int kb = 0; kb < P.k_blocks; ++kb) {
+        const int s = kb % kXtStages;
+        const uint32_t round = kb / kXtStages;
+        if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort, 5)) break;
+        uint8_t* sa = smem + s * kXtStage;
+        mbar_expect_tx(&full[s], kXtA + kXtB);
+        tma_load_2d(sa, &P.tmap_x, &full[s], kb * kBK, row0);
+        tma_load_2d(sa + kXtA, &P.tmap_bt, &full[s], kb * kBK, member * 16);
+        last_phase[s] = (int)(round & 1);
+      }
+      for (int s = 0; s < kXtStages; ++s)
+        if (last_phase[s] >= 0) {
+          const long long t0 = clock64();
+          while (!mbar_try_wait(&full[s], (uint32_t)last_phase[s]) && clock64() - t0 < kWaitCycles) {
+          }
+        }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---- MMA issuer
+      bool ok = true, issued = false;
+      for (int kb = 0; kb < P.k_blocks; ++kb) {
+        const int s = kb % kXtStages;
+        if (!mbar_wait(&full[s], (kb / kXtStages) & 1, abort, 6)) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t sa = smem_u32(smem + s * kXtStage);
+#pragma unroll
+        for (int k = 0; k < kBK / kUmmaK; ++k) {
+          const uint64_t ad = umma_desc(sa + k * kUmmaK * 2), bd = umma_desc(sa + kXtA + k * kUmmaK * 2);
+          const uint32_t acc = (kb | k) != 0;
+          asm volatile(
+              "{\n\t.reg .pred p;\n\t"
+              "setp.ne.b32 p, %4, 0;\n\t"
+              "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+              ::"r"(tmem_base), "l"(ad), "l"(bd), "r"(kXtIdesc), "r"(acc)
+              : "memory");
+        }
+        issued = true;
+        umma_commit(&empty[s]);
+      }
+      if (ok && issued) umma_commit(accf);
+      if (issued) {
+        umma_commit(drain);
+        const long long t0 = clock64();
+        while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitCycles) {
+        }
+      }
+    }
+  } else {  // ---- epilogue: warps 2..5, one row each
+    const int q = warp & 3;
+    const int m = row0 + q * 32 + lane;
+    int ok = 1;
+    if (lane == 0) ok = mbar_wait(accf, 0, abort, 7) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (ok) {
+      __syncwarp();
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      uint32_t r[16];
+      tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16), r);
+      for (int sidx = 0; sidx < P.n_seg; ++sidx) {
+        float acc[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[c] = __uint_as_float(r[4 * sidx + c]);
+        if (P.S.xb[sidx])
+          reinterpret_cast<float4*>(P.S.xb[sidx])[m] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        if (P.S.xe[sidx]) write_xe(P.S.xe[sidx] + 2 * (size_t)m, P.S.xe_slot[sidx], __ldg(P.S.sigma[sidx] + member), acc);
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (warp == 0) {
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(32) : "memory");
+  }
+}
+
 int launch_xb(const void* x, const float* const* b, float* const* xb, int nseg, int64_t m, int64_t k,
               int32_t rows_per_member, cudaStream_t s, const float* const* sigma = nullptr,
               void* const* xe = nullptr, const int32_t* xe_slot = nullptr) {
@@ -878,6 +1021,9 @@ int prepare_kernels() {
   if (int rc = zt::check_cuda(cudaFuncSetAttribute(eggroll_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    (int)kSmemBytes), "eggroll: shared memory attribute"))
     return rc;
+  if (int rc = zt::check_cuda(cudaFuncSetAttribute(eggroll_xbt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)kXtSmem), "eggroll: shared memory attribute (xb)"))
+    return rc;
   for (auto fn : {eggroll_gemm_pair_kernel<false, false>, eggroll_gemm_pair_kernel<true, false>,
                   eggroll_gemm_pair_kernel<false, true>, eggroll_gemm_pair_kernel<true, true>})
     if (int rc = zt::check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes2),
@@ -909,6 +1055,38 @@ int launch_pair(const EggParams& P, bool ext, cudaStream_t s) {
   else
     eggroll_gemm_pair_kernel<GATED, false><<<2 * clusters, kThreadsEgg, kSmemBytes2, s>>>(P);
   return zt::check_cuda(cudaGetLastError(), GATED ? "eggroll: gated gemm launch" : "eggroll: gemm launch (pair)");
+}
+
+int xb_tensor_cores(const zt_eggroll_xb_args& A, cudaStream_t s) {
+  if (A.n_seg < 1 || A.n_seg > kXbMaxSeg) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: n_seg must be 1, 2 or 3");
+  if (A.m <= 0 || A.k <= 0 || A.m % 128 || A.k % kBK)
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: the tensor-core form needs m % 128 == 0 and k % 64 == 0");
+  if (A.rows_per_member <= 0 || A.rows_per_member % 128 || A.m % A.rows_per_member)
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: rows_per_member must divide m and be a multiple of 128");
+  if (A.m > (int64_t)INT32_MAX || A.k > (int64_t)INT32_MAX) return zt::set_error(ZT_ERR_LIMIT, "zt_eggroll_xb: dimension too large");
+  if (!A.x || ((uintptr_t)A.x & 15) || ((uintptr_t)A.bt & 15))
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: x / bt null or not 16-byte aligned");
+  XbtParams P{};
+  for (int i = 0; i < A.n_seg; ++i) {
+    if (((uintptr_t)A.xb[i] & 15) || (!A.xb[i] && !A.xe[i]))
+      return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: each set needs an aligned xb or xe");
+    if (A.xe[i] && (!A.sigma[i] || ((uintptr_t)A.xe[i] & 15) || A.xe_slot[i] < 0 || A.xe_slot[i] > 2))
+      return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: xe needs sigma, 16-byte alignment and a slot 0-2");
+    P.S.xb[i] = A.xb[i];
+    P.S.xe[i] = static_cast<uint4*>(A.xe[i]);
+    P.S.sigma[i] = A.sigma[i];
+    P.S.xe_slot[i] = A.xe_slot[i];
+  }
+  EncodeFn enc = nullptr;
+  if (int rc = get_encode(&enc)) return rc;
+  if (int rc = make_map(enc, &P.tmap_x, A.x, (uint64_t)A.m, (uint64_t)A.k, 128)) return rc;
+  if (int rc = make_map(enc, &P.tmap_bt, A.bt, (uint64_t)(A.m / A.rows_per_member) * 16, (uint64_t)A.k, 16)) return rc;
+  P.n_seg = A.n_seg;
+  P.k_blocks = (int32_t)(A.k / kBK);
+  P.rows_per_member = A.rows_per_member;
+  if (int rc = prepare_kernels()) return rc;
+  eggroll_xbt_kernel<<<(unsigned)(A.m / 128), kThreadsEgg, kXtSmem, s>>>(P);
+  return zt::check_cuda(cudaGetLastError(), "zt_eggroll_xb: tensor-core launch");
 }
 
 }  // namespace
@@ -1028,6 +1206,7 @@ int zt_eggroll_xb(const zt_eggroll_xb_args* args, void* stream) {
   zt::clear_error();
   if (!args) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: null args");
   const zt_eggroll_xb_args& A = *args;
+  if (A.bt) return xb_tensor_cores(A, zt::as_stream(stream));
   if (A.n_seg < 1 || A.n_seg > kXbMaxSeg) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: n_seg must be 1, 2 or 3");
   if (A.m <= 0 || A.k <= 0) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: empty shape");
   if (A.m % kXbRows || A.k % 4) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_xb: need m % 64 == 0 and k % 4 == 0");

@@ -39,7 +39,8 @@ template <int DT>
 __global__ void __launch_bounds__(kFacThreads) factor_kernel(const __grid_constant__ PairKeys K, int32_t n, int32_t k,
                                                               float4* __restrict__ a, float4* __restrict__ b,
                                                               float* __restrict__ part, uint4* __restrict__ a_ext,
-                                                              int32_t ext_slot) {
+                                                              int32_t ext_slot, __nv_bfloat16* __restrict__ b_ext,
+                                                              int32_t b_ext_row) {
   const int j = blockIdx.y;
   const uint32_t ka = K.ka[j], kb = K.kb[j];
   const int items = n + k;
@@ -74,6 +75,16 @@ __global__ void __launch_bounds__(kFacThreads) factor_kernel(const __grid_consta
       const float4 f = make_float4(v[0], v[1], v[2], v[3]);
       b0[t] = f;
       b0[t + k] = f;
+      if (b_ext) {  // B^T rows of both members: [member][b_ext_row + r][t]
+        __nv_bfloat16* e0 = b_ext + ((size_t)(2 * j) * 16 + b_ext_row) * k + t;
+        __nv_bfloat16* e1 = e0 + (size_t)16 * k;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const __nv_bfloat16 h = __float2bfloat16_rn(v[r]);
+          e0[(size_t)r * k] = h;
+          e1[(size_t)r * k] = h;
+        }
+      }
       gram_add(gq, v);
     }
   }
@@ -102,23 +113,32 @@ __global__ void __launch_bounds__(kFacThreads) factor_kernel(const __grid_consta
   }
 }
 
-// Signed scale of both members of pair j: +-sigma * c_j with
+// Signed scale of both members of pair j (one warp per pair): +-sigma * c_j with
 // c_j = sqrt(n*k) / (||P Psi||_F + 1e-7), each step rounded to the parameter dtype as
 // the reference's low_rank branch evaluates `z * (numel**0.5 / (z.norm() + 1e-7))`.
 // ||P Psi||_F^2 = sum_{r,s} (P^T P)_{rs} (Psi Psi^T)_{rs}.
 template <int DT>
-__global__ void __launch_bounds__(128) factor_scale_kernel(const float* __restrict__ part, int32_t pairs, int32_t nblk,
-                                                           float sqrt_numel, float sigma, int32_t normalize,
-                                                           float* __restrict__ scale) {
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= pairs) return;
+__global__ void __launch_bounds__(32) factor_scale_kernel(const float* __restrict__ part, int32_t nblk,
+                                                          float sqrt_numel, float sigma, int32_t normalize,
+                                                          float* __restrict__ scale) {
+  // one warp per pair: lane l sums the partials of blocks l, l + 32 (nblk <= 64) in fp64,
+  // then a fixed-order butterfly combines the lanes (deterministic)
+  const int j = blockIdx.x, lane = threadIdx.x;
   double g[2 * kGram];
+#pragma unroll
   for (int e = 0; e < 2 * kGram; ++e) g[e] = 0.0;
-  for (int bi = 0; bi < nblk; ++bi)
+  for (int bi = lane; bi < nblk; bi += 32)
+#pragma unroll
     for (int e = 0; e < 2 * kGram; ++e) g[e] += (double)part[((size_t)j * nblk + bi) * (2 * kGram) + e];
+#pragma unroll
+  for (int e = 0; e < 2 * kGram; ++e)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) g[e] += __shfl_xor_sync(0xffffffffu, g[e], o);
+  if (lane != 0) return;
   float c = 1.f;
   if (normalize) {
     double fro2 = 0.0;
+#pragma unroll
     for (int e = 0; e < kGram; ++e) {
       const bool diag = (e == 0 || e == 4 || e == 7 || e == 9);
       fro2 += (diag ? 1.0 : 2.0) * g[e] * g[kGram + e];
@@ -295,19 +315,21 @@ int zt_eggroll_factors(const zt_eggroll_factor_args* args, void* stream) {
   if (A.a_ext && (!aligned16(A.a_ext) || A.ext_slot < 0 || A.ext_slot > 1))
     return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_factors: a_ext not 16-byte aligned or ext_slot not 0/1");
   uint4* ae = static_cast<uint4*>(A.a_ext);
-  const unsigned sgrid = (unsigned)((A.pairs + 127) / 128);
+  if (A.b_ext && (A.b_ext_row < 0 || A.b_ext_row > 12 || A.b_ext_row % 4))
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_factors: b_ext_row must be 0, 4, 8 or 12");
+  __nv_bfloat16* be = static_cast<__nv_bfloat16*>(A.b_ext);
   switch (A.dtype) {
     case ZT_F32:
-      factor_kernel<ZT_F32><<<grid, kFacThreads, 0, s>>>(K, (int32_t)A.n, (int32_t)A.k, a4, b4, A.work, ae, A.ext_slot);
-      factor_scale_kernel<ZT_F32><<<sgrid, 128, 0, s>>>(A.work, A.pairs, (int32_t)nblk, sqrt_numel, A.sigma, A.normalize, A.scale);
+      factor_kernel<ZT_F32><<<grid, kFacThreads, 0, s>>>(K, (int32_t)A.n, (int32_t)A.k, a4, b4, A.work, ae, A.ext_slot, be, A.b_ext_row);
+      factor_scale_kernel<ZT_F32><<<(unsigned)A.pairs, 32, 0, s>>>(A.work, (int32_t)nblk, sqrt_numel, A.sigma, A.normalize, A.scale);
       break;
     case ZT_BF16:
-      factor_kernel<ZT_BF16><<<grid, kFacThreads, 0, s>>>(K, (int32_t)A.n, (int32_t)A.k, a4, b4, A.work, ae, A.ext_slot);
-      factor_scale_kernel<ZT_BF16><<<sgrid, 128, 0, s>>>(A.work, A.pairs, (int32_t)nblk, sqrt_numel, A.sigma, A.normalize, A.scale);
+      factor_kernel<ZT_BF16><<<grid, kFacThreads, 0, s>>>(K, (int32_t)A.n, (int32_t)A.k, a4, b4, A.work, ae, A.ext_slot, be, A.b_ext_row);
+      factor_scale_kernel<ZT_BF16><<<(unsigned)A.pairs, 32, 0, s>>>(A.work, (int32_t)nblk, sqrt_numel, A.sigma, A.normalize, A.scale);
       break;
     default:
-      factor_kernel<ZT_F16><<<grid, kFacThreads, 0, s>>>(K, (int32_t)A.n, (int32_t)A.k, a4, b4, A.work, ae, A.ext_slot);
-      factor_scale_kernel<ZT_F16><<<sgrid, 128, 0, s>>>(A.work, A.pairs, (int32_t)nblk, sqrt_numel, A.sigma, A.normalize, A.scale);
+      factor_kernel<ZT_F16><<<grid, kFacThreads, 0, s>>>(K, (int32_t)A.n, (int32_t)A.k, a4, b4, A.work, ae, A.ext_slot, be, A.b_ext_row);
+      factor_scale_kernel<ZT_F16><<<(unsigned)A.pairs, 32, 0, s>>>(A.work, (int32_t)nblk, sqrt_numel, A.sigma, A.normalize, A.scale);
       break;
   }
   return zt::check_cuda(cudaGetLastError(), "zt_eggroll_factors launch");

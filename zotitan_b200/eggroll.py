@@ -70,13 +70,15 @@ class _Population:
         that each lie inside one member."""
         return rows % 256 == 0 and self.rows_per_member % 256 == 0
 
-    def low_rank(self, idx: int, out_f: int, in_f: int, device, dtype=torch.bfloat16, ext_slot=None):
+    def low_rank(self, idx: int, out_f: int, in_f: int, device, dtype=torch.bfloat16, ext_slot=None, bt=None,
+                 bt_row: int = 0):
         """A [members, out, 4], B [members, in, 4] (fp32 holding dtype-rounded values) and
         the signed scale [members] of tensor idx for the current chunk (zt_eggroll_factors:
         one launch for the factors of every pair plus one for the normalisation); with
-        ext_slot also A's bf16 K-slab rows."""
+        ext_slot also A's bf16 K-slab rows, with bt also B^T into rows bt_row.. of bt."""
         return K.eggroll_factors(self.keys(idx + 2 * self.n_params), self.keys(idx + self.n_params), out_f, in_f,
-                                 self.cfg.sigma, device, dtype, self.cfg.normalize, ext_slot=ext_slot)
+                                 self.cfg.sigma, device, dtype, self.cfg.normalize, ext_slot=ext_slot, b_ext=bt,
+                                 b_ext_row=bt_row)
 
 
 class PopLinear(nn.Module):
@@ -87,9 +89,9 @@ class PopLinear(nn.Module):
         self.weight = base.weight
         self.idx, self.pop = idx, pop
 
-    def factors(self, device, ext_slot=None):
+    def factors(self, device, ext_slot=None, bt=None, bt_row: int = 0):
         out_f, in_f = self.weight.shape
-        return self.pop.low_rank(self.idx, out_f, in_f, device, self.weight.dtype, ext_slot)
+        return self.pop.low_rank(self.idx, out_f, in_f, device, self.weight.dtype, ext_slot, bt, bt_row)
 
     def forward(self, x, fac=None, xb=None, xe=None):
         """fac = the factors and xb = X B (fp32) or xe = its K-slab rows, from a shared
@@ -99,10 +101,12 @@ class PopLinear(nn.Module):
         out_f = self.weight.shape[0]
         rpm = self.pop.rows_per_member
         if fac is None:
-            ext = self.pop.use_ext(x2.shape[0])
-            fac = self.factors(x.device, 0 if ext else None)
-            if ext:
-                xe = K.eggroll_xb_ext(x2, [fac[1]], [fac[2]], [0], rpm)[0]
+            if self.pop.use_ext(x2.shape[0]):
+                bt = torch.zeros((x2.shape[0] // rpm, 16, x2.shape[1]), dtype=torch.bfloat16, device=x.device)
+                fac = self.factors(x.device, 0, bt, 0)
+                xe = K.eggroll_xb_ext(x2, [fac[1]], [fac[2]], [0], rpm, bt=bt)[0]
+            else:
+                fac = self.factors(x.device)
         if xe is not None:
             y = K.eggroll_linear(x2, self.weight.data, fac[0], None, fac[2], rpm, x_ext=xe, w_ext=fac[3])
         else:
@@ -117,8 +121,10 @@ def _shared_input(x, linears, pop, slots=None):
     x2 = x.reshape(-1, x.shape[-1]).contiguous()
     if pop.use_ext(x2.shape[0]):
         slots = slots or [0] * len(linears)
-        facs = [lin.factors(x.device, 1 if sl == 2 else 0) for lin, sl in zip(linears, slots)]
-        xes = K.eggroll_xb_ext(x2, [f[1] for f in facs], [f[2] for f in facs], slots, pop.rows_per_member)
+        rpm = pop.rows_per_member
+        bt = torch.zeros((x2.shape[0] // rpm, 16, x2.shape[1]), dtype=torch.bfloat16, device=x.device)
+        facs = [lin.factors(x.device, 1 if sl == 2 else 0, bt, 4 * i) for i, (lin, sl) in enumerate(zip(linears, slots))]
+        xes = K.eggroll_xb_ext(x2, [f[1] for f in facs], [f[2] for f in facs], slots, rpm, bt=bt)
         return x2, facs, [None] * len(linears), xes
     facs = [lin.factors(x.device) for lin in linears]
     xbs = K.eggroll_xb(x2, [f[1] for f in facs], pop.rows_per_member)

@@ -288,10 +288,18 @@ def eggroll_linear(x: torch.Tensor, w: torch.Tensor, a: torch.Tensor, b: torch.T
     return out
 
 
-def eggroll_xb_ext(x: torch.Tensor, bs: list, scales: list, slots: list, rows_per_member: int) -> list:
+def eggroll_xb_ext(x: torch.Tensor, bs: list, scales: list, slots: list, rows_per_member: int,
+                   bt: torch.Tensor | None = None) -> list:
     """K-slab rows of sigma_i X B_s (zt_eggroll_xb with xe outputs): slot 0 gives a set its
     own [M, 16] bf16 buffer [hi, lo, 0 x 8]; slots 1 and 2 share one buffer (columns 0-7
-    and 8-15, the gated gate/up form). Returns one buffer per set (shared ones repeated)."""
+    and 8-15, the gated gate/up form). Returns one buffer per set (shared ones repeated).
+    With bt (all sets' B^T, [members, 16, K] bf16 from eggroll_factors' b_ext) the product
+    runs on the tensor cores and the fp32 bs are not read."""
+    if bt is not None:
+        _check_cuda(bt, "bt")
+        if bt.dtype != torch.bfloat16 or not bt.is_contiguous() or \
+                bt.shape != (x.shape[0] // rows_per_member, 16, x.shape[1]):
+            raise ValueError("bt must be a contiguous bf16 [members, 16, K] tensor")
     if not 1 <= len(bs) <= 3 or len(scales) != len(bs) or len(slots) != len(bs):
         raise ValueError("one to three factor sets, with a scale and a slot each")
     _check_cuda(x, "x")
@@ -320,7 +328,7 @@ def eggroll_xb_ext(x: torch.Tensor, bs: list, scales: list, slots: list, rows_pe
                              (ctypes.c_void_p * 3)(*([0] * 3)), M, K, n, rows_per_member,
                              (ctypes.c_void_p * 3)(*([sc.data_ptr() for sc in scales] + pad)),
                              (ctypes.c_void_p * 3)(*([t.data_ptr() for t in xes] + pad)),
-                             (ctypes.c_int32 * 3)(*(list(slots) + pad)), 0)
+                             (ctypes.c_int32 * 3)(*(list(slots) + pad)), 0, bt.data_ptr() if bt is not None else None)
     with torch.cuda.device(x.device):
         L.check(L.load().zt_eggroll_xb(ctypes.byref(args), _stream_ptr(x.device)), "zt_eggroll_xb")
     return xes
@@ -344,7 +352,7 @@ def eggroll_xb(x: torch.Tensor, bs: list, rows_per_member: int) -> list:
     xp = [t.data_ptr() for t in xbs] + [0] * (3 - len(bs))
     args = L.ZtEggrollXbArgs(x.data_ptr(), (ctypes.c_void_p * 3)(*bp), (ctypes.c_void_p * 3)(*xp), M, K, len(bs),
                              rows_per_member, (ctypes.c_void_p * 3)(0, 0, 0), (ctypes.c_void_p * 3)(0, 0, 0),
-                             (ctypes.c_int32 * 3)(0, 0, 0), 0)
+                             (ctypes.c_int32 * 3)(0, 0, 0), 0, None)
     with torch.cuda.device(x.device):
         L.check(L.load().zt_eggroll_xb(ctypes.byref(args), _stream_ptr(x.device)), "zt_eggroll_xb")
     return xbs
@@ -402,11 +410,18 @@ def _keys_array(keys):
 
 
 def eggroll_factors(keys_a: list[int], keys_b: list[int], n: int, k: int, sigma: float, device,
-                    dtype: torch.dtype = torch.bfloat16, normalize: bool = True, ext_slot: int | None = None):
+                    dtype: torch.dtype = torch.bfloat16, normalize: bool = True, ext_slot: int | None = None,
+                    b_ext: torch.Tensor | None = None, b_ext_row: int = 0):
     """Rank-4 factors of an [n, k] tensor for antithetic pairs (zt_eggroll_factors):
     returns A [2p, n, 4], B [2p, k, 4] (fp32 holding dtype-rounded values) and the signed
     scale [2p] (+sigma c_j, -sigma c_j), ready for eggroll_linear. With ext_slot (0 or 1)
-    also A_ext [2p, n, 16] bf16, the GEMM's K-slab operand, as a fourth element."""
+    also A_ext [2p, n, 16] bf16, the GEMM's K-slab operand, as a fourth element. With
+    b_ext ([2p, 16, k] bf16, zeroed by the caller) B^T is also written to its rows
+    b_ext_row .. b_ext_row + 3 (the tensor-core X B operand of eggroll_xb_ext)."""
+    if b_ext is not None:
+        _check_cuda(b_ext, "b_ext")
+        if b_ext.dtype != torch.bfloat16 or not b_ext.is_contiguous() or b_ext.shape != (2 * len(keys_a), 16, k):
+            raise ValueError("b_ext must be a contiguous bf16 [2p, 16, k] tensor")
     pairs = len(keys_a)
     if pairs != len(keys_b) or pairs == 0:
         raise ValueError("keys_a and keys_b must be non-empty and of equal length")
@@ -422,7 +437,8 @@ def eggroll_factors(keys_a: list[int], keys_b: list[int], n: int, k: int, sigma:
     args = L.ZtEggrollFactorArgs(ctypes.addressof(ka), ctypes.addressof(kb), pairs, 4, n, k, _DT[dtype],
                                  1 if normalize else 0, float(sigma), 0, a.data_ptr(), b.data_ptr(), scale.data_ptr(),
                                  work.data_ptr(), a_ext.data_ptr() if a_ext is not None else None,
-                                 int(ext_slot or 0), 0)
+                                 int(ext_slot or 0), 0, b_ext.data_ptr() if b_ext is not None else None,
+                                 int(b_ext_row), 0)
     with torch.cuda.device(device):
         L.check(L.load().zt_eggroll_factors(ctypes.byref(args), _stream_ptr(device)), "zt_eggroll_factors")
     return (a, b, scale) if a_ext is None else (a, b, scale, a_ext)
