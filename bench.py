@@ -45,12 +45,14 @@ def parse():
     ap.add_argument("--no-eggroll", action="store_true", help="skip the EGGROLL population measurement")
     ap.add_argument("--no-mezo", action="store_true", help="skip the MeZO full fine-tune step measurement")
     ap.add_argument("--no-lora", action="store_true", help="skip the MeZO-Adam LoRA step measurement")
-    ap.add_argument("--profile-case", choices=["chain", "full", "eggroll", "eggroll-forward"], default=None,
+    ap.add_argument("--profile-case", choices=["chain", "full", "eggroll", "eggroll-gated", "eggroll-forward"],
+                    default=None,
                     help="small case for ncu: one bf16 tensor of 2^28 elements, 3 launches of the "
                          "-2eps pass (chain) or of the restore+accumulate+perturb pass (full); or 3 "
-                         "EGGROLL linear launches on an 8B gate_proj shape, 16 members x 1024 rows (eggroll); "
-                         "or one 16-member EGGROLL population chunk of the 8B model inside the NVTX range "
-                         "'egg_chunk' (eggroll-forward)")
+                         "EGGROLL linear launches (rank-4 term as a K-slab) on the 8B gate_proj shape, 16 "
+                         "members x 1024 rows (eggroll), or 3 gated gate/up/SwiGLU launches on it "
+                         "(eggroll-gated); or one 16-member EGGROLL population chunk of the 8B model inside "
+                         "the NVTX range 'egg_chunk' (eggroll-forward)")
     ap.add_argument("--eggroll-gemm", action="store_true",
                     help="time the EGGROLL population linear layer on the Llama-3-8B layer shapes")
     return ap.parse_args()
@@ -137,14 +139,34 @@ def profile_case(kind: str):
     n = 1 << 28
     p = (torch.randn(n, device="cuda") * 0.02).bfloat16()
     f = lambda x: float(np.float32(x))  # noqa: E731
-    if kind == "eggroll":
-        x, w, a, b, sigma = eggroll_inputs(16384, 14336, 4096, 1024, "cuda")
-        y = torch.empty(16384, 14336, dtype=torch.bfloat16, device="cuda")
-        xb = torch.empty(16384, 4, dtype=torch.float32, device="cuda")
-        for _ in range(3):
-            K.eggroll_linear(x, w, a, b, sigma, 1024, out=y, xb=xb)
+    if kind in ("eggroll", "eggroll-gated"):
+        M, N, Kd, T = 16384, 14336, 4096, 1024
+        g = torch.Generator(device="cuda").manual_seed(0)
+        x = torch.randn(M, Kd, device="cuda", generator=g).bfloat16()
+        w = (torch.randn(N, Kd, device="cuda", generator=g) * 0.02).bfloat16()
+        bt = torch.zeros((M // T, 16, Kd), dtype=torch.bfloat16, device="cuda")
+        fg = K.eggroll_factors(list(range(8)), list(range(8, 16)), N, Kd, 1e-3, "cuda", ext_slot=0, b_ext=bt)
+        if kind == "eggroll":
+            xe = K.eggroll_xb_ext(x, [fg[1]], [fg[2]], [0], T, bt=bt)[0]
+            y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+            run = lambda: K.eggroll_linear(x, w, fg[0], None, fg[2], T, out=y, x_ext=xe, w_ext=fg[3])  # noqa: E731
+            flops = 2.0 * M * N * Kd
+        else:
+            fu = K.eggroll_factors(list(range(16, 24)), list(range(24, 32)), N, Kd, 1e-3, "cuda", ext_slot=1, b_ext=bt,
+                                   b_ext_row=4)
+            xe = K.eggroll_xb_ext(x, [fg[1], fu[1]], [fg[2], fu[2]], [1, 2], T, bt=bt)[0]
+            run = lambda: K.eggroll_gated(x, w, w, fg, fu, None, None, T, x_ext=xe)  # noqa: E731
+            flops = 4.0 * M * N * Kd
+        for _ in range(2):
+            run()
         torch.cuda.synchronize()
-        print(json.dumps({"profile_case": kind, "error": K.eggroll_take_error()}))
+        a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_.record()
+        run()
+        b_.record()
+        torch.cuda.synchronize()
+        ms = a_.elapsed_time(b_)
+        print(json.dumps({"profile_case": kind, "ms": ms, "tflops": flops / ms / 1e9, "error": K.eggroll_take_error()}))
         return
     if kind == "chain":
         tab = K.ParamTable([p])
