@@ -635,10 +635,10 @@ def run_ours(args, rank, local_rank, world):
         achieved, kname, kbytes = perturb_gbs, "chain_kernel: -2eps perturb pass (1 noise stream)", perturb_bytes
     traffic = None
     prof = os.path.join(HERE, "profiles", "pass_kernel_traffic.json")
-    if amean and os.path.exists(prof):
+    if os.path.exists(prof):
         try:
-            traffic = json.load(open(prof)).get("dram_bytes_per_launch")
-        except ValueError:
+            traffic = json.load(open(prof)).get("full_kernel" if amean else "chain_kernel", {}).get("dram_bytes_per_launch")
+        except (ValueError, AttributeError):
             traffic = None
     value = args.steps / (ms * 1e-3)
     line = {
