@@ -344,11 +344,21 @@ def eggroll_member_evals(dev, rank: int, world: int, pairs_per_rank: int = 16, p
     t1.record()
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1)
+    # the ES update every rank applies after the all-gather: rank-4*pairs GEMMs over all
+    # 2-D tensors of the model (pairs of the whole population), timed on its own
+    u0, u1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    all_pairs = list(range(world * pairs_per_rank))
+    coefs = [((j % 7) - 3) / (7.0 * len(all_pairs)) for j in all_pairs]
+    u0.record()
+    pop.apply_update(all_pairs, coefs, lr=1e-6)
+    u1.record()
+    torch.cuda.synchronize()
+    upd_ms = u0.elapsed_time(u1)
     err = K.eggroll_take_error()
     if world > 1:
-        t = torch.tensor([ms], device=dev)
+        t = torch.tensor([ms, upd_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms, upd_ms = t.tolist()
     members = 2 * pairs_per_rank * world
     tokens_per_member = tokens.numel()
     lin_flops = linear_flops_per_token(LLAMA_8B) * tokens_per_member * members
@@ -358,7 +368,8 @@ def eggroll_member_evals(dev, rank: int, world: int, pairs_per_rank: int = 16, p
             "unit": "member-evals/s", "members": members, "members_per_rank": 2 * pairs_per_rank,
             "tokens_per_member": tokens_per_member, "sigma": 1e-3, "rank": 4, "scaling": "weak",
             "ms": ms, "linear_tflops": lin_flops / (ms * 1e-3) / 1e12, "device_error": err,
-            "mean_loss": float(mine.mean())}
+            "mean_loss": float(mine.mean()), "es_update_ms": upd_ms,
+            "es_step_members_per_s": members / ((ms + upd_ms) * 1e-3)}
 
 
 def mezo_full_ft_steps(dev, rank: int, world: int, steps: int = 3, warmup: int = 2, pairs: int = 8):

@@ -67,3 +67,54 @@ def test_population_forward_matches_materialised_members(batch):
     with torch.no_grad():
         l0 = float(base(input_ids=tokens, labels=tokens).loss)
     assert abs(got[0] - got[1]) > 1e-4 and abs(got[0] - l0) > 1e-5
+
+
+def test_es_update_matches_sum_of_materialised_directions():
+    """EggrollPopulation.apply_update (rank-4*pairs GEMM for 2-D tensors, dense Gaussian
+    sum for 1-D) against theta - lr * sum_j coef_j z_j with every z_j materialised by the
+    oracle's restatement of the reference's low_rank branch. The oracle rounds each z_j to
+    bf16 (as the reference does) where the GEMM uses the exact product, so the bar is one
+    bf16 step of theta plus 2^-7 of lr * sum_j |coef_j z_j| (the terms' rounding does not
+    cancel where the terms do)."""
+    from oracle.zo_step import OracleZO
+    from toy_models import build_llama
+    from zotitan_b200.eggroll import EggrollConfig, EggrollPopulation
+    model = build_llama(SHAPE, dtype=torch.bfloat16, seed=0, device="cuda")
+    named = [(n, p) for n, p in model.named_parameters()]
+    host = [p.detach().float().cpu().numpy() for _, p in named]
+    pop = EggrollPopulation(model, EggrollConfig(sigma=SIGMA))
+    seeds = [3, 11, 17, 23]
+    coefs = [0.25, -0.5, 0.125, 0.75]
+    lr = 1e-2
+    pop.apply_update(seeds, coefs, lr)
+    oz = OracleZO([h.copy() for h in host], [__import__("oracle.philox", fromlist=["x"]).BF16] * len(host), _cfg(),
+                  noise="c", semantics="cuda")
+    delta = [np.zeros_like(h, dtype=np.float64) for h in host]
+    mag = [np.zeros_like(h, dtype=np.float64) for h in host]
+    for s, c in zip(seeds, coefs):
+        for d, m_, z in zip(delta, mag, oz.sample_z(s)):
+            d += c * z.astype(np.float64)
+            m_ += abs(c) * np.abs(z.astype(np.float64))
+    for (name, p), h, d, m_ in zip(named, host, delta, mag):
+        got = p.detach().float().cpu().numpy()
+        want = h - lr * d
+        ulp = np.ldexp(1.0, np.frexp(np.maximum(np.abs(want), 2.0 ** -126))[1] - 8)
+        err = np.abs(got - want)
+        bound = ulp + 2.0 ** -7 * lr * m_ + 1e-12
+        assert (err <= bound).all(), (name, float((err / bound).max()))
+        assert not np.array_equal(got, h), name
+
+
+def test_es_step_single_rank():
+    from toy_models import build_llama
+    from zotitan_b200.eggroll import EggrollConfig, EggrollPopulation
+    g = torch.Generator().manual_seed(9)
+    tokens = torch.randint(0, SHAPE["vocab_size"], (4, 64), generator=g).cuda()
+    model = build_llama(SHAPE, dtype=torch.bfloat16, seed=0, device="cuda")
+    pop = EggrollPopulation(model, EggrollConfig(sigma=SIGMA))
+    before = [p.detach().clone() for _, p in pop.named]
+    m = pop.step(tokens, [1, 2, 3, 4, 5, 6], lr=1e-3, strategy="centered_rank", chunk_pairs=4)
+    assert m["members"] == 12 and np.isfinite(m["loss"]) and m["fit_rms"] > 0
+    assert any(not torch.equal(b, p) for b, (_, p) in zip(before, pop.named))
+    from zotitan_b200 import kernels as K
+    assert K.eggroll_take_error() == 0

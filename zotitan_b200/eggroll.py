@@ -29,6 +29,7 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 import torch.nn as nn
 
@@ -239,6 +240,7 @@ class EggrollPopulation:
         self.cfg = cfg or EggrollConfig()
         named = [(n, p) for n, p in model.named_parameters() if p.requires_grad]
         index = {id(p): i for i, (_, p) in enumerate(named)}
+        self.named = named
         self.pop = _Population(len(named), self.cfg)
         from transformers.models.llama import modeling_llama as ml
         replaced = set()
@@ -296,3 +298,85 @@ class EggrollPopulation:
         tgt[:, :-1] = ids[:, 1:]
         ce, _, _ = K.xent_rows(logits.view(-1, V), tgt.view(-1), want_lse=False, want_correct=False)
         return ce.view(P, -1).sum(dim=1) / (S * (T - 1))
+
+    # -- the evolution-strategies step ------------------------------------------------
+
+    def evaluate_all(self, tokens: torch.Tensor, pair_seeds: list[int], chunk_pairs: int = 8) -> torch.Tensor:
+        """evaluate() over pair_seeds in chunks of chunk_pairs pairs: [2*len(pair_seeds)] losses."""
+        out = [self.evaluate(tokens, pair_seeds[c:c + chunk_pairs]) for c in range(0, len(pair_seeds), chunk_pairs)]
+        return torch.cat(out) if out else torch.empty(0, device=tokens.device)
+
+    @torch.no_grad()
+    def apply_update(self, pair_seeds: list[int], coefs: list[float], lr: float):
+        """theta <- theta - lr * sum_j coefs[j] * z_j over every trainable tensor, z_j the
+        pair's direction: c_j P_j Psi_j for 2-D tensors (the reference's normalised
+        low_rank z, train_zo.py:304-320) and the Gaussian field for 1-D ones (:303).
+
+        2-D tensors take the sum as one GEMM of rank 4 * pairs on the tensor cores:
+        [A_hi | A_lo] [B | B]^T with A = (coef_j c_j P_j)_j split into two bf16 parts
+        (~2^-16 relative) and B = (Psi_j^T)_j (bf16-exact), accumulated and returned in
+        fp32. The update is rounded to the parameter dtype once (the reference accumulates
+        grad_est in that dtype pair by pair)."""
+        if len(pair_seeds) != len(coefs):
+            raise ValueError("one coefficient per pair")
+        if not pair_seeds:
+            return
+        pop = self.pop
+        dev = self.named[0][1].device
+        coef = torch.tensor(coefs, dtype=torch.float32, device=dev)
+        saved = pop.pair_seeds
+        pop.pair_seeds = list(pair_seeds)
+        sigma = float(np.float32(self.cfg.sigma))
+        for i, (_, p) in enumerate(self.named):
+            w = p.data
+            if w.dim() == 1:
+                z = K.randn_keys(pop.keys(i), w.numel(), dev)                    # [P, numel]
+                delta = coef @ z
+            elif w.dim() == 2:
+                a, b, scale, *_ = pop.low_rank(i, w.shape[0], w.shape[1], dev, w.dtype)
+                c = scale[0::2] / sigma                                          # c_j
+                ahat = (a[0::2] * (coef * c)[:, None, None]).permute(1, 0, 2).reshape(w.shape[0], -1)
+                bhat = b[0::2].permute(1, 0, 2).reshape(w.shape[1], -1)          # [in, 4P]
+                a_hi = ahat.bfloat16()
+                a_lo = (ahat - a_hi.float()).bfloat16()
+                bb = bhat.bfloat16()
+                delta = torch.mm(torch.cat([a_hi, a_lo], dim=1), torch.cat([bb, bb], dim=1).T, out_dtype=torch.float32)
+            else:
+                raise NotImplementedError("EGGROLL updates 1-D and 2-D tensors")
+            w.copy_((w.float() - float(np.float32(lr)) * delta).to(w.dtype))
+        pop.pair_seeds = saved
+
+    def step(self, tokens: torch.Tensor, pair_seeds: list[int], lr: float, strategy: str = "centered_rank",
+             normalize_std: bool = True, chunk_pairs: int = 8, group=None) -> dict:
+        """One evolution-strategies step: every rank scores its share of the antithetic
+        pairs (pairs r, r+W, ...), one all-gather of the member losses, fitness shaping by
+        the reference's rules (train_zo.py:475-508: centered ranks, GRPO advantages, or the
+        plain (L+ - L-) / (2 sigma)), then the same rank-(4 * pairs) update on every rank."""
+        from .distributed import gather_pair_values, local_pairs, world_info
+        from .train_zo import StepPlanner, f32, f32_recip
+        rank, world = world_info(group)
+        Z = len(pair_seeds)
+        mine = local_pairs(Z, rank, world)
+        local = self.evaluate_all(tokens, [pair_seeds[j] for j in mine], chunk_pairs).view(-1, 2)
+        rows = gather_pair_values(local, Z, rank, world, group) if world > 1 else local
+        vals = rows.flatten().tolist()
+        if strategy == "centered_rank":
+            u = StepPlanner._centered_ranks([-v for v in vals])
+            g = [u[2 * j + 1] - u[2 * j] for j in range(Z)]
+        elif strategy == "grpo":
+            mean = sum(vals) / len(vals)
+            adv = [mean - v for v in vals]
+            if normalize_std:
+                std = (sum(a_ * a_ for a_ in adv) / len(adv)) ** 0.5
+                adv = [a_ / (std + 1e-8) for a_ in adv]
+            g = [adv[2 * j + 1] - adv[2 * j] for j in range(Z)]
+        elif strategy == "none":
+            inv = f32_recip(2 * self.cfg.sigma)
+            g = [float(np.float32(np.float32(np.float32(vals[2 * j]) - np.float32(vals[2 * j + 1])) * np.float32(inv)))
+                 for j in range(Z)]
+        else:
+            raise ValueError(f"unknown fitness strategy {strategy!r}")
+        coefs = [f32(gj / Z) for gj in g]
+        self.apply_update(pair_seeds, coefs, lr)
+        return {"loss": sum(vals) / len(vals), "fit_rms": (sum(x * x for x in g) / Z) ** 0.5,
+                "members": 2 * Z}
