@@ -349,6 +349,8 @@ def eggroll_member_evals(dev, rank: int, world: int, pairs_per_rank: int = 16, p
     u0, u1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     all_pairs = list(range(world * pairs_per_rank))
     coefs = [((j % 7) - 3) / (7.0 * len(all_pairs)) for j in all_pairs]
+    pop.apply_update(all_pairs, [0.0] * len(all_pairs), lr=1e-6)   # untimed warm-up (leaves W unchanged)
+    torch.cuda.synchronize()
     u0.record()
     pop.apply_update(all_pairs, coefs, lr=1e-6)
     u1.record()

@@ -402,6 +402,17 @@ ZT_API int zt_eggroll_rope(void* q, void* k, const void* cos, const void* sin, i
  * act_fn(gate_proj(x)) * up_proj(x). */
 ZT_API int zt_eggroll_swiglu(const void* gate, const void* up, void* out, int64_t n, void* stream);
 
+/* Operands of the EGGROLL evolution-strategies update of one 2-D tensor [n, k] over
+ * `pairs` antithetic pairs, from zt_eggroll_factors' a, b, scale (members 2j):
+ *   a_cat [n, 8*pairs] bf16: row o, pair j -> [hi(v), lo(v)], v = coef_j (scale_2j / sigma) A_2j[o]
+ *   b_cat [k, 8*pairs] bf16: row t, pair j -> [B_2j[t], B_2j[t]]
+ * so that a_cat b_cat^T = sum_j coef_j c_j P_j Psi_j to ~2^-16 relative: the update
+ * theta -= lr * sum_j coef_j z_j of the reference's low_rank directions (zotitan/train_zo.py:
+ * 304-320, 550-556) as one GEMM of inner dimension 8 * pairs. */
+ZT_API int zt_eggroll_update_operands(const float* a, const float* b, const float* scale, const float* coef,
+                                      int32_t pairs, int64_t n, int64_t k, float sigma, void* a_cat, void* b_cat,
+                                      void* stream);
+
 /* ---- the scorer: next-token cross-entropy statistics ------------------------------ */
 
 /* Per-row statistics of bf16 logits [rows, vocab] (row stride ld elements, ld % 8 == 0,

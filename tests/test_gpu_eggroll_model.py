@@ -73,9 +73,10 @@ def test_es_update_matches_sum_of_materialised_directions():
     """EggrollPopulation.apply_update (rank-4*pairs GEMM for 2-D tensors, dense Gaussian
     sum for 1-D) against theta - lr * sum_j coef_j z_j with every z_j materialised by the
     oracle's restatement of the reference's low_rank branch. The oracle rounds each z_j to
-    bf16 (as the reference does) where the GEMM uses the exact product, so the bar is one
-    bf16 step of theta plus 2^-7 of lr * sum_j |coef_j z_j| (the terms' rounding does not
-    cancel where the terms do)."""
+    bf16 twice (product, then the scaled product) and takes the norm of the rounded product,
+    as the reference does; the factors normalise the exact product, whose bf16-rounded norm
+    can sit one step away. So the bar is one bf16 step of theta plus 2^-6 of
+    lr * sum_j |coef_j z_j| (the terms' rounding does not cancel where the terms do)."""
     from oracle.zo_step import OracleZO
     from toy_models import build_llama
     from zotitan_b200.eggroll import EggrollConfig, EggrollPopulation
@@ -100,7 +101,7 @@ def test_es_update_matches_sum_of_materialised_directions():
         want = h - lr * d
         ulp = np.ldexp(1.0, np.frexp(np.maximum(np.abs(want), 2.0 ** -126))[1] - 8)
         err = np.abs(got - want)
-        bound = ulp + 2.0 ** -7 * lr * m_ + 1e-12
+        bound = ulp + 2.0 ** -6 * lr * m_ + 1e-12
         assert (err <= bound).all(), (name, float((err / bound).max()))
         assert not np.array_equal(got, h), name
 

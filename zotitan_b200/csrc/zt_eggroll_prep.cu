@@ -273,6 +273,44 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const uint4* __restrict__ g
   }
 }
 
+// ---- operands of the evolution-strategies update GEMM ------------------------------------
+
+// Row o < n of a_cat: for pair j, columns 8j..8j+3 = hi(v), 8j+4..8j+7 = lo(v) with
+// v = coef_j * (scale_2j / sigma) * A_2j[o]; row t < k of b_cat: B_2j[t] twice. One thread
+// per (row, pair): consecutive threads write consecutive 16-byte pieces of a row.
+__global__ void __launch_bounds__(256) update_operands_kernel(const float4* __restrict__ a, const float4* __restrict__ b,
+                                                              const float* __restrict__ scale,
+                                                              const float* __restrict__ coef, int32_t pairs, int64_t n,
+                                                              int64_t k, float sigma, uint4* __restrict__ a_cat,
+                                                              uint4* __restrict__ b_cat) {
+  const int64_t total = (n + k) * pairs;
+  for (int64_t it = (int64_t)blockIdx.x * 256 + threadIdx.x; it < total; it += (int64_t)gridDim.x * 256) {
+    const int64_t row = it / pairs;
+    const int j = (int)(it - row * pairs);
+    if (row < n) {
+      const float f = coef[j] * (scale[2 * j] / sigma);
+      const float4 v = a[(size_t)(2 * j) * n + row];
+      const float x[4] = {f * v.x, f * v.y, f * v.z, f * v.w};
+      __nv_bfloat16 h[4], l[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        h[r] = __float2bfloat16_rn(x[r]);
+        l[r] = __float2bfloat16_rn(x[r] - __bfloat162float(h[r]));
+      }
+      a_cat[row * pairs + j] = make_uint4(
+          (uint32_t)__bfloat16_as_ushort(h[0]) | ((uint32_t)__bfloat16_as_ushort(h[1]) << 16),
+          (uint32_t)__bfloat16_as_ushort(h[2]) | ((uint32_t)__bfloat16_as_ushort(h[3]) << 16),
+          (uint32_t)__bfloat16_as_ushort(l[0]) | ((uint32_t)__bfloat16_as_ushort(l[1]) << 16),
+          (uint32_t)__bfloat16_as_ushort(l[2]) | ((uint32_t)__bfloat16_as_ushort(l[3]) << 16));
+    } else {
+      const int64_t t = row - n;
+      const float4 v = b[(size_t)(2 * j) * k + t];
+      const uint32_t p0 = bf16x2(v.x, v.y), p1 = bf16x2(v.z, v.w);
+      b_cat[t * pairs + j] = make_uint4(p0, p1, p0, p1);
+    }
+  }
+}
+
 int stream_grid(int64_t items, int per_sm) {
   const int64_t want = (items + 255) / 256;
   const int64_t cap = (int64_t)zt::sm_count() * per_sm;
@@ -389,6 +427,22 @@ int zt_eggroll_swiglu(const void* gate, const void* up, void* out, int64_t n, vo
   swiglu_kernel<<<stream_grid(n / 8, 16), 256, 0, zt::as_stream(stream)>>>(
       static_cast<const uint4*>(gate), static_cast<const uint4*>(up), static_cast<uint4*>(out), n / 8);
   return zt::check_cuda(cudaGetLastError(), "zt_eggroll_swiglu launch");
+}
+
+int zt_eggroll_update_operands(const float* a, const float* b, const float* scale, const float* coef, int32_t pairs,
+                               int64_t n, int64_t k, float sigma, void* a_cat, void* b_cat, void* stream) {
+  zt::clear_error();
+  if (pairs <= 0 || n <= 0 || k <= 0) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_update_operands: empty shape");
+  if (pairs > kMaxPairs) return zt::set_error(ZT_ERR_LIMIT, "zt_eggroll_update_operands: more than ZT_EGGROLL_MAX_PAIRS pairs");
+  if (!a || !b || !scale || !coef || !a_cat || !b_cat)
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_update_operands: null pointer");
+  if (!aligned16(a) || !aligned16(b) || !aligned16(a_cat) || !aligned16(b_cat))
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_update_operands: a, b, a_cat, b_cat not 16-byte aligned");
+  if (!(sigma > 0.f)) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_update_operands: sigma must be positive");
+  update_operands_kernel<<<stream_grid((n + k) * (int64_t)pairs, 16), 256, 0, zt::as_stream(stream)>>>(
+      reinterpret_cast<const float4*>(a), reinterpret_cast<const float4*>(b), scale, coef, pairs, n, k, sigma,
+      static_cast<uint4*>(a_cat), static_cast<uint4*>(b_cat));
+  return zt::check_cuda(cudaGetLastError(), "zt_eggroll_update_operands launch");
 }
 
 }  // extern "C"

@@ -314,9 +314,9 @@ class EggrollPopulation:
 
         2-D tensors take the sum as one GEMM of rank 4 * pairs on the tensor cores:
         [A_hi | A_lo] [B | B]^T with A = (coef_j c_j P_j)_j split into two bf16 parts
-        (~2^-16 relative) and B = (Psi_j^T)_j (bf16-exact), accumulated and returned in
-        fp32. The update is rounded to the parameter dtype once (the reference accumulates
-        grad_est in that dtype pair by pair)."""
+        (~2^-16 relative) and B = (Psi_j^T)_j (bf16-exact), accumulated in fp32 and added to
+        the weight in the GEMM's epilogue (addmm), rounded to the parameter dtype once (the
+        reference accumulates grad_est in that dtype pair by pair)."""
         if len(pair_seeds) != len(coefs):
             raise ValueError("one coefficient per pair")
         if not pair_seeds:
@@ -327,24 +327,32 @@ class EggrollPopulation:
         saved = pop.pair_seeds
         pop.pair_seeds = list(pair_seeds)
         sigma = float(np.float32(self.cfg.sigma))
+        # fp32 accumulation end to end in the update GEMMs (no bf16 split-K partial sums)
+        matmul_flags = torch.backends.cuda.matmul
+        reduced = matmul_flags.allow_bf16_reduced_precision_reduction
+        matmul_flags.allow_bf16_reduced_precision_reduction = False
+        try:
+            self._apply(pair_seeds, coef, lr, sigma, dev)
+        finally:
+            pop.pair_seeds = saved
+            matmul_flags.allow_bf16_reduced_precision_reduction = reduced
+
+    def _apply(self, pair_seeds, coef, lr, sigma, dev):
+        pop = self.pop
+        alpha = -float(np.float32(lr))
         for i, (_, p) in enumerate(self.named):
             w = p.data
-            if w.dim() == 1:
-                z = K.randn_keys(pop.keys(i), w.numel(), dev)                    # [P, numel]
-                delta = coef @ z
-            elif w.dim() == 2:
+            if w.dim() == 2:
                 a, b, scale, *_ = pop.low_rank(i, w.shape[0], w.shape[1], dev, w.dtype)
-                c = scale[0::2] / sigma                                          # c_j
-                ahat = (a[0::2] * (coef * c)[:, None, None]).permute(1, 0, 2).reshape(w.shape[0], -1)
-                bhat = b[0::2].permute(1, 0, 2).reshape(w.shape[1], -1)          # [in, 4P]
-                a_hi = ahat.bfloat16()
-                a_lo = (ahat - a_hi.float()).bfloat16()
-                bb = bhat.bfloat16()
-                delta = torch.mm(torch.cat([a_hi, a_lo], dim=1), torch.cat([bb, bb], dim=1).T, out_dtype=torch.float32)
+                a_cat, b_cat = K.eggroll_update_operands(a, b, scale, coef, sigma)
+                # W <- round(W - lr * a_cat b_cat^T): one GEMM whose epilogue reads W, adds the
+                # fp32 product scaled by -lr and rounds once
+                w.addmm_(a_cat, b_cat.T, beta=1.0, alpha=alpha)
+            elif w.dim() == 1:
+                z = K.randn_keys(pop.keys(i), w.numel(), dev)                    # [P, numel]
+                w.copy_((w.float() + alpha * (coef @ z)).to(w.dtype))
             else:
                 raise NotImplementedError("EGGROLL updates 1-D and 2-D tensors")
-            w.copy_((w.float() - float(np.float32(lr)) * delta).to(w.dtype))
-        pop.pair_seeds = saved
 
     def step(self, tokens: torch.Tensor, pair_seeds: list[int], lr: float, strategy: str = "centered_rank",
              normalize_std: bool = True, chunk_pairs: int = 8, group=None) -> dict:

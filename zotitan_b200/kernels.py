@@ -520,3 +520,27 @@ def xent_rows(logits: torch.Tensor, targets: torch.Tensor, want_lse: bool = True
                                       correct.data_ptr() if correct is not None else None, _stream_ptr(dev)),
                 "zt_xent_rows")
     return loss, lse, correct
+
+
+def eggroll_update_operands(a: torch.Tensor, b: torch.Tensor, scale: torch.Tensor, coef: torch.Tensor,
+                            sigma: float, dtype: torch.dtype = torch.bfloat16):
+    """(a_cat [n, 8p], b_cat [k, 8p]) bf16 operands of the ES update GEMM of one 2-D tensor
+    (zt_eggroll_update_operands), from eggroll_factors' outputs for p pairs and the pairs'
+    coefficients: a_cat @ b_cat.T = sum_j coef_j c_j P_j Psi_j."""
+    if dtype != torch.bfloat16:
+        raise NotImplementedError("bf16 update operands only")
+    pairs = coef.numel()
+    n, k = a.shape[1], b.shape[1]
+    for t, name in ((a, "a"), (b, "b"), (scale, "scale"), (coef, "coef")):
+        _check_cuda(t, name)
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous fp32")
+    if a.shape != (2 * pairs, n, 4) or b.shape != (2 * pairs, k, 4) or scale.shape != (2 * pairs,):
+        raise ValueError("inconsistent shapes")
+    a_cat = torch.empty((n, 8 * pairs), dtype=torch.bfloat16, device=a.device)
+    b_cat = torch.empty((k, 8 * pairs), dtype=torch.bfloat16, device=a.device)
+    with torch.cuda.device(a.device):
+        L.check(L.load().zt_eggroll_update_operands(a.data_ptr(), b.data_ptr(), scale.data_ptr(), coef.data_ptr(),
+                                                    pairs, n, k, float(sigma), a_cat.data_ptr(), b_cat.data_ptr(),
+                                                    _stream_ptr(a.device)), "zt_eggroll_update_operands")
+    return a_cat, b_cat
