@@ -125,6 +125,14 @@ def test_planner_rejects_unsupported():
     from helpers import ns
     cfg = StepCase(_G, "mezo_f32_z1").cfg_dict
     cfg["perturbation"]["distribution"] = "low_rank"
+    assert StepPlanner(ns(cfg)).materialized          # one rank: supported (materialised directions)
+    with pytest.raises(NotImplementedError):
+        StepPlanner(ns(cfg), world=2, rank=0)          # the sharded schedule replays Gaussian fields
+    cfg["mom"]["momentum_method"] = "seed_window"
+    with pytest.raises(NotImplementedError):
+        StepPlanner(ns(cfg))                           # so does seed-window momentum
+    cfg["mom"]["momentum_method"] = "none"
+    cfg["perturbation"]["distribution"] = "sparse"
     with pytest.raises(NotImplementedError):
         StepPlanner(ns(cfg))
     cfg["perturbation"]["distribution"] = "gaussian"

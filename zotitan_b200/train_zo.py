@@ -42,7 +42,7 @@ import torch
 from . import _lib as L
 from .data import PrefetchLoader, get_batches
 from .distributed import gather_pair_values, local_pairs, world_info
-from .kernels import ParamTable, PassCfg, Stream
+from .kernels import ParamTable, PassCfg, Stream, param_key, randn
 from .schedule import BaseTrainConfig, wsd_is_constant, wsd_value
 
 
@@ -106,6 +106,26 @@ class ZOConfig:
     weight_decay: WeightDecayConfig = field(default_factory=WeightDecayConfig)
 
 
+def zeropower_via_newtonschulz(G: torch.Tensor) -> torch.Tensor:
+    """Polar factor of G by the hybrid Newton-Schulz iteration the reference's polar
+    perturbation uses (zotitan/train_zo.py:198-222; DeepSeek-V4 section 2.4): in bf16, the
+    wide orientation, X / (||X|| + 1e-7), 8 steps of aX + b(XX^T)X + c(XX^T)^2 X with
+    (3.4445, -4.7750, 2.0315), then 2 with (2, -1.5, 0.5). Evaluated eagerly (the reference
+    wraps it in torch.compile, whose fusion may round differently)."""
+    assert G.ndim >= 2
+    X = G.to(torch.bfloat16)
+    transposed = X.size(0) > X.size(1)
+    if transposed:
+        X = X.T
+    X = X / (X.norm() + 1e-7)
+    for a, b, c in [(3.4445, -4.7750, 2.0315)] * 8 + [(2.0, -1.5, 0.5)] * 2:
+        A = X @ X.T
+        X = a * X + b * (A @ X) + c * (A @ A @ X)
+    if transposed:
+        X = X.T
+    return X.to(G.dtype)
+
+
 # ── host-side planning (no device work; unit-testable on CPU) ───────────────────
 
 def f32(x) -> float:
@@ -133,18 +153,24 @@ class StepPlanner:
 
     def __init__(self, cfg: ZOConfig, total_steps: int = 0, rank: int = 0, world: int = 1,
                  sharded: bool | None = None):
-        if cfg.perturbation.distribution != "gaussian":
-            # The fused passes regenerate Gaussian fields; low-rank / polar directions
-            # (train_zo.py:304-320) are not part of this path.
-            raise NotImplementedError(
-                f"perturbation.distribution={cfg.perturbation.distribution!r} is not supported by the fused "
-                "zeroth-order passes (gaussian only)")
+        dist_kind = cfg.perturbation.distribution
+        if dist_kind not in ("gaussian", "low_rank", "polar"):
+            raise NotImplementedError(f"perturbation.distribution={dist_kind!r}")
+        # low_rank / polar directions of 2-D tensors (train_zo.py:304-320) are materialised
+        # per pair with the reference's own ops; 1-D tensors keep the fused Gaussian passes
+        self.materialized = dist_kind != "gaussian"
         self.cfg = cfg
         self._t = 0
         self._total_steps = total_steps
         self._seed_ctr = 0
         self.rank, self.world = rank, world
         self.sharded = world > 1 if sharded is None else bool(sharded)
+        if self.materialized and self.sharded:
+            raise NotImplementedError("low_rank / polar perturbations run on one rank: the seed-sharded schedule "
+                                      "replays Gaussian fields in its last pass")
+        if self.materialized and cfg.mom.momentum_method == "seed_window":
+            raise NotImplementedError("seed_window momentum regenerates Gaussian fields in registers; "
+                                      "low_rank / polar directions are not supported with it")
         # Sharded update: the step's last pass covers only this rank's unit range of a
         # flat parameter layout, followed by an all-gather of the updated master (set by
         # ZOOptimizer when the layout is in place).
@@ -302,6 +328,8 @@ class StepPlanner:
         if not self.need_ge:
             ge_mode = L.ZT_GE_NONE
             ge_scale = None
+        # per-pair grad_est coefficients of this step (the materialised directions use them)
+        self.last_ge = (ge_mode, list(ge_coefs), ge_scale)
 
         # seed-window state (:420-422) and replay weights (:337-345)
         mom_coefs = {}
@@ -442,9 +470,13 @@ class ZOOptimizer:
         # theta_0 for anchored decay stays in HBM (the reference pins it in host
         # memory and copies it every step, train_zo.py:274, :406)
         self.theta_0 = [p.clone() for p in self.params] if pl.needs_anchor else None
+        # low_rank / polar: 2-D tensors take materialised directions, 1-D ones the fused passes
+        self.lr_idx = [i for i, p in enumerate(self.params) if p.dim() >= 2] if pl.materialized else []
+        lr_set = set(self.lr_idx)
+        self.dense_idx = [i for i in range(len(self.params)) if i not in lr_set]
         # grad_est buffer of the on-the-fly accumulation (same size as the reference's
-        # zeros_like grad_est for z_batch > 1)
-        self.ge = [torch.zeros_like(p) for p in self.params] if pl.ge_onthefly else None
+        # zeros_like grad_est for z_batch > 1; dense tensors only)
+        self.ge = ([torch.zeros_like(self.params[i]) for i in self.dense_idx] if pl.ge_onthefly else None)
         dev = self.params[0].device
         self.vals_buf = torch.zeros(2 * max(1, cfg.z_batch), dtype=torch.float32, device=dev)
         self.layout = None
@@ -469,6 +501,19 @@ class ZOOptimizer:
             # model reads `live` (the parameters' own storage); `master` stays unperturbed
             self.master = [p.clone() for p in self.params]
             self.table = ParamTable(self.master, live=self.params, m=self.m, v=self.v, anchor=self.theta_0)
+        elif pl.materialized:
+            self.master = None
+            n = len(self.params)
+            sub = lambda lst, idx: None if lst is None else [lst[i] for i in idx]  # noqa: E731
+            self.table = (ParamTable(sub(self.params, self.dense_idx), n_params=n, indices=self.dense_idx,
+                                     m=sub(self.m, self.dense_idx), v=sub(self.v, self.dense_idx),
+                                     anchor=sub(self.theta_0, self.dense_idx), ge=self.ge)
+                          if self.dense_idx else None)
+            self.lr_ge = [torch.zeros_like(self.params[i]) for i in self.lr_idx]
+            self.lr_table = (ParamTable(sub(self.params, self.lr_idx), n_params=n, indices=self.lr_idx,
+                                        m=sub(self.m, self.lr_idx), v=sub(self.v, self.lr_idx),
+                                        anchor=sub(self.theta_0, self.lr_idx), ge=self.lr_ge)
+                             if self.lr_idx else None)
         else:
             self.master = None
             self.table = ParamTable(self.params, m=self.m, v=self.v, anchor=self.theta_0, ge=self.ge)
@@ -490,7 +535,54 @@ class ZOOptimizer:
     def _run(self, spec: PassSpec) -> None:
         if spec.cfg.dev_pair is not None:
             spec.cfg.dev_vals = self.vals_buf.data_ptr() + 8 * spec.cfg.dev_pair
-        self.table.run(spec.cfg, spec.streams)
+        if self.table is not None:
+            self.table.run(spec.cfg, spec.streams)
+
+    # -- materialised low_rank / polar directions (zotitan/train_zo.py:295-322) -------------
+    def _lowrank_z(self, seed: int) -> list:
+        """The reference's _sample_z for the 2-D tensors: P [m, r] and Psi [r, n] from the
+        noise source (keys of positions i + 2n and i + n), cast to the parameter dtype,
+        polar-orthogonalised for "polar", z = P @ Psi scaled to ||z||_F = sqrt(numel)."""
+        pc = self.cfg.perturbation
+        n = len(self.params)
+        out = []
+        for i in self.lr_idx:
+            p = self.params[i]
+            m, r = p.shape[0], min(pc.rank, p.shape[0])
+            P = randn(param_key(seed, n, i + 2 * n), m * r, p.device).view(m, r).to(p.dtype)
+            if pc.distribution == "polar":
+                P, _ = torch.linalg.qr(P)
+            Psi = randn(param_key(seed, n, i + n), r * p.shape[1], p.device).view(r, p.shape[1]).to(p.dtype)
+            if pc.distribution == "polar":
+                Psi = zeropower_via_newtonschulz(Psi)
+            z = P @ Psi
+            out.append(z * (p.numel() ** 0.5 / (z.norm() + 1e-7)))
+        return out
+
+    def _lr_apply(self, z: list, scale: float) -> None:
+        """_apply_z (:350-351) on the 2-D tensors."""
+        if self.lr_idx:
+            torch._foreach_add_([self.params[i] for i in self.lr_idx], z, alpha=scale)
+
+    def _lr_finish(self, spec: PassSpec) -> None:
+        """grad_est of the 2-D tensors from the regenerated directions with this step's pair
+        coefficients (:550-556, :575-577), then the same optimizer stages as the fused pass
+        (ge read from the buffer; no noise streams)."""
+        if not self.lr_idx:
+            return
+        import dataclasses
+        pl = self.planner
+        ge_mode, coefs, _ = pl.last_ge
+        if ge_mode == L.ZT_GE_PRODUCT:
+            for g, r in zip(self.lr_ge, torch._foreach_mul(self._lowrank_z(pl.seeds[0]), coefs[0])):
+                g.copy_(r)
+        elif ge_mode == L.ZT_GE_ACCUM:
+            torch._foreach_zero_(self.lr_ge)
+            for j, seed in enumerate(pl.seeds):
+                torch._foreach_add_(self.lr_ge, self._lowrank_z(seed), alpha=coefs[j])
+        cfg = dataclasses.replace(spec.cfg, ge_mode=L.ZT_GE_ACCUM if ge_mode != L.ZT_GE_NONE else L.ZT_GE_NONE,
+                                  ge_load=ge_mode != L.ZT_GE_NONE, ge_store=False, dev_pair=None, dev_vals=0)
+        self.lr_table.run(cfg, [])
 
     def _acquire(self, model, batch):
         s = self.score_fn(model, batch)
@@ -506,12 +598,18 @@ class ZOOptimizer:
         dev = self.params[0].device
         vals_t, metric_dicts = [], []
         prev = None
+        eps = self.cfg.eps
         with torch.inference_mode():
             for j in local:
+                z = self._lowrank_z(pl.seeds[j]) if self.lr_idx else None
                 self._run(pl.plus_pass(j, prev))
+                self._lr_apply(z, eps)
                 vp, mp = self._acquire(model, batches[j])
                 self._run(pl.minus_pass(j))
+                self._lr_apply(z, -2 * eps)
                 vn, mn = self._acquire(model, batches[j])
+                self._lr_apply(z, eps)
+                del z
                 prev = j
                 vp = vp.detach().float().reshape(()).to(dev)
                 vn = vn.detach().float().reshape(()).to(dev)
@@ -527,6 +625,7 @@ class ZOOptimizer:
             metrics_avg = _aggregate_metrics(metric_dicts)
         spec, metrics = pl.finish(vals)
         with torch.inference_mode():
+            self._lr_finish(spec)
             self._run(spec)
             if self.layout is not None:
                 import torch.distributed as dist
