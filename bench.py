@@ -311,46 +311,45 @@ def run_reference(args, rank, world):
 
 # ── EGGROLL population evaluation (Llama-3-8B shape) ─────────────────────────────────────
 
-def eggroll_member_evals(dev, rank: int, world: int, pairs_per_rank: int = 16, pairs_per_chunk: int = 8):
-    """Member-evals/s of the EGGROLL population forward on the Llama-3-8B-shaped bf16 model:
-    members in antithetic pairs (seeds from the pair counter, rank r takes pairs r, r+W, ...),
-    each scored with cross-entropy on a shared 4 x 256-token batch, sigma = 1e-3, rank-4
-    perturbations regenerated from Philox seeds; one all-gather of the member losses.
-    Weak scaling: fixed members per rank. Timed with CUDA events, max over ranks."""
+def eggroll_member_evals(dev, rank: int, world: int, total_pairs: int = 512, pairs_per_chunk: int = 8):
+    """Member-evals/s of the EGGROLL population forward: the
+    Llama-3-8B-shaped bf16 model, 1024 members (512 antithetic pairs, seeds 0..511) each
+    scored with cross-entropy on a shared 4 x 256-token batch, sigma = 1e-3, rank-4
+    perturbations regenerated from Philox seeds, the population sharded over the ranks
+    (rank r scores pairs r, r+W, ... in chunks of 8 pairs) and one all-gather of the member
+    losses. Strong scaling: the population is fixed. Timed with CUDA events, max over
+    ranks. The ES update every rank then applies (rank-4*512 GEMMs over every weight) is
+    timed separately."""
     import torch
     import torch.distributed as dist
 
     from zotitan_b200 import kernels as K
+    from zotitan_b200.distributed import gather_pair_values, local_pairs
     from zotitan_b200.eggroll import EggrollConfig, EggrollPopulation
     from zotitan_b200.synthetic import LLAMA_8B, build_llama, linear_flops_per_token
     model = build_llama(LLAMA_8B, device=dev, seed=0, max_positions=1024)
     pop = EggrollPopulation(model, EggrollConfig(sigma=1e-3))
     g = torch.Generator().manual_seed(7)
     tokens = torch.randint(0, LLAMA_8B.vocab, (4, 256), generator=g).to(dev)
-    my_pairs = list(range(rank, world * pairs_per_rank, world))
-    pop.evaluate(tokens, my_pairs[:pairs_per_chunk])          # warm-up chunk
+    mine = local_pairs(total_pairs, rank, world)
+    pop.evaluate(tokens, list(range(10_000, 10_000 + pairs_per_chunk)))   # warm-up chunk (other seeds)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
-    losses = []
-    for c in range(0, len(my_pairs), pairs_per_chunk):
-        losses.append(pop.evaluate(tokens, my_pairs[c:c + pairs_per_chunk]))
-    mine = torch.cat(losses)
-    if world > 1:
-        allv = torch.empty(world * mine.numel(), device=dev)
-        dist.all_gather_into_tensor(allv, mine)
+    local = pop.evaluate_all(tokens, mine, pairs_per_chunk).view(-1, 2)
+    rows = gather_pair_values(local, total_pairs, rank, world) if world > 1 else local
     t1.record()
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1)
-    # the ES update every rank applies after the all-gather: rank-4*pairs GEMMs over all
-    # 2-D tensors of the model (pairs of the whole population), timed on its own
-    u0, u1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    all_pairs = list(range(world * pairs_per_rank))
-    coefs = [((j % 7) - 3) / (7.0 * len(all_pairs)) for j in all_pairs]
-    pop.apply_update(all_pairs, [0.0] * len(all_pairs), lr=1e-6)   # untimed warm-up (leaves W unchanged)
+    # the ES update every rank applies after the all-gather: rank-4*512 GEMMs over all 2-D
+    # tensors of the model, timed on its own after an untimed warm-up (W unchanged by it)
+    all_pairs = list(range(total_pairs))
+    coefs = [((j % 7) - 3) / (7.0 * total_pairs) for j in all_pairs]
+    pop.apply_update(all_pairs, [0.0] * total_pairs, lr=1e-6)
     torch.cuda.synchronize()
+    u0, u1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     u0.record()
     pop.apply_update(all_pairs, coefs, lr=1e-6)
     u1.record()
@@ -361,16 +360,17 @@ def eggroll_member_evals(dev, rank: int, world: int, pairs_per_rank: int = 16, p
         t = torch.tensor([ms, upd_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, upd_ms = t.tolist()
-    members = 2 * pairs_per_rank * world
+    members = 2 * total_pairs
     tokens_per_member = tokens.numel()
     lin_flops = linear_flops_per_token(LLAMA_8B) * tokens_per_member * members
+    mean_loss = float(rows.mean())
     del pop, model
     torch.cuda.empty_cache()
     return {"metric": "EGGROLL member-evals/s (Llama-3-8B shape)", "value": members / (ms * 1e-3),
-            "unit": "member-evals/s", "members": members, "members_per_rank": 2 * pairs_per_rank,
-            "tokens_per_member": tokens_per_member, "sigma": 1e-3, "rank": 4, "scaling": "weak",
+            "unit": "member-evals/s", "members": members, "members_per_rank": 2 * len(mine),
+            "tokens_per_member": tokens_per_member, "sigma": 1e-3, "rank": 4, "scaling": "strong",
             "ms": ms, "linear_tflops": lin_flops / (ms * 1e-3) / 1e12, "device_error": err,
-            "mean_loss": float(mine.mean()), "es_update_ms": upd_ms,
+            "mean_loss": mean_loss, "es_update_ms": upd_ms, "es_update_pairs": total_pairs,
             "es_step_members_per_s": members / ((ms + upd_ms) * 1e-3)}
 
 
