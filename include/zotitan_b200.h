@@ -413,6 +413,14 @@ ZT_API int zt_eggroll_update_operands(const float* a, const float* b, const floa
                                       int32_t pairs, int64_t n, int64_t k, float sigma, void* a_cat, void* b_cat,
                                       void* stream);
 
+/* The tail of a LoRA linear (zotitan/lora.py:77-86) in one pass over the output:
+ *   out[t, c] = bf16(out[t, c] + bf16(scale * sum_r xa[t, r] b[c, r]))
+ * with out [rows, n] bf16 holding the base layer's output (updated in place), xa [rows, r]
+ * fp32 = lora_A(x) and b [n, r] fp32 = lora_B.weight; the sum runs over r in order in
+ * fp32. r in {4, 8, 16, 32, 64}; xa and b row-major and contiguous. */
+ZT_API int zt_lora_add(void* out, const float* xa, const float* b, float scale, int64_t rows, int64_t n, int32_t r,
+                       void* stream);
+
 /* ---- the scorer: next-token cross-entropy statistics ------------------------------ */
 
 /* Per-row statistics of bf16 logits [rows, vocab] (row stride ld elements, ld % 8 == 0,

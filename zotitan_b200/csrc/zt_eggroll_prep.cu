@@ -311,6 +311,74 @@ __global__ void __launch_bounds__(256) update_operands_kernel(const float4* __re
   }
 }
 
+// ---- LoRA adapter tail ----------------------------------------------------------------
+
+// out[t, c] = bf16(out[t, c] + bf16(scale * sum_r xa[t, r] B[c, r])), the tail of a LoRA
+// linear (lora_B(lora_A(x)) * scaling cast to bf16 and added to the base output) in one
+// pass. A block owns 256*C columns and a band of kLoraBand rows whose xa rows it stages in
+// shared memory once; each thread keeps the B rows of its C adjacent columns in registers
+// and walks the band 16 rows at a time, the 16 x C outputs loaded together (4-byte
+// accesses for C = 2) before the arithmetic.
+constexpr int kLoraBand = 128, kLoraStep = 16;
+
+template <int R, int C>
+__global__ void __launch_bounds__(256) lora_add_kernel(__nv_bfloat16* __restrict__ out, const float* __restrict__ xa,
+                                                       const float* __restrict__ bw, float scale, int64_t rows,
+                                                       int32_t n) {
+  __shared__ __align__(16) float sxa[kLoraBand][R];
+  const int64_t band0 = (int64_t)blockIdx.y * kLoraBand;
+  const int nb = (int)((rows - band0) < kLoraBand ? (rows - band0) : kLoraBand);
+  for (int i = threadIdx.x; i < kLoraBand * R; i += 256) sxa[i / R][i % R] = i / R < nb ? xa[band0 * R + i] : 0.f;
+  __syncthreads();
+  const int c0 = (blockIdx.x * 256 + threadIdx.x) * C;
+  if (c0 >= n) return;  // n % C == 0: a thread's columns are all in range or all out
+  float b[C][R];
+#pragma unroll
+  for (int j = 0; j < C; ++j)
+#pragma unroll
+    for (int r = 0; r < R; r += 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(bw + (size_t)(c0 + j) * R + r));
+      b[j][r] = v.x; b[j][r + 1] = v.y; b[j][r + 2] = v.z; b[j][r + 3] = v.w;
+    }
+  __nv_bfloat16* ob = out + band0 * n + c0;
+  for (int i0 = 0; i0 < nb; i0 += kLoraStep) {
+    float o[kLoraStep][C];
+#pragma unroll
+    for (int i = 0; i < kLoraStep; ++i) {  // independent loads, in flight together
+      if (C == 2) {
+        const __nv_bfloat162 h = i0 + i < nb ? *reinterpret_cast<const __nv_bfloat162*>(ob + (int64_t)(i0 + i) * n)
+                                             : __floats2bfloat162_rn(0.f, 0.f);
+        o[i][0] = __low2float(h);
+        o[i][C - 1] = __high2float(h);
+      } else {
+        o[i][0] = i0 + i < nb ? __bfloat162float(ob[(int64_t)(i0 + i) * n]) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kLoraStep; ++i) {
+      float v[C];
+#pragma unroll
+      for (int j = 0; j < C; ++j) v[j] = 0.f;
+#pragma unroll
+      for (int r = 0; r < R; r += 4) {
+        const float4 xv = *reinterpret_cast<const float4*>(&sxa[i0 + i][r]);
+#pragma unroll
+        for (int j = 0; j < C; ++j)
+          v[j] = fmaf(xv.w, b[j][r + 3], fmaf(xv.z, b[j][r + 2], fmaf(xv.y, b[j][r + 1], fmaf(xv.x, b[j][r], v[j]))));
+      }
+      if (i0 + i < nb) {
+        float y[C];
+#pragma unroll
+        for (int j = 0; j < C; ++j) y[j] = o[i][j] + __bfloat162float(__float2bfloat16_rn(v[j] * scale));
+        if (C == 2)
+          *reinterpret_cast<__nv_bfloat162*>(ob + (int64_t)(i0 + i) * n) = __floats2bfloat162_rn(y[0], y[C - 1]);
+        else
+          ob[(int64_t)(i0 + i) * n] = __float2bfloat16_rn(y[0]);
+      }
+    }
+  }
+}
+
 int stream_grid(int64_t items, int per_sm) {
   const int64_t want = (items + 255) / 256;
   const int64_t cap = (int64_t)zt::sm_count() * per_sm;
@@ -443,6 +511,41 @@ int zt_eggroll_update_operands(const float* a, const float* b, const float* scal
       reinterpret_cast<const float4*>(a), reinterpret_cast<const float4*>(b), scale, coef, pairs, n, k, sigma,
       static_cast<uint4*>(a_cat), static_cast<uint4*>(b_cat));
   return zt::check_cuda(cudaGetLastError(), "zt_eggroll_update_operands launch");
+}
+
+int zt_lora_add(void* out, const float* xa, const float* b, float scale, int64_t rows, int64_t n, int32_t r,
+                void* stream) {
+  zt::clear_error();
+  if (rows < 0 || n <= 0) return zt::set_error(ZT_ERR_INVALID, "zt_lora_add: bad shape");
+  if (rows == 0) return ZT_OK;
+  if (!out || !xa || !b) return zt::set_error(ZT_ERR_INVALID, "zt_lora_add: null pointer");
+  if (n > (int64_t)INT32_MAX) return zt::set_error(ZT_ERR_LIMIT, "zt_lora_add: shape too large");
+  if (!aligned16(b)) return zt::set_error(ZT_ERR_INVALID, "zt_lora_add: b not 16-byte aligned");
+  if (r != 4 && r != 8 && r != 16 && r != 32 && r != 64)
+    return zt::set_error(ZT_ERR_INVALID, "zt_lora_add: rank must be 4, 8, 16, 32 or 64");
+  const int cols = (r <= 32 && n % 2 == 0 && ((uintptr_t)out & 3) == 0) ? 2 : 1;   // columns per thread
+  const dim3 grid((unsigned)((n + 256 * cols - 1) / (256 * cols)), (unsigned)((rows + kLoraBand - 1) / kLoraBand));
+  if (grid.y > 65535u) return zt::set_error(ZT_ERR_LIMIT, "zt_lora_add: too many rows");
+  cudaStream_t s = zt::as_stream(stream);
+  __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
+  const int32_t ni = (int32_t)n;
+  if (cols == 2) {
+    switch (r) {
+      case 4: lora_add_kernel<4, 2><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      case 8: lora_add_kernel<8, 2><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      case 16: lora_add_kernel<16, 2><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      default: lora_add_kernel<32, 2><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+    }
+  } else {
+    switch (r) {
+      case 4: lora_add_kernel<4, 1><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      case 8: lora_add_kernel<8, 1><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      case 16: lora_add_kernel<16, 1><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      case 32: lora_add_kernel<32, 1><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      default: lora_add_kernel<64, 1><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+    }
+  }
+  return zt::check_cuda(cudaGetLastError(), "zt_lora_add launch");
 }
 
 }  // extern "C"

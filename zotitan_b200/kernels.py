@@ -544,3 +544,22 @@ def eggroll_update_operands(a: torch.Tensor, b: torch.Tensor, scale: torch.Tenso
                                                     pairs, n, k, float(sigma), a_cat.data_ptr(), b_cat.data_ptr(),
                                                     _stream_ptr(a.device)), "zt_eggroll_update_operands")
     return a_cat, b_cat
+
+
+def lora_add_(out: torch.Tensor, xa: torch.Tensor, b: torch.Tensor, scale: float) -> torch.Tensor:
+    """out += bf16(scale * xa @ b.T) in place with bf16 rounding of the delta and of the sum
+    (zt_lora_add): out [rows, n] bf16, xa [rows, r] fp32, b [n, r] fp32."""
+    for t, name in ((out, "out"), (xa, "xa"), (b, "b")):
+        _check_cuda(t, name)
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    if out.dtype != torch.bfloat16 or xa.dtype != torch.float32 or b.dtype != torch.float32:
+        raise ValueError("out must be bf16, xa and b fp32")
+    rows, n = out.shape
+    r = xa.shape[1]
+    if xa.shape[0] != rows or b.shape != (n, r):
+        raise ValueError("inconsistent shapes")
+    with torch.cuda.device(out.device):
+        L.check(L.load().zt_lora_add(out.data_ptr(), xa.data_ptr(), b.data_ptr(), float(scale), rows, n, r,
+                                     _stream_ptr(out.device)), "zt_lora_add")
+    return out

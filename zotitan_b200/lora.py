@@ -24,6 +24,7 @@ LORA_ALPHA = 32
 LORA_TARGETS = {"q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"}
 
 _DTYPES: dict[str, torch.dtype] = {"bf16": torch.bfloat16, "fp32": torch.float32}
+_FUSED_R = (4, 8, 16, 32, 64)   # adapter ranks of the fused CUDA tail
 
 
 @dataclass
@@ -61,7 +62,28 @@ class LoRALinear(nn.Module):
 
     def forward(self, x):
         out = self.base_linear(x)
-        delta = self.lora_B(self.lora_A(x.to(self.lora_dtype))) * self.scaling
+        aw, bw = self.lora_A.weight, self.lora_B.weight
+        if (not torch.is_grad_enabled() and out.is_cuda and out.dtype == torch.bfloat16 and x.dtype == torch.bfloat16
+                and aw.dtype == torch.float32 and bw.dtype == torch.float32 and bw.shape[1] in _FUSED_R
+                and out.is_contiguous()):
+            # Gradients off (the zeroth-order step): x A^T on the tensor cores from the bf16
+            # activations against A split into three bf16 parts that sum to it exactly (each
+            # product exact, fp32 accumulation: the fp32 product up to summation order), then
+            # lora_B(xa) * scaling cast to bf16 and added to `out` in one pass (zt_lora_add),
+            # with the reference's rounding points. No autograd record is made.
+            from . import kernels as K
+            r, n = bw.shape[1], out.shape[-1]
+            a0 = aw.bfloat16()
+            rest = aw - a0.float()
+            a1 = rest.bfloat16()
+            a2 = (rest - a1.float()).bfloat16()
+            x2 = x.reshape(-1, x.shape[-1])
+            xa3 = torch.mm(x2, torch.cat([a0, a1, a2], dim=0).T, out_dtype=torch.float32)   # [rows, 3r]
+            xa = (xa3[:, :r] + xa3[:, r:2 * r] + xa3[:, 2 * r:]).contiguous()
+            K.lora_add_(out.view(-1, n), xa, bw.detach(), self.scaling)
+            return out
+        xa = self.lora_A(x.to(self.lora_dtype))
+        delta = self.lora_B(xa) * self.scaling
         return out + delta.to(out.dtype)
 
 
