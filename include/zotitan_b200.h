@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define ZT_ABI_VERSION 4
+#define ZT_ABI_VERSION 5
 
 /* dtypes of parameter tensors */
 #define ZT_F32 0
@@ -108,6 +108,8 @@ typedef struct zt_plan {
   uint32_t n_params;           /* length of the reference's named-parameter list */
   int32_t device;
   int32_t buffers;             /* ZT_HAS_* bits: optional buffers present on every tensor */
+  int32_t props;               /* ZT_PLAN_* bits: layout properties every tensor shares */
+  int32_t reserved;
 } zt_plan;
 
 #define ZT_HAS_LIVE 1
@@ -115,6 +117,14 @@ typedef struct zt_plan {
 #define ZT_HAS_V 4
 #define ZT_HAS_ANCHOR 8
 #define ZT_HAS_GE 16
+
+/* zt_plan.props. With VEC8 and one uniform dtype, zt_pass runs the pass shapes that
+ * dominate a step (one or two plain noise streams; the restore + grad_est accumulate +
+ * next-perturb pass) through kernels specialised for that dtype. Results are identical. */
+#define ZT_PLAN_VEC8 1       /* every numel a multiple of 8, every present buffer 16-byte aligned */
+#define ZT_PLAN_ALL_F32 2
+#define ZT_PLAN_ALL_BF16 4
+#define ZT_PLAN_ALL_F16 8
 
 #define ZT_UNIT_ELEMS 2048
 

@@ -37,10 +37,10 @@ def cuda_noise(K):
     return noise
 
 
-def make_case(seed, with_live=False, with_m=False, with_v=False, with_anchor=False, with_ge=False):
+def make_case(seed, with_live=False, with_m=False, with_v=False, with_anchor=False, with_ge=False, specs=SPECS):
     rng = np.random.default_rng(seed)
     host, dev, keep = [], {"data": [], "live": [], "m": [], "v": [], "anchor": [], "ge": []}, []
-    for i, (n, dt) in enumerate(SPECS):
+    for i, (n, dt) in enumerate(specs):
         unaligned = dt == "unaligned"
         dt = ph.BF16 if unaligned else dt
         def arr(scale, positive=False):
@@ -79,15 +79,17 @@ def compare(host, dev, keys=("data", "live", "m", "v", "ge")):
             if t[k] is None:
                 continue
             got = dev[k][i].float().cpu().numpy()
-            assert np.array_equal(got, t[k]), (i, k, SPECS[i], int(np.sum(got != t[k])))
+            assert np.array_equal(got, t[k]), (i, k, t[k].size, t["dtype"], int(np.sum(got != t[k])))
 
 
 N_PARAMS = 40  # tensors sit at indices 0..9 of a 40-long parameter list
 
 
-def run_both(K, cfg, streams, dev_values=None, **case_kw):
+def run_both(K, cfg, streams, dev_values=None, props=None, **case_kw):
     host, dev, keep = make_case(3, **case_kw)
     tab = table(K, dev, N_PARAMS)
+    if props is not None:
+        assert tab.plan.props == props
     if dev_values is not None:
         vals = torch.tensor(dev_values, dtype=torch.float32, device="cuda")
         cfg.dev_vals = vals.data_ptr()
@@ -118,6 +120,46 @@ def test_onthefly_accumulation_with_device_coefficient(K, tau):
 def L():
     from zotitan_b200 import _lib
     return _lib
+
+
+UNIFORM_SIZES = [8, 2048, 4096, 24, 100000, 2056, 16]
+
+
+@pytest.mark.parametrize("dt", [ph.BF16, ph.F32, ph.F16])
+def test_uniform_plan_specialised_shapes(K, dt):
+    """A plan whose tensors share one dtype and are whole, 16-byte aligned 8-element groups
+    (ZT_PLAN_VEC8) runs the one-stream (+eps, -2eps, live copies), two-stream and
+    restore + accumulate + perturb passes through kernels specialised for that dtype:
+    every buffer they write is bit-identical to the oracle. The last pass (update) still
+    takes the generic kernel on the same plan."""
+    l = L()
+    f = lambda x: float(np.float32(x))  # noqa: E731
+    e, m2 = f(1e-3), f(-2e-3)
+    props = l.ZT_PLAN_VEC8 | {ph.BF16: l.ZT_PLAN_ALL_BF16, ph.F32: l.ZT_PLAN_ALL_F32, ph.F16: l.ZT_PLAN_ALL_F16}[dt]
+    specs = [(n, dt) for n in UNIFORM_SIZES]
+    live, data = l.ZT_BUF_LIVE, l.ZT_BUF_DATA
+    acc = dict(ge_mode=l.ZT_GE_ACCUM, ge_store=True, dev_inv2eps=f(1 / f(2e-3)), dev_invz=f(1 / f(3)),
+               dev_tau=float("inf"))
+    cases = [
+        (K.PassCfg(), [K.Stream(60, (e,))], None, {}),
+        (K.PassCfg(), [K.Stream(61, (m2,))], None, {}),
+        (K.PassCfg(src=live, dst=live), [K.Stream(62, (m2,))], None, {"with_live": True}),
+        (K.PassCfg(src=data, dst=live), [K.Stream(63, (e,))], None, {"with_live": True}),
+        (K.PassCfg(src=data, dst=data | live), [K.Stream(63, (e,))], None, {"with_live": True}),
+        (K.PassCfg(), [K.Stream(64, (e,)), K.Stream(65, (e,))], None, {}),
+        (K.PassCfg(ge_load=True, **acc), [K.Stream(66, (e,), ge_dev=True), K.Stream(67, (e,))], (2.0137, 2.0051),
+         {"with_ge": True}),
+        (K.PassCfg(ge_load=False, **acc), [K.Stream(68, (e,), ge_dev=True), K.Stream(69, (e,))], (1.5, 1.7),
+         {"with_ge": True}),
+        (K.PassCfg(ge_load=True, **{**acc, "dev_tau": f(3.0)}), [K.Stream(70, (e,), ge_dev=True), K.Stream(71, (e,))],
+         (2.5, 2.0), {"with_ge": True}),
+        (K.PassCfg(ge_mode=l.ZT_GE_ACCUM, ge_load=True, ge_store=True), [K.Stream(72, (e,), ge=f(0.3)),
+                                                                        K.Stream(73, (e,))], None, {"with_ge": True}),
+        (K.PassCfg(ge_mode=l.ZT_GE_ACCUM, ge_load=True, update=True, lr=f(1e-2)), [K.Stream(74, (e,), ge=f(0.7))],
+         None, {"with_ge": True}),
+    ]
+    for cfg, streams, dv, kw in cases:
+        run_both(K, cfg, streams, dev_values=dv, props=props, specs=specs, **kw)
 
 
 def test_perturb_and_restore_chain(K):

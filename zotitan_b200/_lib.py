@@ -22,6 +22,7 @@ ZT_GE_NONE, ZT_GE_PRODUCT, ZT_GE_ACCUM = 0, 1, 2
 ZT_MOM_NONE, ZT_MOM_STORED_EMA, ZT_MOM_SEED_WINDOW = 0, 1, 2
 ZT_WD_NONE, ZT_WD_STANDARD, ZT_WD_ANCHORED_L2, ZT_WD_ANCHORED_L1 = 0, 1, 2, 3
 ZT_BUF_DATA, ZT_BUF_LIVE = 1, 2
+ZT_PLAN_VEC8, ZT_PLAN_ALL_F32, ZT_PLAN_ALL_BF16, ZT_PLAN_ALL_F16 = 1, 2, 4, 8
 
 # every function include/zotitan_b200.h declares
 EXPORTS = ("zt_last_error", "zt_abi_version", "zt_param_key", "zt_philox_words", "zt_randn",
@@ -32,7 +33,7 @@ EXPORTS = ("zt_last_error", "zt_abi_version", "zt_param_key", "zt_philox_words",
 ZT_STATIC_MAX_TENSORS = 1024
 ZT_EGGROLL_MAX_PAIRS = 512
 ZT_EGGROLL_FACTOR_WORK_FLOATS = 64 * 20
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 
 class ZtTensor(ctypes.Structure):
@@ -44,7 +45,8 @@ class ZtTensor(ctypes.Structure):
 class ZtPlan(ctypes.Structure):
     _fields_ = [("tensors", ctypes.c_void_p), ("unit_prefix", ctypes.c_void_p), ("n_units", ctypes.c_int64),
                 ("numel_total", ctypes.c_int64), ("n_tensors", ctypes.c_int32), ("n_params", ctypes.c_uint32),
-                ("device", ctypes.c_int32), ("buffers", ctypes.c_int32)]
+                ("device", ctypes.c_int32), ("buffers", ctypes.c_int32), ("props", ctypes.c_int32),
+                ("reserved", ctypes.c_int32)]
 
 
 class ZtStream(ctypes.Structure):

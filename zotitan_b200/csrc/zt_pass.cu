@@ -383,6 +383,192 @@ full_kernel(const __grid_constant__ PassParams P) {
   walk_units<true, kFullEpt>(P);
 }
 
+// ---- kernels specialised for the pass shapes that dominate a step -------------------
+// For plans whose tensors share one dtype and whose 8-element groups are all whole and
+// 16-byte aligned (ZT_PLAN_VEC8), these shapes run without the per-unit dtype dispatch,
+// the scalar fallback and the stream loop of the generic kernels. That keeps the
+// register footprint low enough for more resident warps. Arithmetic and its order are
+// those of run_chain / run_full, so the results are identical.
+enum FastShape : int {
+  kFastChain1 = 0,  // one stream, one coefficient, no roles (the +eps and -2eps passes)
+  kFastChain2 = 1,  // two such streams (restore one pair, perturb the next)
+  kFastAccum = 2,   // stream 0: +a z and its grad_est term (ACCUM, stored); stream 1: +a z
+  kFastShapes = 3,
+};
+
+#ifndef ZT_FAST_CHAIN_MINB
+#define ZT_FAST_CHAIN_MINB 5
+#endif
+#ifndef ZT_FAST_ACCUM_MINB
+#define ZT_FAST_ACCUM_MINB 4
+#endif
+
+// 8 elements as 32-bit storage words: two per word for 16-bit formats, one for fp32.
+template <int DT> struct Words {
+  static constexpr int kBytes = Elem<DT>::kBytes;
+  static constexpr int kPer = 4 / kBytes;
+  static constexpr int kNW = 8 / kPer;
+  __device__ static __forceinline__ void unpack(uint32_t w, float (&v)[kPer]) {
+    if constexpr (DT == ZT_F32) {
+      v[0] = __uint_as_float(w);
+    } else if constexpr (DT == ZT_BF16) {
+      v[0] = __uint_as_float(w << 16);
+      v[1] = __uint_as_float(w & 0xffff0000u);
+    } else {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+      v[0] = f.x;
+      v[1] = f.y;
+    }
+  }
+  __device__ static __forceinline__ uint32_t pack(const float (&v)[kPer]) {
+    if constexpr (DT == ZT_F32) {
+      return __float_as_uint(v[0]);
+    } else if constexpr (DT == ZT_BF16) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(v[0], v[1]);
+      return *reinterpret_cast<const uint32_t*>(&h);
+    } else {
+      const __half2 h = __floats2half2_rn(v[0], v[1]);
+      return *reinterpret_cast<const uint32_t*>(&h);
+    }
+  }
+};
+
+// Per-tensor state of the unit being processed. It is block-uniform and kept in shared
+// memory, so it holds no registers across the noise loop. Unit and element indices are
+// 32-bit: the host takes this path only when the plan has fewer than 2^31 units, and a
+// tensor has fewer than 2^31 elements.
+struct FastTensor {
+  const char* src;
+  char* data;
+  char* live;
+  char* ge;
+  uint32_t numel;
+  int32_t lo, hi;
+  uint32_t key0, key1;
+};
+
+__device__ __forceinline__ void st_global16(char* p, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+  __stwb(reinterpret_cast<uint4*>(p), make_uint4(x, y, z, w));
+}
+
+template <int NW>
+__device__ __forceinline__ void st_words_global(char* p, const uint32_t (&w)[NW]) {
+  static_assert(NW % 4 == 0, "16-byte groups");
+#pragma unroll
+  for (int i = 0; i < NW / 4; ++i) st_global16(p + 16 * i, w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+}
+
+template <int DT, int SHAPE>
+__device__ __forceinline__ void fast_walk(const PassParams& P) {
+  using W = Words<DT>;
+  const zt_pass_cfg& c = P.cfg;
+  const KStream& S0 = P.streams[0];
+  const KStream& S1 = P.streams[1];
+  const float a0 = S0.chain[0];
+  const float a1 = S1.chain[0];
+  float gcoef = 0.0f;
+  if (SHAPE == kFastAccum) {
+    gcoef = S0.ge_coef;
+    if (S0.flags & ZT_STREAM_GE_DEV) {  // as walk_units: (v+ - v-) / (2 eps), clamp, / z_batch
+      const float d = __fsub_rn(__ldg(c.dev_vals), __ldg(c.dev_vals + 1));
+      float pg = __fmul_rn(d, c.dev_inv2eps);
+      pg = pg < -c.dev_tau ? -c.dev_tau : (pg > c.dev_tau ? c.dev_tau : pg);
+      gcoef = __fmul_rn(pg, c.dev_invz);
+    }
+  }
+  __shared__ FastTensor st;
+  const int32_t n_units = (int32_t)P.n_units;
+  int32_t lo = 0, hi = -1;
+  for (int32_t u = (int32_t)P.unit_begin + (int32_t)blockIdx.x; u < n_units; u += (int32_t)gridDim.x) {
+    if (u < lo || u >= hi) {  // u, lo and hi are block-uniform
+      __syncthreads();  // every thread is done with the previous tensor's state
+      if (threadIdx.x == 0) {
+        const int ti = find_tensor(P.unit_prefix, P.n_tensors, u);
+        const zt_tensor& t = P.tensors[ti];
+        st.lo = (int32_t)__ldg(P.unit_prefix + ti);
+        st.hi = (int32_t)__ldg(P.unit_prefix + ti + 1);
+        st.numel = (uint32_t)t.numel;
+        st.src = static_cast<const char*>(c.src == ZT_BUF_LIVE ? t.live : t.data);
+        st.data = static_cast<char*>(t.data);
+        st.live = static_cast<char*>(t.live);
+        st.ge = static_cast<char*>(t.ge);
+        st.key0 = zt::param_key(S0.seed, P.n_params, (uint32_t)t.index);
+        st.key1 = SHAPE != kFastChain1 ? zt::param_key(S1.seed, P.n_params, (uint32_t)t.index) : 0u;
+      }
+      __syncthreads();
+      lo = st.lo;
+      hi = st.hi;
+    }
+    const uint32_t e0 = (uint32_t)(u - lo) * ZT_UNIT_ELEMS + threadIdx.x * 8u;
+    if (e0 >= st.numel) continue;
+    const size_t off = (size_t)e0 * W::kBytes;
+    // Values stay packed in their storage format between noise streams: packing with
+    // round-to-nearest is the rounding to the parameter dtype after each step.
+    uint32_t w[W::kNW], gw[W::kNW];
+    ld_words<W::kNW>(st.src + off, w);
+    if (SHAPE == kFastAccum) {
+      if (c.ge_load) {
+        ld_words<W::kNW>(st.ge + off, gw);
+      } else {
+#pragma unroll
+        for (int k = 0; k < W::kNW; ++k) gw[k] = 0u;  // +0.0 in every format
+      }
+    }
+    {
+      const zt::RoundKeys rk = zt::round_keys(st.key0);
+#pragma unroll
+      for (int k = 0; k < W::kNW; ++k) {
+        float t[W::kPer], gg[W::kPer];
+        W::unpack(w[k], t);
+        if (SHAPE == kFastAccum) W::unpack(gw[k], gg);
+#pragma unroll
+        for (int i = 0; i < W::kPer; ++i) {
+          const float z = zt::gauss_rk(e0 + (uint32_t)(k * W::kPer + i), rk);
+          t[i] = __fmaf_rn(z, a0, t[i]);
+          if (SHAPE == kFastAccum) gg[i] = __fmaf_rn(z, gcoef, gg[i]);
+        }
+        w[k] = W::pack(t);
+        if (SHAPE == kFastAccum) gw[k] = W::pack(gg);
+      }
+    }
+    if (SHAPE != kFastChain1) {
+      const zt::RoundKeys rk = zt::round_keys(st.key1);
+#pragma unroll
+      for (int k = 0; k < W::kNW; ++k) {
+        float t[W::kPer];
+        W::unpack(w[k], t);
+#pragma unroll
+        for (int i = 0; i < W::kPer; ++i) t[i] = __fmaf_rn(zt::gauss_rk(e0 + (uint32_t)(k * W::kPer + i), rk), a1, t[i]);
+        w[k] = W::pack(t);
+      }
+    }
+    if (SHAPE == kFastAccum) st_words_global<W::kNW>(st.ge + off, gw);
+    if (c.dst & ZT_BUF_DATA) st_words_global<W::kNW>(st.data + off, w);
+    if (c.dst & ZT_BUF_LIVE) st_words_global<W::kNW>(st.live + off, w);
+  }
+}
+
+template <int DT, int SHAPE>
+__global__ void __launch_bounds__(ZT_UNIT_ELEMS / 8, SHAPE == kFastAccum ? ZT_FAST_ACCUM_MINB : ZT_FAST_CHAIN_MINB)
+fast_kernel(const __grid_constant__ PassParams P) {
+  fast_walk<DT, SHAPE>(P);
+}
+
+// The specialised shape a pass matches, or -1 for the generic kernels.
+int fast_shape(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* s, int32_t n) {
+  if (!(plan->props & ZT_PLAN_VEC8) || plan->n_units > (int64_t)INT32_MAX - (1 << 24) || cfg->update || cfg->ge_scale_on) return -1;
+  auto plain = [](const zt_stream& x) { return x.n_chain == 1 && x.flags == 0; };
+  if (!cfg->ge_load && !cfg->ge_store) {
+    if (n == 1 && plain(s[0])) return kFastChain1;
+    if (n == 2 && plain(s[0]) && plain(s[1])) return kFastChain2;
+    return -1;
+  }
+  if (cfg->ge_mode == ZT_GE_ACCUM && cfg->ge_store && n == 2 && s[0].n_chain == 1 &&
+      (s[0].flags & ~ZT_STREAM_GE_DEV) == ZT_STREAM_GE && plain(s[1]))
+    return kFastAccum;
+  return -1;
+}
+
 // Grid = SMs x resident blocks per SM (occupancy queried once per kernel).
 template <typename K>
 int grid_for(K kernel, int threads, int64_t n_units, std::atomic<int>& occ_cache) {
@@ -396,6 +582,23 @@ int grid_for(K kernel, int threads, int64_t n_units, std::atomic<int>& occ_cache
 }
 
 std::atomic<int> g_occ_chain{0}, g_occ_full{0};
+std::atomic<int> g_occ_fast[3][kFastShapes];
+
+template <int DT>
+void launch_fast(int shape, const PassParams& P, int64_t units, cudaStream_t s) {
+  constexpr int th = ZT_UNIT_ELEMS / 8;
+  switch (shape) {
+    case kFastChain1:
+      fast_kernel<DT, kFastChain1><<<grid_for(fast_kernel<DT, kFastChain1>, th, units, g_occ_fast[DT][kFastChain1]), th, 0, s>>>(P);
+      break;
+    case kFastChain2:
+      fast_kernel<DT, kFastChain2><<<grid_for(fast_kernel<DT, kFastChain2>, th, units, g_occ_fast[DT][kFastChain2]), th, 0, s>>>(P);
+      break;
+    default:
+      fast_kernel<DT, kFastAccum><<<grid_for(fast_kernel<DT, kFastAccum>, th, units, g_occ_fast[DT][kFastAccum]), th, 0, s>>>(P);
+      break;
+  }
+}
 
 }  // namespace
 
@@ -434,6 +637,8 @@ int plan_build(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_para
   std::vector<int64_t> prefix((size_t)n_tensors + 1, 0);
   int64_t total = 0;
   int32_t buffers = ZT_HAS_LIVE | ZT_HAS_M | ZT_HAS_V | ZT_HAS_ANCHOR | ZT_HAS_GE;
+  int32_t props = ZT_PLAN_VEC8 | ZT_PLAN_ALL_F32 | ZT_PLAN_ALL_BF16 | ZT_PLAN_ALL_F16;
+  auto a16 = [](const void* p) { return ((uintptr_t)p & 15u) == 0; };  // null counts as aligned
   for (int32_t i = 0; i < n_tensors; ++i) {
     const zt_tensor& t = host_tensors[i];
     if (t.numel < 0 || t.numel > (int64_t)ZT_MAX_NUMEL)
@@ -450,6 +655,11 @@ int plan_build(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_para
       if (!t.v) buffers &= ~ZT_HAS_V;
       if (!t.anchor) buffers &= ~ZT_HAS_ANCHOR;
       if (!t.ge) buffers &= ~ZT_HAS_GE;
+      if (t.numel % 8 != 0 || !a16(t.data) || !a16(t.live) || !a16(t.m) || !a16(t.v) || !a16(t.anchor) || !a16(t.ge))
+        props &= ~ZT_PLAN_VEC8;
+      if (t.dtype != ZT_F32) props &= ~ZT_PLAN_ALL_F32;
+      if (t.dtype != ZT_BF16) props &= ~ZT_PLAN_ALL_BF16;
+      if (t.dtype != ZT_F16) props &= ~ZT_PLAN_ALL_F16;
     }
     prefix[i + 1] = prefix[i] + (t.numel + ZT_UNIT_ELEMS - 1) / ZT_UNIT_ELEMS;
     total += t.numel;
@@ -479,6 +689,8 @@ int plan_build(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_para
   plan->n_params = n_params;
   plan->device = dev;
   plan->buffers = buffers;
+  plan->props = props;
+  plan->reserved = 0;
   return ZT_OK;
 }
 
@@ -549,9 +761,17 @@ int pass_launch(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* st
     K.pad[0] = K.pad[1] = 0;
   }
   for (int s = n_streams; s < ZT_MAX_STREAMS; ++s) P.streams[s] = KStream{};
+  const int shape = fast_shape(plan, cfg, streams, n_streams);
+  const int32_t all_dt = plan->props & (ZT_PLAN_ALL_F32 | ZT_PLAN_ALL_BF16 | ZT_PLAN_ALL_F16);
   bool full = cfg->update || cfg->ge_scale_on || cfg->ge_load || cfg->ge_store;
   for (int s = 0; s < n_streams; ++s) full = full || streams[s].flags != 0;
-  if (full) {
+  if (shape >= 0 && all_dt == ZT_PLAN_ALL_BF16) {
+    launch_fast<ZT_BF16>(shape, P, ue - ub, zt::as_stream(stream));
+  } else if (shape >= 0 && all_dt == ZT_PLAN_ALL_F32) {
+    launch_fast<ZT_F32>(shape, P, ue - ub, zt::as_stream(stream));
+  } else if (shape >= 0 && all_dt == ZT_PLAN_ALL_F16) {
+    launch_fast<ZT_F16>(shape, P, ue - ub, zt::as_stream(stream));
+  } else if (full) {
     constexpr int th = ZT_UNIT_ELEMS / kFullEpt;
     full_kernel<<<grid_for(full_kernel, th, ue - ub, g_occ_full), th, 0, zt::as_stream(stream)>>>(P);
   } else {
