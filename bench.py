@@ -182,11 +182,13 @@ def profile_case(kind: str):
         tab.run(cfg, streams)
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10   # back to back, so the host's launch latency stays off the device clock
     a.record()
-    tab.run(cfg, streams)
+    for _ in range(reps):
+        tab.run(cfg, streams)
     b.record()
     torch.cuda.synchronize()
-    ms = a.elapsed_time(b)
+    ms = a.elapsed_time(b) / reps
     print(json.dumps({"profile_case": kind, "elements": n, "ms": ms, "G_elem_per_s": n / ms / 1e6}))
 
 
@@ -312,7 +314,7 @@ def run_reference(args, rank, world):
 # ── EGGROLL population evaluation (Llama-3-8B shape) ─────────────────────────────────────
 
 def eggroll_member_evals(dev, rank: int, world: int, total_pairs: int = 512, pairs_per_chunk: int = 8):
-    """Member-evals/s of the EGGROLL population forward: the
+    """Member-evals/s of the EGGROLL population forward on the
     Llama-3-8B-shaped bf16 model, 1024 members (512 antithetic pairs, seeds 0..511) each
     scored with cross-entropy on a shared 4 x 256-token batch, sigma = 1e-3, rank-4
     perturbations regenerated from Philox seeds, the population sharded over the ranks
@@ -380,7 +382,8 @@ def mezo_full_ft_steps(dev, rank: int, world: int, steps: int = 3, warmup: int =
     the ranks (rank r scores pairs r, r+W, ...), each pair on its own 16 x 512 batch of
     uniform random tokens (batch of pair j at step t from seed 1000*t + j), next-token
     CE + 1e-4 z-loss through the fused CUDA scorer, eps = 1e-3, lr = 1e-5. One step =
-    2 forwards per local pair + the fused perturb/restore/update passes + the all-gather
+    2 forwards per local pair (transformers' Llama with the fused RMSNorm, RoPE and
+    SwiGLU forwards of zotitan_b200.llama_fused) + the fused perturb/restore/update passes + the all-gather
     of the pair losses (and, with W > 1, the sharded update's parameter all-gather).
     Batches are built on the device before the timed region. Timed with CUDA events
     over `steps` steps, max over ranks; weak in pairs per rank only when W divides 8."""
@@ -391,8 +394,10 @@ def mezo_full_ft_steps(dev, rank: int, world: int, steps: int = 3, warmup: int =
     from zotitan_b200.objective import SyntheticTokensObjective
     from zotitan_b200.synthetic import LLAMA_1B, build_llama
     from zotitan_b200.train_zo import ZOConfig, ZOOptimizer
+    from zotitan_b200.llama_fused import fuse_llama
     B, S = 16, 512
     model = build_llama(LLAMA_1B, device=dev, seed=0, max_positions=S)
+    fuse_llama(model)   # fused RMSNorm / in-place RoPE / SwiGLU in the no-grad forwards
     objective = SyntheticTokensObjective(LLAMA_1B.vocab, S, z_loss_weight=1e-4)
     cfg = ZOConfig()
     cfg.eps, cfg.z_batch, cfg.base.lr = EPS, pairs, 1e-5
@@ -450,9 +455,11 @@ def mezo_adam_lora_steps(dev, rank: int, world: int, steps: int = 3, warmup: int
     from zotitan_b200.objective import SyntheticTokensObjective
     from zotitan_b200.synthetic import LLAMA_8B, build_llama
     from zotitan_b200.train_zo import ZOConfig, ZOOptimizer
+    from zotitan_b200.llama_fused import fuse_llama
     B, S, r = 8, 1024, 16
     model = build_llama(LLAMA_8B, device=dev, seed=0, max_positions=S)
     make_lora(model, LoRAConfig(r=r, alpha=32, dtype="fp32"))
+    fuse_llama(model)   # fused RMSNorm / in-place RoPE / SwiGLU in the no-grad forwards
     g = torch.Generator(device=dev).manual_seed(1)
     with torch.no_grad():
         for n, p in model.named_parameters():
@@ -643,14 +650,15 @@ def run_ours(args, rank, local_rank, world):
     perturb_gbs = perturb_bytes / (pmean * 1e-3) / 1e9 if pmean else None
     if amean:   # single-GPU schedule: the restore/accumulate/perturb pass dominates
         achieved, kname, kbytes = accum_bytes / (amean * 1e-3) / 1e9, \
-            "full_kernel: restore + grad_est accumulation + perturb (2 noise streams)", accum_bytes
+            "fast_kernel<bf16, kFastAccum>: restore + grad_est accumulation + perturb (2 noise streams)", accum_bytes
     else:       # sharded schedule: the +eps / -2eps passes on the live copy dominate
-        achieved, kname, kbytes = perturb_gbs, "chain_kernel: -2eps perturb pass (1 noise stream)", perturb_bytes
+        achieved, kname, kbytes = perturb_gbs, "fast_kernel<bf16, kFastChain1>: -2eps perturb pass (1 noise stream)", \
+            perturb_bytes
     traffic = None
     prof = os.path.join(HERE, "profiles", "pass_kernel_traffic.json")
     if os.path.exists(prof):
         try:
-            traffic = json.load(open(prof)).get("full_kernel" if amean else "chain_kernel", {}).get("dram_bytes_per_launch")
+            traffic = json.load(open(prof)).get("accum_pass" if amean else "perturb_pass", {}).get("dram_bytes_per_launch")
         except (ValueError, AttributeError):
             traffic = None
     value = args.steps / (ms * 1e-3)

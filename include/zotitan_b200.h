@@ -400,6 +400,13 @@ typedef struct zt_eggroll_norm_args {
 
 ZT_API int zt_eggroll_rmsnorm(const zt_eggroll_norm_args* args, void* stream);
 
+/* Llama RMSNorm of x [rows, d] with one weight w [d] (bf16, d % 8 == 0, 16-byte aligned):
+ *   y = w * bf16(x * rsqrt(mean(x^2) + eps)),
+ * the mean and rsqrt in fp32 (transformers' LlamaRMSNorm.forward on bf16 tensors; only
+ * the summation order of a row's squares differs). Replaces that module's forward in a
+ * no-grad decoder pass. */
+ZT_API int zt_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t d, float eps, void* stream);
+
 /* In-place rotary position embedding of q [rows, q_heads*head_dim] and k [rows,
  * k_heads*head_dim] (bf16, rows contiguous; row r is at position r % seq):
  *   x = x * cos[pos] + rotate_half(x) * sin[pos],  cos, sin [seq, head_dim] bf16,

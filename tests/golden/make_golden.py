@@ -11,7 +11,7 @@ wrappers cannot build on this CPU). Writes:
   ref_steps.npz   ZOOptimizer.step (zotitan/train_zo.py:510-606) on toy Llama models under
                   every optimizer branch: per-forward values/metrics, the perturbed
                   parameters seen by the first two forwards, parameters after each step
-  ref_config1.npz one step of BASELINE config 1 (Llama 4L/d256, 6.29M fp32 params):
+  ref_config1.npz one MeZO step of the 4-layer Llama (d256, 6.29M fp32 params):
                   loss / proj_grad and a seeded sample of parameter positions
 
     python tests/golden/make_golden.py /path/to/reference [--skip-config1]
@@ -196,7 +196,7 @@ def main(ref_root: str, skip_config1: bool):
 
     if skip_config1:
         return
-    # -- one MeZO step, 6.29M fp32 params -------------------
+    # -- one MeZO step of the 4-layer Llama, 6.29M fp32 params -------------------
     model = build_llama(C1, dtype=torch.float32, seed=0)
     named = [(n, p) for n, p in model.named_parameters() if p.requires_grad]
     cfg = tz.ZOConfig()

@@ -136,7 +136,7 @@ def test_real_forward_losses_match_reference():
 
 
 def test_config1_step_on_gpu():
-    """BASELINE config 1 (Llama 4L/d256/V4096, 6.29M fp32 params, seed 1234, eps 1e-3,
+    """One MeZO step of the 4-layer Llama (d256/V4096, 6.29M fp32 params, seed 1234, eps 1e-3,
     lr 1e-6) stepped on the GPU: loss within 1e-3 of the reference's CPU step and the
     sampled parameters within 1e-6 relative."""
     from toy_models import C1, build_llama, token_batch, torch_xentropy_score

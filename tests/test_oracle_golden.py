@@ -131,7 +131,7 @@ def test_oracle_step_replays_reference(name):
 
 
 def test_config1_step_matches_reference():
-    """BASELINE config 1 (Llama 4L/d256, 6.29M fp32 params, seed 1234): the oracle step
+    """One MeZO step of the 4-layer Llama (d256, 6.29M fp32 params, seed 1234): the oracle step
     with the reference's recorded losses reproduces its proj_grad and sampled parameters."""
     import torch
     from toy_models import C1, build_llama

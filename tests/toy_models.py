@@ -1,6 +1,6 @@
 """Small Llama-shaped models and token batches shared by the golden-vector
 generator and the tests. Weights: ``torch.manual_seed(seed)`` then every
-parameter ``normal_(0, 0.02)`` in ``named_parameters`` order (the BASELINE
+parameter ``normal_(0, 0.02)`` in ``named_parameters`` order (the benchmark
 initialisation for synthetic Llama models)."""
 from __future__ import annotations
 
@@ -10,7 +10,7 @@ TOY = dict(vocab_size=64, hidden_size=16, intermediate_size=32, num_hidden_layer
            num_attention_heads=2, num_key_value_heads=1, max_position_embeddings=64,
            tie_word_embeddings=False)
 
-# Llama 4L/d256/4H/FFN1024/V4096, fp32, untied.
+# The reference's CPU MeZO workload: Llama 4L/d256/4H/FFN1024/V4096, fp32, untied.
 C1 = dict(vocab_size=4096, hidden_size=256, intermediate_size=1024, num_hidden_layers=4,
           num_attention_heads=4, num_key_value_heads=4, max_position_embeddings=256,
           tie_word_embeddings=False)

@@ -468,6 +468,22 @@ int zt_eggroll_rmsnorm(const zt_eggroll_norm_args* args, void* stream) {
   return zt::check_cuda(cudaGetLastError(), "zt_eggroll_rmsnorm launch");
 }
 
+int zt_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t d, float eps, void* stream) {
+  zt::clear_error();
+  if (rows < 0 || d <= 0) return zt::set_error(ZT_ERR_INVALID, "zt_rmsnorm: bad shape");
+  if (rows == 0) return ZT_OK;
+  if (d % 8 || d > (int64_t)ZT_MAX_NUMEL) return zt::set_error(ZT_ERR_INVALID, "zt_rmsnorm: d must be a multiple of 8");
+  if (rows > (int64_t)INT32_MAX) return zt::set_error(ZT_ERR_LIMIT, "zt_rmsnorm: more than 2^31-1 rows");
+  if (!x || !w || !y) return zt::set_error(ZT_ERR_INVALID, "zt_rmsnorm: null pointer");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y)) return zt::set_error(ZT_ERR_INVALID, "zt_rmsnorm: pointers must be 16-byte aligned");
+  // One weight row for all rows: rows_per_member = rows maps every row to member 0.
+  const unsigned grid = (unsigned)((rows + kNormRows - 1) / kNormRows);
+  rmsnorm_kernel<<<grid, 256, 0, zt::as_stream(stream)>>>(static_cast<const uint4*>(x), static_cast<const uint4*>(w),
+                                                          static_cast<uint4*>(y), rows, (int32_t)(d / 8), (int32_t)rows,
+                                                          1.0f / (float)d, eps);
+  return zt::check_cuda(cudaGetLastError(), "zt_rmsnorm launch");
+}
+
 int zt_eggroll_rope(void* q, void* k, const void* cos, const void* sin, int64_t rows, int32_t seq, int32_t q_heads,
                     int32_t k_heads, int32_t head_dim, void* stream) {
   zt::clear_error();

@@ -467,6 +467,25 @@ def eggroll_rmsnorm(x: torch.Tensor, w: torch.Tensor, keys: list[int], sigma: fl
     return y.view(x.shape)
 
 
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """Llama RMSNorm of bf16 rows x [..., d] with weight w [d] (zt_rmsnorm):
+    w * bf16(x * rsqrt(mean(x^2) + eps)), statistics in fp32."""
+    _check_cuda(x, "x")
+    _check_cuda(w, "w")
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise ValueError("x and w must be bf16")
+    if not x.is_contiguous() or not w.is_contiguous():
+        raise ValueError("x and w must be contiguous")
+    d = w.shape[0]
+    if x.shape[-1] != d:
+        raise ValueError("x's last dimension must equal w's length")
+    y = torch.empty_like(x)
+    with torch.cuda.device(x.device):
+        L.check(L.load().zt_rmsnorm(x.data_ptr(), w.data_ptr(), y.data_ptr(), x.numel() // d, d, float(eps),
+                                    _stream_ptr(x.device)), "zt_rmsnorm")
+    return y
+
+
 def eggroll_rope_(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, seq: int, head_dim: int):
     """In-place rotary embedding of q [rows, Hq*hd] and k [rows, Hk*hd] (bf16, row r at
     position r % seq) with cos, sin [seq, hd] bf16 (zt_eggroll_rope)."""

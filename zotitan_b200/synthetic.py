@@ -26,7 +26,7 @@ class LlamaShape:
         return self.d_model // self.heads
 
 
-# BASELINE workloads: Llama-3.2-1B shape (tied embeddings) and Llama-3-8B shape (untied)
+# Benchmark workloads: Llama-3.2-1B shape (tied embeddings) and Llama-3-8B shape (untied)
 LLAMA_1B = LlamaShape(vocab=128256, d_model=2048, layers=16, heads=32, kv_heads=8, ffn=8192, tied=True)
 LLAMA_8B = LlamaShape(vocab=128256, d_model=4096, layers=32, heads=32, kv_heads=8, ffn=14336, tied=False)
 
