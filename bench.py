@@ -45,7 +45,7 @@ def parse():
     ap.add_argument("--no-eggroll", action="store_true", help="skip the EGGROLL population measurement")
     ap.add_argument("--no-mezo", action="store_true", help="skip the MeZO full fine-tune step measurement")
     ap.add_argument("--no-lora", action="store_true", help="skip the MeZO-Adam LoRA step measurement")
-    ap.add_argument("--profile-case", choices=["chain", "full", "eggroll", "eggroll-gated", "eggroll-forward"],
+    ap.add_argument("--profile-case", choices=["chain", "full", "replay", "eggroll", "eggroll-gated", "eggroll-forward"],
                     default=None,
                     help="small case for ncu: one bf16 tensor of 2^28 elements, 3 launches of the "
                          "-2eps pass (chain) or of the restore+accumulate+perturb pass (full); or 3 "
@@ -171,6 +171,10 @@ def profile_case(kind: str):
     if kind == "chain":
         tab = K.ParamTable([p])
         cfg, streams = K.PassCfg(), [K.Stream(5, (f(-2e-3),))]
+    elif kind == "replay":   # the sharded step's last pass: 16 pairs' chains + grad_est + SGD
+        tab = K.ParamTable([p])
+        cfg = K.PassCfg(ge_mode=L.ZT_GE_ACCUM, update=True, lr=f(1e-5))
+        streams = [K.Stream(100 + j, (f(1e-3), f(-2e-3), f(1e-3)), ge=f(0.01 * (j - 8))) for j in range(16)]
     else:
         ge = torch.zeros_like(p)
         vals = torch.tensor([2.01, 2.0], device="cuda")
@@ -189,7 +193,8 @@ def profile_case(kind: str):
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / reps
-    print(json.dumps({"profile_case": kind, "elements": n, "ms": ms, "G_elem_per_s": n / ms / 1e6}))
+    print(json.dumps({"profile_case": kind, "elements": n, "streams": len(streams), "ms": ms,
+                      "G_elem_per_s": n / ms / 1e6, "G_stream_elem_per_s": n * len(streams) / ms / 1e6}))
 
 
 def env_rank():

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define ZT_ABI_VERSION 5
+#define ZT_ABI_VERSION 6
 
 /* dtypes of parameter tensors */
 #define ZT_F32 0
@@ -374,6 +374,15 @@ typedef struct zt_eggroll_factor_args {
                              rows untouched (the caller zeroes the buffer once); NULL to skip */
   int32_t b_ext_row;      /* 0, 4 or 8 */
   int32_t reserved3;
+  /* Keys from device memory instead (keys_a / keys_b then unused): with seeds non-NULL,
+   * pair j's keys are zt_param_key(seeds[j], n_params, key_index_a / key_index_b),
+   * computed by the kernel. Lets a captured CUDA graph be replayed for new pairs after
+   * a copy of their seeds into `seeds`. */
+  const uint64_t* seeds;  /* device [pairs] pair seeds, or NULL */
+  uint32_t n_params;
+  uint32_t key_index_a;   /* index + 2*n_params of the tensor (P) */
+  uint32_t key_index_b;   /* index + n_params (Psi) */
+  int32_t reserved4;
 } zt_eggroll_factor_args;
 
 ZT_API int zt_eggroll_factors(const zt_eggroll_factor_args* args, void* stream);
@@ -396,6 +405,10 @@ typedef struct zt_eggroll_norm_args {
   int32_t rows_per_member;
   float sigma;
   float eps;
+  const uint64_t* seeds;  /* device [pairs] pair seeds, or NULL: with seeds, keys[j] =
+                             zt_param_key(seeds[j], n_params, key_index) on the device */
+  uint32_t n_params;
+  uint32_t key_index;
 } zt_eggroll_norm_args;
 
 ZT_API int zt_eggroll_rmsnorm(const zt_eggroll_norm_args* args, void* stream);
@@ -418,6 +431,15 @@ ZT_API int zt_eggroll_rope(void* q, void* k, const void* cos, const void* sin, i
 /* out = bf16(bf16(silu(gate)) * up) over n bf16 elements (n % 8 == 0): the Llama MLP's
  * act_fn(gate_proj(x)) * up_proj(x). */
 ZT_API int zt_eggroll_swiglu(const void* gate, const void* up, void* out, int64_t n, void* stream);
+
+/* y [m, n] = bf16(bf16(silu(bf16(x w_gate^T))) * bf16(x w_up^T)) for bf16 x [m, k],
+ * w_gate, w_up [n, k] (row-major, 16-byte aligned; m % 256 == 0, n % 128 == 0,
+ * k % 64 == 0): the gate and up projections and the SwiGLU of an unperturbed Llama MLP
+ * (act_fn(gate_proj(x)) * up_proj(x)) as one tcgen05 GEMM over CTA pairs, the SwiGLU in
+ * its epilogue; the rounding points are those of the three torch ops, the fp32
+ * accumulation order is the kernel's. */
+ZT_API int zt_gemm_swiglu(const void* x, const void* w_gate, const void* w_up, void* y, int64_t m, int64_t n,
+                          int64_t k, void* stream);
 
 /* Operands of the EGGROLL evolution-strategies update of one 2-D tensor [n, k] over
  * `pairs` antithetic pairs, from zt_eggroll_factors' a, b, scale (members 2j):

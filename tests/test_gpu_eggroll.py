@@ -238,3 +238,33 @@ def test_tensor_core_xb_matches_cuda_core_xb(M, K, T, nseg):
         sig = f[2].repeat_interleave(T)[:, None].abs()
         assert float((v_tc - v_cc).abs().max()) <= 1e-5 * scale * float(sig.max()) + 2 ** -14 * float(v_cc.abs().max())
         assert not b_[:, 8:].any()
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 128, 64), (512, 384, 256), (2048, 1408, 1024), (8192, 8192, 2048)])
+def test_gemm_swiglu_matches_torch(M, N, K):
+    """zt_gemm_swiglu (the plain pair GEMM, no rank-4 term, SwiGLU in the epilogue) against
+    torch's gate / up GEMMs and F.silu(g) * u on bf16: the same rounding points, so the
+    outputs differ only where the two GEMMs' fp32 accumulation orders put g or u on
+    different sides of a bf16 rounding boundary (>= 99% identical, within 2^-6 relative
+    plus 1e-3 absolute)."""
+    from zotitan_b200 import kernels as K_
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    wg = (torch.randn(N, K, device="cuda", generator=g) * K ** -0.5).bfloat16()
+    wu = (torch.randn(N, K, device="cuda", generator=g) * K ** -0.5).bfloat16()
+    y = K_.gemm_swiglu(x, wg, wu)
+    want = torch.nn.functional.silu(x @ wg.T) * (x @ wu.T)
+    torch.cuda.synchronize()
+    assert K_.eggroll_take_error() == 0
+    d = (y.float() - want.float()).abs()
+    assert bool((d <= 2 ** -6 * want.float().abs() + 1e-3).all()), float(d.max())
+    assert float((d == 0).float().mean()) >= 0.99
+
+
+def test_gemm_swiglu_rejects_bad_shapes():
+    from zotitan_b200 import kernels as K_
+    from zotitan_b200._lib import ZtError
+    x = torch.zeros(200, 64, device="cuda", dtype=torch.bfloat16)
+    w = torch.zeros(128, 64, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(ZtError):
+        K_.gemm_swiglu(x, w, w)   # 200 rows: not whole 256-row tiles

@@ -119,3 +119,46 @@ def test_es_step_single_rank():
     assert any(not torch.equal(b, p) for b, (_, p) in zip(before, pop.named))
     from zotitan_b200 import kernels as K
     assert K.eggroll_take_error() == 0
+
+
+def test_cuda_graph_replay_matches_eager():
+    """cuda_graphs: the first chunk of a shape is captured, later chunks replay it with new
+    pair seeds (device memory) and new tokens. Every replayed result is bit-identical to
+    the eager forward of the same chunk (same kernels, same order)."""
+    from toy_models import build_llama
+    from zotitan_b200.eggroll import EggrollConfig, EggrollPopulation
+    g = torch.Generator().manual_seed(9)
+    toks = [torch.randint(0, SHAPE["vocab_size"], (4, 64), generator=g).cuda() for _ in range(3)]
+    seeds = [[3, 11], [5, 2**63 + 7], [2**64 - 1, 0]]
+    model = build_llama(SHAPE, dtype=torch.bfloat16, seed=0, device="cuda")
+    graphed = EggrollPopulation(model, EggrollConfig(sigma=SIGMA, cuda_graphs=True))
+    got = [graphed.evaluate(t, s).clone() for t, s in zip(toks, seeds)]
+    assert len(graphed._graphs) == 1
+    model2 = build_llama(SHAPE, dtype=torch.bfloat16, seed=0, device="cuda")
+    eager = EggrollPopulation(model2, EggrollConfig(sigma=SIGMA, cuda_graphs=False))
+    want = [eager.evaluate(t, s) for t, s in zip(toks, seeds)]
+    for a, b in zip(got, want):
+        assert torch.equal(a, b), (a, b)
+    assert not torch.equal(got[0], got[1])
+
+
+def test_device_seed_keys_match_host_keys():
+    """zt_eggroll_factors / zt_eggroll_rmsnorm with keys derived on the device from pair
+    seeds equal the calls given the host-computed keys."""
+    from zotitan_b200 import kernels as K
+    from zotitan_b200.eggroll import _key
+    n_params, idx = 291, 17
+    seeds_list = [1, 2**40 + 3, 2**64 - 5]
+    seeds = torch.tensor([s - 2**64 if s >= 2**63 else s for s in seeds_list], dtype=torch.int64, device="cuda")
+    ka = [_key(s, n_params, idx + 2 * n_params) for s in seeds_list]
+    kb = [_key(s, n_params, idx + n_params) for s in seeds_list]
+    host = K.eggroll_factors(ka, kb, 384, 256, 1e-3, "cuda", ext_slot=0)
+    dev = K.eggroll_factors(None, None, 384, 256, 1e-3, "cuda", ext_slot=0,
+                            dev_seeds=(seeds, n_params, idx + 2 * n_params, idx + n_params))
+    for h, d in zip(host, dev):
+        assert torch.equal(h, d)
+    x = torch.randn(6 * 128, 256, device="cuda").bfloat16()
+    w = (1 + 0.1 * torch.randn(256, device="cuda")).bfloat16()
+    yh = K.eggroll_rmsnorm(x, w, [_key(s, n_params, idx) for s in seeds_list], 1e-2, 1e-5, 128)
+    yd = K.eggroll_rmsnorm(x, w, None, 1e-2, 1e-5, 128, dev_seeds=(seeds, n_params, idx))
+    assert torch.equal(yh, yd)

@@ -101,7 +101,7 @@ def test_grad_enabled_falls_back():
 def test_model_loss_close(monkeypatch):
     from zotitan_b200 import kernels as K
     from zotitan_b200.llama_fused import fuse_llama
-    calls = {"rmsnorm": 0, "eggroll_rope_": 0, "eggroll_swiglu": 0}
+    calls = {"rmsnorm": 0, "eggroll_rope_": 0, "eggroll_swiglu": 0, "gemm_swiglu": 0}
     for name in calls:
         fn = getattr(K, name)
 
@@ -119,7 +119,38 @@ def test_model_loss_close(monkeypatch):
     want, lw = loss_and_logits()
     fuse_llama(m)
     got, lg = loss_and_logits()
-    assert calls == {"rmsnorm": 2 * 4 + 1, "eggroll_rope_": 4, "eggroll_swiglu": 4}   # every fused path ran
+    # 4 x 255 rows: not whole 256-row tiles, so the MLP takes the two projections and zt_eggroll_swiglu
+    assert calls == {"rmsnorm": 2 * 4 + 1, "eggroll_rope_": 4, "eggroll_swiglu": 4, "gemm_swiglu": 0}
     assert abs(float(got) - float(want)) <= 1e-3 * abs(float(want))
     scale = float(lw.float().abs().max())
     assert float((lg.float() - lw.float()).abs().max()) <= 2.0 ** -5 * scale
+
+
+def test_mlp_gated_gemm_path(monkeypatch):
+    """Rows in whole 256-row tiles and plain bf16 linears: gate, up and SwiGLU run as one
+    zt_gemm_swiglu; the output is within a bf16 step of |output| plus 2^-6 of the
+    partial-product bound of the module's own forward (the GEMM accumulates in another
+    order, which can move g or u by one bf16 step)."""
+    from zotitan_b200 import kernels as K
+    from zotitan_b200.llama_fused import fuse_llama
+    calls = {"n": 0}
+    fn = K.gemm_swiglu
+
+    def counted(*a, **kw):
+        calls["n"] += 1
+        return fn(*a, **kw)
+    monkeypatch.setattr(K, "gemm_swiglu", counted)
+    m = _model()
+    mlp = m.model.layers[0].mlp
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(4, 128, 256, device="cuda", generator=g).bfloat16()
+    with torch.inference_mode():
+        want = mlp(x)
+        h = mlp.act_fn(mlp.gate_proj(x)) * mlp.up_proj(x)
+        bound = h.float().abs() @ mlp.down_proj.weight.float().abs().T
+        fuse_llama(m)
+        got = mlp(x)
+    assert calls["n"] == 1
+    d = (got.float() - want.float()).abs()
+    ulp = torch.ldexp(torch.ones_like(d), torch.frexp(want.float().abs().clamp_min(2.0 ** -126))[1] - 8)
+    assert bool((d <= ulp + 2.0 ** -6 * bound).all())

@@ -128,10 +128,11 @@ UNIFORM_SIZES = [8, 2048, 4096, 24, 100000, 2056, 16]
 @pytest.mark.parametrize("dt", [ph.BF16, ph.F32, ph.F16])
 def test_uniform_plan_specialised_shapes(K, dt):
     """A plan whose tensors share one dtype and are whole, 16-byte aligned 8-element groups
-    (ZT_PLAN_VEC8) runs the one-stream (+eps, -2eps, live copies), two-stream and
-    restore + accumulate + perturb passes through kernels specialised for that dtype:
-    every buffer they write is bit-identical to the oracle. The last pass (update) still
-    takes the generic kernel on the same plan."""
+    (ZT_PLAN_VEC8) runs the one-stream (+eps, -2eps, live copies), two-stream,
+    restore + accumulate + perturb and replay (chains + grad_est + SGD, with and without
+    weight decay) passes through kernels specialised for that dtype: every buffer they
+    write is bit-identical to the oracle. The last pass of the on-the-fly schedule (it
+    loads grad_est) takes the generic kernel on the same plan."""
     l = L()
     f = lambda x: float(np.float32(x))  # noqa: E731
     e, m2 = f(1e-3), f(-2e-3)
@@ -157,6 +158,14 @@ def test_uniform_plan_specialised_shapes(K, dt):
                                                                         K.Stream(73, (e,))], None, {"with_ge": True}),
         (K.PassCfg(ge_mode=l.ZT_GE_ACCUM, ge_load=True, update=True, lr=f(1e-2)), [K.Stream(74, (e,), ge=f(0.7))],
          None, {"with_ge": True}),
+        # replay shape: every stream's chain and grad_est term in registers, then SGD
+        (K.PassCfg(ge_mode=l.ZT_GE_ACCUM, update=True, lr=f(1e-2)),
+         [K.Stream(80 + j, (e, m2, e), ge=f(0.1 * (j - 3))) for j in range(7)], None, {}),
+        (K.PassCfg(ge_mode=l.ZT_GE_ACCUM, update=True, lr=f(3e-2), wd=l.ZT_WD_STANDARD, wd_factor=f(1 - 3e-4)),
+         [K.Stream(90, (), ge=f(0.4)), K.Stream(91, (e,), ge=f(-0.2)), K.Stream(92, (e, m2), ge=f(0.3)),
+          K.Stream(93, (e, m2, e), ge=f(1.5))], None, {}),
+        (K.PassCfg(dst=data | live, ge_mode=l.ZT_GE_ACCUM, update=True, lr=f(1e-2)),
+         [K.Stream(94, (e, m2, e), ge=f(0.25)), K.Stream(95, (e, m2, e), ge=f(-0.5))], None, {"with_live": True}),
     ]
     for cfg, streams, dv, kw in cases:
         run_both(K, cfg, streams, dev_values=dv, props=props, specs=specs, **kw)

@@ -32,7 +32,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version_and_key(lib):
-    assert lib.zt_abi_version() == L.ABI_VERSION == 5
+    assert lib.zt_abi_version() == L.ABI_VERSION == 6
     from oracle import philox as ph
     for seed, n, i in [(0, 1, 0), (1234, 39, 7), (2**40 + 3, 146, 145), (2**64 - 1, 448, 3)]:
         assert lib.zt_param_key(seed, n, i) == ph.param_key(seed, n, i) == (seed * n + i) & 0x7FFFFFFF
@@ -46,8 +46,9 @@ def test_struct_layouts_match_header(lib):
     assert ctypes.sizeof(L.ZtEggrollArgs) == 112 and L.ZtEggrollArgs.xb_ready.offset == 88
     assert ctypes.sizeof(L.ZtEggrollXbArgs) == 152 and L.ZtEggrollXbArgs.bt.offset == 144
     assert ctypes.sizeof(L.ZtEggrollGatedArgs) == 136 and L.ZtEggrollGatedArgs.x_ext.offset == 112
-    assert ctypes.sizeof(L.ZtEggrollFactorArgs) == 120 and L.ZtEggrollFactorArgs.b_ext.offset == 104
-    assert ctypes.sizeof(L.ZtEggrollNormArgs) == 72 and L.ZtEggrollNormArgs.m.offset == 40
+    assert ctypes.sizeof(L.ZtEggrollFactorArgs) == 144 and L.ZtEggrollFactorArgs.b_ext.offset == 104
+    assert L.ZtEggrollFactorArgs.seeds.offset == 120 and L.ZtEggrollFactorArgs.key_index_b.offset == 136
+    assert ctypes.sizeof(L.ZtEggrollNormArgs) == 88 and L.ZtEggrollNormArgs.seeds.offset == 72
     assert lib.zt_plan_workspace_bytes(0) == 8
     assert lib.zt_plan_workspace_bytes(3) == 256 + 8 * 4
     assert lib.zt_plan_workspace_bytes(5) == 512 + 8 * 6

@@ -29,11 +29,11 @@ EXPORTS = ("zt_last_error", "zt_abi_version", "zt_param_key", "zt_philox_words",
            "zt_randn_at", "zt_plan_workspace_bytes", "zt_plan_init", "zt_pass", "zt_pass_static",
            "zt_eggroll_linear", "zt_eggroll_take_error", "zt_randn_keys", "zt_eggroll_factors",
            "zt_eggroll_rmsnorm", "zt_eggroll_rope", "zt_eggroll_swiglu", "zt_xent_rows",
-           "zt_eggroll_xb", "zt_eggroll_gated", "zt_eggroll_update_operands", "zt_lora_add", "zt_rmsnorm")
+           "zt_eggroll_xb", "zt_eggroll_gated", "zt_eggroll_update_operands", "zt_lora_add", "zt_rmsnorm", "zt_gemm_swiglu")
 ZT_STATIC_MAX_TENSORS = 1024
 ZT_EGGROLL_MAX_PAIRS = 512
 ZT_EGGROLL_FACTOR_WORK_FLOATS = 64 * 20
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 
 class ZtTensor(ctypes.Structure):
@@ -98,14 +98,17 @@ class ZtEggrollFactorArgs(ctypes.Structure):
                 ("normalize", ctypes.c_int32), ("sigma", ctypes.c_float), ("reserved", ctypes.c_int32),
                 ("a", ctypes.c_void_p), ("b", ctypes.c_void_p), ("scale", ctypes.c_void_p), ("work", ctypes.c_void_p),
                 ("a_ext", ctypes.c_void_p), ("ext_slot", ctypes.c_int32), ("reserved2", ctypes.c_int32),
-                ("b_ext", ctypes.c_void_p), ("b_ext_row", ctypes.c_int32), ("reserved3", ctypes.c_int32)]
+                ("b_ext", ctypes.c_void_p), ("b_ext_row", ctypes.c_int32), ("reserved3", ctypes.c_int32),
+                ("seeds", ctypes.c_void_p), ("n_params", ctypes.c_uint32), ("key_index_a", ctypes.c_uint32),
+                ("key_index_b", ctypes.c_uint32), ("reserved4", ctypes.c_int32)]
 
 
 class ZtEggrollNormArgs(ctypes.Structure):
     _fields_ = [("x", ctypes.c_void_p), ("w", ctypes.c_void_p), ("keys", ctypes.c_void_p),
                 ("w_members", ctypes.c_void_p), ("y", ctypes.c_void_p), ("m", ctypes.c_int64), ("d", ctypes.c_int64),
                 ("pairs", ctypes.c_int32), ("rows_per_member", ctypes.c_int32), ("sigma", ctypes.c_float),
-                ("eps", ctypes.c_float)]
+                ("eps", ctypes.c_float), ("seeds", ctypes.c_void_p), ("n_params", ctypes.c_uint32),
+                ("key_index", ctypes.c_uint32)]
 
 
 class ZtError(RuntimeError):
@@ -165,6 +168,8 @@ def load():
     lib.zt_lora_add.argtypes = [P, P, P, ctypes.c_float, I64, I64, I32, P]
     lib.zt_rmsnorm.restype = ctypes.c_int
     lib.zt_rmsnorm.argtypes = [P, P, P, I64, I64, ctypes.c_float, P]
+    lib.zt_gemm_swiglu.restype = ctypes.c_int
+    lib.zt_gemm_swiglu.argtypes = [P, P, P, P, I64, I64, I64, P]
     lib.zt_xent_rows.restype = ctypes.c_int
     lib.zt_xent_rows.argtypes = [P, I64, I64, I64, P, P, P, P, P]
     lib.zt_plan_workspace_bytes.restype = ctypes.c_size_t

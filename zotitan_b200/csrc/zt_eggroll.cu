@@ -426,7 +426,9 @@ __device__ __forceinline__ bool mbar_wait_pair(uint64_t* bar, uint32_t parity, v
 // EXT: the rank-4 term runs on the tensor cores as one more K = 16 slab per tile,
 // X_ext [hi, lo of sigma_i X B_i] against W_ext [A_i, A_i] (gated: gate columns 0-7, up
 // columns 8-15), so the epilogue only converts (and, gated, applies the SwiGLU).
-template <bool GATED, bool EXT>
+// EXT without SLAB: no rank-4 term at all, the plain GEMM (gated: gate, up and SwiGLU of
+// an unperturbed Llama MLP in one kernel).
+template <bool GATED, bool EXT, bool SLAB = EXT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
     eggroll_gemm_pair_kernel(const __grid_constant__ EggParams P) {
   extern __shared__ uint8_t smem_raw[];
@@ -490,7 +492,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
             tma_load_2d_pair(sa + kStageA2, &P.tmap_w, leader_full, kb * kBK, nb * kBN + (int)rank * 128);
           last_phase[s] = (int)(round & 1);
         }
-        if (ok && EXT) {  // the rank-4 K-slab of this tile
+        if (ok && SLAB) {  // the rank-4 K-slab of this tile
           const int s = it % kStages2;
           const uint32_t round = it / kStages2;
           if (!mbar_wait_pair(&empty[s], (round & 1) ^ 1, abort, peer_abort, 1)) {
@@ -542,7 +544,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
           issued = true;
           umma_commit_pair(&empty[s]);  // stage s is free in both CTAs once these MMAs have read it
         }
-        if (ok && EXT) {  // + (sigma_i X B_i) A_i^T as one K = 16 MMA
+        if (ok && SLAB) {  // + (sigma_i X B_i) A_i^T as one K = 16 MMA
           const int s = it % kStages2;
           if (!mbar_wait_pair(&full[s], (it / kStages2) & 1, abort, peer_abort, 3)) {
             ok = false;
@@ -1025,7 +1027,8 @@ int prepare_kernels() {
                                                    (int)kXtSmem), "eggroll: shared memory attribute (xb)"))
     return rc;
   for (auto fn : {eggroll_gemm_pair_kernel<false, false>, eggroll_gemm_pair_kernel<true, false>,
-                  eggroll_gemm_pair_kernel<false, true>, eggroll_gemm_pair_kernel<true, true>})
+                  eggroll_gemm_pair_kernel<false, true>, eggroll_gemm_pair_kernel<true, true>,
+                  eggroll_gemm_pair_kernel<false, true, false>, eggroll_gemm_pair_kernel<true, true, false>})
     if (int rc = zt::check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes2),
                                 "eggroll: shared memory attribute (pair)"))
       return rc;
@@ -1043,15 +1046,18 @@ int prepare_kernels() {
   return ZT_OK;
 }
 
+// mode 0: rank-4 term in the fp32 epilogue, 1: as a K-slab, 2: no rank-4 term.
 template <bool GATED>
-int launch_pair(const EggParams& P, bool ext, cudaStream_t s) {
+int launch_pair(const EggParams& P, int mode, cudaStream_t s) {
   int dev = 0;
   if (int rc = zt::check_cuda(cudaGetDevice(&dev), "eggroll: cudaGetDevice")) return rc;
   const int max_clusters = g_max_pairs[dev];
   const int tiles = (P.m_blocks / 2) * P.n_blocks;
   const int clusters = tiles < max_clusters ? tiles : max_clusters;
-  if (ext)
+  if (mode == 1)
     eggroll_gemm_pair_kernel<GATED, true><<<2 * clusters, kThreadsEgg, kSmemBytes2, s>>>(P);
+  else if (mode == 2)
+    eggroll_gemm_pair_kernel<GATED, true, false><<<2 * clusters, kThreadsEgg, kSmemBytes2, s>>>(P);
   else
     eggroll_gemm_pair_kernel<GATED, false><<<2 * clusters, kThreadsEgg, kSmemBytes2, s>>>(P);
   return zt::check_cuda(cudaGetLastError(), GATED ? "eggroll: gated gemm launch" : "eggroll: gemm launch (pair)");
@@ -1145,7 +1151,7 @@ int zt_eggroll_linear(const zt_eggroll_args* args, void* stream) {
     if (int rc = launch_xb(A.x, bb, xx, 1, A.m, A.k, A.rows_per_member, s)) return rc;
   }
   if (int rc = prepare_kernels()) return rc;
-  if (pair) return launch_pair<false>(P, ext, s);
+  if (pair) return launch_pair<false>(P, ext ? 1 : 0, s);
   const int tiles = P.m_blocks * P.n_blocks;
   const int grid = tiles < zt::sm_count() ? tiles : zt::sm_count();
   eggroll_gemm_kernel<<<grid, kThreadsEgg, kSmemBytes, s>>>(P);
@@ -1199,7 +1205,41 @@ int zt_eggroll_gated(const zt_eggroll_gated_args* args, void* stream) {
   P.n = (int32_t)A.n;
   P.rows_per_member = A.rows_per_member;
   if (int rc = prepare_kernels()) return rc;
-  return launch_pair<true>(P, ext, zt::as_stream(stream));
+  return launch_pair<true>(P, ext ? 1 : 0, zt::as_stream(stream));
+}
+
+int zt_gemm_swiglu(const void* x, const void* w_gate, const void* w_up, void* y, int64_t m, int64_t n, int64_t k,
+                   void* stream) {
+  zt::clear_error();
+  if (!x || !w_gate || !w_up || !y) return zt::set_error(ZT_ERR_INVALID, "zt_gemm_swiglu: null pointer");
+  if (m <= 0 || n <= 0 || k <= 0) return zt::set_error(ZT_ERR_INVALID, "zt_gemm_swiglu: empty shape");
+  if (m % 256 || n % 128 || k % kBK)
+    return zt::set_error(ZT_ERR_INVALID, "zt_gemm_swiglu: need m % 256 == 0, n % 128 == 0, k % 64 == 0");
+  if (m > (int64_t)INT32_MAX || n > (int64_t)INT32_MAX || k > (int64_t)INT32_MAX)
+    return zt::set_error(ZT_ERR_LIMIT, "zt_gemm_swiglu: dimension above 2^31-1");
+  for (const void* p : {x, w_gate, w_up, (const void*)y})
+    if (((uintptr_t)p & 15) != 0) return zt::set_error(ZT_ERR_INVALID, "zt_gemm_swiglu: pointers must be 16-byte aligned");
+  EncodeFn enc = nullptr;
+  if (int rc = get_encode(&enc)) return rc;
+  EggParams P;
+  if (int rc = make_map(enc, &P.tmap_x, x, (uint64_t)m, (uint64_t)k, kBM)) return rc;
+  if (int rc = make_map(enc, &P.tmap_w, w_gate, (uint64_t)n, (uint64_t)k, kHalfRows)) return rc;
+  if (int rc = make_map(enc, &P.tmap_w2, w_up, (uint64_t)n, (uint64_t)k, kHalfRows)) return rc;
+  if (int rc = make_out_map(enc, &P.tmap_y, y, (uint64_t)m, (uint64_t)n)) return rc;
+  P.a = nullptr;
+  P.sigma = nullptr;
+  P.xb = nullptr;
+  P.a2 = nullptr;
+  P.sigma2 = nullptr;
+  P.xb2 = nullptr;
+  P.y = static_cast<__nv_bfloat16*>(y);
+  P.m_blocks = (int32_t)(m / kBM);
+  P.n_blocks = (int32_t)(n / 128);
+  P.k_blocks = (int32_t)(k / kBK);
+  P.n = (int32_t)n;
+  P.rows_per_member = (int32_t)m;  // one "member": no rank-4 term is read
+  if (int rc = prepare_kernels()) return rc;
+  return launch_pair<true>(P, 2, zt::as_stream(stream));
 }
 
 int zt_eggroll_xb(const zt_eggroll_xb_args* args, void* stream) {

@@ -12,10 +12,36 @@ constexpr int kFacThreads = 256;
 constexpr int kFacBlocks = ZT_EGGROLL_FACTOR_BLOCKS;
 constexpr int kGram = 10;  // upper triangle of a symmetric 4 x 4 Gram matrix
 
+// Per-pair Philox keys: by value (ka, kb), or, when seeds is set, derived on the device
+// as zt_param_key(seeds[j], n_params, ia / ib) from pair seeds in device memory.
 struct PairKeys {
   uint32_t ka[kMaxPairs];
   uint32_t kb[kMaxPairs];
+  const uint64_t* seeds;
+  uint32_t n_params, ia, ib;
 };
+
+__device__ __forceinline__ uint32_t pair_key_a(const PairKeys& K, int j) {
+  return K.seeds ? zt::param_key(K.seeds[j], K.n_params, K.ia) : K.ka[j];
+}
+__device__ __forceinline__ uint32_t pair_key_b(const PairKeys& K, int j) {
+  return K.seeds ? zt::param_key(K.seeds[j], K.n_params, K.ib) : K.kb[j];
+}
+
+// Host side: the keys of `pairs` pairs from host arrays, or the device seed form.
+PairKeys make_pair_keys(const uint32_t* keys_a, const uint32_t* keys_b, int pairs, const uint64_t* seeds,
+                        uint32_t n_params, uint32_t ia, uint32_t ib) {
+  PairKeys K;
+  for (int j = 0; j < kMaxPairs; ++j) {
+    K.ka[j] = (!seeds && keys_a && j < pairs) ? keys_a[j] : 0u;
+    K.kb[j] = (!seeds && keys_b && j < pairs) ? keys_b[j] : 0u;
+  }
+  K.seeds = seeds;
+  K.n_params = n_params;
+  K.ia = ia;
+  K.ib = ib;
+  return K;
+}
 
 __device__ __forceinline__ void gram_add(float g[kGram], const float v[4]) {
   g[0] = fmaf(v[0], v[0], g[0]); g[1] = fmaf(v[0], v[1], g[1]); g[2] = fmaf(v[0], v[2], g[2]);
@@ -42,7 +68,7 @@ __global__ void __launch_bounds__(kFacThreads) factor_kernel(const __grid_consta
                                                               int32_t ext_slot, __nv_bfloat16* __restrict__ b_ext,
                                                               int32_t b_ext_row) {
   const int j = blockIdx.y;
-  const uint32_t ka = K.ka[j], kb = K.kb[j];
+  const uint32_t ka = pair_key_a(K, j), kb = pair_key_b(K, j);
   const int items = n + k;
   float gp[kGram], gq[kGram];
 #pragma unroll
@@ -159,7 +185,7 @@ __global__ void __launch_bounds__(32) factor_scale_kernel(const float* __restric
 __global__ void __launch_bounds__(256) norm_weights_kernel(const __grid_constant__ PairKeys K, const __nv_bfloat16* __restrict__ w,
                                                            int32_t d, float sigma, __nv_bfloat16* __restrict__ wm) {
   const int j = blockIdx.y;
-  const uint32_t key = K.ka[j];
+  const uint32_t key = pair_key_a(K, j);
   for (int t = blockIdx.x * 256 + threadIdx.x; t < d; t += gridDim.x * 256) {
     const float z = zt::gauss((uint32_t)t, key);
     const float wf = __bfloat162float(w[t]);
@@ -400,16 +426,12 @@ int zt_eggroll_factors(const zt_eggroll_factor_args* args, void* stream) {
   if (A.pairs > kMaxPairs) return zt::set_error(ZT_ERR_LIMIT, "zt_eggroll_factors: more than ZT_EGGROLL_MAX_PAIRS pairs");
   if (A.n * 4 > (int64_t)ZT_MAX_NUMEL || A.k * 4 > (int64_t)ZT_MAX_NUMEL)
     return zt::set_error(ZT_ERR_LIMIT, "zt_eggroll_factors: factor fields beyond 2^31 elements");
-  if (!A.keys_a || !A.keys_b || !A.a || !A.b || !A.scale || !A.work)
+  if ((!A.seeds && (!A.keys_a || !A.keys_b)) || !A.a || !A.b || !A.scale || !A.work)
     return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_factors: null pointer");
   if (!aligned16(A.a) || !aligned16(A.b)) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_factors: a, b not 16-byte aligned");
   if (A.dtype != ZT_F32 && A.dtype != ZT_BF16 && A.dtype != ZT_F16)
     return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_factors: unknown dtype");
-  PairKeys K;
-  for (int j = 0; j < kMaxPairs; ++j) {
-    K.ka[j] = j < A.pairs ? A.keys_a[j] : 0u;
-    K.kb[j] = j < A.pairs ? A.keys_b[j] : 0u;
-  }
+  const PairKeys K = make_pair_keys(A.keys_a, A.keys_b, A.pairs, A.seeds, A.n_params, A.key_index_a, A.key_index_b);
   const int64_t items = A.n + A.k;
   int64_t nblk = (items + 4 * kFacThreads - 1) / (4 * kFacThreads);
   if (nblk > kFacBlocks) nblk = kFacBlocks;
@@ -450,12 +472,11 @@ int zt_eggroll_rmsnorm(const zt_eggroll_norm_args* args, void* stream) {
   if (A.d % 8 || A.d > (int64_t)ZT_MAX_NUMEL) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_rmsnorm: d must be a multiple of 8");
   if (A.rows_per_member <= 0 || A.m != (int64_t)A.rows_per_member * 2 * A.pairs)
     return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_rmsnorm: m must equal rows_per_member * 2 * pairs");
-  if (!A.keys || !A.x || !A.w || !A.w_members || !A.y) return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_rmsnorm: null pointer");
+  if ((!A.keys && !A.seeds) || !A.x || !A.w || !A.w_members || !A.y)
+    return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_rmsnorm: null pointer");
   if (!aligned16(A.x) || !aligned16(A.w_members) || !aligned16(A.y))
     return zt::set_error(ZT_ERR_INVALID, "zt_eggroll_rmsnorm: x, w_members, y not 16-byte aligned");
-  PairKeys K;
-  for (int j = 0; j < kMaxPairs; ++j) K.ka[j] = j < A.pairs ? A.keys[j] : 0u;
-  for (int j = 0; j < kMaxPairs; ++j) K.kb[j] = 0u;
+  const PairKeys K = make_pair_keys(A.keys, nullptr, A.pairs, A.seeds, A.n_params, A.key_index, 0u);
   cudaStream_t s = zt::as_stream(stream);
   const dim3 wgrid((unsigned)((A.d + 255) / 256), (unsigned)A.pairs);
   norm_weights_kernel<<<wgrid, 256, 0, s>>>(K, static_cast<const __nv_bfloat16*>(A.w), (int32_t)A.d, A.sigma,

@@ -393,7 +393,10 @@ enum FastShape : int {
   kFastChain1 = 0,  // one stream, one coefficient, no roles (the +eps and -2eps passes)
   kFastChain2 = 1,  // two such streams (restore one pair, perturb the next)
   kFastAccum = 2,   // stream 0: +a z and its grad_est term (ACCUM, stored); stream 1: +a z
-  kFastShapes = 3,
+  kFastReplay = 3,  // any number of streams, each its chain and grad_est term (ACCUM, host
+                    // coefficient, in registers), then the SGD update (+ standard decay):
+                    // the last pass of a step, and the sharded replay of every pair
+  kFastShapes = 4,
 };
 
 #ifndef ZT_FAST_CHAIN_MINB
@@ -401,6 +404,9 @@ enum FastShape : int {
 #endif
 #ifndef ZT_FAST_ACCUM_MINB
 #define ZT_FAST_ACCUM_MINB 4
+#endif
+#ifndef ZT_FAST_REPLAY_MINB
+#define ZT_FAST_REPLAY_MINB 4
 #endif
 
 // 8 elements as 32-bit storage words: two per word for 16-bit formats, one for fp32.
@@ -445,6 +451,7 @@ struct FastTensor {
   uint32_t numel;
   int32_t lo, hi;
   uint32_t key0, key1;
+  uint32_t index;
 };
 
 __device__ __forceinline__ void st_global16(char* p, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
@@ -494,6 +501,7 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
         st.ge = static_cast<char*>(t.ge);
         st.key0 = zt::param_key(S0.seed, P.n_params, (uint32_t)t.index);
         st.key1 = SHAPE != kFastChain1 ? zt::param_key(S1.seed, P.n_params, (uint32_t)t.index) : 0u;
+        st.index = (uint32_t)t.index;
       }
       __syncthreads();
       lo = st.lo;
@@ -502,6 +510,53 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
     const uint32_t e0 = (uint32_t)(u - lo) * ZT_UNIT_ELEMS + threadIdx.x * 8u;
     if (e0 >= st.numel) continue;
     const size_t off = (size_t)e0 * W::kBytes;
+    if constexpr (SHAPE == kFastReplay) {
+      using R = zt::Dt<DT>;
+      uint32_t w[W::kNW];
+      ld_words<W::kNW>(st.src + off, w);
+      float th[8], ge[8];
+#pragma unroll
+      for (int k = 0; k < W::kNW; ++k) {
+        float t[W::kPer];
+        W::unpack(w[k], t);
+#pragma unroll
+        for (int i = 0; i < W::kPer; ++i) th[k * W::kPer + i] = t[i];
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ge[e] = 0.0f;
+      for (int s = 0; s < P.n_streams; ++s) {
+        const KStream& S = P.streams[s];
+        const zt::RoundKeys rk = zt::round_keys(zt::param_key(S.seed, P.n_params, st.index));
+        const float c0 = S.chain[0], c1 = S.chain[1], c2 = S.chain[2], gc = S.ge_coef;
+        const int nc = S.n_chain;  // uniform: the branches below are taken by every thread
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float z = zt::gauss_rk(e0 + (uint32_t)e, rk);
+          float x = th[e];
+          if (nc > 0) x = R::round(__fmaf_rn(z, c0, x));
+          if (nc > 1) x = R::round(__fmaf_rn(z, c1, x));
+          if (nc > 2) x = R::round(__fmaf_rn(z, c2, x));
+          th[e] = x;
+          ge[e] = R::round(__fmaf_rn(z, gc, ge[e]));  // (train_zo.py:556)
+        }
+      }
+      const float nlr = -c.lr;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        th[e] = R::round(__fmaf_rn(ge[e], nlr, th[e]));  // (:399)
+        if (c.wd == ZT_WD_STANDARD) th[e] = R::round(__fmul_rn(th[e], c.wd_factor));  // (:401-402)
+      }
+#pragma unroll
+      for (int k = 0; k < W::kNW; ++k) {
+        float t[W::kPer];
+#pragma unroll
+        for (int i = 0; i < W::kPer; ++i) t[i] = th[k * W::kPer + i];
+        w[k] = W::pack(t);
+      }
+      if (c.dst & ZT_BUF_DATA) st_words_global<W::kNW>(st.data + off, w);
+      if (c.dst & ZT_BUF_LIVE) st_words_global<W::kNW>(st.live + off, w);
+      continue;
+    }
     // Values stay packed in their storage format between noise streams: packing with
     // round-to-nearest is the rounding to the parameter dtype after each step.
     uint32_t w[W::kNW], gw[W::kNW];
@@ -549,14 +604,24 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
 }
 
 template <int DT, int SHAPE>
-__global__ void __launch_bounds__(ZT_UNIT_ELEMS / 8, SHAPE == kFastAccum ? ZT_FAST_ACCUM_MINB : ZT_FAST_CHAIN_MINB)
+__global__ void __launch_bounds__(ZT_UNIT_ELEMS / 8, SHAPE == kFastAccum    ? ZT_FAST_ACCUM_MINB
+                                                      : SHAPE == kFastReplay ? ZT_FAST_REPLAY_MINB
+                                                                             : ZT_FAST_CHAIN_MINB)
 fast_kernel(const __grid_constant__ PassParams P) {
   fast_walk<DT, SHAPE>(P);
 }
 
 // The specialised shape a pass matches, or -1 for the generic kernels.
 int fast_shape(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* s, int32_t n) {
-  if (!(plan->props & ZT_PLAN_VEC8) || plan->n_units > (int64_t)INT32_MAX - (1 << 24) || cfg->update || cfg->ge_scale_on) return -1;
+  if (!(plan->props & ZT_PLAN_VEC8) || plan->n_units > (int64_t)INT32_MAX - (1 << 24) || cfg->ge_scale_on) return -1;
+  if (cfg->update) {
+    if (cfg->momentum != ZT_MOM_NONE || cfg->second_moment || (cfg->wd != ZT_WD_NONE && cfg->wd != ZT_WD_STANDARD) ||
+        cfg->ge_mode != ZT_GE_ACCUM || cfg->ge_load || cfg->ge_store || n < 1)
+      return -1;
+    for (int32_t i = 0; i < n; ++i)
+      if (s[i].flags != ZT_STREAM_GE) return -1;  // a host coefficient, no momentum role
+    return kFastReplay;
+  }
   auto plain = [](const zt_stream& x) { return x.n_chain == 1 && x.flags == 0; };
   if (!cfg->ge_load && !cfg->ge_store) {
     if (n == 1 && plain(s[0])) return kFastChain1;
@@ -594,8 +659,11 @@ void launch_fast(int shape, const PassParams& P, int64_t units, cudaStream_t s) 
     case kFastChain2:
       fast_kernel<DT, kFastChain2><<<grid_for(fast_kernel<DT, kFastChain2>, th, units, g_occ_fast[DT][kFastChain2]), th, 0, s>>>(P);
       break;
-    default:
+    case kFastAccum:
       fast_kernel<DT, kFastAccum><<<grid_for(fast_kernel<DT, kFastAccum>, th, units, g_occ_fast[DT][kFastAccum]), th, 0, s>>>(P);
+      break;
+    default:
+      fast_kernel<DT, kFastReplay><<<grid_for(fast_kernel<DT, kFastReplay>, th, units, g_occ_fast[DT][kFastReplay]), th, 0, s>>>(P);
       break;
   }
 }

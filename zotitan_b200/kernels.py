@@ -409,15 +409,35 @@ def _keys_array(keys):
     return arr
 
 
-def eggroll_factors(keys_a: list[int], keys_b: list[int], n: int, k: int, sigma: float, device,
+def _dev_seeds(dev_seeds, device):
+    """(seeds, n_params, *indices) with seeds an int64 CUDA tensor of uint64 pair seeds."""
+    seeds = dev_seeds[0]
+    _check_cuda(seeds, "seeds")
+    device = torch.device(device)
+    if device.index is None:
+        device = torch.device(device.type, torch.cuda.current_device())
+    if seeds.dtype != torch.int64 or not seeds.is_contiguous() or seeds.device != device:
+        raise ValueError("seeds must be a contiguous int64 tensor on the call's device")
+    return seeds, int(dev_seeds[1]), [int(i) & 0xFFFFFFFF for i in dev_seeds[2:]]
+
+
+def eggroll_factors(keys_a: list[int] | None, keys_b: list[int] | None, n: int, k: int, sigma: float, device,
                     dtype: torch.dtype = torch.bfloat16, normalize: bool = True, ext_slot: int | None = None,
-                    b_ext: torch.Tensor | None = None, b_ext_row: int = 0):
+                    b_ext: torch.Tensor | None = None, b_ext_row: int = 0, dev_seeds=None):
     """Rank-4 factors of an [n, k] tensor for antithetic pairs (zt_eggroll_factors):
     returns A [2p, n, 4], B [2p, k, 4] (fp32 holding dtype-rounded values) and the signed
     scale [2p] (+sigma c_j, -sigma c_j), ready for eggroll_linear. With ext_slot (0 or 1)
     also A_ext [2p, n, 16] bf16, the GEMM's K-slab operand, as a fourth element. With
     b_ext ([2p, 16, k] bf16, zeroed by the caller) B^T is also written to its rows
-    b_ext_row .. b_ext_row + 3 (the tensor-core X B operand of eggroll_xb_ext)."""
+    b_ext_row .. b_ext_row + 3 (the tensor-core X B operand of eggroll_xb_ext).
+    dev_seeds = (seeds, n_params, index_a, index_b) derives the keys on the device from
+    the pair seeds in `seeds` (int64 CUDA tensor, one per pair): zt_param_key(seed,
+    n_params, index_a / index_b); keys_a and keys_b are then not used. A captured CUDA
+    graph of the call stays valid for new pairs once their seeds are copied into `seeds`."""
+    seeds = None
+    if dev_seeds is not None:
+        seeds, n_params, (ia, ib) = _dev_seeds(dev_seeds, device)
+        keys_a = keys_b = [0] * seeds.numel()
     if b_ext is not None:
         _check_cuda(b_ext, "b_ext")
         if b_ext.dtype != torch.bfloat16 or not b_ext.is_contiguous() or b_ext.shape != (2 * len(keys_a), 16, k):
@@ -439,15 +459,22 @@ def eggroll_factors(keys_a: list[int], keys_b: list[int], n: int, k: int, sigma:
                                  work.data_ptr(), a_ext.data_ptr() if a_ext is not None else None,
                                  int(ext_slot or 0), 0, b_ext.data_ptr() if b_ext is not None else None,
                                  int(b_ext_row), 0)
+    if seeds is not None:
+        args.seeds, args.n_params, args.key_index_a, args.key_index_b = seeds.data_ptr(), n_params, ia, ib
     with torch.cuda.device(device):
         L.check(L.load().zt_eggroll_factors(ctypes.byref(args), _stream_ptr(device)), "zt_eggroll_factors")
     return (a, b, scale) if a_ext is None else (a, b, scale, a_ext)
 
 
-def eggroll_rmsnorm(x: torch.Tensor, w: torch.Tensor, keys: list[int], sigma: float, eps: float,
-                    rows_per_member: int) -> torch.Tensor:
+def eggroll_rmsnorm(x: torch.Tensor, w: torch.Tensor, keys: list[int] | None, sigma: float, eps: float,
+                    rows_per_member: int, dev_seeds=None) -> torch.Tensor:
     """Llama RMSNorm of population rows x [M, d] with member-perturbed weights
-    (zt_eggroll_rmsnorm): members 2j / 2j+1 use bf16(w +- sigma randn(keys[j]))."""
+    (zt_eggroll_rmsnorm): members 2j / 2j+1 use bf16(w +- sigma randn(keys[j])).
+    dev_seeds = (seeds, n_params, index): keys derived on the device, as eggroll_factors."""
+    seeds = None
+    if dev_seeds is not None:
+        seeds, n_params, (ki,) = _dev_seeds(dev_seeds, x.device)
+        keys = [0] * seeds.numel()
     _check_cuda(x, "x")
     _check_cuda(w, "w")
     if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
@@ -462,6 +489,8 @@ def eggroll_rmsnorm(x: torch.Tensor, w: torch.Tensor, keys: list[int], sigma: fl
     ka = _keys_array(keys)
     args = L.ZtEggrollNormArgs(x2.data_ptr(), w.data_ptr(), ctypes.addressof(ka), wm.data_ptr(), y.data_ptr(),
                                x2.shape[0], d, pairs, rows_per_member, float(sigma), float(eps))
+    if seeds is not None:
+        args.seeds, args.n_params, args.key_index = seeds.data_ptr(), n_params, ki
     with torch.cuda.device(x.device):
         L.check(L.load().zt_eggroll_rmsnorm(ctypes.byref(args), _stream_ptr(x.device)), "zt_eggroll_rmsnorm")
     return y.view(x.shape)
@@ -516,6 +545,25 @@ def eggroll_swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
         L.check(L.load().zt_eggroll_swiglu(gate.data_ptr(), up.data_ptr(), out.data_ptr(), gate.numel(),
                                            _stream_ptr(gate.device)), "zt_eggroll_swiglu")
     return out
+
+
+def gemm_swiglu(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
+    """bf16(bf16(silu(bf16(x w_gate^T))) * bf16(x w_up^T)) as one tcgen05 GEMM
+    (zt_gemm_swiglu): x [m, k], w_gate / w_up [n, k] bf16, m % 256 == 0, n % 128 == 0,
+    k % 64 == 0."""
+    for t, name in ((x, "x"), (w_gate, "w_gate"), (w_up, "w_up")):
+        _check_cuda(t, name)
+        if t.dtype != torch.bfloat16 or not t.is_contiguous() or t.dim() != 2:
+            raise ValueError(f"{name} must be a contiguous bf16 matrix")
+    m, k = x.shape
+    n = w_gate.shape[0]
+    if w_gate.shape != (n, k) or w_up.shape != (n, k):
+        raise ValueError("w_gate and w_up must be [n, k] with x's k")
+    y = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    with torch.cuda.device(x.device):
+        L.check(L.load().zt_gemm_swiglu(x.data_ptr(), w_gate.data_ptr(), w_up.data_ptr(), y.data_ptr(), m, n, k,
+                                        _stream_ptr(x.device)), "zt_gemm_swiglu")
+    return y
 
 
 def xent_rows(logits: torch.Tensor, targets: torch.Tensor, want_lse: bool = True, want_correct: bool = True):

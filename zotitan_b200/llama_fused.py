@@ -14,8 +14,10 @@ LlamaMLP instance of a model for one that calls this package's kernels:
   working), the rotary embedding applied in place on the projection outputs by
   `zt_eggroll_rope` (bit-exact with apply_rotary_pos_emb), the configured attention
   implementation called as LlamaAttention.forward calls it, then o_proj.
-- MLP: gate and up projections, `zt_eggroll_swiglu` (bf16(bf16(silu(g)) * u), torch's
-  rounding points), down projection.
+- MLP: for plain bias-free bf16 linears and rows in 256-row tiles, gate, up and the
+  SwiGLU as one tcgen05 GEMM (`zt_gemm_swiglu`, the SwiGLU in its epilogue); otherwise
+  (LoRA wrappers, ragged rows) the projections as modules and `zt_eggroll_swiglu`
+  (bf16(bf16(silu(g)) * u), torch's rounding points). Then the down projection.
 
 Each fused forward defers to the module's own forward when gradients are enabled,
 the activations are not bf16 on a CUDA device, the layout does not fit (head_dim not a
@@ -76,9 +78,24 @@ def is_silu(act) -> bool:
     return isinstance(act, nn.SiLU) or type(act).__name__ == "SiLUActivation"
 
 
+def _plain_linear(m, k: int) -> bool:
+    w = getattr(m, "weight", None)
+    return (type(m) is nn.Linear and m.bias is None and w is not None and w.dtype == torch.bfloat16
+            and w.is_contiguous() and w.shape[1] == k)
+
+
 def _mlp_forward(self, x):
     if not _fast(x) or not is_silu(self.act_fn):
         return self._zt_orig_forward(x)
+    k = x.shape[-1]
+    rows = x.numel() // k
+    if (_plain_linear(self.gate_proj, k) and _plain_linear(self.up_proj, k) and rows % 256 == 0 and k % 64 == 0
+            and self.gate_proj.weight.shape[0] % 128 == 0 and self.gate_proj.weight.shape == self.up_proj.weight.shape):
+        # gate, up and SwiGLU in one tcgen05 GEMM (zt_gemm_swiglu)
+        x2 = x.reshape(rows, k)
+        x2 = x2 if x2.is_contiguous() else x2.contiguous()
+        h = K.gemm_swiglu(x2, self.gate_proj.weight.detach(), self.up_proj.weight.detach())
+        return self.down_proj(h.view(*x.shape[:-1], -1))
     g = self.gate_proj(x)
     u = self.up_proj(x)
     if g.dtype != torch.bfloat16 or u.dtype != torch.bfloat16 or g.numel() % 8:
