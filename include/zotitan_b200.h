@@ -455,10 +455,25 @@ ZT_API int zt_eggroll_update_operands(const float* a, const float* b, const floa
 /* The tail of a LoRA linear (zotitan/lora.py:77-86) in one pass over the output:
  *   out[t, c] = bf16(out[t, c] + bf16(scale * sum_r xa[t, r] b[c, r]))
  * with out [rows, n] bf16 holding the base layer's output (updated in place), xa [rows, r]
- * fp32 = lora_A(x) and b [n, r] fp32 = lora_B.weight; the sum runs over r in order in
- * fp32. r in {4, 8, 16, 32, 64}; xa and b row-major and contiguous. */
+ * fp32 = lora_A(x) and b [n, r] fp32 = lora_B.weight. r in {4, 8, 16, 32, 64}; xa and b
+ * row-major and contiguous. For r in {8, 16, 32}, n % 8 == 0 and a 16-byte aligned out the
+ * sum runs on the tensor cores (mma.sync on TF32 with each fp32 operand split into a hi
+ * and a lo part, three products: ~2^-22 relative before the bf16 rounding); otherwise in
+ * fp32 FMAs over r in order. */
 ZT_API int zt_lora_add(void* out, const float* xa, const float* b, float scale, int64_t rows, int64_t n, int32_t r,
                        void* stream);
+
+/* zt_lora_add with xa given as three partial products xa3 [rows, 3r] fp32 (the columns of
+ * x [A0; A1; A2]^T for the split of zt_lora_split), summed in fp32 as ((p0 + p1) + p2)
+ * while the kernel stages them: the fp32 x A^T of the reference's lora_A(x.float()). */
+ZT_API int zt_lora_add3(void* out, const float* xa3, const float* b, float scale, int64_t rows, int64_t n, int32_t r,
+                        void* stream);
+
+/* Three bf16 parts of an fp32 array that sum to it exactly: out [3, n] bf16 with
+ * out[0] = bf16(a), out[1] = bf16(a - out[0]), out[2] = bf16(a - out[0] - out[1]) (fp32
+ * differences), so a tensor-core product against [out[0]; out[1]; out[2]] gives the fp32
+ * product's terms exactly (the LoRA A operand). */
+ZT_API int zt_lora_split(const float* a, void* out, int64_t n, void* stream);
 
 /* ---- the scorer: next-token cross-entropy statistics ------------------------------ */
 

@@ -33,3 +33,34 @@ def test_lora_tail_matches_reference(r, n_in, n_out, rows):
     with torch.enable_grad():   # gradients on: the reference's torch path, identical values
         x2 = x.clone().requires_grad_(False)
         assert torch.equal(m(x2), want)
+
+
+def test_lora_split_parts_sum_exactly():
+    """zt_lora_split: the three bf16 parts equal torch's cast-and-subtract chain and sum to
+    the fp32 input exactly (checked in fp64)."""
+    from zotitan_b200 import kernels as K
+    g = torch.Generator(device="cuda").manual_seed(3)
+    a = torch.randn(16, 4096, device="cuda", generator=g) * torch.logspace(-6, 2, 4096, device="cuda")
+    parts = K.lora_split(a)
+    a0 = a.bfloat16()
+    rest = a - a0.float()
+    a1 = rest.bfloat16()
+    a2 = (rest - a1.float()).bfloat16()
+    assert torch.equal(parts[0], a0) and torch.equal(parts[1], a1) and torch.equal(parts[2], a2)
+    assert torch.equal(parts.double().sum(0), a.double())
+
+
+@pytest.mark.parametrize("r", [4, 16, 64])
+def test_lora_add3_equals_summed_lora_add(r):
+    """zt_lora_add3 on three partial products = zt_lora_add on their fp32 sum ((p0+p1)+p2)."""
+    from zotitan_b200 import kernels as K
+    g = torch.Generator(device="cuda").manual_seed(r)
+    rows, n = 300, 1000
+    xa3 = torch.randn(rows, 3 * r, device="cuda", generator=g)
+    b = torch.randn(n, r, device="cuda", generator=g) * 0.1
+    base = torch.randn(rows, n, device="cuda", generator=g).bfloat16()
+    want = base.clone()
+    K.lora_add_(want, ((xa3[:, :r] + xa3[:, r:2 * r]) + xa3[:, 2 * r:]).contiguous(), b, 2.0)
+    got = base.clone()
+    K.lora_add3_(got, xa3, b, 2.0)
+    assert torch.equal(got, want)

@@ -29,7 +29,7 @@ EXPORTS = ("zt_last_error", "zt_abi_version", "zt_param_key", "zt_philox_words",
            "zt_randn_at", "zt_plan_workspace_bytes", "zt_plan_init", "zt_pass", "zt_pass_static",
            "zt_eggroll_linear", "zt_eggroll_take_error", "zt_randn_keys", "zt_eggroll_factors",
            "zt_eggroll_rmsnorm", "zt_eggroll_rope", "zt_eggroll_swiglu", "zt_xent_rows",
-           "zt_eggroll_xb", "zt_eggroll_gated", "zt_eggroll_update_operands", "zt_lora_add", "zt_rmsnorm", "zt_gemm_swiglu")
+           "zt_eggroll_xb", "zt_eggroll_gated", "zt_eggroll_update_operands", "zt_lora_add", "zt_rmsnorm", "zt_gemm_swiglu", "zt_lora_add3", "zt_lora_split")
 ZT_STATIC_MAX_TENSORS = 1024
 ZT_EGGROLL_MAX_PAIRS = 512
 ZT_EGGROLL_FACTOR_WORK_FLOATS = 64 * 20
@@ -166,6 +166,10 @@ def load():
     lib.zt_eggroll_update_operands.argtypes = [P, P, P, P, I32, I64, I64, ctypes.c_float, P, P, P]
     lib.zt_lora_add.restype = ctypes.c_int
     lib.zt_lora_add.argtypes = [P, P, P, ctypes.c_float, I64, I64, I32, P]
+    lib.zt_lora_add3.restype = ctypes.c_int
+    lib.zt_lora_add3.argtypes = [P, P, P, ctypes.c_float, I64, I64, I32, P]
+    lib.zt_lora_split.restype = ctypes.c_int
+    lib.zt_lora_split.argtypes = [P, P, I64, P]
     lib.zt_rmsnorm.restype = ctypes.c_int
     lib.zt_rmsnorm.argtypes = [P, P, P, I64, I64, ctypes.c_float, P]
     lib.zt_gemm_swiglu.restype = ctypes.c_int

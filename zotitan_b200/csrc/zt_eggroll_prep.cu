@@ -2,6 +2,8 @@
 // factors, the per-member RMSNorm, rotary position embedding and SwiGLU of a Llama
 // population forward. Each is one or two bandwidth-bound launches over rows that the
 // population GEMM reads or writes; together they replace ~20 torch launches per layer.
+#include <string>
+
 #include "zt_common.cuh"
 #include "zt_philox.cuh"
 
@@ -347,14 +349,24 @@ __global__ void __launch_bounds__(256) update_operands_kernel(const float4* __re
 // accesses for C = 2) before the arithmetic.
 constexpr int kLoraBand = 128, kLoraStep = 16;
 
-template <int R, int C>
+// PARTS = 3: xa holds three partial products per row, [rows, 3R], summed in fp32 in order
+// ((p0 + p1) + p2) while the band is staged.
+template <int R, int C, int PARTS = 1>
 __global__ void __launch_bounds__(256) lora_add_kernel(__nv_bfloat16* __restrict__ out, const float* __restrict__ xa,
                                                        const float* __restrict__ bw, float scale, int64_t rows,
                                                        int32_t n) {
   __shared__ __align__(16) float sxa[kLoraBand][R];
   const int64_t band0 = (int64_t)blockIdx.y * kLoraBand;
   const int nb = (int)((rows - band0) < kLoraBand ? (rows - band0) : kLoraBand);
-  for (int i = threadIdx.x; i < kLoraBand * R; i += 256) sxa[i / R][i % R] = i / R < nb ? xa[band0 * R + i] : 0.f;
+  for (int i = threadIdx.x; i < kLoraBand * R; i += 256) {
+    const int row = i / R, col = i % R;
+    float v = 0.f;
+    if (row < nb) {
+      const float* p = xa + (band0 + row) * (PARTS * R) + col;
+      v = PARTS == 1 ? p[0] : __fadd_rn(__fadd_rn(p[0], p[R]), p[2 * R]);
+    }
+    sxa[row][col] = v;
+  }
   __syncthreads();
   const int c0 = (blockIdx.x * 256 + threadIdx.x) * C;
   if (c0 >= n) return;  // n % C == 0: a thread's columns are all in range or all out
@@ -412,6 +424,177 @@ int stream_grid(int64_t items, int per_sm) {
 }
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+// The same tail with the rank-R product on the tensor cores: mma.sync m16n8k8 on TF32
+// operands, each fp32 input split as hi = tf32(v), lo = tf32(v - hi) and the product
+// taken as lo*hi + hi*lo + hi*hi (the dropped lo*lo term and the TF32 rounding of lo
+// leave ~2^-22 relative, far inside the bf16 rounding that follows). A block owns 64
+// rows x 128 columns: the band of xa (the three partial products summed in order when
+// PARTS = 3) and the block's 128 rows of b are staged in shared memory; warp w computes
+// rows 16*(w/2) .. +16 and columns 64*(w%2) .. +64 and writes bf16(scale * delta) to a
+// shared tile (rows padded to 136 bf16: conflict-free fragment writes); then every
+// thread updates 8 consecutive outputs of a row with one 16-byte read and write of out.
+constexpr int kMmaRows = 64, kMmaCols = 128, kMmaLdd = kMmaCols + 8;
+
+__device__ __forceinline__ uint32_t tf32_of(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return r;
+}
+
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+template <int R, int PARTS>
+__global__ void __launch_bounds__(256) lora_add_mma_kernel(__nv_bfloat16* __restrict__ out, const float* __restrict__ xa,
+                                                           const float* __restrict__ bw, float scale, int64_t rows,
+                                                           int32_t n) {
+  static_assert(R % 8 == 0, "k steps of 8");
+  constexpr int KS = R / 8;
+  constexpr int LD = R + 4;  // padded rows: conflict-free fragment reads
+  __shared__ float sa[kMmaRows][LD];
+  __shared__ float sb[kMmaCols][LD];
+  __shared__ __align__(16) __nv_bfloat16 sd[kMmaRows][kMmaLdd];
+  const int64_t row0 = (int64_t)blockIdx.y * kMmaRows;
+  const int col0 = blockIdx.x * kMmaCols;
+  const int nr = (int)((rows - row0) < kMmaRows ? (rows - row0) : kMmaRows);
+  const int nc = (n - col0) < kMmaCols ? (n - col0) : kMmaCols;
+  for (int i = threadIdx.x; i < kMmaRows * R; i += 256) {
+    const int rr = i / R, k = i % R;
+    float v = 0.f;
+    if (rr < nr) {
+      const float* p = xa + (row0 + rr) * (PARTS * R) + k;
+      v = PARTS == 1 ? p[0] : __fadd_rn(__fadd_rn(p[0], p[R]), p[2 * R]);
+    }
+    sa[rr][k] = v;
+  }
+  for (int i = threadIdx.x; i < kMmaCols * R; i += 256) {
+    const int cc = i / R, k = i % R;
+    sb[cc][k] = cc < nc ? __ldg(bw + (size_t)(col0 + cc) * R + k) : 0.f;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int g = lane / 4, t = lane % 4;
+  const int wr = (warp / 2) * 16, wc = (warp % 2) * 64;
+  uint32_t ahi[KS][4], alo[KS][4];
+#pragma unroll
+  for (int ks = 0; ks < KS; ++ks) {
+    const int kb = ks * 8;
+    const float v[4] = {sa[wr + g][kb + t], sa[wr + g + 8][kb + t], sa[wr + g][kb + t + 4], sa[wr + g + 8][kb + t + 4]};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      ahi[ks][e] = tf32_of(v[e]);
+      alo[ks][e] = tf32_of(__fsub_rn(v[e], __uint_as_float(ahi[ks][e])));
+    }
+  }
+#pragma unroll
+  for (int ni = 0; ni < 8; ++ni) {
+    const int cb = wc + ni * 8;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      const float bv[2] = {sb[cb + g][ks * 8 + t], sb[cb + g][ks * 8 + t + 4]};
+      uint32_t bhi[2], blo[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        bhi[e] = tf32_of(bv[e]);
+        blo[e] = tf32_of(__fsub_rn(bv[e], __uint_as_float(bhi[e])));
+      }
+      mma_tf32(acc, alo[ks], bhi);
+      mma_tf32(acc, ahi[ks], blo);
+      mma_tf32(acc, ahi[ks], bhi);
+    }
+    // acc: rows wr + g and wr + g + 8, columns cb + 2t, cb + 2t + 1
+    *reinterpret_cast<__nv_bfloat162*>(&sd[wr + g][cb + 2 * t]) = __floats2bfloat162_rn(acc[0] * scale, acc[1] * scale);
+    *reinterpret_cast<__nv_bfloat162*>(&sd[wr + g + 8][cb + 2 * t]) =
+        __floats2bfloat162_rn(acc[2] * scale, acc[3] * scale);
+  }
+  __syncthreads();
+  // 16 threads per row, 8 columns each (n % 8 == 0: a group is wholly in or out of range)
+  const int cq = (threadIdx.x % 16) * 8;
+  for (int rr = threadIdx.x / 16; rr < nr; rr += 16) {
+    if (cq >= nc) continue;
+    uint4* p = reinterpret_cast<uint4*>(out + (row0 + rr) * n + col0 + cq);
+    const uint4 o = *p;
+    const uint4 dv = *reinterpret_cast<const uint4*>(&sd[rr][cq]);
+    const uint32_t ow[4] = {o.x, o.y, o.z, o.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
+    uint32_t yw[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 of = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ow[e]));
+      const float2 df = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dw[e]));
+      const __nv_bfloat162 y = __floats2bfloat162_rn(of.x + df.x, of.y + df.y);
+      yw[e] = *reinterpret_cast<const uint32_t*>(&y);
+    }
+    *p = make_uint4(yw[0], yw[1], yw[2], yw[3]);
+  }
+}
+
+template <int PARTS>
+int lora_add_launch(const char* name, void* out, const float* xa, const float* b, float scale, int64_t rows, int64_t n,
+                    int32_t r, void* stream) {
+  const std::string nm(name);
+  if (rows < 0 || n <= 0) return zt::set_error(ZT_ERR_INVALID, nm + ": bad shape");
+  if (rows == 0) return ZT_OK;
+  if (!out || !xa || !b) return zt::set_error(ZT_ERR_INVALID, nm + ": null pointer");
+  if (n > (int64_t)INT32_MAX) return zt::set_error(ZT_ERR_LIMIT, nm + ": shape too large");
+  if (!aligned16(b)) return zt::set_error(ZT_ERR_INVALID, nm + ": b not 16-byte aligned");
+  if (r != 4 && r != 8 && r != 16 && r != 32 && r != 64)
+    return zt::set_error(ZT_ERR_INVALID, nm + ": rank must be 4, 8, 16, 32 or 64");
+  cudaStream_t s = zt::as_stream(stream);
+  __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
+  const int32_t ni = (int32_t)n;
+  if (r % 8 == 0 && r <= 32 && n % 8 == 0 && ((uintptr_t)out & 15) == 0) {  // tensor-core form
+    const dim3 g2((unsigned)((n + kMmaCols - 1) / kMmaCols), (unsigned)((rows + kMmaRows - 1) / kMmaRows));
+    if (g2.y > 65535u) return zt::set_error(ZT_ERR_LIMIT, nm + ": too many rows");
+    switch (r) {
+      case 8: lora_add_mma_kernel<8, PARTS><<<g2, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      case 16: lora_add_mma_kernel<16, PARTS><<<g2, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      default: lora_add_mma_kernel<32, PARTS><<<g2, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+    }
+    return zt::check_cuda(cudaGetLastError(), (nm + " launch").c_str());
+  }
+  const int cols = (r <= 32 && n % 2 == 0 && ((uintptr_t)out & 3) == 0) ? 2 : 1;   // columns per thread
+  const dim3 grid((unsigned)((n + 256 * cols - 1) / (256 * cols)), (unsigned)((rows + kLoraBand - 1) / kLoraBand));
+  if (grid.y > 65535u) return zt::set_error(ZT_ERR_LIMIT, nm + ": too many rows");
+  if (cols == 2) {
+    switch (r) {
+      case 4: lora_add_kernel<4, 2, PARTS><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      case 8: lora_add_kernel<8, 2, PARTS><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      case 16: lora_add_kernel<16, 2, PARTS><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      default: lora_add_kernel<32, 2, PARTS><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+    }
+  } else {
+    switch (r) {
+      case 4: lora_add_kernel<4, 1, PARTS><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      case 8: lora_add_kernel<8, 1, PARTS><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      case 16: lora_add_kernel<16, 1, PARTS><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      case 32: lora_add_kernel<32, 1, PARTS><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      default: lora_add_kernel<64, 1, PARTS><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+    }
+  }
+  return zt::check_cuda(cudaGetLastError(), (nm + " launch").c_str());
+}
+
+// out[0:n] = bf16(a), out[n:2n] = bf16(a - a0), out[2n:3n] = bf16((a - a0) - a1): three bf16
+// parts that sum to a exactly (a0 + a1 carry 16 of its bits, the rest fits a2), the
+// operand of a tensor-core x A^T whose fp32 result equals the fp32 product.
+__global__ void __launch_bounds__(256) lora_split_kernel(const float* __restrict__ a, __nv_bfloat16* __restrict__ out,
+                                                         int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (int64_t)gridDim.x * 256) {
+    const float v = a[i];
+    const __nv_bfloat16 a0 = __float2bfloat16_rn(v);
+    const float rest = __fsub_rn(v, __bfloat162float(a0));
+    const __nv_bfloat16 a1 = __float2bfloat16_rn(rest);
+    out[i] = a0;
+    out[n + i] = a1;
+    out[2 * n + i] = __float2bfloat16_rn(__fsub_rn(rest, __bfloat162float(a1)));
+  }
+}
 
 }  // namespace
 
@@ -553,36 +736,22 @@ int zt_eggroll_update_operands(const float* a, const float* b, const float* scal
 int zt_lora_add(void* out, const float* xa, const float* b, float scale, int64_t rows, int64_t n, int32_t r,
                 void* stream) {
   zt::clear_error();
-  if (rows < 0 || n <= 0) return zt::set_error(ZT_ERR_INVALID, "zt_lora_add: bad shape");
-  if (rows == 0) return ZT_OK;
-  if (!out || !xa || !b) return zt::set_error(ZT_ERR_INVALID, "zt_lora_add: null pointer");
-  if (n > (int64_t)INT32_MAX) return zt::set_error(ZT_ERR_LIMIT, "zt_lora_add: shape too large");
-  if (!aligned16(b)) return zt::set_error(ZT_ERR_INVALID, "zt_lora_add: b not 16-byte aligned");
-  if (r != 4 && r != 8 && r != 16 && r != 32 && r != 64)
-    return zt::set_error(ZT_ERR_INVALID, "zt_lora_add: rank must be 4, 8, 16, 32 or 64");
-  const int cols = (r <= 32 && n % 2 == 0 && ((uintptr_t)out & 3) == 0) ? 2 : 1;   // columns per thread
-  const dim3 grid((unsigned)((n + 256 * cols - 1) / (256 * cols)), (unsigned)((rows + kLoraBand - 1) / kLoraBand));
-  if (grid.y > 65535u) return zt::set_error(ZT_ERR_LIMIT, "zt_lora_add: too many rows");
-  cudaStream_t s = zt::as_stream(stream);
-  __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
-  const int32_t ni = (int32_t)n;
-  if (cols == 2) {
-    switch (r) {
-      case 4: lora_add_kernel<4, 2><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
-      case 8: lora_add_kernel<8, 2><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
-      case 16: lora_add_kernel<16, 2><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
-      default: lora_add_kernel<32, 2><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
-    }
-  } else {
-    switch (r) {
-      case 4: lora_add_kernel<4, 1><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
-      case 8: lora_add_kernel<8, 1><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
-      case 16: lora_add_kernel<16, 1><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
-      case 32: lora_add_kernel<32, 1><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
-      default: lora_add_kernel<64, 1><<<grid, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
-    }
-  }
-  return zt::check_cuda(cudaGetLastError(), "zt_lora_add launch");
+  return lora_add_launch<1>("zt_lora_add", out, xa, b, scale, rows, n, r, stream);
+}
+
+int zt_lora_add3(void* out, const float* xa3, const float* b, float scale, int64_t rows, int64_t n, int32_t r,
+                 void* stream) {
+  zt::clear_error();
+  return lora_add_launch<3>("zt_lora_add3", out, xa3, b, scale, rows, n, r, stream);
+}
+
+int zt_lora_split(const float* a, void* out, int64_t n, void* stream) {
+  zt::clear_error();
+  if (n < 0) return zt::set_error(ZT_ERR_INVALID, "zt_lora_split: n < 0");
+  if (n == 0) return ZT_OK;
+  if (!a || !out) return zt::set_error(ZT_ERR_INVALID, "zt_lora_split: null pointer");
+  lora_split_kernel<<<stream_grid(n, 8), 256, 0, zt::as_stream(stream)>>>(a, static_cast<__nv_bfloat16*>(out), n);
+  return zt::check_cuda(cudaGetLastError(), "zt_lora_split launch");
 }
 
 }  // extern "C"

@@ -630,3 +630,34 @@ def lora_add_(out: torch.Tensor, xa: torch.Tensor, b: torch.Tensor, scale: float
         L.check(L.load().zt_lora_add(out.data_ptr(), xa.data_ptr(), b.data_ptr(), float(scale), rows, n, r,
                                      _stream_ptr(out.device)), "zt_lora_add")
     return out
+
+
+def lora_add3_(out: torch.Tensor, xa3: torch.Tensor, b: torch.Tensor, scale: float) -> torch.Tensor:
+    """lora_add_ with xa given as three partial products xa3 [rows, 3r] fp32, summed as
+    ((p0 + p1) + p2) in fp32 inside the kernel (zt_lora_add3)."""
+    for t, name in ((out, "out"), (xa3, "xa3"), (b, "b")):
+        _check_cuda(t, name)
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    if out.dtype != torch.bfloat16 or xa3.dtype != torch.float32 or b.dtype != torch.float32:
+        raise ValueError("out must be bf16, xa3 and b fp32")
+    rows, n = out.shape
+    r = b.shape[1]
+    if xa3.shape != (rows, 3 * r) or b.shape != (n, r):
+        raise ValueError("inconsistent shapes")
+    with torch.cuda.device(out.device):
+        L.check(L.load().zt_lora_add3(out.data_ptr(), xa3.data_ptr(), b.data_ptr(), float(scale), rows, n, r,
+                                      _stream_ptr(out.device)), "zt_lora_add3")
+    return out
+
+
+def lora_split(a: torch.Tensor) -> torch.Tensor:
+    """[3, *a.shape] bf16 parts of the fp32 tensor a that sum to it exactly (zt_lora_split):
+    bf16(a), bf16(a - p0), bf16(a - p0 - p1)."""
+    _check_cuda(a, "a")
+    if a.dtype != torch.float32 or not a.is_contiguous():
+        raise ValueError("a must be a contiguous fp32 tensor")
+    out = torch.empty((3, *a.shape), dtype=torch.bfloat16, device=a.device)
+    with torch.cuda.device(a.device):
+        L.check(L.load().zt_lora_split(a.data_ptr(), out.data_ptr(), a.numel(), _stream_ptr(a.device)), "zt_lora_split")
+    return out

@@ -65,22 +65,19 @@ class LoRALinear(nn.Module):
         aw, bw = self.lora_A.weight, self.lora_B.weight
         if (not torch.is_grad_enabled() and out.is_cuda and out.dtype == torch.bfloat16 and x.dtype == torch.bfloat16
                 and aw.dtype == torch.float32 and bw.dtype == torch.float32 and bw.shape[1] in _FUSED_R
-                and out.is_contiguous()):
+                and out.is_contiguous() and aw.is_contiguous() and bw.is_contiguous()):
             # Gradients off (the zeroth-order step): x A^T on the tensor cores from the bf16
-            # activations against A split into three bf16 parts that sum to it exactly (each
-            # product exact, fp32 accumulation: the fp32 product up to summation order), then
-            # lora_B(xa) * scaling cast to bf16 and added to `out` in one pass (zt_lora_add),
-            # with the reference's rounding points. No autograd record is made.
+            # activations against A split into three bf16 parts that sum to it exactly
+            # (zt_lora_split; each product exact, fp32 accumulation: the fp32 product up to
+            # summation order), then the three partial products summed and lora_B(xa) *
+            # scaling cast to bf16 and added to `out` in one pass (zt_lora_add3), with the
+            # reference's rounding points. Three launches; no autograd record is made.
             from . import kernels as K
             r, n = bw.shape[1], out.shape[-1]
-            a0 = aw.bfloat16()
-            rest = aw - a0.float()
-            a1 = rest.bfloat16()
-            a2 = (rest - a1.float()).bfloat16()
+            a3 = K.lora_split(aw.detach()).view(3 * r, -1)                                # [3r, in] bf16
             x2 = x.reshape(-1, x.shape[-1])
-            xa3 = torch.mm(x2, torch.cat([a0, a1, a2], dim=0).T, out_dtype=torch.float32)   # [rows, 3r]
-            xa = (xa3[:, :r] + xa3[:, r:2 * r] + xa3[:, 2 * r:]).contiguous()
-            K.lora_add_(out.view(-1, n), xa, bw.detach(), self.scaling)
+            xa3 = torch.mm(x2, a3.T, out_dtype=torch.float32)                               # [rows, 3r]
+            K.lora_add3_(out.view(-1, n), xa3, bw.detach(), self.scaling)   # sums the 3 parts, then the tail
             return out
         xa = self.lora_A(x.to(self.lora_dtype))
         delta = self.lora_B(xa) * self.scaling
