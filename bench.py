@@ -45,7 +45,8 @@ def parse():
     ap.add_argument("--no-eggroll", action="store_true", help="skip the EGGROLL population measurement")
     ap.add_argument("--no-mezo", action="store_true", help="skip the MeZO full fine-tune step measurement")
     ap.add_argument("--no-lora", action="store_true", help="skip the MeZO-Adam LoRA step measurement")
-    ap.add_argument("--profile-case", choices=["chain", "full", "replay", "eggroll", "eggroll-gated", "eggroll-forward"],
+    ap.add_argument("--profile-case", choices=["chain", "full", "replay", "eggroll", "eggroll-gated", "eggroll-forward",
+                                               "mezo-step", "lora-step"],
                     default=None,
                     help="small case for ncu: one bf16 tensor of 2^28 elements, 3 launches of the "
                          "-2eps pass (chain) or of the restore+accumulate+perturb pass (full); or 3 "
@@ -112,12 +113,55 @@ def eggroll_gemm_bench(rows: int = 16384, T: int = 1024, reps: int = 10):
                       "peak_source": "MEASURED_PEAKS.json bf16_tflops" if "bf16_tflops" in peaks else "fallback"}))
 
 
+def _profile_step(kind: str):
+    """CUDA kernel table (torch.profiler) of one ZO step after two warm-up steps: the MeZO
+    full fine-tune of the Llama-1B shape (8 pairs, 16 x 512 tokens each) or the seed-window
+    MeZO-Adam step on rank-16 LoRA adapters of the Llama-8B shape (8 x 1024 tokens)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    from zotitan_b200.data import synthetic_token_batch
+    from zotitan_b200.llama_fused import fuse_llama
+    from zotitan_b200.lora import LoRAConfig, make_lora
+    from zotitan_b200.objective import SyntheticTokensObjective
+    from zotitan_b200.synthetic import LLAMA_1B, LLAMA_8B, build_llama
+    from zotitan_b200.train_zo import ZOConfig, ZOOptimizer
+    cfg = ZOConfig()
+    if kind == "mezo-step":
+        shape, B, S = LLAMA_1B, 16, 512
+        model = build_llama(shape, device="cuda", seed=0, max_positions=S)
+        objective = SyntheticTokensObjective(shape.vocab, S, z_loss_weight=1e-4)
+        cfg.eps, cfg.z_batch, cfg.base.lr = EPS, 8, 1e-5
+    else:
+        shape, B, S = LLAMA_8B, 8, 1024
+        model = build_llama(shape, device="cuda", seed=0, max_positions=S)
+        make_lora(model, LoRAConfig(r=16, alpha=32, dtype="fp32"))
+        objective = SyntheticTokensObjective(shape.vocab, S)
+        cfg.eps, cfg.z_batch, cfg.base.lr = EPS, 1, 1e-5
+        cfg.mom.momentum_method, cfg.mom.beta1, cfg.mom.beta2, cfg.mom.second_moment = "seed_window", 0.9, 0.999, True
+        cfg.seed_window.size = 16
+    fuse_llama(model)
+    named = [(n, p) for n, p in model.named_parameters() if p.requires_grad]
+    opt = ZOOptimizer(named, cfg, objective.score, total_steps=10)
+    batches = [synthetic_token_batch(shape.vocab, B, S, j, device="cuda") for j in range(cfg.z_batch)]
+    for _ in range(2):
+        opt.step(model, batches)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        opt.step(model, batches)
+        torch.cuda.synchronize()
+    print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=20, max_name_column_width=90))
+
+
 def profile_case(kind: str):
     """A few launches of one pass kind on a 512 MB bf16 tensor (larger than L2)."""
     import torch
 
     from zotitan_b200 import _lib as L
     from zotitan_b200 import kernels as K
+    if kind in ("mezo-step", "lora-step"):
+        _profile_step(kind)
+        return
     if kind == "eggroll-forward":
         from zotitan_b200.eggroll import EggrollConfig, EggrollPopulation
         from zotitan_b200.synthetic import LLAMA_8B, build_llama
