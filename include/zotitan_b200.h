@@ -456,7 +456,7 @@ ZT_API int zt_eggroll_update_operands(const float* a, const float* b, const floa
  *   out[t, c] = bf16(out[t, c] + bf16(scale * sum_r xa[t, r] b[c, r]))
  * with out [rows, n] bf16 holding the base layer's output (updated in place), xa [rows, r]
  * fp32 = lora_A(x) and b [n, r] fp32 = lora_B.weight. r in {4, 8, 16, 32, 64}; xa and b
- * row-major and contiguous. For r in {8, 16, 32}, n % 8 == 0 and a 16-byte aligned out the
+ * row-major and contiguous. For r in {8, 16}, n % 8 == 0 and 16-byte aligned out and xa the
  * sum runs on the tensor cores (mma.sync on TF32 with each fp32 operand split into a hi
  * and a lo part, three products: ~2^-22 relative before the bf16 rounding); otherwise in
  * fp32 FMAs over r in order. */

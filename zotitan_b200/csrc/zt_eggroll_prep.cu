@@ -430,7 +430,8 @@ bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 // taken as lo*hi + hi*lo + hi*hi (the dropped lo*lo term and the TF32 rounding of lo
 // leave ~2^-22 relative, far inside the bf16 rounding that follows). A block owns 64
 // rows x 128 columns: the band of xa (the three partial products summed in order when
-// PARTS = 3) and the block's 128 rows of b are staged in shared memory; warp w computes
+// PARTS = 3) and the block's 128 rows of b are staged in shared memory as their TF32
+// hi / lo parts, split once per element; warp w computes
 // rows 16*(w/2) .. +16 and columns 64*(w%2) .. +64 and writes bf16(scale * delta) to a
 // shared tile (rows padded to 136 bf16: conflict-free fragment writes); then every
 // thread updates 8 consecutive outputs of a row with one 16-byte read and write of out.
@@ -453,28 +454,51 @@ template <int R, int PARTS>
 __global__ void __launch_bounds__(256) lora_add_mma_kernel(__nv_bfloat16* __restrict__ out, const float* __restrict__ xa,
                                                            const float* __restrict__ bw, float scale, int64_t rows,
                                                            int32_t n) {
-  static_assert(R % 8 == 0, "k steps of 8");
+  static_assert(R % 8 == 0 && R <= 16, "k steps of 8; the staged operands fit 48 KB up to R = 16");
   constexpr int KS = R / 8;
   constexpr int LD = R + 4;  // padded rows: conflict-free fragment reads
-  __shared__ float sa[kMmaRows][LD];
-  __shared__ float sb[kMmaCols][LD];
+  constexpr int R4 = R / 4;
+  // operands staged once per block as their TF32 hi / lo parts (bit patterns)
+  __shared__ uint32_t sah[kMmaRows][LD], sal[kMmaRows][LD];
+  __shared__ uint32_t sbh[kMmaCols][LD], sbl[kMmaCols][LD];
   __shared__ __align__(16) __nv_bfloat16 sd[kMmaRows][kMmaLdd];
   const int64_t row0 = (int64_t)blockIdx.y * kMmaRows;
   const int col0 = blockIdx.x * kMmaCols;
   const int nr = (int)((rows - row0) < kMmaRows ? (rows - row0) : kMmaRows);
   const int nc = (n - col0) < kMmaCols ? (n - col0) : kMmaCols;
-  for (int i = threadIdx.x; i < kMmaRows * R; i += 256) {
-    const int rr = i / R, k = i % R;
-    float v = 0.f;
+  // xa rows (PARTS * R floats, 16-byte aligned) and b rows (R floats) in 16-byte pieces
+  for (int i = threadIdx.x; i < kMmaRows * R4; i += 256) {
+    const int rr = i / R4, k = (i % R4) * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (rr < nr) {
       const float* p = xa + (row0 + rr) * (PARTS * R) + k;
-      v = PARTS == 1 ? p[0] : __fadd_rn(__fadd_rn(p[0], p[R]), p[2 * R]);
+      v = *reinterpret_cast<const float4*>(p);
+      if (PARTS == 3) {
+        const float4 v1 = *reinterpret_cast<const float4*>(p + R);
+        const float4 v2 = *reinterpret_cast<const float4*>(p + 2 * R);
+        v = make_float4(__fadd_rn(__fadd_rn(v.x, v1.x), v2.x), __fadd_rn(__fadd_rn(v.y, v1.y), v2.y),
+                        __fadd_rn(__fadd_rn(v.z, v1.z), v2.z), __fadd_rn(__fadd_rn(v.w, v1.w), v2.w));
+      }
     }
-    sa[rr][k] = v;
+    const float e4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t h = tf32_of(e4[e]);
+      sah[rr][k + e] = h;
+      sal[rr][k + e] = tf32_of(__fsub_rn(e4[e], __uint_as_float(h)));
+    }
   }
-  for (int i = threadIdx.x; i < kMmaCols * R; i += 256) {
-    const int cc = i / R, k = i % R;
-    sb[cc][k] = cc < nc ? __ldg(bw + (size_t)(col0 + cc) * R + k) : 0.f;
+  for (int i = threadIdx.x; i < kMmaCols * R4; i += 256) {
+    const int cc = i / R4, k = (i % R4) * 4;
+    const float4 v = cc < nc ? __ldg(reinterpret_cast<const float4*>(bw + (size_t)(col0 + cc) * R + k))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float e4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t h = tf32_of(e4[e]);
+      sbh[cc][k + e] = h;
+      sbl[cc][k + e] = tf32_of(__fsub_rn(e4[e], __uint_as_float(h)));
+    }
   }
   __syncthreads();
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -484,12 +508,11 @@ __global__ void __launch_bounds__(256) lora_add_mma_kernel(__nv_bfloat16* __rest
 #pragma unroll
   for (int ks = 0; ks < KS; ++ks) {
     const int kb = ks * 8;
-    const float v[4] = {sa[wr + g][kb + t], sa[wr + g + 8][kb + t], sa[wr + g][kb + t + 4], sa[wr + g + 8][kb + t + 4]};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      ahi[ks][e] = tf32_of(v[e]);
-      alo[ks][e] = tf32_of(__fsub_rn(v[e], __uint_as_float(ahi[ks][e])));
-    }
+    ahi[ks][0] = sah[wr + g][kb + t];     alo[ks][0] = sal[wr + g][kb + t];
+    ahi[ks][1] = sah[wr + g + 8][kb + t]; alo[ks][1] = sal[wr + g + 8][kb + t];
+    ahi[ks][2] = sah[wr + g][kb + t + 4]; alo[ks][2] = sal[wr + g][kb + t + 4];
+    ahi[ks][3] = sah[wr + g + 8][kb + t + 4];
+    alo[ks][3] = sal[wr + g + 8][kb + t + 4];
   }
 #pragma unroll
   for (int ni = 0; ni < 8; ++ni) {
@@ -497,13 +520,8 @@ __global__ void __launch_bounds__(256) lora_add_mma_kernel(__nv_bfloat16* __rest
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int ks = 0; ks < KS; ++ks) {
-      const float bv[2] = {sb[cb + g][ks * 8 + t], sb[cb + g][ks * 8 + t + 4]};
-      uint32_t bhi[2], blo[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        bhi[e] = tf32_of(bv[e]);
-        blo[e] = tf32_of(__fsub_rn(bv[e], __uint_as_float(bhi[e])));
-      }
+      const uint32_t bhi[2] = {sbh[cb + g][ks * 8 + t], sbh[cb + g][ks * 8 + t + 4]};
+      const uint32_t blo[2] = {sbl[cb + g][ks * 8 + t], sbl[cb + g][ks * 8 + t + 4]};
       mma_tf32(acc, alo[ks], bhi);
       mma_tf32(acc, ahi[ks], blo);
       mma_tf32(acc, ahi[ks], bhi);
@@ -514,12 +532,20 @@ __global__ void __launch_bounds__(256) lora_add_mma_kernel(__nv_bfloat16* __rest
         __floats2bfloat162_rn(acc[2] * scale, acc[3] * scale);
   }
   __syncthreads();
-  // 16 threads per row, 8 columns each (n % 8 == 0: a group is wholly in or out of range)
-  const int cq = (threadIdx.x % 16) * 8;
-  for (int rr = threadIdx.x / 16; rr < nr; rr += 16) {
-    if (cq >= nc) continue;
+  // 16 threads per row, 8 columns each (n % 8 == 0: a group is wholly in or out of range);
+  // a thread's four rows are all loaded before any is written back, so the four reads
+  // of out are in flight together
+  const int cq = (threadIdx.x % 16) * 8, q0 = threadIdx.x / 16;
+  uint4 ov[kMmaRows / 16];
+#pragma unroll
+  for (int j = 0; j < kMmaRows / 16; ++j)
+    if (q0 + 16 * j < nr && cq < nc) ov[j] = *reinterpret_cast<const uint4*>(out + (row0 + q0 + 16 * j) * n + col0 + cq);
+#pragma unroll
+  for (int j = 0; j < kMmaRows / 16; ++j) {
+    const int rr = q0 + 16 * j;
+    if (rr >= nr || cq >= nc) continue;
     uint4* p = reinterpret_cast<uint4*>(out + (row0 + rr) * n + col0 + cq);
-    const uint4 o = *p;
+    const uint4 o = ov[j];
     const uint4 dv = *reinterpret_cast<const uint4*>(&sd[rr][cq]);
     const uint32_t ow[4] = {o.x, o.y, o.z, o.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
     uint32_t yw[4];
@@ -548,13 +574,12 @@ int lora_add_launch(const char* name, void* out, const float* xa, const float* b
   cudaStream_t s = zt::as_stream(stream);
   __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
   const int32_t ni = (int32_t)n;
-  if (r % 8 == 0 && r <= 32 && n % 8 == 0 && ((uintptr_t)out & 15) == 0) {  // tensor-core form
+  if ((r == 8 || r == 16) && n % 8 == 0 && aligned16(out) && aligned16(xa)) {  // tensor-core form
     const dim3 g2((unsigned)((n + kMmaCols - 1) / kMmaCols), (unsigned)((rows + kMmaRows - 1) / kMmaRows));
     if (g2.y > 65535u) return zt::set_error(ZT_ERR_LIMIT, nm + ": too many rows");
     switch (r) {
       case 8: lora_add_mma_kernel<8, PARTS><<<g2, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
-      case 16: lora_add_mma_kernel<16, PARTS><<<g2, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
-      default: lora_add_mma_kernel<32, PARTS><<<g2, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      default: lora_add_mma_kernel<16, PARTS><<<g2, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
     }
     return zt::check_cuda(cudaGetLastError(), (nm + " launch").c_str());
   }
