@@ -45,7 +45,7 @@ def parse():
     ap.add_argument("--no-eggroll", action="store_true", help="skip the EGGROLL population measurement")
     ap.add_argument("--no-mezo", action="store_true", help="skip the MeZO full fine-tune step measurement")
     ap.add_argument("--no-lora", action="store_true", help="skip the MeZO-Adam LoRA step measurement")
-    ap.add_argument("--profile-case", choices=["chain", "full", "replay", "eggroll", "eggroll-gated", "eggroll-forward",
+    ap.add_argument("--profile-case", choices=["chain", "full", "replay", "chain-cached", "full-cached", "eggroll", "eggroll-gated", "eggroll-forward",
                                                "mezo-step", "lora-step"],
                     default=None,
                     help="small case for ncu: one bf16 tensor of 2^28 elements, 3 launches of the "
@@ -215,6 +215,22 @@ def profile_case(kind: str):
     if kind == "chain":
         tab = K.ParamTable([p])
         cfg, streams = K.PassCfg(), [K.Stream(5, (f(-2e-3),))]
+    elif kind == "chain-cached":   # the -2eps pass reading z from the noise cache
+        tab = K.ParamTable([p])
+        zc = tab.noise_cache()
+        tab.run(K.PassCfg(zcache=zc.data_ptr()), [K.Stream(5, (f(1e-3),), z_store=True)])
+        cfg, streams = K.PassCfg(zcache=zc.data_ptr()), [K.Stream(5, (f(-2e-3),), z_load=True)]
+    elif kind == "full-cached":    # restore (z from the cache) + grad_est + next perturb (z stored)
+        ge = torch.zeros_like(p)
+        vals = torch.tensor([2.01, 2.0], device="cuda")
+        tab = K.ParamTable([p], ge=[ge])
+        zc = tab.noise_cache()
+        tab.run(K.PassCfg(zcache=zc.data_ptr()), [K.Stream(4, (f(1e-3),), z_store=True)])
+        cfg = K.PassCfg(ge_mode=L.ZT_GE_ACCUM, ge_load=True, ge_store=True, dev_vals=vals.data_ptr(),
+                        dev_inv2eps=f(500.0), dev_invz=f(1 / 64), dev_tau=float("inf"), zcache=zc.data_ptr())
+        # repeated launches read back the field the previous launch stored: the values
+        # differ from a real schedule's, the work per element is the same
+        streams = [K.Stream(4, (f(1e-3),), ge_dev=True, z_load=True), K.Stream(5, (f(1e-3),), z_store=True)]
     elif kind == "replay":   # the sharded step's last pass: 16 pairs' chains + grad_est + SGD
         tab = K.ParamTable([p])
         cfg = K.PassCfg(ge_mode=L.ZT_GE_ACCUM, update=True, lr=f(1e-5))
@@ -459,31 +475,43 @@ def mezo_full_ft_steps(dev, rank: int, world: int, steps: int = 3, warmup: int =
                 for j in range(pairs)]
 
     plan = [batches_for(t) for t in range(warmup + steps)]
-    for t in range(warmup):
-        opt.step(model, plan[t])
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for t in range(warmup, warmup + steps):
-        m = opt.step(model, plan[t])
-    t1.record()
-    torch.cuda.synchronize()
-    ms = t0.elapsed_time(t1)
-    if world > 1:
-        tt = torch.tensor([ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
+
+    def timed(opt):
+        for t in range(warmup):
+            opt.step(model, plan[t])
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for t in range(warmup, warmup + steps):
+            m = opt.step(model, plan[t])
+        t1.record()
+        torch.cuda.synchronize()
+        ms = t0.elapsed_time(t1)
+        if world > 1:
+            tt = torch.tensor([ms], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms = float(tt.item())
+        return ms, m
+
+    ms, m = timed(opt)
+    cached = opt.zcache is not None
+    del opt
+    # the same steps with the noise cache set the other way (default: on when it fits)
+    ms_nc, _ = timed(ZOOptimizer(named, cfg, objective.score, total_steps=steps + warmup, noise_cache=not cached))
     n_params = sum(p.numel() for _, p in named)
-    del opt, model, named, plan
+    del model, named, plan
     torch.cuda.empty_cache()
     return {"metric": "ZO steps/s (MeZO full fine-tune, Llama-3.2-1B shape)", "value": steps / (ms * 1e-3),
             "unit": "ZO steps/s", "ms_per_step": ms / steps, "steps": steps, "warmup": warmup,
             "pairs_per_step": pairs, "forwards_per_step": 2 * pairs, "batch": B, "seq_len": S,
             "tokens_per_step": 2 * pairs * B * S, "params": n_params, "z_loss": 1e-4,
             "scorer": "fused CUDA cross-entropy (zt_xent_rows)", "parallelism": f"pair-sharded x{world}",
-            "loss_last_step": m["loss"], "proj_grad_last_step": m["proj_grad"]}
+            "loss_last_step": m["loss"], "proj_grad_last_step": m["proj_grad"],
+            "noise_cache": cached,
+            ("no_noise_cache" if cached else "with_noise_cache"): {
+                "value": steps / (ms_nc * 1e-3), "ms_per_step": ms_nc / steps, "cache_bytes": 4 * n_params}}
 
 
 def mezo_adam_lora_steps(dev, rank: int, world: int, steps: int = 3, warmup: int = 2):
@@ -554,6 +582,91 @@ def mezo_adam_lora_steps(dev, rank: int, world: int, steps: int = 3, warmup: int
 
 
 # ── our arm ─────────────────────────────────────────────────────────────────────────
+
+def pass_bytes(noise_cache: bool) -> dict:
+    """Algorithmic bytes per bf16 element of the microbench's passes. Without the noise
+    cache: -2eps pass theta read + written (4), restore/accumulate/perturb pass theta and
+    grad_est read + written (8). With it, z (fp32) is read by the -2eps pass (+4), read
+    and rewritten by the restore/accumulate/perturb pass (+8), written by the first +eps
+    pass (4 + 4)."""
+    return ({"perturb": 8, "accum": 16, "plus": 8} if noise_cache else {"perturb": 4, "accum": 8, "plus": 4})
+
+
+def microbench_variant(args, named, cfg, vals_dev, dev, world, barrier, noise_cache: bool):
+    """The kernel microbench again with the noise cache set the other way (noise_cache=False:
+    every pass regenerates its fields in registers, three noise evaluations per element and
+    pair; True: one). Same seeds, values and steps as the headline run; per-launch CUDA
+    events for the -2eps, the restore / grad_est / next-perturb and the first +eps passes."""
+    import torch
+    import torch.distributed as dist
+
+    from zotitan_b200.objective import Score
+    from zotitan_b200.train_zo import ZOOptimizer
+
+    class Vals:
+        def __init__(self):
+            self.k = 0
+
+        def __call__(self, model, batch):
+            i = self.k % (2 * args.seeds)
+            self.k += 1
+            return Score(vals_dev[i], {})
+
+    opt = ZOOptimizer(named, cfg, Vals(), noise_cache=noise_cache)
+    rng = np.random.default_rng(12345)
+    opt.planner._draw_seeds = lambda n: [int(x) for x in rng.integers(0, 2**64 - 1, n, dtype=np.uint64)]
+    events, on = {"perturb": [], "accum": [], "plus": []}, [False]
+    orig_run = opt.table.run
+
+    def run(cfg_, streams):
+        kind = None
+        if on[0]:
+            if len(streams) == 1 and streams[0].chain and streams[0].chain[0] < 0:
+                kind = "perturb"
+            elif any(s.ge_dev for s in streams):
+                kind = "accum"
+            elif len(streams) == 1 and streams[0].chain and streams[0].chain[0] > 0:
+                kind = "plus"
+        if kind:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+        orig_run(cfg_, streams)
+        if kind:
+            b.record()
+            events[kind].append((a, b))
+    opt.table.run = run
+    batches = [None] * args.seeds
+    for _ in range(args.warmup):
+        opt.step(None, batches)
+    barrier()
+    on[0] = True
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        opt.step(None, batches)
+    t1.record()
+    barrier()
+    on[0] = False
+    ms = t0.elapsed_time(t1)
+    mean = {k: float(np.mean([a.elapsed_time(b) for a, b in v])) if v else 0.0 for k, v in events.items()}
+    if world > 1:
+        t = torch.tensor([ms, mean["perturb"], mean["accum"], mean["plus"]], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, mean["perturb"], mean["accum"], mean["plus"] = t.tolist()
+    numel = opt.table.numel
+    cache_bytes = opt.zcache.numel() * 4 if opt.zcache is not None else 0
+    del opt
+    torch.cuda.empty_cache()
+    b = pass_bytes(noise_cache)
+    gbs = lambda nbytes, t: nbytes / (t * 1e-3) / 1e9 if t else None  # noqa: E731
+    return {"value": args.steps / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms / args.steps,
+            "noise_cache": noise_cache, "cache_bytes": cache_bytes,
+            "perturb_pass_ms": mean["perturb"], "perturb_pass_gbs": gbs(b["perturb"] * numel, mean["perturb"]),
+            "accum_pass_ms": mean["accum"], "accum_pass_gbs": gbs(b["accum"] * numel, mean["accum"]),
+            "plus_pass_ms": mean["plus"], "plus_pass_gbs": gbs(b["plus"] * numel, mean["plus"]),
+            "philox_gelem_per_s": numel / (mean["accum"] * 1e-3) / 1e9 if mean["accum"] else None,
+            "bytes_per_element": b}
+
 
 def run_ours(args, rank, local_rank, world):
     import torch
@@ -677,8 +790,13 @@ def run_ours(args, rank, local_rank, world):
         t = torch.tensor([ms, e2e_ms, pmean, amean], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e2e_ms, pmean, amean = t.tolist()
+    cached = opt.zcache is not None
+    del opt
+    torch.cuda.empty_cache()
+    # the other schedule: every field regenerated in registers (or cached, if the default was off)
+    alt = microbench_variant(args, named, cfg, vals_dev, dev, world, barrier, noise_cache=not cached)
     # release the microbench's buffers, then the EGGROLL population measurement (all ranks)
-    del opt, named
+    del named
     torch.cuda.empty_cache()
     egg = eggroll_member_evals(dev, rank, world) if not args.no_eggroll else None
     mezo = mezo_full_ft_steps(dev, rank, world) if not args.no_mezo else None
@@ -694,20 +812,26 @@ def run_ours(args, rank, local_rank, world):
     except (OSError, ValueError):
         pass
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
-    perturb_bytes = 2 * 2 * numel            # bf16 theta read + write
-    accum_bytes = 2 * 2 * 2 * numel          # bf16 theta and grad_est read + write
+    pb = pass_bytes(cached)
+    perturb_bytes = pb["perturb"] * numel
+    accum_bytes = pb["accum"] * numel
     perturb_gbs = perturb_bytes / (pmean * 1e-3) / 1e9 if pmean else None
     if amean:   # single-GPU schedule: the restore/accumulate/perturb pass dominates
-        achieved, kname, kbytes = accum_bytes / (amean * 1e-3) / 1e9, \
-            "fast_kernel<bf16, kFastAccum>: restore + grad_est accumulation + perturb (2 noise streams)", accum_bytes
+        achieved, kbytes = accum_bytes / (amean * 1e-3) / 1e9, accum_bytes
+        kname = ("fast_kernel<bf16, kFastAccum, kZLoadStore>: restore (z read from the noise cache) + grad_est "
+                 "accumulation + perturb (z regenerated and cached)" if cached else
+                 "fast_kernel<bf16, kFastAccum>: restore + grad_est accumulation + perturb (2 noise streams)")
+        tkey = "accum_pass_cached" if cached else "accum_pass"
     else:       # sharded schedule: the +eps / -2eps passes on the live copy dominate
-        achieved, kname, kbytes = perturb_gbs, "fast_kernel<bf16, kFastChain1>: -2eps perturb pass (1 noise stream)", \
-            perturb_bytes
+        achieved, kbytes = perturb_gbs, perturb_bytes
+        kname = ("fast_kernel<bf16, kFastChain1, kZLoad>: -2eps perturb pass (z read from the noise cache)" if cached
+                 else "fast_kernel<bf16, kFastChain1>: -2eps perturb pass (1 noise stream)")
+        tkey = "perturb_pass_cached" if cached else "perturb_pass"
     traffic = None
     prof = os.path.join(HERE, "profiles", "pass_kernel_traffic.json")
     if os.path.exists(prof):
         try:
-            traffic = json.load(open(prof)).get("accum_pass" if amean else "perturb_pass", {}).get("dram_bytes_per_launch")
+            traffic = json.load(open(prof)).get(tkey, {}).get("dram_bytes_per_launch")
         except (ValueError, AttributeError):
             traffic = None
     value = args.steps / (ms * 1e-3)
@@ -718,14 +842,19 @@ def run_ours(args, rank, local_rank, world):
         "config": {"workload": "Llama-3.2-1B-shaped parameter set, 64 seeds/step (kernel microbench)",
                    "params": numel, "tensors": n_tensors, "seeds_per_step": args.seeds, "eps": EPS,
                    "passes_per_step": 2 * args.seeds + 1, "parallelism": f"seed-sharded x{world}",
-                   "l2": "inputs (2.47 GB of bf16 parameters) larger than L2"},
+                   "l2": "inputs (2.47 GB of bf16 parameters) larger than L2",
+                   "noise_cache": cached},
         "perturb_pass_gbs": perturb_gbs, "perturb_pass_ms": pmean, "accum_pass_ms": amean,
-        "philox_gelem_per_s": numel / (pmean * 1e-3) / 1e9 if pmean else None,
+        "philox_gelem_per_s": (numel / (amean * 1e-3) / 1e9 if cached and amean else
+                               numel / (pmean * 1e-3) / 1e9 if pmean and not cached else None),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": (achieved / hbm_peak) if achieved else None, "traffic": traffic,
                      "kernel": kname, "algorithmic_bytes_per_launch": kbytes,
-                     "note": "instruction-bound (Philox4x32-10 + logf/cosf per element per noise stream); "
-                             "see profiles/",
+                     "note": ("instruction-bound: one Philox4x32-10 + logf/cosf evaluation per element (the next "
+                              "pair's field), z read and rewritten through the noise cache; the -2eps pass reads "
+                              "z from the cache at perturb_pass_gbs; see profiles/" if cached else
+                              "instruction-bound (Philox4x32-10 + logf/cosf per element per noise stream); "
+                              "see profiles/"),
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback 6650 GB/s"},
         "clocks": clk,
         "gpu_launches": launches,
@@ -733,6 +862,7 @@ def run_ours(args, rank, local_rank, world):
                 "h2d_bytes_per_step": 4 * 2 * args.seeds, "d2h_bytes_per_step": 4 * 2 * args.seeds},
         "metrics_last_step": {k: m[k] for k in ("loss", "proj_grad")},
     }
+    line["no_noise_cache" if cached else "noise_cache"] = alt
     if cpu_line is not None:
         line["cpu_baseline"] = cpu_line
     if egg is not None:

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define ZT_ABI_VERSION 6
+#define ZT_ABI_VERSION 7
 
 /* dtypes of parameter tensors */
 #define ZT_F32 0
@@ -144,6 +144,13 @@ ZT_API int zt_plan_init(const zt_tensor* host_tensors, int32_t n_tensors, uint32
 #define ZT_STREAM_MOM 2  /* contributes mom_coef * z to the reconstructed momentum */
 #define ZT_STREAM_GE_DEV 4 /* with ZT_STREAM_GE: ge_coef is computed on the device from
                               cfg->dev_vals (see zt_pass_cfg) instead of taken from ge_coef */
+/* Noise cache (cfg->zcache). The Gaussian field costs far more to regenerate (Philox4x32-10,
+ * log, cos and sqrt per element) than an fp32 read from HBM, so a pair's field can be
+ * written once and read back by the later passes of the same pair. */
+#define ZT_STREAM_Z_STORE 8  /* the regenerated z is also written to cfg->zcache */
+#define ZT_STREAM_Z_LOAD 16  /* z is read from cfg->zcache instead of regenerated; the cache
+                                must hold this stream's field (stored by an earlier pass with
+                                the same seed and plan; the library cannot check this) */
 
 /* One noise stream: z = the Gaussian field of pair seed `seed`. Streams are applied in
  * array order. For each stream, the n_chain perturbations theta <- theta + chain[c] * z
@@ -223,6 +230,13 @@ typedef struct zt_pass_cfg {
    * of a step this way across ranks). */
   int64_t unit_begin;
   int64_t unit_end;
+  /* Noise cache for ZT_STREAM_Z_STORE / ZT_STREAM_Z_LOAD streams: plan->n_units *
+   * ZT_UNIT_ELEMS fp32, 16-byte aligned, caller-owned; unit u's elements sit at
+   * zcache[u * ZT_UNIT_ELEMS ...] (a tensor's last unit is padded). At most one stream
+   * of a pass loads and at most one stores, and the loading stream comes first, so a
+   * pass may read pair j's field and replace it with pair j+1's in place. NULL when no
+   * stream uses it. */
+  float* zcache;
 } zt_pass_cfg;
 
 /* A pass is rejected (ZT_ERR_INVALID) when cfg reads or writes a buffer (live, m, v,
@@ -231,8 +245,9 @@ typedef struct zt_pass_cfg {
  *
  * One fused pass over every element of every tensor of `plan`:
  *   1. theta = src buffer;
- *   2. for each stream in order: regenerate z in registers, apply its chain to theta,
- *      accumulate its ge / momentum contributions (noise is never written to memory);
+ *   2. for each stream in order: regenerate z in registers (or read it from the noise
+ *      cache, ZT_STREAM_Z_LOAD), apply its chain to theta, accumulate its ge / momentum
+ *      contributions (noise is written to memory only for a ZT_STREAM_Z_STORE stream);
  *   3. optional ge scaling, optimizer state (m, v) update and parameter update with
  *      weight decay, in the reference's op order (zotitan/train_zo.py:409-425, 376-407);
  *   4. theta to every buffer in `dst`.

@@ -35,9 +35,29 @@ def dev_coefficient(cfg, dev_values):
 UNIT = 2048
 
 
-def run_pass(tensors, n_params, cfg, streams, noise=ph.randn, dev_values=None):
+def check_noise_cache(zcache, streams):
+    """The noise-cache contract of zt_pass (ZT_STREAM_Z_LOAD / ZT_STREAM_Z_STORE): at most
+    one loading and one storing stream, the load first, and a loading stream's field must
+    be the one the cache holds (the last stored seed). ``zcache`` is a dict standing for
+    the cache's contents; the interpreter itself always regenerates z, which is what a
+    correct cache would return."""
+    loads = [i for i, s in enumerate(streams) if getattr(s, "z_load", False)]
+    stores = [i for i, s in enumerate(streams) if getattr(s, "z_store", False)]
+    assert len(loads) <= 1 and len(stores) <= 1, "one noise-cache load and one store per pass"
+    assert not (loads and stores) or loads[0] < stores[0], "the noise-cache load must precede the store"
+    for i in loads:
+        assert zcache.get("seed") == streams[i].seed, \
+            f"noise cache holds seed {zcache.get('seed')}, stream {i} loads seed {streams[i].seed}"
+    for i in stores:
+        zcache["seed"] = streams[i].seed
+
+
+def run_pass(tensors, n_params, cfg, streams, noise=ph.randn, dev_values=None, zcache=None):
     """A unit range (cfg.unit_begin, cfg.unit_end) restricts the pass to those 2048-element
-    units of the table (numbered in table order); elements outside are left untouched."""
+    units of the table (numbered in table order); elements outside are left untouched.
+    ``zcache``: a dict modelling the noise cache, checked with check_noise_cache."""
+    if zcache is not None:
+        check_noise_cache(zcache, streams)
     dev_coef = dev_coefficient(cfg, dev_values) if dev_values is not None else None
     ub, ue = getattr(cfg, "unit_begin", 0), getattr(cfg, "unit_end", 0)
     base = 0

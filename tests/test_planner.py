@@ -32,9 +32,11 @@ def make_tensors(params, dtypes, planner, sharded):
     return ts
 
 
-def run_planner(case, world, rank=0):
+def run_planner(case, world, rank=0, noise_cache=False):
     params = case.params()
     pl = StepPlanner(case.cfg, total_steps=case.spec["total_steps"], rank=rank, world=world)
+    pl.noise_cache = noise_cache
+    zc = {} if noise_cache else None
     ts = make_tensors(params, case.dtypes, pl, world > 1)
     n = len(params)
     vals_all = iter(case.values)
@@ -45,13 +47,13 @@ def run_planner(case, world, rank=0):
         vals = [next(vals_all) for _ in range(2 * Z)]
         prev = None
         for j in local:
-            run_pass(ts, n, *_spec(pl.plus_pass(j, prev)), dev_values=_dev(pl.plus_pass(j, prev), vals))
+            run_pass(ts, n, *_spec(pl.plus_pass(j, prev)), dev_values=_dev(pl.plus_pass(j, prev), vals), zcache=zc)
             snaps.append(flat([t["live"] if world > 1 else t["data"] for t in ts]))
-            run_pass(ts, n, *_spec(pl.minus_pass(j)))
+            run_pass(ts, n, *_spec(pl.minus_pass(j)), zcache=zc)
             snaps.append(flat([t["live"] if world > 1 else t["data"] for t in ts]))
             prev = j
         spec, m = pl.finish(vals)
-        run_pass(ts, n, spec.cfg, spec.streams)
+        run_pass(ts, n, spec.cfg, spec.streams, zcache=zc)
         afters.append(flat(params))
         if world > 1:
             assert np.array_equal(flat([t["live"] for t in ts]), afters[-1])
@@ -110,6 +112,35 @@ def test_sharded_schedule_master_matches_single_gpu(name, world):
             assert np.array_equal(a, b), rank
         for x, y in zip(mw, m1):
             assert x["proj_grad"] == y["proj_grad"]
+
+
+@pytest.mark.parametrize("world", [1, 2])
+@pytest.mark.parametrize("name", GAUSSIAN)
+def test_noise_cache_schedule_contract(name, world):
+    """With the noise cache on, every pass that reads a pair's field from the cache finds
+    that pair's field there (stored by the pair's +eps pass, never overwritten before its
+    last use), and the schedule is otherwise unchanged: same parameters and metrics."""
+    case = StepCase(_G, name)
+    a0, m0, s0 = run_planner(case, world=world)
+    a1, m1, s1 = run_planner(case, world=world, noise_cache=True)   # asserts the contract
+    for a, b in zip(a0 + s0, a1 + s1):
+        assert np.array_equal(a, b)
+    for x, y in zip(m0, m1):
+        assert x["proj_grad"] == y["proj_grad"]
+
+
+def test_noise_cache_contract_violations_detected():
+    """The interpreter's cache model rejects a load of a field the cache does not hold and
+    a store placed before the load."""
+    from oracle.pass_interp import check_noise_cache
+    from zotitan_b200.kernels import Stream
+    zc = {}
+    check_noise_cache(zc, [Stream(5, (1e-3,), z_store=True)])
+    check_noise_cache(zc, [Stream(5, (-2e-3,), z_load=True)])
+    with pytest.raises(AssertionError):
+        check_noise_cache(zc, [Stream(6, (1e-3,), z_load=True)])
+    with pytest.raises(AssertionError):
+        check_noise_cache(zc, [Stream(7, (1e-3,), z_store=True), Stream(5, (1e-3,), z_load=True)])
 
 
 def test_sharded_first_local_pair_sees_reference_perturbation():

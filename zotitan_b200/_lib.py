@@ -18,6 +18,7 @@ ZT_MAX_CHAIN = 3
 ZT_MAX_NUMEL = 2**31 - 1
 ZT_UNIT_ELEMS = 2048
 ZT_STREAM_GE, ZT_STREAM_MOM, ZT_STREAM_GE_DEV = 1, 2, 4
+ZT_STREAM_Z_STORE, ZT_STREAM_Z_LOAD = 8, 16
 ZT_GE_NONE, ZT_GE_PRODUCT, ZT_GE_ACCUM = 0, 1, 2
 ZT_MOM_NONE, ZT_MOM_STORED_EMA, ZT_MOM_SEED_WINDOW = 0, 1, 2
 ZT_WD_NONE, ZT_WD_STANDARD, ZT_WD_ANCHORED_L2, ZT_WD_ANCHORED_L1 = 0, 1, 2, 3
@@ -33,7 +34,7 @@ EXPORTS = ("zt_last_error", "zt_abi_version", "zt_param_key", "zt_philox_words",
 ZT_STATIC_MAX_TENSORS = 1024
 ZT_EGGROLL_MAX_PAIRS = 512
 ZT_EGGROLL_FACTOR_WORK_FLOATS = 64 * 20
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 
 class ZtTensor(ctypes.Structure):
@@ -65,7 +66,7 @@ class ZtPassCfg(ctypes.Structure):
                 ("wd_factor", ctypes.c_float), ("ge_load", ctypes.c_int32), ("ge_store", ctypes.c_int32),
                 ("dev_vals", ctypes.c_void_p), ("dev_inv2eps", ctypes.c_float), ("dev_invz", ctypes.c_float),
                 ("dev_tau", ctypes.c_float), ("reserved", ctypes.c_int32), ("unit_begin", ctypes.c_int64),
-                ("unit_end", ctypes.c_int64)]
+                ("unit_end", ctypes.c_int64), ("zcache", ctypes.c_void_p)]
 
 
 class ZtEggrollArgs(ctypes.Structure):

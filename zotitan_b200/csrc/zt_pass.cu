@@ -92,6 +92,27 @@ __device__ __forceinline__ void st_words(void* p, const uint32_t (&w)[NW]) {
   }
 }
 
+// Noise cache: a thread's EPT consecutive fp32 z values, 16-byte accesses. The cache
+// covers whole units, so ragged tails read and write full groups too. z is re-read only
+// by a later pass (after a forward in training), so both directions stream past L2.
+template <int EPT>
+__device__ __forceinline__ void ld_z(const float* p, float (&z)[EPT]) {
+  static_assert(EPT % 4 == 0, "16-byte groups");
+#pragma unroll
+  for (int i = 0; i < EPT / 4; ++i) {
+    const float4 v = __ldcs(reinterpret_cast<const float4*>(p) + i);
+    z[4 * i] = v.x; z[4 * i + 1] = v.y; z[4 * i + 2] = v.z; z[4 * i + 3] = v.w;
+  }
+}
+
+template <int EPT>
+__device__ __forceinline__ void st_z(float* p, const float (&z)[EPT]) {
+  static_assert(EPT % 4 == 0, "16-byte groups");
+#pragma unroll
+  for (int i = 0; i < EPT / 4; ++i)
+    __stcs(reinterpret_cast<float4*>(p) + i, make_float4(z[4 * i], z[4 * i + 1], z[4 * i + 2], z[4 * i + 3]));
+}
+
 template <int DT, int EPT> struct Io {
   static constexpr int kNW = EPT * Elem<DT>::kBytes / 4;
   __device__ static __forceinline__ float scalar_ld(const void* base, int64_t i) {
@@ -155,7 +176,8 @@ template <int DT, int EPT> struct Io {
 // Perturb / restore passes: theta <- round(theta + a*z) for each chained coefficient of
 // each stream (train_zo.py:350-351), nothing else.
 template <int DT, int EPT>
-__device__ __forceinline__ void run_chain(const PassParams& P, const zt_tensor& t, int64_t e0, int nvalid, bool vec) {
+__device__ __forceinline__ void run_chain(const PassParams& P, const zt_tensor& t, int64_t e0, int nvalid, bool vec,
+                                          float* zc) {
   using R = zt::Dt<DT>;
   using IO = Io<DT, EPT>;
   const zt_pass_cfg& c = P.cfg;
@@ -164,6 +186,23 @@ __device__ __forceinline__ void run_chain(const PassParams& P, const zt_tensor& 
   const uint32_t ctr0 = (uint32_t)e0;
   for (int s = 0; s < P.n_streams; ++s) {
     const KStream& S = P.streams[s];
+    if (S.flags & (ZT_STREAM_Z_LOAD | ZT_STREAM_Z_STORE)) {  // noise cache: z held as an array
+      float z[EPT];
+      if (S.flags & ZT_STREAM_Z_LOAD) {
+        ld_z<EPT>(zc, z);
+      } else {
+        const zt::RoundKeys rk = zt::round_keys(zt::param_key(S.seed, P.n_params, (uint32_t)t.index));
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) z[e] = zt::gauss_rk(ctr0 + (uint32_t)e, rk);
+        st_z<EPT>(zc, z);
+      }
+      for (int k = 0; k < S.n_chain; ++k) {
+        const float a = S.chain[k];
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) th[e] = R::round(__fmaf_rn(z[e], a, th[e]));
+      }
+      continue;
+    }
     const zt::RoundKeys rk = zt::round_keys(zt::param_key(S.seed, P.n_params, (uint32_t)t.index));
     const float a0 = S.chain[0], a1 = S.chain[1], a2 = S.chain[2];
     switch (S.n_chain) {  // the chain length is uniform: branch once, not per element
@@ -195,7 +234,7 @@ __device__ __forceinline__ void run_chain(const PassParams& P, const zt_tensor& 
 
 template <int DT, int EPT>
 __device__ __forceinline__ void run_full(const PassParams& P, const zt_tensor& t, int64_t e0, int nvalid, bool vec,
-                                         float dev_coef) {
+                                         float dev_coef, float* zc) {
   using R = zt::Dt<DT>;
   using IO = Io<DT, EPT>;
   const zt_pass_cfg& c = P.cfg;
@@ -214,10 +253,15 @@ __device__ __forceinline__ void run_full(const PassParams& P, const zt_tensor& t
   const uint32_t ctr0 = (uint32_t)e0;
   for (int s = 0; s < P.n_streams; ++s) {
     const KStream& S = P.streams[s];
-    const zt::RoundKeys rk = zt::round_keys(zt::param_key(S.seed, P.n_params, (uint32_t)t.index));
     float z[EPT];
+    if (S.flags & ZT_STREAM_Z_LOAD) {
+      ld_z<EPT>(zc, z);
+    } else {
+      const zt::RoundKeys rk = zt::round_keys(zt::param_key(S.seed, P.n_params, (uint32_t)t.index));
 #pragma unroll
-    for (int e = 0; e < EPT; ++e) z[e] = zt::gauss_rk(ctr0 + (uint32_t)e, rk);
+      for (int e = 0; e < EPT; ++e) z[e] = zt::gauss_rk(ctr0 + (uint32_t)e, rk);
+      if (S.flags & ZT_STREAM_Z_STORE) st_z<EPT>(zc, z);
+    }
     // _apply_z: theta <- round(theta + a*z), one rounding per call (train_zo.py:350-351)
     for (int k = 0; k < S.n_chain; ++k) {
       const float a = S.chain[k];
@@ -361,14 +405,16 @@ __device__ __forceinline__ void walk_units(const PassParams& P) {
     const int64_t rem = t.numel - e0;
     const int nvalid = rem < EPT ? (int)rem : EPT;
     const bool vec = base_vec && nvalid == EPT;
+    // this thread's slot of the noise cache (unit u, same offset inside the unit as e0)
+    float* zc = c.zcache ? c.zcache + u * ZT_UNIT_ELEMS + (int64_t)(threadIdx.x % kThreadsT) * EPT : nullptr;
     if (kFull) {
-      if (t.dtype == ZT_BF16) run_full<ZT_BF16, EPT>(P, t, e0, nvalid, vec, dev_coef);
-      else if (t.dtype == ZT_F32) run_full<ZT_F32, EPT>(P, t, e0, nvalid, vec, dev_coef);
-      else run_full<ZT_F16, EPT>(P, t, e0, nvalid, vec, dev_coef);
+      if (t.dtype == ZT_BF16) run_full<ZT_BF16, EPT>(P, t, e0, nvalid, vec, dev_coef, zc);
+      else if (t.dtype == ZT_F32) run_full<ZT_F32, EPT>(P, t, e0, nvalid, vec, dev_coef, zc);
+      else run_full<ZT_F16, EPT>(P, t, e0, nvalid, vec, dev_coef, zc);
     } else {
-      if (t.dtype == ZT_BF16) run_chain<ZT_BF16, EPT>(P, t, e0, nvalid, vec);
-      else if (t.dtype == ZT_F32) run_chain<ZT_F32, EPT>(P, t, e0, nvalid, vec);
-      else run_chain<ZT_F16, EPT>(P, t, e0, nvalid, vec);
+      if (t.dtype == ZT_BF16) run_chain<ZT_BF16, EPT>(P, t, e0, nvalid, vec, zc);
+      else if (t.dtype == ZT_F32) run_chain<ZT_F32, EPT>(P, t, e0, nvalid, vec, zc);
+      else run_chain<ZT_F16, EPT>(P, t, e0, nvalid, vec, zc);
     }
   }
 }
@@ -397,6 +443,15 @@ enum FastShape : int {
                     // coefficient, in registers), then the SGD update (+ standard decay):
                     // the last pass of a step, and the sharded replay of every pair
   kFastShapes = 4,
+};
+
+// Noise-cache variants of the specialised shapes (ZT_STREAM_Z_LOAD / _STORE): stream 0
+// reads its field from the cache, and/or the last stream writes its field to it.
+enum FastZ : int {
+  kZNone = 0,
+  kZLoad = 1,       // stream 0 loads
+  kZStore = 2,      // the last stream (stream 0 of kFastChain1, stream 1 otherwise) stores
+  kZLoadStore = 3,  // stream 0 loads, stream 1 stores (in place: load first)
 };
 
 #ifndef ZT_FAST_CHAIN_MINB
@@ -465,8 +520,10 @@ __device__ __forceinline__ void st_words_global(char* p, const uint32_t (&w)[NW]
   for (int i = 0; i < NW / 4; ++i) st_global16(p + 16 * i, w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
 }
 
-template <int DT, int SHAPE>
+template <int DT, int SHAPE, int ZM>
 __device__ __forceinline__ void fast_walk(const PassParams& P) {
+  static_assert(ZM == kZNone || SHAPE != kFastReplay, "the replay shape regenerates every stream");
+  static_assert(ZM != kZLoadStore || SHAPE != kFastChain1, "one stream cannot both load and store");
   using W = Words<DT>;
   const zt_pass_cfg& c = P.cfg;
   const KStream& S0 = P.streams[0];
@@ -561,6 +618,10 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
     // round-to-nearest is the rounding to the parameter dtype after each step.
     uint32_t w[W::kNW], gw[W::kNW];
     ld_words<W::kNW>(st.src + off, w);
+    // noise-cache slot of this thread: unit u, the same 8-element group as e0
+    float* zc = ZM != kZNone ? c.zcache + (size_t)u * ZT_UNIT_ELEMS + threadIdx.x * 8u : nullptr;
+    float zl[8], zs[8];
+    if constexpr ((ZM & kZLoad) != 0) ld_z<8>(zc, zl);
     if (SHAPE == kFastAccum) {
       if (c.ge_load) {
         ld_words<W::kNW>(st.ge + off, gw);
@@ -578,7 +639,9 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
         if (SHAPE == kFastAccum) W::unpack(gw[k], gg);
 #pragma unroll
         for (int i = 0; i < W::kPer; ++i) {
-          const float z = zt::gauss_rk(e0 + (uint32_t)(k * W::kPer + i), rk);
+          const int e = k * W::kPer + i;
+          const float z = (ZM & kZLoad) ? zl[e] : zt::gauss_rk(e0 + (uint32_t)e, rk);
+          if (SHAPE == kFastChain1 && (ZM & kZStore)) zs[e] = z;
           t[i] = __fmaf_rn(z, a0, t[i]);
           if (SHAPE == kFastAccum) gg[i] = __fmaf_rn(z, gcoef, gg[i]);
         }
@@ -593,26 +656,58 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
         float t[W::kPer];
         W::unpack(w[k], t);
 #pragma unroll
-        for (int i = 0; i < W::kPer; ++i) t[i] = __fmaf_rn(zt::gauss_rk(e0 + (uint32_t)(k * W::kPer + i), rk), a1, t[i]);
+        for (int i = 0; i < W::kPer; ++i) {
+          const int e = k * W::kPer + i;
+          const float z = zt::gauss_rk(e0 + (uint32_t)e, rk);
+          if (ZM & kZStore) zs[e] = z;
+          t[i] = __fmaf_rn(z, a1, t[i]);
+        }
         w[k] = W::pack(t);
       }
     }
+    if constexpr ((ZM & kZStore) != 0) st_z<8>(zc, zs);
     if (SHAPE == kFastAccum) st_words_global<W::kNW>(st.ge + off, gw);
     if (c.dst & ZT_BUF_DATA) st_words_global<W::kNW>(st.data + off, w);
     if (c.dst & ZT_BUF_LIVE) st_words_global<W::kNW>(st.live + off, w);
   }
 }
 
-template <int DT, int SHAPE>
+template <int DT, int SHAPE, int ZM>
 __global__ void __launch_bounds__(ZT_UNIT_ELEMS / 8, SHAPE == kFastAccum    ? ZT_FAST_ACCUM_MINB
                                                       : SHAPE == kFastReplay ? ZT_FAST_REPLAY_MINB
                                                                              : ZT_FAST_CHAIN_MINB)
 fast_kernel(const __grid_constant__ PassParams P) {
-  fast_walk<DT, SHAPE>(P);
+  fast_walk<DT, SHAPE, ZM>(P);
 }
 
-// The specialised shape a pass matches, or -1 for the generic kernels.
+constexpr int32_t kZFlags = ZT_STREAM_Z_LOAD | ZT_STREAM_Z_STORE;
+
+// Noise-cache variant of a specialised shape: stream 0 may load, the last stream may
+// store; anything else (-1) goes to the generic kernels, which take any placement.
+int fast_zmode(int shape, const zt_stream* s, int32_t n) {
+  int zm = 0;
+  for (int32_t i = 0; i < n; ++i) {
+    if ((s[i].flags & ZT_STREAM_Z_LOAD) && i != 0) return -1;
+    if ((s[i].flags & ZT_STREAM_Z_STORE) && i != n - 1) return -1;
+  }
+  if (n > 0 && (s[0].flags & ZT_STREAM_Z_LOAD)) zm |= kZLoad;
+  if (n > 0 && (s[n - 1].flags & ZT_STREAM_Z_STORE)) zm |= kZStore;
+  if (shape == kFastReplay && zm != kZNone) return -1;
+  return zm;
+}
+
+// The specialised shape a pass matches (shape + 16 * noise-cache mode), or -1 for the
+// generic kernels.
+int fast_shape_base(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* s, int32_t n);
+
 int fast_shape(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* s, int32_t n) {
+  const int shape = fast_shape_base(plan, cfg, s, n);
+  if (shape < 0) return -1;
+  const int zm = fast_zmode(shape, s, n);
+  return zm < 0 ? -1 : shape + 16 * zm;
+}
+
+int fast_shape_base(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* s, int32_t n) {
   if (!(plan->props & ZT_PLAN_VEC8) || plan->n_units > (int64_t)INT32_MAX - (1 << 24) || cfg->ge_scale_on) return -1;
   if (cfg->update) {
     if (cfg->momentum != ZT_MOM_NONE || cfg->second_moment || (cfg->wd != ZT_WD_NONE && cfg->wd != ZT_WD_STANDARD) ||
@@ -622,14 +717,14 @@ int fast_shape(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* s, 
       if (s[i].flags != ZT_STREAM_GE) return -1;  // a host coefficient, no momentum role
     return kFastReplay;
   }
-  auto plain = [](const zt_stream& x) { return x.n_chain == 1 && x.flags == 0; };
+  auto plain = [](const zt_stream& x) { return x.n_chain == 1 && (x.flags & ~kZFlags) == 0; };
   if (!cfg->ge_load && !cfg->ge_store) {
     if (n == 1 && plain(s[0])) return kFastChain1;
     if (n == 2 && plain(s[0]) && plain(s[1])) return kFastChain2;
     return -1;
   }
   if (cfg->ge_mode == ZT_GE_ACCUM && cfg->ge_store && n == 2 && s[0].n_chain == 1 &&
-      (s[0].flags & ~ZT_STREAM_GE_DEV) == ZT_STREAM_GE && plain(s[1]))
+      (s[0].flags & ~(ZT_STREAM_GE_DEV | kZFlags)) == ZT_STREAM_GE && plain(s[1]))
     return kFastAccum;
   return -1;
 }
@@ -647,24 +742,27 @@ int grid_for(K kernel, int threads, int64_t n_units, std::atomic<int>& occ_cache
 }
 
 std::atomic<int> g_occ_chain{0}, g_occ_full{0};
-std::atomic<int> g_occ_fast[3][kFastShapes];
+std::atomic<int> g_occ_fast[3][kFastShapes][4];
 
-template <int DT>
-void launch_fast(int shape, const PassParams& P, int64_t units, cudaStream_t s) {
+template <int DT, int SHAPE, int ZM>
+void launch_fast_one(const PassParams& P, int64_t units, cudaStream_t s) {
   constexpr int th = ZT_UNIT_ELEMS / 8;
-  switch (shape) {
-    case kFastChain1:
-      fast_kernel<DT, kFastChain1><<<grid_for(fast_kernel<DT, kFastChain1>, th, units, g_occ_fast[DT][kFastChain1]), th, 0, s>>>(P);
-      break;
-    case kFastChain2:
-      fast_kernel<DT, kFastChain2><<<grid_for(fast_kernel<DT, kFastChain2>, th, units, g_occ_fast[DT][kFastChain2]), th, 0, s>>>(P);
-      break;
-    case kFastAccum:
-      fast_kernel<DT, kFastAccum><<<grid_for(fast_kernel<DT, kFastAccum>, th, units, g_occ_fast[DT][kFastAccum]), th, 0, s>>>(P);
-      break;
-    default:
-      fast_kernel<DT, kFastReplay><<<grid_for(fast_kernel<DT, kFastReplay>, th, units, g_occ_fast[DT][kFastReplay]), th, 0, s>>>(P);
-      break;
+  fast_kernel<DT, SHAPE, ZM><<<grid_for(fast_kernel<DT, SHAPE, ZM>, th, units, g_occ_fast[DT][SHAPE][ZM]), th, 0, s>>>(P);
+}
+
+// Returns false for a (shape, noise-cache mode) pair without a specialised kernel.
+template <int DT>
+bool launch_fast(int code, const PassParams& P, int64_t units, cudaStream_t s) {
+  switch (code) {
+    case kFastChain1: launch_fast_one<DT, kFastChain1, kZNone>(P, units, s); return true;
+    case kFastChain1 + 16 * kZLoad: launch_fast_one<DT, kFastChain1, kZLoad>(P, units, s); return true;
+    case kFastChain1 + 16 * kZStore: launch_fast_one<DT, kFastChain1, kZStore>(P, units, s); return true;
+    case kFastChain2: launch_fast_one<DT, kFastChain2, kZNone>(P, units, s); return true;
+    case kFastChain2 + 16 * kZLoadStore: launch_fast_one<DT, kFastChain2, kZLoadStore>(P, units, s); return true;
+    case kFastAccum: launch_fast_one<DT, kFastAccum, kZNone>(P, units, s); return true;
+    case kFastAccum + 16 * kZLoadStore: launch_fast_one<DT, kFastAccum, kZLoadStore>(P, units, s); return true;
+    case kFastReplay: launch_fast_one<DT, kFastReplay, kZNone>(P, units, s); return true;
+    default: return false;
   }
 }
 
@@ -811,8 +909,10 @@ int pass_launch(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* st
   for (int s = 0; s < n_streams; ++s) {
     const zt_stream& S = streams[s];
     if (S.n_chain < 0 || S.n_chain > ZT_MAX_CHAIN) return zt::set_error(ZT_ERR_INVALID, "zt_pass: n_chain outside [0, 3]");
-    if ((S.flags & ~(ZT_STREAM_GE | ZT_STREAM_MOM | ZT_STREAM_GE_DEV)) != 0)
+    if ((S.flags & ~(ZT_STREAM_GE | ZT_STREAM_MOM | ZT_STREAM_GE_DEV | kZFlags)) != 0)
       return zt::set_error(ZT_ERR_INVALID, "zt_pass: bad stream flags");
+    if ((S.flags & kZFlags) == kZFlags)
+      return zt::set_error(ZT_ERR_INVALID, "zt_pass: a stream cannot both load and store the noise cache");
     if ((S.flags & ZT_STREAM_GE_DEV) && (!(S.flags & ZT_STREAM_GE) || !cfg->dev_vals || cfg->ge_mode != ZT_GE_ACCUM))
       return zt::set_error(ZT_ERR_INVALID, "zt_pass: GE_DEV stream needs GE, dev_vals and ge_mode ACCUM");
     if ((S.flags & ZT_STREAM_GE) && cfg->ge_mode == ZT_GE_NONE)
@@ -829,16 +929,30 @@ int pass_launch(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* st
     K.pad[0] = K.pad[1] = 0;
   }
   for (int s = n_streams; s < ZT_MAX_STREAMS; ++s) P.streams[s] = KStream{};
+  {
+    int n_load = 0, n_store = 0, first_store = n_streams, last_load = -1;
+    for (int s = 0; s < n_streams; ++s) {
+      if (streams[s].flags & ZT_STREAM_Z_LOAD) { ++n_load; last_load = s; }
+      if (streams[s].flags & ZT_STREAM_Z_STORE) { ++n_store; if (s < first_store) first_store = s; }
+    }
+    if (n_load > 1 || n_store > 1)
+      return zt::set_error(ZT_ERR_INVALID, "zt_pass: at most one stream may load and one may store the noise cache");
+    if (last_load > first_store)
+      return zt::set_error(ZT_ERR_INVALID, "zt_pass: the noise-cache load must come before the store");
+    if ((n_load || n_store) && (!cfg->zcache || ((uintptr_t)cfg->zcache & 15u) != 0))
+      return zt::set_error(ZT_ERR_INVALID, "zt_pass: noise-cache streams need a 16-byte aligned cfg->zcache");
+    if (!n_load && !n_store) P.cfg.zcache = nullptr;
+  }
   const int shape = fast_shape(plan, cfg, streams, n_streams);
   const int32_t all_dt = plan->props & (ZT_PLAN_ALL_F32 | ZT_PLAN_ALL_BF16 | ZT_PLAN_ALL_F16);
   bool full = cfg->update || cfg->ge_scale_on || cfg->ge_load || cfg->ge_store;
-  for (int s = 0; s < n_streams; ++s) full = full || streams[s].flags != 0;
-  if (shape >= 0 && all_dt == ZT_PLAN_ALL_BF16) {
-    launch_fast<ZT_BF16>(shape, P, ue - ub, zt::as_stream(stream));
-  } else if (shape >= 0 && all_dt == ZT_PLAN_ALL_F32) {
-    launch_fast<ZT_F32>(shape, P, ue - ub, zt::as_stream(stream));
-  } else if (shape >= 0 && all_dt == ZT_PLAN_ALL_F16) {
-    launch_fast<ZT_F16>(shape, P, ue - ub, zt::as_stream(stream));
+  for (int s = 0; s < n_streams; ++s) full = full || (streams[s].flags & ~kZFlags) != 0;
+  cudaStream_t cs = zt::as_stream(stream);
+  bool done = false;
+  if (shape >= 0 && all_dt == ZT_PLAN_ALL_BF16) done = launch_fast<ZT_BF16>(shape, P, ue - ub, cs);
+  else if (shape >= 0 && all_dt == ZT_PLAN_ALL_F32) done = launch_fast<ZT_F32>(shape, P, ue - ub, cs);
+  else if (shape >= 0 && all_dt == ZT_PLAN_ALL_F16) done = launch_fast<ZT_F16>(shape, P, ue - ub, cs);
+  if (done) {
   } else if (full) {
     constexpr int th = ZT_UNIT_ELEMS / kFullEpt;
     full_kernel<<<grid_for(full_kernel, th, ue - ub, g_occ_full), th, 0, zt::as_stream(stream)>>>(P);

@@ -73,6 +73,8 @@ class Stream:
     ge: float | None = None
     mom: float | None = None
     ge_dev: bool = False      # ge coefficient computed on the device from the pass's dev values
+    z_store: bool = False     # also write the regenerated field to the pass's noise cache
+    z_load: bool = False      # read the field from the noise cache instead of regenerating it
 
     def to_c(self) -> L.ZtStream:
         if len(self.chain) > L.ZT_MAX_CHAIN:
@@ -84,7 +86,9 @@ class Stream:
         s.n_chain = len(self.chain)
         s.flags = ((L.ZT_STREAM_GE if (self.ge is not None or self.ge_dev) else 0)
                    | (L.ZT_STREAM_MOM if self.mom is not None else 0)
-                   | (L.ZT_STREAM_GE_DEV if self.ge_dev else 0))
+                   | (L.ZT_STREAM_GE_DEV if self.ge_dev else 0)
+                   | (L.ZT_STREAM_Z_STORE if self.z_store else 0)
+                   | (L.ZT_STREAM_Z_LOAD if self.z_load else 0))
         s.ge_coef = self.ge if self.ge is not None else 0.0
         s.mom_coef = self.mom if self.mom is not None else 0.0
         return s
@@ -120,6 +124,7 @@ class PassCfg:
     dev_tau: float = float("inf")
     unit_begin: int = 0             # work-unit range of the pass (unit_end 0: all units)
     unit_end: int = 0
+    zcache: int = 0                 # device address of the plan's noise cache (n_units x 2048 fp32)
 
     def to_c(self) -> L.ZtPassCfg:
         c = L.ZtPassCfg()
@@ -134,6 +139,7 @@ class PassCfg:
         c.dev_vals = self.dev_vals or None
         c.dev_inv2eps, c.dev_invz, c.dev_tau = self.dev_inv2eps, self.dev_invz, self.dev_tau
         c.unit_begin, c.unit_end = self.unit_begin, self.unit_end
+        c.zcache = self.zcache or None
         return c
 
 
@@ -183,6 +189,11 @@ class ParamTable:
             L.check(lib.zt_plan_init(self._host, n, self.n_params, self.workspace.data_ptr(), nbytes,
                                      ctypes.byref(self.plan), _stream_ptr(self.device)), "zt_plan_init")
         self.numel = int(self.plan.numel_total)
+
+    def noise_cache(self) -> torch.Tensor:
+        """A noise cache for this plan's passes (zt_pass_cfg.zcache): one fp32 per element
+        slot of every work unit, i.e. about 4 bytes per parameter."""
+        return torch.empty(int(self.plan.n_units) * L.ZT_UNIT_ELEMS, dtype=torch.float32, device=self.device)
 
     def _describe(self, params, n_params, indices, live, m, v, anchor, ge=None):
         """Validate the tensors and build the host zt_tensor array."""

@@ -205,6 +205,11 @@ class StepPlanner:
         # the pairs in order on the master.
         self.ge_onthefly = (not self.sharded and cfg.z_batch > 1 and not self.shaping and self.need_ge
                             and cfg.mom.momentum_method != "seed_window")
+        # Noise cache (set by ZOOptimizer): the +eps pass of pair j also writes z_j to an
+        # fp32 buffer, and the pair's -2eps and restore passes read it back instead of
+        # regenerating it (one Philox/Box-Muller evaluation per element and pair instead
+        # of three on one GPU, one instead of two for a rank's own pairs when sharded).
+        self.noise_cache = False
 
     # -- reference helpers (zotitan/train_zo.py:287-293, 427-508) ----------------
     def _draw_seeds(self, n):
@@ -259,22 +264,25 @@ class StepPlanner:
         """+eps z_j; single-GPU mode also restores the previous pair (+eps z_prev) first and,
         when accumulating on the fly, adds prev's grad_est contribution."""
         a = f32(self.cfg.eps)
+        nc = self.noise_cache
         if self.sharded:
-            return PassSpec(PassCfg(src=L.ZT_BUF_DATA, dst=L.ZT_BUF_LIVE), [Stream(self.seeds[j], (a,))])
+            return PassSpec(PassCfg(src=L.ZT_BUF_DATA, dst=L.ZT_BUF_LIVE), [Stream(self.seeds[j], (a,), z_store=nc)])
         if self.ge_onthefly and prev is not None:
             cfg = PassCfg(src=L.ZT_BUF_DATA, dst=L.ZT_BUF_DATA, ge_mode=L.ZT_GE_ACCUM, ge_load=prev > 0,
                           ge_store=True, dev_pair=prev, dev_inv2eps=f32_recip(2 * self.cfg.eps),
                           dev_invz=f32_recip(self.cfg.z_batch),
                           dev_tau=f32(self.tau) if self.clip_in_loop else float("inf"))
-            return PassSpec(cfg, [Stream(self.seeds[prev], (a,), ge_dev=True), Stream(self.seeds[j], (a,))])
-        streams = ([Stream(self.seeds[prev], (a,))] if prev is not None else []) + [Stream(self.seeds[j], (a,))]
+            return PassSpec(cfg, [Stream(self.seeds[prev], (a,), ge_dev=True, z_load=nc),
+                                  Stream(self.seeds[j], (a,), z_store=nc)])
+        streams = (([Stream(self.seeds[prev], (a,), z_load=nc)] if prev is not None else [])
+                   + [Stream(self.seeds[j], (a,), z_store=nc)])
         return PassSpec(PassCfg(src=L.ZT_BUF_DATA, dst=L.ZT_BUF_DATA), streams)
 
     def minus_pass(self, j: int) -> PassSpec:
         """-2eps z_j (train_zo.py:369)."""
         a = f32(-2 * self.cfg.eps)
         buf = L.ZT_BUF_LIVE if self.sharded else L.ZT_BUF_DATA
-        return PassSpec(PassCfg(src=buf, dst=buf), [Stream(self.seeds[j], (a,))])
+        return PassSpec(PassCfg(src=buf, dst=buf), [Stream(self.seeds[j], (a,), z_load=self.noise_cache)])
 
     def finish(self, vals: list[float]) -> tuple[PassSpec, dict]:
         """vals = [v+_0, v-_0, v+_1, v-_1, ...] for all pairs (fp32 values). Returns the
@@ -353,7 +361,8 @@ class StepPlanner:
                     continue                      # already restored and accumulated
             streams.append(Stream(self.seeds[j], chain,
                                   ge_coefs[j] if ge_mode != L.ZT_GE_NONE else None,
-                                  mom_coefs[0][j] if mom_coefs else None))
+                                  mom_coefs[0][j] if mom_coefs else None,
+                                  z_load=self.noise_cache and not self.sharded and j == Z - 1))
         for i in range(1, len(mom_coefs)):
             for s, c in zip(self.seed_buf[i], mom_coefs[i]):
                 streams.append(Stream(s, (), None, c))
@@ -447,10 +456,17 @@ class ZOOptimizer:
     the step's last pass on 1/W of the elements and one in-place all-gather of the
     updated parameters completes them, instead of every rank regenerating every pair's
     noise over all elements. The trainable tensors are then re-homed into one flat
-    buffer (the Parameters keep their identity; ``p.data`` becomes a view)."""
+    buffer (the Parameters keep their identity; ``p.data`` becomes a view).
+    ``noise_cache``: keep each pair's Gaussian field in an fp32 buffer (about 4 bytes per
+    trainable parameter) between its +eps, -2eps and restore passes instead of
+    regenerating it in each. The field is the same either way, so the step's results are
+    bit-identical; the passes become cheaper because regenerating an element's noise
+    (Philox4x32-10, log, cos, sqrt) costs far more than reading 4 bytes from HBM.
+    None (default): on when the cache takes at most a quarter of the device's free
+    memory; False keeps the noise in registers only."""
 
     def __init__(self, named_params: list, cfg: ZOConfig, score_fn, total_steps: int = 0, process_group=None,
-                 sharded: bool | None = None, shard_update: bool = True):
+                 sharded: bool | None = None, shard_update: bool = True, noise_cache: bool | None = None):
         self.named_params = named_params
         self.params = [p.data for _, p in named_params]
         self.cfg = cfg
@@ -517,6 +533,11 @@ class ZOOptimizer:
         else:
             self.master = None
             self.table = ParamTable(self.params, m=self.m, v=self.v, anchor=self.theta_0, ge=self.ge)
+        if noise_cache is None and self.table is not None:
+            free, _ = torch.cuda.mem_get_info(self.table.device)
+            noise_cache = 4 * int(self.table.plan.n_units) * L.ZT_UNIT_ELEMS <= free // 4
+        self.zcache = self.table.noise_cache() if noise_cache and self.table is not None else None
+        pl.noise_cache = self.zcache is not None
         self._metric_keys = None
 
     # properties mirroring the reference's attributes
@@ -535,6 +556,8 @@ class ZOOptimizer:
     def _run(self, spec: PassSpec) -> None:
         if spec.cfg.dev_pair is not None:
             spec.cfg.dev_vals = self.vals_buf.data_ptr() + 8 * spec.cfg.dev_pair
+        if self.zcache is not None and any(s.z_load or s.z_store for s in spec.streams):
+            spec.cfg.zcache = self.zcache.data_ptr()
         if self.table is not None:
             self.table.run(spec.cfg, spec.streams)
 
