@@ -850,7 +850,9 @@ def run_ours(args, rank, local_rank, world):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": (achieved / hbm_peak) if achieved else None, "traffic": traffic,
                      "kernel": kname, "algorithmic_bytes_per_launch": kbytes,
-                     "note": ("instruction-bound: one Philox4x32-10 + logf/cosf evaluation per element (the next "
+                     "note": ("HBM-bound streaming pass (theta + z read, theta written); see profiles/"
+                              if cached and not amean else
+                              "instruction-bound: one Philox4x32-10 + logf/cosf evaluation per element (the next "
                               "pair's field), z read and rewritten through the noise cache; the -2eps pass reads "
                               "z from the cache at perturb_pass_gbs; see profiles/" if cached else
                               "instruction-bound (Philox4x32-10 + logf/cosf per element per noise stream); "
