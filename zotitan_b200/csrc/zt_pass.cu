@@ -696,17 +696,7 @@ int fast_zmode(int shape, const zt_stream* s, int32_t n) {
   return zm;
 }
 
-// The specialised shape a pass matches (shape + 16 * noise-cache mode), or -1 for the
-// generic kernels.
-int fast_shape_base(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* s, int32_t n);
-
-int fast_shape(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* s, int32_t n) {
-  const int shape = fast_shape_base(plan, cfg, s, n);
-  if (shape < 0) return -1;
-  const int zm = fast_zmode(shape, s, n);
-  return zm < 0 ? -1 : shape + 16 * zm;
-}
-
+// The specialised shape a pass matches, ignoring the noise-cache flags, or -1.
 int fast_shape_base(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* s, int32_t n) {
   if (!(plan->props & ZT_PLAN_VEC8) || plan->n_units > (int64_t)INT32_MAX - (1 << 24) || cfg->ge_scale_on) return -1;
   if (cfg->update) {
@@ -727,6 +717,15 @@ int fast_shape_base(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream
       (s[0].flags & ~(ZT_STREAM_GE_DEV | kZFlags)) == ZT_STREAM_GE && plain(s[1]))
     return kFastAccum;
   return -1;
+}
+
+// The specialised kernel a pass takes (shape + 16 * noise-cache mode), or -1 for the
+// generic kernels.
+int fast_shape(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* s, int32_t n) {
+  const int shape = fast_shape_base(plan, cfg, s, n);
+  if (shape < 0) return -1;
+  const int zm = fast_zmode(shape, s, n);
+  return zm < 0 ? -1 : shape + 16 * zm;
 }
 
 // Grid = SMs x resident blocks per SM (occupancy queried once per kernel).
@@ -952,13 +951,12 @@ int pass_launch(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* st
   if (shape >= 0 && all_dt == ZT_PLAN_ALL_BF16) done = launch_fast<ZT_BF16>(shape, P, ue - ub, cs);
   else if (shape >= 0 && all_dt == ZT_PLAN_ALL_F32) done = launch_fast<ZT_F32>(shape, P, ue - ub, cs);
   else if (shape >= 0 && all_dt == ZT_PLAN_ALL_F16) done = launch_fast<ZT_F16>(shape, P, ue - ub, cs);
-  if (done) {
-  } else if (full) {
+  if (!done && full) {  // the generic kernels take every plan and stream combination
     constexpr int th = ZT_UNIT_ELEMS / kFullEpt;
-    full_kernel<<<grid_for(full_kernel, th, ue - ub, g_occ_full), th, 0, zt::as_stream(stream)>>>(P);
-  } else {
+    full_kernel<<<grid_for(full_kernel, th, ue - ub, g_occ_full), th, 0, cs>>>(P);
+  } else if (!done) {
     constexpr int th = ZT_UNIT_ELEMS / kChainEpt;
-    chain_kernel<<<grid_for(chain_kernel, th, ue - ub, g_occ_chain), th, 0, zt::as_stream(stream)>>>(P);
+    chain_kernel<<<grid_for(chain_kernel, th, ue - ub, g_occ_chain), th, 0, cs>>>(P);
   }
   return zt::check_cuda(cudaGetLastError(), "zt_pass launch");
 }
