@@ -50,8 +50,8 @@ def _sharded_worker(rank, world, port, name, out_dir, shard_update=False):
     layout = None
     if shard_update:   # last pass on this rank's unit range, then all-gather the flat master
         from zotitan_b200.flat import FlatLayout
-        layout = FlatLayout([p.size for p in params], world)
-        pl.unit_range = layout.shard_units(rank)
+        layout = FlatLayout([p.size for p in params], world, chunks=3)
+        pl.unit_ranges = layout.shard_ranges(rank)
     ts = [{"data": p, "live": p.copy(), "m": np.zeros_like(p) if pl.needs_m else None,
            "v": np.zeros_like(p) if pl.needs_v else None, "anchor": p.copy() if pl.needs_anchor else None,
            "ge": None, "dtype": dt, "index": i} for i, (p, dt) in enumerate(zip(params, case.dtypes))]
@@ -71,15 +71,16 @@ def _sharded_worker(rank, world, port, name, out_dir, shard_update=False):
         gathered = gather_pair_values(local_t, Z, rank, world).tolist()
         vals = [x for row in gathered for x in row]
         spec, _ = pl.finish(vals)
-        run_pass(ts, len(ts), spec.cfg, spec.streams)
+        for ub, ue in (spec.unit_ranges or [(0, 0)]):   # chunk by chunk, as ZOOptimizer runs it
+            spec.cfg.unit_begin, spec.cfg.unit_end = ub, ue
+            run_pass(ts, len(ts), spec.cfg, spec.streams)
         if layout is not None:
             buf = np.zeros(layout.numel, np.float32)
             for o, p in zip(layout.offsets, params):
                 buf[o:o + p.size] = p.reshape(-1)
-            ub, ue = layout.shard_units(rank)
-            mine = torch.from_numpy(buf[ub * 2048: ue * 2048].copy())
-            full = torch.zeros(layout.numel, dtype=torch.float32)
-            dist.all_gather_into_tensor(full, mine)
+            full = torch.from_numpy(buf)
+            for k in range(layout.chunks):   # in-place all-gather of each chunk
+                dist.all_gather_into_tensor(layout.chunk(full, k), layout.shard_chunk(full, rank, k).clone())
             full = full.numpy()
             for o, p, t in zip(layout.offsets, params, ts):
                 p.reshape(-1)[:] = full[o:o + p.size]

@@ -121,12 +121,13 @@ def test_noise_cache_schedule_contract(name, world):
     that pair's field there (stored by the pair's +eps pass, never overwritten before its
     last use), and the schedule is otherwise unchanged: same parameters and metrics."""
     case = StepCase(_G, name)
-    a0, m0, s0 = run_planner(case, world=world)
-    a1, m1, s1 = run_planner(case, world=world, noise_cache=True)   # asserts the contract
-    for a, b in zip(a0 + s0, a1 + s1):
-        assert np.array_equal(a, b)
-    for x, y in zip(m0, m1):
-        assert x["proj_grad"] == y["proj_grad"]
+    for rank in range(world):   # every rank, including one without pairs when z_batch < world
+        a0, m0, s0 = run_planner(case, world=world, rank=rank)
+        a1, m1, s1 = run_planner(case, world=world, rank=rank, noise_cache=True)   # asserts the contract
+        for a, b in zip(a0 + s0, a1 + s1):
+            assert np.array_equal(a, b)
+        for x, y in zip(m0, m1):
+            assert x["proj_grad"] == y["proj_grad"]
 
 
 def test_noise_cache_contract_violations_detected():

@@ -522,7 +522,7 @@ __device__ __forceinline__ void st_words_global(char* p, const uint32_t (&w)[NW]
 
 template <int DT, int SHAPE, int ZM>
 __device__ __forceinline__ void fast_walk(const PassParams& P) {
-  static_assert(ZM == kZNone || SHAPE != kFastReplay, "the replay shape regenerates every stream");
+  static_assert(ZM == kZNone || SHAPE != kFastReplay, "the replay shape handles its cache loads per stream");
   static_assert(ZM != kZLoadStore || SHAPE != kFastChain1, "one stream cannot both load and store");
   using W = Words<DT>;
   const zt_pass_cfg& c = P.cfg;
@@ -583,18 +583,25 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
       for (int e = 0; e < 8; ++e) ge[e] = 0.0f;
       for (int s = 0; s < P.n_streams; ++s) {
         const KStream& S = P.streams[s];
-        const zt::RoundKeys rk = zt::round_keys(zt::param_key(S.seed, P.n_params, st.index));
         const float c0 = S.chain[0], c1 = S.chain[1], c2 = S.chain[2], gc = S.ge_coef;
         const int nc = S.n_chain;  // uniform: the branches below are taken by every thread
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float z = zt::gauss_rk(e0 + (uint32_t)e, rk);
+        auto apply = [&](int e, float z) {
           float x = th[e];
           if (nc > 0) x = R::round(__fmaf_rn(z, c0, x));
           if (nc > 1) x = R::round(__fmaf_rn(z, c1, x));
           if (nc > 2) x = R::round(__fmaf_rn(z, c2, x));
           th[e] = x;
           ge[e] = R::round(__fmaf_rn(z, gc, ge[e]));  // (train_zo.py:556)
+        };
+        if (S.flags & ZT_STREAM_Z_LOAD) {  // a field this rank cached (its last own pair)
+          float zl[8];
+          ld_z<8>(c.zcache + (size_t)u * ZT_UNIT_ELEMS + threadIdx.x * 8u, zl);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) apply(e, zl[e]);
+        } else {
+          const zt::RoundKeys rk = zt::round_keys(zt::param_key(S.seed, P.n_params, st.index));
+#pragma unroll
+          for (int e = 0; e < 8; ++e) apply(e, zt::gauss_rk(e0 + (uint32_t)e, rk));
         }
       }
       const float nlr = -c.lr;
@@ -685,6 +692,11 @@ constexpr int32_t kZFlags = ZT_STREAM_Z_LOAD | ZT_STREAM_Z_STORE;
 // Noise-cache variant of a specialised shape: stream 0 may load, the last stream may
 // store; anything else (-1) goes to the generic kernels, which take any placement.
 int fast_zmode(int shape, const zt_stream* s, int32_t n) {
+  if (shape == kFastReplay) {  // reads cached fields stream by stream; stores none
+    for (int32_t i = 0; i < n; ++i)
+      if (s[i].flags & ZT_STREAM_Z_STORE) return -1;
+    return kZNone;
+  }
   int zm = 0;
   for (int32_t i = 0; i < n; ++i) {
     if ((s[i].flags & ZT_STREAM_Z_LOAD) && i != 0) return -1;
@@ -692,7 +704,6 @@ int fast_zmode(int shape, const zt_stream* s, int32_t n) {
   }
   if (n > 0 && (s[0].flags & ZT_STREAM_Z_LOAD)) zm |= kZLoad;
   if (n > 0 && (s[n - 1].flags & ZT_STREAM_Z_STORE)) zm |= kZStore;
-  if (shape == kFastReplay && zm != kZNone) return -1;
   return zm;
 }
 
@@ -703,8 +714,8 @@ int fast_shape_base(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream
     if (cfg->momentum != ZT_MOM_NONE || cfg->second_moment || (cfg->wd != ZT_WD_NONE && cfg->wd != ZT_WD_STANDARD) ||
         cfg->ge_mode != ZT_GE_ACCUM || cfg->ge_load || cfg->ge_store || n < 1)
       return -1;
-    for (int32_t i = 0; i < n; ++i)
-      if (s[i].flags != ZT_STREAM_GE) return -1;  // a host coefficient, no momentum role
+    for (int32_t i = 0; i < n; ++i)  // a host coefficient, no momentum role (z may come from the cache)
+      if ((s[i].flags & ~ZT_STREAM_Z_LOAD) != ZT_STREAM_GE) return -1;
     return kFastReplay;
   }
   auto plain = [](const zt_stream& x) { return x.n_chain == 1 && (x.flags & ~kZFlags) == 0; };

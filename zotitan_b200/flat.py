@@ -1,11 +1,12 @@
 """Flat parameter layout for the sharded update.
 
 Tensors of one dtype are laid back to back in one buffer, each padded to a whole
-number of ZT_UNIT_ELEMS-element work units, and the unit count is padded to a
-multiple of the world size. Unit u then covers elements [u*2048, (u+1)*2048) of the
-buffer, and rank r's share of the step's last pass, units
-[r*U/W, (r+1)*U/W), is one contiguous slice: after the pass one in-place all-gather
-of that slice completes every rank's copy.
+number of ZT_UNIT_ELEMS-element work units. The unit count is padded to a multiple of
+world * chunks, and the buffer is cut into `chunks` equal chunks of world * C units:
+in chunk k, rank r owns units [k*W*C + r*C, k*W*C + (r+1)*C). Unit u covers elements
+[u*2048, (u+1)*2048) of the buffer. The step's last pass then runs chunk by chunk on
+each rank's share, and the in-place all-gather of chunk k (contiguous, rank-major) can
+cross NVLink while the pass works on chunk k+1.
 """
 from __future__ import annotations
 
@@ -15,7 +16,7 @@ from . import _lib as L
 
 
 class FlatLayout:
-    def __init__(self, numels: list[int], world: int):
+    def __init__(self, numels: list[int], world: int, chunks: int = 4):
         u = L.ZT_UNIT_ELEMS
         self.offsets = []
         units = 0
@@ -24,16 +25,26 @@ class FlatLayout:
             units += (n + u - 1) // u
         self.units = units
         self.world = world
-        self.padded_units = ((units + world - 1) // world) * world
+        self.chunks = chunks
+        grain = world * chunks
+        self.padded_units = ((units + grain - 1) // grain) * grain
+        self.per = self.padded_units // grain          # units of one rank in one chunk
         self.numel = self.padded_units * u
         self.numels = list(numels)
 
-    def shard_units(self, rank: int) -> tuple[int, int]:
-        per = self.padded_units // self.world
-        return rank * per, (rank + 1) * per
+    def shard_ranges(self, rank: int) -> list[tuple[int, int]]:
+        """This rank's unit ranges, one per chunk, in chunk order."""
+        w, c = self.world, self.per
+        return [(k * w * c + rank * c, k * w * c + (rank + 1) * c) for k in range(self.chunks)]
 
-    def shard_slice(self, flat: torch.Tensor, rank: int) -> torch.Tensor:
-        ub, ue = self.shard_units(rank)
+    def chunk(self, flat: torch.Tensor, k: int) -> torch.Tensor:
+        """Chunk k of a flat buffer (every rank's share of it, rank-major)."""
+        n = self.world * self.per * L.ZT_UNIT_ELEMS
+        return flat[k * n: (k + 1) * n]
+
+    def shard_chunk(self, flat: torch.Tensor, rank: int, k: int) -> torch.Tensor:
+        """This rank's share of chunk k (a slice of chunk(flat, k): in-place all-gather)."""
+        ub, ue = self.shard_ranges(rank)[k]
         return flat[ub * L.ZT_UNIT_ELEMS: ue * L.ZT_UNIT_ELEMS]
 
     def views(self, flat: torch.Tensor, shapes) -> list[torch.Tensor]:

@@ -142,6 +142,7 @@ def f32_recip(x) -> float:
 class PassSpec:
     cfg: PassCfg
     streams: list
+    unit_ranges: list | None = None   # run once per [unit_begin, unit_end) range, in order
 
 
 class StepPlanner:
@@ -174,7 +175,7 @@ class StepPlanner:
         # Sharded update: the step's last pass covers only this rank's unit range of a
         # flat parameter layout, followed by an all-gather of the updated master (set by
         # ZOOptimizer when the layout is in place).
-        self.unit_range: tuple[int, int] | None = None
+        self.unit_ranges: list[tuple[int, int]] | None = None
         self.has_momentum = cfg.mom.momentum_method != "none"
         self._pg_hist = (collections.deque(maxlen=cfg.clip.window)
                          if cfg.clip.strategy != "none" and cfg.clip.clip_pct > 0 else None)
@@ -359,10 +360,13 @@ class StepPlanner:
                 chain = (a_pos,) if j == Z - 1 else ()   # restore of the last pair (:371)
                 if self.ge_onthefly and j < Z - 1:
                     continue                      # already restored and accumulated
+            # the field still in the noise cache: the last pair (one GPU) or this rank's
+            # last own pair (sharded replay)
+            cached = (bool(self.local) and j == self.local[-1]) if self.sharded else j == Z - 1
             streams.append(Stream(self.seeds[j], chain,
                                   ge_coefs[j] if ge_mode != L.ZT_GE_NONE else None,
                                   mom_coefs[0][j] if mom_coefs else None,
-                                  z_load=self.noise_cache and not self.sharded and j == Z - 1))
+                                  z_load=self.noise_cache and cached))
         for i in range(1, len(mom_coefs)):
             for s, c in zip(self.seed_buf[i], mom_coefs[i]):
                 streams.append(Stream(s, (), None, c))
@@ -379,8 +383,8 @@ class StepPlanner:
             wd_code = L.ZT_WD_STANDARD
         elif wd.strategy == "anchored" and self.wd_enabled:
             wd_code = L.ZT_WD_ANCHORED_L1 if wd.penalty == "l1" else L.ZT_WD_ANCHORED_L2
-        if self.sharded and self.unit_range is not None:
-            dst = L.ZT_BUF_DATA                       # this rank's slice of the master only
+        if self.sharded and self.unit_ranges is not None:
+            dst = L.ZT_BUF_DATA                       # this rank's share of the master only
         elif self.sharded:
             dst = L.ZT_BUF_DATA | L.ZT_BUF_LIVE
         else:
@@ -397,8 +401,6 @@ class StepPlanner:
             bc2=f32(1.0 - mc.beta2 ** t), denom_eps=f32(mc.denom_eps),
             update=True, lr=lr32, wd=wd_code, wd_lam=wd_lam, wd_factor=f32(1.0 - wd_lam),
             ge_load=self.ge_onthefly)
-        if self.sharded and self.unit_range is not None:
-            pcfg.unit_begin, pcfg.unit_end = self.unit_range
         metrics = {
             "loss": mean_loss,
             "proj_grad": sum(pg) / Z,
@@ -408,7 +410,8 @@ class StepPlanner:
             "lr": self.lr,
             **({"fit_rms": (sum(s * s for s in pgc) / Z) ** 0.5} if self.shaping else {}),
         }
-        return PassSpec(pcfg, streams), metrics
+        ranges = list(self.unit_ranges) if self.sharded and self.unit_ranges is not None else None
+        return PassSpec(pcfg, streams, ranges), metrics
 
     # -- exact resume: the whole optimizer trajectory is seeds + scalars ---------------
     def state_dict(self) -> dict:
@@ -512,7 +515,7 @@ class ZOOptimizer:
             self.v = flat_view() if pl.needs_v else None
             self.theta_0 = self.layout.views(self.flat_master.clone(), shapes) if pl.needs_anchor else None
             self.table = ParamTable(self.master, live=self.params, m=self.m, v=self.v, anchor=self.theta_0)
-            pl.unit_range = self.layout.shard_units(rank)
+            pl.unit_ranges = self.layout.shard_ranges(rank)
         elif pl.sharded:
             # model reads `live` (the parameters' own storage); `master` stays unperturbed
             self.master = [p.clone() for p in self.params]
@@ -649,12 +652,22 @@ class ZOOptimizer:
         spec, metrics = pl.finish(vals)
         with torch.inference_mode():
             self._lr_finish(spec)
-            self._run(spec)
             if self.layout is not None:
+                # the last pass chunk by chunk on this rank's share; each chunk's in-place
+                # all-gather starts when its pass is done and overlaps the next chunk's pass
                 import torch.distributed as dist
-                dist.all_gather_into_tensor(self.flat_master, self.layout.shard_slice(self.flat_master, self.rank),
-                                            group=self.group)
-                self.flat_live.copy_(self.flat_master)
+                works = []
+                for k, (ub, ue) in enumerate(spec.unit_ranges):
+                    spec.cfg.unit_begin, spec.cfg.unit_end = ub, ue
+                    self._run(spec)
+                    works.append(dist.all_gather_into_tensor(
+                        self.layout.chunk(self.flat_master, k),
+                        self.layout.shard_chunk(self.flat_master, self.rank, k), group=self.group, async_op=True))
+                for k, w in enumerate(works):
+                    w.wait()
+                    self.layout.chunk(self.flat_live, k).copy_(self.layout.chunk(self.flat_master, k))
+            else:
+                self._run(spec)
         metrics.update(metrics_avg)
         return metrics
 
