@@ -131,8 +131,8 @@ def test_uniform_plan_specialised_shapes(K, dt):
     (ZT_PLAN_VEC8) runs the one-stream (+eps, -2eps, live copies), two-stream,
     restore + accumulate + perturb and replay (chains + grad_est + SGD, with and without
     weight decay) passes through kernels specialised for that dtype: every buffer they
-    write is bit-identical to the oracle. The last pass of the on-the-fly schedule (it
-    loads grad_est) takes the generic kernel on the same plan."""
+    write is bit-identical to the oracle, including the last pass of the on-the-fly
+    schedule (grad_est loaded, the last pair's term, SGD)."""
     l = L()
     f = lambda x: float(np.float32(x))  # noqa: E731
     e, m2 = f(1e-3), f(-2e-3)

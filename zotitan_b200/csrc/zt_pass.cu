@@ -440,8 +440,9 @@ enum FastShape : int {
   kFastChain2 = 1,  // two such streams (restore one pair, perturb the next)
   kFastAccum = 2,   // stream 0: +a z and its grad_est term (ACCUM, stored); stream 1: +a z
   kFastReplay = 3,  // any number of streams, each its chain and grad_est term (ACCUM, host
-                    // coefficient, in registers), then the SGD update (+ standard decay):
-                    // the last pass of a step, and the sharded replay of every pair
+                    // coefficient, in registers; grad_est starting from the ge buffers with
+                    // ge_load), then the SGD update (+ standard decay): the last pass of a
+                    // step, and the sharded replay of every pair
   kFastShapes = 4,
 };
 
@@ -579,8 +580,20 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
 #pragma unroll
         for (int i = 0; i < W::kPer; ++i) th[k * W::kPer + i] = t[i];
       }
+      if (c.ge_load) {  // grad_est accumulated by earlier passes (the on-the-fly schedule)
+        uint32_t gw[W::kNW];
+        ld_words<W::kNW>(st.ge + off, gw);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ge[e] = 0.0f;
+        for (int k = 0; k < W::kNW; ++k) {
+          float t[W::kPer];
+          W::unpack(gw[k], t);
+#pragma unroll
+          for (int i = 0; i < W::kPer; ++i) ge[k * W::kPer + i] = t[i];
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ge[e] = 0.0f;
+      }
       for (int s = 0; s < P.n_streams; ++s) {
         const KStream& S = P.streams[s];
         const float c0 = S.chain[0], c1 = S.chain[1], c2 = S.chain[2], gc = S.ge_coef;
@@ -712,7 +725,7 @@ int fast_shape_base(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream
   if (!(plan->props & ZT_PLAN_VEC8) || plan->n_units > (int64_t)INT32_MAX - (1 << 24) || cfg->ge_scale_on) return -1;
   if (cfg->update) {
     if (cfg->momentum != ZT_MOM_NONE || cfg->second_moment || (cfg->wd != ZT_WD_NONE && cfg->wd != ZT_WD_STANDARD) ||
-        cfg->ge_mode != ZT_GE_ACCUM || cfg->ge_load || cfg->ge_store || n < 1)
+        cfg->ge_mode != ZT_GE_ACCUM || cfg->ge_store || n < 1)
       return -1;
     for (int32_t i = 0; i < n; ++i)  // a host coefficient, no momentum role (z may come from the cache)
       if ((s[i].flags & ~ZT_STREAM_Z_LOAD) != ZT_STREAM_GE) return -1;
