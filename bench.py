@@ -448,7 +448,9 @@ def mezo_full_ft_steps(dev, rank: int, world: int, steps: int = 3, warmup: int =
     uniform random tokens (batch of pair j at step t from seed 1000*t + j), next-token
     CE + 1e-4 z-loss through the fused CUDA scorer, eps = 1e-3, lr = 1e-5. One step =
     2 forwards per local pair (transformers' Llama with the fused RMSNorm, RoPE and
-    SwiGLU forwards of zotitan_b200.llama_fused) + the fused perturb/restore/update passes + the all-gather
+    SwiGLU forwards of zotitan_b200.llama_fused; on one GPU `graphed_forwards` times the
+    same steps with the forwards replayed from CUDA graphs by GraphedScore) + the fused
+    perturb/restore/update passes + the all-gather
     of the pair losses (and, with W > 1, the sharded update's parameter all-gather).
     Batches are built on the device before the timed region. Timed with CUDA events
     over `steps` steps, max over ranks; weak in pairs per rank only when W divides 8."""
@@ -456,6 +458,7 @@ def mezo_full_ft_steps(dev, rank: int, world: int, steps: int = 3, warmup: int =
     import torch.distributed as dist
 
     from zotitan_b200.data import synthetic_token_batch
+    from zotitan_b200.graphs import GraphedScore
     from zotitan_b200.objective import SyntheticTokensObjective
     from zotitan_b200.synthetic import LLAMA_1B, build_llama
     from zotitan_b200.train_zo import ZOConfig, ZOOptimizer
@@ -495,11 +498,18 @@ def mezo_full_ft_steps(dev, rank: int, world: int, steps: int = 3, warmup: int =
             ms = float(tt.item())
         return ms, m
 
-    ms, m = timed(opt)
+    ms, m = timed(opt)   # the default path: forwards issued from Python
     cached = opt.zcache is not None
     del opt
     # the same steps with the noise cache set the other way (default: on when it fits)
     ms_nc, _ = timed(ZOOptimizer(named, cfg, objective.score, total_steps=steps + warmup, noise_cache=not cached))
+    graphed = None
+    if world == 1:   # the forwards replayed from CUDA graphs (zotitan_b200.graphs.GraphedScore, opt-in)
+        try:
+            ms_g, _ = timed(ZOOptimizer(named, cfg, GraphedScore(objective.score), total_steps=steps + warmup))
+            graphed = {"value": steps / (ms_g * 1e-3), "ms_per_step": ms_g / steps}
+        except RuntimeError as e:   # reported, not fatal: the headline path is the eager one
+            graphed = {"error": str(e)[:200]}
     n_params = sum(p.numel() for _, p in named)
     del model, named, plan
     torch.cuda.empty_cache()
@@ -509,7 +519,7 @@ def mezo_full_ft_steps(dev, rank: int, world: int, steps: int = 3, warmup: int =
             "tokens_per_step": 2 * pairs * B * S, "params": n_params, "z_loss": 1e-4,
             "scorer": "fused CUDA cross-entropy (zt_xent_rows)", "parallelism": f"pair-sharded x{world}",
             "loss_last_step": m["loss"], "proj_grad_last_step": m["proj_grad"],
-            "noise_cache": cached,
+            "noise_cache": cached, "graphed_forwards": graphed,
             ("no_noise_cache" if cached else "with_noise_cache"): {
                 "value": steps / (ms_nc * 1e-3), "ms_per_step": ms_nc / steps, "cache_bytes": 4 * n_params}}
 

@@ -26,12 +26,30 @@ multiple of 16, per-sequence position ids), or the MLP's activation is not SiLU.
 """
 from __future__ import annotations
 
+import contextlib
 import types
 
 import torch
 import torch.nn as nn
 
 from . import kernels as K
+
+
+_ASSUME_CAUSAL = False
+
+
+@contextlib.contextmanager
+def assume_causal():
+    """Within this context the fused attention forward ignores the attention mask it is
+    given and lets SDPA apply the causal mask itself (`is_causal`). For batches whose
+    sequences have no padding, where transformers' mask is purely causal; used while a
+    forward is captured into a CUDA graph, when transformers materialises that mask."""
+    global _ASSUME_CAUSAL
+    prev, _ASSUME_CAUSAL = _ASSUME_CAUSAL, True
+    try:
+        yield
+    finally:
+        _ASSUME_CAUSAL = prev
 
 
 def _fast(x: torch.Tensor) -> bool:
@@ -67,6 +85,8 @@ def _attention_forward(self, hidden_states, position_embeddings=None, attention_
     v = v.view(bsz, T, -1, hd).transpose(1, 2)
     if past_key_values is not None:
         k, v = past_key_values.update(k, v, self.layer_idx)
+    if _ASSUME_CAUSAL and past_key_values is None:
+        attention_mask = None   # purely causal: SDPA's is_causal (see assume_causal)
     attn = ALL_ATTENTION_FUNCTIONS.get_interface(self.config._attn_implementation, eager_attention_forward)
     out, weights = attn(self, q, k, v, attention_mask, dropout=0.0 if not self.training else self.attention_dropout,
                         scaling=self.scaling, **kwargs)
