@@ -466,6 +466,14 @@ __global__ void __launch_bounds__(256) lora_add_mma_kernel(__nv_bfloat16* __rest
   const int col0 = blockIdx.x * kMmaCols;
   const int nr = (int)((rows - row0) < kMmaRows ? (rows - row0) : kMmaRows);
   const int nc = (n - col0) < kMmaCols ? (n - col0) : kMmaCols;
+  // The block's tile of out, 16 threads per row and 8 columns each (n % 8 == 0: a group
+  // is wholly in or out of range), is read first, so the HBM reads are in flight while
+  // the operands are staged and multiplied.
+  const int cq = (threadIdx.x % 16) * 8, q0 = threadIdx.x / 16;
+  uint4 ov[kMmaRows / 16];
+#pragma unroll
+  for (int j = 0; j < kMmaRows / 16; ++j)
+    if (q0 + 16 * j < nr && cq < nc) ov[j] = *reinterpret_cast<const uint4*>(out + (row0 + q0 + 16 * j) * n + col0 + cq);
   // xa rows (PARTS * R floats, 16-byte aligned) and b rows (R floats) in 16-byte pieces
   for (int i = threadIdx.x; i < kMmaRows * R4; i += 256) {
     const int rr = i / R4, k = (i % R4) * 4;
@@ -532,14 +540,6 @@ __global__ void __launch_bounds__(256) lora_add_mma_kernel(__nv_bfloat16* __rest
         __floats2bfloat162_rn(acc[2] * scale, acc[3] * scale);
   }
   __syncthreads();
-  // 16 threads per row, 8 columns each (n % 8 == 0: a group is wholly in or out of range);
-  // a thread's four rows are all loaded before any is written back, so the four reads
-  // of out are in flight together
-  const int cq = (threadIdx.x % 16) * 8, q0 = threadIdx.x / 16;
-  uint4 ov[kMmaRows / 16];
-#pragma unroll
-  for (int j = 0; j < kMmaRows / 16; ++j)
-    if (q0 + 16 * j < nr && cq < nc) ov[j] = *reinterpret_cast<const uint4*>(out + (row0 + q0 + 16 * j) * n + col0 + cq);
 #pragma unroll
   for (int j = 0; j < kMmaRows / 16; ++j) {
     const int rr = q0 + 16 * j;
