@@ -851,8 +851,8 @@ def run_ours(args, rank, local_rank, world):
         "config": {"workload": "Llama-3.2-1B-shaped parameter set, 64 seeds/step (kernel microbench)",
                    "params": numel, "tensors": n_tensors, "seeds_per_step": args.seeds, "eps": EPS,
                    "passes_per_step": 2 * args.seeds + 1, "parallelism": f"seed-sharded x{world}",
-                   "l2": "inputs (2.47 GB of bf16 parameters) larger than L2",
-                   "noise_cache": cached},
+                   "l2": "inputs (2.47 GB of bf16 parameters) larger than L2"},
+        "noise_cache": cached,
         "perturb_pass_gbs": perturb_gbs, "perturb_pass_ms": pmean, "accum_pass_ms": amean,
         "philox_gelem_per_s": (numel / (amean * 1e-3) / 1e9 if cached and amean else
                                numel / (pmean * 1e-3) / 1e9 if pmean and not cached else None),
