@@ -7,14 +7,16 @@ with ``.step(model, batches) -> dict`` (:242-606) and ``train_zo(...)`` (:609-67
 What changes underneath: the reference materialises fp32 noise for every tensor
 with a Triton kernel and applies it with torch foreach ops (3 passes per pair plus a
 grad_est buffer, momentum replay and the update). Here every pass is one
-``zt_pass`` launch over all trainable tensors that regenerates the noise in
-registers (include/zotitan_b200.h):
+``zt_pass`` launch over all trainable tensors that generates the noise in registers
+(include/zotitan_b200.h); with the noise cache (the default when it fits) a pair's
+field is generated once, by the pass that applies its +eps, kept as fp32, and read back
+by the pair's -2eps and restore passes:
 
   pair j:    [restore of pair j-1 (+eps z_{j-1}), its grad_est term] fused with
              +eps z_j ; score ; -2eps z_j ; score
   step end:  restore of the last pair + the remaining gradient-estimate terms +
              momentum replay + (m, v) update + parameter update + weight decay,
-             one pass; noise is never stored.
+             one pass; no per-tensor z is materialised.
 
 Arithmetic follows the reference's eager op order with the fp32 opmath scalars of
 torch's CUDA kernels (tensor / Python scalar multiplies by the fp32 reciprocal),
