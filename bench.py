@@ -358,7 +358,8 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     from zotitan_b200.synthetic import LLAMA_1B, llama_param_shapes, numel
-    total = numel(llama_param_shapes(LLAMA_1B))
+    shapes = llama_param_shapes(LLAMA_1B)
+    total = numel(shapes)
     vals = []
     for i in range(args.warmup + args.steps):
         r = cpu_sample_step_rate(total, args.seeds, sample_elems=1 << 25, pairs=4)
@@ -369,7 +370,8 @@ def run_reference(args, rank, world):
             "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "Llama-3.2-1B-shaped parameter set, 64 seeds/step (kernel microbench)",
-                       "params": total, "seeds_per_step": args.seeds, "eps": EPS},
+                       "params": total, "tensors": len(shapes), "seeds_per_step": args.seeds, "eps": EPS,
+                       "passes_per_step": 2 * args.seeds + 1},
             "cpu_baseline": {**r, "value": v},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
