@@ -521,10 +521,17 @@ ZT_API int zt_xent_rows(const void* logits, int64_t ld, int64_t rows, int64_t vo
  * no cudaMalloc, cudaFree or other allocating routine.
  *
  * The first call on a device resolves the array's device address (once per device, with
- * that device current); make that first call before any stream capture. Every call
- * copies its table into the same array, on `stream`, before its pass, and the array keeps
- * the last call's table: calls whose work can overlap on the GPU (different streams, or
- * unordered host threads on one device) race on it. Order such calls on one stream. */
+ * that device current); make that first call before any stream capture. The address
+ * belongs to the device's primary context: after cudaDeviceReset do not call this entry
+ * point again in that process. Every call checks all its arguments first (a rejected
+ * call leaves the array as it was), then copies its table into the same array, on
+ * `stream`, before its pass; the array keeps the last call's table, so calls whose work
+ * can overlap on the GPU (different streams, or unordered host threads on one device)
+ * race on it. Order such calls on one stream. The copy goes through a host image owned
+ * by the library, which the CUDA runtime stages before the call returns: the caller's
+ * table, pinned or not, may be changed or freed as soon as the call returns. A stream
+ * that is capturing is refused with ZT_ERR_INVALID (the copy would replay from that
+ * reused host image). */
 ZT_API int zt_pass_static(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_params,
                           const zt_pass_cfg* cfg, const zt_stream* streams, int32_t n_streams, void* stream);
 

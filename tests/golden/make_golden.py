@@ -233,4 +233,7 @@ def main(ref_root: str, skip_config1: bool):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", "--skip-config1" in sys.argv)
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    if len(args) != 1:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/reference [--skip-config1]")
+    main(args[0], "--skip-config1" in sys.argv)

@@ -55,3 +55,23 @@ def test_synthetic_batches_are_seeded():
     it1, it2 = synthetic_token_batches(50, 2, 8, seed=3), synthetic_token_batches(50, 2, 8, seed=3)
     for _ in range(3):
         assert torch.equal(next(it1)["input_ids"], next(it2)["input_ids"])
+
+
+def test_prefetch_loader_keeps_exactly_depth_batches_ahead():
+    import time
+    pulled = []
+
+    def counting():
+        for i in range(10):
+            pulled.append(i)
+            yield {"input_ids": torch.full((1,), i)}
+
+    for depth in (1, 3):
+        pulled.clear()
+        loader = PrefetchLoader(counting(), "cpu", depth=depth)
+        time.sleep(0.2)
+        assert len(pulled) == depth            # fetched ahead, no further
+        next(loader)
+        time.sleep(0.2)
+        assert len(pulled) == depth + 1
+        loader.close()

@@ -65,3 +65,61 @@ def test_static_pass_rejects_too_many_tensors():
     rc = lib.zt_pass_static(arr, n, n, ctypes.byref(cfg), streams, 0, None)
     assert rc == L.ZT_ERR_LIMIT
     assert b"ZT_STATIC_MAX_TENSORS" in lib.zt_last_error()
+
+
+def test_static_pass_allocates_nothing():
+    """After a first call has resolved the array's address, further calls leave the
+    device's free memory exactly where it was: the entry point allocates nothing."""
+    from zotitan_b200 import _lib as L
+    from zotitan_b200 import kernels as K
+    f = lambda x: float(np.float32(x))  # noqa: E731
+    b = make(5)
+    m_b = [torch.zeros_like(t) for t in b]
+    cfg = K.PassCfg(ge_mode=L.ZT_GE_ACCUM, momentum=L.ZT_MOM_STORED_EMA, beta1=f(0.9), one_minus_beta1=f(0.1),
+                    m_scale=f(1 / f(0.1)), update=True, lr=f(1e-2))
+    streams = [K.Stream(21, (), ge=f(0.25)), K.Stream(22, (f(1e-3),), ge=f(-0.5))]
+    K.pass_static(b, cfg, streams, n_params=20, m=m_b)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for i in range(8):
+        K.pass_static(b, cfg, [K.Stream(30 + i, (f(1e-3),), ge=f(0.1))], n_params=20, m=m_b)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+
+
+def test_static_pass_refuses_capture_and_bad_arguments():
+    """A capturing stream is refused (the table copy would replay from a reused host
+    image), a rejected call reports its error, and the next call still runs."""
+    from zotitan_b200 import _lib as L
+    from zotitan_b200 import kernels as K
+    lib = L.load()
+    a, b = make(7), make(7)
+    K.pass_static(b, K.PassCfg(), [K.Stream(1, (1e-3,))], n_params=20)  # resolves the address first
+    desc = K.ParamTable.__new__(K.ParamTable)
+    desc._describe(b, 20, None, None, None, None, None, None)
+    good = K.PassCfg().to_c()
+    streams = K._streams_array([K.Stream(2, (1e-3,))])
+    side = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        graph.capture_begin()
+        try:
+            rc = lib.zt_pass_static(desc._host, len(b), 20, ctypes.byref(good), streams, 1, ctypes.c_void_p(side.cuda_stream))
+        finally:
+            graph.capture_end()
+    assert rc == L.ZT_ERR_INVALID
+    assert b"capturing" in lib.zt_last_error()
+    bad = K.PassCfg().to_c()
+    bad.src = 7
+    rc = lib.zt_pass_static(desc._host, len(b), 20, ctypes.byref(bad), streams, 1, None)
+    assert rc == L.ZT_ERR_INVALID
+    # the rejected calls changed nothing: b still equals a after the same passes
+    table = K.ParamTable(a, n_params=20)
+    table.run(K.PassCfg(), [K.Stream(1, (1e-3,))])
+    for st in ([K.Stream(2, (1e-3,))], [K.Stream(3, (-2e-3,))]):
+        table.run(K.PassCfg(), st)
+        K.pass_static(b, K.PassCfg(), st, n_params=20)
+    torch.cuda.synchronize()
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)

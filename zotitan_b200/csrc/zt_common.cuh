@@ -21,14 +21,33 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 // SM count of the current device (cached per device).
 int sm_count();
 
-// Validate a tensor table and copy it (with its work-unit prefix) into `workspace`;
-// the body of zt_plan_init. sync_copies: wait for the copies before returning.
+// Workspace layout of a plan of n tensors: the descriptor table at offset 0, the
+// work-unit prefix (n + 1 int64) at this 256-byte aligned offset.
+constexpr size_t plan_prefix_offset(int32_t n_tensors) {
+  return (sizeof(zt_tensor) * (size_t)n_tensors + 255) & ~(size_t)255;
+}
+
+// Validate a host tensor table and compute its work-unit prefix (n_tensors + 1 entries)
+// and the plan's fields, with the table and prefix pointers placed in `workspace`;
+// copies nothing.
+int plan_scan(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_params, void* workspace, int64_t* prefix,
+              zt_plan* plan);
+
+// plan_scan, then copy the table and prefix into `workspace` and wait for the copies;
+// the body of zt_plan_init.
 int plan_build(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_params, void* workspace,
-               size_t workspace_bytes, zt_plan* plan, void* stream, bool sync_copies);
+               size_t workspace_bytes, zt_plan* plan, void* stream);
+
+// Every argument check of a pass (plan, configuration, streams, device), without a launch.
+int pass_check(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* streams, int32_t n_streams);
 
 // Validate a pass and launch it; the body of zt_pass.
 int pass_launch(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* streams, int32_t n_streams,
                 void* stream);
+
+// pass_check (launch = false) or pass_launch (launch = true).
+int pass_run(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* streams, int32_t n_streams, void* stream,
+             bool launch);
 
 // --- parameter-dtype rounding ----------------------------------------------------
 template <int DT> struct Dt;

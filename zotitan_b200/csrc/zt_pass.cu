@@ -795,15 +795,13 @@ extern "C" {
 
 size_t zt_plan_workspace_bytes(int32_t n_tensors) {
   if (n_tensors < 0) return 0;
-  const size_t t = sizeof(zt_tensor) * (size_t)n_tensors;
-  const size_t tp = (t + 255) & ~(size_t)255;
-  return tp + sizeof(int64_t) * ((size_t)n_tensors + 1);
+  return zt::plan_prefix_offset(n_tensors) + sizeof(int64_t) * ((size_t)n_tensors + 1);
 }
 
 int zt_plan_init(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_params, void* workspace,
                  size_t workspace_bytes, zt_plan* plan, void* stream) {
   zt::clear_error();
-  return zt::plan_build(host_tensors, n_tensors, n_params, workspace, workspace_bytes, plan, stream, true);
+  return zt::plan_build(host_tensors, n_tensors, n_params, workspace, workspace_bytes, plan, stream);
 }
 
 int zt_pass(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* streams, int32_t n_streams, void* stream) {
@@ -815,15 +813,13 @@ int zt_pass(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* stream
 
 namespace zt {
 
-int plan_build(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_params, void* workspace,
-               size_t workspace_bytes, zt_plan* plan, void* stream, bool sync_copies) {
-  if (!plan || (n_tensors > 0 && (!host_tensors || !workspace)))
+int plan_scan(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_params, void* workspace, int64_t* prefix,
+              zt_plan* plan) {
+  if (!plan || !prefix || (n_tensors > 0 && (!host_tensors || !workspace)))
     return zt::set_error(ZT_ERR_INVALID, "zt_plan_init: null pointer");
   if (n_tensors < 0) return zt::set_error(ZT_ERR_INVALID, "zt_plan_init: n_tensors < 0");
-  if (workspace_bytes < zt_plan_workspace_bytes(n_tensors))
-    return zt::set_error(ZT_ERR_INVALID, "zt_plan_init: workspace too small");
   if (((uintptr_t)workspace & 15) != 0) return zt::set_error(ZT_ERR_INVALID, "zt_plan_init: workspace not 16-byte aligned");
-  std::vector<int64_t> prefix((size_t)n_tensors + 1, 0);
+  prefix[0] = 0;
   int64_t total = 0;
   int32_t buffers = ZT_HAS_LIVE | ZT_HAS_M | ZT_HAS_V | ZT_HAS_ANCHOR | ZT_HAS_GE;
   int32_t props = ZT_PLAN_VEC8 | ZT_PLAN_ALL_F32 | ZT_PLAN_ALL_BF16 | ZT_PLAN_ALL_F16;
@@ -856,22 +852,8 @@ int plan_build(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_para
   int dev = 0;
   if (int rc = zt::check_cuda(cudaGetDevice(&dev), "zt_plan_init: cudaGetDevice")) return rc;
   char* ws = static_cast<char*>(workspace);
-  const size_t tbytes = sizeof(zt_tensor) * (size_t)n_tensors;
-  const size_t off = (tbytes + 255) & ~(size_t)255;
-  cudaStream_t s = zt::as_stream(stream);
-  if (n_tensors > 0) {
-    if (int rc = zt::check_cuda(cudaMemcpyAsync(ws, host_tensors, tbytes, cudaMemcpyHostToDevice, s), "zt_plan_init: copy tensors")) return rc;
-  }
-  if (int rc = zt::check_cuda(cudaMemcpyAsync(ws + off, prefix.data(), sizeof(int64_t) * prefix.size(),
-                                              cudaMemcpyHostToDevice, s), "zt_plan_init: copy prefix")) return rc;
-  // Copies from pageable host memory are staged before cudaMemcpyAsync returns, so the
-  // host arrays may be freed right away; zt_plan_init still waits for the copies so a
-  // plan is complete on the device when it returns.
-  if (sync_copies) {
-    if (int rc = zt::check_cuda(cudaStreamSynchronize(s), "zt_plan_init: synchronize")) return rc;
-  }
   plan->tensors = reinterpret_cast<const zt_tensor*>(ws);
-  plan->unit_prefix = reinterpret_cast<const int64_t*>(ws + off);
+  plan->unit_prefix = reinterpret_cast<const int64_t*>(ws + plan_prefix_offset(n_tensors));
   plan->n_units = prefix[n_tensors];
   plan->numel_total = total;
   plan->n_tensors = n_tensors;
@@ -883,8 +865,39 @@ int plan_build(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_para
   return ZT_OK;
 }
 
+int plan_build(const zt_tensor* host_tensors, int32_t n_tensors, uint32_t n_params, void* workspace,
+               size_t workspace_bytes, zt_plan* plan, void* stream) {
+  if (n_tensors < 0) return zt::set_error(ZT_ERR_INVALID, "zt_plan_init: n_tensors < 0");
+  if (workspace_bytes < zt_plan_workspace_bytes(n_tensors))
+    return zt::set_error(ZT_ERR_INVALID, "zt_plan_init: workspace too small");
+  std::vector<int64_t> prefix((size_t)n_tensors + 1, 0);
+  if (int rc = plan_scan(host_tensors, n_tensors, n_params, workspace, prefix.data(), plan)) return rc;
+  char* ws = static_cast<char*>(workspace);
+  cudaStream_t s = zt::as_stream(stream);
+  if (n_tensors > 0) {
+    if (int rc = zt::check_cuda(cudaMemcpyAsync(ws, host_tensors, sizeof(zt_tensor) * (size_t)n_tensors,
+                                                cudaMemcpyHostToDevice, s), "zt_plan_init: copy tensors")) return rc;
+  }
+  if (int rc = zt::check_cuda(cudaMemcpyAsync(ws + plan_prefix_offset(n_tensors), prefix.data(),
+                                              sizeof(int64_t) * prefix.size(), cudaMemcpyHostToDevice, s),
+                              "zt_plan_init: copy prefix")) return rc;
+  // The caller's table may be pinned (then the copy reads it when the stream gets there)
+  // and the prefix vector dies on return, so the plan is complete on the device, and
+  // both host arrays are free, only once the copies have run.
+  return zt::check_cuda(cudaStreamSynchronize(s), "zt_plan_init: synchronize");
+}
+
+int pass_check(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* streams, int32_t n_streams) {
+  return pass_run(plan, cfg, streams, n_streams, nullptr, false);
+}
+
 int pass_launch(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* streams, int32_t n_streams,
                 void* stream) {
+  return pass_run(plan, cfg, streams, n_streams, stream, true);
+}
+
+int pass_run(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* streams, int32_t n_streams, void* stream,
+             bool launch) {
   if (!plan || !cfg) return zt::set_error(ZT_ERR_INVALID, "zt_pass: null plan or cfg");
   if (n_streams < 0 || (n_streams > 0 && !streams)) return zt::set_error(ZT_ERR_INVALID, "zt_pass: bad stream list");
   if (n_streams > ZT_MAX_STREAMS)
@@ -966,6 +979,7 @@ int pass_launch(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* st
       return zt::set_error(ZT_ERR_INVALID, "zt_pass: noise-cache streams need a 16-byte aligned cfg->zcache");
     if (!n_load && !n_store) P.cfg.zcache = nullptr;
   }
+  if (!launch) return ZT_OK;
   const int shape = fast_shape(plan, cfg, streams, n_streams);
   const int32_t all_dt = plan->props & (ZT_PLAN_ALL_F32 | ZT_PLAN_ALL_BF16 | ZT_PLAN_ALL_F16);
   bool full = cfg->update || cfg->ge_scale_on || cfg->ge_load || cfg->ge_store;
