@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define ZT_ABI_VERSION 7
+#define ZT_ABI_VERSION 8
 
 /* dtypes of parameter tensors */
 #define ZT_F32 0
@@ -151,6 +151,9 @@ ZT_API int zt_plan_init(const zt_tensor* host_tensors, int32_t n_tensors, uint32
 #define ZT_STREAM_Z_LOAD 16  /* z is read from cfg->zcache instead of regenerated; the cache
                                 must hold this stream's field (stored by an earlier pass with
                                 the same seed and plan; the library cannot check this) */
+#define ZT_STREAM_Z_FIELD 32 /* z is read from slot `zslot` of the field store cfg->zfield
+                                instead of regenerated; the store must hold this stream's field
+                                on the pass's unit range (the library cannot check this) */
 
 /* One noise stream: z = the Gaussian field of pair seed `seed`. Streams are applied in
  * array order. For each stream, the n_chain perturbations theta <- theta + chain[c] * z
@@ -162,7 +165,7 @@ typedef struct zt_stream {
   float ge_coef;
   float mom_coef;
   int32_t flags;
-  int32_t reserved;
+  int32_t zslot;   /* ZT_STREAM_Z_FIELD: slot of this stream's field in cfg->zfield, [0, 65535] */
 } zt_stream;
 
 /* gradient-estimate accumulation modes */
@@ -237,6 +240,16 @@ typedef struct zt_pass_cfg {
    * pass may read pair j's field and replace it with pair j+1's in place. NULL when no
    * stream uses it. */
   float* zcache;
+  /* Field store for ZT_STREAM_Z_FIELD streams: fields of the pass's unit range only.
+   * Unit u of the pass (unit_begin <= u < unit_end) of slot s sits at
+   *   zfield[s * zfield_stride + (u - unit_begin) * ZT_UNIT_ELEMS ...]
+   * (fp32, 16-byte aligned, zfield_stride a multiple of 4 and at least the range's
+   * (unit_end - unit_begin) * ZT_UNIT_ELEMS). The seed-sharded step fills it with the
+   * slices of every pair's field that fall on a rank's share of the parameters, pushed
+   * from the ranks' noise caches (zt_copy_async), so its last pass reads every field
+   * instead of regenerating it. NULL when no stream uses it. */
+  const float* zfield;
+  int64_t zfield_stride;
 } zt_pass_cfg;
 
 /* A pass is rejected (ZT_ERR_INVALID) when cfg reads or writes a buffer (live, m, v,
@@ -246,8 +259,9 @@ typedef struct zt_pass_cfg {
  * One fused pass over every element of every tensor of `plan`:
  *   1. theta = src buffer;
  *   2. for each stream in order: regenerate z in registers (or read it from the noise
- *      cache, ZT_STREAM_Z_LOAD), apply its chain to theta, accumulate its ge / momentum
- *      contributions (noise is written to memory only for a ZT_STREAM_Z_STORE stream);
+ *      cache, ZT_STREAM_Z_LOAD, or from the field store, ZT_STREAM_Z_FIELD), apply its
+ *      chain to theta, accumulate its ge / momentum contributions (noise is written to
+ *      memory only for a ZT_STREAM_Z_STORE stream);
  *   3. optional ge scaling, optimizer state (m, v) update and parameter update with
  *      weight decay, in the reference's op order (zotitan/train_zo.py:409-425, 376-407);
  *   4. theta to every buffer in `dst`.
@@ -503,6 +517,31 @@ ZT_API int zt_lora_split(const float* a, void* out, int64_t n, void* stream);
  * reference's Liger fused cross-entropy (zotitan/losses.py:17-52) after the lm_head GEMM. */
 ZT_API int zt_xent_rows(const void* logits, int64_t ld, int64_t rows, int64_t vocab, const int64_t* targets,
                         float* loss, float* lse, int32_t* correct, void* stream);
+
+/* ---- peer mappings for the sharded step's field exchange ------------------------- */
+
+/* The reference runs one process per GPU with no communication (sweeps/runall.py:5), so
+ * these have no counterpart there. In the seed-sharded step (one process per GPU) each
+ * rank pushes the slices of its own pairs' Gaussian fields into the field stores
+ * (zt_pass_cfg.zfield) of the ranks that own those slices, so that the step's last pass
+ * reads every pair's field instead of regenerating it. The stores are the caller's
+ * device allocations (cudaMalloc-backed, e.g. torch's default allocator); these calls
+ * only map them into another process and copy with the copy engines. */
+#define ZT_IPC_HANDLE_BYTES 64
+
+/* handle_out (ZT_IPC_HANDLE_BYTES) names the device allocation that contains `ptr`, and
+ * offset_out is ptr's byte offset from that allocation's start. */
+ZT_API int zt_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out);
+
+/* Map another process's allocation (a zt_ipc_export handle) into the current device's
+ * address space, with peer access enabled; base_out is the allocation's start (add the
+ * exporter's offset). Unmap with zt_ipc_close. */
+ZT_API int zt_ipc_open(const void* handle, void** base_out);
+ZT_API int zt_ipc_close(void* base);
+
+/* cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, stream): device-to-device, either
+ * side may be a peer mapping (zt_ipc_open); runs on the copy engines. */
+ZT_API int zt_copy_async(void* dst, const void* src, size_t bytes, void* stream);
 
 /* ---- the fused pass without a caller-provided workspace -------------------------- */
 

@@ -52,12 +52,32 @@ def check_noise_cache(zcache, streams):
         zcache["seed"] = streams[i].seed
 
 
-def run_pass(tensors, n_params, cfg, streams, noise=ph.randn, dev_values=None, zcache=None):
+def check_field_store(zfield, streams):
+    """The field-store contract of zt_pass (ZT_STREAM_Z_FIELD): a stream reading slot s
+    must find its own pair's field there. ``zfield`` maps slot -> the seed whose field the
+    slot holds (what the pushes of the sharded step put there); a stream may not combine
+    the field store with the noise cache. The interpreter regenerates z, which is what a
+    correct store returns."""
+    for i, s in enumerate(streams):
+        slot = getattr(s, "z_field", None)
+        if slot is None:
+            continue
+        assert not (getattr(s, "z_load", False) or getattr(s, "z_store", False)), \
+            f"stream {i} combines the field store with the noise cache"
+        assert zfield.get(slot) == s.seed, f"field-store slot {slot} holds {zfield.get(slot)}, stream {i} needs {s.seed}"
+
+
+def run_pass(tensors, n_params, cfg, streams, noise=ph.randn, dev_values=None, zcache=None, zfield=None):
     """A unit range (cfg.unit_begin, cfg.unit_end) restricts the pass to those 2048-element
     units of the table (numbered in table order); elements outside are left untouched.
-    ``zcache``: a dict modelling the noise cache, checked with check_noise_cache."""
+    ``zcache``: a dict modelling the noise cache, checked with check_noise_cache;
+    ``zfield``: a dict modelling the field store, checked with check_field_store."""
     if zcache is not None:
         check_noise_cache(zcache, streams)
+    if zfield is not None:
+        check_field_store(zfield, streams)
+    elif any(getattr(s, "z_field", None) is not None for s in streams):
+        raise AssertionError("a stream reads the field store but none was given")
     dev_coef = dev_coefficient(cfg, dev_values) if dev_values is not None else None
     ub, ue = getattr(cfg, "unit_begin", 0), getattr(cfg, "unit_end", 0)
     base = 0

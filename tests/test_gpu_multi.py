@@ -24,7 +24,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, name, out_dir):
+def _worker(rank, world, port, name, out_dir, exchange=True):
     sys.path[:0] = [os.path.dirname(HERE), HERE]
     from datetime import timedelta
 
@@ -46,27 +46,32 @@ def _worker(rank, world, port, name, out_dir):
         step_vals = case.values[2 * Z * s: 2 * Z * (s + 1)]
         for j in range(rank, Z, world):
             vals += step_vals[2 * j: 2 * j + 2]
-    opt = ZOOptimizer(list(zip(case.names, ps)), case.cfg, ReplayScore(vals, ps))
+    opt = ZOOptimizer(list(zip(case.names, ps)), case.cfg, ReplayScore(vals, ps),
+                      field_exchange=None if exchange else False)
     assert opt.planner.sharded
+    assert (opt.exchange is not None) == exchange   # peer stores mapped over CUDA IPC
     for _ in range(case.spec["steps"]):
         opt.step(None, [None] * Z)
     torch.cuda.synchronize()
     np.save(os.path.join(out_dir, f"rank{rank}.npy"), flat([p.detach().float().cpu().numpy() for p in ps]))
     np.save(os.path.join(out_dir, f"master{rank}.npy"), flat([m.float().cpu().numpy() for m in opt.master]))
     dist.barrier()
+    if opt.exchange is not None:
+        opt.exchange.close()
     dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("exchange", [True, False])
 @pytest.mark.parametrize("name", ["mezo_bf16_z3", "seedwin_adam_bf16_z2"])
-def test_two_gpu_sharded_matches_single_gpu(name, tmp_path):
+def test_two_gpu_sharded_matches_single_gpu(name, exchange, tmp_path):
     from helpers import StepCase, step_cases
     from test_gpu_step import run_gpu
     G, _ = step_cases()
     a1, _, _ = run_gpu(StepCase(G, name))
     ctx = mp.get_context("spawn")
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, name, str(tmp_path))) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, name, str(tmp_path), exchange)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:

@@ -32,7 +32,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version_and_key(lib):
-    assert lib.zt_abi_version() == L.ABI_VERSION == 7
+    assert lib.zt_abi_version() == L.ABI_VERSION == 8
     from oracle import philox as ph
     for seed, n, i in [(0, 1, 0), (1234, 39, 7), (2**40 + 3, 146, 145), (2**64 - 1, 448, 3)]:
         assert lib.zt_param_key(seed, n, i) == ph.param_key(seed, n, i) == (seed * n + i) & 0x7FFFFFFF
@@ -42,8 +42,9 @@ def test_struct_layouts_match_header(lib):
     assert ctypes.sizeof(L.ZtTensor) == 64
     assert ctypes.sizeof(L.ZtStream) == 40
     assert ctypes.sizeof(L.ZtPlan) == 56 and L.ZtPlan.props.offset == 48
-    assert ctypes.sizeof(L.ZtPassCfg) == 136 and L.ZtPassCfg.dev_vals.offset == 88 and L.ZtPassCfg.unit_begin.offset == 112
-    assert L.ZtPassCfg.zcache.offset == 128
+    assert ctypes.sizeof(L.ZtPassCfg) == 152 and L.ZtPassCfg.dev_vals.offset == 88 and L.ZtPassCfg.unit_begin.offset == 112
+    assert L.ZtPassCfg.zcache.offset == 128 and L.ZtPassCfg.zfield.offset == 136 and L.ZtPassCfg.zfield_stride.offset == 144
+    assert L.ZtStream.zslot.offset == 36
     assert ctypes.sizeof(L.ZtEggrollArgs) == 112 and L.ZtEggrollArgs.xb_ready.offset == 88
     assert ctypes.sizeof(L.ZtEggrollXbArgs) == 152 and L.ZtEggrollXbArgs.bt.offset == 144
     assert ctypes.sizeof(L.ZtEggrollGatedArgs) == 136 and L.ZtEggrollGatedArgs.x_ext.offset == 112
@@ -58,6 +59,14 @@ def test_struct_layouts_match_header(lib):
 def test_invalid_arguments_are_reported(lib):
     assert lib.zt_randn(1, 0, -1, None, None) == L.ZT_ERR_INVALID
     assert b"negative" in lib.zt_last_error()
+    # peer-mapping entry points check their pointers before any CUDA call
+    h = (ctypes.c_ubyte * L.ZT_IPC_HANDLE_BYTES)()
+    off = ctypes.c_uint64()
+    assert lib.zt_ipc_export(None, h, ctypes.byref(off)) == L.ZT_ERR_INVALID
+    assert lib.zt_ipc_open(None, None) == L.ZT_ERR_INVALID
+    assert lib.zt_ipc_close(None) == L.ZT_ERR_INVALID
+    assert lib.zt_copy_async(None, None, 16, None) == L.ZT_ERR_INVALID
+    assert lib.zt_copy_async(None, None, 0, None) == L.ZT_OK   # nothing to copy
     assert lib.zt_randn(1, 2**31 - 10, 100, None, None) == L.ZT_ERR_LIMIT
     assert lib.zt_randn(1, 0, 0, None, None) == L.ZT_OK          # empty is a no-op
     assert lib.zt_last_error() == b""

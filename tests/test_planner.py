@@ -32,10 +32,11 @@ def make_tensors(params, dtypes, planner, sharded):
     return ts
 
 
-def run_planner(case, world, rank=0, noise_cache=False):
+def run_planner(case, world, rank=0, noise_cache=False, field_slots=0):
     params = case.params()
     pl = StepPlanner(case.cfg, total_steps=case.spec["total_steps"], rank=rank, world=world)
     pl.noise_cache = noise_cache
+    pl.field_slots = field_slots
     zc = {} if noise_cache else None
     ts = make_tensors(params, case.dtypes, pl, world > 1)
     n = len(params)
@@ -45,6 +46,8 @@ def run_planner(case, world, rank=0, noise_cache=False):
         local = pl.start()
         Z = case.cfg.z_batch
         vals = [next(vals_all) for _ in range(2 * Z)]
+        # every rank pushes its own stored pairs: slot j holds pair j's field at the last pass
+        zf = {j: pl.seeds[j] for j in range(min(field_slots, Z))}
         prev = None
         for j in local:
             run_pass(ts, n, *_spec(pl.plus_pass(j, prev)), dev_values=_dev(pl.plus_pass(j, prev), vals), zcache=zc)
@@ -53,7 +56,7 @@ def run_planner(case, world, rank=0, noise_cache=False):
             snaps.append(flat([t["live"] if world > 1 else t["data"] for t in ts]))
             prev = j
         spec, m = pl.finish(vals)
-        run_pass(ts, n, spec.cfg, spec.streams, zcache=zc)
+        run_pass(ts, n, spec.cfg, spec.streams, zcache=zc, zfield=zf)
         afters.append(flat(params))
         if world > 1:
             assert np.array_equal(flat([t["live"] for t in ts]), afters[-1])
@@ -209,3 +212,30 @@ def test_planner_state_dict_roundtrip():
     s1, _ = pl.finish(v)
     s2, _ = pl2.finish(v)
     assert [(s.seed, s.chain, s.ge, s.mom) for s in s1.streams] == [(s.seed, s.chain, s.ge, s.mom) for s in s2.streams]
+
+
+@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("slots", [1, 2, 64])
+@pytest.mark.parametrize("name", ["mezo_bf16_z3", "seedwin_adam_bf16_z2", "ema_adam_f32_z2", "es_rank_f32"])
+def test_field_store_schedule_contract(name, world, slots):
+    """With the field exchange, the last pass reads pairs j < field_slots from slot j of
+    the field store (checked against the slots' seeds) and the other pairs from the noise
+    cache or regenerated; the schedule's results are unchanged."""
+    case = StepCase(_G, name)
+    for rank in range(world):
+        a0, m0, s0 = run_planner(case, world=world, rank=rank, noise_cache=True)
+        a1, m1, s1 = run_planner(case, world=world, rank=rank, noise_cache=True, field_slots=slots)
+        for a, b in zip(a0 + s0, a1 + s1):
+            assert np.array_equal(a, b)
+        for x, y in zip(m0, m1):
+            assert x["proj_grad"] == y["proj_grad"]
+
+
+def test_field_store_contract_violations_detected():
+    from oracle.pass_interp import check_field_store
+    from zotitan_b200.kernels import Stream
+    check_field_store({0: 5, 1: 6}, [Stream(5, (1e-3,), z_field=0), Stream(6, (1e-3,), z_field=1)])
+    with pytest.raises(AssertionError):
+        check_field_store({0: 5, 1: 6}, [Stream(6, (1e-3,), z_field=0)])
+    with pytest.raises(AssertionError):
+        check_field_store({0: 5}, [Stream(5, (1e-3,), z_field=0, z_load=True)])

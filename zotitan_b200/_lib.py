@@ -18,7 +18,7 @@ ZT_MAX_CHAIN = 3
 ZT_MAX_NUMEL = 2**31 - 1
 ZT_UNIT_ELEMS = 2048
 ZT_STREAM_GE, ZT_STREAM_MOM, ZT_STREAM_GE_DEV = 1, 2, 4
-ZT_STREAM_Z_STORE, ZT_STREAM_Z_LOAD = 8, 16
+ZT_STREAM_Z_STORE, ZT_STREAM_Z_LOAD, ZT_STREAM_Z_FIELD = 8, 16, 32
 ZT_GE_NONE, ZT_GE_PRODUCT, ZT_GE_ACCUM = 0, 1, 2
 ZT_MOM_NONE, ZT_MOM_STORED_EMA, ZT_MOM_SEED_WINDOW = 0, 1, 2
 ZT_WD_NONE, ZT_WD_STANDARD, ZT_WD_ANCHORED_L2, ZT_WD_ANCHORED_L1 = 0, 1, 2, 3
@@ -30,11 +30,13 @@ EXPORTS = ("zt_last_error", "zt_abi_version", "zt_param_key", "zt_philox_words",
            "zt_randn_at", "zt_plan_workspace_bytes", "zt_plan_init", "zt_pass", "zt_pass_static",
            "zt_eggroll_linear", "zt_eggroll_take_error", "zt_randn_keys", "zt_eggroll_factors",
            "zt_eggroll_rmsnorm", "zt_eggroll_rope", "zt_eggroll_swiglu", "zt_xent_rows",
-           "zt_eggroll_xb", "zt_eggroll_gated", "zt_eggroll_update_operands", "zt_lora_add", "zt_rmsnorm", "zt_gemm_swiglu", "zt_lora_add3", "zt_lora_split")
+           "zt_eggroll_xb", "zt_eggroll_gated", "zt_eggroll_update_operands", "zt_lora_add", "zt_rmsnorm", "zt_gemm_swiglu", "zt_lora_add3", "zt_lora_split",
+           "zt_ipc_export", "zt_ipc_open", "zt_ipc_close", "zt_copy_async")
 ZT_STATIC_MAX_TENSORS = 1024
 ZT_EGGROLL_MAX_PAIRS = 512
 ZT_EGGROLL_FACTOR_WORK_FLOATS = 64 * 20
-ABI_VERSION = 7
+ABI_VERSION = 8
+ZT_IPC_HANDLE_BYTES = 64
 
 
 class ZtTensor(ctypes.Structure):
@@ -53,7 +55,7 @@ class ZtPlan(ctypes.Structure):
 class ZtStream(ctypes.Structure):
     _fields_ = [("seed", ctypes.c_uint64), ("chain", ctypes.c_float * ZT_MAX_CHAIN), ("n_chain", ctypes.c_int32),
                 ("ge_coef", ctypes.c_float), ("mom_coef", ctypes.c_float), ("flags", ctypes.c_int32),
-                ("reserved", ctypes.c_int32)]
+                ("zslot", ctypes.c_int32)]
 
 
 class ZtPassCfg(ctypes.Structure):
@@ -66,7 +68,8 @@ class ZtPassCfg(ctypes.Structure):
                 ("wd_factor", ctypes.c_float), ("ge_load", ctypes.c_int32), ("ge_store", ctypes.c_int32),
                 ("dev_vals", ctypes.c_void_p), ("dev_inv2eps", ctypes.c_float), ("dev_invz", ctypes.c_float),
                 ("dev_tau", ctypes.c_float), ("reserved", ctypes.c_int32), ("unit_begin", ctypes.c_int64),
-                ("unit_end", ctypes.c_int64), ("zcache", ctypes.c_void_p)]
+                ("unit_end", ctypes.c_int64), ("zcache", ctypes.c_void_p), ("zfield", ctypes.c_void_p),
+                ("zfield_stride", ctypes.c_int64)]
 
 
 class ZtEggrollArgs(ctypes.Structure):
@@ -177,6 +180,14 @@ def load():
     lib.zt_gemm_swiglu.argtypes = [P, P, P, P, I64, I64, I64, P]
     lib.zt_xent_rows.restype = ctypes.c_int
     lib.zt_xent_rows.argtypes = [P, I64, I64, I64, P, P, P, P, P]
+    lib.zt_ipc_export.restype = ctypes.c_int
+    lib.zt_ipc_export.argtypes = [P, P, ctypes.POINTER(U64)]
+    lib.zt_ipc_open.restype = ctypes.c_int
+    lib.zt_ipc_open.argtypes = [P, ctypes.POINTER(P)]
+    lib.zt_ipc_close.restype = ctypes.c_int
+    lib.zt_ipc_close.argtypes = [P]
+    lib.zt_copy_async.restype = ctypes.c_int
+    lib.zt_copy_async.argtypes = [P, P, ctypes.c_size_t, P]
     lib.zt_plan_workspace_bytes.restype = ctypes.c_size_t
     lib.zt_plan_workspace_bytes.argtypes = [I32]
     if lib.zt_abi_version() != ABI_VERSION:

@@ -41,7 +41,7 @@ struct KStream {
   float mom_coef;
   uint8_t n_chain;
   uint8_t flags;
-  uint8_t pad[2];
+  uint16_t zslot;  // ZT_STREAM_Z_FIELD: slot in cfg.zfield
 };
 static_assert(sizeof(KStream) == 32, "KStream layout");
 
@@ -175,9 +175,15 @@ template <int DT, int EPT> struct Io {
 
 // Perturb / restore passes: theta <- round(theta + a*z) for each chained coefficient of
 // each stream (train_zo.py:350-351), nothing else.
+// Field-store slot of stream S for this thread's group: zf_off = (u - unit_begin) *
+// ZT_UNIT_ELEMS + the group's offset inside the unit.
+__device__ __forceinline__ const float* zfield_at(const PassParams& P, const KStream& S, int64_t zf_off) {
+  return P.cfg.zfield + (int64_t)S.zslot * P.cfg.zfield_stride + zf_off;
+}
+
 template <int DT, int EPT>
 __device__ __forceinline__ void run_chain(const PassParams& P, const zt_tensor& t, int64_t e0, int nvalid, bool vec,
-                                          float* zc) {
+                                          float* zc, int64_t zf_off) {
   using R = zt::Dt<DT>;
   using IO = Io<DT, EPT>;
   const zt_pass_cfg& c = P.cfg;
@@ -186,10 +192,12 @@ __device__ __forceinline__ void run_chain(const PassParams& P, const zt_tensor& 
   const uint32_t ctr0 = (uint32_t)e0;
   for (int s = 0; s < P.n_streams; ++s) {
     const KStream& S = P.streams[s];
-    if (S.flags & (ZT_STREAM_Z_LOAD | ZT_STREAM_Z_STORE)) {  // noise cache: z held as an array
+    if (S.flags & (ZT_STREAM_Z_LOAD | ZT_STREAM_Z_STORE | ZT_STREAM_Z_FIELD)) {  // z held as an array
       float z[EPT];
       if (S.flags & ZT_STREAM_Z_LOAD) {
         ld_z<EPT>(zc, z);
+      } else if (S.flags & ZT_STREAM_Z_FIELD) {
+        ld_z<EPT>(zfield_at(P, S, zf_off), z);
       } else {
         const zt::RoundKeys rk = zt::round_keys(zt::param_key(S.seed, P.n_params, (uint32_t)t.index));
 #pragma unroll
@@ -234,7 +242,7 @@ __device__ __forceinline__ void run_chain(const PassParams& P, const zt_tensor& 
 
 template <int DT, int EPT>
 __device__ __forceinline__ void run_full(const PassParams& P, const zt_tensor& t, int64_t e0, int nvalid, bool vec,
-                                         float dev_coef, float* zc) {
+                                         float dev_coef, float* zc, int64_t zf_off) {
   using R = zt::Dt<DT>;
   using IO = Io<DT, EPT>;
   const zt_pass_cfg& c = P.cfg;
@@ -256,6 +264,8 @@ __device__ __forceinline__ void run_full(const PassParams& P, const zt_tensor& t
     float z[EPT];
     if (S.flags & ZT_STREAM_Z_LOAD) {
       ld_z<EPT>(zc, z);
+    } else if (S.flags & ZT_STREAM_Z_FIELD) {
+      ld_z<EPT>(zfield_at(P, S, zf_off), z);
     } else {
       const zt::RoundKeys rk = zt::round_keys(zt::param_key(S.seed, P.n_params, (uint32_t)t.index));
 #pragma unroll
@@ -407,14 +417,16 @@ __device__ __forceinline__ void walk_units(const PassParams& P) {
     const bool vec = base_vec && nvalid == EPT;
     // this thread's slot of the noise cache (unit u, same offset inside the unit as e0)
     float* zc = c.zcache ? c.zcache + u * ZT_UNIT_ELEMS + (int64_t)(threadIdx.x % kThreadsT) * EPT : nullptr;
+    // and of the field store (units counted from the pass's first unit)
+    const int64_t zf = (u - P.unit_begin) * ZT_UNIT_ELEMS + (int64_t)(threadIdx.x % kThreadsT) * EPT;
     if (kFull) {
-      if (t.dtype == ZT_BF16) run_full<ZT_BF16, EPT>(P, t, e0, nvalid, vec, dev_coef, zc);
-      else if (t.dtype == ZT_F32) run_full<ZT_F32, EPT>(P, t, e0, nvalid, vec, dev_coef, zc);
-      else run_full<ZT_F16, EPT>(P, t, e0, nvalid, vec, dev_coef, zc);
+      if (t.dtype == ZT_BF16) run_full<ZT_BF16, EPT>(P, t, e0, nvalid, vec, dev_coef, zc, zf);
+      else if (t.dtype == ZT_F32) run_full<ZT_F32, EPT>(P, t, e0, nvalid, vec, dev_coef, zc, zf);
+      else run_full<ZT_F16, EPT>(P, t, e0, nvalid, vec, dev_coef, zc, zf);
     } else {
-      if (t.dtype == ZT_BF16) run_chain<ZT_BF16, EPT>(P, t, e0, nvalid, vec, zc);
-      else if (t.dtype == ZT_F32) run_chain<ZT_F32, EPT>(P, t, e0, nvalid, vec, zc);
-      else run_chain<ZT_F16, EPT>(P, t, e0, nvalid, vec, zc);
+      if (t.dtype == ZT_BF16) run_chain<ZT_BF16, EPT>(P, t, e0, nvalid, vec, zc, zf);
+      else if (t.dtype == ZT_F32) run_chain<ZT_F32, EPT>(P, t, e0, nvalid, vec, zc, zf);
+      else run_chain<ZT_F16, EPT>(P, t, e0, nvalid, vec, zc, zf);
     }
   }
 }
@@ -611,6 +623,12 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
           ld_z<8>(c.zcache + (size_t)u * ZT_UNIT_ELEMS + threadIdx.x * 8u, zl);
 #pragma unroll
           for (int e = 0; e < 8; ++e) apply(e, zl[e]);
+        } else if (S.flags & ZT_STREAM_Z_FIELD) {  // a field pushed into this rank's store
+          float zl[8];
+          ld_z<8>(c.zfield + (size_t)S.zslot * (size_t)c.zfield_stride +
+                      (size_t)(u - (int32_t)P.unit_begin) * ZT_UNIT_ELEMS + threadIdx.x * 8u, zl);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) apply(e, zl[e]);
         } else {
           const zt::RoundKeys rk = zt::round_keys(zt::param_key(S.seed, P.n_params, st.index));
 #pragma unroll
@@ -701,6 +719,7 @@ fast_kernel(const __grid_constant__ PassParams P) {
 }
 
 constexpr int32_t kZFlags = ZT_STREAM_Z_LOAD | ZT_STREAM_Z_STORE;
+constexpr int32_t kZSrc = ZT_STREAM_Z_LOAD | ZT_STREAM_Z_FIELD;  // where a stream's z may come from
 
 // Noise-cache variant of a specialised shape: stream 0 may load, the last stream may
 // store; anything else (-1) goes to the generic kernels, which take any placement.
@@ -727,8 +746,8 @@ int fast_shape_base(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream
     if (cfg->momentum != ZT_MOM_NONE || cfg->second_moment || (cfg->wd != ZT_WD_NONE && cfg->wd != ZT_WD_STANDARD) ||
         cfg->ge_mode != ZT_GE_ACCUM || cfg->ge_store || n < 1)
       return -1;
-    for (int32_t i = 0; i < n; ++i)  // a host coefficient, no momentum role (z may come from the cache)
-      if ((s[i].flags & ~ZT_STREAM_Z_LOAD) != ZT_STREAM_GE) return -1;
+    for (int32_t i = 0; i < n; ++i)  // a host coefficient, no momentum role (z may come from memory)
+      if ((s[i].flags & ~kZSrc) != ZT_STREAM_GE) return -1;
     return kFastReplay;
   }
   auto plain = [](const zt_stream& x) { return x.n_chain == 1 && (x.flags & ~kZFlags) == 0; };
@@ -945,10 +964,14 @@ int pass_run(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* strea
   for (int s = 0; s < n_streams; ++s) {
     const zt_stream& S = streams[s];
     if (S.n_chain < 0 || S.n_chain > ZT_MAX_CHAIN) return zt::set_error(ZT_ERR_INVALID, "zt_pass: n_chain outside [0, 3]");
-    if ((S.flags & ~(ZT_STREAM_GE | ZT_STREAM_MOM | ZT_STREAM_GE_DEV | kZFlags)) != 0)
+    if ((S.flags & ~(ZT_STREAM_GE | ZT_STREAM_MOM | ZT_STREAM_GE_DEV | kZFlags | ZT_STREAM_Z_FIELD)) != 0)
       return zt::set_error(ZT_ERR_INVALID, "zt_pass: bad stream flags");
     if ((S.flags & kZFlags) == kZFlags)
       return zt::set_error(ZT_ERR_INVALID, "zt_pass: a stream cannot both load and store the noise cache");
+    if ((S.flags & ZT_STREAM_Z_FIELD) && (S.flags & kZFlags))
+      return zt::set_error(ZT_ERR_INVALID, "zt_pass: a field-store stream cannot also use the noise cache");
+    if ((S.flags & ZT_STREAM_Z_FIELD) && (S.zslot < 0 || S.zslot > 65535))
+      return zt::set_error(ZT_ERR_INVALID, "zt_pass: zslot outside [0, 65535]");
     if ((S.flags & ZT_STREAM_GE_DEV) && (!(S.flags & ZT_STREAM_GE) || !cfg->dev_vals || cfg->ge_mode != ZT_GE_ACCUM))
       return zt::set_error(ZT_ERR_INVALID, "zt_pass: GE_DEV stream needs GE, dev_vals and ge_mode ACCUM");
     if ((S.flags & ZT_STREAM_GE) && cfg->ge_mode == ZT_GE_NONE)
@@ -962,7 +985,7 @@ int pass_run(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* strea
     K.mom_coef = S.mom_coef;
     K.n_chain = (uint8_t)S.n_chain;
     K.flags = (uint8_t)S.flags;
-    K.pad[0] = K.pad[1] = 0;
+    K.zslot = (S.flags & ZT_STREAM_Z_FIELD) ? (uint16_t)S.zslot : (uint16_t)0;
   }
   for (int s = n_streams; s < ZT_MAX_STREAMS; ++s) P.streams[s] = KStream{};
   {
@@ -978,6 +1001,18 @@ int pass_run(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* strea
     if ((n_load || n_store) && (!cfg->zcache || ((uintptr_t)cfg->zcache & 15u) != 0))
       return zt::set_error(ZT_ERR_INVALID, "zt_pass: noise-cache streams need a 16-byte aligned cfg->zcache");
     if (!n_load && !n_store) P.cfg.zcache = nullptr;
+    bool field = false;
+    for (int s = 0; s < n_streams; ++s) field = field || (streams[s].flags & ZT_STREAM_Z_FIELD);
+    if (field) {
+      if (!cfg->zfield || ((uintptr_t)cfg->zfield & 15u) != 0)
+        return zt::set_error(ZT_ERR_INVALID, "zt_pass: field-store streams need a 16-byte aligned cfg->zfield");
+      if (cfg->zfield_stride % 4 != 0 || cfg->zfield_stride < (ue - ub) * (int64_t)ZT_UNIT_ELEMS)
+        return zt::set_error(ZT_ERR_INVALID,
+                             "zt_pass: zfield_stride must be a multiple of 4 and cover the pass's unit range");
+    } else {
+      P.cfg.zfield = nullptr;
+      P.cfg.zfield_stride = 0;
+    }
   }
   if (!launch) return ZT_OK;
   const int shape = fast_shape(plan, cfg, streams, n_streams);

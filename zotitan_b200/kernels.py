@@ -75,6 +75,7 @@ class Stream:
     ge_dev: bool = False      # ge coefficient computed on the device from the pass's dev values
     z_store: bool = False     # also write the regenerated field to the pass's noise cache
     z_load: bool = False      # read the field from the noise cache instead of regenerating it
+    z_field: int | None = None  # read the field from this slot of the pass's field store
 
     def to_c(self) -> L.ZtStream:
         if len(self.chain) > L.ZT_MAX_CHAIN:
@@ -88,7 +89,9 @@ class Stream:
                    | (L.ZT_STREAM_MOM if self.mom is not None else 0)
                    | (L.ZT_STREAM_GE_DEV if self.ge_dev else 0)
                    | (L.ZT_STREAM_Z_STORE if self.z_store else 0)
-                   | (L.ZT_STREAM_Z_LOAD if self.z_load else 0))
+                   | (L.ZT_STREAM_Z_LOAD if self.z_load else 0)
+                   | (L.ZT_STREAM_Z_FIELD if self.z_field is not None else 0))
+        s.zslot = self.z_field if self.z_field is not None else 0
         s.ge_coef = self.ge if self.ge is not None else 0.0
         s.mom_coef = self.mom if self.mom is not None else 0.0
         return s
@@ -125,6 +128,8 @@ class PassCfg:
     unit_begin: int = 0             # work-unit range of the pass (unit_end 0: all units)
     unit_end: int = 0
     zcache: int = 0                 # device address of the plan's noise cache (n_units x 2048 fp32)
+    zfield: int = 0                 # device address of the field store of the pass's unit range
+    zfield_stride: int = 0          # fp32 elements between two slots of the field store
 
     def to_c(self) -> L.ZtPassCfg:
         c = L.ZtPassCfg()
@@ -140,6 +145,8 @@ class PassCfg:
         c.dev_inv2eps, c.dev_invz, c.dev_tau = self.dev_inv2eps, self.dev_invz, self.dev_tau
         c.unit_begin, c.unit_end = self.unit_begin, self.unit_end
         c.zcache = self.zcache or None
+        c.zfield = self.zfield or None
+        c.zfield_stride = self.zfield_stride
         return c
 
 

@@ -178,6 +178,9 @@ class StepPlanner:
         # flat parameter layout, followed by an all-gather of the updated master (set by
         # ZOOptimizer when the layout is in place).
         self.unit_ranges: list[tuple[int, int]] | None = None
+        # Field exchange (sharded update): pairs j < field_slots have their field pushed into
+        # every rank's field store, and the last pass reads it from there (slot j).
+        self.field_slots = 0
         self.has_momentum = cfg.mom.momentum_method != "none"
         self._pg_hist = (collections.deque(maxlen=cfg.clip.window)
                          if cfg.clip.strategy != "none" and cfg.clip.clip_pct > 0 else None)
@@ -363,12 +366,14 @@ class StepPlanner:
                 if self.ge_onthefly and j < Z - 1:
                     continue                      # already restored and accumulated
             # the field still in the noise cache: the last pair (one GPU) or this rank's
-            # last own pair (sharded replay)
+            # last own pair (sharded replay); or pushed into the field store (slot j)
+            field = self.sharded and j < self.field_slots
             cached = (bool(self.local) and j == self.local[-1]) if self.sharded else j == Z - 1
             streams.append(Stream(self.seeds[j], chain,
                                   ge_coefs[j] if ge_mode != L.ZT_GE_NONE else None,
                                   mom_coefs[0][j] if mom_coefs else None,
-                                  z_load=self.noise_cache and cached))
+                                  z_load=self.noise_cache and cached and not field,
+                                  z_field=j if field else None))
         for i in range(1, len(mom_coefs)):
             for s, c in zip(self.seed_buf[i], mom_coefs[i]):
                 streams.append(Stream(s, (), None, c))
@@ -468,10 +473,19 @@ class ZOOptimizer:
     bit-identical; the passes become cheaper because regenerating an element's noise
     (Philox4x32-10, log, cos, sqrt) costs far more than reading 4 bytes from HBM.
     None (default): on when the cache takes at most a quarter of the device's free
-    memory; False keeps the noise in registers only."""
+    memory; False keeps the noise in registers only.
+    ``field_exchange`` (sharded update with the noise cache): each rank pushes the slices
+    of its own pairs' fields into the field stores of the ranks that own those slices
+    (copy engines over NVLink, overlapping the next pair's passes), and the last pass
+    reads every stored field instead of regenerating it (zotitan_b200.exchange). The
+    results are bit-identical either way. None (default): on with more than one rank,
+    storing as many pairs as fit in half of the free device memory; a float sets that
+    fraction and an int (not a bool) the number of stored pairs; True also runs it on a
+    one-rank group; False regenerates every field."""
 
     def __init__(self, named_params: list, cfg: ZOConfig, score_fn, total_steps: int = 0, process_group=None,
-                 sharded: bool | None = None, shard_update: bool = True, noise_cache: bool | None = None):
+                 sharded: bool | None = None, shard_update: bool = True, noise_cache: bool | None = None,
+                 field_exchange: bool | float | None = None):
         self.named_params = named_params
         self.params = [p.data for _, p in named_params]
         self.cfg = cfg
@@ -543,6 +557,22 @@ class ZOOptimizer:
             noise_cache = 4 * int(self.table.plan.n_units) * L.ZT_UNIT_ELEMS <= free // 4
         self.zcache = self.table.noise_cache() if noise_cache and self.table is not None else None
         pl.noise_cache = self.zcache is not None
+        self._zc = self.zcache                  # the noise cache the next pass uses
+        self.exchange = None
+        if (self.layout is not None and self.zcache is not None and field_exchange is not False
+                and (world > 1 or field_exchange is not None)):
+            from .exchange import FieldExchange, slot_bytes
+            # two caches alternate between a rank's pairs, so a pair's pushes overlap the
+            # next pair's passes
+            self.zcaches = [self.zcache, self.table.noise_cache()]
+            if type(field_exchange) is int:
+                budget = field_exchange * slot_bytes(self.layout)
+            else:
+                frac = field_exchange if isinstance(field_exchange, float) else 0.5
+                budget = int(frac * torch.cuda.mem_get_info(dev)[0])
+            self.exchange = FieldExchange(self.layout, int(self.table.plan.n_units), rank, world, cfg.z_batch, dev,
+                                          budget, group=process_group)
+            pl.field_slots = self.exchange.n_slots
         self._metric_keys = None
 
     # properties mirroring the reference's attributes
@@ -561,8 +591,8 @@ class ZOOptimizer:
     def _run(self, spec: PassSpec) -> None:
         if spec.cfg.dev_pair is not None:
             spec.cfg.dev_vals = self.vals_buf.data_ptr() + 8 * spec.cfg.dev_pair
-        if self.zcache is not None and any(s.z_load or s.z_store for s in spec.streams):
-            spec.cfg.zcache = self.zcache.data_ptr()
+        if self._zc is not None and any(s.z_load or s.z_store for s in spec.streams):
+            spec.cfg.zcache = self._zc.data_ptr()
         if self.table is not None:
             self.table.run(spec.cfg, spec.streams)
 
@@ -627,10 +657,16 @@ class ZOOptimizer:
         vals_t, metric_dicts = [], []
         prev = None
         eps = self.cfg.eps
+        ex = self.exchange
         with torch.inference_mode():
-            for j in local:
+            for k, j in enumerate(local):
                 z = self._lowrank_z(pl.seeds[j]) if self.lr_idx else None
+                if ex is not None:
+                    self._zc = self.zcaches[k % 2]
+                    ex.before_cache_write(self._zc)
                 self._run(pl.plus_pass(j, prev))
+                if ex is not None:
+                    ex.push(j, self._zc)
                 self._lr_apply(z, eps)
                 vp, mp = self._acquire(model, batches[j])
                 self._run(pl.minus_pass(j))
@@ -646,6 +682,8 @@ class ZOOptimizer:
                     self.vals_buf[2 * j + 1].copy_(vn)
                 vals_t += [vp, vn]
                 metric_dicts += [mp, mn]
+        if ex is not None:
+            ex.finish_pushes()    # every push lands before the all-gather that ends the pair loop
         if pl.sharded:
             vals, metrics_avg = self._gather(vals_t, metric_dicts, local)
         else:
@@ -661,6 +699,8 @@ class ZOOptimizer:
                 works = []
                 for k, (ub, ue) in enumerate(spec.unit_ranges):
                     spec.cfg.unit_begin, spec.cfg.unit_end = ub, ue
+                    if ex is not None:
+                        spec.cfg.zfield, spec.cfg.zfield_stride = ex.chunk_field(k)
                     self._run(spec)
                     works.append(dist.all_gather_into_tensor(
                         self.layout.chunk(self.flat_master, k),
