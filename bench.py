@@ -44,7 +44,12 @@ def parse():
     ap.add_argument("--no-eggroll", action="store_true", help="skip the EGGROLL population measurement")
     ap.add_argument("--no-mezo", action="store_true", help="skip the MeZO full fine-tune step measurement")
     ap.add_argument("--no-lora", action="store_true", help="skip the MeZO-Adam LoRA step measurement")
-    ap.add_argument("--profile-case", choices=["chain", "full", "replay", "chain-cached", "full-cached", "eggroll", "eggroll-gated", "eggroll-forward",
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's own step on the GPU (baseline/reference_steps.py)")
+    ap.add_argument("--field-exchange", type=float, default=0.8,
+                    help="sharded runs: fraction of free device memory for the field stores (0: regenerate)")
+    ap.add_argument("--profile-case", choices=["chain", "full", "replay", "chain-cached", "full-cached", "plus-cached",
+                                               "replay-field", "eggroll", "eggroll-gated", "eggroll-forward",
                                                "mezo-step", "lora-step"],
                     default=None,
                     help="small case for ncu: one bf16 tensor of 2^28 elements, 3 launches of the "
@@ -230,6 +235,21 @@ def profile_case(kind: str):
         # repeated launches read back the field the previous launch stored: the values
         # differ from a real schedule's, the work per element is the same
         streams = [K.Stream(4, (f(1e-3),), ge_dev=True, z_load=True), K.Stream(5, (f(1e-3),), z_store=True)]
+    elif kind == "plus-cached":   # the sharded +eps pass: live = master + eps z, z written to the cache
+        live = torch.empty_like(p)
+        tab = K.ParamTable([p], live=[live])
+        zc = tab.noise_cache()
+        cfg = K.PassCfg(src=L.ZT_BUF_DATA, dst=L.ZT_BUF_LIVE, zcache=zc.data_ptr())
+        streams = [K.Stream(5, (f(1e-3),), z_store=True)]
+    elif kind == "replay-field":   # the sharded last pass, 16 pairs' fields read from a field store
+        n = 1 << 25
+        p = p[:n]
+        tab = K.ParamTable([p])
+        units = int(tab.plan.n_units)
+        store = torch.randn(16 * units * 2048, device="cuda")
+        cfg = K.PassCfg(ge_mode=L.ZT_GE_ACCUM, update=True, lr=f(1e-5), zfield=store.data_ptr(),
+                        zfield_stride=units * 2048)
+        streams = [K.Stream(100 + j, (f(1e-3), f(-2e-3), f(1e-3)), ge=f(0.01 * (j - 8)), z_field=j) for j in range(16)]
     elif kind == "replay":   # the sharded step's last pass: 16 pairs' chains + grad_est + SGD
         tab = K.ParamTable([p])
         cfg = K.PassCfg(ge_mode=L.ZT_GE_ACCUM, update=True, lr=f(1e-5))
@@ -306,73 +326,153 @@ class ClockSampler:
 
 # ── CPU baseline: the oracle port on host cores ───────────────────────────────────────
 
-def cpu_sample_step_rate(total_numel: int, n_seeds: int, sample_elems: int = 1 << 26, pairs: int = 16):
-    """Time the reference's per-pair algorithm (materialise z, three perturb ops, one
-    grad_est accumulation, zotitan/train_zo.py:534-556) on `sample_elems` bf16 elements
-    for `pairs` pairs plus the update, with one thread per core (ctypes releases the GIL),
-    and extrapolate to steps/s of the full workload."""
-    from concurrent.futures import ThreadPoolExecutor
+def workload_config(world: int, seeds: int, numel: int, n_tensors: int) -> dict:
+    """The `config` of the microbench line, the same in both arms."""
+    return {"workload": "Llama-3.2-1B-shaped parameter set, 64 seeds/step (kernel microbench)",
+            "params": numel, "tensors": n_tensors, "seeds_per_step": seeds, "eps": EPS,
+            "parallelism": f"seed-sharded x{world}", "l2": "inputs (2.47 GB of bf16 parameters) larger than L2"}
 
-    from oracle import philox as ph
-    cores = os.cpu_count() or 1
-    chunk = (sample_elems + cores - 1) // cores
-    rng = np.random.default_rng(0)
-    th = ph.rounded(ph.BF16, (rng.standard_normal(sample_elems) * 0.02).astype(np.float32))
-    ge = np.zeros_like(th)
-    lib = ph.lib()
-    a_p, a_m = float(np.float32(EPS)), float(np.float32(-2 * EPS))
 
-    def pair_chunk(args):
+class PortStep:
+    """The reference's per-pair algorithm (materialise z, three perturb ops, one grad_est
+    accumulation, zotitan/train_zo.py:534-556; the update, :376-407) in the C oracle, over
+    the FULL parameter set (every element of the 1.236e9), one thread per host core
+    (ctypes releases the GIL). theta and grad_est are fp32 carriers of bf16 values; z is
+    generated block by block per thread. A step of 64 pairs is 64 pair passes and the
+    update, so a pair and the update are timed and only the pair count is extrapolated."""
+
+    BLOCK = 1 << 20
+
+    def __init__(self, total_numel: int, n_tensors: int):
+        from concurrent.futures import ThreadPoolExecutor
+
+        from oracle import philox as ph
+        self.ph, self.lib = ph, ph.lib()
+        self.n, self.n_tensors = total_numel, n_tensors
+        self.cores = os.cpu_count() or 1
+        self.th = np.full(total_numel, 2.0 ** -7, dtype=np.float32)    # bf16-exact values
+        self.ge = np.zeros(total_numel, dtype=np.float32)
+        chunk = (total_numel + self.cores - 1) // self.cores
+        self.spans = [(i * chunk, min(total_numel, (i + 1) * chunk)) for i in range(self.cores)
+                      if i * chunk < total_numel]
+        self.pool = ThreadPoolExecutor(self.cores)
+        self.a_p, self.a_m = float(np.float32(EPS)), float(np.float32(-2 * EPS))
+
+    def _pair_span(self, args):
         key, lo, hi, c = args
-        n = hi - lo
-        z = np.empty(n, np.float32)
-        lib.zo_randn(key, lo, n, ph._p(z))
-        t, g = th[lo:hi], ge[lo:hi]
-        for a in (a_p, a_m, a_p):
-            lib.zo_add_scaled(ph.BF16, ph._p(t), ph._p(z), a, n)
-        lib.zo_add_scaled(ph.BF16, ph._p(g), ph._p(z), c, n)
+        ph, lib = self.ph, self.lib
+        z = np.empty(self.BLOCK, np.float32)
+        for b in range(lo, hi, self.BLOCK):
+            n = min(self.BLOCK, hi - b)
+            lib.zo_randn(key, b, n, ph._p(z))
+            t, g = self.th[b:b + n], self.ge[b:b + n]
+            for a in (self.a_p, self.a_m, self.a_p):
+                lib.zo_add_scaled(ph.BF16, ph._p(t), ph._p(z), a, n)
+            lib.zo_add_scaled(ph.BF16, ph._p(g), ph._p(z), c, n)
 
-    def update_chunk(args):
+    def _update_span(self, args):
         lo, hi = args
-        lib.zo_add_scaled(ph.BF16, ph._p(th[lo:hi]), ph._p(ge[lo:hi]), -float(np.float32(LR)), hi - lo)
+        ph = self.ph
+        self.lib.zo_add_scaled(ph.BF16, ph._p(self.th[lo:hi]), ph._p(self.ge[lo:hi]), -float(np.float32(LR)), hi - lo)
 
-    spans = [(i * chunk, min(sample_elems, (i + 1) * chunk)) for i in range(cores) if i * chunk < sample_elems]
-    with ThreadPoolExecutor(cores) as ex:
+    def pair(self, j: int) -> float:
         t0 = time.perf_counter()
-        for j in range(pairs):
-            list(ex.map(pair_chunk, [(ph.param_key(j, 146, 0), lo, hi, 0.01) for lo, hi in spans]))
-        t1 = time.perf_counter()
-        list(ex.map(update_chunk, spans))
-        t2 = time.perf_counter()
-    per_pair_elem = (t1 - t0) / (pairs * sample_elems)
-    per_update_elem = (t2 - t1) / sample_elems
-    step_s = total_numel * (n_seeds * per_pair_elem + per_update_elem)
-    return {"value": 1.0 / step_s, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{pairs} pairs + update over {sample_elems} bf16 elements (C oracle, {cores} threads), "
-                      f"extrapolated to {n_seeds} seeds x {total_numel} elements; measured {t2 - t0:.2f} s"}
+        key = self.ph.param_key(j, self.n_tensors, 0)
+        list(self.pool.map(self._pair_span, [(key, lo, hi, 0.01) for lo, hi in self.spans]))
+        return time.perf_counter() - t0
+
+    def update(self) -> float:
+        t0 = time.perf_counter()
+        list(self.pool.map(self._update_span, self.spans))
+        return time.perf_counter() - t0
+
+    def close(self):
+        self.pool.shutdown()
+        self.th = self.ge = None
+
+
+def cpu_port_baseline(total_numel: int, n_tensors: int, n_seeds: int) -> dict:
+    """One pair and the update over the full parameter set; steps/s = 1 / (seeds x pair + update)."""
+    port = PortStep(total_numel, n_tensors)
+    t_pair = port.pair(0)
+    t_upd = port.update()
+    port.close()
+    return {"value": 1.0 / (n_seeds * t_pair + t_upd), "unit": UNIT, "cores": port.cores, "kind": "port",
+            "sample": f"one pair (z materialised, +eps, -2eps, +eps, grad_est) and the update over all "
+                      f"{total_numel} elements in the C oracle with {port.cores} threads: {t_pair:.2f} s + "
+                      f"{t_upd:.2f} s; the step's {n_seeds} pairs extrapolated from the one"}
+
+
+def reference_config1_subprocess():
+    """Start the reference's own config-1 CPU step (baseline/reference_steps.py) in the
+    background; returns a collector. It runs on its own host threads with CUDA hidden."""
+    script = os.path.join(HERE, "baseline", "reference_steps.py")
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", REF_CPU_THREADS="4", OMP_NUM_THREADS="4")
+    try:
+        proc = subprocess.Popen([sys.executable, script, "cpu-config1"], stdout=subprocess.PIPE,
+                                stderr=subprocess.PIPE, text=True, env=env)
+    except OSError as e:
+        return lambda: {"unavailable": f"could not start: {e}"}
+
+    def collect(timeout_s: float = 300.0) -> dict:
+        try:
+            out, err = proc.communicate(timeout=timeout_s)
+        except subprocess.TimeoutExpired:
+            proc.kill()
+            return {"unavailable": f"did not finish within {timeout_s:.0f} s"}
+        lines = [x for x in out.strip().splitlines() if x.startswith("{")]
+        if proc.returncode != 0 or not lines:
+            return {"unavailable": (err.strip().splitlines() or ["no output"])[-1][:300]}
+        return json.loads(lines[-1])
+    return collect
+
+
+def reference_gpu_microbench(seeds: int) -> dict:
+    """The reference's own ZOOptimizer.step on this GPU over the same parameter set, seeds
+    and pair values (baseline/reference_steps.py gpu-microbench), in a separate process."""
+    script = os.path.join(HERE, "baseline", "reference_steps.py")
+    try:
+        r = subprocess.run([sys.executable, script, "gpu-microbench", "--seeds", str(seeds), "--steps", "2",
+                            "--warmup", "1"], capture_output=True, text=True, timeout=600)
+    except (OSError, subprocess.TimeoutExpired) as e:
+        return {"unavailable": str(e)[:300]}
+    lines = [x for x in r.stdout.strip().splitlines() if x.startswith("{")]
+    if r.returncode != 0 or not lines:
+        return {"unavailable": (r.stderr.strip().splitlines() or ["no output"])[-1][:300]}
+    return json.loads(lines[-1])
 
 
 # ── reference arm ───────────────────────────────────────────────────────────────────
 
 def run_reference(args, rank, world):
+    """The reference arm: the oracle port of the reference's CPU algorithm on the host
+    cores (the reference is Python; nothing of it compiles to a native library). Each
+    timed step is one pair over the full parameter set; the update is timed once in the
+    warm-up; value = 1 / (seeds x mean pair time + update time)."""
     if rank != 0:
         return
     from zotitan_b200.synthetic import LLAMA_1B, llama_param_shapes, numel
     shapes = llama_param_shapes(LLAMA_1B)
     total = numel(shapes)
-    vals = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_sample_step_rate(total, args.seeds, sample_elems=1 << 25, pairs=4)
-        if i >= args.warmup:
-            vals.append(r["value"])
-    v = statistics.median(vals)
+    port = PortStep(total, len(shapes))
+    t_upd = port.update()
+    for j in range(args.warmup):
+        port.pair(j)
+    w0 = time.perf_counter()
+    pairs = [port.pair(args.warmup + j) for j in range(args.steps)]
+    wall = time.perf_counter() - w0
+    port.close()
+    t_pair = statistics.mean(pairs)
+    v = 1.0 / (args.seeds * t_pair + t_upd)
+    sample = (f"each timed step: one pair (z materialised, +eps, -2eps, +eps, grad_est) over all {total} "
+              f"elements in the C oracle with {port.cores} threads, mean {t_pair:.2f} s; update {t_upd:.2f} s "
+              f"(timed once); value extrapolates the pair count to {args.seeds}")
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "strong",
+            "warmup": args.warmup, "ms_per_step": 1000.0 * t_pair, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "Llama-3.2-1B-shaped parameter set, 64 seeds/step (kernel microbench)",
-                       "params": total, "tensors": len(shapes), "seeds_per_step": args.seeds, "eps": EPS,
-                       "passes_per_step": 2 * args.seeds + 1},
-            "cpu_baseline": {**r, "value": v},
+            "config": workload_config(world, args.seeds, total, len(shapes)),
+            "timed_region_s": wall, "full_step_s": args.seeds * t_pair + t_upd,
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": port.cores, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -501,6 +601,7 @@ def mezo_full_ft_steps(dev, rank: int, world: int, steps: int = 3, warmup: int =
 
     ms, m = timed(opt)   # the default path: forwards issued from Python
     cached = opt.zcache is not None
+    opt.close()
     del opt
     # the same steps with the noise cache set the other way (default: on when it fits)
     ms_nc, _ = timed(ZOOptimizer(named, cfg, objective.score, total_steps=steps + warmup, noise_cache=not cached))
@@ -518,7 +619,7 @@ def mezo_full_ft_steps(dev, rank: int, world: int, steps: int = 3, warmup: int =
             "unit": "ZO steps/s", "ms_per_step": ms / steps, "steps": steps, "warmup": warmup,
             "pairs_per_step": pairs, "forwards_per_step": 2 * pairs, "batch": B, "seq_len": S,
             "tokens_per_step": 2 * pairs * B * S, "params": n_params, "z_loss": 1e-4,
-            "scorer": "fused CUDA cross-entropy (zt_xent_rows)", "parallelism": f"pair-sharded x{world}",
+            "scorer": "fused linear cross-entropy (zt_linear_xent: lm_head GEMM + CE statistics in one kernel)", "parallelism": f"pair-sharded x{world}",
             "loss_last_step": m["loss"], "proj_grad_last_step": m["proj_grad"],
             "noise_cache": cached, "graphed_forwards": graphed,
             ("no_noise_cache" if cached else "with_noise_cache"): {
@@ -594,103 +695,215 @@ def mezo_adam_lora_steps(dev, rank: int, world: int, steps: int = 3, warmup: int
 
 # ── our arm ─────────────────────────────────────────────────────────────────────────
 
-def pass_bytes(noise_cache: bool) -> dict:
-    """Algorithmic bytes per bf16 element of the microbench's passes. Without the noise
-    cache: -2eps pass theta read + written (4), restore/accumulate/perturb pass theta and
-    grad_est read + written (8). With it, z (fp32) is read by the -2eps pass (+4), read
-    and rewritten by the restore/accumulate/perturb pass (+8), written by the first +eps
-    pass (4 + 4)."""
-    return ({"perturb": 8, "accum": 16, "plus": 8} if noise_cache else {"perturb": 4, "accum": 8, "plus": 4})
+class PassTimer:
+    """CUDA events on the launching stream around every fused pass of the timed steps,
+    grouped by kind, with each launch's algorithmic bytes (bf16 parameters):
+      plus    +eps pass (one stream storing its field, or regenerating it): theta read and
+              written (the master read and the live copy written when sharded), + 4 B of z
+              per element written to the noise cache;
+      perturb -2eps pass: theta read and written, + 4 B of z read from the cache;
+      accum   restore of pair j (z_j from the cache) + its grad_est term + perturb of pair
+              j+1 (z_{j+1} regenerated and cached): theta and grad_est read and written,
+              z read and written (16 B per element; 8 without the cache);
+      replay  the step's last pass (on this rank's share, chunk by chunk, when sharded):
+              theta read and written, + 4 B per element for every field read from memory
+              (noise cache or field store)."""
+
+    KINDS = ("plus", "perturb", "accum", "replay")
+
+    def __init__(self, opt, esz: int = 2):
+        import torch
+        self.torch = torch
+        self.opt, self.esz = opt, esz
+        self.events = {k: [] for k in self.KINDS}
+        self.on, self.launches = False, 0
+        layout = opt.layout
+        self.n_units = int(opt.table.plan.n_units)
+        self.numel = opt.table.numel
+        # elements per unit range: tensors are unit-aligned back to back
+        sizes = [p.numel() for p in opt.table.params]
+        self.unit_elems = np.zeros(self.n_units, dtype=np.int64)
+        u = 0
+        for n in sizes:
+            k = (n + 2047) // 2048
+            self.unit_elems[u:u + k] = 2048
+            if n % 2048:
+                self.unit_elems[u + k - 1] = n % 2048
+            u += k
+        self.cum = np.concatenate([[0], np.cumsum(self.unit_elems)])
+        self.layout = layout
+        self._orig = opt.table.run
+        opt.table.run = self.run
+
+    @staticmethod
+    def kind(cfg, streams) -> str:
+        if cfg.update:
+            return "replay"
+        if any(s.ge_dev for s in streams):
+            return "accum"
+        if len(streams) == 1 and streams[0].chain and streams[0].chain[0] < 0:
+            return "perturb"
+        return "plus"
+
+    def launch_bytes(self, cfg, streams) -> tuple[int, int]:
+        ub, ue = cfg.unit_begin, cfg.unit_end
+        ue = self.n_units if ue <= 0 or ue > self.n_units else ue
+        elems = int(self.cum[ue] - self.cum[ub])
+        dst = bin(cfg.dst).count("1")
+        per = self.esz * (1 + dst + int(cfg.ge_load) + int(cfg.ge_store))
+        per += 4 * sum(1 for st in streams if st.z_load or st.z_store or st.z_field is not None)
+        return elems, elems * per
+
+    def run(self, cfg, streams):
+        if not self.on:
+            return self._orig(cfg, streams)
+        self.launches += 1
+        k = self.kind(cfg, streams)
+        elems, nbytes = self.launch_bytes(cfg, streams)
+        a = self.torch.cuda.Event(enable_timing=True)
+        b = self.torch.cuda.Event(enable_timing=True)
+        a.record()
+        self._orig(cfg, streams)
+        b.record()
+        self.events[k].append((a, b, elems, nbytes))
+
+    def summary(self, steps: int) -> dict:
+        out = {}
+        for k, evs in self.events.items():
+            if not evs:
+                continue
+            ms = [a.elapsed_time(b) for a, b, _, _ in evs]
+            nbytes = [x for _, _, _, x in evs]
+            elems = [e for _, _, e, _ in evs]
+            out[k] = {"launches_per_step": len(evs) / steps, "ms_per_launch": float(np.mean(ms)),
+                      "ms_per_step": float(np.sum(ms)) / steps,
+                      "bytes_per_launch": float(np.mean(nbytes)), "elems_per_launch": float(np.mean(elems)),
+                      "gbs": float(np.sum(nbytes)) / (float(np.sum(ms)) * 1e-3) / 1e9,
+                      "g_elem_per_s": float(np.sum(elems)) / (float(np.sum(ms)) * 1e-3) / 1e9}
+        return out
+
+
+def global_pair_score(vals, planner, seeds: int):
+    """Synthetic pair values indexed by the global pair: the k-th score call of a step on
+    this rank belongs to its (k // 2)-th own pair, sign k % 2. Every rank count then scores
+    pair j with the same two values, so the runs are comparable across N."""
+    from zotitan_b200.objective import Score
+    state = {"k": 0}
+
+    def score(model, batch):
+        local = planner.local
+        k = state["k"]
+        state["k"] = (k + 1) % (2 * len(local))
+        j = local[k // 2]
+        return Score(vals[2 * j + (k % 2)], {})
+    return score
+
+
+def param_digest(tensors):
+    """Per-tensor int64 sum of the bf16 bit patterns (as int16): equal digests on every
+    rank (and at every GPU count, the schedules being bit-identical) mean equal parameters
+    up to a collision of the sums."""
+    import torch
+    return torch.stack([t.detach().reshape(-1).view(torch.int16).sum(dtype=torch.int64) for t in tensors])
+
+
+def replicas_identical(digest, world: int):
+    import torch.distributed as dist
+    if world == 1:
+        return True
+    allv = [digest.clone() for _ in range(world)]
+    dist.all_gather(allv, digest)
+    return all(bool((x == allv[0]).all()) for x in allv)
 
 
 def microbench_variant(args, named, cfg, vals_dev, dev, world, barrier, noise_cache: bool):
     """The kernel microbench again with the noise cache set the other way (noise_cache=False:
     every pass regenerates its fields in registers, three noise evaluations per element and
     pair; True: one). Same seeds, values and steps as the headline run; per-launch CUDA
-    events for the -2eps, the restore / grad_est / next-perturb and the first +eps passes."""
+    events by pass kind."""
     import torch
     import torch.distributed as dist
 
-    from zotitan_b200.objective import Score
     from zotitan_b200.train_zo import ZOOptimizer
 
-    class Vals:
-        def __init__(self):
-            self.k = 0
-
-        def __call__(self, model, batch):
-            i = self.k % (2 * args.seeds)
-            self.k += 1
-            return Score(vals_dev[i], {})
-
-    opt = ZOOptimizer(named, cfg, Vals(), noise_cache=noise_cache)
+    opt = ZOOptimizer(named, cfg, None, noise_cache=noise_cache)
+    opt.score_fn = global_pair_score(vals_dev, opt.planner, args.seeds)
     rng = np.random.default_rng(12345)
     opt.planner._draw_seeds = lambda n: [int(x) for x in rng.integers(0, 2**64 - 1, n, dtype=np.uint64)]
-    events, on = {"perturb": [], "accum": [], "plus": []}, [False]
-    orig_run = opt.table.run
-
-    def run(cfg_, streams):
-        kind = None
-        if on[0]:
-            if len(streams) == 1 and streams[0].chain and streams[0].chain[0] < 0:
-                kind = "perturb"
-            elif any(s.ge_dev for s in streams):
-                kind = "accum"
-            elif len(streams) == 1 and streams[0].chain and streams[0].chain[0] > 0:
-                kind = "plus"
-        if kind:
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-        orig_run(cfg_, streams)
-        if kind:
-            b.record()
-            events[kind].append((a, b))
-    opt.table.run = run
+    timer = PassTimer(opt)
     batches = [None] * args.seeds
     for _ in range(args.warmup):
         opt.step(None, batches)
     barrier()
-    on[0] = True
+    timer.on = True
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(args.steps):
         opt.step(None, batches)
     t1.record()
     barrier()
-    on[0] = False
+    timer.on = False
     ms = t0.elapsed_time(t1)
-    mean = {k: float(np.mean([a.elapsed_time(b) for a, b in v])) if v else 0.0 for k, v in events.items()}
     if world > 1:
-        t = torch.tensor([ms, mean["perturb"], mean["accum"], mean["plus"]], device=dev)
+        t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, mean["perturb"], mean["accum"], mean["plus"] = t.tolist()
-    numel = opt.table.numel
+        ms = t.item()
+    passes = timer.summary(args.steps)
     cache_bytes = opt.zcache.numel() * 4 if opt.zcache is not None else 0
-    del opt
+    opt.close()
+    del opt, timer
     torch.cuda.empty_cache()
-    b = pass_bytes(noise_cache)
-    gbs = lambda nbytes, t: nbytes / (t * 1e-3) / 1e9 if t else None  # noqa: E731
     return {"value": args.steps / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms / args.steps,
-            "noise_cache": noise_cache, "cache_bytes": cache_bytes,
-            "perturb_pass_ms": mean["perturb"], "perturb_pass_gbs": gbs(b["perturb"] * numel, mean["perturb"]),
-            "accum_pass_ms": mean["accum"], "accum_pass_gbs": gbs(b["accum"] * numel, mean["accum"]),
-            "plus_pass_ms": mean["plus"], "plus_pass_gbs": gbs(b["plus"] * numel, mean["plus"]),
-            "philox_gelem_per_s": numel / (mean["accum"] * 1e-3) / 1e9 if mean["accum"] else None,
-            "bytes_per_element": b}
+            "noise_cache": noise_cache, "cache_bytes": cache_bytes, "passes": passes}
+
+
+def roofline_of(passes: dict, peaks: dict, clk: dict, world: int, traffic_db: dict) -> dict:
+    """Roofline of the kind with the largest time per step (the dominant kernel)."""
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    kind = max(passes, key=lambda k: passes[k]["ms_per_step"])
+    p = passes[kind]
+    achieved = p["bytes_per_launch"] / (p["ms_per_launch"] * 1e-3) / 1e9
+    entry = traffic_db.get(kind, {})
+    traffic = entry.get("dram_bytes_per_elem")
+    line = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+            "traffic": traffic * p["elems_per_launch"] if traffic else None,
+            "kernel": entry.get("kernel", kind), "kind": kind,
+            "algorithmic_bytes_per_launch": p["bytes_per_launch"],
+            "share_of_step": p["ms_per_step"] / sum(x["ms_per_step"] for x in passes.values()),
+            "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in peaks else "fallback 6650 GB/s"}
+    wi = entry.get("warp_inst_per_elem")
+    sm = clk.get("sm_mhz") or peaks.get("sm_max_mhz", 1965.0)
+    if wi:
+        issue = p["elems_per_launch"] * wi / (p["ms_per_launch"] * 1e-3)
+        line["issue"] = {"achieved_warp_inst_per_s": issue, "peak": 4 * 148 * sm * 1e6,
+                         "frac": issue / (4 * 148 * sm * 1e6), "warp_inst_per_elem": wi,
+                         "note": "4 warp-instructions per clock per SM x 148 SMs x the median sampled SM clock; "
+                                 "instructions per element from ncu (profiles/pass_kernel_traffic.json)"}
+    if entry.get("note"):
+        line["note"] = entry["note"]
+    return line
+
+
+def traffic_key(kind: str, cached: bool, exchange: bool) -> str:
+    if kind == "replay" and exchange:
+        return "replay+field"
+    return kind + ("+cache" if cached else "")
 
 
 def run_ours(args, rank, local_rank, world):
+    import hashlib
+
     import torch
     import torch.distributed as dist
 
-    from zotitan_b200 import kernels as K
-    from zotitan_b200.objective import Score
-    from zotitan_b200.synthetic import LLAMA_1B, llama_param_shapes, make_params
+    from zotitan_b200.synthetic import LLAMA_1B, llama_param_shapes, make_params, numel as count
     from zotitan_b200.train_zo import ZOConfig, ZOOptimizer
 
-    cpu_line = None
+    shapes = llama_param_shapes(LLAMA_1B)
+    cpu_line, ref_c1 = None, None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu_line = cpu_sample_step_rate(1_235_814_400, args.seeds)   # before any CUDA work
+        cpu_line = cpu_port_baseline(count(shapes), len(shapes), args.seeds)   # before any CUDA work
+        ref_c1 = reference_config1_subprocess()     # the reference's own CPU step, in the background
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -698,63 +911,27 @@ def run_ours(args, rank, local_rank, world):
         from zotitan_b200.distributed import init_process_group_from_env
         init_process_group_from_env("nccl", timeout_s=300)
 
-    shapes = llama_param_shapes(LLAMA_1B)
     named = make_params(shapes, torch.bfloat16, dev, seed=0)
     numel = sum(p.numel() for _, p in named)
     n_tensors = len(named)
     cfg = ZOConfig()
     cfg.eps, cfg.z_batch, cfg.base.lr = EPS, args.seeds, LR
 
-    # synthetic pair values: fixed device scalars (no forward in this microbench)
+    # synthetic pair values (no forward in this microbench), indexed by global pair
     g = torch.Generator().manual_seed(1)
     vals_host = (2.0 + 0.01 * torch.randn(2 * args.seeds, generator=g)).float()
     vals_dev = vals_host.to(dev)
     vals_pinned = vals_host.pin_memory()
 
-    class Score_:
-        def __init__(self, from_host):
-            self.k = 0
-            self.from_host = from_host
+    class HostVals:   # e2e: each value arrives from pinned host memory
+        def __getitem__(self, i):
+            return vals_pinned[i:i + 1].to(dev, non_blocking=True)[0]
 
-        def __call__(self, model, batch):
-            i = self.k % (2 * args.seeds)
-            self.k += 1
-            if self.from_host:   # e2e: the value arrives from pinned host memory
-                v = vals_pinned[i:i + 1].to(dev, non_blocking=True)[0]
-            else:
-                v = vals_dev[i]
-            return Score(v, {})
-
-    score = Score_(False)
-    opt = ZOOptimizer(named, cfg, score)
+    opt = ZOOptimizer(named, cfg, None, field_exchange=args.field_exchange or False)
+    opt.score_fn = global_pair_score(vals_dev, opt.planner, args.seeds)
     rng = np.random.default_rng(12345)   # seeded uint64 seed stream, identical on every rank
     opt.planner._draw_seeds = lambda n: [int(x) for x in rng.integers(0, 2**64 - 1, n, dtype=np.uint64)]
-
-    # Per-launch CUDA events on the launching (current) stream for the two pass kinds:
-    #  - "perturb": the -2eps pass, one noise stream, read + write of theta (4 B/element bf16);
-    #  - "accum": restore of pair j-1 + its grad_est term + perturb of pair j, two noise
-    #    streams, theta and grad_est read + written (8 B/element) - the dominant kernel.
-    events, counter = {"perturb": [], "accum": []}, {"launches": 0, "on": False}
-    orig_run = opt.table.run
-
-    def run(cfg_, streams):
-        if counter["on"]:
-            counter["launches"] += 1
-        kind = None
-        if counter["on"]:
-            if len(streams) == 1 and streams[0].chain and streams[0].chain[0] < 0:
-                kind = "perturb"
-            elif any(s.ge_dev for s in streams):
-                kind = "accum"
-        if kind:
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-        orig_run(cfg_, streams)
-        if kind:
-            b.record()
-            events[kind].append((a, b))
-    opt.table.run = run
-
+    timer = PassTimer(opt)
     batches = [None] * args.seeds
 
     def barrier():
@@ -768,22 +945,21 @@ def run_ours(args, rank, local_rank, world):
     clocks = ClockSampler(gpu_uuid)
     barrier()
     clocks.start()
-    counter["on"] = True
+    timer.on = True
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(args.steps):
         opt.step(None, batches)
     t1.record()
     barrier()
-    counter["on"] = False
+    timer.on = False
     clk = clocks.stop()
     ms = t0.elapsed_time(t1)
-    pert_ms = [a.elapsed_time(b) for a, b in events["perturb"]]
-    acc_ms = [a.elapsed_time(b) for a, b in events["accum"]]
-    launches = counter["launches"]
+    passes = timer.summary(args.steps)
+    launches = timer.launches
 
-    # e2e: same steps through the public API with every pair value copied from pinned host memory
-    score.from_host = True
+    # e2e: the same steps through the public API with every pair value copied from pinned host memory
+    opt.score_fn = global_pair_score(HostVals(), opt.planner, args.seeds)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -795,14 +971,23 @@ def run_ours(args, rank, local_rank, world):
     wall_e2e = time.perf_counter() - w0
     e2e_ms = e0.elapsed_time(e1)
 
-    pmean = float(np.mean(pert_ms)) if pert_ms else 0.0
-    amean = float(np.mean(acc_ms)) if acc_ms else 0.0
+    digest = param_digest([p for _, p in named])
+    same = replicas_identical(digest, world)
+    pdig = hashlib.sha256(digest.cpu().numpy().tobytes()).hexdigest()[:16]
     if world > 1:
-        t = torch.tensor([ms, e2e_ms, pmean, amean], device=dev)
+        t = torch.tensor([ms, e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms, pmean, amean = t.tolist()
+        ms, e2e_ms = t.tolist()
+        # the dominant kind is the one with the largest max-over-ranks time per step
+        for k in sorted(passes):
+            t = torch.tensor([passes[k]["ms_per_step"], passes[k]["ms_per_launch"]], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            passes[k]["ms_per_step"], passes[k]["ms_per_launch"] = t.tolist()
     cached = opt.zcache is not None
-    del opt
+    exchange = {"pairs_stored": opt.exchange.n_slots, "store_bytes": opt.exchange.store.numel() * 4} \
+        if opt.exchange is not None else None
+    opt.close()
+    del opt, timer
     torch.cuda.empty_cache()
     # the other schedule: every field regenerated in registers (or cached, if the default was off)
     alt = microbench_variant(args, named, cfg, vals_dev, dev, world, barrier, noise_cache=not cached)
@@ -816,68 +1001,48 @@ def run_ours(args, rank, local_rank, world):
         if world > 1:
             dist.destroy_process_group()
         return
+    torch.cuda.empty_cache()
+    ref_gpu = reference_gpu_microbench(args.seeds) if world == 1 and not args.no_reference_gpu else None
 
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(HERE, "MEASURED_PEAKS.json")))
     except (OSError, ValueError):
         pass
-    hbm_peak = peaks.get("hbm_gbs", 6650.0)
-    pb = pass_bytes(cached)
-    perturb_bytes = pb["perturb"] * numel
-    accum_bytes = pb["accum"] * numel
-    perturb_gbs = perturb_bytes / (pmean * 1e-3) / 1e9 if pmean else None
-    if amean:   # single-GPU schedule: the restore/accumulate/perturb pass dominates
-        achieved, kbytes = accum_bytes / (amean * 1e-3) / 1e9, accum_bytes
-        kname = ("fast_kernel<bf16, kFastAccum, kZLoadStore>: restore (z read from the noise cache) + grad_est "
-                 "accumulation + perturb (z regenerated and cached)" if cached else
-                 "fast_kernel<bf16, kFastAccum>: restore + grad_est accumulation + perturb (2 noise streams)")
-        tkey = "accum_pass_cached" if cached else "accum_pass"
-    else:       # sharded schedule: the +eps / -2eps passes on the live copy dominate
-        achieved, kbytes = perturb_gbs, perturb_bytes
-        kname = ("fast_kernel<bf16, kFastChain1, kZLoad>: -2eps perturb pass (z read from the noise cache)" if cached
-                 else "fast_kernel<bf16, kFastChain1>: -2eps perturb pass (1 noise stream)")
-        tkey = "perturb_pass_cached" if cached else "perturb_pass"
-    traffic = None
-    prof = os.path.join(HERE, "profiles", "pass_kernel_traffic.json")
-    if os.path.exists(prof):
-        try:
-            traffic = json.load(open(prof)).get(tkey, {}).get("dram_bytes_per_launch")
-        except (ValueError, AttributeError):
-            traffic = None
+    traffic_db = {}
+    try:
+        db = json.load(open(os.path.join(HERE, "profiles", "pass_kernel_traffic.json"))).get("kinds", {})
+        for k in PassTimer.KINDS:
+            key = traffic_key(k, cached, exchange is not None)
+            if key in db:
+                traffic_db[k] = db[key]
+    except (OSError, ValueError):
+        pass
+    roof = roofline_of(passes, peaks, clk, world, traffic_db)
     value = args.steps / (ms * 1e-3)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "Llama-3.2-1B-shaped parameter set, 64 seeds/step (kernel microbench)",
-                   "params": numel, "tensors": n_tensors, "seeds_per_step": args.seeds, "eps": EPS,
-                   "passes_per_step": 2 * args.seeds + 1, "parallelism": f"seed-sharded x{world}",
-                   "l2": "inputs (2.47 GB of bf16 parameters) larger than L2"},
-        "noise_cache": cached,
-        "perturb_pass_gbs": perturb_gbs, "perturb_pass_ms": pmean, "accum_pass_ms": amean,
-        "philox_gelem_per_s": (numel / (amean * 1e-3) / 1e9 if cached and amean else
-                               numel / (pmean * 1e-3) / 1e9 if pmean and not cached else None),
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": (achieved / hbm_peak) if achieved else None, "traffic": traffic,
-                     "kernel": kname, "algorithmic_bytes_per_launch": kbytes,
-                     "note": ("HBM-bound streaming pass (theta + z read, theta written); see profiles/"
-                              if cached and not amean else
-                              "instruction-bound: one Philox4x32-10 + logf/cosf evaluation per element (the next "
-                              "pair's field), z read and rewritten through the noise cache; the -2eps pass reads "
-                              "z from the cache at perturb_pass_gbs; see profiles/" if cached else
-                              "instruction-bound (Philox4x32-10 + logf/cosf per element per noise stream); "
-                              "see profiles/"),
-                     "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback 6650 GB/s"},
+        "config": workload_config(world, args.seeds, numel, n_tensors),
+        "noise_cache": cached, "field_exchange": exchange,
+        "passes": passes,
+        "perturb_pass_gbs": passes.get("perturb", {}).get("gbs"),
+        "roofline": roof,
         "clocks": clk,
         "gpu_launches": launches,
         "e2e": {"value": args.steps / (e2e_ms * 1e-3), "unit": UNIT, "wall_value": args.steps / wall_e2e,
                 "h2d_bytes_per_step": 4 * 2 * args.seeds, "d2h_bytes_per_step": 4 * 2 * args.seeds},
+        "replicas_identical": same, "param_digest": pdig,
         "metrics_last_step": {k: m[k] for k in ("loss", "proj_grad")},
     }
-    line["no_noise_cache" if cached else "noise_cache"] = alt
+    line["no_noise_cache" if cached else "noise_cache_variant"] = alt
     if cpu_line is not None:
         line["cpu_baseline"] = cpu_line
+    if ref_c1 is not None:
+        line["cpu_baseline"]["reference_code_config1"] = ref_c1()
+    if ref_gpu is not None:
+        line["reference_gpu"] = ref_gpu
     if egg is not None:
         line["eggroll"] = egg
     if mezo is not None:

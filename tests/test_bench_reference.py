@@ -1,6 +1,7 @@
 """The reference arm of bench.py (`--impl reference`) on CPU: one JSON line with the
-contract's keys, the same metric, unit and workload keys as the CUDA arm, and an e2e
-object without host-device traffic (it runs the oracle port on the host cores)."""
+contract's keys, the same metric, unit and config as the CUDA arm, and an e2e object
+without host-device traffic (it runs the oracle port on the host cores). Each timed step
+is one pair over the full parameter set, so the timed region is steps x ms_per_step."""
 import json
 import os
 import subprocess
@@ -20,6 +21,11 @@ def test_reference_arm_prints_contract_line():
         assert k in line, k
     assert line["impl"] == "reference" and line["unit"] == "ZO steps/s" and line["value"] > 0
     assert line["config"]["params"] == 1235814400 and line["config"]["tensors"] == 146
-    assert line["config"]["seeds_per_step"] == 64 and line["config"]["passes_per_step"] == 129
+    assert line["config"]["seeds_per_step"] == 64
+    sys.path.insert(0, ROOT)
+    import bench
+    assert line["config"] == bench.workload_config(1, 64, 1235814400, 146)    # the CUDA arm's config
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == line["value"]
+    assert abs(line["timed_region_s"] - line["steps"] * line["ms_per_step"] / 1000) < 0.5 * line["timed_region_s"]
+    assert line["full_step_s"] > 64 * line["ms_per_step"] / 1000
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]

@@ -51,16 +51,31 @@ int pass_run(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* strea
 
 // --- parameter-dtype rounding ----------------------------------------------------
 template <int DT> struct Dt;
+// round2 rounds two values with one paired conversion (the conversion of a single value
+// runs on the quarter-rate XU pipe; the paired one handles two at once) and unpacks them
+// with integer shifts: the same values as two round() calls.
 template <> struct Dt<ZT_F32> {
   __device__ static __forceinline__ float round(float x) { return x; }
+  __device__ static __forceinline__ void round2(float&, float&) {}
 };
 template <> struct Dt<ZT_BF16> {
   __device__ static __forceinline__ float round(float x) {
     return __bfloat162float(__float2bfloat16_rn(x));
   }
+  __device__ static __forceinline__ void round2(float& a, float& b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(&h);
+    a = __uint_as_float(w << 16);
+    b = __uint_as_float(w & 0xffff0000u);
+  }
 };
 template <> struct Dt<ZT_F16> {
   __device__ static __forceinline__ float round(float x) { return __half2float(__float2half_rn(x)); }
+  __device__ static __forceinline__ void round2(float& a, float& b) {
+    const float2 f = __half22float2(__floats2half2_rn(a, b));
+    a = f.x;
+    b = f.y;
+  }
 };
 
 }  // namespace zt

@@ -173,6 +173,19 @@ template <int DT, int EPT> struct Io {
 
 // ---- one thread's element group -------------------------------------------------
 
+// out[e] = round(f(e)) for e < EPT, two elements per paired conversion (Dt::round2).
+template <int DT, int EPT, class F>
+__device__ __forceinline__ void round_each(float (&out)[EPT], F f) {
+  static_assert(EPT % 2 == 0, "pairs");
+#pragma unroll
+  for (int e = 0; e < EPT; e += 2) {
+    float a = f(e), b = f(e + 1);
+    zt::Dt<DT>::round2(a, b);
+    out[e] = a;
+    out[e + 1] = b;
+  }
+}
+
 // Perturb / restore passes: theta <- round(theta + a*z) for each chained coefficient of
 // each stream (train_zo.py:350-351), nothing else.
 // Field-store slot of stream S for this thread's group: zf_off = (u - unit_begin) *
@@ -206,34 +219,19 @@ __device__ __forceinline__ void run_chain(const PassParams& P, const zt_tensor& 
       }
       for (int k = 0; k < S.n_chain; ++k) {
         const float a = S.chain[k];
-#pragma unroll
-        for (int e = 0; e < EPT; ++e) th[e] = R::round(__fmaf_rn(z[e], a, th[e]));
+        round_each<DT>(th, [&](int e) { return __fmaf_rn(z[e], a, th[e]); });
       }
       continue;
     }
     const zt::RoundKeys rk = zt::round_keys(zt::param_key(S.seed, P.n_params, (uint32_t)t.index));
     const float a0 = S.chain[0], a1 = S.chain[1], a2 = S.chain[2];
-    switch (S.n_chain) {  // the chain length is uniform: branch once, not per element
-      case 1:
+    if (S.n_chain > 0) {  // the chain length is uniform: branch once, not per element
+      float z[EPT];
 #pragma unroll
-        for (int e = 0; e < EPT; ++e) th[e] = R::round(__fmaf_rn(zt::gauss_rk(ctr0 + (uint32_t)e, rk), a0, th[e]));
-        break;
-      case 2:
-#pragma unroll
-        for (int e = 0; e < EPT; ++e) {
-          const float z = zt::gauss_rk(ctr0 + (uint32_t)e, rk);
-          th[e] = R::round(__fmaf_rn(z, a1, R::round(__fmaf_rn(z, a0, th[e]))));
-        }
-        break;
-      case 3:
-#pragma unroll
-        for (int e = 0; e < EPT; ++e) {
-          const float z = zt::gauss_rk(ctr0 + (uint32_t)e, rk);
-          th[e] = R::round(__fmaf_rn(z, a2, R::round(__fmaf_rn(z, a1, R::round(__fmaf_rn(z, a0, th[e]))))));
-        }
-        break;
-      default:
-        break;
+      for (int e = 0; e < EPT; ++e) z[e] = zt::gauss_rk(ctr0 + (uint32_t)e, rk);
+      round_each<DT>(th, [&](int e) { return __fmaf_rn(z[e], a0, th[e]); });
+      if (S.n_chain > 1) round_each<DT>(th, [&](int e) { return __fmaf_rn(z[e], a1, th[e]); });
+      if (S.n_chain > 2) round_each<DT>(th, [&](int e) { return __fmaf_rn(z[e], a2, th[e]); });
     }
   }
   if (c.dst & ZT_BUF_DATA) IO::store(t.data, e0, nvalid, vec, th);
@@ -275,8 +273,7 @@ __device__ __forceinline__ void run_full(const PassParams& P, const zt_tensor& t
     // _apply_z: theta <- round(theta + a*z), one rounding per call (train_zo.py:350-351)
     for (int k = 0; k < S.n_chain; ++k) {
       const float a = S.chain[k];
-#pragma unroll
-      for (int e = 0; e < EPT; ++e) th[e] = R::round(__fmaf_rn(z[e], a, th[e]));
+      round_each<DT>(th, [&](int e) { return __fmaf_rn(z[e], a, th[e]); });
     }
     if (S.flags & ZT_STREAM_GE) {
       const float a = (S.flags & ZT_STREAM_GE_DEV) ? dev_coef : S.ge_coef;
@@ -284,14 +281,12 @@ __device__ __forceinline__ void run_full(const PassParams& P, const zt_tensor& t
 #pragma unroll
         for (int e = 0; e < EPT; ++e) ge[e] = __fmul_rn(z[e], a);  // fp32 (train_zo.py:552)
       } else {
-#pragma unroll
-        for (int e = 0; e < EPT; ++e) ge[e] = R::round(__fmaf_rn(z[e], a, ge[e]));  // (:556, :577)
+        round_each<DT>(ge, [&](int e) { return __fmaf_rn(z[e], a, ge[e]); });  // (:556, :577)
       }
     }
     if (S.flags & ZT_STREAM_MOM) {
       const float a = S.mom_coef;
-#pragma unroll
-      for (int e = 0; e < EPT; ++e) mom[e] = R::round(__fmaf_rn(z[e], a, mom[e]));  // (:345)
+      round_each<DT>(mom, [&](int e) { return __fmaf_rn(z[e], a, mom[e]); });  // (:345)
     }
   }
 
@@ -610,36 +605,48 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
         const KStream& S = P.streams[s];
         const float c0 = S.chain[0], c1 = S.chain[1], c2 = S.chain[2], gc = S.ge_coef;
         const int nc = S.n_chain;  // uniform: the branches below are taken by every thread
-        auto apply = [&](int e, float z) {
-          float x = th[e];
-          if (nc > 0) x = R::round(__fmaf_rn(z, c0, x));
-          if (nc > 1) x = R::round(__fmaf_rn(z, c1, x));
-          if (nc > 2) x = R::round(__fmaf_rn(z, c2, x));
-          th[e] = x;
-          ge[e] = R::round(__fmaf_rn(z, gc, ge[e]));  // (train_zo.py:556)
+        // elements e and e+1 together: each rounding is one paired conversion (round2)
+        auto apply2 = [&](int e, float za, float zb) {
+          float xa = th[e], xb = th[e + 1];
+          if (nc > 0) { xa = __fmaf_rn(za, c0, xa); xb = __fmaf_rn(zb, c0, xb); R::round2(xa, xb); }
+          if (nc > 1) { xa = __fmaf_rn(za, c1, xa); xb = __fmaf_rn(zb, c1, xb); R::round2(xa, xb); }
+          if (nc > 2) { xa = __fmaf_rn(za, c2, xa); xb = __fmaf_rn(zb, c2, xb); R::round2(xa, xb); }
+          th[e] = xa;
+          th[e + 1] = xb;
+          float ga = __fmaf_rn(za, gc, ge[e]), gb = __fmaf_rn(zb, gc, ge[e + 1]);  // (train_zo.py:556)
+          R::round2(ga, gb);
+          ge[e] = ga;
+          ge[e + 1] = gb;
         };
-        if (S.flags & ZT_STREAM_Z_LOAD) {  // a field this rank cached (its last own pair)
+        if (S.flags & (ZT_STREAM_Z_LOAD | ZT_STREAM_Z_FIELD)) {
+          // a field this rank cached (its last own pair) or one pushed into its field store
+          const float* zp = (S.flags & ZT_STREAM_Z_LOAD)
+                                ? c.zcache + (size_t)u * ZT_UNIT_ELEMS + threadIdx.x * 8u
+                                : c.zfield + (size_t)S.zslot * (size_t)c.zfield_stride +
+                                      (size_t)(u - (int32_t)P.unit_begin) * ZT_UNIT_ELEMS + threadIdx.x * 8u;
           float zl[8];
-          ld_z<8>(c.zcache + (size_t)u * ZT_UNIT_ELEMS + threadIdx.x * 8u, zl);
+          ld_z<8>(zp, zl);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) apply(e, zl[e]);
-        } else if (S.flags & ZT_STREAM_Z_FIELD) {  // a field pushed into this rank's store
-          float zl[8];
-          ld_z<8>(c.zfield + (size_t)S.zslot * (size_t)c.zfield_stride +
-                      (size_t)(u - (int32_t)P.unit_begin) * ZT_UNIT_ELEMS + threadIdx.x * 8u, zl);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) apply(e, zl[e]);
+          for (int e = 0; e < 8; e += 2) apply2(e, zl[e], zl[e + 1]);
         } else {
           const zt::RoundKeys rk = zt::round_keys(zt::param_key(S.seed, P.n_params, st.index));
 #pragma unroll
-          for (int e = 0; e < 8; ++e) apply(e, zt::gauss_rk(e0 + (uint32_t)e, rk));
+          for (int e = 0; e < 8; e += 2)
+            apply2(e, zt::gauss_rk(e0 + (uint32_t)e, rk), zt::gauss_rk(e0 + (uint32_t)e + 1u, rk));
         }
       }
       const float nlr = -c.lr;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        th[e] = R::round(__fmaf_rn(ge[e], nlr, th[e]));  // (:399)
-        if (c.wd == ZT_WD_STANDARD) th[e] = R::round(__fmul_rn(th[e], c.wd_factor));  // (:401-402)
+      for (int e = 0; e < 8; e += 2) {
+        float xa = __fmaf_rn(ge[e], nlr, th[e]), xb = __fmaf_rn(ge[e + 1], nlr, th[e + 1]);  // (:399)
+        R::round2(xa, xb);
+        if (c.wd == ZT_WD_STANDARD) {  // (:401-402)
+          xa = __fmul_rn(xa, c.wd_factor);
+          xb = __fmul_rn(xb, c.wd_factor);
+          R::round2(xa, xb);
+        }
+        th[e] = xa;
+        th[e + 1] = xb;
       }
 #pragma unroll
       for (int k = 0; k < W::kNW; ++k) {

@@ -125,6 +125,7 @@ class FieldExchange:
                 self._opened.append(base.value)
                 ptrs[p] = base.value + o
         self.peer_store = ptrs
+        self.group = group
         self.plans = [push_plan(layout, n_units, j, world) for j in range(self.n_slots)]
         # one copy stream per destination: the copies to different peers run side by side
         self.streams = [torch.cuda.Stream(self.device) for _ in range(world)]
@@ -179,17 +180,22 @@ class FieldExchange:
         self._last = [None] * self.world
         self._by_cache.clear()
 
-    def close(self) -> None:
+    def close(self, barrier: bool = True) -> None:
+        """Unmap the peers' stores. With `barrier` (collective over the group) every rank
+        has unmapped before any rank returns, so none frees a store another still maps."""
         lib = L.load()
         torch.cuda.synchronize(self.device)
         with torch.cuda.device(self.device):
             for base in self._opened:
                 lib.zt_ipc_close(ctypes.c_void_p(base))
         self._opened = []
+        if barrier and self.world > 1:
+            import torch.distributed as dist
+            dist.barrier(group=self.group)
 
     def __del__(self):
         try:
             if self._opened:
-                self.close()
+                self.close(barrier=False)
         except Exception:
             pass

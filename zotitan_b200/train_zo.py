@@ -575,6 +575,13 @@ class ZOOptimizer:
             pl.field_slots = self.exchange.n_slots
         self._metric_keys = None
 
+    def close(self) -> None:
+        """Release the field exchange's peer mappings (collective over the process group
+        when the exchange is on); call on every rank before dropping the optimizer."""
+        if self.exchange is not None:
+            self.exchange.close()
+            self.exchange = None
+
     # properties mirroring the reference's attributes
     @property
     def _t(self):
