@@ -49,7 +49,7 @@ def parse():
     ap.add_argument("--field-exchange", type=float, default=0.8,
                     help="sharded runs: fraction of free device memory for the field stores (0: regenerate)")
     ap.add_argument("--profile-case", choices=["chain", "full", "replay", "chain-cached", "full-cached", "plus-cached",
-                                               "replay-field", "eggroll", "eggroll-gated", "eggroll-forward",
+                                               "replay-field", "lce", "eggroll", "eggroll-gated", "eggroll-forward",
                                                "mezo-step", "lora-step"],
                     default=None,
                     help="small case for ncu: one bf16 tensor of 2^28 elements, 3 launches of the "
@@ -183,6 +183,36 @@ def profile_case(kind: str):
         torch.cuda.synchronize()
         print(json.dumps({"profile_case": kind, "members": 16, "ms": a.elapsed_time(b),
                           "mean_loss": float(losses.mean()), "error": K.eggroll_take_error()}))
+        return
+    if kind == "lce":   # the config-3 scorer: 16 x 512 rows, vocabulary 128256, d 2048
+        rows, vocab, k = 16 * 512, 128256, 2048
+        g = torch.Generator(device="cuda").manual_seed(0)
+        x = torch.randn(rows, k, device="cuda", generator=g).bfloat16()
+        w = (torch.randn(vocab, k, device="cuda", generator=g) * 0.02).bfloat16()
+        t = torch.randint(0, vocab, (rows,), device="cuda", generator=g)
+        for _ in range(3):
+            K.linear_xent(x, w, t)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        a.record()
+        for _ in range(reps):
+            K.linear_xent(x, w, t)
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / reps
+        # the path it replaces: cuBLAS lm_head in 8192-row chunks + zt_xent_rows
+        from zotitan_b200.losses import CHUNK_ROWS
+        a.record()
+        for _ in range(reps):
+            for r0 in range(0, rows, CHUNK_ROWS):
+                K.xent_rows(torch.nn.functional.linear(x[r0:r0 + CHUNK_ROWS], w), t[r0:r0 + CHUNK_ROWS])
+        b.record()
+        torch.cuda.synchronize()
+        ms_old = a.elapsed_time(b) / reps
+        flops = 2.0 * rows * vocab * k
+        print(json.dumps({"profile_case": kind, "ms": ms, "tflops": flops / ms / 1e9, "ms_gemm_then_xent": ms_old,
+                          "tflops_gemm_then_xent": flops / ms_old / 1e9, "error": K.linear_xent_take_error()}))
         return
     n = 1 << 28
     p = (torch.randn(n, device="cuda") * 0.02).bfloat16()

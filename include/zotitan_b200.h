@@ -518,6 +518,36 @@ ZT_API int zt_lora_split(const float* a, void* out, int64_t n, void* stream);
 ZT_API int zt_xent_rows(const void* logits, int64_t ld, int64_t rows, int64_t vocab, const int64_t* targets,
                         float* loss, float* lse, int32_t* correct, void* stream);
 
+/* ---- the scorer: fused linear cross-entropy --------------------------------------- */
+
+/* Arguments of zt_linear_xent. */
+typedef struct zt_lce_args {
+  const void* x;           /* [rows, k] bf16 hidden states, row-major, 16-byte aligned */
+  const void* w;           /* [vocab, k] bf16 lm_head weight (torch's [out, in]), 16-byte aligned */
+  const int64_t* targets;  /* [rows] target token ids; negative = ignored position */
+  float* loss;             /* [rows] out */
+  float* lse;              /* [rows] out, or NULL */
+  int32_t* correct;        /* [rows] out, or NULL */
+  void* workspace;         /* zt_linear_xent_workspace_bytes(rows, vocab, k) bytes, 16-byte aligned */
+  size_t workspace_bytes;
+  int64_t rows, vocab, k;  /* k a multiple of 64 */
+} zt_lce_args;
+
+/* The lm_head GEMM and the cross-entropy statistics of zt_xent_rows in one pass, without
+ * writing the logits: logits[r, v] = bf16(x[r, :] . w[v, :]) (fp32 accumulation on the
+ * tensor cores, one rounding to bf16, as the reference's bf16 lm_head produces them), and
+ * from them lse, loss and correct exactly as zt_xent_rows defines them (ignored rows 0 in
+ * all three, a target >= vocab gives NaN). Replaces the Liger fused linear cross-entropy
+ * of zotitan/losses.py:17-52 (and the lm_head + torch cross-entropy of :55-79). The
+ * workspace holds per-row partial statistics of vocabulary splits; its size depends on
+ * the current device's SM count. */
+ZT_API size_t zt_linear_xent_workspace_bytes(int64_t rows, int64_t vocab, int64_t k);
+ZT_API int zt_linear_xent(const zt_lce_args* args, void* stream);
+
+/* Reads and clears the fused scorer's device error flag (nonzero: a bounded wait inside
+ * the GEMM expired; its outputs are then incomplete). Synchronises with the device. */
+ZT_API int zt_linear_xent_take_error(int32_t* code);
+
 /* ---- peer mappings for the sharded step's field exchange ------------------------- */
 
 /* The reference runs one process per GPU with no communication (sweeps/runall.py:5), so

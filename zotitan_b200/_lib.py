@@ -31,7 +31,8 @@ EXPORTS = ("zt_last_error", "zt_abi_version", "zt_param_key", "zt_philox_words",
            "zt_eggroll_linear", "zt_eggroll_take_error", "zt_randn_keys", "zt_eggroll_factors",
            "zt_eggroll_rmsnorm", "zt_eggroll_rope", "zt_eggroll_swiglu", "zt_xent_rows",
            "zt_eggroll_xb", "zt_eggroll_gated", "zt_eggroll_update_operands", "zt_lora_add", "zt_rmsnorm", "zt_gemm_swiglu", "zt_lora_add3", "zt_lora_split",
-           "zt_ipc_export", "zt_ipc_open", "zt_ipc_close", "zt_copy_async")
+           "zt_ipc_export", "zt_ipc_open", "zt_ipc_close", "zt_copy_async",
+           "zt_linear_xent_workspace_bytes", "zt_linear_xent", "zt_linear_xent_take_error")
 ZT_STATIC_MAX_TENSORS = 1024
 ZT_EGGROLL_MAX_PAIRS = 512
 ZT_EGGROLL_FACTOR_WORK_FLOATS = 64 * 20
@@ -115,6 +116,13 @@ class ZtEggrollNormArgs(ctypes.Structure):
                 ("key_index", ctypes.c_uint32)]
 
 
+class ZtLceArgs(ctypes.Structure):
+    _fields_ = [("x", ctypes.c_void_p), ("w", ctypes.c_void_p), ("targets", ctypes.c_void_p),
+                ("loss", ctypes.c_void_p), ("lse", ctypes.c_void_p), ("correct", ctypes.c_void_p),
+                ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t), ("rows", ctypes.c_int64),
+                ("vocab", ctypes.c_int64), ("k", ctypes.c_int64)]
+
+
 class ZtError(RuntimeError):
     """A C-ABI call returned a nonzero status."""
 
@@ -188,6 +196,12 @@ def load():
     lib.zt_ipc_close.argtypes = [P]
     lib.zt_copy_async.restype = ctypes.c_int
     lib.zt_copy_async.argtypes = [P, P, ctypes.c_size_t, P]
+    lib.zt_linear_xent_workspace_bytes.restype = ctypes.c_size_t
+    lib.zt_linear_xent_workspace_bytes.argtypes = [I64, I64, I64]
+    lib.zt_linear_xent.restype = ctypes.c_int
+    lib.zt_linear_xent.argtypes = [ctypes.POINTER(ZtLceArgs), P]
+    lib.zt_linear_xent_take_error.restype = ctypes.c_int
+    lib.zt_linear_xent_take_error.argtypes = [ctypes.POINTER(ctypes.c_int32)]
     lib.zt_plan_workspace_bytes.restype = ctypes.c_size_t
     lib.zt_plan_workspace_bytes.argtypes = [I32]
     if lib.zt_abi_version() != ABI_VERSION:

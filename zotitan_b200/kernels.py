@@ -607,6 +607,56 @@ def xent_rows(logits: torch.Tensor, targets: torch.Tensor, want_lse: bool = True
     return loss, lse, correct
 
 
+def linear_xent_supported(x: torch.Tensor, w: torch.Tensor) -> bool:
+    """Whether zt_linear_xent takes these operands: bf16, contiguous, 16-byte aligned, the
+    inner dimension a multiple of 64."""
+    return (x.is_cuda and w.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.dim() == 2
+            and w.dim() == 2 and x.shape[1] == w.shape[1] and x.shape[1] % 64 == 0 and x.is_contiguous()
+            and w.is_contiguous() and x.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0 and x.shape[0] > 0)
+
+
+_LCE_WS: dict = {}
+
+
+def linear_xent(x: torch.Tensor, w: torch.Tensor, targets: torch.Tensor, want_lse: bool = True,
+                want_correct: bool = True):
+    """Fused lm_head + cross-entropy statistics (zt_linear_xent): x [rows, k] bf16 hidden
+    states, w [vocab, k] bf16 head weight, int64 targets [rows] (negative = ignored).
+    Returns (loss, lse | None, correct | None) as zt_xent_rows on bf16(x @ w.T) would,
+    without writing the logits."""
+    if not linear_xent_supported(x, w):
+        raise ValueError("x and w must be contiguous 16-byte aligned bf16 CUDA matrices with k % 64 == 0")
+    if targets.dtype != torch.int64 or targets.shape != (x.shape[0],) or not targets.is_contiguous():
+        raise ValueError("targets must be a contiguous int64 [rows] vector")
+    rows, k = x.shape
+    vocab = w.shape[0]
+    dev = x.device
+    lib = L.load()
+    with torch.cuda.device(dev):
+        need = lib.zt_linear_xent_workspace_bytes(rows, vocab, k)
+        if need == 0:
+            L.check(L.ZT_ERR_INVALID, "zt_linear_xent_workspace_bytes")
+        ws = _LCE_WS.get(dev)
+        if ws is None or ws.numel() < need:
+            ws = torch.empty(need, dtype=torch.uint8, device=dev)
+            _LCE_WS[dev] = ws
+        loss = torch.empty(rows, dtype=torch.float32, device=dev)
+        lse = torch.empty(rows, dtype=torch.float32, device=dev) if want_lse else None
+        correct = torch.empty(rows, dtype=torch.int32, device=dev) if want_correct else None
+        args = L.ZtLceArgs(x.data_ptr(), w.data_ptr(), targets.data_ptr(), loss.data_ptr(),
+                           lse.data_ptr() if lse is not None else None,
+                           correct.data_ptr() if correct is not None else None, ws.data_ptr(), ws.numel(), rows,
+                           vocab, k)
+        L.check(lib.zt_linear_xent(ctypes.byref(args), _stream_ptr(dev)), "zt_linear_xent")
+    return loss, lse, correct
+
+
+def linear_xent_take_error() -> int:
+    code = ctypes.c_int32(0)
+    L.check(L.load().zt_linear_xent_take_error(ctypes.byref(code)), "zt_linear_xent_take_error")
+    return int(code.value)
+
+
 def eggroll_update_operands(a: torch.Tensor, b: torch.Tensor, scale: torch.Tensor, coef: torch.Tensor,
                             sigma: float, dtype: torch.dtype = torch.bfloat16):
     """(a_cat [n, 8p], b_cat [k, 8p]) bf16 operands of the ES update GEMM of one 2-D tensor

@@ -1,12 +1,15 @@
 """Cross-entropy scorers over the model's LM head (zotitan/losses.py).
 
 ``get_xentropy(fused)`` picks the scorer as the reference does (zotitan/losses.py:7-15):
-``fused=True`` -> ``fused_xentropy``: the decoder's hidden states, the lm_head GEMM in row
-chunks (a plain bf16 GEMM) and ``zt_xent_rows`` (one CUDA read of each logits row giving
-its loss, logsumexp and argmax) in place of the Liger fused linear cross-entropy
-(zotitan/losses.py:17-52); ``fused=False`` -> ``torch_xentropy``, the reference's torch
-path (zotitan/losses.py:55-79), run eagerly. Both return (ce, z_loss | None, extra | None)
-with ce and z_loss kept apart, as the reference's contract does.
+``fused=True`` -> ``fused_xentropy``: the decoder's hidden states and ``zt_linear_xent``, the
+lm_head GEMM on the tensor cores with the per-row loss, logsumexp and first argmax kept in
+its epilogue so no logit reaches HBM, in place of the Liger fused linear cross-entropy
+(zotitan/losses.py:17-52); heads it cannot take (a bias, other dtypes, an inner dimension
+that is not a multiple of 64) go through the lm_head GEMM in row chunks and
+``zt_xent_rows`` (one CUDA read of each logits row). ``fused=False`` -> ``torch_xentropy``,
+the reference's torch path (zotitan/losses.py:55-79), run eagerly. Both return
+(ce, z_loss | None, extra | None) with ce and z_loss kept apart, as the reference's
+contract does.
 """
 from __future__ import annotations
 
@@ -44,8 +47,11 @@ def torch_xentropy(model, batch, z_loss_weight: float, compute_accuracy: bool):
 def head_xentropy(hidden: torch.Tensor, targets: torch.Tensor, weight: torch.Tensor, bias=None,
                   want_lse: bool = True, want_correct: bool = True, chunk_rows: int = CHUNK_ROWS):
     """Per-row (loss, lse, correct) of next-token CE for hidden rows [R, d] against
-    targets [R] (negative = ignored): logits = hidden @ weight^T (+ bias) in bf16, one
-    chunk of rows at a time, each chunk scored by zt_xent_rows."""
+    targets [R] (negative = ignored), logits = bf16(hidden @ weight^T (+ bias)): the fused
+    kernel (zt_linear_xent) when it takes the operands, else one chunk of rows at a time
+    through the GEMM and zt_xent_rows."""
+    if bias is None and K.linear_xent_supported(hidden, weight):
+        return K.linear_xent(hidden, weight, targets, want_lse, want_correct)
     R = hidden.shape[0]
     dev = hidden.device
     loss = torch.empty(R, dtype=torch.float32, device=dev)
@@ -66,16 +72,21 @@ def head_xentropy(hidden: torch.Tensor, targets: torch.Tensor, weight: torch.Ten
 
 def fused_xentropy(model, batch, z_loss_weight: float, compute_accuracy: bool):
     """The fused scorer: decoder forward, causal shift (hidden[:, :-1] predicts
-    labels[:, 1:], -100 ignored), chunked lm_head GEMM and zt_xent_rows. Same return
-    contract and reductions as the reference's paths: ce = mean CE over the unmasked
-    positions, z_loss = z_loss_weight * mean(lse^2), acc = mean(argmax == label)."""
+    labels[:, 1:], -100 ignored), head_xentropy. Every position is scored against the next
+    label, the last one of each sequence against -100 (ignored), so the hidden states are
+    read in place. Same return contract and reductions as the reference's paths:
+    ce = mean CE over the unmasked positions, z_loss = z_loss_weight * mean(lse^2),
+    acc = mean(argmax == label)."""
     m = getattr(model, "_orig_mod", model)
     hidden = m.get_decoder()(input_ids=batch["input_ids"], attention_mask=batch.get("attention_mask"),
                              use_cache=False).last_hidden_state
     head = m.get_output_embeddings()
-    d = hidden.shape[-1]
-    shift_h = hidden[:, :-1, :].reshape(-1, d)
-    shift_t = batch["labels"][:, 1:].reshape(-1).contiguous()
+    B, S, d = hidden.shape
+    shift_h = hidden.reshape(-1, d)
+    labels = batch["labels"]
+    shift_t = torch.full((B, S), IGNORE_INDEX, dtype=torch.int64, device=labels.device)
+    shift_t[:, :-1] = labels[:, 1:]
+    shift_t = shift_t.reshape(-1)
     if shift_h.dtype != torch.bfloat16:
         raise NotImplementedError("the fused scorer reads bf16 logits; use fused=False for other dtypes")
     has_z = z_loss_weight != 0.0
