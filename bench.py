@@ -49,7 +49,7 @@ def parse():
     ap.add_argument("--field-exchange", type=float, default=0.8,
                     help="sharded runs: fraction of free device memory for the field stores (0: regenerate)")
     ap.add_argument("--profile-case", choices=["chain", "full", "replay", "chain-cached", "full-cached", "plus-cached",
-                                               "replay-field", "lce", "eggroll", "eggroll-gated", "eggroll-forward",
+                                               "replay-field", "replay-mixed", "lce", "eggroll", "eggroll-gated", "eggroll-forward",
                                                "mezo-step", "lora-step"],
                     default=None,
                     help="small case for ncu: one bf16 tensor of 2^28 elements, 3 launches of the "
@@ -201,8 +201,13 @@ def profile_case(kind: str):
         b.record()
         torch.cuda.synchronize()
         ms = a.elapsed_time(b) / reps
-        # the path it replaces: cuBLAS lm_head in 8192-row chunks + zt_xent_rows
+        # the path it replaces: cuBLAS lm_head in 8192-row chunks + zt_xent_rows (warmed up:
+        # the logits buffer allocated and cuBLAS's choice made before the timed calls)
         from zotitan_b200.losses import CHUNK_ROWS
+        for _ in range(3):
+            for r0 in range(0, rows, CHUNK_ROWS):
+                K.xent_rows(torch.nn.functional.linear(x[r0:r0 + CHUNK_ROWS], w), t[r0:r0 + CHUNK_ROWS])
+        torch.cuda.synchronize()
         a.record()
         for _ in range(reps):
             for r0 in range(0, rows, CHUNK_ROWS):
@@ -271,7 +276,9 @@ def profile_case(kind: str):
         zc = tab.noise_cache()
         cfg = K.PassCfg(src=L.ZT_BUF_DATA, dst=L.ZT_BUF_LIVE, zcache=zc.data_ptr())
         streams = [K.Stream(5, (f(1e-3),), z_store=True)]
-    elif kind == "replay-field":   # the sharded last pass, 16 pairs' fields read from a field store
+    elif kind in ("replay-field", "replay-mixed"):
+        # the sharded last pass, 16 pairs' fields read from a field store (replay-mixed: every
+        # other pair's field regenerated instead, as when the store holds only some pairs)
         n = 1 << 25
         p = p[:n]
         tab = K.ParamTable([p])
@@ -279,7 +286,9 @@ def profile_case(kind: str):
         store = torch.randn(16 * units * 2048, device="cuda")
         cfg = K.PassCfg(ge_mode=L.ZT_GE_ACCUM, update=True, lr=f(1e-5), zfield=store.data_ptr(),
                         zfield_stride=units * 2048)
-        streams = [K.Stream(100 + j, (f(1e-3), f(-2e-3), f(1e-3)), ge=f(0.01 * (j - 8)), z_field=j) for j in range(16)]
+        mixed = kind == "replay-mixed"
+        streams = [K.Stream(100 + j, (f(1e-3), f(-2e-3), f(1e-3)), ge=f(0.01 * (j - 8)),
+                            z_field=None if mixed and j % 2 else j) for j in range(16)]
     elif kind == "replay":   # the sharded step's last pass: 16 pairs' chains + grad_est + SGD
         tab = K.ParamTable([p])
         cfg = K.PassCfg(ge_mode=L.ZT_GE_ACCUM, update=True, lr=f(1e-5))

@@ -294,7 +294,9 @@ typedef struct zt_eggroll_args {
   int32_t rows_per_member;  /* multiple of 128 dividing m */
   int32_t rank;           /* must be 4 */
   int32_t xb_ready;       /* nonzero: xb already holds X B_i (zt_eggroll_xb) and is only read */
-  int32_t reserved;
+  int32_t test_stall_loads; /* test hook, 0 in normal use: the GEMM's loader issues no copies, so
+                               its first wait for a loaded stage expires (~2 s) with nothing in
+                               flight and the call reports it through zt_eggroll_take_error */
   /* Optional rank-4 K-slab (both non-NULL: a, b, sigma, xb are not read). The correction
    * sigma_i (X B_i) A_i^T then runs on the tensor cores as one extra K = 16 MMA per tile:
    * x_ext [m, 16] bf16 rows [hi(sigma_i X B_i), lo(sigma_i X B_i), 0 x 8] (zt_eggroll_xb,
@@ -481,6 +483,20 @@ ZT_API int zt_eggroll_update_operands(const float* a, const float* b, const floa
                                       int32_t pairs, int64_t n, int64_t k, float sigma, void* a_cat, void* b_cat,
                                       void* stream);
 
+/* w[i, j] <- bf16(w[i, j] + alpha * sum_t a[i, t] b[j, t]) for w [m, n] bf16 (row stride ldw,
+ * a multiple of 8), a [m, k] and b [n, k] bf16 row-major (k % 64 == 0, n % 32 == 0, all
+ * 16-byte aligned): the product on the tensor cores with fp32 accumulation, w read, updated
+ * with one fused multiply-add and rounded once in the epilogue. With a = a_cat, b = b_cat of
+ * zt_eggroll_update_operands and alpha = -lr it is the evolution-strategies update
+ * theta -= lr * sum_j coef_j z_j of a 2-D tensor (zotitan/train_zo.py:550-556, 376-407 with
+ * the low_rank directions of :304-320). */
+ZT_API int zt_gemm_addto(void* w, int64_t ldw, const void* a, const void* b, float alpha, int64_t m, int64_t n,
+                         int64_t k, void* stream);
+
+/* Reads and clears zt_gemm_addto's device error flag (nonzero: a bounded wait inside the
+ * GEMM expired and w is partly updated). Synchronises with the device. */
+ZT_API int zt_gemm_take_error(int32_t* code);
+
 /* The tail of a LoRA linear (zotitan/lora.py:77-86) in one pass over the output:
  *   out[t, c] = bf16(out[t, c] + bf16(scale * sum_r xa[t, r] b[c, r]))
  * with out [rows, n] bf16 holding the base layer's output (updated in place), xa [rows, r]
@@ -531,6 +547,14 @@ typedef struct zt_lce_args {
   void* workspace;         /* zt_linear_xent_workspace_bytes(rows, vocab, k) bytes, 16-byte aligned */
   size_t workspace_bytes;
   int64_t rows, vocab, k;  /* k a multiple of 64 */
+  /* Test hooks, 0 in normal use. With test_stall_loads the GEMM's loader issues no copies,
+   * so the first wait for a loaded stage expires (after test_wait_cycles clock cycles; 0:
+   * the default bound of ~2 s) with no copy and no MMA in flight: the kernel records the
+   * expiry (zt_linear_xent_take_error), frees its tensor memory and returns, and the
+   * outputs are incomplete. It exercises the abort path without a fault. */
+  int32_t test_stall_loads;
+  int32_t reserved;
+  int64_t test_wait_cycles;
 } zt_lce_args;
 
 /* The lm_head GEMM and the cross-entropy statistics of zt_xent_rows in one pass, without

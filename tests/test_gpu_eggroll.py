@@ -268,3 +268,40 @@ def test_gemm_swiglu_rejects_bad_shapes():
     w = torch.zeros(128, 64, device="cuda", dtype=torch.bfloat16)
     with pytest.raises(ZtError):
         K_.gemm_swiglu(x, w, w)   # 200 rows: not whole 256-row tiles
+
+
+@pytest.mark.parametrize("m,n,k", [(512, 256, 128), (1000, 96, 64), (1024, 4096, 4096), (4096, 4096, 512)])
+def test_gemm_addto_matches_fp32_reference(m, n, k):
+    """zt_gemm_addto: w <- bf16(w + alpha a b^T) against the fp32 product added to w and
+    rounded once in torch: equal, or one bf16 step apart where the fp32 sums of the two
+    accumulation orders straddle a rounding boundary (rare)."""
+    from zotitan_b200 import kernels as K
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    w = (torch.randn(m, n, device="cuda", generator=g) * 0.02).bfloat16()
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    b = torch.randn(n, k, device="cuda", generator=g).bfloat16()
+    alpha = -1e-3
+    exact = w.double() + alpha * (a.double() @ b.double().T)
+    want = exact.float().bfloat16()
+    got = K.gemm_addto(w.clone(), a, b, alpha)
+    torch.cuda.synchronize()
+    assert K.gemm_take_error() == 0
+    diff = (got.double() - exact).abs()
+    # one bf16 step of the result, plus the fp32 accumulation error of the product term
+    # (where w and the term nearly cancel the result's own step is smaller than that)
+    step = torch.ldexp(torch.ones_like(diff), torch.frexp(exact.abs().clamp_min(2.0 ** -126))[1] - 8)
+    bound = step + abs(alpha) * 2.0 ** -20 * (a.double().abs() @ b.double().abs().T)
+    assert bool((diff <= bound).all()), float((diff / bound).max())
+    assert float((got != want).float().mean()) < 0.01
+    assert not torch.equal(got, w)
+
+
+def test_gemm_addto_rejects_bad_shapes():
+    from zotitan_b200 import _lib as L
+    lib = L.load()
+    w = torch.zeros(256, 96, dtype=torch.bfloat16, device="cuda")
+    a = torch.zeros(256, 64, dtype=torch.bfloat16, device="cuda")
+    b = torch.zeros(96, 64, dtype=torch.bfloat16, device="cuda")
+    assert lib.zt_gemm_addto(w.data_ptr(), 96, a.data_ptr(), b.data_ptr(), 1.0, 256, 96, 48, None) == L.ZT_ERR_INVALID
+    assert lib.zt_gemm_addto(w.data_ptr(), 96, a.data_ptr(), b.data_ptr(), 1.0, 256, 80, 64, None) == L.ZT_ERR_INVALID
+    assert lib.zt_gemm_addto(w.data_ptr(), 90, a.data_ptr(), b.data_ptr(), 1.0, 256, 96, 64, None) == L.ZT_ERR_INVALID

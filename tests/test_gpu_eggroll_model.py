@@ -69,7 +69,8 @@ def test_population_forward_matches_materialised_members(batch):
     assert abs(got[0] - got[1]) > 1e-4 and abs(got[0] - l0) > 1e-5
 
 
-def test_es_update_matches_sum_of_materialised_directions():
+@pytest.mark.parametrize("n_pairs", [4, 8])
+def test_es_update_matches_sum_of_materialised_directions(n_pairs):
     """EggrollPopulation.apply_update (rank-4*pairs GEMM for 2-D tensors, dense Gaussian
     sum for 1-D) against theta - lr * sum_j coef_j z_j with every z_j materialised by the
     oracle's restatement of the reference's low_rank branch. The oracle rounds each z_j to
@@ -84,10 +85,24 @@ def test_es_update_matches_sum_of_materialised_directions():
     named = [(n, p) for n, p in model.named_parameters()]
     host = [p.detach().float().cpu().numpy() for _, p in named]
     pop = EggrollPopulation(model, EggrollConfig(sigma=SIGMA))
-    seeds = [3, 11, 17, 23]
-    coefs = [0.25, -0.5, 0.125, 0.75]
+    # 4 pairs: inner dimension 32, the update through torch's addmm; 8 pairs: 64, zt_gemm_addto
+    seeds = [3, 11, 17, 23, 29, 31, 37, 41][:n_pairs]
+    coefs = [0.25, -0.5, 0.125, 0.75, -0.375, 0.0625, 0.5, -0.25][:n_pairs]
     lr = 1e-2
-    pop.apply_update(seeds, coefs, lr)
+    from zotitan_b200 import kernels as K
+    calls = {"n": 0}
+    orig = K.gemm_addto
+
+    def counting(*a, **kw):
+        calls["n"] += 1
+        return orig(*a, **kw)
+
+    K.gemm_addto = counting
+    try:
+        pop.apply_update(seeds, coefs, lr)
+    finally:
+        K.gemm_addto = orig
+    assert (calls["n"] > 0) == (n_pairs == 8)
     oz = OracleZO([h.copy() for h in host], [__import__("oracle.philox", fromlist=["x"]).BF16] * len(host), _cfg(),
                   noise="c", semantics="cuda")
     delta = [np.zeros_like(h, dtype=np.float64) for h in host]

@@ -57,3 +57,51 @@ def test_polar_direction_is_orthogonal_and_normalised():
     w0, n0 = ps[0].detach().clone(), ps[1].detach().clone()
     m = opt.step(None, [None, None])
     assert np.isfinite(m["loss"]) and not torch.equal(w0, ps[0]) and not torch.equal(n0, ps[1])
+
+
+@pytest.mark.parametrize("dist_kind", ["low_rank", "polar"])
+def test_sharded_low_rank_matches_single_gpu(dist_kind):
+    """The seed-sharded schedule with materialised directions (one-rank NCCL group): each
+    own pair perturbs the live copy from the master, the last pass replays every pair's
+    +eps / -2eps / +eps chain on the master (the 2-D tensors with the reference's ops, the
+    1-D ones in the fused pass) and updates it; the parameters equal the single-GPU run's
+    exactly, and the forwards see master + eps z."""
+    import os
+
+    import torch.distributed as dist
+    from zotitan_b200.objective import Score
+    from zotitan_b200.train_zo import ZOConfig, ZOOptimizer
+
+    # bf16 for low_rank; fp32 for polar, whose QR (torch.linalg.qr) has no bf16 CUDA kernel,
+    # so the reference's own polar branch runs only on fp32 parameters on a GPU
+    dt = torch.bfloat16 if dist_kind == "low_rank" else torch.float32
+
+    def run(sharded):
+        g = torch.Generator(device="cuda").manual_seed(11)
+        ps = [torch.nn.Parameter((torch.randn(48, 80, device="cuda", generator=g) * 0.02).to(dt)),
+              torch.nn.Parameter(torch.ones(48, device="cuda").to(dt)),
+              torch.nn.Parameter((torch.randn(80, 48, device="cuda", generator=g) * 0.02).to(dt))]
+        cfg = ZOConfig()
+        cfg.eps, cfg.z_batch, cfg.base.lr = 1e-3, 3, 5e-2
+        cfg.perturbation.distribution, cfg.perturbation.rank = dist_kind, 4
+        vals = iter([2.0, 1.9, 2.1, 2.15, 1.8, 1.75, 2.2, 2.3, 2.05, 1.95, 2.0, 2.12])
+        opt = ZOOptimizer([(f"p{i}", p) for i, p in enumerate(ps)], cfg,
+                          lambda m, b: Score(torch.tensor(next(vals), device="cuda"), {}), sharded=sharded)
+        for _ in range(2):
+            opt.step(None, [None] * 3)
+        torch.cuda.synchronize()
+        return [p.detach().float().cpu().numpy() for p in ps], opt
+
+    a1, _ = run(False)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ["MASTER_PORT"] = "29541"
+    dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device("cuda", 0))
+    try:
+        aw, opt = run(True)
+        assert opt.planner.sharded and opt.lr_idx == [0, 2] and opt.master is not None
+        for x, y in zip(a1, aw):
+            assert np.array_equal(x, y)
+        for m, p in zip(opt.master, opt.params):
+            assert torch.equal(m, p)
+    finally:
+        dist.destroy_process_group()

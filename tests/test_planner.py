@@ -161,11 +161,10 @@ def test_planner_rejects_unsupported():
     cfg = StepCase(_G, "mezo_f32_z1").cfg_dict
     cfg["perturbation"]["distribution"] = "low_rank"
     assert StepPlanner(ns(cfg)).materialized          # one rank: supported (materialised directions)
-    with pytest.raises(NotImplementedError):
-        StepPlanner(ns(cfg), world=2, rank=0)          # the sharded schedule replays Gaussian fields
+    assert StepPlanner(ns(cfg), world=2, rank=0).sharded   # sharded: the 2-D replay runs on the master
     cfg["mom"]["momentum_method"] = "seed_window"
-    with pytest.raises(NotImplementedError):
-        StepPlanner(ns(cfg))                           # so does seed-window momentum
+    with pytest.raises(AssertionError, match="seed_window momentum is incompatible"):
+        StepPlanner(ns(cfg))                           # refused as the reference refuses it (train_zo.py:268-270)
     cfg["mom"]["momentum_method"] = "none"
     cfg["perturbation"]["distribution"] = "sparse"
     with pytest.raises(NotImplementedError):

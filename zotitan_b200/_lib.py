@@ -32,7 +32,8 @@ EXPORTS = ("zt_last_error", "zt_abi_version", "zt_param_key", "zt_philox_words",
            "zt_eggroll_rmsnorm", "zt_eggroll_rope", "zt_eggroll_swiglu", "zt_xent_rows",
            "zt_eggroll_xb", "zt_eggroll_gated", "zt_eggroll_update_operands", "zt_lora_add", "zt_rmsnorm", "zt_gemm_swiglu", "zt_lora_add3", "zt_lora_split",
            "zt_ipc_export", "zt_ipc_open", "zt_ipc_close", "zt_copy_async",
-           "zt_linear_xent_workspace_bytes", "zt_linear_xent", "zt_linear_xent_take_error")
+           "zt_linear_xent_workspace_bytes", "zt_linear_xent", "zt_linear_xent_take_error",
+           "zt_gemm_addto", "zt_gemm_take_error")
 ZT_STATIC_MAX_TENSORS = 1024
 ZT_EGGROLL_MAX_PAIRS = 512
 ZT_EGGROLL_FACTOR_WORK_FLOATS = 64 * 20
@@ -78,7 +79,7 @@ class ZtEggrollArgs(ctypes.Structure):
                 ("sigma", ctypes.c_void_p), ("xb", ctypes.c_void_p), ("y", ctypes.c_void_p),
                 ("m", ctypes.c_int64), ("n", ctypes.c_int64), ("k", ctypes.c_int64),
                 ("rows_per_member", ctypes.c_int32), ("rank", ctypes.c_int32), ("xb_ready", ctypes.c_int32),
-                ("reserved", ctypes.c_int32), ("x_ext", ctypes.c_void_p), ("w_ext", ctypes.c_void_p)]
+                ("test_stall_loads", ctypes.c_int32), ("x_ext", ctypes.c_void_p), ("w_ext", ctypes.c_void_p)]
 
 
 class ZtEggrollGatedArgs(ctypes.Structure):
@@ -120,7 +121,8 @@ class ZtLceArgs(ctypes.Structure):
     _fields_ = [("x", ctypes.c_void_p), ("w", ctypes.c_void_p), ("targets", ctypes.c_void_p),
                 ("loss", ctypes.c_void_p), ("lse", ctypes.c_void_p), ("correct", ctypes.c_void_p),
                 ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t), ("rows", ctypes.c_int64),
-                ("vocab", ctypes.c_int64), ("k", ctypes.c_int64)]
+                ("vocab", ctypes.c_int64), ("k", ctypes.c_int64), ("test_stall_loads", ctypes.c_int32),
+                ("reserved", ctypes.c_int32), ("test_wait_cycles", ctypes.c_int64)]
 
 
 class ZtError(RuntimeError):
@@ -202,6 +204,10 @@ def load():
     lib.zt_linear_xent.argtypes = [ctypes.POINTER(ZtLceArgs), P]
     lib.zt_linear_xent_take_error.restype = ctypes.c_int
     lib.zt_linear_xent_take_error.argtypes = [ctypes.POINTER(ctypes.c_int32)]
+    lib.zt_gemm_addto.restype = ctypes.c_int
+    lib.zt_gemm_addto.argtypes = [P, I64, P, P, ctypes.c_float, I64, I64, I64, P]
+    lib.zt_gemm_take_error.restype = ctypes.c_int
+    lib.zt_gemm_take_error.argtypes = [ctypes.POINTER(ctypes.c_int32)]
     lib.zt_plan_workspace_bytes.restype = ctypes.c_size_t
     lib.zt_plan_workspace_bytes.argtypes = [I32]
     if lib.zt_abi_version() != ABI_VERSION:

@@ -73,6 +73,7 @@ struct EggParams {
   int32_t m_blocks, n_blocks, k_blocks;
   int32_t n;
   int32_t rows_per_member;
+  int32_t stall_loads;  // test hook: the loader issues no copies (zt_eggroll_args.test_stall_loads)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -207,6 +208,7 @@ __global__ void __launch_bounds__(kThreadsEgg, 1) eggroll_gemm_kernel(const __gr
       for (int s = 0; s < kStages; ++s) last_phase[s] = -1;
       uint32_t it = 0;
       bool ok = true;
+      if (P.stall_loads) ok = false;
       for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
         int mb, nb;
         tile_coords(tile, P.m_blocks, P.n_blocks, mb, nb);
@@ -474,7 +476,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsEgg, 1)
       int last_phase[kStages2];
       for (int s = 0; s < kStages2; ++s) last_phase[s] = -1;
       uint32_t it = 0;
-      for (int tile = cid; tile < n_tiles; tile += ncl) {
+      for (int tile = cid; !P.stall_loads && tile < n_tiles; tile += ncl) {
         int mb, nb;
         tile_coords(tile, m_tiles, P.n_blocks, mb, nb);
         bool ok = true;
@@ -1124,6 +1126,7 @@ int zt_eggroll_linear(const zt_eggroll_args* args, void* stream) {
   // CTA pairs (cta_group::2) whenever the rows split into 256-row tiles
   const bool pair = (A.m % 256) == 0;
   EggParams P;
+  P.stall_loads = A.test_stall_loads ? 1 : 0;
   if (int rc = make_map(enc, &P.tmap_x, A.x, (uint64_t)A.m, (uint64_t)A.k, kBM)) return rc;
   if (int rc = make_map(enc, &P.tmap_w, A.w, (uint64_t)A.n, (uint64_t)A.k, pair ? kHalfRows : kBN)) return rc;
   if (pair)
@@ -1182,6 +1185,7 @@ int zt_eggroll_gated(const zt_eggroll_gated_args* args, void* stream) {
   EncodeFn enc = nullptr;
   if (int rc = get_encode(&enc)) return rc;
   EggParams P;
+  P.stall_loads = 0;
   if (int rc = make_map(enc, &P.tmap_x, A.x, (uint64_t)A.m, (uint64_t)A.k, kBM)) return rc;
   if (int rc = make_map(enc, &P.tmap_w, A.w_gate, (uint64_t)A.n, (uint64_t)A.k, kHalfRows)) return rc;
   if (int rc = make_map(enc, &P.tmap_w2, A.w_up, (uint64_t)A.n, (uint64_t)A.k, kHalfRows)) return rc;
@@ -1222,6 +1226,7 @@ int zt_gemm_swiglu(const void* x, const void* w_gate, const void* w_up, void* y,
   EncodeFn enc = nullptr;
   if (int rc = get_encode(&enc)) return rc;
   EggParams P;
+  P.stall_loads = 0;
   if (int rc = make_map(enc, &P.tmap_x, x, (uint64_t)m, (uint64_t)k, kBM)) return rc;
   if (int rc = make_map(enc, &P.tmap_w, w_gate, (uint64_t)n, (uint64_t)k, kHalfRows)) return rc;
   if (int rc = make_map(enc, &P.tmap_w2, w_up, (uint64_t)n, (uint64_t)k, kHalfRows)) return rc;

@@ -46,6 +46,8 @@ struct LceParams {
   float4* partials;    // [n_splits][rows_pad]: (max, sum exp(x - max), target logit, argmax bits)
   int32_t rows, vocab, k_blocks;
   int32_t m_tiles, n_tiles, split_tiles, n_splits, rows_pad;
+  int32_t stall_loads;    // test hook: the loader issues no copies
+  long long wait_cycles;  // bound of every wait
 };
 
 __device__ __forceinline__ void item_range(const LceParams& P, int item, int& mt, int& split, int& nt0, int& nt1) {
@@ -104,7 +106,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int last_phase[kStages];
       for (int s = 0; s < kStages; ++s) last_phase[s] = -1;
       uint32_t it = 0;
-      bool ok = true;
+      bool ok = !P.stall_loads;
       for (int item = cid; ok && item < n_items; item += ncl) {
         int mt, split, nt0, nt1;
         item_range(P, item, mt, split, nt0, nt1);
@@ -112,7 +114,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           for (int kb = 0; kb < P.k_blocks; ++kb, ++it) {
             const int s = it % kStages;
             const uint32_t round = it / kStages;
-            if (!mbar_wait_pair(&empty[s], (round & 1) ^ 1, abort, peer_abort, &g_lce_error, 1)) { ok = false; break; }
+            if (!mbar_wait_pair(&empty[s], (round & 1) ^ 1, abort, peer_abort, &g_lce_error, 1, P.wait_cycles)) { ok = false; break; }
             uint8_t* sa = stage_base + s * kStageBytes;
             const uint32_t leader_full = peer_addr(&full[s], 0);
             if (leader) mbar_expect_tx(&full[s], 2 * kStageBytes);
@@ -137,12 +139,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         item_range(P, item, mt, split, nt0, nt1);
         for (int nt = nt0; ok && nt < nt1; ++nt, ++tcount) {
           const uint32_t b = tcount & 1;
-          if (!mbar_wait_pair(&acce[b], ((tcount >> 1) & 1) ^ 1, abort, peer_abort, &g_lce_error, 2)) { ok = false; break; }
+          if (!mbar_wait_pair(&acce[b], ((tcount >> 1) & 1) ^ 1, abort, peer_abort, &g_lce_error, 2, P.wait_cycles)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t tmem_d = tmem_base + b * kTile;
           for (int kb = 0; kb < P.k_blocks; ++kb, ++it) {
             const int s = it % kStages;
-            if (!mbar_wait_pair(&full[s], (it / kStages) & 1, abort, peer_abort, &g_lce_error, 3)) { ok = false; break; }
+            if (!mbar_wait_pair(&full[s], (it / kStages) & 1, abort, peer_abort, &g_lce_error, 3, P.wait_cycles)) { ok = false; break; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t sa = smem_u32(stage_base + s * kStageBytes);
             const uint32_t sb = sa + kStageA;
@@ -178,7 +180,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int nt = nt0; nt < nt1; ++nt, ++tcount) {
         const uint32_t b = tcount & 1;
         int okw = 1;
-        if (lane == 0) okw = mbar_wait_pair(&accf[b], (tcount >> 1) & 1, abort, peer_abort, &g_lce_error, 4) ? 1 : 0;
+        if (lane == 0) okw = mbar_wait_pair(&accf[b], (tcount >> 1) & 1, abort, peer_abort, &g_lce_error, 4, P.wait_cycles) ? 1 : 0;
         okw = __shfl_sync(0xffffffffu, okw, 0);
         if (!okw) { ok = false; break; }
         __syncwarp();
@@ -379,6 +381,8 @@ int zt_linear_xent(const zt_lce_args* a, void* stream) {
   P.split_tiles = sp.split_tiles;
   P.n_splits = sp.n_splits;
   P.rows_pad = sp.rows_pad;
+  P.stall_loads = a->test_stall_loads ? 1 : 0;
+  P.wait_cycles = a->test_wait_cycles > 0 ? (long long)a->test_wait_cycles : kWaitCycles;
   const int items = sp.m_tiles * sp.n_splits;
   const int clusters = items < pairs ? items : pairs;
   cudaStream_t s = zt::as_stream(stream);

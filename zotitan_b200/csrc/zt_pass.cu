@@ -462,6 +462,12 @@ enum FastZ : int {
   kZLoadStore = 3,  // stream 0 loads, stream 1 stores (in place: load first)
 };
 
+constexpr int32_t kZFlags = ZT_STREAM_Z_LOAD | ZT_STREAM_Z_STORE;
+constexpr int32_t kZSrc = ZT_STREAM_Z_LOAD | ZT_STREAM_Z_FIELD;  // where a stream's z may come from
+
+#ifndef ZT_EARLY_GEN
+#define ZT_EARLY_GEN 1  // generate the next pair's field before applying the cached one
+#endif
 #ifndef ZT_FAST_CHAIN_MINB
 #define ZT_FAST_CHAIN_MINB 5
 #endif
@@ -601,6 +607,20 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) ge[e] = 0.0f;
       }
+      // Fields read from memory are requested one stream ahead, so a load is in flight
+      // while the previous stream's chain (or its noise regeneration) runs.
+      float zn[8];
+      auto prefetch = [&](int s2) {
+        if (s2 < P.n_streams && (P.streams[s2].flags & kZSrc)) {
+          const KStream& T = P.streams[s2];
+          const float* zp = (T.flags & ZT_STREAM_Z_LOAD)
+                                ? c.zcache + (size_t)u * ZT_UNIT_ELEMS + threadIdx.x * 8u
+                                : c.zfield + (size_t)T.zslot * (size_t)c.zfield_stride +
+                                      (size_t)(u - (int32_t)P.unit_begin) * ZT_UNIT_ELEMS + threadIdx.x * 8u;
+          ld_z<8>(zp, zn);
+        }
+      };
+      prefetch(0);
       for (int s = 0; s < P.n_streams; ++s) {
         const KStream& S = P.streams[s];
         const float c0 = S.chain[0], c1 = S.chain[1], c2 = S.chain[2], gc = S.ge_coef;
@@ -618,17 +638,17 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
           ge[e] = ga;
           ge[e + 1] = gb;
         };
-        if (S.flags & (ZT_STREAM_Z_LOAD | ZT_STREAM_Z_FIELD)) {
-          // a field this rank cached (its last own pair) or one pushed into its field store
-          const float* zp = (S.flags & ZT_STREAM_Z_LOAD)
-                                ? c.zcache + (size_t)u * ZT_UNIT_ELEMS + threadIdx.x * 8u
-                                : c.zfield + (size_t)S.zslot * (size_t)c.zfield_stride +
-                                      (size_t)(u - (int32_t)P.unit_begin) * ZT_UNIT_ELEMS + threadIdx.x * 8u;
+        if (S.flags & kZSrc) {
+          // a field this rank cached (its last own pair) or one pushed into its field store,
+          // loaded while the previous stream ran; the next such field is requested now
           float zl[8];
-          ld_z<8>(zp, zl);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) zl[e] = zn[e];
+          prefetch(s + 1);
 #pragma unroll
           for (int e = 0; e < 8; e += 2) apply2(e, zl[e], zl[e + 1]);
         } else {
+          prefetch(s + 1);
           const zt::RoundKeys rk = zt::round_keys(zt::param_key(S.seed, P.n_params, st.index));
 #pragma unroll
           for (int e = 0; e < 8; e += 2)
@@ -675,6 +695,16 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
         for (int k = 0; k < W::kNW; ++k) gw[k] = 0u;  // +0.0 in every format
       }
     }
+    // When stream 0 reads its field from the cache, stream 1's field is generated first:
+    // it needs none of the loaded values, so the loads land while the noise is computed
+    // (applying the streams stays in their order).
+    constexpr bool kEarly = ZT_EARLY_GEN && (ZM & kZLoad) != 0 && SHAPE != kFastChain1;
+    float z1[8];
+    if constexpr (kEarly) {
+      const zt::RoundKeys rk = zt::round_keys(st.key1);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) z1[e] = zt::gauss_rk(e0 + (uint32_t)e, rk);
+    }
     {
       const zt::RoundKeys rk = zt::round_keys(st.key0);
 #pragma unroll
@@ -695,7 +725,7 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
       }
     }
     if (SHAPE != kFastChain1) {
-      const zt::RoundKeys rk = zt::round_keys(st.key1);
+      const zt::RoundKeys rk = zt::round_keys(kEarly ? 0u : st.key1);
 #pragma unroll
       for (int k = 0; k < W::kNW; ++k) {
         float t[W::kPer];
@@ -703,7 +733,7 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
 #pragma unroll
         for (int i = 0; i < W::kPer; ++i) {
           const int e = k * W::kPer + i;
-          const float z = zt::gauss_rk(e0 + (uint32_t)e, rk);
+          const float z = kEarly ? z1[e] : zt::gauss_rk(e0 + (uint32_t)e, rk);
           if (ZM & kZStore) zs[e] = z;
           t[i] = __fmaf_rn(z, a1, t[i]);
         }
@@ -725,8 +755,6 @@ fast_kernel(const __grid_constant__ PassParams P) {
   fast_walk<DT, SHAPE, ZM>(P);
 }
 
-constexpr int32_t kZFlags = ZT_STREAM_Z_LOAD | ZT_STREAM_Z_STORE;
-constexpr int32_t kZSrc = ZT_STREAM_Z_LOAD | ZT_STREAM_Z_FIELD;  // where a stream's z may come from
 
 // Noise-cache variant of a specialised shape: stream 0 may load, the last stream may
 // store; anything else (-1) goes to the generic kernels, which take any placement.

@@ -129,15 +129,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Bounded wait on a barrier of this CTA. On expiry it records `code` in *error, raises
-// this CTA's and the peer CTA's abort flags and returns false; it also returns false as
-// soon as another role of either CTA has aborted.
+// Bounded wait on a barrier of this CTA (at most `limit` clock cycles). On expiry it
+// records `code` in *error, raises this CTA's and the peer CTA's abort flags and returns
+// false; it also returns false as soon as another role of either CTA has aborted.
 __device__ __forceinline__ bool mbar_wait_pair(uint64_t* bar, uint32_t parity, volatile int* abort, uint32_t peer_abort,
-                                               int* error, int code) {
+                                               int* error, int code, long long limit = kWaitCycles) {
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (*abort) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       atomicExch(error, code);
       *abort = 1;
       asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer_abort), "r"(1) : "memory");

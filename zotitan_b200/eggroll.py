@@ -402,9 +402,12 @@ class EggrollPopulation:
             if w.dim() == 2:
                 a, b, scale, *_ = pop.low_rank(i, w.shape[0], w.shape[1], dev, w.dtype)
                 a_cat, b_cat = K.eggroll_update_operands(a, b, scale, coef, sigma)
-                # W <- round(W - lr * a_cat b_cat^T): one GEMM whose epilogue reads W, adds the
-                # fp32 product scaled by -lr and rounds once
-                w.addmm_(a_cat, b_cat.T, beta=1.0, alpha=alpha)
+                # W <- round(W - lr * a_cat b_cat^T): one tensor-core GEMM whose epilogue reads W,
+                # adds the fp32 product scaled by -lr and rounds once (zt_gemm_addto)
+                if K.gemm_addto_supported(w, a_cat.shape[1]):
+                    K.gemm_addto(w, a_cat, b_cat, alpha)
+                else:
+                    w.addmm_(a_cat, b_cat.T, beta=1.0, alpha=alpha)
             elif w.dim() == 1:
                 z = K.randn_keys(pop.keys(i), w.numel(), dev)                    # [P, numel]
                 w.copy_((w.float() + alpha * (coef @ z)).to(w.dtype))

@@ -7,6 +7,7 @@ from __future__ import annotations
 import ctypes
 from dataclasses import dataclass, field
 
+import numpy as np
 import torch
 
 from . import _lib as L
@@ -249,7 +250,7 @@ class ParamTable:
 def eggroll_linear(x: torch.Tensor, w: torch.Tensor, a: torch.Tensor, b: torch.Tensor | None, sigma: torch.Tensor,
                    rows_per_member: int, out: torch.Tensor | None = None, xb: torch.Tensor | None = None,
                    xb_ready: bool = False, x_ext: torch.Tensor | None = None,
-                   w_ext: torch.Tensor | None = None) -> torch.Tensor:
+                   w_ext: torch.Tensor | None = None, test_stall_loads: bool = False) -> torch.Tensor:
     """EGGROLL population linear layer (zt_eggroll_linear):
     Y = X W^T + sigma_i (X B_i) A_i^T for the rows of member i.
 
@@ -257,7 +258,9 @@ def eggroll_linear(x: torch.Tensor, w: torch.Tensor, a: torch.Tensor, b: torch.T
     sigma [members] fp32; returns Y [M, N] bf16. M % 128, N % 256, K % 64 must be 0 and
     rows_per_member a multiple of 128 dividing M. With xb_ready, xb already holds X B_i
     (from eggroll_xb) and b may be None. With x_ext (eggroll_xb_ext) and w_ext (the
-    factors' A_ext) the rank-4 term runs on the tensor cores as a K = 16 slab."""
+    factors' A_ext) the rank-4 term runs on the tensor cores as a K = 16 slab.
+    test_stall_loads: test hook (zt_eggroll_args.test_stall_loads), the GEMM loads nothing
+    and reports an expired wait through eggroll_take_error."""
     if (x_ext is None) != (w_ext is None):
         raise ValueError("x_ext and w_ext go together")
     if x_ext is not None:
@@ -272,7 +275,7 @@ def eggroll_linear(x: torch.Tensor, w: torch.Tensor, a: torch.Tensor, b: torch.T
         if out is None:
             out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
         args = L.ZtEggrollArgs(x.data_ptr(), w.data_ptr(), None, None, None, None, out.data_ptr(), M, N, K,
-                               rows_per_member, 4, 0, 0, x_ext.data_ptr(), w_ext.data_ptr())
+                               rows_per_member, 4, 0, int(test_stall_loads), x_ext.data_ptr(), w_ext.data_ptr())
         with torch.cuda.device(x.device):
             L.check(L.load().zt_eggroll_linear(ctypes.byref(args), _stream_ptr(x.device)), "zt_eggroll_linear")
         return out
@@ -300,7 +303,7 @@ def eggroll_linear(x: torch.Tensor, w: torch.Tensor, a: torch.Tensor, b: torch.T
         xb = torch.empty((M, 4), dtype=torch.float32, device=x.device)
     args = L.ZtEggrollArgs(x.data_ptr(), w.data_ptr(), a.data_ptr(), b.data_ptr() if b is not None else None,
                            sigma.data_ptr(), xb.data_ptr(), out.data_ptr(), M, N, K, rows_per_member, 4,
-                           1 if xb_ready else 0, 0)
+                           1 if xb_ready else 0, int(test_stall_loads))
     with torch.cuda.device(x.device):
         L.check(L.load().zt_eggroll_linear(ctypes.byref(args), _stream_ptr(x.device)), "zt_eggroll_linear")
     return out
@@ -607,6 +610,34 @@ def xent_rows(logits: torch.Tensor, targets: torch.Tensor, want_lse: bool = True
     return loss, lse, correct
 
 
+def gemm_addto(w: torch.Tensor, a: torch.Tensor, b: torch.Tensor, alpha: float) -> torch.Tensor:
+    """In place: w <- bf16(w + alpha * a @ b.T) (zt_gemm_addto), w [m, n], a [m, k], b [n, k]
+    bf16 contiguous; one rounding of w, the product accumulated in fp32 on the tensor cores."""
+    for t, name in ((w, "w"), (a, "a"), (b, "b")):
+        _check_cuda(t, name)
+        if t.dtype != torch.bfloat16 or t.dim() != 2 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous bf16 matrix")
+    m, n = w.shape
+    k = a.shape[1]
+    if a.shape != (m, k) or b.shape != (n, k):
+        raise ValueError("inconsistent shapes")
+    with torch.cuda.device(w.device):
+        L.check(L.load().zt_gemm_addto(w.data_ptr(), n, a.data_ptr(), b.data_ptr(), float(np.float32(alpha)), m, n, k,
+                                       _stream_ptr(w.device)), "zt_gemm_addto")
+    return w
+
+
+def gemm_addto_supported(w: torch.Tensor, k: int) -> bool:
+    return (w.is_cuda and w.dtype == torch.bfloat16 and w.dim() == 2 and w.is_contiguous() and w.shape[1] % 32 == 0
+            and k % 64 == 0 and w.data_ptr() % 16 == 0)
+
+
+def gemm_take_error() -> int:
+    code = ctypes.c_int32(0)
+    L.check(L.load().zt_gemm_take_error(ctypes.byref(code)), "zt_gemm_take_error")
+    return int(code.value)
+
+
 def linear_xent_supported(x: torch.Tensor, w: torch.Tensor) -> bool:
     """Whether zt_linear_xent takes these operands: bf16, contiguous, 16-byte aligned, the
     inner dimension a multiple of 64."""
@@ -619,11 +650,12 @@ _LCE_WS: dict = {}
 
 
 def linear_xent(x: torch.Tensor, w: torch.Tensor, targets: torch.Tensor, want_lse: bool = True,
-                want_correct: bool = True):
+                want_correct: bool = True, test_stall_loads: bool = False, test_wait_cycles: int = 0):
     """Fused lm_head + cross-entropy statistics (zt_linear_xent): x [rows, k] bf16 hidden
     states, w [vocab, k] bf16 head weight, int64 targets [rows] (negative = ignored).
     Returns (loss, lse | None, correct | None) as zt_xent_rows on bf16(x @ w.T) would,
-    without writing the logits."""
+    without writing the logits. test_stall_loads / test_wait_cycles: the test hooks of
+    zt_lce_args (the GEMM loads nothing and reports an expired wait)."""
     if not linear_xent_supported(x, w):
         raise ValueError("x and w must be contiguous 16-byte aligned bf16 CUDA matrices with k % 64 == 0")
     if targets.dtype != torch.int64 or targets.shape != (x.shape[0],) or not targets.is_contiguous():
@@ -646,7 +678,7 @@ def linear_xent(x: torch.Tensor, w: torch.Tensor, targets: torch.Tensor, want_ls
         args = L.ZtLceArgs(x.data_ptr(), w.data_ptr(), targets.data_ptr(), loss.data_ptr(),
                            lse.data_ptr() if lse is not None else None,
                            correct.data_ptr() if correct is not None else None, ws.data_ptr(), ws.numel(), rows,
-                           vocab, k)
+                           vocab, k, int(test_stall_loads), 0, int(test_wait_cycles))
         L.check(lib.zt_linear_xent(ctypes.byref(args), _stream_ptr(dev)), "zt_linear_xent")
     return loss, lse, correct
 

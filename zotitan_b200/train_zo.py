@@ -168,12 +168,10 @@ class StepPlanner:
         self._seed_ctr = 0
         self.rank, self.world = rank, world
         self.sharded = world > 1 if sharded is None else bool(sharded)
-        if self.materialized and self.sharded:
-            raise NotImplementedError("low_rank / polar perturbations run on one rank: the seed-sharded schedule "
-                                      "replays Gaussian fields in its last pass")
-        if self.materialized and cfg.mom.momentum_method == "seed_window":
-            raise NotImplementedError("seed_window momentum regenerates Gaussian fields in registers; "
-                                      "low_rank / polar directions are not supported with it")
+        # the reference refuses this combination itself (zotitan/train_zo.py:268-270)
+        if dist_kind != "gaussian":
+            assert cfg.mom.momentum_method != "seed_window", \
+                "seed_window momentum is incompatible with non-gaussian perturbation distributions"
         # Sharded update: the step's last pass covers only this rank's unit range of a
         # flat parameter layout, followed by an all-gather of the updated master (set by
         # ZOOptimizer when the layout is in place).
@@ -516,7 +514,7 @@ class ZOOptimizer:
         self.vals_buf = torch.zeros(2 * max(1, cfg.z_batch), dtype=torch.float32, device=dev)
         self.layout = None
         one_dtype = len({p.dtype for p in self.params}) == 1
-        if pl.sharded and shard_update and one_dtype:
+        if pl.sharded and shard_update and one_dtype and not pl.materialized:
             from .flat import FlatLayout
             self.layout = FlatLayout([p.numel() for p in self.params], world)
             dt = self.params[0].dtype
@@ -532,20 +530,24 @@ class ZOOptimizer:
             self.theta_0 = self.layout.views(self.flat_master.clone(), shapes) if pl.needs_anchor else None
             self.table = ParamTable(self.master, live=self.params, m=self.m, v=self.v, anchor=self.theta_0)
             pl.unit_ranges = self.layout.shard_ranges(rank)
-        elif pl.sharded:
+        elif pl.sharded and not pl.materialized:
             # model reads `live` (the parameters' own storage); `master` stays unperturbed
             self.master = [p.clone() for p in self.params]
             self.table = ParamTable(self.master, live=self.params, m=self.m, v=self.v, anchor=self.theta_0)
         elif pl.materialized:
-            self.master = None
+            # sharded: the model reads `live` (the parameters); the 1-D tensors' master and the
+            # 2-D tensors' master take the last pass's replay and the update
+            self.master = [p.clone() for p in self.params] if pl.sharded else None
+            own = self.master if pl.sharded else self.params
             n = len(self.params)
             sub = lambda lst, idx: None if lst is None else [lst[i] for i in idx]  # noqa: E731
-            self.table = (ParamTable(sub(self.params, self.dense_idx), n_params=n, indices=self.dense_idx,
+            self.table = (ParamTable(sub(own, self.dense_idx), n_params=n, indices=self.dense_idx,
+                                     live=sub(self.params, self.dense_idx) if pl.sharded else None,
                                      m=sub(self.m, self.dense_idx), v=sub(self.v, self.dense_idx),
                                      anchor=sub(self.theta_0, self.dense_idx), ge=self.ge)
                           if self.dense_idx else None)
             self.lr_ge = [torch.zeros_like(self.params[i]) for i in self.lr_idx]
-            self.lr_table = (ParamTable(sub(self.params, self.lr_idx), n_params=n, indices=self.lr_idx,
+            self.lr_table = (ParamTable(sub(own, self.lr_idx), n_params=n, indices=self.lr_idx,
                                         m=sub(self.m, self.lr_idx), v=sub(self.v, self.lr_idx),
                                         anchor=sub(self.theta_0, self.lr_idx), ge=self.lr_ge)
                              if self.lr_idx else None)
@@ -624,10 +626,26 @@ class ZOOptimizer:
             out.append(z * (p.numel() ** 0.5 / (z.norm() + 1e-7)))
         return out
 
-    def _lr_apply(self, z: list, scale: float) -> None:
-        """_apply_z (:350-351) on the 2-D tensors."""
+    def _lr_apply(self, z: list, scale: float, target=None) -> None:
+        """_apply_z (:350-351) on the 2-D tensors (of `target`, default the parameters)."""
         if self.lr_idx:
-            torch._foreach_add_([self.params[i] for i in self.lr_idx], z, alpha=scale)
+            tgt = self.params if target is None else target
+            torch._foreach_add_([tgt[i] for i in self.lr_idx], z, alpha=scale)
+
+    def _lr_plus_live(self, z: list, scale: float) -> None:
+        """Sharded: live = master + scale * z on the 2-D tensors, rounded once (what the
+        fused +eps pass does for the others)."""
+        for i, zz in zip(self.lr_idx, z):
+            torch.add(self.master[i], zz, alpha=scale, out=self.params[i])
+
+    def _lr_replay_master(self) -> None:
+        """Sharded: every pair's +eps / -2eps / +eps rounding chain on the 2-D tensors'
+        master, in pair order, as the single-GPU parameters went through them."""
+        eps = self.cfg.eps
+        for seed in self.planner.seeds:
+            z = self._lowrank_z(seed)
+            for a in (eps, -2 * eps, eps):
+                self._lr_apply(z, a, target=self.master)
 
     def _lr_finish(self, spec: PassSpec) -> None:
         """grad_est of the 2-D tensors from the regenerated directions with this step's pair
@@ -645,8 +663,10 @@ class ZOOptimizer:
             torch._foreach_zero_(self.lr_ge)
             for j, seed in enumerate(pl.seeds):
                 torch._foreach_add_(self.lr_ge, self._lowrank_z(seed), alpha=coefs[j])
+        # the 2-D tensors' table has no live copy: the sharded schedule copies master -> live after
         cfg = dataclasses.replace(spec.cfg, ge_mode=L.ZT_GE_ACCUM if ge_mode != L.ZT_GE_NONE else L.ZT_GE_NONE,
-                                  ge_load=ge_mode != L.ZT_GE_NONE, ge_store=False, dev_pair=None, dev_vals=0)
+                                  ge_load=ge_mode != L.ZT_GE_NONE, ge_store=False, dev_pair=None, dev_vals=0,
+                                  src=L.ZT_BUF_DATA, dst=L.ZT_BUF_DATA)
         self.lr_table.run(cfg, [])
 
     def _acquire(self, model, batch):
@@ -674,12 +694,17 @@ class ZOOptimizer:
                 self._run(pl.plus_pass(j, prev))
                 if ex is not None:
                     ex.push(j, self._zc)
-                self._lr_apply(z, eps)
+                if pl.sharded:
+                    if z is not None:
+                        self._lr_plus_live(z, eps)
+                else:
+                    self._lr_apply(z, eps)
                 vp, mp = self._acquire(model, batches[j])
                 self._run(pl.minus_pass(j))
                 self._lr_apply(z, -2 * eps)
                 vn, mn = self._acquire(model, batches[j])
-                self._lr_apply(z, eps)
+                if not pl.sharded:
+                    self._lr_apply(z, eps)
                 del z
                 prev = j
                 vp = vp.detach().float().reshape(()).to(dev)
@@ -698,7 +723,12 @@ class ZOOptimizer:
             metrics_avg = _aggregate_metrics(metric_dicts)
         spec, metrics = pl.finish(vals)
         with torch.inference_mode():
+            if pl.sharded and self.lr_idx:
+                self._lr_replay_master()
             self._lr_finish(spec)
+            if pl.sharded and self.lr_idx:
+                for i in self.lr_idx:
+                    self.params[i].copy_(self.master[i])
             if self.layout is not None:
                 # the last pass chunk by chunk on this rank's share; each chunk's in-place
                 # all-gather starts when its pass is done and overlaps the next chunk's pass
