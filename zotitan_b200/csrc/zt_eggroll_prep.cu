@@ -71,6 +71,7 @@ __global__ void __launch_bounds__(kFacThreads) factor_kernel(const __grid_consta
                                                               int32_t b_ext_row) {
   const int j = blockIdx.y;
   const uint32_t ka = pair_key_a(K, j), kb = pair_key_b(K, j);
+  const zt::RoundKeys rka = zt::round_keys(ka), rkb = zt::round_keys(kb);  // once per block
   const int items = n + k;
   float gp[kGram], gq[kGram];
 #pragma unroll
@@ -81,7 +82,9 @@ __global__ void __launch_bounds__(kFacThreads) factor_kernel(const __grid_consta
     float v[4];
     if (i < n) {
 #pragma unroll
-      for (int r = 0; r < 4; ++r) v[r] = zt::Dt<DT>::round(zt::gauss((uint32_t)(4 * i + r), ka));
+      for (int r = 0; r < 4; ++r) v[r] = zt::gauss_rk((uint32_t)(4 * i + r), rka);
+      zt::Dt<DT>::round2(v[0], v[1]);
+      zt::Dt<DT>::round2(v[2], v[3]);
       const float4 f = make_float4(v[0], v[1], v[2], v[3]);
       a0[i] = f;
       a0[i + n] = f;
@@ -99,7 +102,9 @@ __global__ void __launch_bounds__(kFacThreads) factor_kernel(const __grid_consta
     } else {
       const int t = i - n;
 #pragma unroll
-      for (int r = 0; r < 4; ++r) v[r] = zt::Dt<DT>::round(zt::gauss((uint32_t)(r * k + t), kb));
+      for (int r = 0; r < 4; ++r) v[r] = zt::gauss_rk((uint32_t)(r * k + t), rkb);
+      zt::Dt<DT>::round2(v[0], v[1]);
+      zt::Dt<DT>::round2(v[2], v[3]);
       const float4 f = make_float4(v[0], v[1], v[2], v[3]);
       b0[t] = f;
       b0[t + k] = f;
