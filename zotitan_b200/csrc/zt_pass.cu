@@ -468,6 +468,9 @@ constexpr int32_t kZSrc = ZT_STREAM_Z_LOAD | ZT_STREAM_Z_FIELD;  // where a stre
 #ifndef ZT_EARLY_GEN
 #define ZT_EARLY_GEN 1  // generate the next pair's field before applying the cached one
 #endif
+#ifndef ZT_EARLY_GEN0
+#define ZT_EARLY_GEN0 1  // generate a regenerated stream-0 field before unpacking theta
+#endif
 #ifndef ZT_FAST_CHAIN_MINB
 #define ZT_FAST_CHAIN_MINB 5
 #endif
@@ -705,8 +708,17 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) z1[e] = zt::gauss_rk(e0 + (uint32_t)e, rk);
     }
-    {
+    // A stream-0 field that is regenerated is computed before theta is unpacked, so the
+    // loads land while the noise is computed.
+    constexpr bool kEarly0 = ZT_EARLY_GEN0 && (ZM & kZLoad) == 0;
+    float z0[8];
+    if constexpr (kEarly0) {
       const zt::RoundKeys rk = zt::round_keys(st.key0);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) z0[e] = zt::gauss_rk(e0 + (uint32_t)e, rk);
+    }
+    {
+      const zt::RoundKeys rk = zt::round_keys(kEarly0 ? 0u : st.key0);
 #pragma unroll
       for (int k = 0; k < W::kNW; ++k) {
         float t[W::kPer], gg[W::kPer];
@@ -715,7 +727,7 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
 #pragma unroll
         for (int i = 0; i < W::kPer; ++i) {
           const int e = k * W::kPer + i;
-          const float z = (ZM & kZLoad) ? zl[e] : zt::gauss_rk(e0 + (uint32_t)e, rk);
+          const float z = (ZM & kZLoad) ? zl[e] : (kEarly0 ? z0[e] : zt::gauss_rk(e0 + (uint32_t)e, rk));
           if (SHAPE == kFastChain1 && (ZM & kZStore)) zs[e] = z;
           t[i] = __fmaf_rn(z, a0, t[i]);
           if (SHAPE == kFastAccum) gg[i] = __fmaf_rn(z, gcoef, gg[i]);
