@@ -48,6 +48,8 @@ def parse():
                     help="skip timing the reference's own step on the GPU (baseline/reference_steps.py)")
     ap.add_argument("--field-exchange", type=float, default=0.8,
                     help="sharded runs: fraction of free device memory for the field stores (0: regenerate)")
+    ap.add_argument("--exchange-mode", choices=["copies", "in_pass"], default="copies",
+                    help="sharded runs: push the fields by copy-engine copies or from the +eps pass")
     ap.add_argument("--profile-case", choices=["chain", "full", "replay", "chain-cached", "full-cached", "plus-cached",
                                                "replay-field", "replay-mixed", "lce", "eggroll", "eggroll-gated", "eggroll-forward",
                                                "mezo-step", "lora-step"],
@@ -966,7 +968,7 @@ def run_ours(args, rank, local_rank, world):
         def __getitem__(self, i):
             return vals_pinned[i:i + 1].to(dev, non_blocking=True)[0]
 
-    opt = ZOOptimizer(named, cfg, None, field_exchange=args.field_exchange or False)
+    opt = ZOOptimizer(named, cfg, None, field_exchange=args.field_exchange or False, exchange_mode=args.exchange_mode)
     opt.score_fn = global_pair_score(vals_dev, opt.planner, args.seeds)
     rng = np.random.default_rng(12345)   # seeded uint64 seed stream, identical on every rank
     opt.planner._draw_seeds = lambda n: [int(x) for x in rng.integers(0, 2**64 - 1, n, dtype=np.uint64)]
@@ -987,7 +989,10 @@ def run_ours(args, rank, local_rank, world):
     timer.on = True
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
+    stored_per_step = []      # the field exchange's stored-pair count of each timed step
     for _ in range(args.steps):
+        if opt.exchange is not None:
+            stored_per_step.append(opt.exchange.active)
         opt.step(None, batches)
     t1.record()
     barrier()
@@ -1023,8 +1028,9 @@ def run_ours(args, rank, local_rank, world):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             passes[k]["ms_per_step"], passes[k]["ms_per_launch"] = t.tolist()
     cached = opt.zcache is not None
-    exchange = {"pairs_stored": opt.exchange.n_slots, "store_bytes": opt.exchange.store.numel() * 4} \
-        if opt.exchange is not None else None
+    exchange = {"mode": "in_pass" if opt.exchange.in_pass else "copies", "slots": opt.exchange.n_slots,
+                "pairs_stored": opt.exchange.active, "pairs_stored_per_step": stored_per_step,
+                "store_bytes": opt.exchange.store.numel() * 4} if opt.exchange is not None else None
     opt.close()
     del opt, timer
     torch.cuda.empty_cache()

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define ZT_ABI_VERSION 8
+#define ZT_ABI_VERSION 9
 
 /* dtypes of parameter tensors */
 #define ZT_F32 0
@@ -48,6 +48,7 @@ extern "C" {
 #define ZT_MAX_STREAMS 256      /* noise streams per zt_pass call */
 #define ZT_MAX_CHAIN 3          /* perturbation coefficients per stream */
 #define ZT_MAX_NUMEL 2147483647 /* per-tensor element limit (int32 offsets, as the reference) */
+#define ZT_MAX_PUSH_RANKS 8     /* ranks a pass can push a field to (zt_pass_cfg.zpush) */
 
 /* Last error message of the calling host thread ("" if none). */
 ZT_API const char* zt_last_error(void);
@@ -245,11 +246,26 @@ typedef struct zt_pass_cfg {
    *   zfield[s * zfield_stride + (u - unit_begin) * ZT_UNIT_ELEMS ...]
    * (fp32, 16-byte aligned, zfield_stride a multiple of 4 and at least the range's
    * (unit_end - unit_begin) * ZT_UNIT_ELEMS). The seed-sharded step fills it with the
-   * slices of every pair's field that fall on a rank's share of the parameters, pushed
-   * from the ranks' noise caches (zt_copy_async), so its last pass reads every field
-   * instead of regenerating it. NULL when no stream uses it. */
+   * slices of every pair's field that fall on a rank's share of the parameters (pushed by
+   * the ranks' +eps passes, zpush below, or copied from their noise caches with
+   * zt_copy_async), so its last pass reads every field instead of regenerating it. NULL
+   * when no stream uses it. */
   const float* zfield;
   int64_t zfield_stride;
+  /* Push of a stored field into the ranks' field stores, from the pass that generates it
+   * (zpush_ranks > 0): the ZT_STREAM_Z_STORE stream's field is also written, unit by unit,
+   * to the store of the rank that owns the unit, over peer memory (zt_ipc_open mappings):
+   * for a flat layout of `zpush_ranks` ranks cut into chunks of zpush_ranks * C units
+   * (C = zpush_chunk_units; in chunk k rank p owns units [k*R*C + p*C, k*R*C + (p+1)*C)),
+   * unit u of chunk k, offset o in rank p's part, goes to
+   *   zpush[p][zpush_slot * zpush_stride + (k * C + o) * ZT_UNIT_ELEMS ...]
+   * followed by a system-scope fence. Only the specialised +eps pass (one storing stream,
+   * a plan of one dtype with ZT_PLAN_VEC8) takes it; other passes are rejected. */
+  float* zpush[ZT_MAX_PUSH_RANKS];
+  int32_t zpush_ranks;
+  int32_t zpush_slot;
+  int64_t zpush_chunk_units;
+  int64_t zpush_stride;
 } zt_pass_cfg;
 
 /* A pass is rejected (ZT_ERR_INVALID) when cfg reads or writes a buffer (live, m, v,

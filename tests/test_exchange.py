@@ -59,3 +59,64 @@ def test_slots_that_fit():
     assert slots_that_fit(layout, 64, 0) == 0
     assert slots_that_fit(layout, 64, 3 * slot_bytes + 5) == 3
     assert slots_that_fit(layout, 4, 100 * slot_bytes) == 4
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_in_pass_destination_formula_matches_push_plan(world):
+    """The +eps pass kernel's push (zt_pass_cfg.zpush) puts unit u of the flat layout at
+    zpush[p][slot * stride + (kc * C + o) * 2048] with kc = u / (W C), p = (u mod W C) / C,
+    o = u mod C; the copy path's push_plan puts the same unit at the same place."""
+    layout = FlatLayout([5000, 2048 * 3, 8, 2048 * 9 + 8, 24, 40000, 2048 * 70], world)
+    n_units, C, W = layout.units, layout.per, world
+    stride = layout.chunks * C * U
+    slot = 3
+    want = {}
+    for c in push_plan(layout, n_units, slot, world):
+        first_unit = c.src_elem // U
+        for i in range(c.n_elems // U):
+            want[first_unit + i] = (c.dst, c.dst_elem + i * U)
+    got = {}
+    for u in range(n_units):
+        kc, within = divmod(u, W * C)
+        p, o = divmod(within, C)
+        got[u] = (p, slot * stride + (kc * C + o) * U)
+    assert got == want
+
+
+def _bare_exchange(s_max, world=4):
+    from zotitan_b200.exchange import FieldExchange
+    ex = object.__new__(FieldExchange)
+    ex.world, ex.in_pass, ex.adaptive = world, False, True
+    ex.s_max = ex.s = s_max
+    return ex
+
+
+def test_adapt_stores_fewer_pairs_while_pushes_lag_and_cost_more_than_regeneration():
+    ex = _bare_exchange(8)
+    assert ex.active == 32 and ex.stored(31) and not ex.stored(32)
+    ex.adapt(lag=10.0, push=2.0, plus=1.5, local_pairs=8)     # 4 pushes too many -> drop 4
+    assert ex.s == 4 and ex.active == 16
+    ex.adapt(lag=1.5, push=2.0, plus=1.5, local_pairs=8)      # within one push: hold
+    assert ex.s == 4
+    ex.adapt(lag=0.5, push=2.0, plus=1.5, local_pairs=8)      # ends early: one more
+    assert ex.s == 5
+    ex.adapt(lag=10.0, push=1.0, plus=1.5, local_pairs=8)     # pushes cheaper than regenerating: hold
+    assert ex.s == 5
+    ex.adapt(lag=100.0, push=2.0, plus=1.5, local_pairs=8)    # never below zero
+    assert ex.s == 0
+    ex.adapt(lag=0.0, push=0.0, plus=0.0, local_pairs=8)      # nothing measured: hold
+    assert ex.s == 0
+
+
+def test_adapt_caps_at_slots_and_local_pairs():
+    ex = _bare_exchange(3)
+    ex.s = 2
+    ex.adapt(lag=0.0, push=2.0, plus=1.0, local_pairs=2)
+    assert ex.s == 2
+    ex.adapt(lag=0.0, push=2.0, plus=1.0, local_pairs=8)
+    assert ex.s == 3
+    ex.adapt(lag=0.0, push=2.0, plus=1.0, local_pairs=8)
+    assert ex.s == 3
+    ex.adaptive = False
+    ex.adapt(lag=50.0, push=2.0, plus=1.0, local_pairs=8)
+    assert ex.s == 3

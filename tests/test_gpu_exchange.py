@@ -153,21 +153,88 @@ def one_rank_group():
 ONE_DTYPE = ["mezo_bf16_z3", "seedwin_adam_bf16_z2", "ema_adam_f32_z2", "clip_norm_bf16", "wd_anchored_l1_bf16"]
 
 
+@pytest.mark.parametrize("mode", ["in_pass", "copies"])
 @pytest.mark.parametrize("setting", [True, 1])
 @pytest.mark.parametrize("name", ONE_DTYPE)
-def test_sharded_step_with_field_exchange(one_rank_group, name, setting):
+def test_sharded_step_with_field_exchange(one_rank_group, name, setting, mode):
     """The sharded schedule with the field exchange on a one-rank group: the pushes are
-    device-local copies into the store, and the last pass reads the stored fields
+    stores of the +eps pass into the store (in_pass, when the plan takes the specialised
+    kernel) or device-local copies (copies), and the last pass reads the stored fields
     (every pair, or only the first one: the others regenerated); the parameters equal
     the single-GPU step's."""
     from test_gpu_noise_cache import run_opt
     case = StepCase(_G, name)
     _, a1, m1, _ = run_opt(case, noise_cache=False)
-    opt, aw, mw, _ = run_opt(case, sharded=True, noise_cache=True, field_exchange=setting)
+    opt, aw, mw, _ = run_opt(case, sharded=True, noise_cache=True, field_exchange=setting, exchange_mode=mode)
     assert opt.exchange is not None and opt.layout is not None
     assert opt.exchange.n_slots == (case.cfg.z_batch if setting is True else 1)
+    uniform = bool(int(opt.table.plan.props) & 1)
+    assert opt.exchange.in_pass == (mode == "in_pass" and uniform)
     for a, b in zip(aw, a1):
         assert np.array_equal(a, b)
     for x, y in zip(mw, m1):
         assert x["proj_grad"] == y["proj_grad"]
     opt.exchange.close()
+
+
+@pytest.mark.parametrize("world", [2, 3, 4])
+def test_in_pass_push_fills_every_rank_store(K, L, world):
+    """The +eps pass with zt_pass_cfg.zpush on one GPU, `world` local stores standing for
+    the ranks' stores: each store receives exactly the slices push_plan assigns to it (the
+    field zt_randn gives for each tensor's key), NaN everywhere else; the pass's own
+    results (live copy, noise cache) equal the same pass without the push."""
+    from zotitan_b200.exchange import push_plan, store_elems
+    from zotitan_b200.flat import FlatLayout
+    layout = FlatLayout(NUMELS, world)
+    _, va, _ = flat_tables(K, layout, torch.bfloat16, 9)
+    _, vb, _ = flat_tables(K, layout, torch.bfloat16, 9)
+    live_a = [torch.empty_like(v) for v in va]
+    live_b = [torch.empty_like(v) for v in vb]
+    ta, tb = K.ParamTable(va, live=live_a), K.ParamTable(vb, live=live_b)
+    n_units = int(ta.plan.n_units)
+    slots, slot, seed = 3, 2, 2**62 + 17
+    stores = [torch.full((store_elems(layout, slots),), float("nan"), device="cuda") for _ in range(world)]
+    za, zb = ta.noise_cache(), tb.noise_cache()
+    za.fill_(float("nan"))   # a tensor's last unit is written only up to its numel
+    zb.fill_(float("nan"))
+    cfg_a = K.PassCfg(src=L.ZT_BUF_DATA, dst=L.ZT_BUF_LIVE, zcache=za.data_ptr())
+    cfg_b = K.PassCfg(src=L.ZT_BUF_DATA, dst=L.ZT_BUF_LIVE, zcache=zb.data_ptr(),
+                      zpush=tuple(t.data_ptr() for t in stores), zpush_slot=slot,
+                      zpush_chunk_units=layout.per, zpush_stride=layout.chunks * layout.per * 2048)
+    st = [K.Stream(seed, (f(1e-3),), z_store=True)]
+    ta.run(cfg_a, st)
+    tb.run(cfg_b, st)
+    torch.cuda.synchronize()
+    assert all(torch.equal(x, y) for x, y in zip(live_a, live_b))
+    want = [torch.full_like(t, float("nan")) for t in stores]
+    for c in push_plan(layout, n_units, slot, world):
+        want[c.dst][c.dst_elem:c.dst_elem + c.n_elems] = za[c.src_elem:c.src_elem + c.n_elems]
+    for got, w in zip(stores, want):
+        assert torch.equal(torch.nan_to_num(got, nan=7.0), torch.nan_to_num(w, nan=7.0))
+
+
+def test_in_pass_push_argument_errors(K, L):
+    from zotitan_b200.flat import FlatLayout
+    lib = L.load()
+    layout = FlatLayout(NUMELS, 2)
+    _, v, _ = flat_tables(K, layout, torch.bfloat16, 1)
+    live = [torch.empty_like(x) for x in v]
+    t = K.ParamTable(v, live=live)
+    zc = t.noise_cache()
+    store = torch.zeros(1 << 20, device="cuda")
+
+    def rc(streams, **kw):
+        base = dict(src=L.ZT_BUF_DATA, dst=L.ZT_BUF_LIVE, zcache=zc.data_ptr(), zpush_slot=0,
+                    zpush_chunk_units=layout.per, zpush_stride=4096)
+        base.update(kw)
+        cfg = K.PassCfg(**base).to_c()
+        arr = K._streams_array(streams)
+        return lib.zt_pass(ctypes.byref(t.plan), ctypes.byref(cfg), arr, len(streams), None)
+
+    S = K.Stream
+    ok = (store.data_ptr(), store.data_ptr())
+    assert rc([S(1, (f(1e-3),), z_store=True)], zpush=(store.data_ptr() + 4, store.data_ptr())) == L.ZT_ERR_INVALID
+    assert rc([S(1, (f(1e-3),), z_store=True)], zpush=ok, zpush_chunk_units=0) == L.ZT_ERR_INVALID
+    assert rc([S(1, (f(1e-3),))], zpush=ok) == L.ZT_ERR_INVALID                     # no storing stream
+    assert rc([S(1, (f(1e-3), f(1e-3)), z_store=True)], zpush=ok) == L.ZT_ERR_INVALID   # not the +eps shape
+    torch.cuda.synchronize()

@@ -32,7 +32,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version_and_key(lib):
-    assert lib.zt_abi_version() == L.ABI_VERSION == 8
+    assert lib.zt_abi_version() == L.ABI_VERSION == 9
     from oracle import philox as ph
     for seed, n, i in [(0, 1, 0), (1234, 39, 7), (2**40 + 3, 146, 145), (2**64 - 1, 448, 3)]:
         assert lib.zt_param_key(seed, n, i) == ph.param_key(seed, n, i) == (seed * n + i) & 0x7FFFFFFF
@@ -42,8 +42,9 @@ def test_struct_layouts_match_header(lib):
     assert ctypes.sizeof(L.ZtTensor) == 64
     assert ctypes.sizeof(L.ZtStream) == 40
     assert ctypes.sizeof(L.ZtPlan) == 56 and L.ZtPlan.props.offset == 48
-    assert ctypes.sizeof(L.ZtPassCfg) == 152 and L.ZtPassCfg.dev_vals.offset == 88 and L.ZtPassCfg.unit_begin.offset == 112
+    assert ctypes.sizeof(L.ZtPassCfg) == 240 and L.ZtPassCfg.dev_vals.offset == 88 and L.ZtPassCfg.unit_begin.offset == 112
     assert L.ZtPassCfg.zcache.offset == 128 and L.ZtPassCfg.zfield.offset == 136 and L.ZtPassCfg.zfield_stride.offset == 144
+    assert L.ZtPassCfg.zpush.offset == 152 and L.ZtPassCfg.zpush_ranks.offset == 216 and L.ZtPassCfg.zpush_stride.offset == 232
     assert L.ZtStream.zslot.offset == 36
     assert ctypes.sizeof(L.ZtEggrollArgs) == 112 and L.ZtEggrollArgs.xb_ready.offset == 88
     assert ctypes.sizeof(L.ZtEggrollXbArgs) == 152 and L.ZtEggrollXbArgs.bt.offset == 144

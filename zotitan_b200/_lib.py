@@ -16,6 +16,7 @@ ZT_OK, ZT_ERR_INVALID, ZT_ERR_CUDA, ZT_ERR_LIMIT = 0, 1, 2, 3
 ZT_MAX_STREAMS = 256
 ZT_MAX_CHAIN = 3
 ZT_MAX_NUMEL = 2**31 - 1
+ZT_MAX_PUSH_RANKS = 8
 ZT_UNIT_ELEMS = 2048
 ZT_STREAM_GE, ZT_STREAM_MOM, ZT_STREAM_GE_DEV = 1, 2, 4
 ZT_STREAM_Z_STORE, ZT_STREAM_Z_LOAD, ZT_STREAM_Z_FIELD = 8, 16, 32
@@ -37,7 +38,7 @@ EXPORTS = ("zt_last_error", "zt_abi_version", "zt_param_key", "zt_philox_words",
 ZT_STATIC_MAX_TENSORS = 1024
 ZT_EGGROLL_MAX_PAIRS = 512
 ZT_EGGROLL_FACTOR_WORK_FLOATS = 64 * 20
-ABI_VERSION = 8
+ABI_VERSION = 9
 ZT_IPC_HANDLE_BYTES = 64
 
 
@@ -71,7 +72,9 @@ class ZtPassCfg(ctypes.Structure):
                 ("dev_vals", ctypes.c_void_p), ("dev_inv2eps", ctypes.c_float), ("dev_invz", ctypes.c_float),
                 ("dev_tau", ctypes.c_float), ("reserved", ctypes.c_int32), ("unit_begin", ctypes.c_int64),
                 ("unit_end", ctypes.c_int64), ("zcache", ctypes.c_void_p), ("zfield", ctypes.c_void_p),
-                ("zfield_stride", ctypes.c_int64)]
+                ("zfield_stride", ctypes.c_int64), ("zpush", ctypes.c_void_p * ZT_MAX_PUSH_RANKS),
+                ("zpush_ranks", ctypes.c_int32), ("zpush_slot", ctypes.c_int32), ("zpush_chunk_units", ctypes.c_int64),
+                ("zpush_stride", ctypes.c_int64)]
 
 
 class ZtEggrollArgs(ctypes.Structure):

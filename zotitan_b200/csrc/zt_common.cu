@@ -50,6 +50,7 @@ uint32_t zt_param_key(uint64_t seed, uint32_t n_params, uint32_t index) {
 }  // extern "C"
 
 // The ctypes mirror (zotitan_b200/_lib.py) and its layout test assume these sizes.
-static_assert(sizeof(zt_pass_cfg) == 152 && offsetof(zt_pass_cfg, zcache) == 128 && offsetof(zt_pass_cfg, zfield_stride) == 144,
+static_assert(sizeof(zt_pass_cfg) == 240 && offsetof(zt_pass_cfg, zcache) == 128 && offsetof(zt_pass_cfg, zfield_stride) == 144 &&
+                  offsetof(zt_pass_cfg, zpush) == 152 && offsetof(zt_pass_cfg, zpush_stride) == 232,
               "zt_pass_cfg layout");
 static_assert(sizeof(zt_stream) == 40 && sizeof(zt_tensor) == 64, "zt_stream / zt_tensor layout");

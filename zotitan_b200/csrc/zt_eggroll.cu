@@ -21,23 +21,19 @@
 // Every mbarrier wait is bounded by a clock deadline; on expiry the kernel records an
 // error code, stops issuing, drains its own copies and MMAs (again bounded), frees its
 // tensor memory and returns.
-#include <cuda.h>
-
-#include <mutex>
-
-#include "zt_common.cuh"
+#include "zt_tc.cuh"
 
 namespace {
 
-constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
-constexpr int kUmmaK = 16;
+using namespace zt::tc;
+
+constexpr int kBM = 128, kBN = 256, kStages = 4;
 constexpr int kThreadsEgg = 192;  // 6 warps
 constexpr uint32_t kStageA = kBM * kBK * 2;   // 16 KB
 constexpr uint32_t kStageB = kBN * kBK * 2;   // 32 KB
 constexpr uint32_t kStageBytes = kStageA + kStageB;
 constexpr uint32_t kTmemCols = 2 * kBN;       // two fp32 accumulators of 128 x 256
 constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + kStages * kStageBytes + 256 /*barriers, flags*/;
-constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
 constexpr int kGroupN = 16;  // N-blocks per rasterisation group
 
 // Tile order: groups of kGroupN N-blocks; inside a group the M-blocks are swept with the
@@ -76,98 +72,17 @@ struct EggParams {
   int32_t stall_loads;  // test hook: the loader issues no copies (zt_eggroll_args.test_stall_loads)
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait for the completion of the phase with the given parity. Returns false if
-// the deadline passes or another role already aborted (*abort != 0).
+// The library's common mbarrier / TMA / tcgen05 helpers (zt_tc.cuh) with this file's
+// error flag, instruction descriptor and wait bound.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int code) {
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (*abort) return false;
-    if (clock64() - t0 > kWaitCycles) {
-      atomicExch(&g_eggroll_error, code);
-      *abort = 1;
-      return false;
-    }
-  }
-  return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tmap, uint64_t* bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
-      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
-
-// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row groups
-// 1024 bytes apart (stride byte offset), leading byte offset unused (1), descriptor
-// version 1, layout type 2 (SWIZZLE_128B).
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
-// Same for a 32-byte-swizzled K-major tile (rows of 16 bf16): 8-row groups 256 bytes
-// apart, layout type 6 (SWIZZLE_32B).
-__device__ __forceinline__ uint64_t umma_desc32(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(256 >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)6 << 61);
+  return zt::tc::mbar_wait(bar, parity, abort, &g_eggroll_error, code);
 }
 
 // Instruction descriptor: fp32 accumulator, bf16 A and B, both K-major, N = 256, M = 128.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
-                            ((uint32_t)(kBM >> 4) << 24);
+constexpr uint32_t kIdesc = idesc_bf16(kBM, kBN);
 
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  zt::tc::umma_bf16<kIdesc>(tmem_d, adesc, bdesc, accumulate);
 }
 
 __global__ void __launch_bounds__(kThreadsEgg, 1) eggroll_gemm_kernel(const __grid_constant__ EggParams P) {
@@ -340,84 +255,16 @@ constexpr uint32_t kExtTile = kHalfRows * 16 * 2;     // 128 rows of a 16-column
 constexpr uint32_t kOutChunk = 32 * 32 * 2;           // one warp's 32 x 32 bf16 output chunk
 constexpr uint32_t kOutBytes2 = 4 * 2 * kOutChunk;     // 4 epilogue warps x 2 buffers
 constexpr size_t kSmemBytes2 = 1024 + kStages2 * kStageBytes2 + kOutBytes2 + 256;
-constexpr uint32_t kIdesc2 = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
-                             ((uint32_t)(256 >> 4) << 24);
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t cluster_id_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t n_clusters_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
-  return r;
-}
-
-// shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster
-__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
-  return r;
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
-__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* tmap, uint32_t leader_bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
-      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(leader_bar), "r"(x), "r"(y)
-      : "memory");
-}
+constexpr uint32_t kIdesc2 = idesc_bf16(256, 256);
 
 __device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc2), "r"(accumulate)
-      : "memory");
-}
-
-// arrive once on the barrier at this offset in both CTAs of the pair
-__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
-      ::"r"(smem_u32(bar)), "h"((uint16_t)0x3) : "memory");
-}
-
-__device__ __forceinline__ void umma_commit_pair_local(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
+  zt::tc::umma_bf16_pair<kIdesc2>(tmem_d, adesc, bdesc, accumulate);
 }
 
 // Bounded wait that also raises the peer CTA's abort flag when it gives up.
 __device__ __forceinline__ bool mbar_wait_pair(uint64_t* bar, uint32_t parity, volatile int* abort, uint32_t peer_abort,
                                                int code) {
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (*abort) return false;
-    if (clock64() - t0 > kWaitCycles) {
-      atomicExch(&g_eggroll_error, code);
-      *abort = 1;
-      asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer_abort), "r"(1) : "memory");
-      return false;
-    }
-  }
-  return true;
+  return zt::tc::mbar_wait_pair(bar, parity, abort, peer_abort, &g_eggroll_error, code);
 }
 
 // GATED: the pair computes the Llama MLP's gate and up projections of the same 128
@@ -951,39 +798,10 @@ int launch_xb(const void* x, const float* const* b, float* const* xb, int nseg, 
   return zt::check_cuda(cudaGetLastError(), "eggroll xb launch");
 }
 
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
-using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-int get_encode(EncodeFn* fn) {
-  static std::mutex mu;
-  static EncodeFn cached = nullptr;
-  std::lock_guard<std::mutex> lock(mu);
-  if (!cached) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (int rc = zt::check_cuda(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q),
-                                "zt_eggroll_linear: cudaGetDriverEntryPoint"))
-      return rc;
-    if (!p || q != cudaDriverEntryPointSuccess)
-      return zt::set_error(ZT_ERR_CUDA, "zt_eggroll_linear: cuTensorMapEncodeTiled unavailable");
-    cached = reinterpret_cast<EncodeFn>(p);
-  }
-  *fn = cached;
-  return ZT_OK;
-}
+int get_encode(EncodeFn* fn) { return zt::tc::get_encode(fn, "zt_eggroll_linear"); }
 
 int make_map(EncodeFn enc, CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
-  const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {cols * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kBK, box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return zt::set_error(ZT_ERR_CUDA, "zt_eggroll_linear: cuTensorMapEncodeTiled failed");
-  return ZT_OK;
+  return make_map_bf16(enc, map, base, rows, cols, box_rows, "zt_eggroll_linear");
 }
 
 // A 16-column bf16 K-slab [rows, 16]: box {16, 128}, 32-byte swizzle.

@@ -460,6 +460,7 @@ enum FastZ : int {
   kZLoad = 1,       // stream 0 loads
   kZStore = 2,      // the last stream (stream 0 of kFastChain1, stream 1 otherwise) stores
   kZLoadStore = 3,  // stream 0 loads, stream 1 stores (in place: load first)
+  kZPush = 4,       // with kZStore (kFastChain1): the stored field also goes to the owners' stores
 };
 
 constexpr int32_t kZFlags = ZT_STREAM_Z_LOAD | ZT_STREAM_Z_STORE;
@@ -753,6 +754,21 @@ __device__ __forceinline__ void fast_walk(const PassParams& P) {
       }
     }
     if constexpr ((ZM & kZStore) != 0) st_z<8>(zc, zs);
+    if constexpr ((ZM & kZPush) != 0) {
+      // the owner of unit u in the flat layout of zpush_ranks ranks, and the unit's place in
+      // its store (u and the geometry are block-uniform)
+      // (32-bit: this kernel runs on plans of fewer than 2^31 units)
+      const uint32_t cu = (uint32_t)c.zpush_chunk_units;
+      const uint32_t per_chunk = (uint32_t)c.zpush_ranks * cu;
+      const uint32_t kc = (uint32_t)u / per_chunk;
+      const uint32_t within = (uint32_t)u - kc * per_chunk;
+      const uint32_t p = within / cu;
+      const uint32_t o = within - p * cu;
+      float* dst = c.zpush[p] + (size_t)c.zpush_slot * (size_t)c.zpush_stride +
+                   ((size_t)kc * cu + o) * ZT_UNIT_ELEMS + threadIdx.x * 8u;
+      reinterpret_cast<float4*>(dst)[0] = make_float4(zs[0], zs[1], zs[2], zs[3]);
+      reinterpret_cast<float4*>(dst)[1] = make_float4(zs[4], zs[5], zs[6], zs[7]);
+    }
     if (SHAPE == kFastAccum) st_words_global<W::kNW>(st.ge + off, gw);
     if (c.dst & ZT_BUF_DATA) st_words_global<W::kNW>(st.data + off, w);
     if (c.dst & ZT_BUF_LIVE) st_words_global<W::kNW>(st.live + off, w);
@@ -765,6 +781,9 @@ __global__ void __launch_bounds__(ZT_UNIT_ELEMS / 8, SHAPE == kFastAccum    ? ZT
                                                                              : ZT_FAST_CHAIN_MINB)
 fast_kernel(const __grid_constant__ PassParams P) {
   fast_walk<DT, SHAPE, ZM>(P);
+  // pushed fields: this thread's stores to the other GPUs' stores are ordered before
+  // anything the host orders after the kernel (the collective that ends the pair loop)
+  if constexpr ((ZM & kZPush) != 0) __threadfence_system();
 }
 
 
@@ -784,6 +803,12 @@ int fast_zmode(int shape, const zt_stream* s, int32_t n) {
   if (n > 0 && (s[0].flags & ZT_STREAM_Z_LOAD)) zm |= kZLoad;
   if (n > 0 && (s[n - 1].flags & ZT_STREAM_Z_STORE)) zm |= kZStore;
   return zm;
+}
+
+// The push variant applies to the +eps pass that stores its field (kFastChain1, kZStore).
+int fast_zmode_push(int shape, int zm, const zt_pass_cfg* cfg) {
+  if (cfg->zpush_ranks <= 0) return zm;
+  return (shape == kFastChain1 && zm == kZStore) ? (zm | kZPush) : -1;
 }
 
 // The specialised shape a pass matches, ignoring the noise-cache flags, or -1.
@@ -814,7 +839,8 @@ int fast_shape_base(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream
 int fast_shape(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* s, int32_t n) {
   const int shape = fast_shape_base(plan, cfg, s, n);
   if (shape < 0) return -1;
-  const int zm = fast_zmode(shape, s, n);
+  int zm = fast_zmode(shape, s, n);
+  if (zm >= 0) zm = fast_zmode_push(shape, zm, cfg);
   return zm < 0 ? -1 : shape + 16 * zm;
 }
 
@@ -831,7 +857,7 @@ int grid_for(K kernel, int threads, int64_t n_units, std::atomic<int>& occ_cache
 }
 
 std::atomic<int> g_occ_chain{0}, g_occ_full{0};
-std::atomic<int> g_occ_fast[3][kFastShapes][4];
+std::atomic<int> g_occ_fast[3][kFastShapes][8];
 
 template <int DT, int SHAPE, int ZM>
 void launch_fast_one(const PassParams& P, int64_t units, cudaStream_t s) {
@@ -846,6 +872,7 @@ bool launch_fast(int code, const PassParams& P, int64_t units, cudaStream_t s) {
     case kFastChain1: launch_fast_one<DT, kFastChain1, kZNone>(P, units, s); return true;
     case kFastChain1 + 16 * kZLoad: launch_fast_one<DT, kFastChain1, kZLoad>(P, units, s); return true;
     case kFastChain1 + 16 * kZStore: launch_fast_one<DT, kFastChain1, kZStore>(P, units, s); return true;
+    case kFastChain1 + 16 * (kZStore | kZPush): launch_fast_one<DT, kFastChain1, kZStore | kZPush>(P, units, s); return true;
     case kFastChain2: launch_fast_one<DT, kFastChain2, kZNone>(P, units, s); return true;
     case kFastChain2 + 16 * kZLoadStore: launch_fast_one<DT, kFastChain2, kZLoadStore>(P, units, s); return true;
     case kFastAccum: launch_fast_one<DT, kFastAccum, kZNone>(P, units, s); return true;
@@ -1059,6 +1086,23 @@ int pass_run(const zt_plan* plan, const zt_pass_cfg* cfg, const zt_stream* strea
     } else {
       P.cfg.zfield = nullptr;
       P.cfg.zfield_stride = 0;
+    }
+    if (cfg->zpush_ranks != 0) {
+      if (cfg->zpush_ranks < 0 || cfg->zpush_ranks > ZT_MAX_PUSH_RANKS)
+        return zt::set_error(ZT_ERR_INVALID, "zt_pass: zpush_ranks outside [0, ZT_MAX_PUSH_RANKS]");
+      for (int p = 0; p < cfg->zpush_ranks; ++p)
+        if (!cfg->zpush[p] || ((uintptr_t)cfg->zpush[p] & 15u) != 0)
+          return zt::set_error(ZT_ERR_INVALID, "zt_pass: every zpush store must be a 16-byte aligned pointer");
+      if (cfg->zpush_chunk_units <= 0 || cfg->zpush_chunk_units * cfg->zpush_ranks > (int64_t)INT32_MAX ||
+          cfg->zpush_slot < 0 || cfg->zpush_stride < 0 || cfg->zpush_stride % 4 != 0)
+        return zt::set_error(ZT_ERR_INVALID, "zt_pass: bad zpush geometry (chunk units, slot, stride)");
+      const int32_t uni = plan->props & (ZT_PLAN_ALL_F32 | ZT_PLAN_ALL_BF16 | ZT_PLAN_ALL_F16);
+      if (!uni || fast_shape(plan, cfg, streams, n_streams) != kFastChain1 + 16 * (kZStore | kZPush))
+        return zt::set_error(ZT_ERR_INVALID,
+                             "zt_pass: zpush needs the specialised +eps pass (one storing stream, one chain "
+                             "coefficient, a plan of one dtype with ZT_PLAN_VEC8)");
+    } else {
+      for (int p = 0; p < ZT_MAX_PUSH_RANKS; ++p) P.cfg.zpush[p] = nullptr;
     }
   }
   if (!launch) return ZT_OK;

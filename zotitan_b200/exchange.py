@@ -6,11 +6,25 @@ generates the Gaussian field of each of its own pairs over every parameter in th
 pair's +eps pass (the forward needs all of them perturbed), and the step's last pass on
 rank r replays every pair's rounding chain on r's share of the parameters. Regenerating
 those fields there doubles the noise work of the step (the passes are bound by
-instruction issue, one Philox4x32-10 + log/cos per element). Here the +eps pass keeps its
-field in a noise cache, and copy-engine copies push the slice of it that falls on each
-rank's share into that rank's *field store* (``zt_pass_cfg.zfield``). The copies run on
-the copy engines over NVLink (peer mappings through CUDA IPC) and overlap the next pair's
-passes; the last pass then reads every stored field from HBM.
+instruction issue, one Philox4x32-10 + log/cos per element). Instead every pair's field
+lands in the *field stores* (``zt_pass_cfg.zfield``) of the ranks that replay it, and the
+last pass reads every stored field from HBM. Two ways of getting it there:
+
+- by copies (the default): the +eps pass keeps its field in a noise cache and copy-engine
+  copies (``zt_copy_async``) push the slices into the stores, overlapping the next pairs'
+  passes; two or three caches rotate between a rank's pairs;
+- in the pass (``in_pass``, when the plan takes the specialised +eps kernel and there are
+  at most ZT_MAX_PUSH_RANKS ranks): the +eps pass that generates the field also stores
+  each unit of it straight into the owning rank's store over NVLink (``zt_pass_cfg.zpush``,
+  peer mappings through CUDA IPC), then fences at system scope. Measured at 4 ranks it
+  made the +eps pass the bottleneck (193 against 157 ms per step by copies): the remote
+  stores run at the all-to-all rate, ~350-400 GB/s per GPU, and hold the pass's warps.
+
+The all-to-all rate bounds what the copies can carry: at 4 ranks one pair's push costs
+about as much as regenerating its field. So the number of stored pairs adapts (``adapt``):
+each rank times how long its pushes ran past its local passes in the previous step, the
+timings ride on the pair-value all-gather, and every rank applies the same rule to the
+same maxima, so the count changes between steps and identically everywhere.
 
 Store layout on each rank: ``n_slots`` slots (pairs j < n_slots are stored, the same on
 every rank), each holding the rank's share in chunk order: chunk k's C units at
@@ -18,13 +32,13 @@ every rank), each holding the rank's share in chunk order: chunk k's C units at
 launch over chunk k then passes ``zfield = store + k * C * 2048`` and reads unit u at
 ``(u - unit_begin) * 2048`` of a slot, as zt_pass documents.
 
-Ordering (no kernel waits on another rank; the collectives order the copies):
-- a pair's pushes start after its +eps pass (event on the compute stream) and the noise
-  cache they read is reused two pairs later only after they finished (two caches
-  alternate);
+Ordering (no kernel waits on another rank; the collectives order the pushes):
+- copies: a pair's pushes start after its +eps pass (event on the compute stream) and the
+  noise cache they read is reused two pairs later only after they finished;
 - every push of a step finishes before this rank's all-gather of the pair values starts
-  (the compute stream waits for the push streams), so a rank whose all-gather completed
-  knows every rank's pushes into its store have landed;
+  (in the pass: the +eps kernels precede it on the compute stream and end with a
+  system-scope fence; copies: the compute stream waits for the copy streams), so a rank
+  whose all-gather completed knows every rank's pushes into its store have landed;
 - pushes of the next step start after this rank's parameter all-gather completed, which
   needs every rank's contribution, sent only after that rank's last pass had read its
   store.
@@ -95,7 +109,7 @@ class FieldExchange:
     budget; the slot count is the smallest any rank can hold."""
 
     def __init__(self, layout, n_units: int, rank: int, world: int, z_batch: int, device, budget_bytes: int,
-                 group=None):
+                 group=None, in_pass: bool = False):
         import torch.distributed as dist
         self.layout, self.n_units, self.rank, self.world = layout, n_units, rank, world
         self.device = torch.device(device)
@@ -126,33 +140,112 @@ class FieldExchange:
                 ptrs[p] = base.value + o
         self.peer_store = ptrs
         self.group = group
+        self.in_pass = bool(in_pass) and world <= L.ZT_MAX_PUSH_RANKS
         self.plans = [push_plan(layout, n_units, j, world) for j in range(self.n_slots)]
         # one copy stream per destination: the copies to different peers run side by side
         self.streams = [torch.cuda.Stream(self.device) for _ in range(world)]
         self._last = [None] * world          # last push event per destination
         self._by_cache = {}                  # cache address -> push events that read it
+        # Stored pairs in use: pairs j < active = s * world, i.e. the first s own pairs of
+        # every rank (pairs go round-robin: pair j is rank j % W's (j // W)-th). Every rank
+        # updates s with the same rule from the same all-gathered timings (adapt).
+        self.s_max = self.n_slots // world
+        self.s = self.s_max
+        self.adaptive = not self.in_pass
+        self._cur = self._prev = None
+
+    @property
+    def active(self) -> int:
+        return self.s * self.world
 
     def stored(self, j: int) -> bool:
-        return j < self.n_slots
+        return j < self.active
+
+    # -- timing of the copies against the local passes, for the stored-pair count --------
+    def begin_step(self) -> None:
+        """Start the step's timing record (the previous step's is kept for stats())."""
+        self._prev, self._cur = self._cur, {"push_start": None, "push_end": [], "plus": None, "local_done": None,
+                                            "pushed": 0}
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(self.device))
+        self._cur["start"] = ev
+
+    def note_plus(self, before, after) -> None:
+        """Events around one +eps pass of the step (its duration is the cost of
+        regenerating one pair's worth of noise)."""
+        if self._cur is not None and self._cur["plus"] is None:
+            self._cur["plus"] = (before, after)
+
+    def local_done(self) -> None:
+        if self._cur is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(torch.cuda.current_stream(self.device))
+            self._cur["local_done"] = ev
+
+    def stats(self) -> tuple[float, float, float]:
+        """(lag, push, plus) in ms from the previous step: how long its pushes ran past the
+        end of its local passes, the copy time of one pair's push at the rate it sustained,
+        and one +eps pass. Zeros when there is nothing to report."""
+        t = self._prev
+        if not self.adaptive or t is None or t["push_start"] is None or not t["push_end"] or t["plus"] is None \
+                or t["local_done"] is None or t["pushed"] == 0:
+            return 0.0, 0.0, 0.0
+        evs = [t["push_start"], t["local_done"], *t["push_end"], *t["plus"]]
+        if not all(e.query() for e in evs):
+            return 0.0, 0.0, 0.0
+        end = max(t["push_start"].elapsed_time(e) for e in t["push_end"])      # first push start -> last end
+        lag = max(0.0, end - t["push_start"].elapsed_time(t["local_done"]))
+        push = end / t["pushed"]
+        plus = t["plus"][0].elapsed_time(t["plus"][1])
+        return lag, push, plus
+
+    def adapt(self, lag: float, push: float, plus: float, local_pairs: int) -> None:
+        """Update the stored own-pair count s from the all-gathered maxima of stats(): while
+        the pushes run more than one pair's push past the local passes and a pair's push
+        costs more than regenerating its noise in the last pass (about one +eps pass), store
+        fewer pairs; when they end within half a push, store one more."""
+        if not self.adaptive or push <= 0.0:
+            return
+        s_cap = min(self.s_max, local_pairs)
+        if lag > push and push > plus and self.s > 0:
+            self.s = max(0, self.s - max(1, int((lag - push) / push + 0.999)))
+        elif lag < 0.5 * push and self.s < s_cap:
+            self.s += 1
+
+    def set_push(self, cfg, j: int) -> None:
+        """In-pass mode: point the +eps pass of pair j (a kernels.PassCfg) at slot j of every
+        rank's store, if pair j is stored."""
+        if self.in_pass and self.stored(j):
+            cfg.zpush = tuple(self.peer_store)
+            cfg.zpush_slot = j
+            cfg.zpush_chunk_units = self.layout.per
+            cfg.zpush_stride = self.layout.chunks * self.layout.per * U
 
     def chunk_field(self, k: int) -> tuple[int, int]:
         return chunk_field(self.layout, self.store.data_ptr(), k)
 
     def before_cache_write(self, cache: torch.Tensor) -> None:
         """The compute stream waits until the pushes reading `cache` are done."""
+        if self.in_pass:
+            return
         cur = torch.cuda.current_stream(self.device)
         for ev in self._by_cache.pop(cache.data_ptr(), []):
             cur.wait_event(ev)
 
     def push(self, j: int, cache: torch.Tensor) -> None:
         """Push pair j's field (in `cache`, written by work already on the compute stream)
-        to every rank's store."""
-        if not self.stored(j):
+        to every rank's store (copies; in-pass mode pushes from the +eps pass itself)."""
+        if self.in_pass or not self.stored(j):
             return
         lib = L.load()
         cur = torch.cuda.current_stream(self.device)
-        ready = torch.cuda.Event()
+        timing = self.adaptive and self._cur is not None
+        ready = torch.cuda.Event(enable_timing=timing)
         ready.record(cur)
+        if timing:
+            if self._cur["push_start"] is None:
+                self._cur["push_start"] = ready
+            self._cur["pushed"] += 1
         src = cache.data_ptr()
         evs = []
         by_dst: dict[int, list[Copy]] = {}
@@ -164,11 +257,13 @@ class FieldExchange:
             for c in copies:
                 L.check(lib.zt_copy_async(self.peer_store[p] + 4 * c.dst_elem, src + 4 * c.src_elem, 4 * c.n_elems,
                                           ctypes.c_void_p(s.cuda_stream)), "zt_copy_async")
-            ev = torch.cuda.Event()
+            ev = torch.cuda.Event(enable_timing=timing)
             ev.record(s)
             self._last[p] = ev
             evs.append(ev)
         self._by_cache.setdefault(src, []).extend(evs)
+        if timing:
+            self._cur["push_end"] = [e for e in self._last if e is not None]
 
     def finish_pushes(self) -> None:
         """The compute stream waits for every push issued so far (before the step's

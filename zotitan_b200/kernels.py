@@ -131,6 +131,10 @@ class PassCfg:
     zcache: int = 0                 # device address of the plan's noise cache (n_units x 2048 fp32)
     zfield: int = 0                 # device address of the field store of the pass's unit range
     zfield_stride: int = 0          # fp32 elements between two slots of the field store
+    zpush: tuple = ()               # per rank: device address (peer mapping) of its field store
+    zpush_slot: int = 0             # slot the pushed field goes to
+    zpush_chunk_units: int = 0      # units of one rank in one chunk of the flat layout
+    zpush_stride: int = 0           # fp32 elements between two slots of a store
 
     def to_c(self) -> L.ZtPassCfg:
         c = L.ZtPassCfg()
@@ -148,6 +152,13 @@ class PassCfg:
         c.zcache = self.zcache or None
         c.zfield = self.zfield or None
         c.zfield_stride = self.zfield_stride
+        if self.zpush:
+            if len(self.zpush) > L.ZT_MAX_PUSH_RANKS:
+                raise ValueError(f"zpush: at most {L.ZT_MAX_PUSH_RANKS} ranks")
+            for i, ptr in enumerate(self.zpush):
+                c.zpush[i] = ptr
+            c.zpush_ranks = len(self.zpush)
+            c.zpush_slot, c.zpush_chunk_units, c.zpush_stride = self.zpush_slot, self.zpush_chunk_units, self.zpush_stride
         return c
 
 

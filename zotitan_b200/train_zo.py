@@ -479,11 +479,17 @@ class ZOOptimizer:
     results are bit-identical either way. None (default): on with more than one rank,
     storing as many pairs as fit in half of the free device memory; a float sets that
     fraction and an int (not a bool) the number of stored pairs; True also runs it on a
-    one-rank group; False regenerates every field."""
+    one-rank group; False regenerates every field. ``exchange_mode``: "copies" (copy-engine
+    copies from the noise cache, overlapping the next pair's passes; the stored-pair count
+    adapts step by step to the copy bandwidth) or "in_pass" (the +eps pass stores its
+    field into the owners' stores over NVLink itself, when its plan takes the specialised
+    kernel)."""
 
     def __init__(self, named_params: list, cfg: ZOConfig, score_fn, total_steps: int = 0, process_group=None,
                  sharded: bool | None = None, shard_update: bool = True, noise_cache: bool | None = None,
-                 field_exchange: bool | float | None = None):
+                 field_exchange: bool | float | None = None, exchange_mode: str = "copies"):
+        if exchange_mode not in ("copies", "in_pass"):
+            raise ValueError(f"exchange_mode must be 'copies' or 'in_pass', got {exchange_mode!r}")
         self.named_params = named_params
         self.params = [p.data for _, p in named_params]
         self.cfg = cfg
@@ -564,17 +570,27 @@ class ZOOptimizer:
         if (self.layout is not None and self.zcache is not None and field_exchange is not False
                 and (world > 1 or field_exchange is not None)):
             from .exchange import FieldExchange, slot_bytes
-            # two caches alternate between a rank's pairs, so a pair's pushes overlap the
-            # next pair's passes
-            self.zcaches = [self.zcache, self.table.noise_cache()]
+            # the +eps pass pushes its field itself when the plan takes the specialised kernel
+            props = int(self.table.plan.props)
+            cache_bytes = 4 * int(self.table.plan.n_units) * L.ZT_UNIT_ELEMS
+            in_pass = bool(props & L.ZT_PLAN_VEC8) and bool(props & (L.ZT_PLAN_ALL_F32 | L.ZT_PLAN_ALL_BF16
+                                                                     | L.ZT_PLAN_ALL_F16))
+            in_pass = in_pass and world <= L.ZT_MAX_PUSH_RANKS and exchange_mode == "in_pass"
+            # with copies, caches rotate between a rank's pairs, so a pair's pushes overlap the
+            # next pairs' passes (three when memory allows: measured 157 against 164 ms per step
+            # with two at 4 ranks)
+            self.zcaches = [self.zcache]
+            if not in_pass:
+                n_caches = 3 if 4 * cache_bytes <= torch.cuda.mem_get_info(dev)[0] else 2
+                self.zcaches += [self.table.noise_cache() for _ in range(n_caches - 1)]
             if type(field_exchange) is int:
                 budget = field_exchange * slot_bytes(self.layout)
             else:
                 frac = field_exchange if isinstance(field_exchange, float) else 0.5
                 budget = int(frac * torch.cuda.mem_get_info(dev)[0])
             self.exchange = FieldExchange(self.layout, int(self.table.plan.n_units), rank, world, cfg.z_batch, dev,
-                                          budget, group=process_group)
-            pl.field_slots = self.exchange.n_slots
+                                          budget, group=process_group, in_pass=in_pass)
+            pl.field_slots = self.exchange.active
         self._metric_keys = None
 
     def close(self) -> None:
@@ -685,13 +701,27 @@ class ZOOptimizer:
         prev = None
         eps = self.cfg.eps
         ex = self.exchange
+        if ex is not None:
+            ex.begin_step()
+            pl.field_slots = ex.active      # the stored pairs of this step (pushes and last pass)
         with torch.inference_mode():
             for k, j in enumerate(local):
                 z = self._lowrank_z(pl.seeds[j]) if self.lr_idx else None
                 if ex is not None:
-                    self._zc = self.zcaches[k % 2]
+                    self._zc = self.zcaches[k % len(self.zcaches)]
                     ex.before_cache_write(self._zc)
-                self._run(pl.plus_pass(j, prev))
+                spec = pl.plus_pass(j, prev)
+                timed = ex is not None and ex.adaptive and k == 0
+                if timed:
+                    t0 = torch.cuda.Event(enable_timing=True)
+                    t0.record()
+                if ex is not None:
+                    ex.set_push(spec.cfg, j)
+                self._run(spec)
+                if timed:
+                    t1 = torch.cuda.Event(enable_timing=True)
+                    t1.record()
+                    ex.note_plus(t0, t1)
                 if ex is not None:
                     ex.push(j, self._zc)
                 if pl.sharded:
@@ -715,6 +745,7 @@ class ZOOptimizer:
                 vals_t += [vp, vn]
                 metric_dicts += [mp, mn]
         if ex is not None:
+            ex.local_done()
             ex.finish_pushes()    # every push lands before the all-gather that ends the pair loop
         if pl.sharded:
             vals, metrics_avg = self._gather(vals_t, metric_dicts, local)
@@ -760,8 +791,12 @@ class ZOOptimizer:
             self._metric_keys = sorted({k for ks in allk for k in ks})
         keys = self._metric_keys
         dev = self.params[0].device
-        C = 2 + 2 * len(keys)
+        ex = self.exchange
+        n_ex = 3 if ex is not None and ex.adaptive else 0   # the field exchange's timings ride along
+        C = 2 + 2 * len(keys) + n_ex
         rows = torch.full((len(local), C), float("nan"), dtype=torch.float32, device=dev)
+        if n_ex and len(local):
+            rows[:, C - n_ex:] = torch.tensor(ex.stats(), dtype=torch.float32)
         for r in range(len(local)):
             rows[r, 0] = vals_t[2 * r]
             rows[r, 1] = vals_t[2 * r + 1]
@@ -773,6 +808,10 @@ class ZOOptimizer:
                         rows[r, 2 + 2 * k_i + s] = v.detach().float() if isinstance(v, torch.Tensor) else float(v)
         allrows = gather_pair_values(rows, self.cfg.z_batch, self.rank, self.world, self.group).cpu().tolist()
         vals = [x for row in allrows for x in row[:2]]
+        if n_ex:   # the same maxima on every rank, so every rank takes the same stored-pair count
+            mx = [max((row[C - n_ex + i] for row in allrows if not math.isnan(row[C - n_ex + i])), default=0.0)
+                  for i in range(n_ex)]
+            ex.adapt(*mx, local_pairs=-(-self.cfg.z_batch // self.world))
         metrics = {}
         for k_i, k in enumerate(keys):
             xs = [x for row in allrows for x in row[2 + 2 * k_i: 4 + 2 * k_i] if not math.isnan(x)]
