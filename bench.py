@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--exchange-mode", choices=["copies", "in_pass"], default="copies",
                     help="sharded runs: push the fields by copy-engine copies or from the +eps pass")
     ap.add_argument("--profile-case", choices=["chain", "full", "replay", "chain-cached", "full-cached", "plus-cached",
-                                               "replay-field", "replay-mixed", "lce", "eggroll", "eggroll-gated", "eggroll-forward",
+                                               "replay-field", "replay-mixed", "lce", "lowrank", "eggroll", "eggroll-gated", "eggroll-forward",
                                                "mezo-step", "lora-step"],
                     default=None,
                     help="small case for ncu: one bf16 tensor of 2^28 elements, 3 launches of the "
@@ -117,6 +117,58 @@ def eggroll_gemm_bench(rows: int = 16384, T: int = 1024, reps: int = 10):
     assert K_.eggroll_take_error() == 0
     print(json.dumps({"eggroll_gemm": res, "peak_tflops": peak,
                       "peak_source": "MEASURED_PEAKS.json bf16_tflops" if "bf16_tflops" in peaks else "fallback"}))
+
+
+def _profile_lowrank():
+    """The fused low-rank direction (zt_lowrank_prepare / zt_lowrank_apply) on a
+    [16384, 8192] bf16 matrix (268 MB, larger than L2) at rank 64, against the reference's
+    materialised ops (P @ Psi on cuBLAS, norm, scale, foreach add). Algorithmic bytes of
+    one apply: the parameter read and written, 4 B per element."""
+    import torch
+
+    from zotitan_b200 import kernels as K
+    from zotitan_b200.kernels import param_key, randn
+    m, n, r = 16384, 8192, 64
+    g = torch.Generator(device="cuda").manual_seed(0)
+    theta = (torch.randn(m, n, device="cuda", generator=g) * 0.02).bfloat16()
+    ge = torch.zeros_like(theta)
+    keys = [param_key(s, 3, 0) for s in range(8)], [param_key(s, 3, 1) for s in range(8)]
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    def timed(fn, reps):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        a, b = ev(), ev()
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    one = K.LowRankFactors((m, n), r, torch.bfloat16, keys[0][:1], keys[1][:1], "cuda")
+    ms_prep = timed(lambda: K.LowRankFactors((m, n), r, torch.bfloat16, keys[0][:1], keys[1][:1], "cuda"), 5)
+    ms_apply = timed(lambda: one.apply(src=theta, dst=theta, alphas=(1e-3,)), 10)
+    eight = K.LowRankFactors((m, n), r, torch.bfloat16, keys[0], keys[1], "cuda")
+    ms_ge8 = timed(lambda: eight.apply(ge=ge, coefs=[0.1] * 8, ge_init=True), 5)
+
+    def materialised():
+        P = randn(keys[0][0], m * r, "cuda").view(m, r).bfloat16()
+        Psi = randn(keys[1][0], r * n, "cuda").view(r, n).bfloat16()
+        z = P @ Psi
+        z = z * ((m * n) ** 0.5 / (z.norm() + 1e-7))
+        torch._foreach_add_([theta], [z], alpha=1e-3)
+    ms_mat = timed(materialised, 5)
+    try:
+        peak = json.load(open(os.path.join(HERE, "MEASURED_PEAKS.json")))["hbm_gbs"]
+    except (OSError, ValueError, KeyError):
+        peak = 6650.0
+    gbs = 4.0 * m * n / ms_apply / 1e6
+    print(json.dumps({"profile_case": "lowrank", "shape": [m, n], "rank": r, "ms_prepare": ms_prep,
+                      "ms_apply": ms_apply, "apply_gbs": gbs, "apply_frac_of_measured_hbm": gbs / peak,
+                      "ms_ge_8_streams": ms_ge8, "ms_materialised_one_use": ms_mat,
+                      "error": K.lowrank_take_error()}))
 
 
 def _profile_step(kind: str):
@@ -220,6 +272,9 @@ def profile_case(kind: str):
         flops = 2.0 * rows * vocab * k
         print(json.dumps({"profile_case": kind, "ms": ms, "tflops": flops / ms / 1e9, "ms_gemm_then_xent": ms_old,
                           "tflops_gemm_then_xent": flops / ms_old / 1e9, "error": K.linear_xent_take_error()}))
+        return
+    if kind == "lowrank":   # one low_rank direction of a [16384, 8192] bf16 matrix, rank 64
+        _profile_lowrank()
         return
     n = 1 << 28
     p = (torch.randn(n, device="cuda") * 0.02).bfloat16()

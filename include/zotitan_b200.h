@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define ZT_ABI_VERSION 9
+#define ZT_ABI_VERSION 10
 
 /* dtypes of parameter tensors */
 #define ZT_F32 0
@@ -587,6 +587,63 @@ ZT_API int zt_linear_xent(const zt_lce_args* args, void* stream);
 /* Reads and clears the fused scorer's device error flag (nonzero: a bounded wait inside
  * the GEMM expired; its outputs are then incomplete). Synchronises with the device. */
 ZT_API int zt_linear_xent_take_error(int32_t* code);
+
+/* ---- low-rank directions (distribution "low_rank") on the tensor cores ----------- */
+
+/* Replaces the materialised direction of _sample_z for a 2-D parameter
+ * (zotitan/train_zo.py:295-322): P = randn(key_p, m r).view(m, r).to(dtype),
+ * Psi = randn(key_psi, r n).view(r, n).to(dtype), z = P @ Psi, then
+ * z * (sqrt(m n) / (||z||_F + 1e-7)), and its uses in _apply_z (:350-351) and the grad
+ * estimate (:550-556, :575-577), without z ever being written to memory. One parameter of
+ * dtype ZT_BF16 or ZT_F16 at a time, for n_streams pair seeds at once. The product is the
+ * fp32 sum of the r exact products in K order, rounded to the dtype: an element can differ
+ * by one unit in the last place from a library GEMM that sums in another order. */
+#define ZT_LOWRANK_MAX_STREAMS 128
+
+typedef struct zt_lowrank_desc {
+  int64_t m, n;     /* parameter shape, row-major, contiguous */
+  int32_t r;        /* rank used: min(rank, m); 1 <= r <= kp */
+  int32_t kp;       /* padded rank: a multiple of 64, at most 1024 */
+  int32_t dtype;    /* ZT_BF16 or ZT_F16 */
+  int32_t n_streams; /* 1..ZT_LOWRANK_MAX_STREAMS */
+  uint32_t keys_p[ZT_LOWRANK_MAX_STREAMS];   /* noise key of P per stream: position i + 2N (:311) */
+  uint32_t keys_psi[ZT_LOWRANK_MAX_STREAMS]; /* noise key of Psi per stream: position i + N (:315) */
+  void* p;          /* device [n_streams * m, kp] dtype, 16-byte aligned: P of each stream, zero-padded */
+  void* psi_t;      /* device [n_streams * n, kp] dtype, 16-byte aligned: Psi transposed, zero-padded */
+  float* scale;     /* device [n_streams]: the dtype-rounded scale of each stream's product */
+  void* workspace;  /* device, zt_lowrank_workspace_bytes, 16-byte aligned (zt_lowrank_prepare) */
+  size_t workspace_bytes;
+} zt_lowrank_desc;
+
+typedef struct zt_lowrank_apply_args {
+  const void* src;  /* parameter read by stream 0 (later streams read dst); may equal dst */
+  void* dst;        /* parameter written; NULL: the parameter is not updated (n_alpha 0) */
+  void* ge;         /* grad estimate [m, n] dtype, or NULL */
+  int32_t n_alpha;  /* 0..3: per stream, theta <- round(theta + alpha[t] z) for t < n_alpha */
+  float alpha[3];
+  int32_t ge_init;  /* 1: stream 0 sets ge = round(coef[0] z); else every stream adds round(ge + coef z) */
+  float coef[ZT_LOWRANK_MAX_STREAMS]; /* grad-estimate coefficient per stream */
+  int32_t test_stall_loads; /* test hook: the loader issues no copies, every wait expires (0 normally) */
+  int32_t reserved;
+  int64_t test_wait_cycles; /* bound of each wait in clock cycles; 0: about two seconds */
+} zt_lowrank_apply_args;
+
+ZT_API int zt_lowrank_workspace_bytes(int64_t m, int64_t n, int32_t n_streams, size_t* bytes);
+
+/* Writes d->p, d->psi_t and d->scale: the factors of every stream from the noise source,
+ * then the product's sum of squares (tensor cores, the product never stored) and the
+ * scale in torch's op order on the dtype: round(sqrt(ss)), + 1e-7, reciprocal,
+ * * sqrt(m n), each rounded. Deterministic (fixed summation order). */
+ZT_API int zt_lowrank_prepare(const zt_lowrank_desc* d, void* stream);
+
+/* For each tile of the parameter and each stream in order: z = round(round(P Psi) * scale),
+ * theta <- round(theta + alpha z) for the chained coefficients, ge <- round(ge + coef z).
+ * Uses the factors and scales of a zt_lowrank_prepare on the same descriptor. */
+ZT_API int zt_lowrank_apply(const zt_lowrank_desc* d, const zt_lowrank_apply_args* a, void* stream);
+
+/* Reads and clears the low-rank GEMMs' device error flag (nonzero: a bounded wait
+ * expired and the call's outputs are incomplete). Synchronises with the device. */
+ZT_API int zt_lowrank_take_error(int32_t* code);
 
 /* ---- peer mappings for the sharded step's field exchange ------------------------- */
 

@@ -3,7 +3,8 @@
 Every mbarrier wait in the fused cross-entropy GEMM (zt_linear_xent) and the EGGROLL GEMMs
 (zt_eggroll_linear) gives up after a clock deadline: the kernel then records an error
 code, raises both CTAs' abort flags, drains its own copies and MMAs, frees its tensor
-memory and returns. The test hook `test_stall_loads` makes the loader issue no copies, so
+memory and returns. The same holds for the fused low-rank GEMM (zt_lowrank_apply). The test hook
+`test_stall_loads` makes the loader issue no copies, so
 the first wait for a loaded stage expires with no copy and no MMA in flight (nothing to
 drain). The tests check that the call reports the expiry through the take-error entry
 point, that the context stays usable, and that the next normal call is correct.
@@ -54,3 +55,18 @@ def test_eggroll_gemm_wait_expiry_reported_and_context_usable():
     torch.cuda.synchronize()
     assert K.eggroll_take_error() == 0
     torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2)
+
+
+def test_lowrank_gemm_wait_expiry_reported_and_context_usable():
+    from zotitan_b200 import kernels as K
+    f = K.LowRankFactors((512, 512), 64, torch.bfloat16, [3], [4], "cuda")
+    theta = torch.zeros(512, 512, device="cuda", dtype=torch.bfloat16)
+    assert K.lowrank_take_error() == 0
+    f.apply(src=theta, dst=theta, alphas=(1.0,), test_stall_loads=True, test_wait_cycles=2_000_000)
+    torch.cuda.synchronize()
+    assert K.lowrank_take_error() in (3, 4)
+    assert K.lowrank_take_error() == 0
+    z = f.directions()
+    torch.cuda.synchronize()
+    assert K.lowrank_take_error() == 0
+    assert abs(float(z.float().norm()) - 512.0) <= 4.0     # ||z||_F = sqrt(m n)

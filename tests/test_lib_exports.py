@@ -32,7 +32,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version_and_key(lib):
-    assert lib.zt_abi_version() == L.ABI_VERSION == 9
+    assert lib.zt_abi_version() == L.ABI_VERSION == 10
     from oracle import philox as ph
     for seed, n, i in [(0, 1, 0), (1234, 39, 7), (2**40 + 3, 146, 145), (2**64 - 1, 448, 3)]:
         assert lib.zt_param_key(seed, n, i) == ph.param_key(seed, n, i) == (seed * n + i) & 0x7FFFFFFF
@@ -52,6 +52,9 @@ def test_struct_layouts_match_header(lib):
     assert ctypes.sizeof(L.ZtEggrollFactorArgs) == 144 and L.ZtEggrollFactorArgs.b_ext.offset == 104
     assert L.ZtEggrollFactorArgs.seeds.offset == 120 and L.ZtEggrollFactorArgs.key_index_b.offset == 136
     assert ctypes.sizeof(L.ZtEggrollNormArgs) == 88 and L.ZtEggrollNormArgs.seeds.offset == 72
+    assert ctypes.sizeof(L.ZtLowrankDesc) == 1096 and L.ZtLowrankDesc.p.offset == 1056
+    assert ctypes.sizeof(L.ZtLowrankApplyArgs) == 576 and L.ZtLowrankApplyArgs.coef.offset == 44
+    assert L.ZtLowrankApplyArgs.test_wait_cycles.offset == 568
     assert lib.zt_plan_workspace_bytes(0) == 8
     assert lib.zt_plan_workspace_bytes(3) == 256 + 8 * 4
     assert lib.zt_plan_workspace_bytes(5) == 512 + 8 * 6
@@ -95,6 +98,41 @@ def test_invalid_arguments_are_reported(lib):
     t[0].numel, t[0].index = 10, 5
     assert lib.zt_plan_init(t, 1, 1, ctypes.c_void_p(256), 4096, ctypes.byref(out), None) == L.ZT_ERR_INVALID
     assert lib.zt_plan_init(t, 1, 1, ctypes.c_void_p(256), 8, ctypes.byref(out), None) == L.ZT_ERR_INVALID
+
+
+def test_lowrank_arguments_checked_before_launch(lib):
+    """The low-rank entry points reject bad descriptors on the host (no CUDA call)."""
+    sz = ctypes.c_size_t()
+    assert lib.zt_lowrank_workspace_bytes(300, 520, 3, ctypes.byref(sz)) == L.ZT_OK
+    assert sz.value == 2 * 3 * 3 * 32 * 4                       # tiles x streams x partials x fp32
+    assert lib.zt_lowrank_workspace_bytes(300, 520, 0, ctypes.byref(sz)) == L.ZT_ERR_INVALID
+    d = L.ZtLowrankDesc()
+    d.m, d.n, d.r, d.kp, d.dtype, d.n_streams = 256, 512, 64, 64, L.ZT_BF16, 1
+    d.p, d.psi_t, d.scale, d.workspace, d.workspace_bytes = 256, 512, 1024, 2048, 1 << 20
+    a = L.ZtLowrankApplyArgs()
+    a.src, a.dst, a.n_alpha = 4096, 4096, 1
+    for field, value, code, msg in [("dtype", L.ZT_F32, L.ZT_ERR_INVALID, b"dtype"),
+                                    ("kp", 48, L.ZT_ERR_INVALID, b"multiple of 64"),
+                                    ("r", 65, L.ZT_ERR_INVALID, b"r <="),
+                                    ("n_streams", 129, L.ZT_ERR_INVALID, b"n_streams"),
+                                    ("m", 2**31, L.ZT_ERR_LIMIT, b"32-bit"),
+                                    ("p", 8, L.ZT_ERR_INVALID, b"aligned")]:
+        old = getattr(d, field)
+        setattr(d, field, value)
+        assert lib.zt_lowrank_prepare(ctypes.byref(d), None) == code, field
+        assert msg in lib.zt_last_error(), (field, lib.zt_last_error())
+        assert lib.zt_lowrank_apply(ctypes.byref(d), ctypes.byref(a), None) == code, field
+        setattr(d, field, old)
+    d.workspace_bytes = 8
+    assert lib.zt_lowrank_prepare(ctypes.byref(d), None) == L.ZT_ERR_INVALID
+    assert b"workspace" in lib.zt_last_error()
+    a.n_alpha = 0
+    assert lib.zt_lowrank_apply(ctypes.byref(d), ctypes.byref(a), None) == L.ZT_ERR_INVALID   # dst without alpha
+    a.dst = None
+    assert lib.zt_lowrank_apply(ctypes.byref(d), ctypes.byref(a), None) == L.ZT_ERR_INVALID   # nothing to write
+    a.src, a.dst, a.n_alpha = 4096, 4096 + 1024, 1                                          # partial overlap
+    assert lib.zt_lowrank_apply(ctypes.byref(d), ctypes.byref(a), None) == L.ZT_ERR_INVALID
+    assert b"overlap" in lib.zt_last_error()
 
 
 def test_missing_library_raises(tmp_path, monkeypatch):

@@ -34,11 +34,13 @@ EXPORTS = ("zt_last_error", "zt_abi_version", "zt_param_key", "zt_philox_words",
            "zt_eggroll_xb", "zt_eggroll_gated", "zt_eggroll_update_operands", "zt_lora_add", "zt_rmsnorm", "zt_gemm_swiglu", "zt_lora_add3", "zt_lora_split",
            "zt_ipc_export", "zt_ipc_open", "zt_ipc_close", "zt_copy_async",
            "zt_linear_xent_workspace_bytes", "zt_linear_xent", "zt_linear_xent_take_error",
-           "zt_gemm_addto", "zt_gemm_take_error")
+           "zt_gemm_addto", "zt_gemm_take_error",
+           "zt_lowrank_workspace_bytes", "zt_lowrank_prepare", "zt_lowrank_apply", "zt_lowrank_take_error")
 ZT_STATIC_MAX_TENSORS = 1024
 ZT_EGGROLL_MAX_PAIRS = 512
 ZT_EGGROLL_FACTOR_WORK_FLOATS = 64 * 20
-ABI_VERSION = 9
+ABI_VERSION = 10
+ZT_LOWRANK_MAX_STREAMS = 128
 ZT_IPC_HANDLE_BYTES = 64
 
 
@@ -128,6 +130,21 @@ class ZtLceArgs(ctypes.Structure):
                 ("reserved", ctypes.c_int32), ("test_wait_cycles", ctypes.c_int64)]
 
 
+class ZtLowrankDesc(ctypes.Structure):
+    _fields_ = [("m", ctypes.c_int64), ("n", ctypes.c_int64), ("r", ctypes.c_int32), ("kp", ctypes.c_int32),
+                ("dtype", ctypes.c_int32), ("n_streams", ctypes.c_int32),
+                ("keys_p", ctypes.c_uint32 * 128), ("keys_psi", ctypes.c_uint32 * 128),
+                ("p", ctypes.c_void_p), ("psi_t", ctypes.c_void_p), ("scale", ctypes.c_void_p),
+                ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t)]
+
+
+class ZtLowrankApplyArgs(ctypes.Structure):
+    _fields_ = [("src", ctypes.c_void_p), ("dst", ctypes.c_void_p), ("ge", ctypes.c_void_p),
+                ("n_alpha", ctypes.c_int32), ("alpha", ctypes.c_float * 3), ("ge_init", ctypes.c_int32),
+                ("coef", ctypes.c_float * 128), ("test_stall_loads", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("test_wait_cycles", ctypes.c_int64)]
+
+
 class ZtError(RuntimeError):
     """A C-ABI call returned a nonzero status."""
 
@@ -211,6 +228,14 @@ def load():
     lib.zt_gemm_addto.argtypes = [P, I64, P, P, ctypes.c_float, I64, I64, I64, P]
     lib.zt_gemm_take_error.restype = ctypes.c_int
     lib.zt_gemm_take_error.argtypes = [ctypes.POINTER(ctypes.c_int32)]
+    lib.zt_lowrank_workspace_bytes.restype = ctypes.c_int
+    lib.zt_lowrank_workspace_bytes.argtypes = [I64, I64, I32, ctypes.POINTER(ctypes.c_size_t)]
+    lib.zt_lowrank_prepare.restype = ctypes.c_int
+    lib.zt_lowrank_prepare.argtypes = [ctypes.POINTER(ZtLowrankDesc), P]
+    lib.zt_lowrank_apply.restype = ctypes.c_int
+    lib.zt_lowrank_apply.argtypes = [ctypes.POINTER(ZtLowrankDesc), ctypes.POINTER(ZtLowrankApplyArgs), P]
+    lib.zt_lowrank_take_error.restype = ctypes.c_int
+    lib.zt_lowrank_take_error.argtypes = [ctypes.POINTER(ctypes.c_int32)]
     lib.zt_plan_workspace_bytes.restype = ctypes.c_size_t
     lib.zt_plan_workspace_bytes.argtypes = [I32]
     if lib.zt_abi_version() != ABI_VERSION:

@@ -772,3 +772,109 @@ def lora_split(a: torch.Tensor) -> torch.Tensor:
     with torch.cuda.device(a.device):
         L.check(L.load().zt_lora_split(a.data_ptr(), out.data_ptr(), a.numel(), _stream_ptr(a.device)), "zt_lora_split")
     return out
+
+
+# ---- low-rank directions (distribution "low_rank") -----------------------------------
+
+_LR_DTYPES = {torch.bfloat16: L.ZT_BF16, torch.float16: L.ZT_F16}
+
+
+def lowrank_supported(p: torch.Tensor) -> bool:
+    """Whether zt_lowrank_* take this parameter: a contiguous 2-D bf16 or f16 CUDA tensor
+    at an even address (the product runs on the tensor cores, which have no fp32 kind)."""
+    return (p.is_cuda and p.dim() == 2 and p.dtype in _LR_DTYPES and p.is_contiguous() and p.data_ptr() % 2 == 0
+            and p.numel() > 0)
+
+
+class LowRankFactors:
+    """The low-rank directions of one 2-D parameter for up to ZT_LOWRANK_MAX_STREAMS pair
+    seeds, prepared on the device (zt_lowrank_prepare): P and Psi^T of every seed in
+    K-major buffers padded to a multiple of 64, and each seed's rounded scale. The
+    direction z itself is never stored; `apply` recomputes it tile by tile.
+
+    keys_p / keys_psi are the noise keys of P and Psi (positions i + 2N and i + N of the
+    reference's _sample_z, zotitan/train_zo.py:311-315)."""
+
+    def __init__(self, shape, r: int, dtype: torch.dtype, keys_p, keys_psi, device):
+        m, n = int(shape[0]), int(shape[1])
+        S = len(keys_p)
+        if not 1 <= S <= L.ZT_LOWRANK_MAX_STREAMS or len(keys_psi) != S:
+            raise ValueError(f"1..{L.ZT_LOWRANK_MAX_STREAMS} streams with one P and one Psi key each")
+        if dtype not in _LR_DTYPES:
+            raise ValueError("low-rank directions on the tensor cores take bf16 or f16 parameters")
+        kp = 64 * ((r + 63) // 64)
+        self.shape, self.r, self.kp, self.dtype, self.n_streams = (m, n), r, kp, dtype, S
+        self.p = torch.empty((S * m, kp), dtype=dtype, device=device)
+        self.psi_t = torch.empty((S * n, kp), dtype=dtype, device=device)
+        self.scale = torch.empty(S, dtype=torch.float32, device=device)
+        lib = L.load()
+        ws = ctypes.c_size_t()
+        L.check(lib.zt_lowrank_workspace_bytes(m, n, S, ctypes.byref(ws)), "zt_lowrank_workspace_bytes")
+        self._ws = torch.empty(max(16, ws.value), dtype=torch.uint8, device=device)
+        d = L.ZtLowrankDesc()
+        d.m, d.n, d.r, d.kp, d.dtype, d.n_streams = m, n, r, kp, _LR_DTYPES[dtype], S
+        for s in range(S):
+            d.keys_p[s], d.keys_psi[s] = int(keys_p[s]), int(keys_psi[s])
+        d.p, d.psi_t, d.scale = self.p.data_ptr(), self.psi_t.data_ptr(), self.scale.data_ptr()
+        d.workspace, d.workspace_bytes = self._ws.data_ptr(), self._ws.numel()
+        self.desc = d
+        self.device = torch.device(device)
+        with torch.cuda.device(self.device):
+            L.check(lib.zt_lowrank_prepare(ctypes.byref(d), _stream_ptr(self.device)), "zt_lowrank_prepare")
+
+    def apply(self, src: torch.Tensor | None = None, dst: torch.Tensor | None = None, alphas=(), ge=None, coefs=None,
+              ge_init: bool = False, test_stall_loads: bool = False, test_wait_cycles: int = 0) -> None:
+        """For each stream in order: dst <- round(dst + a z) for each a in `alphas` (stream
+        0 reads src), ge <- round(ge + coef z) (ge = round(coef z) for stream 0 with
+        ge_init)."""
+        for t, name in ((src, "src"), (dst, "dst"), (ge, "ge")):
+            if t is not None:
+                _check_cuda(t, name)
+                if tuple(t.shape) != self.shape or t.dtype != self.dtype or not t.is_contiguous():
+                    raise ValueError(f"{name} must be a contiguous {self.dtype} tensor of shape {self.shape}")
+        if len(alphas) > 3:
+            raise ValueError("at most 3 chained coefficients")
+        a = L.ZtLowrankApplyArgs()
+        a.src = src.data_ptr() if src is not None else None
+        a.dst = dst.data_ptr() if dst is not None else None
+        a.ge = ge.data_ptr() if ge is not None else None
+        a.n_alpha = len(alphas)
+        for t, v in enumerate(alphas):
+            a.alpha[t] = float(np.float32(v))
+        a.ge_init = 1 if ge_init else 0
+        if coefs is not None:
+            if len(coefs) != self.n_streams:
+                raise ValueError("one grad-estimate coefficient per stream")
+            for s, v in enumerate(coefs):
+                a.coef[s] = float(np.float32(v))
+        a.test_stall_loads = 1 if test_stall_loads else 0
+        a.test_wait_cycles = int(test_wait_cycles)
+        with torch.cuda.device(self.device):
+            L.check(L.load().zt_lowrank_apply(ctypes.byref(self.desc), ctypes.byref(a), _stream_ptr(self.device)),
+                    "zt_lowrank_apply")
+
+    def directions(self) -> torch.Tensor:
+        """The scaled directions [S, m, n] (test use: writes them into a zero tensor)."""
+        S, (m, n) = self.n_streams, self.shape
+        out = torch.empty((S, m, n), dtype=self.dtype, device=self.device)
+        zero = torch.zeros((m, n), dtype=self.dtype, device=self.device)
+        for s in range(S):
+            one = LowRankFactors.__new__(LowRankFactors)
+            one.__dict__.update(self.__dict__)
+            d = L.ZtLowrankDesc()
+            ctypes.pointer(d)[0] = self.desc
+            esz = self.p.element_size()
+            d.n_streams = 1
+            d.keys_p[0], d.keys_psi[0] = self.desc.keys_p[s], self.desc.keys_psi[s]
+            d.p = self.p.data_ptr() + s * m * self.kp * esz
+            d.psi_t = self.psi_t.data_ptr() + s * n * self.kp * esz
+            d.scale = self.scale.data_ptr() + 4 * s
+            one.desc, one.n_streams = d, 1
+            one.apply(src=zero, dst=out[s], alphas=(1.0,))
+        return out
+
+
+def lowrank_take_error() -> int:
+    code = ctypes.c_int32(0)
+    L.check(L.load().zt_lowrank_take_error(ctypes.byref(code)), "zt_lowrank_take_error")
+    return int(code.value)

@@ -42,6 +42,7 @@ import numpy as np
 import torch
 
 from . import _lib as L
+from . import kernels as K
 from .data import PrefetchLoader, get_batches
 from .distributed import gather_pair_values, local_pairs, world_info
 from .kernels import ParamTable, PassCfg, Stream, param_key, randn
@@ -487,7 +488,8 @@ class ZOOptimizer:
 
     def __init__(self, named_params: list, cfg: ZOConfig, score_fn, total_steps: int = 0, process_group=None,
                  sharded: bool | None = None, shard_update: bool = True, noise_cache: bool | None = None,
-                 field_exchange: bool | float | None = None, exchange_mode: str = "copies"):
+                 field_exchange: bool | float | None = None, exchange_mode: str = "copies",
+                 lowrank_fused: bool = True):
         if exchange_mode not in ("copies", "in_pass"):
             raise ValueError(f"exchange_mode must be 'copies' or 'in_pass', got {exchange_mode!r}")
         self.named_params = named_params
@@ -512,6 +514,10 @@ class ZOOptimizer:
         # low_rank / polar: 2-D tensors take materialised directions, 1-D ones the fused passes
         self.lr_idx = [i for i, p in enumerate(self.params) if p.dim() >= 2] if pl.materialized else []
         lr_set = set(self.lr_idx)
+        # distribution "low_rank" on bf16/f16 matrices: the direction is recomputed on the
+        # tensor cores inside each use (zt_lowrank_*), never stored
+        self.lr_fused = {i for i in self.lr_idx if lowrank_fused and cfg.perturbation.distribution == "low_rank"
+                         and K.lowrank_supported(self.params[i])}
         self.dense_idx = [i for i in range(len(self.params)) if i not in lr_set]
         # grad_est buffer of the on-the-fly accumulation (same size as the reference's
         # zeros_like grad_est for z_batch > 1; dense tensors only)
@@ -621,47 +627,80 @@ class ZOOptimizer:
         if self.table is not None:
             self.table.run(spec.cfg, spec.streams)
 
-    # -- materialised low_rank / polar directions (zotitan/train_zo.py:295-322) -------------
+    # -- low_rank / polar directions of the 2-D tensors (zotitan/train_zo.py:295-322) ------
     def _lowrank_z(self, seed: int) -> list:
-        """The reference's _sample_z for the 2-D tensors: P [m, r] and Psi [r, n] from the
-        noise source (keys of positions i + 2n and i + n), cast to the parameter dtype,
+        """The reference's _sample_z for the 2-D tensors, one entry per tensor of lr_idx: for
+        the fused ones the prepared factors (K.LowRankFactors, z never stored), for the
+        others the materialised direction: P [m, r] and Psi [r, n] from the noise source
+        (keys of positions i + 2n and i + n), cast to the parameter dtype,
         polar-orthogonalised for "polar", z = P @ Psi scaled to ||z||_F = sqrt(numel)."""
+        return [self._lowrank_one(i, [seed]) if i in self.lr_fused else self._lowrank_dense(i, seed)
+                for i in self.lr_idx]
+
+    def _lowrank_one(self, i: int, seeds: list) -> "K.LowRankFactors":
+        p = self.params[i]
+        n = len(self.params)
+        r = min(self.cfg.perturbation.rank, p.shape[0])
+        return K.LowRankFactors(p.shape, r, p.dtype, [param_key(sd, n, i + 2 * n) for sd in seeds],
+                                [param_key(sd, n, i + n) for sd in seeds], p.device)
+
+    def _lowrank_dense(self, i: int, seed: int) -> torch.Tensor:
         pc = self.cfg.perturbation
         n = len(self.params)
-        out = []
-        for i in self.lr_idx:
-            p = self.params[i]
-            m, r = p.shape[0], min(pc.rank, p.shape[0])
-            P = randn(param_key(seed, n, i + 2 * n), m * r, p.device).view(m, r).to(p.dtype)
-            if pc.distribution == "polar":
-                P, _ = torch.linalg.qr(P)
-            Psi = randn(param_key(seed, n, i + n), r * p.shape[1], p.device).view(r, p.shape[1]).to(p.dtype)
-            if pc.distribution == "polar":
-                Psi = zeropower_via_newtonschulz(Psi)
-            z = P @ Psi
-            out.append(z * (p.numel() ** 0.5 / (z.norm() + 1e-7)))
-        return out
+        p = self.params[i]
+        m, r = p.shape[0], min(pc.rank, p.shape[0])
+        P = randn(param_key(seed, n, i + 2 * n), m * r, p.device).view(m, r).to(p.dtype)
+        if pc.distribution == "polar":
+            P, _ = torch.linalg.qr(P)
+        Psi = randn(param_key(seed, n, i + n), r * p.shape[1], p.device).view(r, p.shape[1]).to(p.dtype)
+        if pc.distribution == "polar":
+            Psi = zeropower_via_newtonschulz(Psi)
+        z = P @ Psi
+        return z * (p.numel() ** 0.5 / (z.norm() + 1e-7))
 
     def _lr_apply(self, z: list, scale: float, target=None) -> None:
         """_apply_z (:350-351) on the 2-D tensors (of `target`, default the parameters)."""
-        if self.lr_idx:
-            tgt = self.params if target is None else target
-            torch._foreach_add_([tgt[i] for i in self.lr_idx], z, alpha=scale)
+        if not self.lr_idx:
+            return
+        tgt = self.params if target is None else target
+        dense = [(tgt[i], zz) for i, zz in zip(self.lr_idx, z) if i not in self.lr_fused]
+        if dense:
+            torch._foreach_add_([t for t, _ in dense], [zz for _, zz in dense], alpha=scale)
+        for i, zz in zip(self.lr_idx, z):
+            if i in self.lr_fused:
+                zz.apply(src=tgt[i], dst=tgt[i], alphas=(scale,))
 
     def _lr_plus_live(self, z: list, scale: float) -> None:
         """Sharded: live = master + scale * z on the 2-D tensors, rounded once (what the
         fused +eps pass does for the others)."""
         for i, zz in zip(self.lr_idx, z):
-            torch.add(self.master[i], zz, alpha=scale, out=self.params[i])
+            if i in self.lr_fused:
+                zz.apply(src=self.master[i], dst=self.params[i], alphas=(scale,))
+            else:
+                torch.add(self.master[i], zz, alpha=scale, out=self.params[i])
+
+    def _lr_seed_chunks(self, seeds: list) -> list:
+        M = L.ZT_LOWRANK_MAX_STREAMS
+        return [seeds[c:c + M] for c in range(0, len(seeds), M)]
 
     def _lr_replay_master(self) -> None:
         """Sharded: every pair's +eps / -2eps / +eps rounding chain on the 2-D tensors'
-        master, in pair order, as the single-GPU parameters went through them."""
+        master, in pair order, as the single-GPU parameters went through them (fused
+        tensors: every pair of a chunk in one launch per tensor)."""
         eps = self.cfg.eps
-        for seed in self.planner.seeds:
-            z = self._lowrank_z(seed)
-            for a in (eps, -2 * eps, eps):
-                self._lr_apply(z, a, target=self.master)
+        seeds = self.planner.seeds
+        for i in self.lr_idx:
+            if i in self.lr_fused:
+                for chunk in self._lr_seed_chunks(seeds):
+                    self._lowrank_one(i, chunk).apply(src=self.master[i], dst=self.master[i],
+                                                      alphas=(eps, -2 * eps, eps))
+        dense = [i for i in self.lr_idx if i not in self.lr_fused]
+        if dense:
+            tgt = [self.master[i] for i in dense]
+            for seed in seeds:
+                zs = [self._lowrank_dense(i, seed) for i in dense]
+                for a in (eps, -2 * eps, eps):
+                    torch._foreach_add_(tgt, zs, alpha=a)
 
     def _lr_finish(self, spec: PassSpec) -> None:
         """grad_est of the 2-D tensors from the regenerated directions with this step's pair
@@ -672,13 +711,27 @@ class ZOOptimizer:
         import dataclasses
         pl = self.planner
         ge_mode, coefs, _ = pl.last_ge
+        pos = {i: t for t, i in enumerate(self.lr_idx)}
+        dense = [i for i in self.lr_idx if i not in self.lr_fused]
+        dge = [self.lr_ge[pos[i]] for i in dense]
         if ge_mode == L.ZT_GE_PRODUCT:
-            for g, r in zip(self.lr_ge, torch._foreach_mul(self._lowrank_z(pl.seeds[0]), coefs[0])):
-                g.copy_(r)
+            if dense:
+                zs = [self._lowrank_dense(i, pl.seeds[0]) for i in dense]
+                for g, r in zip(dge, torch._foreach_mul(zs, coefs[0])):
+                    g.copy_(r)
+            for i in self.lr_idx:
+                if i in self.lr_fused:
+                    self._lowrank_one(i, pl.seeds[:1]).apply(ge=self.lr_ge[pos[i]], coefs=[coefs[0]], ge_init=True)
         elif ge_mode == L.ZT_GE_ACCUM:
-            torch._foreach_zero_(self.lr_ge)
-            for j, seed in enumerate(pl.seeds):
-                torch._foreach_add_(self.lr_ge, self._lowrank_z(seed), alpha=coefs[j])
+            if dense:
+                torch._foreach_zero_(dge)
+                for j, seed in enumerate(pl.seeds):
+                    torch._foreach_add_(dge, [self._lowrank_dense(i, seed) for i in dense], alpha=coefs[j])
+            for i in self.lr_idx:
+                if i in self.lr_fused:
+                    for c, chunk in enumerate(self._lr_seed_chunks(list(range(len(pl.seeds))))):
+                        self._lowrank_one(i, [pl.seeds[j] for j in chunk]).apply(
+                            ge=self.lr_ge[pos[i]], coefs=[coefs[j] for j in chunk], ge_init=c == 0)
         # the 2-D tensors' table has no live copy: the sharded schedule copies master -> live after
         cfg = dataclasses.replace(spec.cfg, ge_mode=L.ZT_GE_ACCUM if ge_mode != L.ZT_GE_NONE else L.ZT_GE_NONE,
                                   ge_load=ge_mode != L.ZT_GE_NONE, ge_store=False, dev_pair=None, dev_vals=0,
