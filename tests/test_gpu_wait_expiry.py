@@ -64,7 +64,13 @@ def test_lowrank_gemm_wait_expiry_reported_and_context_usable():
     assert K.lowrank_take_error() == 0
     f.apply(src=theta, dst=theta, alphas=(1.0,), test_stall_loads=True, test_wait_cycles=2_000_000)
     torch.cuda.synchronize()
-    assert K.lowrank_take_error() in (3, 4)
+    assert K.lowrank_take_error() in (1, 3, 4)   # a wait of the stage pipeline
+    # the ragged-row kernel (rows not whole 16-byte groups) takes the same hook
+    g = K.LowRankFactors((300, 300), 64, torch.bfloat16, [3], [4], "cuda")
+    t3 = torch.zeros(300, 300, device="cuda", dtype=torch.bfloat16)
+    g.apply(src=t3, dst=t3, alphas=(1.0,), test_stall_loads=True, test_wait_cycles=2_000_000)
+    torch.cuda.synchronize()
+    assert K.lowrank_take_error() in (1, 3, 4)
     assert K.lowrank_take_error() == 0
     z = f.directions()
     torch.cuda.synchronize()

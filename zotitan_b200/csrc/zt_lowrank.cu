@@ -195,8 +195,8 @@ __device__ __forceinline__ void stage_chunk(const uint32_t (&acc)[32], float sc,
 // Phase 2 on 8 consecutive elements (one 16-byte group of the parameter, the grad
 // estimate and the staged direction): theta = round(theta + a zs) for each chained
 // coefficient, g = round(g + c zs) (g = round(c zs) when `init`).
-template <int DT, bool TH, bool GE>
-__device__ __forceinline__ void apply8(uint4& th, uint4& gv, const uint4 zs, const LrParams& P, float c, bool init) {
+template <int DT, bool TH, bool GE, typename PT>
+__device__ __forceinline__ void apply8(uint4& th, uint4& gv, const uint4 zs, const PT& P, float c, bool init) {
   uint32_t tw[4] = {th.x, th.y, th.z, th.w};
   uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
   const uint32_t zw[4] = {zs.x, zs.y, zs.z, zs.w};
@@ -533,33 +533,322 @@ __global__ void __launch_bounds__(256) lr_scale_kernel(const float* __restrict__
   }
 }
 
-// ---- host side ----------------------------------------------------------------------------
+// ---- apply with the parameter slice resident in shared memory ---------------------------
+//
+// For parameters whose rows are whole 16-byte groups at 16-byte aligned addresses. Each
+// CTA's 128 x 256 slice of a tile (of the parameter, the grad estimate, or both) comes in
+// by TMA one tile ahead of its use. Every stream of the tile is applied to it in shared
+// memory, and one TMA store writes it back: HBM sees the parameter once per tile whatever
+// the stream count, and the copies run on the TMA engine instead of the epilogue warps.
+// The slice is held in the 128-byte-swizzled layout the tile maps use: 16-byte chunk c of
+// row r at r * 128 + ((c ^ (r & 7)) << 4) inside each 64-column box.
+constexpr int kTStages = 2;
+constexpr uint32_t kBoxBytes = 128 * 128;        // 64 columns x 128 rows of 16-bit values
+constexpr uint32_t kSliceBytes = 4 * kBoxBytes;  // a CTA's 128 x 256 slice of a tile
+constexpr size_t kSmemT = 1024 + kTStages * kStageBytes + 2 * kSliceBytes + 256;
+
+struct LrTileParams {
+  CUtensorMap tmap_a;    // stacked P    [S m, kp], box {64, 128}
+  CUtensorMap tmap_b;    // stacked Psi^T [S n, kp], box {64, 128}
+  CUtensorMap tmap_src;  // parameter read   [m, n], box {64, 128}, 128-byte swizzle
+  CUtensorMap tmap_dst;  // parameter written
+  CUtensorMap tmap_ge;   // grad estimate (read unless ge_init, written)
+  const float* scale;
+  float alpha[3];
+  int32_t n_alpha;
+  int32_t ge_init;
+  int32_t m, n, k_blocks, m_tiles, n_tiles, n_streams;
+  int32_t stall_loads;
+  long long wait_cycles;
+  float coef[ZT_LOWRANK_MAX_STREAMS];
+};
 
 template <int DT, int MODE>
-int prepare_gemm(int* pairs) {
-  static int cached[64] = {0};
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    lr_tile_kernel(const __grid_constant__ LrTileParams P) {
+  constexpr bool TH = MODE == kModeTheta || MODE == kModeBoth;
+  constexpr bool GE = MODE == kModeGe || MODE == kModeBoth;
+  constexpr int kBufs = (TH && GE) ? 1 : 2;  // slices in flight: two, or one of each kind
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t* stage_base = smem;
+  uint8_t* slices = smem + kTStages * kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(slices + 2 * kSliceBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kTStages;
+  uint64_t* accf = bars + 2 * kTStages;
+  uint64_t* acce = accf + 2;
+  uint64_t* drain = acce + 2;
+  uint64_t* tfull = drain + 1;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* tdone = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tdone + 2);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 2 * kEpiWarps);
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 1);
+      mbar_init(&tdone[b], kEpiWarps);
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncwarp();
+  cluster_sync_all();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t peer_abort = peer_addr((const void*)abort, rank ^ 1u);
+  const long long wl = P.wait_cycles;
+
+  const int n_tiles = P.m_tiles * P.n_tiles;
+  const int S = P.n_streams;
+  const int cid = (int)cluster_id_x(), ncl = (int)n_clusters_x();
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer (both CTAs): the tile's slice, then every stream's K blocks
+      int last_phase[kTStages];
+      for (int s = 0; s < kTStages; ++s) last_phase[s] = -1;
+      int slice_phase[2] = {-1, -1};
+      uint32_t it = 0;
+      bool ok = true;
+      int ti = 0;
+      for (int tile = cid; ok && tile < n_tiles; tile += ncl, ++ti) {
+        int mt, nt;
+        tile_coords(tile, P.m_tiles, P.n_tiles, mt, nt);
+        const int tb = kBufs == 2 ? (ti & 1) : 0;
+        const uint32_t u = kBufs == 2 ? (uint32_t)(ti >> 1) : (uint32_t)ti;
+        if (!mbar_wait_pair(&tempty[tb], (u & 1) ^ 1, abort, peer_abort, &g_lowrank_error, 5, wl)) break;
+        uint8_t* th_buf = slices + (kBufs == 2 ? tb * kSliceBytes : 0);
+        uint8_t* ge_buf = kBufs == 2 ? th_buf : slices + kSliceBytes;
+        const bool load_ge = GE && !P.ge_init;
+        const uint32_t bytes = (TH ? kSliceBytes : 0u) + (load_ge ? kSliceBytes : 0u);
+        const int x0 = nt * (int)kTile, y0 = mt * (int)kTile + (int)rank * (int)kHalfRows;
+        if (bytes) {
+          mbar_expect_tx(&tfull[tb], bytes);
+#pragma unroll
+          for (int box = 0; box < 4; ++box) {
+            if (TH) tma_load_2d(th_buf + box * kBoxBytes, &P.tmap_src, &tfull[tb], x0 + box * 64, y0);
+            if (load_ge) tma_load_2d(ge_buf + box * kBoxBytes, &P.tmap_ge, &tfull[tb], x0 + box * 64, y0);
+          }
+          slice_phase[tb] = (int)(u & 1);
+        } else {
+          mbar_arrive(&tfull[tb]);
+        }
+        for (int st = 0; ok && st < S; ++st) {
+          for (int kb = 0; kb < P.k_blocks; ++kb, ++it) {
+            const int s = it % kTStages;
+            const uint32_t round = it / kTStages;
+            if (!mbar_wait_pair(&empty[s], (round & 1) ^ 1, abort, peer_abort, &g_lowrank_error, 1, wl)) {
+              ok = false;
+              break;
+            }
+            if (P.stall_loads) continue;
+            uint8_t* sa = stage_base + s * kStageBytes;
+            const uint32_t leader_full = peer_addr(&full[s], 0);
+            if (leader) mbar_expect_tx(&full[s], 2 * kStageBytes);
+            tma_load_2d_pair(sa, &P.tmap_a, leader_full, kb * kBK,
+                             st * P.m + mt * (int)kTile + (int)rank * (int)kHalfRows);
+            tma_load_2d_pair(sa + kStageA, &P.tmap_b, leader_full, kb * kBK,
+                             st * P.n + nt * (int)kTile + (int)rank * (int)kHalfRows);
+            last_phase[s] = (int)(round & 1);
+          }
+        }
+      }
+      for (int b = 0; b < 2; ++b)
+        if (slice_phase[b] >= 0) mbar_drain(&tfull[b], (uint32_t)slice_phase[b]);
+      if (leader)
+        for (int s = 0; s < kTStages; ++s)
+          if (last_phase[s] >= 0) mbar_drain(&full[s], (uint32_t)last_phase[s]);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {  // ---- MMA issuer (leader CTA only)
+      uint32_t it = 0, tcount = 0;
+      bool ok = true, issued = false;
+      for (int tile = cid; ok && tile < n_tiles; tile += ncl) {
+        for (int st = 0; ok && st < S; ++st, ++tcount) {
+          const uint32_t b = tcount & 1;
+          if (!mbar_wait_pair(&acce[b], ((tcount >> 1) & 1) ^ 1, abort, peer_abort, &g_lowrank_error, 2, wl)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t tmem_d = tmem_base + b * kTile;
+          for (int kb = 0; kb < P.k_blocks; ++kb, ++it) {
+            const int s = it % kTStages;
+            if (!mbar_wait_pair(&full[s], (it / kTStages) & 1, abort, peer_abort, &g_lowrank_error, 3, wl)) {
+              ok = false;
+              break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t sa = smem_u32(stage_base + s * kStageBytes);
+            const uint32_t sb = sa + kStageA;
+#pragma unroll
+            for (int k = 0; k < kBK / kUmmaK; ++k) {
+              if (DT == ZT_BF16)
+                umma_bf16_pair<kIdescBf16>(tmem_d, umma_desc(sa + k * kUmmaK * 2), umma_desc(sb + k * kUmmaK * 2),
+                                           (kb | k) != 0);
+              else
+                umma_bf16_pair<kIdescF16>(tmem_d, umma_desc(sa + k * kUmmaK * 2), umma_desc(sb + k * kUmmaK * 2),
+                                          (kb | k) != 0);
+            }
+            issued = true;
+            umma_commit_pair(&empty[s]);
+          }
+          if (!ok) break;
+          umma_commit_pair(&accf[b]);
+        }
+      }
+      if (issued) {
+        umma_commit_pair_local(drain);
+        mbar_drain(drain, 0);
+      }
+    }
+  } else {  // ---- epilogue: warps 2..17 of both CTAs; a warp owns 32 rows x 64 columns (one box)
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int quarter = ew >> 2;
+    const int r = q * 32 + lane;  // row of the CTA's slice = tensor-memory lane
+    const uint32_t leader_acce0 = peer_addr(&acce[0], 0), leader_acce1 = peer_addr(&acce[1], 0);
+    uint32_t tcount = 0;
+    bool ok = true;
+    int ti = 0;
+    for (int tile = cid; ok && tile < n_tiles; tile += ncl, ++ti) {
+      int mt, nt;
+      tile_coords(tile, P.m_tiles, P.n_tiles, mt, nt);
+      const int tb = kBufs == 2 ? (ti & 1) : 0;
+      const uint32_t u = kBufs == 2 ? (uint32_t)(ti >> 1) : (uint32_t)ti;
+      uint8_t* th_buf = slices + (kBufs == 2 ? tb * kSliceBytes : 0);
+      uint8_t* ge_buf = kBufs == 2 ? th_buf : slices + kSliceBytes;
+      int okw = 1;
+      if (lane == 0) okw = mbar_wait_pair(&tfull[tb], u & 1, abort, peer_abort, &g_lowrank_error, 6, wl) ? 1 : 0;
+      okw = __shfl_sync(0xffffffffu, okw, 0);
+      if (!okw) break;
+      uint8_t* th_row = th_buf + quarter * kBoxBytes + r * 128;
+      uint8_t* ge_row = ge_buf + quarter * kBoxBytes + r * 128;
+      for (int st = 0; st < S; ++st, ++tcount) {
+        const uint32_t b = tcount & 1;
+        okw = 1;
+        if (lane == 0)
+          okw = mbar_wait_pair(&accf[b], (tcount >> 1) & 1, abort, peer_abort, &g_lowrank_error, 4, wl) ? 1 : 0;
+        okw = __shfl_sync(0xffffffffu, okw, 0);
+        if (!okw) {
+          ok = false;
+          break;
+        }
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + b * kTile + (uint32_t)(quarter * 64);
+        const float sc = P.scale[st];
+        const float c = P.coef[st];
+        const bool init = P.ge_init && st == 0;
+#pragma unroll 1
+        for (int c2 = 0; c2 < 2; ++c2) {
+          uint32_t acc[32];
+          tmem_ld32(taddr + (uint32_t)(c2 * 32), acc);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int off = ((c2 * 4 + k) ^ (r & 7)) << 4;
+            uint32_t zw[4];
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+              float za = __uint_as_float(acc[8 * k + 2 * w]), zb = __uint_as_float(acc[8 * k + 2 * w + 1]);
+              H<DT>::round2(za, zb);
+              zw[w] = H<DT>::pack(__fmul_rn(za, sc), __fmul_rn(zb, sc));
+            }
+            uint4 tv = make_uint4(0u, 0u, 0u, 0u), gv = make_uint4(0u, 0u, 0u, 0u);
+            if (TH) tv = *reinterpret_cast<const uint4*>(th_row + off);
+            if (GE && !init) gv = *reinterpret_cast<const uint4*>(ge_row + off);
+            apply8<DT, TH, GE>(tv, gv, make_uint4(zw[0], zw[1], zw[2], zw[3]), P, c, init);
+            if (TH) *reinterpret_cast<uint4*>(th_row + off) = tv;
+            if (GE) *reinterpret_cast<uint4*>(ge_row + off) = gv;
+          }
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(b ? leader_acce1 : leader_acce0);
+      }
+      if (!ok) break;
+      // the slice is complete: every warp's writes made visible to the TMA engine, then
+      // one thread stores it once all sixteen warps have arrived
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tdone[tb]);
+      if (ew == 0 && lane == 0) {
+        if (!mbar_wait_pair(&tdone[tb], u & 1, abort, peer_abort, &g_lowrank_error, 7, wl)) {
+          ok = false;
+        } else {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          const int x0 = nt * (int)kTile, y0 = mt * (int)kTile + (int)rank * (int)kHalfRows;
+#pragma unroll
+          for (int box = 0; box < 4; ++box) {
+            if (TH) tma_store_2d(&P.tmap_dst, th_buf + box * kBoxBytes, x0 + box * 64, y0);
+            if (GE) tma_store_2d(&P.tmap_ge, ge_buf + box * kBoxBytes, x0 + box * 64, y0);
+          }
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+          mbar_arrive(&tempty[tb]);
+        }
+      }
+      okw = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0);
+      if (!okw) break;
+    }
+    if (ew == 0 && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncwarp();
+  cluster_sync_all();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (warp == 0) {
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+  }
+}
+
+// ---- host side ----------------------------------------------------------------------------
+
+// CTA pairs of `kern` that fit on the GPU at once (cached per device and kernel).
+template <typename Kern>
+int pairs_for(Kern kern, size_t smem, int (&cache)[64], int* pairs) {
   static std::mutex mu;
   int dev = 0;
   if (int rc = zt::check_cuda(cudaGetDevice(&dev), "zt_lowrank: cudaGetDevice")) return rc;
   if (dev < 0 || dev >= 64) return zt::set_error(ZT_ERR_LIMIT, "zt_lowrank: device ordinal >= 64");
   std::lock_guard<std::mutex> lock(mu);
-  if (cached[dev] <= 0) {
-    if (int rc = zt::check_cuda(cudaFuncSetAttribute(lr_gemm_kernel<DT, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                     (int)kSmem), "zt_lowrank: shared memory attribute"))
+  if (cache[dev] <= 0) {
+    if (int rc = zt::check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                                "zt_lowrank: shared memory attribute"))
       return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (unsigned)(zt::sm_count() / 2));
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmem;
+    cfg.dynamicSmemBytes = smem;
     int n = 0;
-    if (int rc = zt::check_cuda(cudaOccupancyMaxActiveClusters(&n, lr_gemm_kernel<DT, MODE>, &cfg),
-                                "zt_lowrank: cudaOccupancyMaxActiveClusters"))
+    if (int rc = zt::check_cuda(cudaOccupancyMaxActiveClusters(&n, kern, &cfg), "zt_lowrank: cudaOccupancyMaxActiveClusters"))
       return rc;
     if (n <= 0) return zt::set_error(ZT_ERR_CUDA, "zt_lowrank: no CTA pair fits on this GPU");
-    cached[dev] = n;
+    cache[dev] = n;
   }
-  *pairs = cached[dev];
+  *pairs = cache[dev];
   return ZT_OK;
+}
+
+template <int DT, int MODE>
+int prepare_gemm(int* pairs) {
+  static int cache[64] = {0};
+  return pairs_for(lr_gemm_kernel<DT, MODE>, kSmem, cache, pairs);
 }
 
 int64_t tiles_of(int64_t m, int64_t n) { return ((m + kTile - 1) / kTile) * ((n + kTile - 1) / kTile); }
@@ -605,6 +894,44 @@ int launch_gemm(const zt_lowrank_desc* d, LrParams& P, cudaStream_t st, const ch
   const int clusters = tiles < pairs ? (int)tiles : pairs;
   lr_gemm_kernel<DT, MODE><<<2 * clusters, kThreads, kSmem, st>>>(P);
   return zt::check_cuda(cudaGetLastError(), (std::string(who) + ": launch").c_str());
+}
+
+template <int DT, int MODE>
+int launch_tile(const zt_lowrank_desc* d, const zt_lowrank_apply_args* a, cudaStream_t st) {
+  const char* who = "zt_lowrank_apply";
+  static int cache[64] = {0};
+  int pairs = 0;
+  if (int rc = pairs_for(lr_tile_kernel<DT, MODE>, kSmemT, cache, &pairs)) return rc;
+  EncodeFn enc = nullptr;
+  if (int rc = get_encode(&enc, who)) return rc;
+  LrTileParams P;
+  memset(&P, 0, sizeof(P));
+  const uint64_t S = (uint64_t)d->n_streams, m = (uint64_t)d->m, n = (uint64_t)d->n;
+  if (int rc = make_map_bf16(enc, &P.tmap_a, d->p, S * m, (uint64_t)d->kp, kHalfRows, who)) return rc;
+  if (int rc = make_map_bf16(enc, &P.tmap_b, d->psi_t, S * n, (uint64_t)d->kp, kHalfRows, who)) return rc;
+  if (a->dst) {
+    if (int rc = make_map_bf16(enc, &P.tmap_src, a->src, m, n, kHalfRows, who)) return rc;
+    if (int rc = make_map_bf16(enc, &P.tmap_dst, a->dst, m, n, kHalfRows, who)) return rc;
+  }
+  if (a->ge)
+    if (int rc = make_map_bf16(enc, &P.tmap_ge, a->ge, m, n, kHalfRows, who)) return rc;
+  P.scale = d->scale;
+  P.n_alpha = a->n_alpha;
+  for (int i = 0; i < 3; ++i) P.alpha[i] = a->alpha[i];
+  P.ge_init = a->ge_init ? 1 : 0;
+  for (int s = 0; s < d->n_streams; ++s) P.coef[s] = a->coef[s];
+  P.m = (int32_t)d->m;
+  P.n = (int32_t)d->n;
+  P.k_blocks = d->kp / kBK;
+  P.m_tiles = (int32_t)((d->m + kTile - 1) / kTile);
+  P.n_tiles = (int32_t)((d->n + kTile - 1) / kTile);
+  P.n_streams = d->n_streams;
+  P.stall_loads = a->test_stall_loads ? 1 : 0;
+  P.wait_cycles = a->test_wait_cycles > 0 ? (long long)a->test_wait_cycles : kWaitCycles;
+  const int64_t tiles = (int64_t)P.m_tiles * P.n_tiles;
+  const int clusters = tiles < pairs ? (int)tiles : pairs;
+  lr_tile_kernel<DT, MODE><<<2 * clusters, kThreads, kSmemT, st>>>(P);
+  return zt::check_cuda(cudaGetLastError(), "zt_lowrank_apply: launch");
 }
 
 template <int DT>
@@ -696,6 +1023,15 @@ int zt_lowrank_apply(const zt_lowrank_desc* d, const zt_lowrank_apply_args* a, v
   P.wait_cycles = a->test_wait_cycles > 0 ? (long long)a->test_wait_cycles : kWaitCycles;
   const cudaStream_t st = zt::as_stream(stream);
   const bool th = a->dst != nullptr, ge = a->ge != nullptr;
+  if (vec) {  // whole 16-byte row groups at aligned addresses: the slice-resident kernel
+    if (d->dtype == ZT_BF16)
+      return th && ge ? launch_tile<ZT_BF16, kModeBoth>(d, a, st)
+             : th     ? launch_tile<ZT_BF16, kModeTheta>(d, a, st)
+                      : launch_tile<ZT_BF16, kModeGe>(d, a, st);
+    return th && ge ? launch_tile<ZT_F16, kModeBoth>(d, a, st)
+           : th     ? launch_tile<ZT_F16, kModeTheta>(d, a, st)
+                    : launch_tile<ZT_F16, kModeGe>(d, a, st);
+  }
   if (d->dtype == ZT_BF16)
     return th && ge ? launch_gemm<ZT_BF16, kModeBoth>(d, P, st, who)
            : th     ? launch_gemm<ZT_BF16, kModeTheta>(d, P, st, who)

@@ -91,6 +91,15 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* t
       : "memory");
 }
 
+// A 2-D tile from this CTA's shared memory to global memory (bulk group of the issuing
+// thread; the coordinates must not be negative). Elements outside the tensor map's
+// extent are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tmap, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row groups 1024
 // bytes apart (stride byte offset), leading byte offset unused (1), descriptor version 1,
 // layout type 2 (SWIZZLE_128B).
