@@ -138,3 +138,71 @@ def test_optimizer_low_rank_fused_against_materialised():
         u = ulp_diff(x, y, torch.bfloat16)
         assert float(u.max()) <= 2.0
         assert float((u == 0).double().mean()) >= 0.99
+
+
+def test_fp32_low_rank_direction_close_to_reference_ops():
+    """fp32 parameters: P and Psi split exactly into three bf16 parts each, the nine
+    cross products summed on the tensor cores in fp32 (every product exact), so z is the
+    fp32 product up to summation order; the scale in fp32 as torch computes it."""
+    from zotitan_b200 import kernels as K
+    m, n, r = 300, 520, 64
+    keys_p, keys_psi = [12345, 777], [4242, 31]
+    f = K.LowRankFactors((m, n), r, torch.float32, keys_p, keys_psi, "cuda")
+    got = f.directions()
+    for s in range(2):
+        z_ref, _, _ = torch_direction(m, n, r, torch.float32, keys_p[s], keys_psi[s])
+        torch.testing.assert_close(got[s], z_ref, rtol=2e-6, atol=2e-6)
+    torch.cuda.synchronize()
+    assert K.lowrank_take_error() == 0
+
+
+def test_polar_fp32_direction_from_given_factors():
+    """polar: the factors go through the reference's QR and Newton-Schulz (torch ops on the
+    small m x r and r x n matrices); the product and its uses run fused. P is split into
+    three bf16 parts, Psi (the bf16 iteration's output) is exact in bf16."""
+    from zotitan_b200 import kernels as K
+    from zotitan_b200.kernels import randn
+    from zotitan_b200.train_zo import zeropower_via_newtonschulz
+    m, n, r = 256, 384, 16
+    P = randn(99, m * r, "cuda").view(m, r)
+    P, _ = torch.linalg.qr(P)
+    Psi = zeropower_via_newtonschulz(randn(98, r * n, "cuda").view(r, n))
+    z = P @ Psi
+    z_ref = z * ((m * n) ** 0.5 / (z.norm() + 1e-7))
+    f = K.LowRankFactors.from_factors((m, n), [P], [Psi], torch.float32)
+    got = f.directions()[0]
+    torch.testing.assert_close(got, z_ref, rtol=2e-6, atol=2e-6)
+    theta = torch.randn(m, n, device="cuda") * 0.02
+    ref = theta.clone()
+    for a in (1e-3, -2e-3, 1e-3):
+        torch._foreach_add_([ref], [got], alpha=a)
+    f.apply(src=theta, dst=theta, alphas=(1e-3, -2e-3, 1e-3))
+    assert torch.equal(theta, ref)
+
+
+@pytest.mark.parametrize("dist_kind", ["low_rank", "polar"])
+def test_optimizer_fp32_fused_against_materialised(dist_kind):
+    """fp32 low_rank and polar MeZO steps through the fused kernels against the reference's
+    materialised ops with the same pair values: parameters within a few fp32 units."""
+    from zotitan_b200.objective import Score
+    from zotitan_b200.train_zo import ZOConfig, ZOOptimizer
+
+    def run(fused):
+        g = torch.Generator(device="cuda").manual_seed(8)
+        ps = [torch.nn.Parameter(torch.randn(256, 512, device="cuda", generator=g) * 0.02),
+              torch.nn.Parameter(torch.ones(512, device="cuda")),
+              torch.nn.Parameter(torch.randn(384, 256, device="cuda", generator=g) * 0.02)]
+        cfg = ZOConfig()
+        cfg.eps, cfg.z_batch, cfg.base.lr = 1e-3, 3, 5e-2
+        cfg.perturbation.distribution, cfg.perturbation.rank = dist_kind, 16
+        vals = iter([2.0, 1.9, 2.1, 2.15, 1.8, 1.75, 2.2, 2.3, 2.05, 1.95, 2.0, 2.12])
+        opt = ZOOptimizer([(f"p{i}", p) for i, p in enumerate(ps)], cfg,
+                          lambda m, b: Score(torch.tensor(next(vals), device="cuda"), {}), lowrank_fused=fused)
+        assert opt.lr_fused == ({0, 2} if fused else set())
+        for _ in range(2):
+            opt.step(None, [None] * 3)
+        torch.cuda.synchronize()
+        return [p.detach().clone() for p in ps]
+
+    for x, y in zip(run(True), run(False)):
+        torch.testing.assert_close(x, y, rtol=1e-6, atol=1e-8)

@@ -583,11 +583,12 @@ class ZOOptimizer:
                                                                      | L.ZT_PLAN_ALL_F16))
             in_pass = in_pass and world <= L.ZT_MAX_PUSH_RANKS and exchange_mode == "in_pass"
             # with copies, caches rotate between a rank's pairs, so a pair's pushes overlap the
-            # next pairs' passes (three when memory allows: measured 157 against 164 ms per step
-            # with two at 4 ranks)
+            # next pairs' passes: three from 4 ranks on when memory allows (157 against 164 ms
+            # per step with two at 4 ranks), two at 2 ranks, whose pushes to one peer already
+            # hide under the passes (3.39 against 3.29 ZO steps/s with three)
             self.zcaches = [self.zcache]
             if not in_pass:
-                n_caches = 3 if 4 * cache_bytes <= torch.cuda.mem_get_info(dev)[0] else 2
+                n_caches = 3 if world >= 4 and 4 * cache_bytes <= torch.cuda.mem_get_info(dev)[0] else 2
                 self.zcaches += [self.table.noise_cache() for _ in range(n_caches - 1)]
             if type(field_exchange) is int:
                 budget = field_exchange * slot_bytes(self.layout)
