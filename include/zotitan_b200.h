@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define ZT_ABI_VERSION 10
+#define ZT_ABI_VERSION 11
 
 /* dtypes of parameter tensors */
 #define ZT_F32 0
@@ -595,24 +595,32 @@ ZT_API int zt_linear_xent_take_error(int32_t* code);
  * Psi = randn(key_psi, r n).view(r, n).to(dtype), z = P @ Psi, then
  * z * (sqrt(m n) / (||z||_F + 1e-7)), and its uses in _apply_z (:350-351) and the grad
  * estimate (:550-556, :575-577), without z ever being written to memory. One parameter of
- * dtype ZT_BF16 or ZT_F16 at a time, for n_streams pair seeds at once. The product is the
- * fp32 sum of the r exact products in K order, rounded to the dtype: an element can differ
- * by one unit in the last place from a library GEMM that sums in another order. */
+ * dtype ZT_BF16, ZT_F16 or ZT_F32 at a time, for n_streams pair seeds at once. The product
+ * is the fp32 sum of exact products in K order, rounded to the dtype: an element can differ
+ * by one unit in the last place from a library GEMM that sums in another order. The
+ * tensor cores take 16-bit operands: for ZT_F32 the factor buffers hold bf16 values, each
+ * fp32 factor split exactly into three bf16 parts, and the nine cross products of the
+ * parts laid out along K (block (a, b) of width r holds part a of P and part b of Psi),
+ * which sum to the fp32 product P Psi. The polar distribution's factors (:307-317, QR and
+ * Newton-Schulz) come from the caller (factors_given). */
 #define ZT_LOWRANK_MAX_STREAMS 128
 
 typedef struct zt_lowrank_desc {
   int64_t m, n;     /* parameter shape, row-major, contiguous */
   int32_t r;        /* rank used: min(rank, m); 1 <= r <= kp */
-  int32_t kp;       /* padded rank: a multiple of 64, at most 1024 */
-  int32_t dtype;    /* ZT_BF16 or ZT_F16 */
+  int32_t kp;       /* padded K: a multiple of 64, at most 1024 (>= r; >= 9 r for ZT_F32 factors from keys) */
+  int32_t dtype;    /* ZT_BF16, ZT_F16 or ZT_F32: the parameter's */
   int32_t n_streams; /* 1..ZT_LOWRANK_MAX_STREAMS */
   uint32_t keys_p[ZT_LOWRANK_MAX_STREAMS];   /* noise key of P per stream: position i + 2N (:311) */
   uint32_t keys_psi[ZT_LOWRANK_MAX_STREAMS]; /* noise key of Psi per stream: position i + N (:315) */
-  void* p;          /* device [n_streams * m, kp] dtype, 16-byte aligned: P of each stream, zero-padded */
-  void* psi_t;      /* device [n_streams * n, kp] dtype, 16-byte aligned: Psi transposed, zero-padded */
+  void* p;          /* device [n_streams * m, kp] 16-bit (bf16 for ZT_F32), 16-byte aligned: P of each stream, zero-padded */
+  void* psi_t;      /* device [n_streams * n, kp], same type: Psi transposed, zero-padded */
   float* scale;     /* device [n_streams]: the dtype-rounded scale of each stream's product */
   void* workspace;  /* device, zt_lowrank_workspace_bytes, 16-byte aligned (zt_lowrank_prepare) */
   size_t workspace_bytes;
+  int32_t factors_given; /* 1: p and psi_t already hold the factors (written by the caller in the
+                            layout above); zt_lowrank_prepare then only computes the scales */
+  int32_t reserved;
 } zt_lowrank_desc;
 
 typedef struct zt_lowrank_apply_args {

@@ -183,7 +183,10 @@ def test_polar_fp32_direction_from_given_factors():
 @pytest.mark.parametrize("dist_kind", ["low_rank", "polar"])
 def test_optimizer_fp32_fused_against_materialised(dist_kind):
     """fp32 low_rank and polar MeZO steps through the fused kernels against the reference's
-    materialised ops with the same pair values: parameters within a few fp32 units."""
+    materialised ops with the same pair values. The tensor cores accumulate the split
+    products in fp32 in their own order, so z differs from the library's fp32 GEMM by up to
+    ~2e-6 of its scale (direction tests above). Here proj_grad is 50 and the update moves
+    the parameters by O(1), so the bar is 1e-5 relative plus 4e-6 absolute."""
     from zotitan_b200.objective import Score
     from zotitan_b200.train_zo import ZOConfig, ZOOptimizer
 
@@ -205,4 +208,4 @@ def test_optimizer_fp32_fused_against_materialised(dist_kind):
         return [p.detach().clone() for p in ps]
 
     for x, y in zip(run(True), run(False)):
-        torch.testing.assert_close(x, y, rtol=1e-6, atol=1e-8)
+        torch.testing.assert_close(x, y, rtol=1e-5, atol=4e-6)

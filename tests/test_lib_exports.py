@@ -32,7 +32,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version_and_key(lib):
-    assert lib.zt_abi_version() == L.ABI_VERSION == 10
+    assert lib.zt_abi_version() == L.ABI_VERSION == 11
     from oracle import philox as ph
     for seed, n, i in [(0, 1, 0), (1234, 39, 7), (2**40 + 3, 146, 145), (2**64 - 1, 448, 3)]:
         assert lib.zt_param_key(seed, n, i) == ph.param_key(seed, n, i) == (seed * n + i) & 0x7FFFFFFF
@@ -52,7 +52,8 @@ def test_struct_layouts_match_header(lib):
     assert ctypes.sizeof(L.ZtEggrollFactorArgs) == 144 and L.ZtEggrollFactorArgs.b_ext.offset == 104
     assert L.ZtEggrollFactorArgs.seeds.offset == 120 and L.ZtEggrollFactorArgs.key_index_b.offset == 136
     assert ctypes.sizeof(L.ZtEggrollNormArgs) == 88 and L.ZtEggrollNormArgs.seeds.offset == 72
-    assert ctypes.sizeof(L.ZtLowrankDesc) == 1096 and L.ZtLowrankDesc.p.offset == 1056
+    assert ctypes.sizeof(L.ZtLowrankDesc) == 1104 and L.ZtLowrankDesc.p.offset == 1056
+    assert L.ZtLowrankDesc.factors_given.offset == 1096
     assert ctypes.sizeof(L.ZtLowrankApplyArgs) == 576 and L.ZtLowrankApplyArgs.coef.offset == 44
     assert L.ZtLowrankApplyArgs.test_wait_cycles.offset == 568
     assert lib.zt_plan_workspace_bytes(0) == 8
@@ -111,7 +112,7 @@ def test_lowrank_arguments_checked_before_launch(lib):
     d.p, d.psi_t, d.scale, d.workspace, d.workspace_bytes = 256, 512, 1024, 2048, 1 << 20
     a = L.ZtLowrankApplyArgs()
     a.src, a.dst, a.n_alpha = 4096, 4096, 1
-    for field, value, code, msg in [("dtype", L.ZT_F32, L.ZT_ERR_INVALID, b"dtype"),
+    for field, value, code, msg in [("dtype", 7, L.ZT_ERR_INVALID, b"dtype"),
                                     ("kp", 48, L.ZT_ERR_INVALID, b"multiple of 64"),
                                     ("r", 65, L.ZT_ERR_INVALID, b"r <="),
                                     ("n_streams", 129, L.ZT_ERR_INVALID, b"n_streams"),

@@ -39,7 +39,7 @@ EXPORTS = ("zt_last_error", "zt_abi_version", "zt_param_key", "zt_philox_words",
 ZT_STATIC_MAX_TENSORS = 1024
 ZT_EGGROLL_MAX_PAIRS = 512
 ZT_EGGROLL_FACTOR_WORK_FLOATS = 64 * 20
-ABI_VERSION = 10
+ABI_VERSION = 11
 ZT_LOWRANK_MAX_STREAMS = 128
 ZT_IPC_HANDLE_BYTES = 64
 
@@ -135,7 +135,8 @@ class ZtLowrankDesc(ctypes.Structure):
                 ("dtype", ctypes.c_int32), ("n_streams", ctypes.c_int32),
                 ("keys_p", ctypes.c_uint32 * 128), ("keys_psi", ctypes.c_uint32 * 128),
                 ("p", ctypes.c_void_p), ("psi_t", ctypes.c_void_p), ("scale", ctypes.c_void_p),
-                ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t)]
+                ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+                ("factors_given", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
 class ZtLowrankApplyArgs(ctypes.Structure):

@@ -54,7 +54,8 @@ static_assert(sizeof(zt_pass_cfg) == 240 && offsetof(zt_pass_cfg, zcache) == 128
                   offsetof(zt_pass_cfg, zpush) == 152 && offsetof(zt_pass_cfg, zpush_stride) == 232,
               "zt_pass_cfg layout");
 static_assert(sizeof(zt_stream) == 40 && sizeof(zt_tensor) == 64, "zt_stream / zt_tensor layout");
-static_assert(sizeof(zt_lowrank_desc) == 1096 && offsetof(zt_lowrank_desc, p) == 1056 &&
+static_assert(sizeof(zt_lowrank_desc) == 1104 && offsetof(zt_lowrank_desc, p) == 1056 &&
+                  offsetof(zt_lowrank_desc, factors_given) == 1096 &&
                   sizeof(zt_lowrank_apply_args) == 576 && offsetof(zt_lowrank_apply_args, coef) == 44 &&
                   offsetof(zt_lowrank_apply_args, test_wait_cycles) == 568,
               "zt_lowrank_desc / zt_lowrank_apply_args layout");

@@ -41,17 +41,21 @@ using namespace zt::tc;
 constexpr int kThreads = 576;  // warp 0 TMA, warp 1 MMA (leader), warps 2-17 epilogue
 constexpr int kEpiWarps = 16;
 constexpr int kWarpCols = 256 / (kEpiWarps / 4);  // columns of a tile per epilogue warp (64)
-constexpr int kStages = 4;
 constexpr uint32_t kHalfRows = 128;
 constexpr uint32_t kStageA = kHalfRows * kBK * 2;
 constexpr uint32_t kStageBytes = 2 * kStageA;
 constexpr uint32_t kTile = 256;
 constexpr uint32_t kTmemCols = 2 * kTile;
-// apply epilogue: each warp stages its 32 rows x 64 columns of the scaled direction in
-// shared memory (rows padded by 16 bytes: the row-per-thread writes hit distinct banks)
-constexpr uint32_t kZRow = kWarpCols * 2 + 16;
-constexpr uint32_t kZWarp = 32 * kZRow;
-constexpr size_t kSmem = 1024 + kStages * kStageBytes + kEpiWarps * kZWarp + 256;
+// Per parameter dtype: the A/B stages, and the apply epilogue's staging of the scaled
+// direction (each warp's 32 rows x 64 columns in shared memory, rows padded by 16 bytes so
+// the row-per-thread writes hit distinct banks). fp32 parameters keep z in fp32.
+template <int DT> struct Cfg {
+  static constexpr int kStages = DT == ZT_F32 ? 2 : 4;
+  static constexpr uint32_t kEsz = DT == ZT_F32 ? 4 : 2;
+  static constexpr uint32_t kZRow = kWarpCols * kEsz + 16;
+  static constexpr uint32_t kZWarp = 32 * kZRow;
+  static constexpr size_t kSmem = 1024 + kStages * kStageBytes + kEpiWarps * kZWarp + 256;
+};
 constexpr int kGroupN = 16;
 constexpr int kPartials = 2 * kEpiWarps;  // per (tile, stream): one per epilogue warp of the pair
 constexpr uint32_t kIdescBf16 = idesc_bf16(256, 256);
@@ -59,8 +63,12 @@ constexpr uint32_t kIdescF16 = idesc_f16(256, 256);
 
 __device__ int g_lowrank_error = 0;
 
-// 16-bit storage <-> fp32 and rounding of the two dtypes the tensor cores take here.
+// 16-bit storage <-> fp32 and rounding of the parameter dtypes (fp32: no rounding).
 template <int DT> struct H;
+template <> struct H<ZT_F32> {
+  __device__ static __forceinline__ float round(float x) { return x; }
+  __device__ static __forceinline__ void round2(float&, float&) {}
+};
 template <> struct H<ZT_BF16> {
   __device__ static __forceinline__ float lo(uint32_t w) { return __uint_as_float(w << 16); }
   __device__ static __forceinline__ float hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
@@ -96,14 +104,40 @@ struct FactorKeys {
   uint32_t psi[ZT_LOWRANK_MAX_STREAMS];
 };
 
+// Part `part` (0, 1, 2) of the exact three-way bf16 split of an fp32 value: x = hi + mid
+// + lo with hi = bf16(x), mid = bf16(x - hi), lo = x - hi - mid (each difference exact in
+// fp32, and lo has at most 8 significant bits, so it is exact in bf16).
+__device__ __forceinline__ float split3(float x, int part) {
+  const float hi = zt::Dt<ZT_BF16>::round(x);
+  if (part == 0) return hi;
+  const float r1 = __fsub_rn(x, hi);
+  const float mid = zt::Dt<ZT_BF16>::round(r1);
+  if (part == 1) return mid;
+  return __fsub_rn(r1, mid);
+}
+
+// Factor value at K position kk of a row: the factor itself for 16-bit parameters
+// (k = kk < r, else 0); for fp32 parameters the 9-block split layout, block (a, b) =
+// kk / r holding part a of P on the P rows and part b of Psi on the Psi rows, so that the
+// product of the two buffers sums all nine exact cross products.
+template <int DT>
+__device__ __forceinline__ float factor_at(int32_t kk, int32_t r, bool is_p, uint32_t ctr_base, uint32_t ctr_step,
+                                           uint32_t key) {
+  if (DT != ZT_F32) return kk < r ? zt::gauss(ctr_base + (uint32_t)kk * ctr_step, key) : 0.0f;
+  if (kk >= 9 * r) return 0.0f;
+  const int32_t blk = kk / r, k = kk - blk * r;
+  return split3(zt::gauss(ctr_base + (uint32_t)k * ctr_step, key), is_p ? blk / 3 : blk % 3);
+}
+
 // Row `row` of the stacked factor buffers, 8 consecutive K positions per thread:
 // rows [0, S m) are P (stream row / m, element i = row % m: P[i, k] = noise(i r + k)),
-// rows [S m, S (m + n)) are Psi^T (element j: Psi[k, j] = noise(k n + j)); K positions
-// k >= r are zero.
+// rows [S m, S (m + n)) are Psi^T (element j: Psi[k, j] = noise(k n + j)); the operand
+// format is the parameter's (bf16 splits for fp32 parameters).
 template <int DT>
 __global__ void __launch_bounds__(256) lr_factor_kernel(const __grid_constant__ FactorKeys K, uint16_t* __restrict__ p,
                                                         uint16_t* __restrict__ psi_t, int32_t S, int32_t m, int32_t n,
                                                         int32_t r, int32_t kp) {
+  constexpr int OT = DT == ZT_F16 ? ZT_F16 : ZT_BF16;  // operand type
   const int32_t groups = kp / 8;
   const int64_t rows = (int64_t)S * ((int64_t)m + n);
   const int64_t total = rows * groups;
@@ -115,24 +149,18 @@ __global__ void __launch_bounds__(256) lr_factor_kernel(const __grid_constant__ 
       const int32_t s = (int32_t)(row / m), i = (int32_t)(row - (int64_t)s * m);
       const uint32_t key = K.p[s];
 #pragma unroll
-      for (int e = 0; e < 8; e += 2) {
-        const int32_t ka = k0 + e, kb = k0 + e + 1;
-        const float a = ka < r ? zt::gauss((uint32_t)(i * r + ka), key) : 0.0f;
-        const float b = kb < r ? zt::gauss((uint32_t)(i * r + kb), key) : 0.0f;
-        w[e / 2] = H<DT>::pack(a, b);
-      }
+      for (int e = 0; e < 8; e += 2)
+        w[e / 2] = H<OT>::pack(factor_at<DT>(k0 + e, r, true, (uint32_t)(i * r), 1u, key),
+                               factor_at<DT>(k0 + e + 1, r, true, (uint32_t)(i * r), 1u, key));
       *reinterpret_cast<uint4*>(p + row * kp + k0) = make_uint4(w[0], w[1], w[2], w[3]);
     } else {
       const int64_t rr = row - (int64_t)S * m;
       const int32_t s = (int32_t)(rr / n), j = (int32_t)(rr - (int64_t)s * n);
       const uint32_t key = K.psi[s];
 #pragma unroll
-      for (int e = 0; e < 8; e += 2) {
-        const int32_t ka = k0 + e, kb = k0 + e + 1;
-        const float a = ka < r ? zt::gauss((uint32_t)(ka * n + j), key) : 0.0f;
-        const float b = kb < r ? zt::gauss((uint32_t)(kb * n + j), key) : 0.0f;
-        w[e / 2] = H<DT>::pack(a, b);
-      }
+      for (int e = 0; e < 8; e += 2)
+        w[e / 2] = H<OT>::pack(factor_at<DT>(k0 + e, r, false, (uint32_t)j, (uint32_t)n, key),
+                               factor_at<DT>(k0 + e + 1, r, false, (uint32_t)j, (uint32_t)n, key));
       *reinterpret_cast<uint4*>(psi_t + rr * kp + k0) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
@@ -147,9 +175,9 @@ enum : int { kModeNorm = 0, kModeTheta = 1, kModeGe = 2, kModeBoth = 3 };
 struct LrParams {
   CUtensorMap tmap_a;  // stacked P    [S m, kp], box {64, 128}
   CUtensorMap tmap_b;  // stacked Psi^T [S n, kp], box {64, 128}
-  const uint16_t* src;  // parameter read by stream 0 (later streams read dst)
-  uint16_t* dst;        // parameter written (nullptr: no parameter update)
-  uint16_t* ge;         // grad estimate (nullptr: none)
+  const void* src;      // parameter read by stream 0 (later streams read dst)
+  void* dst;            // parameter written (nullptr: no parameter update)
+  void* ge;             // grad estimate (nullptr: none)
   const float* scale;   // [S] rounded scale of each stream's direction
   float* partial;       // norm mode: [tiles * S][kPartials]
   float alpha[3];
@@ -173,22 +201,32 @@ __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, 
 }
 
 // Phase 1 of the apply epilogue: 32 accumulator columns of this thread's row ->
-// zs = round(round(acc) * sc), packed, into the warp's staging rows in shared memory.
+// zs = round(round(acc) * sc) into the warp's staging row (packed 16-bit values, or fp32
+// for fp32 parameters, where nothing is rounded).
 template <int DT>
 __device__ __forceinline__ void stage_chunk(const uint32_t (&acc)[32], float sc, uint4* dst) {
+  if constexpr (DT == ZT_F32) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint32_t w[4];
+    for (int i = 0; i < 8; ++i)
+      dst[i] = make_uint4(__float_as_uint(__fmul_rn(__uint_as_float(acc[4 * i]), sc)),
+                          __float_as_uint(__fmul_rn(__uint_as_float(acc[4 * i + 1]), sc)),
+                          __float_as_uint(__fmul_rn(__uint_as_float(acc[4 * i + 2]), sc)),
+                          __float_as_uint(__fmul_rn(__uint_as_float(acc[4 * i + 3]), sc)));
+  } else {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int j = 4 * i + k;
-      float za = __uint_as_float(acc[2 * j]), zb = __uint_as_float(acc[2 * j + 1]);
-      H<DT>::round2(za, zb);
-      za = __fmul_rn(za, sc);
-      zb = __fmul_rn(zb, sc);
-      w[k] = H<DT>::pack(za, zb);   // the second rounding
+    for (int i = 0; i < 4; ++i) {
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int j = 4 * i + k;
+        float za = __uint_as_float(acc[2 * j]), zb = __uint_as_float(acc[2 * j + 1]);
+        H<DT>::round2(za, zb);
+        za = __fmul_rn(za, sc);
+        zb = __fmul_rn(zb, sc);
+        w[k] = H<DT>::pack(za, zb);   // the second rounding
+      }
+      dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
     }
-    dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -225,24 +263,72 @@ __device__ __forceinline__ void apply8(uint4& th, uint4& gv, const uint4 zs, con
   gv = make_uint4(gw[0], gw[1], gw[2], gw[3]);
 }
 
+// The same on 8 fp32 elements (two 16-byte words each): no rounding, fused multiply-adds.
+template <bool TH, bool GE, typename PT>
+__device__ __forceinline__ void apply8_f32(uint4 (&th)[2], uint4 (&gv)[2], const uint4 (&zs)[2], const PT& P, float c,
+                                           bool init) {
+#pragma unroll
+  for (int w = 0; w < 2; ++w) {
+    const float z[4] = {__uint_as_float(zs[w].x), __uint_as_float(zs[w].y), __uint_as_float(zs[w].z),
+                        __uint_as_float(zs[w].w)};
+    float x[4] = {__uint_as_float(th[w].x), __uint_as_float(th[w].y), __uint_as_float(th[w].z),
+                  __uint_as_float(th[w].w)};
+    float g[4] = {__uint_as_float(gv[w].x), __uint_as_float(gv[w].y), __uint_as_float(gv[w].z),
+                  __uint_as_float(gv[w].w)};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (TH) {
+#pragma unroll
+        for (int t = 0; t < 3; ++t)
+          if (t < P.n_alpha) x[e] = __fmaf_rn(z[e], P.alpha[t], x[e]);
+      }
+      if (GE) g[e] = init ? __fmul_rn(z[e], c) : __fmaf_rn(z[e], c, g[e]);
+    }
+    th[w] = make_uint4(__float_as_uint(x[0]), __float_as_uint(x[1]), __float_as_uint(x[2]), __float_as_uint(x[3]));
+    gv[w] = make_uint4(__float_as_uint(g[0]), __float_as_uint(g[1]), __float_as_uint(g[2]), __float_as_uint(g[3]));
+  }
+}
+
+template <int DT, bool TH, bool GE, int VW, typename PT>
+__device__ __forceinline__ void apply8v(uint4 (&th)[VW], uint4 (&gv)[VW], const uint4 (&zs)[VW], const PT& P, float c,
+                                        bool init) {
+  if constexpr (DT == ZT_F32)
+    apply8_f32<TH, GE>(th, gv, zs, P, c, init);
+  else
+    apply8<DT, TH, GE>(th[0], gv[0], zs[0], P, c, init);
+}
+
 // The same element by element for columns below `n` (rows whose length is not a multiple
-// of 8 or buffers not 16-byte aligned).
-template <int DT>
-__device__ __forceinline__ void apply_scalar8(const uint16_t* srow, uint16_t* drow, uint16_t* grow, int col,
-                                              const uint4 zs, const LrParams& P, float c, bool init) {
-  const uint32_t zw[4] = {zs.x, zs.y, zs.z, zs.w};
+// of 8 or buffers not 16-byte aligned); row pointers and the staged row as bytes.
+template <int DT, typename PT>
+__device__ __forceinline__ void apply_scalar8(const uint8_t* srow, uint8_t* drow, uint8_t* grow, int col,
+                                              const uint8_t* zrow, const PT& P, float c, bool init) {
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     if (col + e >= P.n) continue;
-    const float z = (e & 1) ? H<DT>::hi(zw[e >> 1]) : H<DT>::lo(zw[e >> 1]);
-    if (drow) {
-      float x = H<DT>::val(srow[col + e]);
-      for (int t = 0; t < P.n_alpha; ++t) x = H<DT>::round(__fmaf_rn(z, P.alpha[t], x));
-      drow[col + e] = H<DT>::bits(x);
-    }
-    if (grow) {
-      const float gv = init ? __fmul_rn(z, c) : __fmaf_rn(z, c, H<DT>::val(grow[col + e]));
-      grow[col + e] = H<DT>::bits(gv);
+    if constexpr (DT == ZT_F32) {
+      const float z = reinterpret_cast<const float*>(zrow)[e];
+      if (drow) {
+        float x = reinterpret_cast<const float*>(srow)[col + e];
+        for (int t = 0; t < P.n_alpha; ++t) x = __fmaf_rn(z, P.alpha[t], x);
+        reinterpret_cast<float*>(drow)[col + e] = x;
+      }
+      if (grow) {
+        float* g = reinterpret_cast<float*>(grow) + col + e;
+        *g = init ? __fmul_rn(z, c) : __fmaf_rn(z, c, *g);
+      }
+    } else {
+      const float z = H<DT>::val(reinterpret_cast<const uint16_t*>(zrow)[e]);
+      if (drow) {
+        float x = H<DT>::val(reinterpret_cast<const uint16_t*>(srow)[col + e]);
+        for (int t = 0; t < P.n_alpha; ++t) x = H<DT>::round(__fmaf_rn(z, P.alpha[t], x));
+        reinterpret_cast<uint16_t*>(drow)[col + e] = H<DT>::bits(x);
+      }
+      if (grow) {
+        uint16_t* g = reinterpret_cast<uint16_t*>(grow) + col + e;
+        const float gv = init ? __fmul_rn(z, c) : __fmaf_rn(z, c, H<DT>::val(*g));
+        *g = H<DT>::bits(gv);
+      }
     }
   }
 }
@@ -250,6 +336,8 @@ __device__ __forceinline__ void apply_scalar8(const uint16_t* srow, uint16_t* dr
 template <int DT, int MODE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     lr_gemm_kernel(const __grid_constant__ LrParams P) {
+  constexpr int kStages = Cfg<DT>::kStages;
+  constexpr uint32_t kZRow = Cfg<DT>::kZRow, kZWarp = Cfg<DT>::kZWarp, kEsz = Cfg<DT>::kEsz;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t* stage_base = smem;
@@ -346,7 +434,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const uint32_t sb = sa + kStageA;
 #pragma unroll
             for (int k = 0; k < kBK / kUmmaK; ++k) {
-              if (DT == ZT_BF16)
+              if (DT != ZT_F16)  // bf16 operands (bf16 splits for fp32 parameters)
                 umma_bf16_pair<kIdescBf16>(tmem_d, umma_desc(sa + k * kUmmaK * 2),
                                                      umma_desc(sb + k * kUmmaK * 2), (kb | k) != 0);
               else
@@ -389,23 +477,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         constexpr bool GE = MODE == kModeGe || MODE == kModeBoth;
         constexpr int kLanesPerRow = kWarpCols / 8, kRowsPerStep = 32 / kLanesPerRow;
         constexpr int kSteps = 32 / kRowsPerStep;
-        constexpr int kBatch = (TH && GE) ? kSteps / 2 : kSteps;  // loads in flight per lane
+        constexpr int kVW = DT == ZT_F32 ? 2 : 1;  // 16-byte words per 8 elements
+        constexpr int kBatch = ((TH && GE) ? kSteps / 2 : kSteps) / kVW;  // row steps in flight per lane
         const bool init = P.ge_init && st == 0;
-        const uint16_t* src = st == 0 ? P.src : P.dst;
+        const uint8_t* src = static_cast<const uint8_t*>(st == 0 ? P.src : P.dst);
+        uint8_t* dstb = static_cast<uint8_t*>(P.dst);
+        uint8_t* geb = static_cast<uint8_t*>(P.ge);
         const int rbase = mt * (int)kTile + (int)rank * (int)kHalfRows + q * 32;
         const int cg = (lane % kLanesPerRow) * 8;
         const int rsub = lane / kLanesPerRow;
         const int col = colh + cg;
         const bool col_ok = col < P.n;
-        uint4 th[kBatch], gv[kBatch];
+        uint4 th[kBatch][kVW], gv[kBatch][kVW];
         auto load_batch = [&](int i0) {
 #pragma unroll
           for (int i = 0; i < kBatch; ++i) {
             const int row = rbase + kRowsPerStep * (i0 + i) + rsub;
             if (row < P.m && col_ok) {
-              const size_t off = (size_t)row * P.n + col;
-              if (TH) th[i] = *reinterpret_cast<const uint4*>(src + off);
-              if (GE && !init) gv[i] = *reinterpret_cast<const uint4*>(P.ge + off);
+              const size_t off = ((size_t)row * P.n + col) * kEsz;
+#pragma unroll
+              for (int w = 0; w < kVW; ++w) {
+                if (TH) th[i][w] = reinterpret_cast<const uint4*>(src + off)[w];
+                if (GE && !init) gv[i][w] = reinterpret_cast<const uint4*>(geb + off)[w];
+              }
             }
           }
         };
@@ -452,13 +546,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           for (int c = 0; c < kWarpCols / 32; ++c) {
             uint32_t acc[32];
             tmem_ld32(taddr + (uint32_t)(c * 32), acc);
-            stage_chunk<DT>(acc, sc, reinterpret_cast<uint4*>(zw + lane * kZRow + c * 64));
+            stage_chunk<DT>(acc, sc, reinterpret_cast<uint4*>(zw + lane * kZRow + c * 32 * kEsz));
           }
           asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(b ? leader_acce1 : leader_acce0);
           // phase 2: four rows per step, 8 lanes per row, 8 consecutive columns per lane
-          // (coalesced 128-byte row segments)
+          // (coalesced 128- or 256-byte row segments)
           const float c = P.coef[st];
           if (vec) {
 #pragma unroll 1
@@ -469,11 +563,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const int rl = kRowsPerStep * (i0 + i) + rsub;
                 const int row = rbase + rl;
                 if (row < P.m && col_ok) {
-                  const uint4 zs = *reinterpret_cast<const uint4*>(zw + rl * kZRow + cg * 2);
-                  const size_t off = (size_t)row * P.n + col;
-                  apply8<DT, TH, GE>(th[i], gv[i], zs, P, c, init);
-                  if (TH) *reinterpret_cast<uint4*>(P.dst + off) = th[i];
-                  if (GE) *reinterpret_cast<uint4*>(P.ge + off) = gv[i];
+                  uint4 zs[kVW];
+#pragma unroll
+                  for (int w = 0; w < kVW; ++w) zs[w] = reinterpret_cast<const uint4*>(zw + rl * kZRow + cg * kEsz)[w];
+                  const size_t off = ((size_t)row * P.n + col) * kEsz;
+                  apply8v<DT, TH, GE>(th[i], gv[i], zs, P, c, init);
+#pragma unroll
+                  for (int w = 0; w < kVW; ++w) {
+                    if (TH) reinterpret_cast<uint4*>(dstb + off)[w] = th[i][w];
+                    if (GE) reinterpret_cast<uint4*>(geb + off)[w] = gv[i][w];
+                  }
                 }
               }
             }
@@ -483,10 +582,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               const int rl = kRowsPerStep * i + rsub;
               const int row = rbase + rl;
               if (row >= P.m || !col_ok) continue;
-              const uint4 zs = *reinterpret_cast<const uint4*>(zw + rl * kZRow + cg * 2);
-              const size_t roff = (size_t)row * P.n;
-              apply_scalar8<DT>(TH ? src + roff : nullptr, TH ? P.dst + roff : nullptr, GE ? P.ge + roff : nullptr,
-                                col, zs, P, c, init);
+              const uint8_t* zrow = zw + rl * kZRow + cg * kEsz;
+              const size_t roff = (size_t)row * P.n * kEsz;
+              apply_scalar8<DT>(TH ? src + roff : nullptr, TH ? dstb + roff : nullptr, GE ? geb + roff : nullptr, col,
+                                zrow, P, c, init);
             }
           }
           __syncwarp();  // every lane has read the staging rows before the next item rewrites them
@@ -848,7 +947,7 @@ int pairs_for(Kern kern, size_t smem, int (&cache)[64], int* pairs) {
 template <int DT, int MODE>
 int prepare_gemm(int* pairs) {
   static int cache[64] = {0};
-  return pairs_for(lr_gemm_kernel<DT, MODE>, kSmem, cache, pairs);
+  return pairs_for(lr_gemm_kernel<DT, MODE>, Cfg<DT>::kSmem, cache, pairs);
 }
 
 int64_t tiles_of(int64_t m, int64_t n) { return ((m + kTile - 1) / kTile) * ((n + kTile - 1) / kTile); }
@@ -856,12 +955,14 @@ int64_t tiles_of(int64_t m, int64_t n) { return ((m + kTile - 1) / kTile) * ((n 
 int check_desc(const zt_lowrank_desc* d, const char* who) {
   if (!d) return zt::set_error(ZT_ERR_INVALID, std::string(who) + ": null descriptor");
   if (d->m <= 0 || d->n <= 0) return zt::set_error(ZT_ERR_INVALID, std::string(who) + ": m and n must be positive");
-  if (d->dtype != ZT_BF16 && d->dtype != ZT_F16)
-    return zt::set_error(ZT_ERR_INVALID, std::string(who) + ": dtype must be ZT_BF16 or ZT_F16");
+  if (d->dtype != ZT_BF16 && d->dtype != ZT_F16 && d->dtype != ZT_F32)
+    return zt::set_error(ZT_ERR_INVALID, std::string(who) + ": dtype must be ZT_BF16, ZT_F16 or ZT_F32");
   if (d->kp <= 0 || d->kp % kBK || d->kp > 1024)
     return zt::set_error(ZT_ERR_INVALID, std::string(who) + ": kp must be a positive multiple of 64, at most 1024");
   if (d->r < 1 || d->r > d->kp || d->r > d->m)
     return zt::set_error(ZT_ERR_INVALID, std::string(who) + ": need 1 <= r <= min(kp, m)");
+  if (d->dtype == ZT_F32 && !d->factors_given && d->kp < 9 * d->r)
+    return zt::set_error(ZT_ERR_INVALID, std::string(who) + ": fp32 factors from the noise source need kp >= 9 r");
   if (d->n_streams < 1 || d->n_streams > ZT_LOWRANK_MAX_STREAMS)
     return zt::set_error(ZT_ERR_INVALID, std::string(who) + ": n_streams must be in [1, ZT_LOWRANK_MAX_STREAMS]");
   const int64_t S = d->n_streams;
@@ -892,7 +993,7 @@ int launch_gemm(const zt_lowrank_desc* d, LrParams& P, cudaStream_t st, const ch
   P.scale = d->scale;
   const int64_t tiles = (int64_t)P.m_tiles * P.n_tiles;
   const int clusters = tiles < pairs ? (int)tiles : pairs;
-  lr_gemm_kernel<DT, MODE><<<2 * clusters, kThreads, kSmem, st>>>(P);
+  lr_gemm_kernel<DT, MODE><<<2 * clusters, kThreads, Cfg<DT>::kSmem, st>>>(P);
   return zt::check_cuda(cudaGetLastError(), (std::string(who) + ": launch").c_str());
 }
 
@@ -942,12 +1043,14 @@ int prepare_impl(const zt_lowrank_desc* d, cudaStream_t st) {
     K.p[s] = d->keys_p[s];
     K.psi[s] = d->keys_psi[s];
   }
-  const int64_t total = (int64_t)d->n_streams * (d->m + d->n) * (d->kp / 8);
-  const int64_t want = (total + 255) / 256, cap = (int64_t)zt::sm_count() * 16;
-  lr_factor_kernel<DT><<<(unsigned)(want < cap ? want : cap), 256, 0, st>>>(
-      K, static_cast<uint16_t*>(d->p), static_cast<uint16_t*>(d->psi_t), d->n_streams, (int32_t)d->m, (int32_t)d->n,
-      d->r, d->kp);
-  if (int rc = zt::check_cuda(cudaGetLastError(), "zt_lowrank_prepare: factor launch")) return rc;
+  if (!d->factors_given) {
+    const int64_t total = (int64_t)d->n_streams * (d->m + d->n) * (d->kp / 8);
+    const int64_t want = (total + 255) / 256, cap = (int64_t)zt::sm_count() * 16;
+    lr_factor_kernel<DT><<<(unsigned)(want < cap ? want : cap), 256, 0, st>>>(
+        K, static_cast<uint16_t*>(d->p), static_cast<uint16_t*>(d->psi_t), d->n_streams, (int32_t)d->m,
+        (int32_t)d->n, d->r, d->kp);
+    if (int rc = zt::check_cuda(cudaGetLastError(), "zt_lowrank_prepare: factor launch")) return rc;
+  }
   LrParams P;
   memset(&P, 0, sizeof(P));
   P.partial = static_cast<float*>(d->workspace);
@@ -980,7 +1083,9 @@ int zt_lowrank_prepare(const zt_lowrank_desc* d, void* stream) {
     return zt::set_error(ZT_ERR_INVALID, "zt_lowrank_prepare: workspace missing, misaligned or below "
                                          "zt_lowrank_workspace_bytes");
   const cudaStream_t st = zt::as_stream(stream);
-  return d->dtype == ZT_BF16 ? prepare_impl<ZT_BF16>(d, st) : prepare_impl<ZT_F16>(d, st);
+  return d->dtype == ZT_BF16 ? prepare_impl<ZT_BF16>(d, st)
+         : d->dtype == ZT_F16 ? prepare_impl<ZT_F16>(d, st)
+                              : prepare_impl<ZT_F32>(d, st);
 }
 
 int zt_lowrank_apply(const zt_lowrank_desc* d, const zt_lowrank_apply_args* a, void* stream) {
@@ -994,7 +1099,8 @@ int zt_lowrank_apply(const zt_lowrank_desc* d, const zt_lowrank_apply_args* a, v
   if (a->n_alpha == 0 && a->dst)
     return zt::set_error(ZT_ERR_INVALID, "zt_lowrank_apply: dst given without coefficients");
   if (!a->dst && !a->ge) return zt::set_error(ZT_ERR_INVALID, "zt_lowrank_apply: nothing to write");
-  const size_t bytes = (size_t)d->m * (size_t)d->n * 2;
+  const size_t esz = d->dtype == ZT_F32 ? 4 : 2;
+  const size_t bytes = (size_t)d->m * (size_t)d->n * esz;
   if (a->src && a->dst && a->src != a->dst) {
     const uintptr_t s0 = (uintptr_t)a->src, d0 = (uintptr_t)a->dst;
     if (s0 < d0 + bytes && d0 < s0 + bytes)
@@ -1005,12 +1111,12 @@ int zt_lowrank_apply(const zt_lowrank_desc* d, const zt_lowrank_apply_args* a, v
     if (g0 < d0 + bytes && d0 < g0 + bytes) return zt::set_error(ZT_ERR_INVALID, "zt_lowrank_apply: ge overlaps dst");
   }
   for (const void* p : {a->src, (const void*)a->dst, (const void*)a->ge})
-    if (((uintptr_t)p & 1) != 0) return zt::set_error(ZT_ERR_INVALID, "zt_lowrank_apply: misaligned parameter buffer");
+    if (((uintptr_t)p & (esz - 1)) != 0) return zt::set_error(ZT_ERR_INVALID, "zt_lowrank_apply: misaligned parameter buffer");
   LrParams P;
   memset(&P, 0, sizeof(P));
-  P.src = static_cast<const uint16_t*>(a->src);
-  P.dst = static_cast<uint16_t*>(a->dst);
-  P.ge = static_cast<uint16_t*>(a->ge);
+  P.src = a->src;
+  P.dst = a->dst;
+  P.ge = a->ge;
   P.n_alpha = a->n_alpha;
   for (int i = 0; i < 3; ++i) P.alpha[i] = a->alpha[i];
   P.ge_init = a->ge_init ? 1 : 0;
@@ -1023,6 +1129,10 @@ int zt_lowrank_apply(const zt_lowrank_desc* d, const zt_lowrank_apply_args* a, v
   P.wait_cycles = a->test_wait_cycles > 0 ? (long long)a->test_wait_cycles : kWaitCycles;
   const cudaStream_t st = zt::as_stream(stream);
   const bool th = a->dst != nullptr, ge = a->ge != nullptr;
+  if (d->dtype == ZT_F32)
+    return th && ge ? launch_gemm<ZT_F32, kModeBoth>(d, P, st, who)
+           : th     ? launch_gemm<ZT_F32, kModeTheta>(d, P, st, who)
+                    : launch_gemm<ZT_F32, kModeGe>(d, P, st, who);
   if (vec) {  // whole 16-byte row groups at aligned addresses: the slice-resident kernel
     if (d->dtype == ZT_BF16)
       return th && ge ? launch_tile<ZT_BF16, kModeBoth>(d, a, st)

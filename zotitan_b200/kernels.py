@@ -776,14 +776,23 @@ def lora_split(a: torch.Tensor) -> torch.Tensor:
 
 # ---- low-rank directions (distribution "low_rank") -----------------------------------
 
-_LR_DTYPES = {torch.bfloat16: L.ZT_BF16, torch.float16: L.ZT_F16}
+_LR_DTYPES = {torch.bfloat16: L.ZT_BF16, torch.float16: L.ZT_F16, torch.float32: L.ZT_F32}
 
 
 def lowrank_supported(p: torch.Tensor) -> bool:
-    """Whether zt_lowrank_* take this parameter: a contiguous 2-D bf16 or f16 CUDA tensor
-    at an even address (the product runs on the tensor cores, which have no fp32 kind)."""
-    return (p.is_cuda and p.dim() == 2 and p.dtype in _LR_DTYPES and p.is_contiguous() and p.data_ptr() % 2 == 0
-            and p.numel() > 0)
+    """Whether zt_lowrank_* take this parameter: a contiguous 2-D bf16, f16 or fp32 CUDA
+    tensor at an address aligned to its element size."""
+    return (p.is_cuda and p.dim() == 2 and p.dtype in _LR_DTYPES and p.is_contiguous()
+            and p.data_ptr() % p.element_size() == 0 and p.numel() > 0)
+
+
+def _split3(x: torch.Tensor) -> list:
+    """The exact three-way bf16 split of an fp32 tensor: x = hi + mid + lo."""
+    hi = x.bfloat16()
+    r1 = x - hi.float()
+    mid = r1.bfloat16()
+    lo = (r1 - mid.float()).bfloat16()
+    return [hi, mid, lo]
 
 
 class LowRankFactors:
@@ -795,17 +804,23 @@ class LowRankFactors:
     keys_p / keys_psi are the noise keys of P and Psi (positions i + 2N and i + N of the
     reference's _sample_z, zotitan/train_zo.py:311-315)."""
 
-    def __init__(self, shape, r: int, dtype: torch.dtype, keys_p, keys_psi, device):
+    def __init__(self, shape, r: int, dtype: torch.dtype, keys_p, keys_psi, device, _given=None):
         m, n = int(shape[0]), int(shape[1])
         S = len(keys_p)
         if not 1 <= S <= L.ZT_LOWRANK_MAX_STREAMS or len(keys_psi) != S:
             raise ValueError(f"1..{L.ZT_LOWRANK_MAX_STREAMS} streams with one P and one Psi key each")
         if dtype not in _LR_DTYPES:
-            raise ValueError("low-rank directions on the tensor cores take bf16 or f16 parameters")
-        kp = 64 * ((r + 63) // 64)
+            raise ValueError("low-rank directions take bf16, f16 or fp32 parameters")
+        # fp32: nine blocks of r along K (the cross products of the three-way bf16 splits)
+        width = 9 * r if dtype == torch.float32 else r
+        kp = 64 * ((width + 63) // 64)
+        op = torch.float16 if dtype == torch.float16 else torch.bfloat16
         self.shape, self.r, self.kp, self.dtype, self.n_streams = (m, n), r, kp, dtype, S
-        self.p = torch.empty((S * m, kp), dtype=dtype, device=device)
-        self.psi_t = torch.empty((S * n, kp), dtype=dtype, device=device)
+        if _given is None:
+            self.p = torch.empty((S * m, kp), dtype=op, device=device)
+            self.psi_t = torch.empty((S * n, kp), dtype=op, device=device)
+        else:
+            self.p, self.psi_t = _given
         self.scale = torch.empty(S, dtype=torch.float32, device=device)
         lib = L.load()
         ws = ctypes.c_size_t()
@@ -817,10 +832,37 @@ class LowRankFactors:
             d.keys_p[s], d.keys_psi[s] = int(keys_p[s]), int(keys_psi[s])
         d.p, d.psi_t, d.scale = self.p.data_ptr(), self.psi_t.data_ptr(), self.scale.data_ptr()
         d.workspace, d.workspace_bytes = self._ws.data_ptr(), self._ws.numel()
+        d.factors_given = 1 if _given is not None else 0
         self.desc = d
         self.device = torch.device(device)
         with torch.cuda.device(self.device):
             L.check(lib.zt_lowrank_prepare(ctypes.byref(d), _stream_ptr(self.device)), "zt_lowrank_prepare")
+
+    @classmethod
+    def from_factors(cls, shape, Ps: list, Psis: list, dtype: torch.dtype) -> "LowRankFactors":
+        """Directions from factors computed by the caller (the polar distribution: P after
+        QR, Psi after the Newton-Schulz iteration, zotitan/train_zo.py:307-317), one
+        (P [m, r], Psi [r, n]) per stream, in the parameter dtype. Only the product, its
+        norm and its uses run here."""
+        m, n = int(shape[0]), int(shape[1])
+        S, r = len(Ps), int(Ps[0].shape[1])
+        dev = Ps[0].device
+        width = 9 * r if dtype == torch.float32 else r
+        kp = 64 * ((width + 63) // 64)
+        op = torch.float16 if dtype == torch.float16 else torch.bfloat16
+        A = torch.zeros((S * m, kp), dtype=op, device=dev)
+        B = torch.zeros((S * n, kp), dtype=op, device=dev)
+        for s, (P, Psi) in enumerate(zip(Ps, Psis)):
+            P, Psi = P.to(dtype), Psi.to(dtype)
+            if dtype == torch.float32:
+                ps, qs = _split3(P), _split3(Psi.t())
+                for blk in range(9):
+                    A[s * m:(s + 1) * m, blk * r:(blk + 1) * r] = ps[blk // 3]
+                    B[s * n:(s + 1) * n, blk * r:(blk + 1) * r] = qs[blk % 3]
+            else:
+                A[s * m:(s + 1) * m, :r] = P
+                B[s * n:(s + 1) * n, :r] = Psi.t()
+        return cls(shape, r, dtype, [0] * S, [0] * S, dev, _given=(A, B))
 
     def apply(self, src: torch.Tensor | None = None, dst: torch.Tensor | None = None, alphas=(), ge=None, coefs=None,
               ge_init: bool = False, test_stall_loads: bool = False, test_wait_cycles: int = 0) -> None:
@@ -865,6 +907,7 @@ class LowRankFactors:
             ctypes.pointer(d)[0] = self.desc
             esz = self.p.element_size()
             d.n_streams = 1
+            d.factors_given = 1
             d.keys_p[0], d.keys_psi[0] = self.desc.keys_p[s], self.desc.keys_psi[s]
             d.p = self.p.data_ptr() + s * m * self.kp * esz
             d.psi_t = self.psi_t.data_ptr() + s * n * self.kp * esz

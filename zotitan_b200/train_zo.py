@@ -514,10 +514,12 @@ class ZOOptimizer:
         # low_rank / polar: 2-D tensors take materialised directions, 1-D ones the fused passes
         self.lr_idx = [i for i, p in enumerate(self.params) if p.dim() >= 2] if pl.materialized else []
         lr_set = set(self.lr_idx)
-        # distribution "low_rank" on bf16/f16 matrices: the direction is recomputed on the
+        # low_rank matrices, and polar ones in fp32 (the reference's QR has no 16-bit CUDA
+        # kernel, so its polar branch runs only there): the direction is recomputed on the
         # tensor cores inside each use (zt_lowrank_*), never stored
-        self.lr_fused = {i for i in self.lr_idx if lowrank_fused and cfg.perturbation.distribution == "low_rank"
-                         and K.lowrank_supported(self.params[i])}
+        dist_kind = cfg.perturbation.distribution
+        self.lr_fused = {i for i in self.lr_idx if lowrank_fused and K.lowrank_supported(self.params[i])
+                         and (dist_kind == "low_rank" or self.params[i].dtype == torch.float32)}
         self.dense_idx = [i for i in range(len(self.params)) if i not in lr_set]
         # grad_est buffer of the on-the-fly accumulation (same size as the reference's
         # zeros_like grad_est for z_batch > 1; dense tensors only)
@@ -642,8 +644,23 @@ class ZOOptimizer:
         p = self.params[i]
         n = len(self.params)
         r = min(self.cfg.perturbation.rank, p.shape[0])
+        if self.cfg.perturbation.distribution == "polar":   # factors through QR / Newton-Schulz
+            Ps, Psis = zip(*(self._polar_factors(i, sd) for sd in seeds))
+            return K.LowRankFactors.from_factors(p.shape, list(Ps), list(Psis), p.dtype)
         return K.LowRankFactors(p.shape, r, p.dtype, [param_key(sd, n, i + 2 * n) for sd in seeds],
                                 [param_key(sd, n, i + n) for sd in seeds], p.device)
+
+    def _polar_factors(self, i: int, seed: int):
+        """P (QR of the noise factor) and Psi (Newton-Schulz polar factor) of the reference's
+        polar branch (zotitan/train_zo.py:307-317), before their product."""
+        pc = self.cfg.perturbation
+        n = len(self.params)
+        p = self.params[i]
+        m, r = p.shape[0], min(pc.rank, p.shape[0])
+        P = randn(param_key(seed, n, i + 2 * n), m * r, p.device).view(m, r).to(p.dtype)
+        P, _ = torch.linalg.qr(P)
+        Psi = randn(param_key(seed, n, i + n), r * p.shape[1], p.device).view(r, p.shape[1]).to(p.dtype)
+        return P, zeropower_via_newtonschulz(Psi)
 
     def _lowrank_dense(self, i: int, seed: int) -> torch.Tensor:
         pc = self.cfg.perturbation
