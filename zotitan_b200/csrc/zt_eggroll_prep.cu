@@ -433,14 +433,17 @@ bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 // The same tail with the rank-R product on the tensor cores: mma.sync m16n8k8 on TF32
 // operands, each fp32 input split as hi = tf32(v), lo = tf32(v - hi) and the product
 // taken as lo*hi + hi*lo + hi*hi (the dropped lo*lo term and the TF32 rounding of lo
-// leave ~2^-22 relative, far inside the bf16 rounding that follows). A block owns 64
-// rows x 128 columns: the band of xa (the three partial products summed in order when
-// PARTS = 3) and the block's 128 rows of b are staged in shared memory as their TF32
-// hi / lo parts, split once per element; warp w computes
-// rows 16*(w/2) .. +16 and columns 64*(w%2) .. +64 and writes bf16(scale * delta) to a
-// shared tile (rows padded to 136 bf16: conflict-free fragment writes); then every
-// thread updates 8 consecutive outputs of a row with one 16-byte read and write of out.
+// leave ~2^-22 relative, far inside the bf16 rounding that follows). A block owns a band
+// of 64 rows and walks up to kBandChunks chunks of 128 columns: the band of xa (the three
+// partial products summed in order when PARTS = 3) is staged once as TF32 hi / lo parts
+// and kept in registers as MMA fragments; per chunk, the chunk's 128 rows of b are staged
+// the same way, warp w computes rows 16*(w/2) .. +16 and columns 64*(w%2) .. +64 and
+// writes bf16(scale * delta) to a shared tile (rows padded to 136 bf16: conflict-free
+// fragment writes), and every thread updates 8 consecutive outputs of a row with one
+// 16-byte read and write of out. The next chunk's out tile and b rows are requested
+// before the current chunk is multiplied, so HBM reads overlap the arithmetic.
 constexpr int kMmaRows = 64, kMmaCols = 128, kMmaLdd = kMmaCols + 8;
+constexpr int kBandChunks = 8;
 
 __device__ __forceinline__ uint32_t tf32_of(float v) {
   uint32_t r;
@@ -456,30 +459,46 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], 
 }
 
 template <int R, int PARTS>
-__global__ void __launch_bounds__(256) lora_add_mma_kernel(__nv_bfloat16* __restrict__ out, const float* __restrict__ xa,
-                                                           const float* __restrict__ bw, float scale, int64_t rows,
-                                                           int32_t n) {
+__global__ void __launch_bounds__(256, 2) lora_add_mma_kernel(__nv_bfloat16* __restrict__ out,
+                                                              const float* __restrict__ xa,
+                                                              const float* __restrict__ bw, float scale,
+                                                              int64_t rows, int32_t n, int32_t chunks_per_block) {
   static_assert(R % 8 == 0 && R <= 16, "k steps of 8; the staged operands fit 48 KB up to R = 16");
   constexpr int KS = R / 8;
   constexpr int LD = R + 4;  // padded rows: conflict-free fragment reads
   constexpr int R4 = R / 4;
-  // operands staged once per block as their TF32 hi / lo parts (bit patterns)
+  constexpr int BV = (kMmaCols * R4 + 255) / 256;  // b float4 pieces per thread per chunk
+  // operands staged as their TF32 hi / lo parts (bit patterns)
   __shared__ uint32_t sah[kMmaRows][LD], sal[kMmaRows][LD];
   __shared__ uint32_t sbh[kMmaCols][LD], sbl[kMmaCols][LD];
   __shared__ __align__(16) __nv_bfloat16 sd[kMmaRows][kMmaLdd];
   const int64_t row0 = (int64_t)blockIdx.y * kMmaRows;
-  const int col0 = blockIdx.x * kMmaCols;
   const int nr = (int)((rows - row0) < kMmaRows ? (rows - row0) : kMmaRows);
-  const int nc = (n - col0) < kMmaCols ? (n - col0) : kMmaCols;
-  // The block's tile of out, 16 threads per row and 8 columns each (n % 8 == 0: a group
-  // is wholly in or out of range), is read first, so the HBM reads are in flight while
-  // the operands are staged and multiplied.
+  const int n_chunks = (n + kMmaCols - 1) / kMmaCols;
+  const int c_begin = blockIdx.x * chunks_per_block;
+  const int c_end = min(c_begin + chunks_per_block, n_chunks);
   const int cq = (threadIdx.x % 16) * 8, q0 = threadIdx.x / 16;
-  uint4 ov[kMmaRows / 16];
+  uint4 ov[kMmaRows / 16], ovn[kMmaRows / 16];
+  float4 bv[BV], bvn[BV];
+  // out tile (16 threads per row, 8 columns each; n % 8 == 0: a group is wholly in or out
+  // of range) and b rows of chunk c into registers
+  auto load_chunk = [&](int c, uint4 (&o)[kMmaRows / 16], float4 (&b)[BV]) {
+    const int col0 = c * kMmaCols;
+    const int nc = (n - col0) < kMmaCols ? (n - col0) : kMmaCols;
 #pragma unroll
-  for (int j = 0; j < kMmaRows / 16; ++j)
-    if (q0 + 16 * j < nr && cq < nc) ov[j] = *reinterpret_cast<const uint4*>(out + (row0 + q0 + 16 * j) * n + col0 + cq);
-  // xa rows (PARTS * R floats, 16-byte aligned) and b rows (R floats) in 16-byte pieces
+    for (int j = 0; j < kMmaRows / 16; ++j)
+      if (q0 + 16 * j < nr && cq < nc) o[j] = *reinterpret_cast<const uint4*>(out + (row0 + q0 + 16 * j) * n + col0 + cq);
+#pragma unroll
+    for (int v = 0; v < BV; ++v) {
+      const int i = threadIdx.x + 256 * v;
+      const int cc = i / R4, k = (i % R4) * 4;
+      b[v] = (i < kMmaCols * R4 && cc < nc) ? __ldg(reinterpret_cast<const float4*>(bw + (size_t)(col0 + cc) * R + k))
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  if (c_begin >= c_end) return;
+  load_chunk(c_begin, ov, bv);
+  // the band of xa, once per block
   for (int i = threadIdx.x; i < kMmaRows * R4; i += 256) {
     const int rr = i / R4, k = (i % R4) * 4;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -501,18 +520,6 @@ __global__ void __launch_bounds__(256) lora_add_mma_kernel(__nv_bfloat16* __rest
       sal[rr][k + e] = tf32_of(__fsub_rn(e4[e], __uint_as_float(h)));
     }
   }
-  for (int i = threadIdx.x; i < kMmaCols * R4; i += 256) {
-    const int cc = i / R4, k = (i % R4) * 4;
-    const float4 v = cc < nc ? __ldg(reinterpret_cast<const float4*>(bw + (size_t)(col0 + cc) * R + k))
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float e4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const uint32_t h = tf32_of(e4[e]);
-      sbh[cc][k + e] = h;
-      sbl[cc][k + e] = tf32_of(__fsub_rn(e4[e], __uint_as_float(h)));
-    }
-  }
   __syncthreads();
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int g = lane / 4, t = lane % 4;
@@ -527,41 +534,65 @@ __global__ void __launch_bounds__(256) lora_add_mma_kernel(__nv_bfloat16* __rest
     ahi[ks][3] = sah[wr + g + 8][kb + t + 4];
     alo[ks][3] = sal[wr + g + 8][kb + t + 4];
   }
+  for (int c = c_begin; c < c_end; ++c) {
+    const int col0 = c * kMmaCols;
+    const int nc = (n - col0) < kMmaCols ? (n - col0) : kMmaCols;
+    __syncthreads();  // the previous chunk is done with sbh / sbl and sd
 #pragma unroll
-  for (int ni = 0; ni < 8; ++ni) {
-    const int cb = wc + ni * 8;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int v = 0; v < BV; ++v) {
+      const int i = threadIdx.x + 256 * v;
+      if (i >= kMmaCols * R4) continue;
+      const int cc = i / R4, k = (i % R4) * 4;
+      const float e4[4] = {bv[v].x, bv[v].y, bv[v].z, bv[v].w};
 #pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {
-      const uint32_t bhi[2] = {sbh[cb + g][ks * 8 + t], sbh[cb + g][ks * 8 + t + 4]};
-      const uint32_t blo[2] = {sbl[cb + g][ks * 8 + t], sbl[cb + g][ks * 8 + t + 4]};
-      mma_tf32(acc, alo[ks], bhi);
-      mma_tf32(acc, ahi[ks], blo);
-      mma_tf32(acc, ahi[ks], bhi);
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t h = tf32_of(e4[e]);
+        sbh[cc][k + e] = h;
+        sbl[cc][k + e] = tf32_of(__fsub_rn(e4[e], __uint_as_float(h)));
+      }
     }
-    // acc: rows wr + g and wr + g + 8, columns cb + 2t, cb + 2t + 1
-    *reinterpret_cast<__nv_bfloat162*>(&sd[wr + g][cb + 2 * t]) = __floats2bfloat162_rn(acc[0] * scale, acc[1] * scale);
-    *reinterpret_cast<__nv_bfloat162*>(&sd[wr + g + 8][cb + 2 * t]) =
-        __floats2bfloat162_rn(acc[2] * scale, acc[3] * scale);
-  }
-  __syncthreads();
+    if (c + 1 < c_end) load_chunk(c + 1, ovn, bvn);   // in flight while this chunk is multiplied
+    __syncthreads();
 #pragma unroll
-  for (int j = 0; j < kMmaRows / 16; ++j) {
-    const int rr = q0 + 16 * j;
-    if (rr >= nr || cq >= nc) continue;
-    uint4* p = reinterpret_cast<uint4*>(out + (row0 + rr) * n + col0 + cq);
-    const uint4 o = ov[j];
-    const uint4 dv = *reinterpret_cast<const uint4*>(&sd[rr][cq]);
-    const uint32_t ow[4] = {o.x, o.y, o.z, o.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
-    uint32_t yw[4];
+    for (int ni = 0; ni < 8; ++ni) {
+      const int cb = wc + ni * 8;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 of = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ow[e]));
-      const float2 df = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dw[e]));
-      const __nv_bfloat162 y = __floats2bfloat162_rn(of.x + df.x, of.y + df.y);
-      yw[e] = *reinterpret_cast<const uint32_t*>(&y);
+      for (int ks = 0; ks < KS; ++ks) {
+        const uint32_t bhi[2] = {sbh[cb + g][ks * 8 + t], sbh[cb + g][ks * 8 + t + 4]};
+        const uint32_t blo[2] = {sbl[cb + g][ks * 8 + t], sbl[cb + g][ks * 8 + t + 4]};
+        mma_tf32(acc, alo[ks], bhi);
+        mma_tf32(acc, ahi[ks], blo);
+        mma_tf32(acc, ahi[ks], bhi);
+      }
+      // acc: rows wr + g and wr + g + 8, columns cb + 2t, cb + 2t + 1
+      *reinterpret_cast<__nv_bfloat162*>(&sd[wr + g][cb + 2 * t]) = __floats2bfloat162_rn(acc[0] * scale, acc[1] * scale);
+      *reinterpret_cast<__nv_bfloat162*>(&sd[wr + g + 8][cb + 2 * t]) =
+          __floats2bfloat162_rn(acc[2] * scale, acc[3] * scale);
     }
-    *p = make_uint4(yw[0], yw[1], yw[2], yw[3]);
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kMmaRows / 16; ++j) {
+      const int rr = q0 + 16 * j;
+      if (rr >= nr || cq >= nc) continue;
+      uint4* p = reinterpret_cast<uint4*>(out + (row0 + rr) * n + col0 + cq);
+      const uint4 o = ov[j];
+      const uint4 dv = *reinterpret_cast<const uint4*>(&sd[rr][cq]);
+      const uint32_t ow[4] = {o.x, o.y, o.z, o.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
+      uint32_t yw[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 of = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ow[e]));
+        const float2 df = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dw[e]));
+        const __nv_bfloat162 y = __floats2bfloat162_rn(of.x + df.x, of.y + df.y);
+        yw[e] = *reinterpret_cast<const uint32_t*>(&y);
+      }
+      *p = make_uint4(yw[0], yw[1], yw[2], yw[3]);
+    }
+#pragma unroll
+    for (int j = 0; j < kMmaRows / 16; ++j) ov[j] = ovn[j];
+#pragma unroll
+    for (int v = 0; v < BV; ++v) bv[v] = bvn[v];
   }
 }
 
@@ -580,11 +611,16 @@ int lora_add_launch(const char* name, void* out, const float* xa, const float* b
   __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
   const int32_t ni = (int32_t)n;
   if ((r == 8 || r == 16) && n % 8 == 0 && aligned16(out) && aligned16(xa)) {  // tensor-core form
-    const dim3 g2((unsigned)((n + kMmaCols - 1) / kMmaCols), (unsigned)((rows + kMmaRows - 1) / kMmaRows));
+    // chunks of 128 columns per block: enough blocks for ~4 per SM, at most kBandChunks
+    const int64_t n_chunks = (n + kMmaCols - 1) / kMmaCols, bands = (rows + kMmaRows - 1) / kMmaRows;
+    const int64_t want = 4 * (int64_t)zt::sm_count();
+    int64_t per = (n_chunks * bands) / want;
+    per = per < 1 ? 1 : (per > kBandChunks ? kBandChunks : per);
+    const dim3 g2((unsigned)((n_chunks + per - 1) / per), (unsigned)bands);
     if (g2.y > 65535u) return zt::set_error(ZT_ERR_LIMIT, nm + ": too many rows");
     switch (r) {
-      case 8: lora_add_mma_kernel<8, PARTS><<<g2, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
-      default: lora_add_mma_kernel<16, PARTS><<<g2, 256, 0, s>>>(o, xa, b, scale, rows, ni); break;
+      case 8: lora_add_mma_kernel<8, PARTS><<<g2, 256, 0, s>>>(o, xa, b, scale, rows, ni, (int32_t)per); break;
+      default: lora_add_mma_kernel<16, PARTS><<<g2, 256, 0, s>>>(o, xa, b, scale, rows, ni, (int32_t)per); break;
     }
     return zt::check_cuda(cudaGetLastError(), (nm + " launch").c_str());
   }
