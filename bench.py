@@ -50,6 +50,10 @@ def parse():
                     help="sharded runs: fraction of free device memory for the field stores (0: regenerate)")
     ap.add_argument("--exchange-mode", choices=["copies", "in_pass"], default="copies",
                     help="sharded runs: push the fields by copy-engine copies or from the +eps pass")
+    ap.add_argument("--push-order", choices=["rotate", "all"], default="rotate",
+                    help="sharded runs: field pushes to one peer at a time in rotating order, or to all at once")
+    ap.add_argument("--push-streams", type=int, default=1,
+                    help="sharded runs with --push-order all: copy streams per destination")
     ap.add_argument("--profile-case", choices=["chain", "full", "replay", "chain-cached", "full-cached", "plus-cached",
                                                "replay-field", "replay-mixed", "lce", "lowrank", "eggroll", "eggroll-gated", "eggroll-forward",
                                                "mezo-step", "lora-step"],
@@ -1023,7 +1027,8 @@ def run_ours(args, rank, local_rank, world):
         def __getitem__(self, i):
             return vals_pinned[i:i + 1].to(dev, non_blocking=True)[0]
 
-    opt = ZOOptimizer(named, cfg, None, field_exchange=args.field_exchange or False, exchange_mode=args.exchange_mode)
+    opt = ZOOptimizer(named, cfg, None, field_exchange=args.field_exchange or False, exchange_mode=args.exchange_mode,
+                      push_order=args.push_order, push_streams=args.push_streams)
     opt.score_fn = global_pair_score(vals_dev, opt.planner, args.seeds)
     rng = np.random.default_rng(12345)   # seeded uint64 seed stream, identical on every rank
     opt.planner._draw_seeds = lambda n: [int(x) for x in rng.integers(0, 2**64 - 1, n, dtype=np.uint64)]
@@ -1083,7 +1088,8 @@ def run_ours(args, rank, local_rank, world):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             passes[k]["ms_per_step"], passes[k]["ms_per_launch"] = t.tolist()
     cached = opt.zcache is not None
-    exchange = {"mode": "in_pass" if opt.exchange.in_pass else "copies", "slots": opt.exchange.n_slots,
+    exchange = {"mode": "in_pass" if opt.exchange.in_pass else "copies", "push_order": opt.exchange.push_order,
+                "slots": opt.exchange.n_slots,
                 "pairs_stored": opt.exchange.active, "pairs_stored_per_step": stored_per_step,
                 "store_bytes": opt.exchange.store.numel() * 4} if opt.exchange is not None else None
     opt.close()

@@ -489,7 +489,7 @@ class ZOOptimizer:
     def __init__(self, named_params: list, cfg: ZOConfig, score_fn, total_steps: int = 0, process_group=None,
                  sharded: bool | None = None, shard_update: bool = True, noise_cache: bool | None = None,
                  field_exchange: bool | float | None = None, exchange_mode: str = "copies",
-                 lowrank_fused: bool = True):
+                 lowrank_fused: bool = True, push_order: str = "rotate", push_streams: int = 1):
         if exchange_mode not in ("copies", "in_pass"):
             raise ValueError(f"exchange_mode must be 'copies' or 'in_pass', got {exchange_mode!r}")
         self.named_params = named_params
@@ -598,7 +598,7 @@ class ZOOptimizer:
                 frac = field_exchange if isinstance(field_exchange, float) else 0.5
                 budget = int(frac * torch.cuda.mem_get_info(dev)[0])
             self.exchange = FieldExchange(self.layout, int(self.table.plan.n_units), rank, world, cfg.z_batch, dev,
-                                          budget, group=process_group, in_pass=in_pass)
+                                          budget, group=process_group, in_pass=in_pass, push_order=push_order, push_streams=push_streams)
             pl.field_slots = self.exchange.active
         self._metric_keys = None
 
