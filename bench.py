@@ -55,7 +55,7 @@ def parse():
     ap.add_argument("--push-streams", type=int, default=1,
                     help="sharded runs with --push-order all: copy streams per destination")
     ap.add_argument("--profile-case", choices=["chain", "full", "replay", "chain-cached", "full-cached", "plus-cached",
-                                               "replay-field", "replay-mixed", "lce", "lowrank", "eggroll", "eggroll-gated", "eggroll-forward",
+                                               "replay-field", "replay-mixed", "lce", "lowrank", "push-rates", "eggroll", "eggroll-gated", "eggroll-forward",
                                                "mezo-step", "lora-step"],
                     default=None,
                     help="small case for ncu: one bf16 tensor of 2^28 elements, 3 launches of the "
@@ -121,6 +121,97 @@ def eggroll_gemm_bench(rows: int = 16384, T: int = 1024, reps: int = 10):
     assert K_.eggroll_take_error() == 0
     print(json.dumps({"eggroll_gemm": res, "peak_tflops": peak,
                       "peak_source": "MEASURED_PEAKS.json bf16_tflops" if "bf16_tflops" in peaks else "fallback"}))
+
+
+def _profile_push_rates():
+    """Peer-to-peer push rates between the ranks of one node (run under torchrun, one rank
+    per GPU): copy-engine pushes of 512 MB per (sender, receiver) into CUDA-IPC-mapped
+    buffers with every peer at once (1, 2 or 4 streams per peer), one peer at a time in
+    rotating order (rank r sends to r + 1, r + 2, ...: every moment a permutation), every
+    rank to its next neighbour only, and NCCL all_to_all_single of the same volume. CUDA
+    events around each test between barriers, best of 3, max over ranks; rank 0 prints one
+    JSON line per test (GB/s sent per GPU)."""
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    from zotitan_b200 import _lib as L
+    from zotitan_b200.distributed import init_process_group_from_env
+    init_process_group_from_env("nccl", timeout_s=300)
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+    torch.cuda.set_device(dev)
+    lib = L.load()
+    slot = 512 << 20
+    store = torch.empty(world * slot, dtype=torch.uint8, device=dev)
+    src = torch.full((world * slot,), rank, dtype=torch.uint8, device=dev)
+    h = (ctypes.c_ubyte * L.ZT_IPC_HANDLE_BYTES)()
+    off = ctypes.c_uint64()
+    L.check(lib.zt_ipc_export(store.data_ptr(), h, ctypes.byref(off)), "zt_ipc_export")
+    handles = [None] * world
+    dist.all_gather_object(handles, (bytes(h), off.value))
+    peer, opened = [0] * world, []
+    for p, (hb, o) in enumerate(handles):
+        if p == rank:
+            peer[p] = store.data_ptr()
+            continue
+        base = ctypes.c_void_p()
+        L.check(lib.zt_ipc_open((ctypes.c_ubyte * L.ZT_IPC_HANDLE_BYTES).from_buffer_copy(hb), ctypes.byref(base)),
+                "zt_ipc_open")
+        opened.append(base.value)
+        peer[p] = base.value + o
+
+    def timed(fn):
+        dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def copies(plan):   # plan: list of (stream index, peer, piece index, pieces)
+        streams = [torch.cuda.Stream(dev) for _ in range(1 + max(q for q, _, _, _ in plan))]
+
+        def run():
+            cur = torch.cuda.current_stream(dev)
+            for st in streams:
+                st.wait_stream(cur)
+            for q, p, i, k in plan:
+                piece = slot // k
+                L.check(lib.zt_copy_async(peer[p] + rank * slot + i * piece, src.data_ptr() + p * slot + i * piece,
+                                          piece, ctypes.c_void_p(streams[q].cuda_stream)), "zt_copy_async")
+            for st in streams:
+                cur.wait_stream(st)
+        return run
+
+    others = [(rank + k) % world for k in range(1, world)]
+    tests = []
+    for k in (1, 2, 4):
+        plan = [(j * k + i, p, i, k) for j, p in enumerate(others) for i in range(k)]
+        tests.append((f"every_peer_at_once_{k}_streams_per_peer", copies(plan), len(others) * slot))
+    tests.append(("one_peer_at_a_time_rotating", copies([(0, p, 0, 1) for p in others]), len(others) * slot))
+    tests.append(("next_neighbour_only", copies([(0, others[0], 0, 1)]), slot))
+    out = torch.empty_like(src)
+    tests.append(("nccl_all_to_all_single", lambda: dist.all_to_all_single(out, src), len(others) * slot))
+    rows = []
+    for name, fn, nbytes in tests:
+        fn()
+        ms = min(timed(fn) for _ in range(3))
+        rows.append({"profile_case": "push-rates", "world": world, "test": name, "ms": ms,
+                     "gbs_sent_per_gpu": nbytes / ms / 1e6})
+    torch.cuda.synchronize()
+    for base in opened:
+        lib.zt_ipc_close(ctypes.c_void_p(base))
+    dist.barrier()
+    if rank == 0:
+        for r in rows:
+            print(json.dumps(r))
+    dist.destroy_process_group()
 
 
 def _profile_lowrank():
@@ -279,6 +370,9 @@ def profile_case(kind: str):
         return
     if kind == "lowrank":   # one low_rank direction of a [16384, 8192] bf16 matrix, rank 64
         _profile_lowrank()
+        return
+    if kind == "push-rates":   # under torchrun: peer-to-peer push rates of the field exchange
+        _profile_push_rates()
         return
     n = 1 << 28
     p = (torch.randn(n, device="cuda") * 0.02).bfloat16()

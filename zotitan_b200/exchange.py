@@ -12,7 +12,11 @@ last pass reads every stored field from HBM. Two ways of getting it there:
 
 - by copies (the default): the +eps pass keeps its field in a noise cache and copy-engine
   copies (``zt_copy_async``) push the slices into the stores, overlapping the next pairs'
-  passes; two or three caches rotate between a rank's pairs;
+  passes; two or three caches rotate between a rank's pairs. The slices of a pair go to
+  rank + 1, rank + 2, ... one after another on one link stream (``push_order="rotate"``):
+  the ranks push in step, so every moment is a permutation of the ranks, which the copy
+  engines carry at the one-peer rate (763 GB/s per GPU measured at 4 ranks, against 390
+  with every peer at once);
 - in the pass (``in_pass``, when the plan takes the specialised +eps kernel and there are
   at most ZT_MAX_PUSH_RANKS ranks): the +eps pass that generates the field also stores
   each unit of it straight into the owning rank's store over NVLink (``zt_pass_cfg.zpush``,
@@ -20,8 +24,7 @@ last pass reads every stored field from HBM. Two ways of getting it there:
   made the +eps pass the bottleneck (193 against 157 ms per step by copies): the remote
   stores run at the all-to-all rate, ~350-400 GB/s per GPU, and hold the pass's warps.
 
-The all-to-all rate bounds what the copies can carry: at 4 ranks one pair's push costs
-about as much as regenerating its field. So the number of stored pairs adapts (``adapt``):
+The push rate bounds what the copies can carry. So the number of stored pairs adapts (``adapt``):
 each rank times how long its pushes ran past its local passes in the previous step, the
 timings ride on the pair-value all-gather, and every rank applies the same rule to the
 same maxima, so the count changes between steps and identically everywhere.
