@@ -697,8 +697,16 @@ class ZOOptimizer:
             else:
                 torch.add(self.master[i], zz, alpha=scale, out=self.params[i])
 
-    def _lr_seed_chunks(self, seeds: list) -> list:
-        M = L.ZT_LOWRANK_MAX_STREAMS
+    _LR_CHUNK_BYTES = 2 << 30   # factor buffers of one launch over many seeds
+
+    def _lr_seed_chunks(self, seeds: list, i: int) -> list:
+        """Seeds of one launch for tensor i: at most ZT_LOWRANK_MAX_STREAMS, and at most about
+        2 GB of factor buffers ((m + n) x the padded K per seed, 9 r for fp32)."""
+        p = self.params[i]
+        r = min(self.cfg.perturbation.rank, p.shape[0])
+        width = 9 * r if p.dtype == torch.float32 else r
+        per_seed = (p.shape[0] + p.shape[1]) * 64 * ((width + 63) // 64) * 2
+        M = max(1, min(L.ZT_LOWRANK_MAX_STREAMS, self._LR_CHUNK_BYTES // per_seed))
         return [seeds[c:c + M] for c in range(0, len(seeds), M)]
 
     def _lr_replay_master(self) -> None:
@@ -709,7 +717,7 @@ class ZOOptimizer:
         seeds = self.planner.seeds
         for i in self.lr_idx:
             if i in self.lr_fused:
-                for chunk in self._lr_seed_chunks(seeds):
+                for chunk in self._lr_seed_chunks(seeds, i):
                     self._lowrank_one(i, chunk).apply(src=self.master[i], dst=self.master[i],
                                                       alphas=(eps, -2 * eps, eps))
         dense = [i for i in self.lr_idx if i not in self.lr_fused]
@@ -747,7 +755,7 @@ class ZOOptimizer:
                     torch._foreach_add_(dge, [self._lowrank_dense(i, seed) for i in dense], alpha=coefs[j])
             for i in self.lr_idx:
                 if i in self.lr_fused:
-                    for c, chunk in enumerate(self._lr_seed_chunks(list(range(len(pl.seeds))))):
+                    for c, chunk in enumerate(self._lr_seed_chunks(list(range(len(pl.seeds))), i)):
                         self._lowrank_one(i, [pl.seeds[j] for j in chunk]).apply(
                             ge=self.lr_ge[pos[i]], coefs=[coefs[j] for j in chunk], ge_init=c == 0)
         # the 2-D tensors' table has no live copy: the sharded schedule copies master -> live after
