@@ -52,6 +52,8 @@ def parse():
                     help="sharded runs: push the fields by copy-engine copies or from the +eps pass")
     ap.add_argument("--push-order", choices=["rotate", "all"], default="rotate",
                     help="sharded runs: field pushes to one peer at a time in rotating order, or to all at once")
+    ap.add_argument("--push-after", choices=["plus", "minus"], default=None,
+                    help="sharded runs: start a pair's field pushes after its +eps or its -2eps pass")
     ap.add_argument("--push-streams", type=int, default=1,
                     help="sharded runs with --push-order all: copy streams per destination")
     ap.add_argument("--profile-case", choices=["chain", "full", "replay", "chain-cached", "full-cached", "plus-cached",
@@ -126,7 +128,8 @@ def eggroll_gemm_bench(rows: int = 16384, T: int = 1024, reps: int = 10):
 def _profile_push_rates():
     """Peer-to-peer push rates between the ranks of one node (run under torchrun, one rank
     per GPU): copy-engine pushes of 512 MB per (sender, receiver) into CUDA-IPC-mapped
-    buffers with every peer at once (1, 2 or 4 streams per peer), one peer at a time in
+    buffers with every peer at once, issued in the same peer order on every rank or
+    starting at each rank's next peer (1, 2 or 4 streams per peer), one peer at a time in
     rotating order (rank r sends to r + 1, r + 2, ...: every moment a permutation), every
     rank to its next neighbour only, and NCCL all_to_all_single of the same volume. CUDA
     events around each test between barriers, best of 3, max over ranks; rank 0 prints one
@@ -191,6 +194,11 @@ def _profile_push_rates():
 
     others = [(rank + k) % world for k in range(1, world)]
     tests = []
+    # every rank issuing its copies in the same peer order (lowest rank first): the ranks'
+    # first copies all land on the same receiver
+    same = [p for p in range(world) if p != rank]
+    tests.append(("every_peer_at_once_same_order", copies([(j, p, 0, 1) for j, p in enumerate(same)]),
+                  len(others) * slot))
     for k in (1, 2, 4):
         plan = [(j * k + i, p, i, k) for j, p in enumerate(others) for i in range(k)]
         tests.append((f"every_peer_at_once_{k}_streams_per_peer", copies(plan), len(others) * slot))
@@ -1122,7 +1130,8 @@ def run_ours(args, rank, local_rank, world):
             return vals_pinned[i:i + 1].to(dev, non_blocking=True)[0]
 
     opt = ZOOptimizer(named, cfg, None, field_exchange=args.field_exchange or False, exchange_mode=args.exchange_mode,
-                      push_order=args.push_order, push_streams=args.push_streams)
+                      push_order=args.push_order, push_streams=args.push_streams,
+                      **({"push_after": args.push_after} if args.push_after else {}))
     opt.score_fn = global_pair_score(vals_dev, opt.planner, args.seeds)
     rng = np.random.default_rng(12345)   # seeded uint64 seed stream, identical on every rank
     opt.planner._draw_seeds = lambda n: [int(x) for x in rng.integers(0, 2**64 - 1, n, dtype=np.uint64)]
@@ -1183,6 +1192,7 @@ def run_ours(args, rank, local_rank, world):
             passes[k]["ms_per_step"], passes[k]["ms_per_launch"] = t.tolist()
     cached = opt.zcache is not None
     exchange = {"mode": "in_pass" if opt.exchange.in_pass else "copies", "push_order": opt.exchange.push_order,
+                "push_after": opt.push_after,
                 "slots": opt.exchange.n_slots,
                 "pairs_stored": opt.exchange.active, "pairs_stored_per_step": stored_per_step,
                 "store_bytes": opt.exchange.store.numel() * 4} if opt.exchange is not None else None

@@ -14,9 +14,9 @@ last pass reads every stored field from HBM. Two ways of getting it there:
   copies (``zt_copy_async``) push the slices into the stores, overlapping the next pairs'
   passes; two or three caches rotate between a rank's pairs. The slices of a pair go to
   rank + 1, rank + 2, ... one after another on one link stream (``push_order="rotate"``):
-  the ranks push in step, so every moment is a permutation of the ranks, which the copy
-  engines carry at the one-peer rate (763 GB/s per GPU measured at 4 ranks, against 390
-  with every peer at once);
+  the ranks push in step, so every moment is a permutation of the ranks (762 GB/s per GPU
+  measured at 4 ranks). Every rank pushing to its peers in the same order (lowest rank
+  first) puts all first copies on one receiver: 391 GB/s;
 - in the pass (``in_pass``, when the plan takes the specialised +eps kernel and there are
   at most ZT_MAX_PUSH_RANKS ranks): the +eps pass that generates the field also stores
   each unit of it straight into the owning rank's store over NVLink (``zt_pass_cfg.zpush``,
@@ -147,10 +147,11 @@ class FieldExchange:
         self.plans = [push_plan(layout, n_units, j, world) for j in range(self.n_slots)]
         # Push order. "rotate" (default): one link stream sends a pair's slices to rank + 1,
         # rank + 2, ... in turn, so while the ranks push in step every moment is a permutation
-        # (each GPU sends to one peer and receives from one), which the copy engines carry at
-        # the one-peer rate; the rank's own slice goes on a second stream. "all": copy streams
-        # per destination (`push_streams` each), every peer at once. Measured at 4 ranks: one
-        # peer per GPU 749 GB/s, every peer at once 392-409 GB/s whatever the streams per peer.
+        # (each GPU sends to one peer and receives from one); the rank's own slice goes on a
+        # second stream. "all": copy streams per destination (`push_streams` each), issued in
+        # rank order, every peer at once. Measured at 4 ranks (bench.py --profile-case
+        # push-rates): rotating 762 GB/s per GPU; every peer at once 713-759 GB/s when each
+        # rank starts at its next peer, 391 GB/s when all ranks start at the same peer.
         if push_order not in ("rotate", "all"):
             raise ValueError(f"push_order must be 'rotate' or 'all', got {push_order!r}")
         self.push_order = push_order
