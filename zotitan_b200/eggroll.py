@@ -372,8 +372,9 @@ class EggrollPopulation:
         2-D tensors take the sum as one GEMM of rank 4 * pairs on the tensor cores:
         [A_hi | A_lo] [B | B]^T with A = (coef_j c_j P_j)_j split into two bf16 parts
         (~2^-16 relative) and B = (Psi_j^T)_j (bf16-exact), accumulated in fp32 and added to
-        the weight in the GEMM's epilogue (addmm), rounded to the parameter dtype once (the
-        reference accumulates grad_est in that dtype pair by pair)."""
+        the weight in the GEMM's epilogue (zt_gemm_addto; torch's addmm for shapes it does
+        not take), rounded to the parameter dtype once (the reference accumulates grad_est
+        in that dtype pair by pair)."""
         if len(pair_seeds) != len(coefs):
             raise ValueError("one coefficient per pair")
         if not pair_seeds:

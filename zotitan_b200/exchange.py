@@ -21,8 +21,10 @@ last pass reads every stored field from HBM. Two ways of getting it there:
   at most ZT_MAX_PUSH_RANKS ranks): the +eps pass that generates the field also stores
   each unit of it straight into the owning rank's store over NVLink (``zt_pass_cfg.zpush``,
   peer mappings through CUDA IPC), then fences at system scope. Measured at 4 ranks it
-  made the +eps pass the bottleneck (193 against 157 ms per step by copies): the remote
-  stores run at the all-to-all rate, ~350-400 GB/s per GPU, and hold the pass's warps.
+  made the +eps pass the bottleneck (193 against 157 ms per step by copies in rank order):
+  every rank's kernel walks the units in the same order, so all ranks store to the same
+  owner at once (the hot spot of copies issued in rank order, ~390 GB/s per GPU), and the
+  remote stores hold the pass's warps.
 
 The push rate bounds what the copies can carry. So the number of stored pairs adapts (``adapt``):
 each rank times how long its pushes ran past its local passes in the previous step, the
