@@ -9,7 +9,7 @@ field_j[u*2048 ...] -- for every rank, chunk, unit of its share and stored pair.
 import numpy as np
 import pytest
 
-from zotitan_b200.exchange import chunk_field, push_plan, slots_that_fit, store_elems
+from zotitan_b200.exchange import chunk_field, push_plan, rotating_peers, slots_that_fit, store_elems
 from zotitan_b200.flat import FlatLayout
 
 U = 2048
@@ -120,3 +120,14 @@ def test_adapt_caps_at_slots_and_local_pairs():
     ex.adaptive = False
     ex.adapt(lag=50.0, push=2.0, plus=1.0, local_pairs=8)
     assert ex.s == 3
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_rotating_pushes_are_permutations_at_every_step(world):
+    """Push k of every rank goes to rank + k: each step is a permutation (no receiver gets
+    two senders at once), every rank reaches every peer exactly once, never itself."""
+    orders = [rotating_peers(r, world) for r in range(world)]
+    for r, o in enumerate(orders):
+        assert sorted(o) == [p for p in range(world) if p != r]
+    for k in range(world - 1):
+        assert sorted(o[k] for o in orders) == list(range(world))

@@ -88,6 +88,14 @@ def push_plan(layout, n_units: int, slot: int, world: int) -> list[Copy]:
     return out
 
 
+def rotating_peers(rank: int, world: int) -> list[int]:
+    """The peers rank `rank` pushes a pair's slices to, in order: rank + 1, rank + 2, ...
+    (mod world). The k-th push of every rank goes to rank + k, so when the ranks push in
+    step each of the world - 1 steps is a permutation: every rank sends to one peer and
+    receives from one."""
+    return [(rank + k) % world for k in range(1, world)]
+
+
 def store_elems(layout, n_slots: int) -> int:
     return n_slots * layout.chunks * layout.per * U
 
@@ -271,7 +279,7 @@ class FieldExchange:
         for c in self.plans[j]:
             by_dst.setdefault(c.dst, []).append(c)
         if self.push_order == "rotate":
-            work = [(0, self.streams[0][0], [(self.rank + k) % self.world for k in range(1, self.world)]),
+            work = [(0, self.streams[0][0], rotating_peers(self.rank, self.world)),
                     (1, self.streams[1][0], [self.rank])]
         else:
             work = []
