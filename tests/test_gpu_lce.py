@@ -4,7 +4,7 @@ Against torch on the same operands: logits = F.linear(x, w) in bf16 (the referen
 bf16 lm_head), then loss / logsumexp / first argmax on their fp32 upcast, as
 zotitan/losses.py:55-79 computes them. The kernel accumulates the dot products on the
 tensor cores in another order than cuBLAS, so a logit can round to the neighbouring
-bf16 value: loss and lse agree within 1e-3 relative (the north star's loss tolerance),
+bf16 value: loss and lse agree within 1e-3 relative (the losses' tolerance of the parity bar),
 and the argmax flag agrees on all but a handful of near-tied rows. Shapes cover ragged
 row and vocabulary counts (partial 256-row tiles, a partial last vocabulary tile), the
 config-3 scorer shape (16 x 512 rows, vocabulary 128,256, d 2048), ignored rows and an
