@@ -484,7 +484,12 @@ class ZOOptimizer:
     copies from the noise cache, overlapping the next pair's passes; the stored-pair count
     adapts step by step to the copy bandwidth) or "in_pass" (the +eps pass stores its
     field into the owners' stores over NVLink itself, when its plan takes the specialised
-    kernel)."""
+    kernel). ``push_order``: "rotate" (default; a pair's slices go to rank + 1, rank + 2,
+    ... one after another, so every moment is a permutation of the ranks) or "all" (every
+    peer at once, ``push_streams`` copy streams per peer). ``push_after``: "minus"
+    (default; a pair's pushes start after its -2eps pass) or "plus" (after its +eps pass).
+    ``lowrank_fused``: low_rank / polar directions of 2-D tensors recomputed on the tensor
+    cores in each use (zt_lowrank_*) instead of materialised with the reference's ops."""
 
     def __init__(self, named_params: list, cfg: ZOConfig, score_fn, total_steps: int = 0, process_group=None,
                  sharded: bool | None = None, shard_update: bool = True, noise_cache: bool | None = None,
